@@ -1,0 +1,575 @@
+/*
+ * aljabr_oracle.c -- TEST INFRASTRUCTURE ONLY (see aljabr_oracle.h).
+ *
+ * Compiled with -ffp-contract=off so that every `a * b + c` rounds twice,
+ * as Java float arithmetic does; fused multiply-adds appear only where the
+ * reference itself calls Math.fma or FloatVector.fma.
+ *
+ * Where the reference uses the Java Vector API, the lane width follows the
+ * species it names: GGUFVectorOps uses SPECIES_PREFERRED (machine
+ * dependent; restated here as 8 lanes, the AVX2 width) and the Q8 raw dot
+ * uses SPECIES_256 (8 float lanes).  reduceLanes(ADD) has no specified
+ * order; it is restated as a left-to-right lane sum.
+ */
+#include "aljabr_oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define VLANES 8
+
+static const float NF4_TABLE[16] = {
+    /* engine/safetensor/.../DequantizationKernel.java:23-28 */
+    -1.0f, -0.6961928009986877f, -0.5250730514526367f, -0.39491748809814453f,
+    -0.28444138169288635f, -0.18477343022823334f, -0.09105003625154495f, 0.0f,
+    0.07958029955625534f, 0.16093020141124725f, 0.24611230194568634f, 0.33791524171829224f,
+    0.44070982933044434f, 0.5626170039176941f, 0.7229568362236023f, 1.0f};
+
+static inline float f32_from_bits(uint32_t b) { float f; memcpy(&f, &b, 4); return f; }
+static inline uint32_t bits_of(float f) { uint32_t b; memcpy(&b, &f, 4); return b; }
+static inline uint16_t le16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+/* ------------------------------------------------------------------------ */
+/* RT/GgufQuantTables.java:143-165 (f16ToF32Slow; the 64K table is built from it). */
+float orc_f16_to_f32(uint16_t half) {
+    int sign = (half >> 15) & 1;
+    int exponent = (half >> 10) & 0x1F;
+    int mantissa = half & 0x3FF;
+    if (exponent == 0) {
+        if (mantissa == 0) return sign ? -0.0f : 0.0f;
+        float value = ldexpf((float)mantissa / 1024.0f, -14);   /* Math.scalb, exact */
+        return sign ? -value : value;
+    }
+    if (exponent == 31) {
+        if (mantissa == 0) return sign ? -INFINITY : INFINITY;
+        return f32_from_bits(0x7FC00000u);                       /* Float.NaN */
+    }
+    return f32_from_bits(((uint32_t)sign << 31) | ((uint32_t)(exponent + 112) << 23) | ((uint32_t)mantissa << 13));
+}
+
+/* GW:360-387.  Float.floatToIntBits canonicalises NaN first. */
+uint16_t orc_f32_to_f16_bits(float value) {
+    uint32_t bits = bits_of(value);
+    if (value != value) bits = 0x7FC00000u;
+    int sign = (int)((bits >> 16) & 0x8000);
+    int exponent = (int)((bits >> 23) & 0xFF) - 127 + 15;
+    int mantissa = (int)(bits & 0x7FFFFF);
+    if (exponent >= 31) return (uint16_t)(sign | 0x7C00 | (mantissa == 0 ? 0 : 1));
+    if (exponent <= 0) {
+        if (exponent < -10) return (uint16_t)sign;
+        mantissa |= 0x800000;
+        int shift = 14 - exponent;
+        int half_mantissa = mantissa >> shift;
+        if (((mantissa >> (shift - 1)) & 1) != 0) half_mantissa++;
+        return (uint16_t)(sign | half_mantissa);
+    }
+    int half = sign | (exponent << 10) | (mantissa >> 13);
+    if ((mantissa & 0x1000) != 0) half++;
+    return (uint16_t)half;
+}
+
+/* java.lang.Math.round(float): nearest int, ties toward +inf, NaN -> 0,
+ * saturating.  floor(a + 0.5) in double is exact for every float. */
+int orc_java_round(float value) {
+    if (value != value) return 0;
+    double r = floor((double)value + 0.5);
+    if (r >= 2147483647.0) return 2147483647;
+    if (r <= -2147483648.0) return (int)-2147483648LL;
+    return (int)r;
+}
+
+uint16_t orc_f32_to_bf16_rne(float value) {
+    uint32_t b = bits_of(value);
+    if ((b & 0x7FFFFFFFu) > 0x7F800000u) return (uint16_t)((b >> 16) | 0x40);   /* quiet NaN */
+    uint32_t lsb = (b >> 16) & 1u;
+    b += 0x7FFFu + lsb;
+    return (uint16_t)(b >> 16);
+}
+
+static inline float bf16_to_f32(uint16_t h) { return f32_from_bits((uint32_t)h << 16); }
+
+/* ------------------------------------------------------------------------ */
+static float java_max_abs(const float* v, int n) {            /* GW:196-202 */
+    float m = 0.0f;
+    for (int i = 0; i < n; i++) {
+        float a = fabsf(v[i]);
+        if (a != a) { m = a; continue; }                       /* Math.max propagates NaN */
+        if (m != m) continue;
+        if (a > m) m = a;
+    }
+    return m;
+}
+static inline int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
+
+void orc_encode_q8_0(const float* values, int64_t n, uint8_t* out) {   /* GW:163-177 */
+    for (int64_t block = 0; block < n; block += 32) {
+        float scale = java_max_abs(values + block, 32) / 127.0f;
+        uint16_t h = orc_f32_to_f16_bits(scale);
+        out[0] = (uint8_t)(h & 0xFF); out[1] = (uint8_t)(h >> 8);
+        for (int i = 0; i < 32; i++) {
+            int q = scale == 0.0f ? 0 : orc_java_round(values[block + i] / scale);
+            out[2 + i] = (uint8_t)(clampi(q, -127, 127) & 0xFF);
+        }
+        out += 34;
+    }
+}
+
+static int quantize4(float value, float scale) {              /* GW:204-209 */
+    if (scale == 0.0f) return 0;
+    return clampi(orc_java_round(value / scale), -8, 7);
+}
+
+void orc_encode_q4_0(const float* values, int64_t n, uint8_t* out) {   /* GW:179-194 */
+    for (int64_t block = 0; block < n; block += 32) {
+        float scale = java_max_abs(values + block, 32) / 7.0f;
+        uint16_t h = orc_f32_to_f16_bits(scale);
+        out[0] = (uint8_t)(h & 0xFF); out[1] = (uint8_t)(h >> 8);
+        for (int i = 0; i < 16; i++) {
+            int lo = quantize4(values[block + i], scale) + 8;
+            int hi = quantize4(values[block + 16 + i], scale) + 8;
+            out[2 + i] = (uint8_t)((hi << 4) | lo);
+        }
+        out += 18;
+    }
+}
+
+void orc_quantize_nf4(const float* values, int64_t n, int group_size, uint8_t* codes, float* absmax) {
+    int64_t groups = (n + group_size - 1) / group_size;
+    for (int64_t g = 0; g < groups; g++) {
+        int64_t start = g * group_size;
+        int len = (int)((start + group_size <= n) ? group_size : n - start);
+        absmax[g] = java_max_abs(values + start, len);
+    }
+    for (int64_t i = 0; i < n; i++) {
+        float s = absmax[i / group_size];
+        int best = 7;
+        if (s != 0.0f) {
+            float v = values[i] / s;
+            float bestd = INFINITY;
+            for (int c = 0; c < 16; c++) {
+                float d = fabsf(NF4_TABLE[c] - v);
+                if (d < bestd) { bestd = d; best = c; }
+            }
+        }
+        if ((i & 1) == 0) codes[i >> 1] = (uint8_t)(best << 4);
+        else codes[i >> 1] |= (uint8_t)best;
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* DK:84-102.  The odd element reuses the even element's group index. */
+void orc_dequantize_nf4(const uint8_t* src, float* dst, const float* scales, int64_t numel, int group_size) {
+    int64_t num_bytes = (numel + 1) / 2;
+    for (int64_t i = 0; i < num_bytes; i++) {
+        int b = src[i];
+        int v1 = (b >> 4) & 0x0F;
+        int v2 = b & 0x0F;
+        float scale = scales[(i * 2) / group_size];
+        dst[i * 2] = NF4_TABLE[v1] * scale;
+        if (i * 2 + 1 < numel) dst[i * 2 + 1] = NF4_TABLE[v2] * scale;
+    }
+}
+
+/* RT/GgufBlockDequantizer.java:33-37 -> dequantizeQ4Block :366-415 with
+ * zeroPoint 8 and bias +0.0f (the bias add turns -0.0 into +0.0). */
+void orc_dequantize_q4_0(const uint8_t* blocks, float* dst, int64_t numel) {
+    for (int64_t b = 0; b < numel / 32; b++) {
+        const uint8_t* blk = blocks + b * 18;
+        float d = orc_f16_to_f32(le16(blk));
+        float* o = dst + b * 32;
+        for (int j = 0; j < 16; j++) {
+            int quant = blk[2 + j];
+            o[j] = (float)((quant & 0x0F) - 8) * d + 0.0f;
+            o[16 + j] = (float)((quant >> 4) - 8) * d + 0.0f;
+        }
+    }
+}
+
+/* RT/GgufRowDequantizer.java:142-151 -> GgufBlockDequantizer.java:231-265. */
+void orc_dequantize_q8_0(const uint8_t* blocks, float* dst, int64_t numel) {
+    for (int64_t b = 0; b < numel / 32; b++) {
+        const uint8_t* blk = blocks + b * 34;
+        float d = orc_f16_to_f32(le16(blk));
+        for (int j = 0; j < 32; j++) dst[b * 32 + j] = (float)(int8_t)blk[2 + j] * d;
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* RT/GgufQ32RawDot.java:454-462 (dotQ4_0PackedNibbleByte). */
+static inline float q4_nibble_byte(int quant, const float* v, int index) {
+    return (float)((quant & 0x0F) - 8) * v[index] + (float)((quant >> 4) - 8) * v[16 + index];
+}
+
+/* RT/GgufQ32RawDot.java:428-452: byte i of the 16 code bytes feeds lane
+ * i % 4; each lane sums its four bytes left to right. */
+static float q4_0_unscaled_block(const uint8_t* codes, const float* v) {
+    float s[4];
+    for (int lane = 0; lane < 4; lane++) {
+        s[lane] = q4_nibble_byte(codes[lane], v, lane) + q4_nibble_byte(codes[4 + lane], v, 4 + lane)
+                + q4_nibble_byte(codes[8 + lane], v, 8 + lane) + q4_nibble_byte(codes[12 + lane], v, 12 + lane);
+    }
+    return s[0] + s[1] + s[2] + s[3];
+}
+
+static inline float q4_0_block(const uint8_t* blk, const float* v) {   /* :342-348 */
+    float d = orc_f16_to_f32(le16(blk));
+    return d * q4_0_unscaled_block(blk + 2, v);
+}
+
+float orc_dot_row_q4_0(const uint8_t* row, int columns, const float* x) {   /* :34-67 */
+    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+    int blocks = columns / 32, block = 0, unrolled_limit = blocks - 4;
+    for (; block <= unrolled_limit; block += 4) {
+        s0 += q4_0_block(row + (size_t)block * 18, x + block * 32);
+        s1 += q4_0_block(row + (size_t)(block + 1) * 18, x + (block + 1) * 32);
+        s2 += q4_0_block(row + (size_t)(block + 2) * 18, x + (block + 2) * 32);
+        s3 += q4_0_block(row + (size_t)(block + 3) * 18, x + (block + 3) * 32);
+    }
+    float sum = s0 + s1 + s2 + s3;
+    for (; block < blocks; block++) sum += q4_0_block(row + (size_t)block * 18, x + block * 32);
+    return sum;
+}
+
+/* RT/GgufQ8RawDot.java:784-830: lane l sums bytes l, l+4, l+8, ... in pairs. */
+static float q8_unscaled_block_scalar(const uint8_t* q, const float* v) {
+    float s[4];
+    for (int lane = 0; lane < 4; lane++) {
+        float acc = (float)(int8_t)q[lane] * v[lane] + (float)(int8_t)q[lane + 4] * v[lane + 4];
+        acc += (float)(int8_t)q[lane + 8] * v[lane + 8] + (float)(int8_t)q[lane + 12] * v[lane + 12];
+        acc += (float)(int8_t)q[lane + 16] * v[lane + 16] + (float)(int8_t)q[lane + 20] * v[lane + 20];
+        acc += (float)(int8_t)q[lane + 24] * v[lane + 24] + (float)(int8_t)q[lane + 28] * v[lane + 28];
+        s[lane] = acc;
+    }
+    return s[0] + s[1] + s[2] + s[3];
+}
+
+float orc_dot_row_q8_0_scalar(const uint8_t* row, int columns, const float* x) {   /* :138-185 */
+    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+    int blocks = columns / 32, block = 0, unrolled_limit = blocks - 4;
+    for (; block <= unrolled_limit; block += 4) {
+        for (int u = 0; u < 4; u++) {
+            const uint8_t* blk = row + (size_t)(block + u) * 34;
+            float t = orc_f16_to_f32(le16(blk)) * q8_unscaled_block_scalar(blk + 2, x + (block + u) * 32);
+            if (u == 0) s0 += t; else if (u == 1) s1 += t; else if (u == 2) s2 += t; else s3 += t;
+        }
+    }
+    float sum = s0 + s1 + s2 + s3;
+    for (; block < blocks; block++) {
+        const uint8_t* blk = row + (size_t)block * 34;
+        float d = orc_f16_to_f32(le16(blk));
+        sum += d * q8_unscaled_block_scalar(blk + 2, x + block * 32);
+    }
+    return sum;
+}
+
+/* RT/GgufQ8RawDot.java:755-782: one block into an 8-lane accumulator. */
+static void q8_block_vector(const uint8_t* q, const float* v, float scale, float* acc) {
+    for (int l = 0; l < VLANES; l++) {
+        float b = (float)(int8_t)q[l] * v[l];
+        b = fmaf((float)(int8_t)q[8 + l], v[8 + l], b);
+        b = fmaf((float)(int8_t)q[16 + l], v[16 + l], b);
+        b = fmaf((float)(int8_t)q[24 + l], v[24 + l], b);
+        acc[l] = fmaf(b, scale, acc[l]);
+    }
+}
+
+float orc_dot_row_q8_0_vector(const uint8_t* row, int columns, const float* x) {   /* :63-121 */
+    float a[4][VLANES];
+    memset(a, 0, sizeof a);
+    int blocks = columns / 32, block = 0, unrolled_limit = blocks - 4;
+    for (; block <= unrolled_limit; block += 4)
+        for (int u = 0; u < 4; u++) {
+            const uint8_t* blk = row + (size_t)(block + u) * 34;
+            q8_block_vector(blk + 2, x + (block + u) * 32, orc_f16_to_f32(le16(blk)), a[u]);
+        }
+    float acc[VLANES];
+    for (int l = 0; l < VLANES; l++) acc[l] = a[0][l] + a[1][l] + a[2][l] + a[3][l];
+    for (; block < blocks; block++) {
+        const uint8_t* blk = row + (size_t)block * 34;
+        q8_block_vector(blk + 2, x + block * 32, orc_f16_to_f32(le16(blk)), acc);
+    }
+    float r = 0.0f;
+    for (int l = 0; l < VLANES; l++) r += acc[l];
+    return r;
+}
+
+/* ------------------------------------------------------------------------ */
+/* Row parallelism: rows split into 2 chunks per thread, chunks pulled from a
+ * shared counter (RT/GgufParallelConfig.java:14-15,56-73, GgufRows.java:133). */
+typedef struct {
+    int type, K, N, group, vector_order;
+    const uint8_t* w; const float* absmax; const float* x; const float* bias;
+    float* y; double* y64;
+    int chunks; int next; pthread_mutex_t lock;
+} job_t;
+
+static float nf4_row_dot(const uint8_t* codes, const float* absmax, const float* x, int K, int group, int64_t row) {
+    /* dequantise the row exactly as DK:84-102 does for the flat tensor, then
+     * a sequential fp32 dot (stand-in for the closed cblas_sgemv). */
+    float s = 0.0f;
+    int64_t base = row * (int64_t)K;
+    for (int k = 0; k < K; k += 2) {
+        int64_t i = (base + k) >> 1;
+        int b = codes[i];
+        float scale = absmax[(i * 2) / group];
+        s += NF4_TABLE[(b >> 4) & 15] * scale * x[k];
+        if (k + 1 < K) s += NF4_TABLE[b & 15] * scale * x[k + 1];
+    }
+    return s;
+}
+
+static double f64_row_dot(const job_t* j, int64_t row) {
+    int K = j->K;
+    double s = 0.0;
+    if (j->type == ORC_Q4_0) {
+        const uint8_t* r = j->w + row * (int64_t)(K / 32) * 18;
+        for (int b = 0; b < K / 32; b++) {
+            double d = orc_f16_to_f32(le16(r + b * 18));
+            for (int t = 0; t < 16; t++) {
+                int q = r[b * 18 + 2 + t];
+                s += d * ((q & 15) - 8) * (double)j->x[b * 32 + t];
+                s += d * ((q >> 4) - 8) * (double)j->x[b * 32 + 16 + t];
+            }
+        }
+    } else if (j->type == ORC_Q8_0) {
+        const uint8_t* r = j->w + row * (int64_t)(K / 32) * 34;
+        for (int b = 0; b < K / 32; b++) {
+            double d = orc_f16_to_f32(le16(r + b * 34));
+            for (int t = 0; t < 32; t++) s += d * (int8_t)r[b * 34 + 2 + t] * (double)j->x[b * 32 + t];
+        }
+    } else {
+        int64_t base = row * (int64_t)K;
+        for (int k = 0; k < K; k++) {
+            int64_t e = base + k;
+            int b = j->w[e >> 1];
+            int code = (e & 1) ? (b & 15) : ((b >> 4) & 15);
+            s += (double)NF4_TABLE[code] * (double)j->absmax[((e >> 1) * 2) / j->group] * (double)j->x[k];
+        }
+    }
+    return s;
+}
+
+static void* worker(void* arg) {
+    job_t* j = (job_t*)arg;
+    for (;;) {
+        pthread_mutex_lock(&j->lock);
+        int c = j->next++;
+        pthread_mutex_unlock(&j->lock);
+        if (c >= j->chunks) break;
+        int64_t r0 = (int64_t)j->N * c / j->chunks, r1 = (int64_t)j->N * (c + 1) / j->chunks;
+        for (int64_t r = r0; r < r1; r++) {
+            if (j->y64) { j->y64[r] = f64_row_dot(j, r); continue; }
+            float v;
+            if (j->type == ORC_Q4_0) v = orc_dot_row_q4_0(j->w + r * (int64_t)(j->K / 32) * 18, j->K, j->x);
+            else if (j->type == ORC_Q8_0)
+                v = j->vector_order ? orc_dot_row_q8_0_vector(j->w + r * (int64_t)(j->K / 32) * 34, j->K, j->x)
+                                    : orc_dot_row_q8_0_scalar(j->w + r * (int64_t)(j->K / 32) * 34, j->K, j->x);
+            else {
+                v = nf4_row_dot(j->w, j->absmax, j->x, j->K, j->group, r);
+                if (j->bias) v += j->bias[r];
+            }
+            j->y[r] = v;
+        }
+    }
+    return NULL;
+}
+
+static void run_job(job_t* j, int threads) {
+    if (threads < 1) threads = 1;
+    if (threads > 256) threads = 256;
+    j->chunks = threads == 1 ? 1 : threads * 2;
+    if (j->chunks > j->N) j->chunks = j->N > 0 ? j->N : 1;
+    j->next = 0;
+    pthread_mutex_init(&j->lock, NULL);
+    if (threads == 1) { worker(j); pthread_mutex_destroy(&j->lock); return; }
+    pthread_t tid[256];
+    for (int t = 0; t < threads; t++) pthread_create(&tid[t], NULL, worker, j);
+    for (int t = 0; t < threads; t++) pthread_join(tid[t], NULL);
+    pthread_mutex_destroy(&j->lock);
+}
+
+void orc_matvec_q4_0(const uint8_t* w, const float* x, float* y, int K, int N, int threads) {
+    job_t j; memset(&j, 0, sizeof j);
+    j.type = ORC_Q4_0; j.K = K; j.N = N; j.w = w; j.x = x; j.y = y;
+    run_job(&j, threads);
+}
+
+void orc_matvec_q8_0(const uint8_t* w, const float* x, float* y, int K, int N, int vector_order, int threads) {
+    job_t j; memset(&j, 0, sizeof j);
+    j.type = ORC_Q8_0; j.K = K; j.N = N; j.w = w; j.x = x; j.y = y; j.vector_order = vector_order;
+    run_job(&j, threads);
+}
+
+void orc_matvec_nf4(const uint8_t* codes, const float* absmax, const float* x, float* y,
+                    int K, int N, int group_size, const float* bias, int threads) {
+    job_t j; memset(&j, 0, sizeof j);
+    j.type = ORC_NF4; j.K = K; j.N = N; j.w = codes; j.absmax = absmax; j.x = x; j.y = y;
+    j.group = group_size; j.bias = bias;
+    run_job(&j, threads);
+}
+
+void orc_matvec_f64(int type, const void* w, const float* absmax, const float* x, double* y,
+                    int K, int N, int group_size, int threads) {
+    job_t j; memset(&j, 0, sizeof j);
+    j.type = type; j.K = K; j.N = N; j.w = (const uint8_t*)w; j.absmax = absmax; j.x = x;
+    j.y64 = y; j.group = group_size;
+    run_job(&j, threads);
+}
+
+/* ------------------------------------------------------------------------ */
+float orc_vec_dot(const float* a, const float* b, int len) {   /* VO:43-55 */
+    float acc[VLANES] = {0};
+    int i = 0, bound = len - len % VLANES;
+    for (; i < bound; i += VLANES)
+        for (int l = 0; l < VLANES; l++) acc[l] = fmaf(a[i + l], b[i + l], acc[l]);
+    float r = 0.0f;
+    for (int l = 0; l < VLANES; l++) r += acc[l];
+    for (; i < len; i++) r += a[i] * b[i];
+    return r;
+}
+
+void orc_softmax(float* a, int len) {   /* VO:302-317 */
+    float max = a[0];
+    for (int i = 1; i < len; i++) if (a[i] > max) max = a[i];
+    float sum = 0.0f;
+    for (int i = 0; i < len; i++) {
+        a[i] = (float)exp((double)(a[i] - max));
+        sum += a[i];
+    }
+    float inv = 1.0f / sum;
+    for (int i = 0; i < len; i++) a[i] *= inv;
+}
+
+void orc_gqa_decode_attention(const float* q, float* out, float* scores,
+                              const float* k_cache, const float* v_cache, int stride,
+                              int kv_heads, int q_heads, int head_dim,
+                              int seq_len, int start_pos, float scale) {   /* AT:70-106 */
+    memset(out, 0, sizeof(float) * (size_t)q_heads * head_dim);
+    int active = seq_len - start_pos;
+    for (int head = 0; head < q_heads; head++) {
+        int kv_head = head / (q_heads / kv_heads);
+        const float* qh = q + (size_t)head * head_dim;
+        for (int p = start_pos; p < seq_len; p++)
+            scores[p - start_pos] = orc_vec_dot(qh, k_cache + (size_t)p * stride + (size_t)kv_head * head_dim, head_dim) * scale;
+        orc_softmax(scores, active);
+        float* oh = out + (size_t)head * head_dim;
+        for (int p = start_pos; p < seq_len; p++) {
+            const float* vr = v_cache + (size_t)p * stride + (size_t)kv_head * head_dim;
+            float s = scores[p - start_pos];
+            for (int i = 0; i < head_dim; i++) oh[i] = oh[i] + vr[i] * s;   /* VO:165-174 */
+        }
+    }
+}
+
+void orc_rms_norm(const float* x, const float* w, float* out, int len, float eps) {   /* VO:211-234 */
+    float acc[VLANES] = {0};
+    int i = 0, bound = len - len % VLANES;
+    for (; i < bound; i += VLANES)
+        for (int l = 0; l < VLANES; l++) acc[l] = fmaf(x[i + l], x[i + l], acc[l]);
+    float ss = 0.0f;
+    for (int l = 0; l < VLANES; l++) ss += acc[l];
+    for (; i < len; i++) ss += x[i] * x[i];
+    float scale = 1.0f / (float)sqrt((double)(ss / (float)len + eps));
+    for (i = 0; i < len; i++) out[i] = x[i] * scale * w[i];
+}
+
+void orc_rope(float* x, int n_heads, int head_dim, int rotary_dim, int pos, float freq_base) {   /* VO:383-440 */
+    int half = rotary_dim / 2;
+    float table[2048];
+    for (int i = 0; i < half; i++) {
+        float expo = -2.0f * (float)i / (float)rotary_dim;
+        float inv_freq = (float)pow((double)freq_base, (double)expo);
+        float theta = ((float)pos * inv_freq) / 1.0f;
+        table[i] = (float)cos((double)theta);
+        table[half + i] = (float)sin((double)theta);
+    }
+    for (int h = 0; h < n_heads; h++) {
+        float* b = x + (size_t)h * head_dim;
+        for (int i = 0; i < half; i++) {
+            float c = table[i], s = table[half + i];
+            float x0 = b[i], x1 = b[i + half];
+            b[i] = x0 * c - x1 * s;
+            b[i + half] = x0 * s + x1 * c;
+        }
+    }
+}
+
+void orc_swiglu(const float* gate, const float* up, float* dst, int len) {   /* VO:333-338 */
+    for (int i = 0; i < len; i++) {
+        float g = gate[i] / (1.0f + (float)exp(-(double)gate[i]));
+        dst[i] = g * up[i];
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+static void nf4_matvec_seq(const uint8_t* codes, const float* absmax, const float* x, float* y, int K, int N, int g) {
+    for (int r = 0; r < N; r++) y[r] = nf4_row_dot(codes, absmax, x, K, g, r);
+}
+
+void orc_decode_step_nf4(const orc_llama_cfg* c, const uint8_t* const* codes, const float* const* absmax,
+                         const float* norms, uint16_t* k_cache, uint16_t* v_cache,
+                         int token, int pos, float* x_out, float* logits) {
+    int H = c->hidden, D = c->head_dim, Hq = c->q_heads, Hkv = c->kv_heads, F = c->ffn;
+    int QD = Hq * D, KVD = Hkv * D, L = c->layers, g = c->group;
+    float* x = (float*)calloc((size_t)H, 4);
+    float* xb = (float*)calloc((size_t)(H > QD ? H : QD), 4);
+    float* q = (float*)calloc((size_t)QD, 4);
+    float* k = (float*)calloc((size_t)KVD, 4);
+    float* v = (float*)calloc((size_t)KVD, 4);
+    float* att = (float*)calloc((size_t)QD, 4);
+    float* gate = (float*)calloc((size_t)F, 4);
+    float* up = (float*)calloc((size_t)F, 4);
+    float* hb = (float*)calloc((size_t)F, 4);
+    float* scores = (float*)calloc((size_t)(pos + 1), 4);
+    float* kf = (float*)calloc((size_t)(pos + 1) * KVD, 4);
+    float* vf = (float*)calloc((size_t)(pos + 1) * KVD, 4);
+
+    /* embedding row: NF4 dequantisation of row `token` (tensor 7*L) */
+    {
+        int64_t base = (int64_t)token * H;
+        for (int k2 = 0; k2 < H; k2++) {
+            int64_t e = base + k2;
+            int b = codes[7 * L][e >> 1];
+            int code = (e & 1) ? (b & 15) : ((b >> 4) & 15);
+            x[k2] = NF4_TABLE[code] * absmax[7 * L][((e >> 1) * 2) / g];
+        }
+    }
+    float scale = (float)(1.0 / sqrt((double)D));                           /* DP:368-377 */
+    for (int l = 0; l < L; l++) {
+        const uint8_t* const* cw = codes + 7 * l;
+        const float* const* aw = absmax + 7 * l;
+        orc_rms_norm(x, norms + (size_t)l * 2 * H, xb, H, c->eps);             /* DP:305 */
+        nf4_matvec_seq(cw[0], aw[0], xb, q, H, QD, g);                           /* DP:309 */
+        nf4_matvec_seq(cw[1], aw[1], xb, k, H, KVD, g);
+        nf4_matvec_seq(cw[2], aw[2], xb, v, H, KVD, g);
+        orc_rope(q, Hq, D, D, pos, c->rope_theta);                               /* DP:333 */
+        orc_rope(k, Hkv, D, D, pos, c->rope_theta);                              /* DP:360 */
+        size_t lbase = (size_t)l * c->max_ctx * KVD;
+        for (int i = 0; i < KVD; i++) {                                          /* DP:362 */
+            k_cache[lbase + (size_t)pos * KVD + i] = orc_f32_to_bf16_rne(k[i]);
+            v_cache[lbase + (size_t)pos * KVD + i] = orc_f32_to_bf16_rne(v[i]);
+        }
+        for (size_t i = 0; i < (size_t)(pos + 1) * KVD; i++) {
+            kf[i] = bf16_to_f32(k_cache[lbase + i]);
+            vf[i] = bf16_to_f32(v_cache[lbase + i]);
+        }
+        orc_gqa_decode_attention(q, att, scores, kf, vf, KVD, Hkv, Hq, D, pos + 1, 0, scale);   /* DP:386 */
+        nf4_matvec_seq(cw[3], aw[3], att, xb, QD, H, g);                         /* DP:475 */
+        for (int i = 0; i < H; i++) x[i] += xb[i];                               /* DP:481 */
+        orc_rms_norm(x, norms + (size_t)l * 2 * H + H, xb, H, c->eps);           /* DP:485 */
+        nf4_matvec_seq(cw[4], aw[4], xb, gate, H, F, g);                         /* DP:492 */
+        nf4_matvec_seq(cw[5], aw[5], xb, up, H, F, g);
+        orc_swiglu(gate, up, hb, F);                                             /* DP:497 */
+        nf4_matvec_seq(cw[6], aw[6], hb, xb, F, H, g);                           /* DP:504 */
+        for (int i = 0; i < H; i++) x[i] += xb[i];                               /* DP:511 */
+    }
+    memcpy(x_out, x, sizeof(float) * H);
+    if (logits) {
+        orc_rms_norm(x, norms + (size_t)L * 2 * H, xb, H, c->eps);
+        nf4_matvec_seq(codes[7 * L + 1], absmax[7 * L + 1], xb, logits, H, c->vocab, g);
+    }
+    free(x); free(xb); free(q); free(k); free(v); free(att); free(gate); free(up); free(hb);
+    free(scores); free(kf); free(vf);
+}

@@ -1,0 +1,112 @@
+/*
+ * aljabr_oracle.h -- TEST INFRASTRUCTURE ONLY.
+ *
+ * CPU restatement of the reference's arithmetic for the quantized decode
+ * path (NF4 / GGUF Q4_0 / Q8_0 dequantise-and-matvec, GQA decode attention,
+ * and the decode-step glue).  It is the checker for the CUDA path and the
+ * timed CPU baseline; nothing in the product links, loads or calls it.
+ *
+ * Paths in citations are relative to the reference project root
+ * (andalus-ai/aljabr).  Abbreviations used below:
+ *   RT  = engine/gguf/aljabr-gguf-core/src/main/java/tech/kayys/aljabr/gguf/runtime
+ *   VO  = engine/gguf/aljabr-gguf-core/src/main/java/tech/kayys/aljabr/gguf/loader/tensor/GGUFVectorOps.java
+ *   GW  = engine/gguf/aljabr-gguf-core/src/main/java/tech/kayys/aljabr/gguf/writer/GGUFWriter.java
+ *   DK  = engine/safetensor/aljabr-safetensor-core/src/main/java/tech/kayys/aljabr/safetensor/core/tensor/DequantizationKernel.java
+ *   AT  = engine/gguf/aljabr-gguf-java/src/main/java/tech/kayys/aljabr/gguf/javabackend/GgufDecodeAttentionExecution.java
+ *   DP  = engine/gguf/aljabr-gguf-java/src/main/java/tech/kayys/aljabr/gguf/javabackend/GgufDecodePass.java
+ *
+ * Parity status: the GGUF and attention restatements are pinned by the
+ * reference's own known-answer tests (restated as fixtures under
+ * tests/golden/).  The NF4 fp32 GEMV half follows Apple Accelerate
+ * cblas_sgemv, which is closed and macOS-only, and the NF4 quantizer lives
+ * in an external project: both are "parity unpinned"; NF4 *dequantisation*
+ * is pinned by its in-repo table and nibble order.
+ */
+#ifndef ALJABR_ORACLE_H
+#define ALJABR_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- scalar conversions ------------------------------------------------ */
+float    orc_f16_to_f32(uint16_t half);          /* RT/GgufQuantTables.java:143-165 */
+uint16_t orc_f32_to_f16_bits(float value);       /* GW:360-387 (floatToHalfBits)   */
+int      orc_java_round(float value);            /* java.lang.Math.round(float)     */
+uint16_t orc_f32_to_bf16_rne(float value);       /* bf16 KV-cache store rounding    */
+
+/* ---- encoders (fixture generators) ------------------------------------- */
+void orc_encode_q4_0(const float* values, int64_t n, uint8_t* out);   /* GW:179-194 */
+void orc_encode_q8_0(const float* values, int64_t n, uint8_t* out);   /* GW:163-177 */
+/* Own NF4 quantizer (the reference's lives in an external project):
+ * per-group fp32 absmax, nearest codebook entry, high nibble = even index. */
+void orc_quantize_nf4(const float* values, int64_t n, int group_size,
+                      uint8_t* codes, float* absmax);
+
+/* ---- dequantisation (bit-exact targets) -------------------------------- */
+void orc_dequantize_nf4(const uint8_t* src, float* dst, const float* scales,
+                        int64_t numel, int group_size);               /* DK:84-102 */
+void orc_dequantize_q4_0(const uint8_t* blocks, float* dst, int64_t numel); /* RT/GgufBlockDequantizer.java:33-37,366-415 */
+void orc_dequantize_q8_0(const uint8_t* blocks, float* dst, int64_t numel); /* RT/GgufRowDequantizer.java:142-151 */
+
+/* ---- row dots in the reference's summation order ------------------------ */
+float orc_dot_row_q4_0(const uint8_t* row, int columns, const float* x);          /* RT/GgufQ32RawDot.java:34-67 */
+float orc_dot_row_q8_0_scalar(const uint8_t* row, int columns, const float* x);   /* RT/GgufQ8RawDot.java:138-185 */
+float orc_dot_row_q8_0_vector(const uint8_t* row, int columns, const float* x);   /* RT/GgufQ8RawDot.java:63-121 */
+
+/* ---- matvec (rows parallel over `threads` host threads, 2 chunks each) -- */
+enum { ORC_Q4_0 = 2, ORC_Q8_0 = 8, ORC_NF4 = 100 };
+void orc_matvec_q4_0(const uint8_t* w, const float* x, float* y, int K, int N, int threads);
+void orc_matvec_q8_0(const uint8_t* w, const float* x, float* y, int K, int N, int vector_order, int threads);
+/* NF4: dequantise (DK:84-102) then a plain fp32 row dot (stands in for the
+ * closed cblas_sgemv at engine/safetensor/.../AccelOps.java:444-451). */
+void orc_matvec_nf4(const uint8_t* codes, const float* absmax, const float* x, float* y,
+                    int K, int N, int group_size, const float* bias, int threads);
+/* fp64 ground truth on the dequantised weights (type = ORC_*). */
+void orc_matvec_f64(int type, const void* w, const float* absmax, const float* x, double* y,
+                    int K, int N, int group_size, int threads);
+
+/* ---- decode attention --------------------------------------------------- */
+/* AT:70-106 with VO:43-55 (dot), VO:302-317 (softmax), VO:165-174 (axpy).
+ * K/V are fp32 [position][kvHeads*headDim] with `stride` floats/position. */
+void orc_gqa_decode_attention(const float* q, float* out, float* scores,
+                              const float* k_cache, const float* v_cache, int stride,
+                              int kv_heads, int q_heads, int head_dim,
+                              int seq_len, int start_pos, float scale);
+
+/* ---- decode-step glue --------------------------------------------------- */
+float orc_vec_dot(const float* a, const float* b, int len);                      /* VO:43-55   */
+void  orc_rms_norm(const float* x, const float* w, float* out, int len, float eps); /* VO:211-234 */
+void  orc_rope(float* x, int n_heads, int head_dim, int rotary_dim, int pos, float freq_base); /* VO:383-440 */
+void  orc_swiglu(const float* gate, const float* up, float* dst, int len);       /* VO:333-338 */
+void  orc_softmax(float* a, int len);                                            /* VO:302-317 */
+
+/* One batch-1 decode step of a Llama-shaped model with NF4 linear weights,
+ * following DP:297-545 (pre-norm, q/k/v, split-half RoPE, KV store,
+ * attention, o-proj + residual, SwiGLU FFN + residual) and the logits
+ * projection.  The KV cache holds bf16 bit patterns ([layer][pos][kvH*D]);
+ * the current token's k/v are rounded to bf16 (RNE) when stored, which is
+ * the one intended deviation from the reference's fp32 cache.
+ *
+ * Weight layout per layer l (NF4, group g, row-major [N][K]):
+ *   wq [Hq*D][H], wk [Hkv*D][H], wv [Hkv*D][H], wo [H][Hq*D],
+ *   wg [F][H], wu [F][H], wd [H][F]; embedding [V][H]; lm_head [V][H].
+ * Codes/absmax of all tensors are passed as arrays of pointers in that
+ * order: 7 per layer, then embedding, then lm_head. */
+typedef struct {
+    int layers, hidden, q_heads, kv_heads, head_dim, ffn, vocab, max_ctx, group;
+    float eps, rope_theta;
+} orc_llama_cfg;
+void orc_decode_step_nf4(const orc_llama_cfg* cfg,
+                         const uint8_t* const* codes, const float* const* absmax,
+                         const float* norms,   /* [layers][2][H] (attn, ffn) then [H] output norm */
+                         uint16_t* k_cache, uint16_t* v_cache,
+                         int token, int pos, float* x_out, float* logits);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
