@@ -1,0 +1,78 @@
+// Internal (library-private) declarations shared by the .cu translation units
+// of libaljabr_blackwell.so.  The public C-ABI lives in include/aljabr_blackwell.h.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/aljabr_blackwell.h"
+
+// Bits of the device fault word.
+#define ALJ_FAULT_TIMEOUT 0x1u      // an mbarrier / flag wait ran out of its limit
+#define ALJ_FAULT_BOUNDS 0x2u       // a checked index fell outside its buffer
+
+namespace alj {
+
+enum WeightFormat : int { FMT_Q4_0 = 0, FMT_Q8_0 = 1, FMT_NF4 = 2 };
+
+// x-side prologue fused into a matvec (decode-step fusion).
+enum Prologue : int {
+    PRO_NONE = 0,
+    PRO_RMSNORM = 1,   // x' = x * rsqrt(mean(x^2) + eps) * norm_w
+    PRO_SWIGLU = 2,    // x' = silu(gate) * x
+};
+
+struct MatvecSegment {
+    const uint8_t* w;        // Q4_0 / Q8_0 blocks, or NF4 packed codes (row-major [rows][K])
+    const float* absmax;     // NF4 per-group fp32 scales, else null
+    const float* bias;       // optional, y += bias[row]
+    const float* residual;   // optional, y = residual[row] + W x (may alias y)
+    float* y;
+    int rows;
+};
+
+struct MatvecParams {
+    MatvecSegment seg[3];
+    int nseg;
+    int K;
+    int total_rows;
+    int group;               // NF4 group size
+    const float* x;
+    int prologue;
+    const float* norm_w;
+    float norm_eps;
+    const float* gate;
+};
+
+// Kernel launchers (return cudaError_t of the launch).  `pdl` enables
+// programmatic dependent launch on the stream.
+cudaError_t launch_matvec(int fmt, const MatvecParams& p, cudaStream_t stream, bool pdl);
+bool matvec_tma_supported(int fmt, int K, int group);
+
+cudaError_t launch_dequant(int fmt, float* dst, const uint8_t* src, const float* absmax, int64_t numel,
+                           int group, cudaStream_t stream);
+
+// GQA decode attention (split-K flash decoding).  kv_dtype: ALJ_KV_F32 / ALJ_KV_BF16.
+struct AttnParams {
+    float* out;              // [q_heads * head_dim]
+    const float* q;          // [q_heads * head_dim]
+    const void* k;           // cache rows [pos][stride]
+    const void* v;
+    int kv_dtype;
+    int stride;              // elements between consecutive positions
+    long long head_stride;   // elements between consecutive kv heads (head_dim for [pos][kvh][d])
+    int kv_heads, q_heads, head_dim;
+    int seq_len, start_pos;
+    float scale;
+    float* part_o;           // scratch [q_heads][splits][head_dim]
+    float* part_ml;          // scratch [q_heads][splits][2]  (running max, running sum)
+    int splits;
+};
+int attention_splits(int seq_len, int kv_heads, int sm_count);
+size_t attention_scratch_floats(int q_heads, int head_dim, int splits);
+cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl);
+
+int sm_count_for_current_device();
+
+}  // namespace alj

@@ -1,0 +1,654 @@
+// C-ABI of libaljabr_blackwell.so (declared in include/aljabr_blackwell.h):
+// per-device state, the registry of model buffers copied to HBM, host-buffer
+// staging for the Metal-shaped "tb" entry points, and argument validation.
+// No entry point falls back to the CPU: anything the kernels cannot run is
+// reported as an error code.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "aljabr_blackwell_internal.h"
+
+namespace alj {
+
+extern __device__ unsigned int g_fault_word;
+
+namespace {
+
+thread_local std::string t_last_error;
+thread_local int t_device = -1;
+thread_local bool t_pdl = false;
+int g_verbose = 0;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    if (g_verbose) fprintf(stderr, "[aljabr_blackwell] error %d: %s\n", code, buf);
+    return code;
+}
+
+#define ALJ_CUDA(expr)                                                                               \
+    do {                                                                                             \
+        cudaError_t _e = (expr);                                                                     \
+        if (_e != cudaSuccess) return fail(ALJ_ERR_CUDA, "%s: %s (%s:%d)", #expr, cudaGetErrorString(_e), \
+                                           __FILE__, __LINE__);                                      \
+    } while (0)
+
+struct Registered {
+    size_t bytes;
+    void* dev;
+};
+
+// Grow-only device / pinned host staging buffer.
+struct DevBuf {
+    void* p = nullptr;
+    size_t cap = 0;
+    cudaError_t ensure(size_t bytes) {
+        if (bytes <= cap) return cudaSuccess;
+        if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+        cudaError_t e = cudaMalloc(&p, bytes);
+        if (e == cudaSuccess) cap = bytes;
+        return e;
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+    }
+};
+struct HostBuf {
+    void* p = nullptr;
+    size_t cap = 0;
+    cudaError_t ensure(size_t bytes) {
+        if (bytes <= cap) return cudaSuccess;
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+        cap = 0;
+        cudaError_t e = cudaMallocHost(&p, bytes);
+        if (e == cudaSuccess) cap = bytes;
+        return e;
+    }
+    void release() {
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+        cap = 0;
+    }
+};
+
+struct DeviceState {
+    int device = 0;
+    int sms = 0;
+    cudaStream_t stream = nullptr;
+    std::mutex mu;                          // serialises the staging buffers of tb calls
+    std::map<uintptr_t, Registered> reg;    // host base -> HBM copy
+    std::mutex reg_mu;
+    DevBuf dx, dy, dtmp, dscratch;
+    HostBuf hx, hy;
+};
+
+std::mutex g_mu;
+std::vector<std::unique_ptr<DeviceState>> g_dev;
+
+int current_device() {
+    if (t_device >= 0) return t_device;
+    int d = 0;
+    cudaGetDevice(&d);
+    return d;
+}
+
+// State of the calling thread's device, created on first use.
+DeviceState* state(int* err) {
+    const int d = current_device();
+    std::lock_guard<std::mutex> g(g_mu);
+    if (static_cast<int>(g_dev.size()) <= d) g_dev.resize(d + 1);
+    if (!g_dev[d]) {
+        int count = 0;
+        if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+            *err = fail(ALJ_ERR_NOT_INITIALIZED, "no CUDA device visible");
+            return nullptr;
+        }
+        if (d >= count) {
+            *err = fail(ALJ_ERR_BAD_ARG, "device %d out of range (%d devices)", d, count);
+            return nullptr;
+        }
+        cudaSetDevice(d);
+        auto s = std::make_unique<DeviceState>();
+        s->device = d;
+        cudaDeviceGetAttribute(&s->sms, cudaDevAttrMultiProcessorCount, d);
+        if (cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) != cudaSuccess) {
+            *err = fail(ALJ_ERR_CUDA, "stream creation failed on device %d", d);
+            return nullptr;
+        }
+        g_dev[d] = std::move(s);
+    }
+    cudaSetDevice(d);
+    return g_dev[d].get();
+}
+
+// Map a weight pointer to device memory: a registered host address, or a
+// pointer that is already device-accessible.
+const void* resolve(DeviceState* st, const void* p) {
+    if (!p) return nullptr;
+    {
+        std::lock_guard<std::mutex> g(st->reg_mu);
+        const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+        auto it = st->reg.upper_bound(a);
+        if (it != st->reg.begin()) {
+            --it;
+            if (a - it->first < it->second.bytes) return static_cast<const uint8_t*>(it->second.dev) + (a - it->first);
+        }
+    }
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    if (attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged) return p;
+    if (attr.type == cudaMemoryTypeHost && attr.devicePointer) return attr.devicePointer;
+    return nullptr;
+}
+
+int fmt_of(int type) {
+    switch (type) {
+        case ALJ_TYPE_Q4_0: return FMT_Q4_0;
+        case ALJ_TYPE_Q8_0: return FMT_Q8_0;
+        case ALJ_TYPE_NF4: return FMT_NF4;
+    }
+    return -1;
+}
+
+int check_dims(int type, long long K, long long N) {
+    if (K <= 0 || N <= 0) return fail(ALJ_ERR_BAD_DIMS, "K=%lld N=%lld must be positive", K, N);
+    if (K > (1 << 24) || N > (1 << 28)) return fail(ALJ_ERR_BAD_DIMS, "K=%lld N=%lld too large", K, N);
+    if ((type == ALJ_TYPE_Q4_0 || type == ALJ_TYPE_Q8_0) && K % 32 != 0)
+        return fail(ALJ_ERR_BAD_DIMS, "K=%lld is not a multiple of the 32-value block", K);
+    if (fmt_of(type) < 0) return fail(ALJ_ERR_UNSUPPORTED, "weight type %d has no Blackwell kernel", type);
+    return ALJ_OK;
+}
+
+int launch_status(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return ALJ_OK;
+    if (e == cudaErrorNotSupported) return fail(ALJ_ERR_UNSUPPORTED, "%s: shape not supported", what);
+    return fail(ALJ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+cudaStream_t pick_stream(DeviceState* st, void* stream) {
+    return stream ? static_cast<cudaStream_t>(stream) : st->stream;
+}
+
+struct MatSpec {
+    int type;
+    const void* w;        // device
+    const float* absmax;  // device (NF4)
+    const float* bias;    // device
+    float* y;             // device
+    int N;
+};
+
+// One fused launch when every matrix shares the format; otherwise one per matrix.
+int run_matvecs(DeviceState* st, const MatSpec* m, int n, const float* dx, int K, int group, cudaStream_t stream,
+                bool pdl = false) {
+    bool same = true;
+    for (int i = 1; i < n; ++i) same = same && m[i].type == m[0].type;
+    if (same) {
+        MatvecParams p = {};
+        p.nseg = n;
+        p.K = K;
+        p.group = group;
+        p.x = dx;
+        for (int i = 0; i < n; ++i) {
+            p.seg[i].w = static_cast<const uint8_t*>(m[i].w);
+            p.seg[i].absmax = m[i].absmax;
+            p.seg[i].bias = m[i].bias;
+            p.seg[i].y = m[i].y;
+            p.seg[i].rows = m[i].N;
+            p.total_rows += m[i].N;
+        }
+        return launch_status(launch_matvec(fmt_of(m[0].type), p, stream, pdl), "matvec");
+    }
+    for (int i = 0; i < n; ++i) {
+        int rc = run_matvecs(st, m + i, 1, dx, K, group, stream, pdl);
+        if (rc) return rc;
+    }
+    return ALJ_OK;
+}
+
+// Host-buffer path shared by every tb entry point: stage A, run, copy C out.
+struct HostOut {
+    void* C;
+    int N;
+};
+int tb_matvec(int nmat, const int* types, const void* const* B, const float* const* absmax_host, const float* bias_host,
+              const HostOut* outs, const void* A, int K, int group, int batch) {
+    int err = 0;
+    DeviceState* st = state(&err);
+    if (!st) return err;
+    if (!A) return fail(ALJ_ERR_BAD_ARG, "A is null");
+    for (int i = 0; i < nmat; ++i) {
+        if (!outs[i].C || !B[i]) return fail(ALJ_ERR_BAD_ARG, "null C or B pointer (matrix %d)", i);
+        int rc = check_dims(types[i], K, outs[i].N);
+        if (rc) return rc;
+        if (types[i] == ALJ_TYPE_NF4 && (group <= 0 || !absmax_host[i]))
+            return fail(ALJ_ERR_BAD_ARG, "NF4 needs absmax and a positive block size");
+    }
+    MatSpec spec[3];
+    size_t ytotal = 0;
+    for (int i = 0; i < nmat; ++i) {
+        spec[i].type = types[i];
+        spec[i].w = resolve(st, B[i]);
+        if (!spec[i].w) return fail(ALJ_ERR_NOT_REGISTERED, "weight pointer %p is neither registered nor device memory", B[i]);
+        spec[i].absmax = nullptr;
+        if (types[i] == ALJ_TYPE_NF4) {
+            spec[i].absmax = static_cast<const float*>(resolve(st, absmax_host[i]));
+            if (!spec[i].absmax) return fail(ALJ_ERR_NOT_REGISTERED, "absmax pointer %p is neither registered nor device memory", absmax_host[i]);
+        }
+        spec[i].N = outs[i].N;
+        ytotal += static_cast<size_t>(outs[i].N);
+    }
+    std::lock_guard<std::mutex> g(st->mu);
+    const size_t xbytes = static_cast<size_t>(K) * batch * 4;
+    const size_t nb = nmat == 1 && bias_host ? static_cast<size_t>(outs[0].N) : 0;
+    const size_t ybytes = (ytotal * batch + nb) * 4;
+    ALJ_CUDA(st->dx.ensure(xbytes));
+    ALJ_CUDA(st->dy.ensure(ybytes));
+    ALJ_CUDA(st->hx.ensure(xbytes > (nb * 4) ? xbytes : nb * 4));
+    ALJ_CUDA(st->hy.ensure(ybytes));
+    memcpy(st->hx.p, A, xbytes);
+    ALJ_CUDA(cudaMemcpyAsync(st->dx.p, st->hx.p, xbytes, cudaMemcpyHostToDevice, st->stream));
+    float* dbias = nullptr;
+    if (nb) {
+        dbias = static_cast<float*>(st->dy.p) + ytotal * batch;
+        ALJ_CUDA(cudaStreamSynchronize(st->stream));   // hx is reused for the bias below
+        memcpy(st->hx.p, bias_host, nb * 4);
+        ALJ_CUDA(cudaMemcpyAsync(dbias, st->hx.p, nb * 4, cudaMemcpyHostToDevice, st->stream));
+    }
+    for (int b = 0; b < batch; ++b) {
+        size_t off = 0;
+        for (int i = 0; i < nmat; ++i) {
+            spec[i].y = static_cast<float*>(st->dy.p) + static_cast<size_t>(b) * ytotal + off;
+            spec[i].bias = (i == 0) ? dbias : nullptr;
+            off += static_cast<size_t>(outs[i].N);
+        }
+        int rc = run_matvecs(st, spec, nmat, static_cast<const float*>(st->dx.p) + static_cast<size_t>(b) * K, K,
+                             group, st->stream);
+        if (rc) return rc;
+    }
+    ALJ_CUDA(cudaMemcpyAsync(st->hy.p, st->dy.p, ytotal * batch * 4, cudaMemcpyDeviceToHost, st->stream));
+    ALJ_CUDA(cudaStreamSynchronize(st->stream));
+    // scatter [b][matrix][N] staging into the callers' buffers
+    for (int i = 0, off = 0; i < nmat; off += outs[i].N, ++i)
+        for (int b = 0; b < batch; ++b)
+            memcpy(static_cast<float*>(outs[i].C) + static_cast<size_t>(b) * outs[i].N,
+                   static_cast<const float*>(st->hy.p) + static_cast<size_t>(b) * ytotal + off,
+                   static_cast<size_t>(outs[i].N) * 4);
+    return ALJ_OK;
+}
+
+int tb_dequant(int type, void* dst, const void* src, const void* scales, long long numel, int group) {
+    int err = 0;
+    DeviceState* st = state(&err);
+    if (!st) return err;
+    if (!dst || !src) return fail(ALJ_ERR_BAD_ARG, "null dst or src");
+    if (numel <= 0) return fail(ALJ_ERR_BAD_DIMS, "numel=%lld must be positive", numel);
+    if (type != ALJ_TYPE_NF4 && numel % 32) return fail(ALJ_ERR_BAD_DIMS, "numel=%lld is not a multiple of 32", numel);
+    if (type == ALJ_TYPE_NF4 && (group <= 0 || !scales)) return fail(ALJ_ERR_BAD_ARG, "NF4 needs scales and group > 0");
+    const void* dsrc = resolve(st, src);
+    if (!dsrc) return fail(ALJ_ERR_NOT_REGISTERED, "src %p is neither registered nor device memory", src);
+    const float* dscale = nullptr;
+    if (type == ALJ_TYPE_NF4) {
+        dscale = static_cast<const float*>(resolve(st, scales));
+        if (!dscale) return fail(ALJ_ERR_NOT_REGISTERED, "scales %p is neither registered nor device memory", scales);
+    }
+    std::lock_guard<std::mutex> g(st->mu);
+    ALJ_CUDA(st->dtmp.ensure(static_cast<size_t>(numel) * 4));
+    int rc = launch_status(launch_dequant(fmt_of(type), static_cast<float*>(st->dtmp.p), static_cast<const uint8_t*>(dsrc),
+                                          dscale, numel, group, st->stream),
+                           "dequantize");
+    if (rc) return rc;
+    ALJ_CUDA(cudaMemcpyAsync(dst, st->dtmp.p, static_cast<size_t>(numel) * 4, cudaMemcpyDeviceToHost, st->stream));
+    ALJ_CUDA(cudaStreamSynchronize(st->stream));
+    return ALJ_OK;
+}
+
+int attn_check(const void* k, const void* v, int kv_dtype, int stride, int kv_heads, int q_heads, int head_dim,
+               int seq_len, int start_pos) {
+    if (!k || !v) return fail(ALJ_ERR_BAD_ARG, "null K or V cache");
+    if (kv_dtype != ALJ_KV_F32 && kv_dtype != ALJ_KV_BF16) return fail(ALJ_ERR_UNSUPPORTED, "kv dtype %d", kv_dtype);
+    if (kv_heads <= 0 || head_dim <= 0 || q_heads <= 0 || q_heads % kv_heads)
+        return fail(ALJ_ERR_BAD_DIMS, "query heads must be a positive multiple of KV heads");
+    if (stride < kv_heads * head_dim) return fail(ALJ_ERR_BAD_DIMS, "stride %d < kv_heads*head_dim", stride);
+    if (start_pos < 0 || start_pos >= seq_len) return fail(ALJ_ERR_BAD_DIMS, "start %d outside [0, %d)", start_pos, seq_len);
+    return ALJ_OK;
+}
+
+int run_attention(DeviceState* st, float* dout, const float* dq, const void* k, const void* v, int kv_dtype, int stride,
+                  long long head_stride, int kv_heads, int q_heads, int head_dim, int seq_len, int start_pos, float scale, cudaStream_t stream,
+                  DevBuf* scratch) {
+    AttnParams p = {};
+    p.out = dout;
+    p.q = dq;
+    p.k = k;
+    p.v = v;
+    p.kv_dtype = kv_dtype;
+    p.stride = stride;
+    p.head_stride = head_stride;
+    p.kv_heads = kv_heads;
+    p.q_heads = q_heads;
+    p.head_dim = head_dim;
+    p.seq_len = seq_len;
+    p.start_pos = start_pos;
+    p.scale = scale;
+    p.splits = attention_splits(seq_len - start_pos, kv_heads, st->sms);
+    if (p.splits > 1) {
+        ALJ_CUDA(scratch->ensure(attention_scratch_floats(q_heads, head_dim, p.splits) * 4));
+        p.part_o = static_cast<float*>(scratch->p);
+        p.part_ml = p.part_o + static_cast<size_t>(q_heads) * p.splits * head_dim;
+    }
+    return launch_status(launch_attention(p, stream, false), "decode attention");
+}
+
+}  // namespace
+
+int sm_count_for_current_device() {
+    int err = 0;
+    DeviceState* st = state(&err);
+    return st && st->sms > 0 ? st->sms : 148;
+}
+
+}  // namespace alj
+
+using namespace alj;
+
+extern "C" {
+
+int aljabr_blackwell_init(int device_id) {
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+        cudaGetLastError();
+        return fail(ALJ_ERR_NOT_INITIALIZED, "no CUDA device visible");
+    }
+    if (device_id < 0 || device_id >= count) return fail(ALJ_ERR_BAD_ARG, "device %d out of range (%d devices)", device_id, count);
+    t_device = device_id;
+    int err = 0;
+    DeviceState* st = state(&err);
+    if (!st) return err;
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device_id);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device_id);
+    if (major != 10) return fail(ALJ_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a", device_id, major, minor);
+    return ALJ_OK;
+}
+
+int aljabr_blackwell_device_count(void) {
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return count;
+}
+
+int aljabr_blackwell_device_name(int device_id, char* buf, int buf_len) {
+    if (!buf || buf_len <= 0) return fail(ALJ_ERR_BAD_ARG, "null buffer");
+    cudaDeviceProp prop;
+    ALJ_CUDA(cudaGetDeviceProperties(&prop, device_id));
+    snprintf(buf, static_cast<size_t>(buf_len), "%s", prop.name);
+    return ALJ_OK;
+}
+
+int aljabr_blackwell_compute_capability(int device_id) {
+    int major = 0, minor = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device_id) != cudaSuccess) return ALJ_ERR_CUDA;
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device_id);
+    return major * 10 + minor;
+}
+
+long long aljabr_blackwell_free_memory(void) {
+    int err = 0;
+    if (!state(&err)) return err;
+    size_t f = 0, t = 0;
+    if (cudaMemGetInfo(&f, &t) != cudaSuccess) return ALJ_ERR_CUDA;
+    return static_cast<long long>(f);
+}
+
+const char* aljabr_blackwell_last_error(void) { return t_last_error.c_str(); }
+
+int aljabr_blackwell_set_pdl(int enable) {
+    t_pdl = enable != 0;
+    return ALJ_OK;
+}
+
+void aljabr_blackwell_set_verbose(int enable) { g_verbose = enable; }
+
+int aljabr_blackwell_device_status(unsigned int* fault_bits) {
+    int err = 0;
+    DeviceState* st = state(&err);
+    if (!st) return err;
+    unsigned int v = 0, zero = 0;
+    ALJ_CUDA(cudaMemcpyFromSymbol(&v, g_fault_word, sizeof v));
+    ALJ_CUDA(cudaMemcpyToSymbol(g_fault_word, &zero, sizeof zero));
+    if (fault_bits) *fault_bits = v;
+    return v & ALJ_FAULT_TIMEOUT ? ALJ_ERR_TIMEOUT : ALJ_OK;
+}
+
+int aljabr_blackwell_shutdown(void) {
+    std::lock_guard<std::mutex> g(g_mu);
+    for (auto& s : g_dev) {
+        if (!s) continue;
+        cudaSetDevice(s->device);
+        cudaStreamSynchronize(s->stream);
+        for (auto& kv : s->reg) cudaFree(kv.second.dev);
+        s->reg.clear();
+        s->dx.release(); s->dy.release(); s->dtmp.release(); s->dscratch.release();
+        s->hx.release(); s->hy.release();
+        cudaStreamDestroy(s->stream);
+        s.reset();
+    }
+    g_dev.clear();
+    return ALJ_OK;
+}
+
+int aljabr_blackwell_register_model_buffer(const void* base_ptr, size_t total_bytes) {
+    int err = 0;
+    DeviceState* st = state(&err);
+    if (!st) return err;
+    if (!base_ptr || total_bytes == 0) return fail(ALJ_ERR_BAD_ARG, "null or empty model buffer");
+    {
+        std::lock_guard<std::mutex> g(st->reg_mu);
+        auto it = st->reg.find(reinterpret_cast<uintptr_t>(base_ptr));
+        if (it != st->reg.end()) {
+            if (it->second.bytes >= total_bytes) return ALJ_OK;
+            cudaFree(it->second.dev);
+            st->reg.erase(it);
+        }
+    }
+    void* dev = nullptr;
+    cudaError_t e = cudaMalloc(&dev, total_bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(ALJ_ERR_NO_MEMORY, "cudaMalloc(%zu) for the model buffer: %s", total_bytes, cudaGetErrorString(e));
+    }
+    e = cudaMemcpy(dev, base_ptr, total_bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(dev);
+        return fail(ALJ_ERR_CUDA, "copying the model buffer to HBM: %s", cudaGetErrorString(e));
+    }
+    std::lock_guard<std::mutex> g(st->reg_mu);
+    st->reg[reinterpret_cast<uintptr_t>(base_ptr)] = Registered{total_bytes, dev};
+    return ALJ_OK;
+}
+
+int aljabr_blackwell_unregister_model_buffer(const void* base_ptr) {
+    int err = 0;
+    DeviceState* st = state(&err);
+    if (!st) return err;
+    std::lock_guard<std::mutex> g(st->reg_mu);
+    auto it = st->reg.find(reinterpret_cast<uintptr_t>(base_ptr));
+    if (it == st->reg.end()) return fail(ALJ_ERR_NOT_REGISTERED, "buffer %p is not registered", base_ptr);
+    cudaStreamSynchronize(st->stream);
+    cudaFree(it->second.dev);
+    st->reg.erase(it);
+    return ALJ_OK;
+}
+
+void* aljabr_blackwell_device_address(const void* host_ptr) {
+    int err = 0;
+    DeviceState* st = state(&err);
+    if (!st) return nullptr;
+    return const_cast<void*>(resolve(st, host_ptr));
+}
+
+int aljabr_blackwell_matvec_tb_q4_0(void* C, const void* A, const void* B, int K, int N) {
+    const int t = ALJ_TYPE_Q4_0;
+    const void* b[1] = {B};
+    const float* am[1] = {nullptr};
+    HostOut o[1] = {{C, N}};
+    return tb_matvec(1, &t, b, am, nullptr, o, A, K, 0, 1);
+}
+
+int aljabr_blackwell_matvec_tb_q8_0(void* C, const void* A, const void* B, int K, int N) {
+    const int t = ALJ_TYPE_Q8_0;
+    const void* b[1] = {B};
+    const float* am[1] = {nullptr};
+    HostOut o[1] = {{C, N}};
+    return tb_matvec(1, &t, b, am, nullptr, o, A, K, 0, 1);
+}
+
+int aljabr_blackwell_matvec_tb_nf4(void* C, const void* A, const void* B_packed, const void* absmax, int K, int N,
+                                   int blockSize) {
+    return aljabr_blackwell_linear_nf4(C, A, B_packed, absmax, nullptr, K, N, blockSize);
+}
+
+int aljabr_blackwell_linear_nf4(void* C, const void* A, const void* B_packed, const void* absmax, const void* bias,
+                                int K, int N, int blockSize) {
+    const int t = ALJ_TYPE_NF4;
+    const void* b[1] = {B_packed};
+    const float* am[1] = {static_cast<const float*>(absmax)};
+    HostOut o[1] = {{C, N}};
+    return tb_matvec(1, &t, b, am, static_cast<const float*>(bias), o, A, K, blockSize, 1);
+}
+
+int aljabr_blackwell_matvec_tb_pair(void* C0, void* C1, const void* A, const void* B0, const void* B1, int K, int N0,
+                                    int N1, int type0, int type1) {
+    const int t[2] = {type0, type1};
+    const void* b[2] = {B0, B1};
+    const float* am[2] = {nullptr, nullptr};
+    if (type0 == ALJ_TYPE_NF4 || type1 == ALJ_TYPE_NF4) return fail(ALJ_ERR_UNSUPPORTED, "NF4 pairs need absmax: use linear_nf4");
+    HostOut o[2] = {{C0, N0}, {C1, N1}};
+    return tb_matvec(2, t, b, am, nullptr, o, A, K, 0, 1);
+}
+
+int aljabr_blackwell_matvec_tb_triple(void* C0, void* C1, void* C2, const void* A, const void* B0, const void* B1,
+                                      const void* B2, int K, int N0, int N1, int N2, int type0, int type1, int type2) {
+    const int t[3] = {type0, type1, type2};
+    const void* b[3] = {B0, B1, B2};
+    const float* am[3] = {nullptr, nullptr, nullptr};
+    if (type0 == ALJ_TYPE_NF4 || type1 == ALJ_TYPE_NF4 || type2 == ALJ_TYPE_NF4)
+        return fail(ALJ_ERR_UNSUPPORTED, "NF4 triples need absmax: use linear_nf4");
+    HostOut o[3] = {{C0, N0}, {C1, N1}, {C2, N2}};
+    return tb_matvec(3, t, b, am, nullptr, o, A, K, 0, 1);
+}
+
+int aljabr_blackwell_matvec_tb_batch(void* C, const void* A, const void* B, int K, int N, int type, int batchSize) {
+    if (batchSize <= 0) return fail(ALJ_ERR_BAD_DIMS, "batchSize=%d", batchSize);
+    if (type == ALJ_TYPE_NF4) return fail(ALJ_ERR_UNSUPPORTED, "NF4 batches need absmax: use linear_nf4");
+    const void* b[1] = {B};
+    const float* am[1] = {nullptr};
+    HostOut o[1] = {{C, N}};
+    return tb_matvec(1, &type, b, am, nullptr, o, A, K, 0, batchSize);
+}
+
+int aljabr_blackwell_dequantize_nf4(void* dst, const void* src, const void* scales, long long numel, int groupSize) {
+    return tb_dequant(ALJ_TYPE_NF4, dst, src, scales, numel, groupSize);
+}
+int aljabr_blackwell_dequantize_q4_0(void* dst, const void* blocks, long long numel) {
+    return tb_dequant(ALJ_TYPE_Q4_0, dst, blocks, nullptr, numel, 0);
+}
+int aljabr_blackwell_dequantize_q8_0(void* dst, const void* blocks, long long numel) {
+    return tb_dequant(ALJ_TYPE_Q8_0, dst, blocks, nullptr, numel, 0);
+}
+
+int aljabr_blackwell_decode_attention(float* out, const float* q, const void* k_cache, const void* v_cache, int kv_dtype,
+                                      int cache_head_stride, int kv_heads, int q_heads, int head_dim, int seq_len,
+                                      int start_pos, float scale) {
+    int err = 0;
+    DeviceState* st = state(&err);
+    if (!st) return err;
+    if (!out || !q) return fail(ALJ_ERR_BAD_ARG, "null q or out");
+    int rc = attn_check(k_cache, v_cache, kv_dtype, cache_head_stride, kv_heads, q_heads, head_dim, seq_len, start_pos);
+    if (rc) return rc;
+    const void* dk = resolve(st, k_cache);
+    const void* dv = resolve(st, v_cache);
+    if (!dk || !dv) return fail(ALJ_ERR_NOT_REGISTERED, "K/V caches must be device or registered memory");
+    std::lock_guard<std::mutex> g(st->mu);
+    const size_t n = static_cast<size_t>(q_heads) * head_dim;
+    ALJ_CUDA(st->dx.ensure(n * 4));
+    ALJ_CUDA(st->dy.ensure(n * 4));
+    ALJ_CUDA(st->hx.ensure(n * 4));
+    ALJ_CUDA(st->hy.ensure(n * 4));
+    memcpy(st->hx.p, q, n * 4);
+    ALJ_CUDA(cudaMemcpyAsync(st->dx.p, st->hx.p, n * 4, cudaMemcpyHostToDevice, st->stream));
+    rc = run_attention(st, static_cast<float*>(st->dy.p), static_cast<const float*>(st->dx.p), dk, dv, kv_dtype,
+                       cache_head_stride, head_dim, kv_heads, q_heads, head_dim, seq_len, start_pos, scale, st->stream, &st->dscratch);
+    if (rc) return rc;
+    ALJ_CUDA(cudaMemcpyAsync(st->hy.p, st->dy.p, n * 4, cudaMemcpyDeviceToHost, st->stream));
+    ALJ_CUDA(cudaStreamSynchronize(st->stream));
+    memcpy(out, st->hy.p, n * 4);
+    return ALJ_OK;
+}
+
+int aljabr_blackwell_matvec_dev(int type, float* y, const float* x, const void* w, const float* absmax, int K, int N,
+                                int group, const float* bias, void* stream) {
+    int err = 0;
+    DeviceState* st = state(&err);
+    if (!st) return err;
+    int rc = check_dims(type, K, N);
+    if (rc) return rc;
+    if (!y || !x || !w) return fail(ALJ_ERR_BAD_ARG, "null y, x or w");
+    if (type == ALJ_TYPE_NF4 && (!absmax || group <= 0)) return fail(ALJ_ERR_BAD_ARG, "NF4 needs absmax and group > 0");
+    MatSpec m = {type, w, absmax, bias, y, N};
+    return run_matvecs(st, &m, 1, x, K, group, pick_stream(st, stream), t_pdl);
+}
+
+int aljabr_blackwell_dequantize_dev(int type, float* dst, const void* src, const float* absmax, long long numel, int group,
+                                    void* stream) {
+    int err = 0;
+    DeviceState* st = state(&err);
+    if (!st) return err;
+    if (!dst || !src) return fail(ALJ_ERR_BAD_ARG, "null dst or src");
+    if (fmt_of(type) < 0) return fail(ALJ_ERR_UNSUPPORTED, "type %d", type);
+    if (numel <= 0 || (type != ALJ_TYPE_NF4 && numel % 32)) return fail(ALJ_ERR_BAD_DIMS, "numel=%lld", numel);
+    if (type == ALJ_TYPE_NF4 && (!absmax || group <= 0)) return fail(ALJ_ERR_BAD_ARG, "NF4 needs absmax and group > 0");
+    return launch_status(launch_dequant(fmt_of(type), dst, static_cast<const uint8_t*>(src), absmax, numel, group,
+                                        pick_stream(st, stream)),
+                         "dequantize");
+}
+
+int aljabr_blackwell_decode_attention_dev(float* out, const float* q, const void* k_cache, const void* v_cache,
+                                          int kv_dtype, int cache_head_stride, int kv_heads, int q_heads, int head_dim,
+                                          int seq_len, int start_pos, float scale, void* stream) {
+    int err = 0;
+    DeviceState* st = state(&err);
+    if (!st) return err;
+    if (!out || !q) return fail(ALJ_ERR_BAD_ARG, "null q or out");
+    int rc = attn_check(k_cache, v_cache, kv_dtype, cache_head_stride, kv_heads, q_heads, head_dim, seq_len, start_pos);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> g(st->mu);   // the split scratch is shared per device
+    return run_attention(st, out, q, k_cache, v_cache, kv_dtype, cache_head_stride, head_dim, kv_heads, q_heads, head_dim,
+                         seq_len, start_pos, scale, pick_stream(st, stream), &st->dscratch);
+}
+
+}  // extern "C"

@@ -1,0 +1,125 @@
+"""ctypes binding of libaljabr_blackwell.so (include/aljabr_blackwell.h).
+
+This is the same surface a Java FFM binding (BlackwellBinding) downcalls; the
+Python side exists so the parity tests and the benchmark drive exactly the
+C-ABI a JVM would.  There is no CPU fallback: if the library is missing or a
+call fails, an exception says why.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libaljabr_blackwell.so")
+HEADER_PATH = os.path.join(os.path.dirname(_HERE), "include", "aljabr_blackwell.h")
+
+ALJ_OK = 0
+ALJ_ERR_NOT_INITIALIZED = -1
+ALJ_ERR_BAD_DIMS = -2
+ALJ_ERR_UNSUPPORTED = -3
+ALJ_ERR_NOT_REGISTERED = -4
+ALJ_ERR_CUDA = -5
+ALJ_ERR_TIMEOUT = -6
+ALJ_ERR_BAD_ARG = -7
+ALJ_ERR_NO_MEMORY = -8
+
+TYPE_Q4_0 = 2
+TYPE_Q8_0 = 8
+TYPE_NF4 = 100
+KV_F32 = 0
+KV_BF16 = 1
+
+
+class ProviderError(RuntimeError):
+    """A non-zero status from the native provider (mirrors ProviderException)."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(f"aljabr_blackwell error {code}: {message}")
+        self.code = code
+
+
+class UnsupportedOperation(ProviderError):
+    """ALJ_ERR_UNSUPPORTED (mirrors UnsupportedOperationException)."""
+
+
+_p = ctypes.c_void_p
+_i = ctypes.c_int
+_ll = ctypes.c_longlong
+_f = ctypes.c_float
+_sz = ctypes.c_size_t
+
+# name -> (restype, argtypes); every symbol declared in the header is listed.
+SIGNATURES = {
+    "aljabr_blackwell_init": (_i, [_i]),
+    "aljabr_blackwell_device_count": (_i, []),
+    "aljabr_blackwell_device_name": (_i, [_i, ctypes.c_char_p, _i]),
+    "aljabr_blackwell_compute_capability": (_i, [_i]),
+    "aljabr_blackwell_free_memory": (_ll, []),
+    "aljabr_blackwell_last_error": (ctypes.c_char_p, []),
+    "aljabr_blackwell_set_verbose": (None, [_i]),
+    "aljabr_blackwell_device_status": (_i, [ctypes.POINTER(ctypes.c_uint)]),
+    "aljabr_blackwell_shutdown": (_i, []),
+    "aljabr_blackwell_set_pdl": (_i, [_i]),
+    "aljabr_blackwell_register_model_buffer": (_i, [_p, _sz]),
+    "aljabr_blackwell_unregister_model_buffer": (_i, [_p]),
+    "aljabr_blackwell_device_address": (_p, [_p]),
+    "aljabr_blackwell_matvec_tb_q4_0": (_i, [_p, _p, _p, _i, _i]),
+    "aljabr_blackwell_matvec_tb_q8_0": (_i, [_p, _p, _p, _i, _i]),
+    "aljabr_blackwell_matvec_tb_nf4": (_i, [_p, _p, _p, _p, _i, _i, _i]),
+    "aljabr_blackwell_linear_nf4": (_i, [_p, _p, _p, _p, _p, _i, _i, _i]),
+    "aljabr_blackwell_matvec_tb_pair": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i]),
+    "aljabr_blackwell_matvec_tb_triple": (_i, [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i]),
+    "aljabr_blackwell_matvec_tb_batch": (_i, [_p, _p, _p, _i, _i, _i, _i]),
+    "aljabr_blackwell_dequantize_nf4": (_i, [_p, _p, _p, _ll, _i]),
+    "aljabr_blackwell_dequantize_q4_0": (_i, [_p, _p, _ll]),
+    "aljabr_blackwell_dequantize_q8_0": (_i, [_p, _p, _ll]),
+    "aljabr_blackwell_decode_attention": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _f]),
+    "aljabr_blackwell_matvec_dev": (_i, [_i, _p, _p, _p, _p, _i, _i, _i, _p, _p]),
+    "aljabr_blackwell_dequantize_dev": (_i, [_i, _p, _p, _p, _ll, _i, _p]),
+    "aljabr_blackwell_decode_attention_dev": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _p]),
+}
+
+
+def header_symbols() -> list[str]:
+    """Every function the public header declares (parsed from the header text)."""
+    with open(HEADER_PATH) as f:
+        text = f.read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(aljabr_blackwell_\w+)\s*\(", text)))
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load the native library (built in-tree by aljabr_b200.build)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ProviderError(ALJ_ERR_NOT_INITIALIZED,
+                                f"{LIB_PATH} is missing: run `python -m aljabr_b200.build` (nvcc, sm_100a)")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    msg = lib().aljabr_blackwell_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(rc: int) -> int:
+    if rc != ALJ_OK:
+        cls = UnsupportedOperation if rc == ALJ_ERR_UNSUPPORTED else ProviderError
+        raise cls(rc, last_error())
+    return rc
+
+
+def call(name: str, *args) -> int:
+    return check(getattr(lib(), name)(*args))

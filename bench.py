@@ -1,0 +1,505 @@
+"""Benchmark of the quantized-decode hot path on B200.
+
+Headline (BASELINE.json metric "NF4/Q4_0 matvec HBM GB/s"; workload = its
+configs[1]): GGUF Q4_0 dequantise-and-matvec at the Llama FFN shapes.  One
+step = one up/gate matvec (14336 x 4096) plus one down matvec (4096 x 14336),
+batch 1, fp32 activations.  Weights rotate through a pool of independent
+matrices larger than twice the L2 cache, so every launch streams from HBM.
+
+  value   = algorithmic bytes (weights + x + y) / device time, whole job
+            (N ranks each run the same per-GPU workload: weak scaling)
+  e2e     = same metric through the host-buffer C-ABI call
+            (aljabr_blackwell_matvec_tb_q4_0: H2D of x, kernel, D2H of y)
+  roofline= the Q4_0 kernel's achieved GB/s vs the measured HBM peak
+
+Also reported under "extra": NF4 4096x4096, Q8_0 one Llama-3-8B
+layer and GQA decode attention (Hq 32, Hkv 8, D 128, ctx 4096).
+
+`--impl reference` times the CPU implementation of the same path: the C
+restatement of the reference's Java row kernels (the Java reference cannot
+run on these hosts: no JDK), over all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+UP_N, UP_K = 14336, 4096
+DOWN_N, DOWN_K = 4096, 14336
+Q4_BLOCK = 18
+
+
+def q4_bytes(n, k):
+    return n * (k // 32) * Q4_BLOCK
+
+
+STEP_BYTES = (q4_bytes(UP_N, UP_K) + 4 * UP_K + 4 * UP_N) + (q4_bytes(DOWN_N, DOWN_K) + 4 * DOWN_K + 4 * DOWN_N)
+WORKLOAD = "GGUF Q4_0 dequant-matvec, Llama FFN shapes: up/gate 14336x4096 + down 4096x14336, batch 1"
+METRIC = "Q4_0 dequant-matvec HBM GB/s (Llama FFN shapes, batch 1)"
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def load_traffic(name):
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f).get(name)
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- our arm
+def run_ours(args, rank, world, local_rank):
+    import ctypes
+
+    import torch
+
+    import oracle
+    from aljabr_b200 import native
+
+    torch.cuda.set_device(local_rank)
+    native.call("aljabr_blackwell_init", local_rank)
+    native.call("aljabr_blackwell_set_pdl", 0 if args.no_pdl else 1)   # weights are static here
+    dev = torch.device("cuda", local_rank)
+    L = native.lib()
+    props = torch.cuda.get_device_properties(local_rank)
+    l2 = getattr(props, "L2_cache_size", 126 * 2 ** 20) or 126 * 2 ** 20
+
+    # ---- synthetic pool: distinct matrices, total > 2 x L2 -------------------
+    g = np.random.default_rng(20260101 + rank)
+    base_up = oracle.encode_q4_0(g.normal(0, 0.02, size=(UP_N, UP_K)).astype(np.float32))
+    base_dn = oracle.encode_q4_0(g.normal(0, 0.02, size=(DOWN_N, DOWN_K)).astype(np.float32))
+    pair_bytes = base_up.nbytes + base_dn.nbytes
+    pool = max(3, int(np.ceil(2.5 * l2 / pair_bytes)))
+    up_d, dn_d = [], []
+    t_up = torch.from_numpy(base_up).to(dev)
+    t_dn = torch.from_numpy(base_dn).to(dev)
+    for i in range(pool):
+        # distinct contents per slot: XOR the code bytes (scales untouched)
+        u = t_up.clone()
+        d = t_dn.clone()
+        if i:
+            u.view(-1, 18)[:, 2:] ^= (i * 37) & 0xFF
+            d.view(-1, 18)[:, 2:] ^= (i * 53) & 0xFF
+        up_d.append(u)
+        dn_d.append(d)
+    xs_up = [torch.randn(UP_K, device=dev) for _ in range(pool)]
+    xs_dn = [torch.randn(DOWN_K, device=dev) for _ in range(pool)]
+    ys_up = [torch.empty(UP_N, device=dev) for _ in range(pool)]
+    ys_dn = [torch.empty(DOWN_N, device=dev) for _ in range(pool)]
+    stream = torch.cuda.Stream(device=dev)
+    sh = ctypes.c_void_p(stream.cuda_stream)
+
+    def step(i):
+        j = i % pool
+        native.check(L.aljabr_blackwell_matvec_dev(native.TYPE_Q4_0, ys_up[j].data_ptr(), xs_up[j].data_ptr(),
+                                                   up_d[j].data_ptr(), None, UP_K, UP_N, 0, None, sh))
+        native.check(L.aljabr_blackwell_matvec_dev(native.TYPE_Q4_0, ys_dn[j].data_ptr(), xs_dn[j].data_ptr(),
+                                                   dn_d[j].data_ptr(), None, DOWN_K, DOWN_N, 0, None, sh))
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    # Launches are recorded into CUDA graphs (chunks of steps replayed back to
+    # back) so the host's launch rate does not bound the device timeline.
+    chunk = graph_chunk(args.steps)
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+    torch.cuda.synchronize(dev)
+    graph = capture(torch, stream, lambda: [step(i) for i in range(chunk)])
+    replays = args.steps // chunk
+    graph.replay()                      # one untimed replay: graph upload
+    torch.cuda.synchronize(dev)
+
+    # ---- timed region: K steps, device time by CUDA events on the stream -----
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local_rank) as clk:
+        start.record(stream)
+        for _ in range(replays):
+            graph.replay()
+        end.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    ms = start.elapsed_time(end)
+    ms_max = ms
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms_max = float(t.item())
+    per_launch_ms = ms / (2 * args.steps)
+
+    # correctness spot check of the timed kernels (slot 0, oracle as checker)
+    y_chk = ys_up[0].cpu().numpy()
+    x_chk = xs_up[0].cpu().numpy()
+    ref = oracle.matvec_q4_0(up_d[0].cpu().numpy(), x_chk, UP_N, threads=os.cpu_count() or 8)
+    err = float(np.max(np.abs(y_chk - ref) / np.maximum(np.abs(ref), 1e-3 * np.abs(ref).max())))
+
+    # ---- e2e: host buffers through the Metal-shaped C-ABI ---------------------
+    e2e = None
+    if rank == 0 or world > 1:
+        host_up = [base_up] + [None]
+        model_up = np.ascontiguousarray(base_up)
+        model_dn = np.ascontiguousarray(base_dn)
+        native.call("aljabr_blackwell_register_model_buffer", ctypes.c_void_p(model_up.ctypes.data), model_up.nbytes)
+        native.call("aljabr_blackwell_register_model_buffer", ctypes.c_void_p(model_dn.ctypes.data), model_dn.nbytes)
+        hx_up = np.random.default_rng(1).normal(size=UP_K).astype(np.float32)
+        hx_dn = np.random.default_rng(2).normal(size=DOWN_K).astype(np.float32)
+        hy_up = np.empty(UP_N, np.float32)
+        hy_dn = np.empty(DOWN_N, np.float32)
+
+        def e2e_step():
+            native.check(L.aljabr_blackwell_matvec_tb_q4_0(hy_up.ctypes.data, hx_up.ctypes.data,
+                                                           ctypes.c_void_p(model_up.ctypes.data), UP_K, UP_N))
+            native.check(L.aljabr_blackwell_matvec_tb_q4_0(hy_dn.ctypes.data, hx_dn.ctypes.data,
+                                                           ctypes.c_void_p(model_dn.ctypes.data), DOWN_K, DOWN_N))
+
+        for _ in range(max(3, args.warmup)):
+            e2e_step()
+        e2e_steps = min(args.steps, 2000)
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            e2e_step()
+        t1 = time.perf_counter()
+        barrier()
+        e2e_s = t1 - t0
+        if world > 1:
+            t = torch.tensor([e2e_s], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            e2e_s = float(t.item())
+        e2e = {"value": round(STEP_BYTES * e2e_steps * world / e2e_s / 1e9, 2), "unit": "GB/s", "steps": e2e_steps,
+               "h2d_bytes_per_step": 4 * (UP_K + DOWN_K), "d2h_bytes_per_step": 4 * (UP_N + DOWN_N),
+               "timer": "host wall clock around the blocking C-ABI calls (weights registered, HBM-resident)",
+               "host_api": "aljabr_blackwell_matvec_tb_q4_0"}
+        del host_up
+        native.call("aljabr_blackwell_unregister_model_buffer", ctypes.c_void_p(model_up.ctypes.data))
+        native.call("aljabr_blackwell_unregister_model_buffer", ctypes.c_void_p(model_dn.ctypes.data))
+
+    extra = {}
+    if not args.no_extra:
+        extra = run_extra(args, dev, stream, sh, l2)
+
+    bits = ctypes.c_uint(0)
+    native.check(L.aljabr_blackwell_device_status(ctypes.byref(bits)))
+
+    peak, peak_kind = load_peaks()
+    achieved = (STEP_BYTES / 2) / (per_launch_ms * 1e-3) / 1e9
+    value = STEP_BYTES * args.steps * world / (ms_max * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 codes, fp16 scales -> f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "batch": 1, "weights": "N(0,0.02) -> GGUF Q4_0 (GGUFWriter.encodeQ4_0)",
+                   "x": "N(0,1) fp32", "pool_matrices": 2 * pool, "pool_bytes": pool * pair_bytes,
+                   "l2_bytes": l2, "l2_policy": "inputs larger than L2: weights rotate through a pool > 2x L2",
+                   "parallelism": f"independent replicas x{world} (rows of each matrix on one GPU)",
+                   "launch": "CUDA graphs of 500 steps" + ("" if args.no_pdl else ", programmatic dependent launch")},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                     "traffic": load_traffic("q4_0_matvec"),
+                     "kernel": "matvec_tma_kernel<Q4_0> (avg of 14336x4096 and 4096x14336 launches)",
+                     "algorithmic_bytes_per_launch": STEP_BYTES // 2},
+        "gpu_launches": 2 * args.steps,
+        "e2e": e2e,
+        "parity": {"max_rel_err_vs_oracle": err, "tolerance": 1e-3},
+        "device_fault_bits": bits.value,
+        "clocks": clk.summary(),
+        "extra": extra,
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args, 8.0)
+    return line
+
+
+def graph_chunk(steps: int) -> int:
+    """Largest divisor of `steps` that is at most 500 (steps per graph)."""
+    for c in range(min(500, steps), 0, -1):
+        if steps % c == 0:
+            return c
+    return 1
+
+
+def capture(torch, stream, record):
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        record()
+    return g
+
+
+def run_extra(args, dev, stream, sh, l2):
+    """Secondary configs, each with its own pool > 2 x L2 and device timing."""
+    import torch
+
+    import oracle
+    from aljabr_b200 import native
+
+    L = native.lib()
+    out = {}
+    reps = 200
+
+    def timed(fn, n):
+        """Device ms per call: n calls captured in one graph, replayed 3x."""
+        with torch.cuda.stream(stream):
+            for i in range(3):
+                fn(i)
+        torch.cuda.synchronize(dev)
+        gr = capture(torch, stream, lambda: [fn(i) for i in range(n)])
+        gr.replay()
+        torch.cuda.synchronize(dev)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for _ in range(3):
+            gr.replay()
+        e.record(stream)
+        torch.cuda.synchronize(dev)
+        return s.elapsed_time(e) / (3 * n)
+
+    # NF4 4096 x 4096, block 64
+    N = K = 4096
+    g = np.random.default_rng(7)
+    codes, absmax = oracle.quantize_nf4(g.normal(0, 0.02, size=(N, K)).astype(np.float32), 64)
+    per = codes.nbytes + absmax.nbytes
+    pool = max(2, int(np.ceil(2.5 * l2 / per)))
+    cd = torch.from_numpy(codes).to(dev)
+    ad = torch.from_numpy(absmax).to(dev)
+    cs = [cd.clone() for _ in range(pool)]
+    ams = [ad.clone() for _ in range(pool)]
+    xs = [torch.randn(K, device=dev) for _ in range(pool)]
+    ys = [torch.empty(N, device=dev) for _ in range(pool)]
+    with torch.cuda.stream(stream):
+        ms = timed(lambda i: native.check(L.aljabr_blackwell_matvec_dev(
+            native.TYPE_NF4, ys[i % pool].data_ptr(), xs[i % pool].data_ptr(), cs[i % pool].data_ptr(),
+            ctypes_ptr(ams[i % pool]), K, N, 64, None, sh)), reps * 4)
+    alg = per + 4 * K + 4 * N
+    out["nf4_matvec_4096x4096_b64"] = {"GB/s": round(alg / (ms * 1e-3) / 1e9, 1), "us_per_launch": round(ms * 1e3, 3),
+                                       "algorithmic_bytes": alg, "pool": pool}
+    del cs, ams
+
+    # Q8_0: one Llama-3-8B layer's projections
+    shapes = [("q", 4096, 4096), ("k", 1024, 4096), ("v", 1024, 4096), ("o", 4096, 4096),
+              ("gate", 14336, 4096), ("up", 14336, 4096), ("down", 4096, 14336)]
+    mats = {}
+    for name, n, k in shapes:
+        mats[name] = torch.from_numpy(oracle.encode_q8_0(g.normal(0, 0.02, size=(n, k)).astype(np.float32))).to(dev)
+    layer_w = sum(m.numel() for m in mats.values())
+    pool8 = max(2, int(np.ceil(2.5 * l2 / layer_w)))
+    layers = [{k2: v.clone() for k2, v in mats.items()} for _ in range(pool8)]
+    xq = {k: torch.randn(kk, device=dev) for k, _, kk in shapes}
+    yq = {k: torch.empty(n, device=dev) for k, n, _ in shapes}
+
+    def q8_layer(i):
+        lay = layers[i % pool8]
+        for name, n, k in shapes:
+            native.check(L.aljabr_blackwell_matvec_dev(native.TYPE_Q8_0, yq[name].data_ptr(), xq[name].data_ptr(),
+                                                       lay[name].data_ptr(), None, k, n, 0, None, sh))
+    with torch.cuda.stream(stream):
+        ms = timed(q8_layer, reps)
+    alg = layer_w + sum(4 * (n + k) for _, n, k in shapes)
+    out["q8_0_llama3_8b_layer"] = {"GB/s": round(alg / (ms * 1e-3) / 1e9, 1), "us_per_layer": round(ms * 1e3, 3),
+                                   "launches_per_layer": len(shapes), "weight_bytes": layer_w}
+    del layers
+
+    # GQA decode attention, Hq 32 / Hkv 8 / D 128, ctx 4096, bf16 KV
+    Hq, Hkv, D, ctx = 32, 8, 128, 4096
+    kvb = ctx * Hkv * D * 2
+    poola = max(2, int(np.ceil(2.5 * l2 / (2 * kvb))))
+    ks = [torch.randn(ctx, Hkv * D, device=dev).to(torch.bfloat16) for _ in range(poola)]
+    vs = [torch.randn(ctx, Hkv * D, device=dev).to(torch.bfloat16) for _ in range(poola)]
+    q = torch.randn(Hq * D, device=dev)
+    o = torch.empty(Hq * D, device=dev)
+    with torch.cuda.stream(stream):
+        ms = timed(lambda i: native.check(L.aljabr_blackwell_decode_attention_dev(
+            o.data_ptr(), q.data_ptr(), ks[i % poola].data_ptr(), vs[i % poola].data_ptr(), native.KV_BF16,
+            Hkv * D, Hkv, Hq, D, ctx, 0, 1.0 / 128 ** 0.5, sh)), reps * 4)
+    alg = 2 * kvb + 8 * Hq * D
+    out["gqa_decode_attention_ctx4096_bf16"] = {"GB/s": round(alg / (ms * 1e-3) / 1e9, 1),
+                                                "us_per_call": round(ms * 1e3, 3), "algorithmic_bytes": alg,
+                                                "launches_per_call": 2}
+    return out
+
+
+def ctypes_ptr(t):
+    import ctypes
+    return ctypes.c_void_p(t.data_ptr())
+
+
+# ----------------------------------------------------------------- CPU legs
+def cpu_baseline(args, seconds: float):
+    """The C restatement of the reference's Q4_0 row kernels
+    (GgufQ32RawDot.dotRowQ4_0 with GgufRows' 2-chunks-per-thread split) on
+    the host cores, over a bounded sample of the same workload."""
+    import oracle
+    threads = os.cpu_count() or 1
+    g = np.random.default_rng(99)
+    up = oracle.encode_q4_0(g.normal(0, 0.02, size=(UP_N, UP_K)).astype(np.float32))
+    dn = oracle.encode_q4_0(g.normal(0, 0.02, size=(DOWN_N, DOWN_K)).astype(np.float32))
+    xu = g.normal(size=UP_K).astype(np.float32)
+    xd = g.normal(size=DOWN_K).astype(np.float32)
+    oracle.matvec_q4_0(up, xu, UP_N, threads=threads)
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        oracle.matvec_q4_0(up, xu, UP_N, threads=threads)
+        oracle.matvec_q4_0(dn, xd, DOWN_N, threads=threads)
+        n += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(STEP_BYTES * n / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} up+down step(s) of the headline workload in {dt:.1f} s "
+                      "(C restatement of GgufQ32RawDot.dotRowQ4_0, rows in 2 chunks per thread)"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    import oracle
+    oracle.build()
+    threads = os.cpu_count() or 1
+    g = np.random.default_rng(99)
+    up = oracle.encode_q4_0(g.normal(0, 0.02, size=(UP_N, UP_K)).astype(np.float32))
+    dn = oracle.encode_q4_0(g.normal(0, 0.02, size=(DOWN_N, DOWN_K)).astype(np.float32))
+    xu = g.normal(size=UP_K).astype(np.float32)
+    xd = g.normal(size=DOWN_K).astype(np.float32)
+    for _ in range(args.warmup):
+        oracle.matvec_q4_0(up, xu, UP_N, threads=threads)
+        oracle.matvec_q4_0(dn, xd, DOWN_N, threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.matvec_q4_0(up, xu, UP_N, threads=threads)
+        oracle.matvec_q4_0(dn, xd, DOWN_N, threads=threads)
+    dt = time.perf_counter() - t0
+    v = STEP_BYTES * args.steps / dt / 1e9
+    sample = (f"{args.steps} steps of the headline workload (one up 14336x4096 + one down 4096x14336 Q4_0 "
+              f"matvec each) on {threads} host threads")
+    return {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "q4_0 codes, fp16 scales -> f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "batch": 1},
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": sample,
+                             "note": "C restatement of the reference's Java CPU kernels; the Java reference "
+                                     "itself cannot run here (no JDK on these hosts)"},
+            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-extra", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-pdl", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    if world > 1:
+        import datetime
+
+        import torch
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local_rank))
+    line = run_ours(args, rank, world, local_rank)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,172 @@
+/*
+ * aljabr_blackwell.h -- C-ABI of libaljabr_blackwell.so, the B200 (sm_100a)
+ * provider for Aljabr's quantized decode path.
+ *
+ * This is the native library that the reference's Blackwell FFM binding
+ * loads (backend/blackwell/aljabr-kernel-blackwell/src/main/java/tech/kayys/
+ * aljabr/blackwell/binding/BlackwellBinding.java:52-78 names the library
+ * and its `aljabr_blackwell_*` symbols; the source it expects under
+ * src/main/cpp/blackwell does not exist in the reference).  The matvec and
+ * model-buffer entry points keep the shapes of the Metal provider's C API
+ * (backend/metal/aljabr-backend-metal/src/main/cpp/metal/
+ * aljabr_metal_matvec_api.h), so GgufExecutionDispatcher's bridge can call
+ * either provider the same way.
+ *
+ * Conventions
+ *  - Every entry point returns int: 0 on success, a negative ALJ_ERR_* code
+ *    otherwise (the Metal API's 0 / negative convention), with a message in
+ *    aljabr_blackwell_last_error() for the calling thread.  Nothing falls
+ *    back to the CPU: an unsupported type or shape is an error.
+ *  - "tb" (host-buffer) entry points take host float buffers for the
+ *    activation A and the result C, exactly like aljabr_metal_matvec_tb_*.
+ *    The weight pointer B is a host address inside a buffer previously given
+ *    to aljabr_blackwell_register_model_buffer (the mmap'd GGUF file), which
+ *    the library copied to HBM once; a device pointer is accepted as well.
+ *    They block until C is written.
+ *  - "_dev" entry points take device pointers for everything and are
+ *    stream-ordered (stream = cudaStream_t, NULL = the library's stream for
+ *    the current device); they do not synchronize.
+ *  - Weight layouts: Q4_0 and Q8_0 are ggml blocks (GgmlType ids 2 and 8,
+ *    18 and 34 bytes per 32 values; element j of a Q4_0 block is the low
+ *    nibble of code byte j, element j+16 the high nibble).  NF4 is the
+ *    safetensors/bitsandbytes layout of DequantizationKernel.java:84-102:
+ *    two codes per byte, high nibble first, one fp32 absmax per
+ *    `block_size` consecutive elements of the flattened [N][K] tensor.
+ *  - Threads: calls are thread-safe; each thread uses the device made
+ *    current by aljabr_blackwell_init (default 0).
+ */
+#ifndef ALJABR_BLACKWELL_H
+#define ALJABR_BLACKWELL_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (negative; mirrors the Metal provider's convention) ---- */
+#define ALJ_OK                  0
+#define ALJ_ERR_NOT_INITIALIZED (-1)
+#define ALJ_ERR_BAD_DIMS        (-2)
+#define ALJ_ERR_UNSUPPORTED     (-3)   /* no kernel for this type / shape     */
+#define ALJ_ERR_NOT_REGISTERED  (-4)   /* B is neither registered nor device  */
+#define ALJ_ERR_CUDA            (-5)
+#define ALJ_ERR_TIMEOUT         (-6)   /* a device-side bounded wait gave up  */
+#define ALJ_ERR_BAD_ARG         (-7)   /* null pointer, bad alignment, range  */
+#define ALJ_ERR_NO_MEMORY       (-8)
+
+/* ---- weight type ids (GgmlType.java ids; NF4 has no ggml id) ------------ */
+#define ALJ_TYPE_Q4_0 2
+#define ALJ_TYPE_Q8_0 8
+#define ALJ_TYPE_NF4  100
+
+/* ---- KV-cache element types --------------------------------------------- */
+#define ALJ_KV_F32  0   /* the reference's fp32 cache (KVCache.java:22-23)  */
+#define ALJ_KV_BF16 1   /* bf16 cache (half the bytes)                      */
+
+/* ---- lifecycle (BlackwellBinding.java:52-78 names) ----------------------- */
+/* Select `device_id` for the calling thread and create its state.  Replaces
+ * the binding's FN_INIT ("aljabr_blackwell_init"). */
+int aljabr_blackwell_init(int device_id);
+/* Number of CUDA devices (FN_DEVICE_COUNT). */
+int aljabr_blackwell_device_count(void);
+/* Device name into buf (FN_DEVICE_NAME); returns 0 or an error. */
+int aljabr_blackwell_device_name(int device_id, char* buf, int buf_len);
+/* major*10+minor, e.g. 100 for B200 (FN_COMPUTE_CAP). */
+int aljabr_blackwell_compute_capability(int device_id);
+/* Free device memory in bytes for the current device (FN_FREE_MEM). */
+long long aljabr_blackwell_free_memory(void);
+/* Message for the last failing call on this thread ("" if none). */
+const char* aljabr_blackwell_last_error(void);
+/* Verbose diagnostics to stderr (aljabr_metal_set_verbose). */
+void aljabr_blackwell_set_verbose(int enable);
+/* Read and clear the device fault word (bit 0: a bounded wait timed out). */
+int aljabr_blackwell_device_status(unsigned int* fault_bits);
+/* Release every buffer and stream the library holds on every device. */
+int aljabr_blackwell_shutdown(void);
+/* Programmatic dependent launch for the stream-ordered (_dev) calls of this
+ * thread (default off).  When on, a matvec may begin streaming its weights
+ * while the previous kernel on the same stream is still running; it still
+ * waits for that kernel before reading x or writing y.  Only enable it when
+ * weight buffers are not written by the kernel immediately preceding a call
+ * (true for weights loaded once, as in a decode loop). */
+int aljabr_blackwell_set_pdl(int enable);
+
+/* ---- model buffers (aljabr_metal_buffers.h:15) ---------------------------- */
+/* Copy [base, base+bytes) to HBM once; later calls may pass host pointers
+ * inside this range as weight pointers.  Re-registering the same base is a
+ * no-op. */
+int aljabr_blackwell_register_model_buffer(const void* base_ptr, size_t total_bytes);
+int aljabr_blackwell_unregister_model_buffer(const void* base_ptr);
+/* Device address that a registered host address maps to (NULL if none). */
+void* aljabr_blackwell_device_address(const void* host_ptr);
+
+/* ---- host-buffer matvec, y = W x (aljabr_metal_matvec_api.h:56-95) -------- */
+/* Replaces GgufTensorOps.matVecParallel for Q4_0 (GgufQ32RawDot.dotRowQ4_0,
+ * engine/gguf/aljabr-gguf-core/.../runtime/GgufQ32RawDot.java:34-67).
+ * C: float[N] (host), A: float[K] (host), B: N rows of K/32 Q4_0 blocks. */
+int aljabr_blackwell_matvec_tb_q4_0(void* C, const void* A, const void* B, int K, int N);
+/* Q8_0 (GgufQ8RawDot.dotRowQ8_0, .../runtime/GgufQ8RawDot.java:40-50);
+ * same shape as aljabr_metal_matvec_tb_q8_0. */
+int aljabr_blackwell_matvec_tb_q8_0(void* C, const void* A, const void* B, int K, int N);
+/* NF4: AccelOps.linear's dequantise-then-sgemv for M == 1
+ * (engine/safetensor/.../tensor/AccelOps.java:392-451); same shape as
+ * aljabr_metal_matvec_tb_nf4.  absmax: float[N*K/blockSize]. */
+int aljabr_blackwell_matvec_tb_nf4(void* C, const void* A, const void* B_packed, const void* absmax,
+                                   int K, int N, int blockSize);
+/* NF4 with an optional bias (AccelOps.java:465-467); bias may be NULL. */
+int aljabr_blackwell_linear_nf4(void* C, const void* A, const void* B_packed, const void* absmax,
+                                const void* bias, int K, int N, int blockSize);
+/* Two / three projections of one input (GgufExecutionDispatcher
+ * dispatchMatVecPair / dispatchMatVecTriple, GgufExecutionDispatcher.java:37-55;
+ * aljabr_metal_matvec_tb_pair / _triple).  typeN: ALJ_TYPE_Q4_0 / Q8_0. */
+int aljabr_blackwell_matvec_tb_pair(void* C0, void* C1, const void* A, const void* B0, const void* B1,
+                                    int K, int N0, int N1, int type0, int type1);
+int aljabr_blackwell_matvec_tb_triple(void* C0, void* C1, void* C2, const void* A, const void* B0,
+                                      const void* B1, const void* B2, int K, int N0, int N1, int N2,
+                                      int type0, int type1, int type2);
+/* batchSize inputs A[b][K] -> C[b][N] (dispatchMatVecBatch,
+ * GgufExecutionDispatcher.java:57-72; aljabr_metal_matvec_tb_batch). */
+int aljabr_blackwell_matvec_tb_batch(void* C, const void* A, const void* B, int K, int N, int type,
+                                     int batchSize);
+
+/* ---- host-buffer dequantisation (bit-exact with the reference) ----------- */
+/* DequantizationKernel.dequantizeNf4(src, dst, scales, numel, groupSize),
+ * .../tensor/DequantizationKernel.java:84-102.  dst: float[numel] host. */
+int aljabr_blackwell_dequantize_nf4(void* dst, const void* src, const void* scales, long long numel,
+                                    int groupSize);
+/* GgufBlockDequantizer.dequantizeQ4_0Block over numel/32 blocks
+ * (.../runtime/GgufBlockDequantizer.java:33-37). */
+int aljabr_blackwell_dequantize_q4_0(void* dst, const void* blocks, long long numel);
+/* Q8_0 rows (.../runtime/GgufRowDequantizer.java:142-151). */
+int aljabr_blackwell_dequantize_q8_0(void* dst, const void* blocks, long long numel);
+
+/* ---- GQA decode attention ------------------------------------------------ */
+/* GgufDecodeAttentionExecution.execute(query, output, scores, keyCache,
+ * valueCache, cacheHeadStride, kvHeads, queryHeads, headDimension,
+ * sequenceLength, startPosition, scale)
+ * (engine/gguf/aljabr-gguf-java/.../javabackend/GgufDecodeAttentionExecution.java:70-106).
+ * out, q: host float[q_heads*head_dim]; k_cache, v_cache: device or
+ * registered memory, rows of `cache_head_stride` elements per position of
+ * type kv_dtype.  Attends positions [start_pos, seq_len). */
+int aljabr_blackwell_decode_attention(float* out, const float* q, const void* k_cache, const void* v_cache,
+                                      int kv_dtype, int cache_head_stride, int kv_heads, int q_heads,
+                                      int head_dim, int seq_len, int start_pos, float scale);
+
+/* ---- device-pointer, stream-ordered variants ----------------------------- */
+/* y[N] = W x (+ bias); type ALJ_TYPE_*; absmax/group only for NF4. */
+int aljabr_blackwell_matvec_dev(int type, float* y, const float* x, const void* w, const float* absmax,
+                                int K, int N, int group, const float* bias, void* stream);
+int aljabr_blackwell_dequantize_dev(int type, float* dst, const void* src, const float* absmax,
+                                    long long numel, int group, void* stream);
+int aljabr_blackwell_decode_attention_dev(float* out, const float* q, const void* k_cache,
+                                          const void* v_cache, int kv_dtype, int cache_head_stride,
+                                          int kv_heads, int q_heads, int head_dim, int seq_len,
+                                          int start_pos, float scale, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ALJABR_BLACKWELL_H */

@@ -1,0 +1,46 @@
+"""Seeded synthetic inputs with the BASELINE configs' distributions
+(weights N(0, 0.02), activations N(0, 1)); used by tests and smoke."""
+from __future__ import annotations
+
+import numpy as np
+
+import oracle
+
+
+def rng(seed: int):
+    return np.random.default_rng(seed)
+
+
+def weights(seed: int, n: int, k: int, std: float = 0.02) -> np.ndarray:
+    return rng(seed).normal(0.0, std, size=(n, k)).astype(np.float32)
+
+
+def activation(seed: int, k: int) -> np.ndarray:
+    return rng(seed).normal(0.0, 1.0, size=k).astype(np.float32)
+
+
+def q4_0(seed: int, n: int, k: int) -> np.ndarray:
+    return oracle.encode_q4_0(weights(seed, n, k))
+
+
+def q8_0(seed: int, n: int, k: int) -> np.ndarray:
+    return oracle.encode_q8_0(weights(seed, n, k))
+
+
+def nf4(seed: int, n: int, k: int, group: int = 64):
+    return oracle.quantize_nf4(weights(seed, n, k), group)
+
+
+def max_rel_err(got, ref) -> float:
+    """max_i |got_i - ref_i| / max(|ref_i|, 1e-3 * max|ref|): the north-star
+    metric (element-wise relative error, guarded where ref_i is near zero)."""
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    floor = 1e-3 * max(np.abs(ref).max(), 1e-30)
+    return float(np.max(np.abs(got - ref) / np.maximum(np.abs(ref), floor)))
+
+
+def normwise_rel_err(got, ref) -> float:
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    return float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30))
