@@ -43,7 +43,8 @@ def build(force: bool = False, verbose_ptxas: bool = False) -> str:
     if not force and not _stale():
         return LIB
     nvcc = os.environ.get("NVCC", "nvcc")
-    cmd = [nvcc, *NVCC_FLAGS, *(["-Xptxas", "-v"] if verbose_ptxas else []), *sources(), "-o", LIB + ".tmp"]
+    cmd = [nvcc, *NVCC_FLAGS, *(["-Xptxas", "-v"] if verbose_ptxas else []), *sources(), "-o", LIB + ".tmp",
+           "-ldl"]
     subprocess.check_call(cmd)
     os.replace(LIB + ".tmp", LIB)
     return LIB

@@ -68,6 +68,7 @@ struct AttnParams {
     float* part_o;           // scratch [q_heads][splits][head_dim]
     float* part_ml;          // scratch [q_heads][splits][2]  (running max, running sum)
     int splits;
+    const int* dev_pos;      // if set, seq_len = *dev_pos + 1 is read on the device (graph replay)
 };
 int attention_splits(int seq_len, int kv_heads, int sm_count);
 size_t attention_scratch_floats(int q_heads, int head_dim, int splits);

@@ -86,7 +86,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_split_kernel(const AttnP
     const int kvh = blockIdx.x;
     const int split = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int active = p.seq_len - p.start_pos;
+    const int seq_len = p.dev_pos ? *p.dev_pos + 1 : p.seq_len;
+    const int active = seq_len - p.start_pos;
     const int c0 = p.start_pos + static_cast<int>(static_cast<long long>(active) * split / p.splits);
     const int c1 = p.start_pos + static_cast<int>(static_cast<long long>(active) * (split + 1) / p.splits);
 
@@ -182,7 +183,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_split_kernel(const AttnP
         }
         const int qh = kvh * G + g;
         if (p.splits == 1) {
-            p.out[qh * D + d] = acc / L;
+            p.out[qh * D + d] = L > 0.0f ? acc / L : 0.0f;
         } else {
             p.part_o[(static_cast<long long>(qh) * p.splits + split) * D + d] = acc;
             if (d == 0) {
@@ -354,7 +355,7 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl)
         if (e != cudaSuccess || p.splits == 1) return e;
         return launch_pdl(attn_combine_kernel, dim3(p.q_heads), dim3(128), 0, stream, pdl, p);
     }
-    if (active > kMaxFallbackPositions) return cudaErrorNotSupported;
+    if (p.dev_pos || active > kMaxFallbackPositions) return cudaErrorNotSupported;
     const size_t smem = static_cast<size_t>(active) * sizeof(float);
     auto kern = p.kv_dtype == ALJ_KV_BF16 ? attn_fallback_kernel<ALJ_KV_BF16> : attn_fallback_kernel<ALJ_KV_F32>;
     if (smem > 48 * 1024) {

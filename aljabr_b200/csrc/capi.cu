@@ -368,6 +368,14 @@ int sm_count_for_current_device() {
     return st && st->sms > 0 ? st->sms : 148;
 }
 
+int decode_fail(int code, const char* msg) { return fail(code, "%s", msg); }
+
+const void* decode_resolve(const void* p) {
+    int err = 0;
+    DeviceState* st = state(&err);
+    return st ? resolve(st, p) : nullptr;
+}
+
 }  // namespace alj
 
 using namespace alj;

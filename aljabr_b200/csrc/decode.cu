@@ -1,0 +1,651 @@
+// Full batch-1 decode step of a Llama-shaped model with NF4 linear weights,
+// resident in HBM and replayed as one CUDA graph per token.  This is the
+// device-resident counterpart of the reference's per-layer loop
+// (engine/gguf/aljabr-gguf-java/.../GgufDecodePass.java:297-545) and of the
+// Metal provider's registered-layer decode step (aljabr_metal_matvec_api.h:
+// aljabr_metal_register_decode_layer / aljabr_metal_decode_step_token).
+//
+// Per layer (one GPU): fused q/k/v matvec with the RMSNorm prologue -> RoPE +
+// KV store -> split-K attention (+ combine) -> o-proj with the residual add
+// in its epilogue -> gate/up pair with the RMSNorm prologue -> down-proj
+// with the SwiGLU prologue and the residual epilogue.  Seven launches per
+// layer, chained with programmatic dependent launch inside the graph.
+//
+// Tensor parallelism (2/4/8 GPUs, one process or thread per GPU): every
+// weight is row-sharded (the caller passes each rank's contiguous row
+// block); attention is local to the rank's heads; output slices are joined
+// with ncclAllGather (attention output, o-proj output, SwiGLU output,
+// down-proj output, logits), captured in the same graph.
+#include "common.cuh"
+
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <array>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <vector>
+
+namespace alj {
+namespace {
+
+// ------------------------------------------------------------------ NCCL
+// NCCL is bound at run time, the first time a tensor-parallel model is
+// created, so that loading this library never pins a libnccl.so.2 version
+// into the process.  If the host process already loaded NCCL (for example
+// through its ML framework), that copy is used; otherwise the system one.
+struct NcclApi {
+    bool tried = false, ok = false;
+    ncclResult_t (*getUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*commInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*allGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
+};
+NcclApi g_nccl;
+std::mutex g_nccl_mu;
+
+bool nccl_load() {
+    std::lock_guard<std::mutex> g(g_nccl_mu);
+    if (g_nccl.tried) return g_nccl.ok;
+    g_nccl.tried = true;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return false;
+    g_nccl.getUniqueId = reinterpret_cast<decltype(g_nccl.getUniqueId)>(dlsym(h, "ncclGetUniqueId"));
+    g_nccl.commInitRank = reinterpret_cast<decltype(g_nccl.commInitRank)>(dlsym(h, "ncclCommInitRank"));
+    g_nccl.allGather = reinterpret_cast<decltype(g_nccl.allGather)>(dlsym(h, "ncclAllGather"));
+    g_nccl.commDestroy = reinterpret_cast<decltype(g_nccl.commDestroy)>(dlsym(h, "ncclCommDestroy"));
+    g_nccl.ok = g_nccl.getUniqueId && g_nccl.commInitRank && g_nccl.allGather && g_nccl.commDestroy;
+    return g_nccl.ok;
+}
+
+// ------------------------------------------------------------------ kernels
+__global__ void embed_nf4_kernel(float* x, const uint8_t* codes, const float* absmax, const int* io, int H, int group) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const long long base = static_cast<long long>(io[1]) * H;   // io = {pos, token}
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < H; i += gridDim.x * blockDim.x) {
+        const long long e = base + i;
+        const int b = codes[e >> 1];
+        const int code = (e & 1) ? (b & 15) : (b >> 4);
+        x[i] = __fmul_rn(nf4_value(code), absmax[((e >> 1) * 2) / group]);
+    }
+}
+
+// Split-half RoPE (GGUFVectorOps.rope, GGUFVectorOps.java:383-440, with the
+// angle table computed as the reference does: pow/cos/sin in double, cast to
+// float) on the rank's q and k heads, then the KV store at `pos`
+// (GgufKvCacheWriteExecution.storeToken).
+__global__ void rope_store_kernel(float* q, float* k, const float* v, void* kc, void* vc, const int* io, int hq,
+                                  int hkv, int D, float theta, int kv_dtype) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int pos = io[0];
+    const int half = D / 2;
+    const int stride = hkv * D;
+    const int pairs = (hq + hkv) * half;
+    for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < pairs; idx += gridDim.x * blockDim.x) {
+        const int head = idx / half, i = idx - head * half;
+        const float expo = __fdiv_rn(-2.0f * static_cast<float>(i), static_cast<float>(D));
+        const float inv = static_cast<float>(pow(static_cast<double>(theta), static_cast<double>(expo)));
+        const float ang = __fmul_rn(static_cast<float>(pos), inv);
+        const float c = static_cast<float>(cos(static_cast<double>(ang)));
+        const float s = static_cast<float>(sin(static_cast<double>(ang)));
+        float* b = head < hq ? q + head * D : k + (head - hq) * D;
+        const float x0 = b[i], x1 = b[i + half];
+        const float r0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+        const float r1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+        b[i] = r0;
+        b[i + half] = r1;
+        if (head >= hq) {
+            const long long off = static_cast<long long>(pos) * stride + (head - hq) * D + i;
+            if (kv_dtype == ALJ_KV_BF16) {
+                static_cast<__nv_bfloat16*>(kc)[off] = __float2bfloat16_rn(r0);
+                static_cast<__nv_bfloat16*>(kc)[off + half] = __float2bfloat16_rn(r1);
+            } else {
+                static_cast<float*>(kc)[off] = r0;
+                static_cast<float*>(kc)[off + half] = r1;
+            }
+        }
+    }
+    for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < stride; idx += gridDim.x * blockDim.x) {
+        const long long off = static_cast<long long>(pos) * stride + idx;
+        if (kv_dtype == ALJ_KV_BF16) static_cast<__nv_bfloat16*>(vc)[off] = __float2bfloat16_rn(v[idx]);
+        else static_cast<float*>(vc)[off] = v[idx];
+    }
+}
+
+__global__ void add_kernel(float* x, const float* d, int n) {
+    pdl_launch_dependents();
+    pdl_wait();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) x[i] = x[i] + d[i];
+}
+
+// GGUFVectorOps.swiGLU (GGUFVectorOps.java:333-338): silu(g) * u.
+__global__ void swiglu_kernel(float* h, const float* gate, const float* up, int n) {
+    pdl_launch_dependents();
+    pdl_wait();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float g = gate[i];
+        h[i] = g / (1.0f + expf(-g)) * up[i];
+    }
+}
+
+// Greedy hand-off inside the graph: the step's argmax becomes the next
+// step's token, the position advances, and the token is logged at `pos`.
+__global__ void advance_kernel(int* io, int* tokens, int max_ctx) {
+    pdl_launch_dependents();
+    pdl_wait();
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+        const int pos = io[0];
+        if (pos >= 0 && pos < max_ctx) tokens[pos] = io[2];
+        io[1] = io[2];
+        io[0] = pos + 1 < max_ctx ? pos + 1 : max_ctx - 1;
+    }
+}
+
+// First index of the maximum logit (greedy sampling).
+__global__ void argmax_kernel(const float* logits, int n, int* out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = logits[i];
+        if (v > best) { best = v; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = best; si[threadIdx.x >> 5] = bi; }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        const int nw = blockDim.x >> 5;
+        best = threadIdx.x < nw ? sv[threadIdx.x] : -INFINITY;
+        bi = threadIdx.x < nw ? si[threadIdx.x] : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+        }
+        if (threadIdx.x == 0) *out = bi == 0x7fffffff ? 0 : bi;
+    }
+}
+
+template <typename... Args, typename... Actual>
+cudaError_t launch_small(void (*kernel)(Args...), int grid, int block, cudaStream_t s, Actual... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+// ------------------------------------------------------------------ model
+struct Nf4 {
+    const uint8_t* codes = nullptr;
+    const float* absmax = nullptr;
+};
+
+enum { W_Q = 0, W_K, W_V, W_O, W_GATE, W_UP, W_DOWN, W_COUNT };
+
+struct DecodeModel {
+    int device = 0;
+    int layers, H, Hq, Hkv, D, F, V, max_ctx, group, kv_dtype;
+    float eps, theta;
+    int T = 1, rank = 0;
+    int hq, hkv, f, h, v;              // this rank's shard sizes
+    std::vector<std::array<Nf4, W_COUNT>> w;
+    std::vector<bool> layer_set;
+    Nf4 embd, head;
+    bool output_set = false;
+    float* norms = nullptr;            // [layers][2][H] then [H]
+    void *kc = nullptr, *vc = nullptr; // [layers][max_ctx][hkv*D]
+    float *x, *q, *k, *vv, *att_l, *att, *delta_l, *delta, *gate, *up, *h_l, *hh, *logits_l, *logits, *scratch;
+    float* act_base = nullptr;
+    int* io = nullptr;                 // device {pos, token, argmax}
+    int* tokens = nullptr;             // device [max_ctx]: greedy token emitted at each position
+    int* host_io = nullptr;            // pinned
+    float* host_logits = nullptr;      // pinned
+    int splits = 1;
+    cudaStream_t stream = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    int steps_run = 0;
+    ncclComm_t comm = nullptr;
+    std::mutex mu;
+
+    size_t kv_elem() const { return kv_dtype == ALJ_KV_BF16 ? 2 : 4; }
+    size_t kv_layer_elems() const { return static_cast<size_t>(max_ctx) * hkv * D; }
+};
+
+std::mutex g_models_mu;
+std::map<unsigned long long, std::unique_ptr<DecodeModel>> g_models;
+unsigned long long g_next_handle = 1;
+
+DecodeModel* find(unsigned long long h) {
+    std::lock_guard<std::mutex> g(g_models_mu);
+    auto it = g_models.find(h);
+    return it == g_models.end() ? nullptr : it->second.get();
+}
+
+cudaError_t matvec(const DecodeModel& m, const Nf4* ws, float* const* ys, const int* rows, int n, const float* x, int K,
+                   int prologue, const float* norm_w, const float* gate, const float* residual) {
+    MatvecParams p = {};
+    p.nseg = n;
+    p.K = K;
+    p.group = m.group;
+    p.x = x;
+    p.prologue = prologue;
+    p.norm_w = norm_w;
+    p.norm_eps = m.eps;
+    p.gate = gate;
+    for (int i = 0; i < n; ++i) {
+        p.seg[i].w = ws[i].codes;
+        p.seg[i].absmax = ws[i].absmax;
+        p.seg[i].y = ys[i];
+        p.seg[i].rows = rows[i];
+        p.seg[i].residual = residual;
+        p.total_rows += rows[i];
+    }
+    return launch_matvec(FMT_NF4, p, m.stream, true);
+}
+
+#define REC(expr)                                  \
+    do {                                           \
+        cudaError_t _e = (expr);                   \
+        if (_e != cudaSuccess) return _e;          \
+    } while (0)
+#define RECN(expr)                                             \
+    do {                                                       \
+        if ((expr) != ncclSuccess) return cudaErrorUnknown;    \
+    } while (0)
+
+// Enqueue one full decode step on m.stream (eagerly or under capture).
+cudaError_t record_step(DecodeModel& m) {
+    const int D = m.D;
+    const int sms = sm_count_for_current_device();
+    REC(launch_small(embed_nf4_kernel, (m.H + 255) / 256, 256, m.stream, m.x, m.embd.codes, m.embd.absmax,
+                     static_cast<const int*>(m.io), m.H, m.group));
+    for (int l = 0; l < m.layers; ++l) {
+        const auto& w = m.w[l];
+        const float* attn_norm = m.norms + static_cast<size_t>(l) * 2 * m.H;
+        const float* ffn_norm = attn_norm + m.H;
+        void* kc = static_cast<uint8_t*>(m.kc) + static_cast<size_t>(l) * m.kv_layer_elems() * m.kv_elem();
+        void* vc = static_cast<uint8_t*>(m.vc) + static_cast<size_t>(l) * m.kv_layer_elems() * m.kv_elem();
+        {   // q, k, v (GgufDecodePass.java:305-309)
+            const Nf4 ws[3] = {w[W_Q], w[W_K], w[W_V]};
+            float* ys[3] = {m.q, m.k, m.vv};
+            const int rows[3] = {m.hq * D, m.hkv * D, m.hkv * D};
+            REC(matvec(m, ws, ys, rows, 3, m.x, m.H, PRO_RMSNORM, attn_norm, nullptr, nullptr));
+        }
+        // RoPE on q and k, KV store (GgufDecodePass.java:333-362)
+        REC(launch_small(rope_store_kernel, std::max(1, ((m.hq + m.hkv) * D / 2 + 255) / 256), 256, m.stream, m.q,
+                         m.k, static_cast<const float*>(m.vv), kc, vc, static_cast<const int*>(m.io), m.hq, m.hkv, D,
+                         m.theta, m.kv_dtype));
+        {   // attention (GgufDecodePass.java:368-389)
+            AttnParams a = {};
+            a.out = m.T > 1 ? m.att_l : m.att;
+            a.q = m.q;
+            a.k = kc;
+            a.v = vc;
+            a.kv_dtype = m.kv_dtype;
+            a.stride = m.hkv * D;
+            a.head_stride = D;
+            a.kv_heads = m.hkv;
+            a.q_heads = m.hq;
+            a.head_dim = D;
+            a.seq_len = m.max_ctx;
+            a.start_pos = 0;
+            a.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)));
+            a.splits = m.splits;
+            a.part_o = m.scratch;
+            a.part_ml = m.scratch + static_cast<size_t>(m.hq) * m.splits * D;
+            a.dev_pos = m.io;
+            REC(launch_attention(a, m.stream, true));
+        }
+        if (m.T > 1) RECN(g_nccl.allGather(m.att_l, m.att, static_cast<size_t>(m.hq) * D, ncclFloat, m.comm, m.stream));
+        {   // o-proj + residual (GgufDecodePass.java:475-481)
+            const Nf4 ws[1] = {w[W_O]};
+            float* ys[1] = {m.T > 1 ? m.delta_l : m.x};
+            const int rows[1] = {m.h};
+            REC(matvec(m, ws, ys, rows, 1, m.att, m.Hq * D, PRO_NONE, nullptr, nullptr, m.T > 1 ? nullptr : m.x));
+        }
+        if (m.T > 1) {
+            RECN(g_nccl.allGather(m.delta_l, m.delta, m.h, ncclFloat, m.comm, m.stream));
+            REC(launch_small(add_kernel, (m.H + 255) / 256, 256, m.stream, m.x, static_cast<const float*>(m.delta), m.H));
+        }
+        {   // gate / up (GgufDecodePass.java:485-492)
+            const Nf4 ws[2] = {w[W_GATE], w[W_UP]};
+            float* ys[2] = {m.gate, m.up};
+            const int rows[2] = {m.f, m.f};
+            REC(matvec(m, ws, ys, rows, 2, m.x, m.H, PRO_RMSNORM, ffn_norm, nullptr, nullptr));
+        }
+        {   // SwiGLU + down-proj + residual (GgufDecodePass.java:497-511)
+            const Nf4 ws[1] = {w[W_DOWN]};
+            if (m.T > 1) {
+                REC(launch_small(swiglu_kernel, (m.f + 255) / 256, 256, m.stream, m.h_l,
+                                 static_cast<const float*>(m.gate), static_cast<const float*>(m.up), m.f));
+                RECN(g_nccl.allGather(m.h_l, m.hh, m.f, ncclFloat, m.comm, m.stream));
+                float* ys[1] = {m.delta_l};
+                const int rows[1] = {m.h};
+                REC(matvec(m, ws, ys, rows, 1, m.hh, m.F, PRO_NONE, nullptr, nullptr, nullptr));
+                RECN(g_nccl.allGather(m.delta_l, m.delta, m.h, ncclFloat, m.comm, m.stream));
+                REC(launch_small(add_kernel, (m.H + 255) / 256, 256, m.stream, m.x, static_cast<const float*>(m.delta),
+                                 m.H));
+            } else {
+                float* ys[1] = {m.x};
+                const int rows[1] = {m.h};
+                REC(matvec(m, ws, ys, rows, 1, m.up, m.F, PRO_SWIGLU, nullptr, m.gate, m.x));
+            }
+        }
+    }
+    {   // output norm + logits (GgufLogitsProcessor.compute)
+        const Nf4 ws[1] = {m.head};
+        float* ys[1] = {m.T > 1 ? m.logits_l : m.logits};
+        const int rows[1] = {m.v};
+        REC(matvec(m, ws, ys, rows, 1, m.x, m.H, PRO_RMSNORM, m.norms + static_cast<size_t>(m.layers) * 2 * m.H, nullptr,
+                   nullptr));
+    }
+    if (m.T > 1) RECN(g_nccl.allGather(m.logits_l, m.logits, m.v, ncclFloat, m.comm, m.stream));
+    REC(launch_small(argmax_kernel, 1, 1024, m.stream, static_cast<const float*>(m.logits), m.V, m.io + 2));
+    REC(launch_small(advance_kernel, 1, 32, m.stream, m.io, m.tokens, m.max_ctx));
+    (void)sms;
+    return cudaSuccess;
+}
+
+// Enqueue n steps: the first ever step runs eagerly (NCCL connects there),
+// later ones replay the captured graph.  No synchronisation.
+cudaError_t enqueue_steps(DecodeModel& m, int n) {
+    for (int i = 0; i < n; ++i) {
+        cudaError_t e = cudaSuccess;
+        if (m.steps_run == 0) {
+            e = record_step(m);
+        } else {
+            if (!m.exec) {
+                cudaGraph_t graph = nullptr;
+                e = cudaStreamBeginCapture(m.stream, cudaStreamCaptureModeThreadLocal);
+                if (e == cudaSuccess) {
+                    cudaError_t rec = record_step(m);
+                    e = cudaStreamEndCapture(m.stream, &graph);
+                    if (rec != cudaSuccess) e = rec;
+                }
+                if (e == cudaSuccess) e = cudaGraphInstantiate(&m.exec, graph, 0);
+                if (graph) cudaGraphDestroy(graph);
+            }
+            if (e == cudaSuccess) e = cudaGraphLaunch(m.exec, m.stream);
+        }
+        if (e != cudaSuccess) return e;
+        m.steps_run++;
+    }
+    return cudaSuccess;
+}
+
+void destroy(DecodeModel* m) {
+    cudaSetDevice(m->device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    if (m->exec) cudaGraphExecDestroy(m->exec);
+    if (m->comm) g_nccl.commDestroy(m->comm);
+    cudaFree(m->kc);
+    cudaFree(m->vc);
+    cudaFree(m->act_base);
+    cudaFree(m->norms);
+    cudaFree(m->io);
+    cudaFree(m->tokens);
+    cudaFreeHost(m->host_io);
+    cudaFreeHost(m->host_logits);
+    if (m->stream) cudaStreamDestroy(m->stream);
+}
+
+}  // namespace
+
+// Helpers shared with capi.cu.
+int decode_fail(int code, const char* msg);
+const void* decode_resolve(const void* p);
+
+}  // namespace alj
+
+using namespace alj;
+
+extern "C" {
+
+int aljabr_blackwell_nccl_unique_id(void* out, int out_len) {
+    if (!out || out_len < static_cast<int>(sizeof(ncclUniqueId))) return decode_fail(ALJ_ERR_BAD_ARG, "need a 128-byte buffer");
+    if (!nccl_load()) return decode_fail(ALJ_ERR_UNSUPPORTED, "libnccl.so.2 could not be loaded");
+    ncclUniqueId id;
+    if (g_nccl.getUniqueId(&id) != ncclSuccess) return decode_fail(ALJ_ERR_CUDA, "ncclGetUniqueId failed");
+    memcpy(out, &id, sizeof id);
+    return ALJ_OK;
+}
+
+int aljabr_blackwell_decode_model_create(const int* dims, float eps, float rope_theta, int tp_world, int tp_rank,
+                                         const void* nccl_id, unsigned long long* handle) {
+    if (!dims || !handle) return decode_fail(ALJ_ERR_BAD_ARG, "null dims or handle");
+    auto m = std::make_unique<DecodeModel>();
+    cudaGetDevice(&m->device);
+    m->layers = dims[0]; m->H = dims[1]; m->Hq = dims[2]; m->Hkv = dims[3]; m->D = dims[4];
+    m->F = dims[5]; m->V = dims[6]; m->max_ctx = dims[7]; m->group = dims[8]; m->kv_dtype = dims[9];
+    m->eps = eps;
+    m->theta = rope_theta;
+    m->T = tp_world < 1 ? 1 : tp_world;
+    m->rank = tp_rank;
+    const int T = m->T;
+    if (m->layers <= 0 || m->H <= 0 || m->Hq <= 0 || m->Hkv <= 0 || m->D <= 0 || m->F <= 0 || m->V <= 0 ||
+        m->max_ctx <= 0 || m->Hq % m->Hkv)
+        return decode_fail(ALJ_ERR_BAD_DIMS, "invalid model dimensions");
+    if (m->Hkv % T || m->Hq % T || m->F % T || m->H % T || m->V % T || tp_rank < 0 || tp_rank >= T)
+        return decode_fail(ALJ_ERR_BAD_DIMS, "heads, hidden, ffn and vocab must divide by the TP world size");
+    if (m->H % 256 || m->F % 256 || (m->Hq * m->D) % 256 || !matvec_tma_supported(FMT_NF4, m->H, m->group) ||
+        !matvec_tma_supported(FMT_NF4, m->F, m->group) || !matvec_tma_supported(FMT_NF4, m->Hq * m->D, m->group))
+        return decode_fail(ALJ_ERR_UNSUPPORTED, "decode step needs hidden, ffn, heads*head_dim multiples of 256 and NF4 group 64/128");
+    if (m->kv_dtype != ALJ_KV_BF16 && m->kv_dtype != ALJ_KV_F32) return decode_fail(ALJ_ERR_UNSUPPORTED, "kv dtype");
+    const int G = m->Hq / m->Hkv;
+    if (!(m->D == 64 || m->D == 128 || m->D == 256) || !(G == 1 || G == 2 || G == 4 || G == 8))
+        return decode_fail(ALJ_ERR_UNSUPPORTED, "decode attention needs head_dim 64/128/256 and group 1/2/4/8");
+    if (m->D / 32 * (32 / G) > 64 || (G * m->D / 32) > 32)
+        return decode_fail(ALJ_ERR_UNSUPPORTED, "decode attention register budget exceeded for this head_dim/group");
+    m->hq = m->Hq / T; m->hkv = m->Hkv / T; m->f = m->F / T; m->h = m->H / T; m->v = m->V / T;
+    m->w.resize(m->layers);
+    m->layer_set.assign(m->layers, false);
+    m->splits = attention_splits(m->max_ctx, m->hkv, sm_count_for_current_device());
+
+    auto ok = [&](cudaError_t e) { return e == cudaSuccess; };
+    const size_t kvb = static_cast<size_t>(m->layers) * m->kv_layer_elems() * m->kv_elem();
+    const size_t acts = static_cast<size_t>(m->H) + m->hq * m->D + 2 * m->hkv * m->D + m->hq * m->D + m->Hq * m->D +
+                        m->h + m->H + 2 * m->f + m->f + m->F + m->v + m->V +
+                        attention_scratch_floats(m->hq, m->D, m->splits) + 64;
+    if (!ok(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking)) || !ok(cudaMalloc(&m->kc, kvb)) ||
+        !ok(cudaMalloc(&m->vc, kvb)) || !ok(cudaMalloc(&m->act_base, acts * 4)) ||
+        !ok(cudaMalloc(&m->norms, (static_cast<size_t>(m->layers) * 2 + 1) * m->H * 4)) ||
+        !ok(cudaMalloc(&m->io, 4 * sizeof(int))) || !ok(cudaMallocHost(&m->host_io, 4 * sizeof(int))) ||
+        !ok(cudaMalloc(&m->tokens, static_cast<size_t>(m->max_ctx) * sizeof(int))) ||
+        !ok(cudaMallocHost(&m->host_logits, static_cast<size_t>(m->V) * 4))) {
+        cudaGetLastError();
+        destroy(m.get());
+        return decode_fail(ALJ_ERR_NO_MEMORY, "allocating the decode model's KV cache / activations failed");
+    }
+    cudaMemsetAsync(m->kc, 0, kvb, m->stream);
+    cudaMemsetAsync(m->vc, 0, kvb, m->stream);
+    cudaMemsetAsync(m->act_base, 0, acts * 4, m->stream);
+    float* p = m->act_base;
+    auto take = [&](size_t n) { float* r = p; p += (n + 3) / 4 * 4; return r; };
+    m->x = take(m->H); m->q = take(m->hq * m->D); m->k = take(m->hkv * m->D); m->vv = take(m->hkv * m->D);
+    m->att_l = take(m->hq * m->D); m->att = take(m->Hq * m->D); m->delta_l = take(m->h); m->delta = take(m->H);
+    m->gate = take(m->f); m->up = take(m->f); m->h_l = take(m->f); m->hh = take(m->F);
+    m->logits_l = take(m->v); m->logits = take(m->V);
+    m->scratch = take(attention_scratch_floats(m->hq, m->D, m->splits));
+    if (T > 1) {
+        if (!nccl_id) { destroy(m.get()); return decode_fail(ALJ_ERR_BAD_ARG, "TP > 1 needs an NCCL unique id"); }
+        if (!nccl_load()) { destroy(m.get()); return decode_fail(ALJ_ERR_UNSUPPORTED, "libnccl.so.2 could not be loaded"); }
+        ncclUniqueId id;
+        memcpy(&id, nccl_id, sizeof id);
+        if (g_nccl.commInitRank(&m->comm, T, id, tp_rank) != ncclSuccess) {
+            m->comm = nullptr;
+            destroy(m.get());
+            return decode_fail(ALJ_ERR_CUDA, "ncclCommInitRank failed");
+        }
+    }
+    if (!ok(cudaStreamSynchronize(m->stream))) { destroy(m.get()); return decode_fail(ALJ_ERR_CUDA, "model init failed"); }
+    std::lock_guard<std::mutex> g(g_models_mu);
+    *handle = g_next_handle++;
+    g_models[*handle] = std::move(m);
+    return ALJ_OK;
+}
+
+int aljabr_blackwell_register_decode_layer(unsigned long long handle, int layer, const void* const* codes,
+                                           const void* const* absmax, const float* attn_norm, const float* ffn_norm) {
+    DecodeModel* m = find(handle);
+    if (!m) return decode_fail(ALJ_ERR_BAD_ARG, "unknown decode model handle");
+    if (layer < 0 || layer >= m->layers) return decode_fail(ALJ_ERR_BAD_DIMS, "layer index out of range");
+    if (!codes || !absmax || !attn_norm || !ffn_norm) return decode_fail(ALJ_ERR_BAD_ARG, "null layer pointer");
+    std::lock_guard<std::mutex> g(m->mu);
+    cudaSetDevice(m->device);
+    for (int i = 0; i < W_COUNT; ++i) {
+        m->w[layer][i].codes = static_cast<const uint8_t*>(decode_resolve(codes[i]));
+        m->w[layer][i].absmax = static_cast<const float*>(decode_resolve(absmax[i]));
+        if (!m->w[layer][i].codes || !m->w[layer][i].absmax)
+            return decode_fail(ALJ_ERR_NOT_REGISTERED, "layer weights must be device or registered memory");
+    }
+    float* dst = m->norms + static_cast<size_t>(layer) * 2 * m->H;
+    if (cudaMemcpy(dst, attn_norm, m->H * 4, cudaMemcpyDefault) != cudaSuccess ||
+        cudaMemcpy(dst + m->H, ffn_norm, m->H * 4, cudaMemcpyDefault) != cudaSuccess)
+        return decode_fail(ALJ_ERR_CUDA, "copying layer norms failed");
+    m->layer_set[layer] = true;
+    if (m->exec) { cudaGraphExecDestroy(m->exec); m->exec = nullptr; }
+    return ALJ_OK;
+}
+
+int aljabr_blackwell_register_output(unsigned long long handle, const void* embd_codes, const void* embd_absmax,
+                                     const void* head_codes, const void* head_absmax, const float* output_norm) {
+    DecodeModel* m = find(handle);
+    if (!m) return decode_fail(ALJ_ERR_BAD_ARG, "unknown decode model handle");
+    if (!output_norm) return decode_fail(ALJ_ERR_BAD_ARG, "null output norm");
+    std::lock_guard<std::mutex> g(m->mu);
+    cudaSetDevice(m->device);
+    m->embd.codes = static_cast<const uint8_t*>(decode_resolve(embd_codes));
+    m->embd.absmax = static_cast<const float*>(decode_resolve(embd_absmax));
+    m->head.codes = static_cast<const uint8_t*>(decode_resolve(head_codes));
+    m->head.absmax = static_cast<const float*>(decode_resolve(head_absmax));
+    if (!m->embd.codes || !m->embd.absmax || !m->head.codes || !m->head.absmax)
+        return decode_fail(ALJ_ERR_NOT_REGISTERED, "output weights must be device or registered memory");
+    if (cudaMemcpy(m->norms + static_cast<size_t>(m->layers) * 2 * m->H, output_norm, m->H * 4, cudaMemcpyDefault) !=
+        cudaSuccess)
+        return decode_fail(ALJ_ERR_CUDA, "copying the output norm failed");
+    m->output_set = true;
+    if (m->exec) { cudaGraphExecDestroy(m->exec); m->exec = nullptr; }
+    return ALJ_OK;
+}
+
+int aljabr_blackwell_decode_step_token(unsigned long long handle, int token, int pos, float* logits_out,
+                                       int* argmax_out) {
+    DecodeModel* m = find(handle);
+    if (!m) return decode_fail(ALJ_ERR_BAD_ARG, "unknown decode model handle");
+    if (pos < 0 || pos >= m->max_ctx) return decode_fail(ALJ_ERR_BAD_DIMS, "position outside the KV cache");
+    if (token < 0 || token >= m->V) return decode_fail(ALJ_ERR_BAD_DIMS, "token id outside the vocabulary");
+    std::lock_guard<std::mutex> g(m->mu);
+    cudaSetDevice(m->device);
+    if (!m->output_set) return decode_fail(ALJ_ERR_NOT_INITIALIZED, "output weights not registered");
+    for (int l = 0; l < m->layers; ++l)
+        if (!m->layer_set[l]) return decode_fail(ALJ_ERR_NOT_INITIALIZED, "decode layer not registered");
+    m->host_io[0] = pos;
+    m->host_io[1] = token;
+    cudaError_t e = cudaMemcpyAsync(m->io, m->host_io, 2 * sizeof(int), cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess) e = enqueue_steps(*m, 1);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(m->host_io + 2, m->io + 2, sizeof(int), cudaMemcpyDeviceToHost, m->stream);
+    if (e == cudaSuccess && logits_out)
+        e = cudaMemcpyAsync(m->host_logits, m->logits, static_cast<size_t>(m->V) * 4, cudaMemcpyDeviceToHost, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return decode_fail(ALJ_ERR_CUDA, cudaGetErrorString(e));
+    }
+    if (argmax_out) *argmax_out = m->host_io[2];
+    if (logits_out) memcpy(logits_out, m->host_logits, static_cast<size_t>(m->V) * 4);
+    return ALJ_OK;
+}
+
+int aljabr_blackwell_decode_run(unsigned long long handle, int token, int pos, int n_tokens, int* tokens_out) {
+    DecodeModel* m = find(handle);
+    if (!m) return decode_fail(ALJ_ERR_BAD_ARG, "unknown decode model handle");
+    if (n_tokens <= 0 || pos < 0 || pos + n_tokens > m->max_ctx)
+        return decode_fail(ALJ_ERR_BAD_DIMS, "positions [pos, pos + n_tokens) must lie inside the KV cache");
+    if (token < 0 || token >= m->V) return decode_fail(ALJ_ERR_BAD_DIMS, "token id outside the vocabulary");
+    std::lock_guard<std::mutex> g(m->mu);
+    cudaSetDevice(m->device);
+    if (!m->output_set) return decode_fail(ALJ_ERR_NOT_INITIALIZED, "output weights not registered");
+    for (int l = 0; l < m->layers; ++l)
+        if (!m->layer_set[l]) return decode_fail(ALJ_ERR_NOT_INITIALIZED, "decode layer not registered");
+    m->host_io[0] = pos;
+    m->host_io[1] = token;
+    cudaError_t e = cudaMemcpyAsync(m->io, m->host_io, 2 * sizeof(int), cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess) e = enqueue_steps(*m, n_tokens);
+    if (e == cudaSuccess && tokens_out)
+        e = cudaMemcpyAsync(tokens_out, m->tokens + pos, static_cast<size_t>(n_tokens) * sizeof(int),
+                            cudaMemcpyDeviceToHost, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return decode_fail(ALJ_ERR_CUDA, cudaGetErrorString(e));
+    }
+    return ALJ_OK;
+}
+
+int aljabr_blackwell_sync_kv_cache(unsigned long long handle, int layer, int seq_len, const void* k, const void* v) {
+    DecodeModel* m = find(handle);
+    if (!m) return decode_fail(ALJ_ERR_BAD_ARG, "unknown decode model handle");
+    if (layer < 0 || layer >= m->layers || seq_len < 0 || seq_len > m->max_ctx)
+        return decode_fail(ALJ_ERR_BAD_DIMS, "layer or sequence length out of range");
+    if (!k || !v) return decode_fail(ALJ_ERR_BAD_ARG, "null K or V");
+    std::lock_guard<std::mutex> g(m->mu);
+    cudaSetDevice(m->device);
+    const size_t bytes = static_cast<size_t>(seq_len) * m->hkv * m->D * m->kv_elem();
+    const size_t off = static_cast<size_t>(layer) * m->kv_layer_elems() * m->kv_elem();
+    cudaError_t e = cudaMemcpyAsync(static_cast<uint8_t*>(m->kc) + off, k, bytes, cudaMemcpyDefault, m->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(static_cast<uint8_t*>(m->vc) + off, v, bytes, cudaMemcpyDefault, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) return decode_fail(ALJ_ERR_CUDA, cudaGetErrorString(e));
+    return ALJ_OK;
+}
+
+int aljabr_blackwell_decode_read_state(unsigned long long handle, float* x_out, void* k_cache_out, void* v_cache_out) {
+    DecodeModel* m = find(handle);
+    if (!m) return decode_fail(ALJ_ERR_BAD_ARG, "unknown decode model handle");
+    std::lock_guard<std::mutex> g(m->mu);
+    cudaSetDevice(m->device);
+    const size_t kvb = static_cast<size_t>(m->layers) * m->kv_layer_elems() * m->kv_elem();
+    cudaError_t e = cudaStreamSynchronize(m->stream);
+    if (e == cudaSuccess && x_out) e = cudaMemcpy(x_out, m->x, static_cast<size_t>(m->H) * 4, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && k_cache_out) e = cudaMemcpy(k_cache_out, m->kc, kvb, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && v_cache_out) e = cudaMemcpy(v_cache_out, m->vc, kvb, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return decode_fail(ALJ_ERR_CUDA, cudaGetErrorString(e));
+    return ALJ_OK;
+}
+
+int aljabr_blackwell_decode_model_destroy(unsigned long long handle) {
+    std::unique_ptr<DecodeModel> m;
+    {
+        std::lock_guard<std::mutex> g(g_models_mu);
+        auto it = g_models.find(handle);
+        if (it == g_models.end()) return decode_fail(ALJ_ERR_BAD_ARG, "unknown decode model handle");
+        m = std::move(it->second);
+        g_models.erase(it);
+    }
+    destroy(m.get());
+    return ALJ_OK;
+}
+
+}  // extern "C"

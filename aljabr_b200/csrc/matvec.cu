@@ -86,7 +86,8 @@ __device__ __forceinline__ float q4_0_group(const uint8_t* src, const float* xg)
     }
     const f2 k01 = mk2(-(kTwo23 + 8.0f), -(kTwo23 + 128.0f));
     const f2 k23 = mk2(-(kTwo23 + 2048.0f), -(kTwo23 + 32768.0f));
-    const f2 fold = mk2(1.0f / 256.0f, 1.0f / 4096.0f);
+    // a23 holds 256x / 4096x partials; scaled by 1/256 they line up with a01's 1x / 16x units
+    const f2 fold = mk2(1.0f / 256.0f, 1.0f / 256.0f);
     float acc = 0.0f;
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
@@ -117,7 +118,7 @@ __device__ __forceinline__ float q4_0_group(const uint8_t* src, const float* xg)
             a01 = fma2(p2, mk2(xc.x, xc.y), a01);
             a23 = fma2(p3, mk2(xc.z, xc.w), a23);
         }
-        const f2 t = fma2(a23, fold, a01);               // (s1 + s256/256, s16 + s4096/4096)
+        const f2 t = fma2(a23, fold, a01);               // (1x sums, 16x sums)
         const float bs = fmaf(hi(t), 0.0625f, lo(t));
         acc = fmaf(__half2float(__ushort_as_half(static_cast<unsigned short>(dbits))), bs, acc);
     }

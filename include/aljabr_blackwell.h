@@ -165,6 +165,50 @@ int aljabr_blackwell_decode_attention_dev(float* out, const float* q, const void
                                           int kv_heads, int q_heads, int head_dim, int seq_len,
                                           int start_pos, float scale, void* stream);
 
+/* ---- full decode step (Llama-shaped, NF4 weights, one CUDA graph/token) ---
+ * The device-resident form of GgufDecodePass.forward's layer loop
+ * (engine/gguf/aljabr-gguf-java/.../GgufDecodePass.java:297-545), shaped like
+ * the Metal provider's registered decode step (aljabr_metal_matvec_api.h:
+ * aljabr_metal_init_kv_cache / register_decode_layer / register_output /
+ * register_token_embd / decode_step_token), but handle-based so several
+ * models can coexist.
+ *
+ * dims = {layers, hidden, q_heads, kv_heads, head_dim, ffn, vocab, max_ctx,
+ *         nf4_group, kv_dtype}.  With tp_world > 1 every weight passed in is
+ * this rank's contiguous row block ([rows/tp_world] of each matrix; the
+ * q/k/v row blocks are whole heads), the KV cache holds this rank's heads,
+ * and nccl_id is the 128-byte id from aljabr_blackwell_nccl_unique_id,
+ * shared by all ranks; one call per rank, each with its own current device. */
+int aljabr_blackwell_nccl_unique_id(void* out, int out_len);
+int aljabr_blackwell_decode_model_create(const int* dims, float eps, float rope_theta, int tp_world, int tp_rank,
+                                         const void* nccl_id, unsigned long long* handle);
+/* codes[7] / absmax[7]: q, k, v, o, gate, up, down (device or registered
+ * memory, referenced, not copied); norms are host or device float[hidden]. */
+int aljabr_blackwell_register_decode_layer(unsigned long long handle, int layer, const void* const* codes,
+                                           const void* const* absmax, const float* attn_norm, const float* ffn_norm);
+/* Token embedding [vocab][hidden] (full on every rank) and lm_head rows. */
+int aljabr_blackwell_register_output(unsigned long long handle, const void* embd_codes, const void* embd_absmax,
+                                     const void* head_codes, const void* head_absmax, const float* output_norm);
+/* One token at position `pos` (its K/V are written at pos; attention covers
+ * [0, pos]).  logits_out: host float[vocab] or NULL; argmax_out: host int or
+ * NULL (greedy next token). */
+int aljabr_blackwell_decode_step_token(unsigned long long handle, int token, int pos, float* logits_out,
+                                       int* argmax_out);
+/* n_tokens greedy steps entirely on the device: the argmax of each step is
+ * the next step's token, positions pos .. pos+n_tokens-1; the emitted tokens
+ * go to tokens_out (host int[n_tokens], may be NULL).  One synchronisation
+ * at the end. */
+int aljabr_blackwell_decode_run(unsigned long long handle, int token, int pos, int n_tokens, int* tokens_out);
+/* Load positions [0, seq_len) of one layer's K and V cache (prompt prefill
+ * or a restored session; aljabr_metal_sync_kv_cache).  k, v: host or device
+ * memory holding seq_len x (kv_heads/tp * head_dim) elements of kv_dtype. */
+int aljabr_blackwell_sync_kv_cache(unsigned long long handle, int layer, int seq_len, const void* k, const void* v);
+/* Copy the residual stream x (float[hidden]) and this rank's KV caches
+ * ([layers][max_ctx][kv_heads/tp*head_dim] of kv_dtype) to host memory;
+ * any pointer may be NULL. */
+int aljabr_blackwell_decode_read_state(unsigned long long handle, float* x_out, void* k_cache_out, void* v_cache_out);
+int aljabr_blackwell_decode_model_destroy(unsigned long long handle);
+
 #ifdef __cplusplus
 }
 #endif

@@ -86,7 +86,7 @@ def _declare(L):
     L.orc_rope.argtypes = [_p, _i, _i, _i, _i, _f]
     L.orc_swiglu.argtypes = [_p, _p, _p, _i]
     L.orc_softmax.argtypes = [_p, _i]
-    L.orc_decode_step_nf4.argtypes = [_p, _p, _p, _p, _p, _p, _i, _i, _p, _p]
+    L.orc_decode_step_nf4.argtypes = [_p, _p, _p, _p, _p, _p, _i, _i, _i, _p, _p]
 
 
 def _ptr(a):
@@ -272,16 +272,19 @@ class LlamaCfg(ctypes.Structure):
 
 def decode_step_nf4(cfg: LlamaCfg, codes: list, absmax: list, norms, k_cache, v_cache,
                     token: int, pos: int, want_logits: bool = True):
-    """One decode step (DP:297-545); k_cache/v_cache (uint16 bf16 bits) are
-    updated in place at `pos`.  Returns (x, logits)."""
+    """One decode step (DP:297-545); k_cache/v_cache ([layers][max_ctx][Hkv*D],
+    float32 or uint16 bf16 bits) are updated in place at `pos`.
+    Returns (x, logits)."""
     codes = [_c(c, np.uint8) for c in codes]
     absmax = [_c(a, np.float32) for a in absmax]
     cp = (ctypes.c_void_p * len(codes))(*[c.ctypes.data for c in codes])
     ap = (ctypes.c_void_p * len(absmax))(*[a.ctypes.data for a in absmax])
     norms = _c(norms, np.float32)
-    assert k_cache.dtype == np.uint16 and k_cache.flags.c_contiguous
+    assert k_cache.dtype in (np.uint16, np.float32) and k_cache.flags.c_contiguous
+    assert v_cache.dtype == k_cache.dtype and v_cache.flags.c_contiguous
+    kv_bf16 = int(k_cache.dtype == np.uint16)
     x = np.empty(cfg.hidden, dtype=np.float32)
     logits = np.empty(cfg.vocab, dtype=np.float32) if want_logits else None
     lib().orc_decode_step_nf4(ctypes.byref(cfg), cp, ap, _ptr(norms), _ptr(k_cache), _ptr(v_cache),
-                              token, pos, _ptr(x), _ptr(logits))
+                              kv_bf16, token, pos, _ptr(x), _ptr(logits))
     return x, logits

@@ -306,17 +306,24 @@ typedef struct {
 } job_t;
 
 static float nf4_row_dot(const uint8_t* codes, const float* absmax, const float* x, int K, int group, int64_t row) {
-    /* dequantise the row exactly as DK:84-102 does for the flat tensor, then
-     * a sequential fp32 dot (stand-in for the closed cblas_sgemv). */
-    float s = 0.0f;
+    /* Dequantise the row exactly as DK:84-102 does for the flat tensor
+     * (element e = row*K + k: nibble (e & 1 ? low : high) of byte e >> 1,
+     * scale absmax[(e >> 1) * 2 / group]), then an 8-lane FMA dot with a
+     * left-to-right lane sum -- the shape of a SIMD cblas_sgemv row, which
+     * is what AccelOps.linear calls (closed, macOS-only; parity unpinned).
+     * A plain sequential fp32 sum would itself drift past 1e-3 relative
+     * error on K = 14336 rows with cancellation. */
+    float acc[VLANES] = {0};
     int64_t base = row * (int64_t)K;
-    for (int k = 0; k < K; k += 2) {
-        int64_t i = (base + k) >> 1;
-        int b = codes[i];
-        float scale = absmax[(i * 2) / group];
-        s += NF4_TABLE[(b >> 4) & 15] * scale * x[k];
-        if (k + 1 < K) s += NF4_TABLE[b & 15] * scale * x[k + 1];
+    for (int k = 0; k < K; k++) {
+        int64_t e = base + k;
+        int b = codes[e >> 1];
+        int code = (e & 1) ? (b & 15) : ((b >> 4) & 15);
+        float w = NF4_TABLE[code] * absmax[((e >> 1) * 2) / group];
+        acc[k % VLANES] = fmaf(w, x[k], acc[k % VLANES]);
     }
+    float s = 0.0f;
+    for (int l = 0; l < VLANES; l++) s += acc[l];
     return s;
 }
 
@@ -509,7 +516,7 @@ static void nf4_matvec_seq(const uint8_t* codes, const float* absmax, const floa
 }
 
 void orc_decode_step_nf4(const orc_llama_cfg* c, const uint8_t* const* codes, const float* const* absmax,
-                         const float* norms, uint16_t* k_cache, uint16_t* v_cache,
+                         const float* norms, void* k_cache_v, void* v_cache_v, int kv_bf16,
                          int token, int pos, float* x_out, float* logits) {
     int H = c->hidden, D = c->head_dim, Hq = c->q_heads, Hkv = c->kv_heads, F = c->ffn;
     int QD = Hq * D, KVD = Hkv * D, L = c->layers, g = c->group;
@@ -547,13 +554,24 @@ void orc_decode_step_nf4(const orc_llama_cfg* c, const uint8_t* const* codes, co
         orc_rope(q, Hq, D, D, pos, c->rope_theta);                               /* DP:333 */
         orc_rope(k, Hkv, D, D, pos, c->rope_theta);                              /* DP:360 */
         size_t lbase = (size_t)l * c->max_ctx * KVD;
-        for (int i = 0; i < KVD; i++) {                                          /* DP:362 */
-            k_cache[lbase + (size_t)pos * KVD + i] = orc_f32_to_bf16_rne(k[i]);
-            v_cache[lbase + (size_t)pos * KVD + i] = orc_f32_to_bf16_rne(v[i]);
-        }
-        for (size_t i = 0; i < (size_t)(pos + 1) * KVD; i++) {
-            kf[i] = bf16_to_f32(k_cache[lbase + i]);
-            vf[i] = bf16_to_f32(v_cache[lbase + i]);
+        if (kv_bf16) {                                                           /* DP:362 */
+            uint16_t* kc = (uint16_t*)k_cache_v;
+            uint16_t* vc = (uint16_t*)v_cache_v;
+            for (int i = 0; i < KVD; i++) {
+                kc[lbase + (size_t)pos * KVD + i] = orc_f32_to_bf16_rne(k[i]);
+                vc[lbase + (size_t)pos * KVD + i] = orc_f32_to_bf16_rne(v[i]);
+            }
+            for (size_t i = 0; i < (size_t)(pos + 1) * KVD; i++) {
+                kf[i] = bf16_to_f32(kc[lbase + i]);
+                vf[i] = bf16_to_f32(vc[lbase + i]);
+            }
+        } else {
+            float* kc = (float*)k_cache_v;
+            float* vc = (float*)v_cache_v;
+            memcpy(kc + lbase + (size_t)pos * KVD, k, sizeof(float) * KVD);
+            memcpy(vc + lbase + (size_t)pos * KVD, v, sizeof(float) * KVD);
+            memcpy(kf, kc + lbase, sizeof(float) * (size_t)(pos + 1) * KVD);
+            memcpy(vf, vc + lbase, sizeof(float) * (size_t)(pos + 1) * KVD);
         }
         orc_gqa_decode_attention(q, att, scores, kf, vf, KVD, Hkv, Hq, D, pos + 1, 0, scale);   /* DP:386 */
         nf4_matvec_seq(cw[3], aw[3], att, xb, QD, H, g);                         /* DP:475 */

@@ -87,9 +87,9 @@ void  orc_softmax(float* a, int len);                                           
 /* One batch-1 decode step of a Llama-shaped model with NF4 linear weights,
  * following DP:297-545 (pre-norm, q/k/v, split-half RoPE, KV store,
  * attention, o-proj + residual, SwiGLU FFN + residual) and the logits
- * projection.  The KV cache holds bf16 bit patterns ([layer][pos][kvH*D]);
- * the current token's k/v are rounded to bf16 (RNE) when stored, which is
- * the one intended deviation from the reference's fp32 cache.
+ * projection.  The KV cache is [layer][max_ctx][kvH*D] of either fp32
+ * (kv_bf16 = 0, the reference's cache) or bf16 bit patterns (kv_bf16 = 1:
+ * the current token's k/v are rounded to bf16, RNE, when stored).
  *
  * Weight layout per layer l (NF4, group g, row-major [N][K]):
  *   wq [Hq*D][H], wk [Hkv*D][H], wv [Hkv*D][H], wo [H][Hq*D],
@@ -103,7 +103,7 @@ typedef struct {
 void orc_decode_step_nf4(const orc_llama_cfg* cfg,
                          const uint8_t* const* codes, const float* const* absmax,
                          const float* norms,   /* [layers][2][H] (attn, ffn) then [H] output norm */
-                         uint16_t* k_cache, uint16_t* v_cache,
+                         void* k_cache, void* v_cache, int kv_bf16,
                          int token, int pos, float* x_out, float* logits);
 
 #ifdef __cplusplus
