@@ -184,14 +184,15 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize(dev)
     graph = capture(torch, stream, lambda: [step(i) for i in range(chunk)])
     replays = args.steps // chunk
-    graph.replay()                      # one untimed replay: graph upload
+    with torch.cuda.stream(stream):     # replay() launches on the current stream
+        graph.replay()                  # one untimed replay: graph upload
     torch.cuda.synchronize(dev)
 
     # ---- timed region: K steps, device time by CUDA events on the stream -----
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize(dev)
-    with ClockSampler(local_rank) as clk:
+    with ClockSampler(local_rank) as clk, torch.cuda.stream(stream):
         start.record(stream)
         for _ in range(replays):
             graph.replay()
@@ -312,8 +313,9 @@ def capture(torch, stream, record):
     return g
 
 
-def run_extra(args, dev, stream, sh, l2):
-    """Secondary configs, each with its own pool > 2 x L2 and device timing."""
+def run_extra(args, dev, stream, sh, l2, which=None, reps=200):
+    """Secondary configs, each with its own pool > 2 x L2 and device timing.
+    `which` selects a subset of {"nf4", "q8", "attention"} (all if None)."""
     import torch
 
     import oracle
@@ -321,7 +323,6 @@ def run_extra(args, dev, stream, sh, l2):
 
     L = native.lib()
     out = {}
-    reps = 200
 
     def timed(fn, n):
         """Device ms per call: n calls captured in one graph, replayed 3x."""
@@ -330,77 +331,88 @@ def run_extra(args, dev, stream, sh, l2):
                 fn(i)
         torch.cuda.synchronize(dev)
         gr = capture(torch, stream, lambda: [fn(i) for i in range(n)])
-        gr.replay()
+        with torch.cuda.stream(stream):
+            gr.replay()
         torch.cuda.synchronize(dev)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        for _ in range(3):
-            gr.replay()
-        e.record(stream)
+        with torch.cuda.stream(stream):
+            s.record(stream)
+            for _ in range(3):
+                gr.replay()
+            e.record(stream)
         torch.cuda.synchronize(dev)
         return s.elapsed_time(e) / (3 * n)
 
-    # NF4 4096 x 4096, block 64
-    N = K = 4096
+    want = (lambda name: which is None or name in which)
     g = np.random.default_rng(7)
-    codes, absmax = oracle.quantize_nf4(g.normal(0, 0.02, size=(N, K)).astype(np.float32), 64)
-    per = codes.nbytes + absmax.nbytes
-    pool = max(2, int(np.ceil(2.5 * l2 / per)))
-    cd = torch.from_numpy(codes).to(dev)
-    ad = torch.from_numpy(absmax).to(dev)
-    cs = [cd.clone() for _ in range(pool)]
-    ams = [ad.clone() for _ in range(pool)]
-    xs = [torch.randn(K, device=dev) for _ in range(pool)]
-    ys = [torch.empty(N, device=dev) for _ in range(pool)]
-    with torch.cuda.stream(stream):
+
+    def nf4_section():
+        # NF4 4096 x 4096, block 64
+        N = K = 4096
+        codes, absmax = oracle.quantize_nf4(g.normal(0, 0.02, size=(N, K)).astype(np.float32), 64)
+        per = codes.nbytes + absmax.nbytes
+        pool = max(2, int(np.ceil(2.5 * l2 / per)))
+        cd = torch.from_numpy(codes).to(dev)
+        ad = torch.from_numpy(absmax).to(dev)
+        cs = [cd.clone() for _ in range(pool)]
+        ams = [ad.clone() for _ in range(pool)]
+        xs = [torch.randn(K, device=dev) for _ in range(pool)]
+        ys = [torch.empty(N, device=dev) for _ in range(pool)]
         ms = timed(lambda i: native.check(L.aljabr_blackwell_matvec_dev(
             native.TYPE_NF4, ys[i % pool].data_ptr(), xs[i % pool].data_ptr(), cs[i % pool].data_ptr(),
             ctypes_ptr(ams[i % pool]), K, N, 64, None, sh)), reps * 4)
-    alg = per + 4 * K + 4 * N
-    out["nf4_matvec_4096x4096_b64"] = {"GB/s": round(alg / (ms * 1e-3) / 1e9, 1), "us_per_launch": round(ms * 1e3, 3),
-                                       "algorithmic_bytes": alg, "pool": pool}
-    del cs, ams
+        alg = per + 4 * K + 4 * N
+        out["nf4_matvec_4096x4096_b64"] = {"GB/s": round(alg / (ms * 1e-3) / 1e9, 1),
+                                           "us_per_launch": round(ms * 1e3, 3), "algorithmic_bytes": alg,
+                                           "pool": pool}
 
-    # Q8_0: one Llama-3-8B layer's projections
-    shapes = [("q", 4096, 4096), ("k", 1024, 4096), ("v", 1024, 4096), ("o", 4096, 4096),
-              ("gate", 14336, 4096), ("up", 14336, 4096), ("down", 4096, 14336)]
-    mats = {}
-    for name, n, k in shapes:
-        mats[name] = torch.from_numpy(oracle.encode_q8_0(g.normal(0, 0.02, size=(n, k)).astype(np.float32))).to(dev)
-    layer_w = sum(m.numel() for m in mats.values())
-    pool8 = max(2, int(np.ceil(2.5 * l2 / layer_w)))
-    layers = [{k2: v.clone() for k2, v in mats.items()} for _ in range(pool8)]
-    xq = {k: torch.randn(kk, device=dev) for k, _, kk in shapes}
-    yq = {k: torch.empty(n, device=dev) for k, n, _ in shapes}
-
-    def q8_layer(i):
-        lay = layers[i % pool8]
+    def q8_section():
+        # Q8_0: one Llama-3-8B layer's projections
+        shapes = [("q", 4096, 4096), ("k", 1024, 4096), ("v", 1024, 4096), ("o", 4096, 4096),
+                  ("gate", 14336, 4096), ("up", 14336, 4096), ("down", 4096, 14336)]
+        mats = {}
         for name, n, k in shapes:
-            native.check(L.aljabr_blackwell_matvec_dev(native.TYPE_Q8_0, yq[name].data_ptr(), xq[name].data_ptr(),
-                                                       lay[name].data_ptr(), None, k, n, 0, None, sh))
-    with torch.cuda.stream(stream):
-        ms = timed(q8_layer, reps)
-    alg = layer_w + sum(4 * (n + k) for _, n, k in shapes)
-    out["q8_0_llama3_8b_layer"] = {"GB/s": round(alg / (ms * 1e-3) / 1e9, 1), "us_per_layer": round(ms * 1e3, 3),
-                                   "launches_per_layer": len(shapes), "weight_bytes": layer_w}
-    del layers
+            mats[name] = torch.from_numpy(
+                oracle.encode_q8_0(g.normal(0, 0.02, size=(n, k)).astype(np.float32))).to(dev)
+        layer_w = sum(m.numel() for m in mats.values())
+        pool8 = max(2, int(np.ceil(2.5 * l2 / layer_w)))
+        layers = [{k2: v.clone() for k2, v in mats.items()} for _ in range(pool8)]
+        xq = {k: torch.randn(kk, device=dev) for k, _, kk in shapes}
+        yq = {k: torch.empty(n, device=dev) for k, n, _ in shapes}
 
-    # GQA decode attention, Hq 32 / Hkv 8 / D 128, ctx 4096, bf16 KV
-    Hq, Hkv, D, ctx = 32, 8, 128, 4096
-    kvb = ctx * Hkv * D * 2
-    poola = max(2, int(np.ceil(2.5 * l2 / (2 * kvb))))
-    ks = [torch.randn(ctx, Hkv * D, device=dev).to(torch.bfloat16) for _ in range(poola)]
-    vs = [torch.randn(ctx, Hkv * D, device=dev).to(torch.bfloat16) for _ in range(poola)]
-    q = torch.randn(Hq * D, device=dev)
-    o = torch.empty(Hq * D, device=dev)
-    with torch.cuda.stream(stream):
+        def q8_layer(i):
+            lay = layers[i % pool8]
+            for name, n, k in shapes:
+                native.check(L.aljabr_blackwell_matvec_dev(native.TYPE_Q8_0, yq[name].data_ptr(),
+                                                           xq[name].data_ptr(), lay[name].data_ptr(), None, k, n,
+                                                           0, None, sh))
+        ms = timed(q8_layer, reps)
+        alg = layer_w + sum(4 * (n + k) for _, n, k in shapes)
+        out["q8_0_llama3_8b_layer"] = {"GB/s": round(alg / (ms * 1e-3) / 1e9, 1),
+                                       "us_per_layer": round(ms * 1e3, 3), "launches_per_layer": len(shapes),
+                                       "weight_bytes": layer_w}
+
+    def attention_section():
+        # GQA decode attention, Hq 32 / Hkv 8 / D 128, ctx 4096, bf16 KV
+        Hq, Hkv, D, ctx = 32, 8, 128, 4096
+        kvb = ctx * Hkv * D * 2
+        poola = max(2, int(np.ceil(2.5 * l2 / (2 * kvb))))
+        ks = [torch.randn(ctx, Hkv * D, device=dev).to(torch.bfloat16) for _ in range(poola)]
+        vs = [torch.randn(ctx, Hkv * D, device=dev).to(torch.bfloat16) for _ in range(poola)]
+        q = torch.randn(Hq * D, device=dev)
+        o = torch.empty(Hq * D, device=dev)
         ms = timed(lambda i: native.check(L.aljabr_blackwell_decode_attention_dev(
             o.data_ptr(), q.data_ptr(), ks[i % poola].data_ptr(), vs[i % poola].data_ptr(), native.KV_BF16,
             Hkv * D, Hkv, Hq, D, ctx, 0, 1.0 / 128 ** 0.5, sh)), reps * 4)
-    alg = 2 * kvb + 8 * Hq * D
-    out["gqa_decode_attention_ctx4096_bf16"] = {"GB/s": round(alg / (ms * 1e-3) / 1e9, 1),
-                                                "us_per_call": round(ms * 1e3, 3), "algorithmic_bytes": alg,
-                                                "launches_per_call": 2}
+        alg = 2 * kvb + 8 * Hq * D
+        out["gqa_decode_attention_ctx4096_bf16"] = {"GB/s": round(alg / (ms * 1e-3) / 1e9, 1),
+                                                    "us_per_call": round(ms * 1e3, 3), "algorithmic_bytes": alg,
+                                                    "launches_per_call": 2}
+
+    for name, fn in (("nf4", nf4_section), ("q8", q8_section), ("attention", attention_section)):
+        if want(name):
+            fn()
+            torch.cuda.empty_cache()
     return out
 
 
@@ -559,6 +571,26 @@ def run_reference(args, rank, world):
             "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def run_only(args, rank, world, local_rank):
+    import ctypes
+
+    import torch
+
+    from aljabr_b200 import native
+    torch.cuda.set_device(local_rank)
+    native.call("aljabr_blackwell_init", local_rank)
+    native.call("aljabr_blackwell_set_pdl", 0 if args.no_pdl else 1)
+    dev = torch.device("cuda", local_rank)
+    if args.only == "decode":
+        return {"only": "decode", **run_decode(args, rank, world, dev, tokens_per_run=args.decode_tokens, runs=1)}
+    props = torch.cuda.get_device_properties(local_rank)
+    l2 = getattr(props, "L2_cache_size", 126 * 2 ** 20) or 126 * 2 ** 20
+    stream = torch.cuda.Stream(device=dev)
+    out = run_extra(args, dev, stream, ctypes.c_void_p(stream.cuda_stream), l2, which={args.only},
+                    reps=max(1, args.steps))
+    return {"only": args.only, **out}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -568,6 +600,9 @@ def main():
     ap.add_argument("--no-extra", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--only", choices=["nf4", "q8", "attention", "decode"],
+                    help="run one secondary workload alone (for profiling); prints its dict")
+    ap.add_argument("--decode-tokens", type=int, default=32)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -589,7 +624,10 @@ def main():
         torch.cuda.set_device(local_rank)
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local_rank))
-    line = run_ours(args, rank, world, local_rank)
+    if args.only:
+        line = run_only(args, rank, world, local_rank)
+    else:
+        line = run_ours(args, rank, world, local_rank)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
