@@ -194,27 +194,51 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_split_kernel(const AttnP
     }
 }
 
-__global__ void attn_combine_kernel(const AttnParams p) {
+// Merge the splits of one query head: the per-split (max, sum) pairs are
+// staged in shared memory and turned into weights once, then each thread
+// sums its head-dim element over the splits with independent loads.
+constexpr int kMaxSplits = 256;
+
+__global__ void __launch_bounds__(128) attn_combine_kernel(const AttnParams p) {
     pdl_launch_dependents();
     pdl_wait();
+    __shared__ float s_w[kMaxSplits];
+    __shared__ float s_red[4];
     const int qh = blockIdx.x;
     const int D = p.head_dim;
-    const float* ml = p.part_ml + static_cast<long long>(qh) * p.splits * 2;
-    float M = -INFINITY;
-    for (int j = 0; j < p.splits; ++j) M = fmaxf(M, ml[2 * j]);
-    float L = 0.0f;
-    for (int j = 0; j < p.splits; ++j) {
+    const int S = p.splits;
+    const float* ml = p.part_ml + static_cast<long long>(qh) * S * 2;
+    float mx = -INFINITY;
+    for (int j = threadIdx.x; j < S; j += blockDim.x) mx = fmaxf(mx, ml[2 * j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    const float M = fmaxf(fmaxf(s_red[0], s_red[1]), fmaxf(s_red[2], s_red[3]));
+    __syncthreads();
+    float l = 0.0f;
+    for (int j = threadIdx.x; j < S; j += blockDim.x) {
         const float mj = ml[2 * j];
-        if (mj != -INFINITY) L = fmaf(ml[2 * j + 1], exp2f((mj - M) * kLog2e), L);
+        const float w = mj == -INFINITY ? 0.0f : exp2f((mj - M) * kLog2e);
+        s_w[j] = w;
+        l = fmaf(ml[2 * j + 1], w, l);
     }
+    l = warp_sum(l);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = l;
+    __syncthreads();
+    const float inv = 1.0f / (s_red[0] + s_red[1] + s_red[2] + s_red[3]);
+    const float* po = p.part_o + static_cast<long long>(qh) * S * D;
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
-        float acc = 0.0f;
-        for (int j = 0; j < p.splits; ++j) {
-            const float mj = ml[2 * j];
-            if (mj != -INFINITY)
-                acc = fmaf(p.part_o[(static_cast<long long>(qh) * p.splits + j) * D + d], exp2f((mj - M) * kLog2e), acc);
+        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+        int j = 0;
+        for (; j + 4 <= S; j += 4) {
+            a0 = fmaf(po[(j + 0) * D + d], s_w[j + 0], a0);
+            a1 = fmaf(po[(j + 1) * D + d], s_w[j + 1], a1);
+            a2 = fmaf(po[(j + 2) * D + d], s_w[j + 2], a2);
+            a3 = fmaf(po[(j + 3) * D + d], s_w[j + 3], a3);
         }
-        p.out[qh * D + d] = acc / L;
+        for (; j < S; ++j) a0 = fmaf(po[j * D + d], s_w[j], a0);
+        p.out[qh * D + d] = ((a0 + a1) + (a2 + a3)) * inv;
     }
 }
 
@@ -338,7 +362,7 @@ int attention_splits(int seq_len, int kv_heads, int sm_count) {
     // ~2 CTAs per SM in total, at least 64 positions per split
     const int want = std::max(1, (2 * sm_count + kv_heads - 1) / std::max(kv_heads, 1));
     const int cap = std::max(1, seq_len / 64);
-    return std::min(want, cap);
+    return std::min(std::min(want, cap), kMaxSplits);
 }
 
 size_t attention_scratch_floats(int q_heads, int head_dim, int splits) {

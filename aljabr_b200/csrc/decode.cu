@@ -63,24 +63,27 @@ bool nccl_load() {
 }
 
 // ------------------------------------------------------------------ kernels
-__global__ void embed_nf4_kernel(float* x, const uint8_t* codes, const float* absmax, const int* io, int H, int group) {
+// io = {pos, token, argmax, -, argmax key (u64)}.  The embedding kernel is the
+// first of each step, so it also clears the argmax key.
+__global__ void embed_nf4_kernel(float* x, const uint8_t* codes, const float* absmax, int* io, int H, int group) {
     pdl_launch_dependents();
     pdl_wait();
-    const long long base = static_cast<long long>(io[1]) * H;   // io = {pos, token}
+    const long long base = static_cast<long long>(io[1]) * H;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < H; i += gridDim.x * blockDim.x) {
         const long long e = base + i;
         const int b = codes[e >> 1];
         const int code = (e & 1) ? (b & 15) : (b >> 4);
         x[i] = __fmul_rn(nf4_value(code), absmax[((e >> 1) * 2) / group]);
     }
+    if (blockIdx.x == 0 && threadIdx.x == 0) *reinterpret_cast<unsigned long long*>(io + 4) = 0ull;
 }
 
-// Split-half RoPE (GGUFVectorOps.rope, GGUFVectorOps.java:383-440, with the
-// angle table computed as the reference does: pow/cos/sin in double, cast to
-// float) on the rank's q and k heads, then the KV store at `pos`
-// (GgufKvCacheWriteExecution.storeToken).
-__global__ void rope_store_kernel(float* q, float* k, const float* v, void* kc, void* vc, const int* io, int hq,
-                                  int hkv, int D, float theta, int kv_dtype) {
+// Split-half RoPE (GGUFVectorOps.rope, GGUFVectorOps.java:383-440) on the
+// rank's q and k heads, then the KV store at `pos`
+// (GgufKvCacheWriteExecution.storeToken).  rope[pos * D/2 + i] holds
+// (cos, sin) of the reference's angle, computed on the host once.
+__global__ void rope_store_kernel(float* q, float* k, const float* v, void* kc, void* vc, const int* io,
+                                  const float2* rope, int hq, int hkv, int D, int kv_dtype) {
     pdl_launch_dependents();
     pdl_wait();
     const int pos = io[0];
@@ -89,11 +92,8 @@ __global__ void rope_store_kernel(float* q, float* k, const float* v, void* kc, 
     const int pairs = (hq + hkv) * half;
     for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < pairs; idx += gridDim.x * blockDim.x) {
         const int head = idx / half, i = idx - head * half;
-        const float expo = __fdiv_rn(-2.0f * static_cast<float>(i), static_cast<float>(D));
-        const float inv = static_cast<float>(pow(static_cast<double>(theta), static_cast<double>(expo)));
-        const float ang = __fmul_rn(static_cast<float>(pos), inv);
-        const float c = static_cast<float>(cos(static_cast<double>(ang)));
-        const float s = static_cast<float>(sin(static_cast<double>(ang)));
+        const float2 cs = rope[static_cast<long long>(pos) * half + i];
+        const float c = cs.x, s = cs.y;
         float* b = head < hq ? q + head * D : k + (head - hq) * D;
         const float x0 = b[i], x1 = b[i + half];
         const float r0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
@@ -140,44 +140,42 @@ __global__ void advance_kernel(int* io, int* tokens, int max_ctx) {
     pdl_launch_dependents();
     pdl_wait();
     if (threadIdx.x == 0 && blockIdx.x == 0) {
+        const unsigned long long key = *reinterpret_cast<const unsigned long long*>(io + 4);
+        // key 0: no finite logit was seen (all NaN); fall back to token 0
+        const int idx = key ? static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(key & 0xFFFFFFFFull)) : 0;
         const int pos = io[0];
-        if (pos >= 0 && pos < max_ctx) tokens[pos] = io[2];
-        io[1] = io[2];
+        io[2] = idx;
+        if (pos >= 0 && pos < max_ctx) tokens[pos] = idx;
+        io[1] = idx;
         io[0] = pos + 1 < max_ctx ? pos + 1 : max_ctx - 1;
     }
 }
 
-// First index of the maximum logit (greedy sampling).
-__global__ void argmax_kernel(const float* logits, int n, int* out) {
+// Greedy sampling: index of the maximum logit, the first one on ties.  Each
+// CTA reduces a slice and folds (order-preserving value bits, ~index) into
+// one 64-bit atomicMax.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
+    uint32_t b = __float_as_uint(v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return (static_cast<unsigned long long>(b) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(i));
+}
+
+__global__ void argmax_kernel(const float* logits, int n, int* io) {
     pdl_launch_dependents();
     pdl_wait();
-    __shared__ float sv[32];
-    __shared__ int si[32];
-    float best = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    __shared__ unsigned long long sk[32];
+    unsigned long long best = 0ull;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const float v = logits[i];
-        if (v > best) { best = v; bi = i; }
+        if (v == v) best = max(best, argmax_key(v, i));
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
-    }
-    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = best; si[threadIdx.x >> 5] = bi; }
+    for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+    if ((threadIdx.x & 31) == 0) sk[threadIdx.x >> 5] = best;
     __syncthreads();
-    if (threadIdx.x < 32) {
-        const int nw = blockDim.x >> 5;
-        best = threadIdx.x < nw ? sv[threadIdx.x] : -INFINITY;
-        bi = threadIdx.x < nw ? si[threadIdx.x] : 0x7fffffff;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
-        }
-        if (threadIdx.x == 0) *out = bi == 0x7fffffff ? 0 : bi;
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) best = max(best, sk[w]);
+        atomicMax(reinterpret_cast<unsigned long long*>(io + 4), best);
     }
 }
 
@@ -214,6 +212,7 @@ struct DecodeModel {
     Nf4 embd, head;
     bool output_set = false;
     float* norms = nullptr;            // [layers][2][H] then [H]
+    float2* rope = nullptr;            // [max_ctx][D/2] (cos, sin)
     void *kc = nullptr, *vc = nullptr; // [layers][max_ctx][hkv*D]
     float *x, *q, *k, *vv, *att_l, *att, *delta_l, *delta, *gate, *up, *h_l, *hh, *logits_l, *logits, *scratch;
     float* act_base = nullptr;
@@ -278,8 +277,8 @@ cudaError_t matvec(const DecodeModel& m, const Nf4* ws, float* const* ys, const 
 cudaError_t record_step(DecodeModel& m) {
     const int D = m.D;
     const int sms = sm_count_for_current_device();
-    REC(launch_small(embed_nf4_kernel, (m.H + 255) / 256, 256, m.stream, m.x, m.embd.codes, m.embd.absmax,
-                     static_cast<const int*>(m.io), m.H, m.group));
+    REC(launch_small(embed_nf4_kernel, (m.H + 255) / 256, 256, m.stream, m.x, m.embd.codes, m.embd.absmax, m.io,
+                     m.H, m.group));
     for (int l = 0; l < m.layers; ++l) {
         const auto& w = m.w[l];
         const float* attn_norm = m.norms + static_cast<size_t>(l) * 2 * m.H;
@@ -294,8 +293,8 @@ cudaError_t record_step(DecodeModel& m) {
         }
         // RoPE on q and k, KV store (GgufDecodePass.java:333-362)
         REC(launch_small(rope_store_kernel, std::max(1, ((m.hq + m.hkv) * D / 2 + 255) / 256), 256, m.stream, m.q,
-                         m.k, static_cast<const float*>(m.vv), kc, vc, static_cast<const int*>(m.io), m.hq, m.hkv, D,
-                         m.theta, m.kv_dtype));
+                         m.k, static_cast<const float*>(m.vv), kc, vc, static_cast<const int*>(m.io),
+                         static_cast<const float2*>(m.rope), m.hq, m.hkv, D, m.kv_dtype));
         {   // attention (GgufDecodePass.java:368-389)
             AttnParams a = {};
             a.out = m.T > 1 ? m.att_l : m.att;
@@ -361,7 +360,8 @@ cudaError_t record_step(DecodeModel& m) {
                    nullptr));
     }
     if (m.T > 1) RECN(g_nccl.allGather(m.logits_l, m.logits, m.v, ncclFloat, m.comm, m.stream));
-    REC(launch_small(argmax_kernel, 1, 1024, m.stream, static_cast<const float*>(m.logits), m.V, m.io + 2));
+    REC(launch_small(argmax_kernel, std::max(1, std::min(sms, (m.V + 1023) / 1024)), 1024, m.stream,
+                     static_cast<const float*>(m.logits), m.V, m.io));
     REC(launch_small(advance_kernel, 1, 32, m.stream, m.io, m.tokens, m.max_ctx));
     (void)sms;
     return cudaSuccess;
@@ -403,6 +403,7 @@ void destroy(DecodeModel* m) {
     cudaFree(m->vc);
     cudaFree(m->act_base);
     cudaFree(m->norms);
+    cudaFree(m->rope);
     cudaFree(m->io);
     cudaFree(m->tokens);
     cudaFreeHost(m->host_io);
@@ -470,7 +471,8 @@ int aljabr_blackwell_decode_model_create(const int* dims, float eps, float rope_
     if (!ok(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking)) || !ok(cudaMalloc(&m->kc, kvb)) ||
         !ok(cudaMalloc(&m->vc, kvb)) || !ok(cudaMalloc(&m->act_base, acts * 4)) ||
         !ok(cudaMalloc(&m->norms, (static_cast<size_t>(m->layers) * 2 + 1) * m->H * 4)) ||
-        !ok(cudaMalloc(&m->io, 4 * sizeof(int))) || !ok(cudaMallocHost(&m->host_io, 4 * sizeof(int))) ||
+        !ok(cudaMalloc(&m->io, 8 * sizeof(int))) || !ok(cudaMallocHost(&m->host_io, 8 * sizeof(int))) ||
+        !ok(cudaMalloc(&m->rope, static_cast<size_t>(m->max_ctx) * (m->D / 2) * sizeof(float2))) ||
         !ok(cudaMalloc(&m->tokens, static_cast<size_t>(m->max_ctx) * sizeof(int))) ||
         !ok(cudaMallocHost(&m->host_logits, static_cast<size_t>(m->V) * 4))) {
         cudaGetLastError();
@@ -480,6 +482,27 @@ int aljabr_blackwell_decode_model_create(const int* dims, float eps, float rope_
     cudaMemsetAsync(m->kc, 0, kvb, m->stream);
     cudaMemsetAsync(m->vc, 0, kvb, m->stream);
     cudaMemsetAsync(m->act_base, 0, acts * 4, m->stream);
+    {
+        // RoPE angle table exactly as GGUFVectorOps.rope (GGUFVectorOps.java:425-431):
+        // invFreq = (float) pow(base, -2f*i/rotaryDim); theta = (pos * invFreq) / 1f;
+        // cos / sin in double, cast to float.
+        const int half = m->D / 2;
+        std::vector<float2> tab(static_cast<size_t>(m->max_ctx) * half);
+        for (int i = 0; i < half; ++i) {
+            const float expo = -2.0f * static_cast<float>(i) / static_cast<float>(m->D);
+            const float inv = static_cast<float>(std::pow(static_cast<double>(m->theta), static_cast<double>(expo)));
+            for (int pos = 0; pos < m->max_ctx; ++pos) {
+                const float ang = static_cast<float>(pos) * inv;
+                tab[static_cast<size_t>(pos) * half + i] =
+                    make_float2(static_cast<float>(std::cos(static_cast<double>(ang))),
+                                static_cast<float>(std::sin(static_cast<double>(ang))));
+            }
+        }
+        if (!ok(cudaMemcpy(m->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice))) {
+            destroy(m.get());
+            return decode_fail(ALJ_ERR_CUDA, "uploading the RoPE table failed");
+        }
+    }
     float* p = m->act_base;
     auto take = [&](size_t n) { float* r = p; p += (n + 3) / 4 * 4; return r; };
     m->x = take(m->H); m->q = take(m->hq * m->D); m->k = take(m->hkv * m->D); m->vv = take(m->hkv * m->D);

@@ -56,7 +56,8 @@ def test_golden_known_answers_q4_0_q8_0(lib, golden):
 
 
 @pytest.mark.parametrize("N,K", [(7, 256), (33, 512), (300, 2048), (1024, 4096), (4096, 4096),
-                                 (14336, 4096), (4096, 14336), (5, 160), (3, 96)])
+                                 (14336, 4096), (4096, 14336), (5, 160), (3, 96), (36, 256), (64, 2304),
+                                 (148 * 4 + 4, 6144)])
 def test_q4_0_matvec_parity(lib, N, K):
     w = synth.q4_0(1000 + N, N, K)
     x = synth.activation(2000 + K, K)
@@ -68,7 +69,8 @@ def test_q4_0_matvec_parity(lib, N, K):
     assert synth.normwise_rel_err(y, g) < 1e-5
 
 
-@pytest.mark.parametrize("N,K", [(7, 256), (1024, 4096), (4096, 4096), (14336, 4096), (4096, 14336), (5, 160)])
+@pytest.mark.parametrize("N,K", [(7, 256), (1024, 4096), (4096, 4096), (14336, 4096), (4096, 14336), (5, 160),
+                                 (64, 1280), (36, 256)])
 def test_q8_0_matvec_parity(lib, N, K):
     w = synth.q8_0(3000 + N, N, K)
     x = synth.activation(4000 + K, K)
@@ -82,7 +84,8 @@ def test_q8_0_matvec_parity(lib, N, K):
 
 
 @pytest.mark.parametrize("N,K,group", [(7, 256, 64), (4096, 4096, 64), (1024, 4096, 128), (14336, 4096, 64),
-                                       (4096, 14336, 64), (9, 200, 64), (6, 384, 96)])
+                                       (4096, 14336, 64), (9, 200, 64), (6, 384, 96), (64, 1280, 64),
+                                       (8, 1536, 128), (128256 // 16, 4096, 64)])
 def test_nf4_matvec_parity(lib, N, K, group):
     codes, absmax = synth.nf4(5000 + N, N, K, group)
     x = synth.activation(6000 + K, K)
