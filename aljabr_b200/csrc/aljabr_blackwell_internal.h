@@ -16,11 +16,10 @@ namespace alj {
 
 enum WeightFormat : int { FMT_Q4_0 = 0, FMT_Q8_0 = 1, FMT_NF4 = 2 };
 
-// x-side prologue fused into a matvec (decode-step fusion).
-enum Prologue : int {
-    PRO_NONE = 0,
-    PRO_RMSNORM = 1,   // x' = x * rsqrt(mean(x^2) + eps) * norm_w
-    PRO_SWIGLU = 2,    // x' = silu(gate) * x
+// Output-side fusions of a matvec (decode-step fusion).
+enum Epilogue : int {
+    EPI_STORE = 0,         // y = W x (+ bias) (+ residual)
+    EPI_SWIGLU_PAIR = 1,   // segments 0 (gate) and 1 (up) of equal rows: seg[0].y = silu(W_g x) * (W_u x)
 };
 
 struct MatvecSegment {
@@ -36,14 +35,22 @@ struct MatvecParams {
     MatvecSegment seg[3];
     int nseg;
     int K;
-    int total_rows;
+    int total_rows;          // rows of all segments (EPI_SWIGLU_PAIR: rows of one segment)
     int group;               // NF4 group size
     const float* x;
-    int prologue;
+    int epilogue;
+    // Optional RMSNorm of the finished output (single segment): the last CTA
+    // to finish writes norm_out = y * rsqrt(mean(y^2) + eps) * norm_w.
+    // norm_partials holds one float per CTA (>= 2 * SM count); norm_counter
+    // starts at 0 and is left at 0.
+    float* norm_out;
     const float* norm_w;
     float norm_eps;
-    const float* gate;
+    float* norm_partials;
+    unsigned int* norm_counter;
 };
+// CTAs a TMA matvec launches (the size norm_partials must have).
+int matvec_max_ctas();
 
 // Kernel launchers (return cudaError_t of the launch).  `pdl` enables
 // programmatic dependent launch on the stream.

@@ -5,11 +5,12 @@
 // Metal provider's registered-layer decode step (aljabr_metal_matvec_api.h:
 // aljabr_metal_register_decode_layer / aljabr_metal_decode_step_token).
 //
-// Per layer (one GPU): fused q/k/v matvec with the RMSNorm prologue -> RoPE +
-// KV store -> split-K attention (+ combine) -> o-proj with the residual add
-// in its epilogue -> gate/up pair with the RMSNorm prologue -> down-proj
-// with the SwiGLU prologue and the residual epilogue.  Seven launches per
-// layer, chained with programmatic dependent launch inside the graph.
+// Per layer (one GPU): q/k/v triple matvec on the normed x -> RoPE + KV
+// store -> split-K attention (+ combine) -> o-proj whose epilogue adds the
+// residual and, in its last CTA, writes RMSNorm(x) for the FFN -> gate/up
+// pair whose epilogue applies SwiGLU -> down-proj whose epilogue adds the
+// residual and writes the next layer's normed x.  Seven launches per layer,
+// chained with programmatic dependent launch inside one CUDA graph.
 //
 // Tensor parallelism (2/4/8 GPUs, one process or thread per GPU): every
 // weight is row-sharded (the caller passes each rank's contiguous row
@@ -63,19 +64,41 @@ bool nccl_load() {
 }
 
 // ------------------------------------------------------------------ kernels
-// io = {pos, token, argmax, -, argmax key (u64)}.  The embedding kernel is the
-// first of each step, so it also clears the argmax key.
-__global__ void embed_nf4_kernel(float* x, const uint8_t* codes, const float* absmax, int* io, int H, int group) {
+// Block-wide sum over a 1024-thread CTA (result in every thread).
+__device__ __forceinline__ float block_sum_1024(float v, float* red) {
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 32; ++w) t += red[w];
+    __syncthreads();
+    return t;
+}
+
+// io = {pos, token, argmax, -, argmax key (u64)}.  First kernel of a step:
+// x = dequantised embedding row of the token; xn = RMSNorm(x) * norm_w (the
+// first layer's attention norm, GGUFVectorOps.rmsNorm); clears the argmax key.
+// One CTA of 1024 threads.
+__global__ void __launch_bounds__(1024) embed_nf4_kernel(float* x, float* xn, const uint8_t* codes,
+                                                         const float* absmax, int* io, int H, int group,
+                                                         const float* norm_w, float eps) {
+    __shared__ float red[32];
     pdl_launch_dependents();
     pdl_wait();
     const long long base = static_cast<long long>(io[1]) * H;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < H; i += gridDim.x * blockDim.x) {
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
         const long long e = base + i;
         const int b = codes[e >> 1];
         const int code = (e & 1) ? (b & 15) : (b >> 4);
-        x[i] = __fmul_rn(nf4_value(code), absmax[((e >> 1) * 2) / group]);
+        const float v = __fmul_rn(nf4_value(code), absmax[((e >> 1) * 2) / group]);
+        x[i] = v;
+        ss = fmaf(v, v, ss);
     }
-    if (blockIdx.x == 0 && threadIdx.x == 0) *reinterpret_cast<unsigned long long*>(io + 4) = 0ull;
+    const float scale = 1.0f / sqrtf(block_sum_1024(ss, red) / static_cast<float>(H) + eps);
+    for (int i = threadIdx.x; i < H; i += blockDim.x) xn[i] = x[i] * scale * norm_w[i];
+    if (threadIdx.x == 0) *reinterpret_cast<unsigned long long*>(io + 4) = 0ull;
 }
 
 // Split-half RoPE (GGUFVectorOps.rope, GGUFVectorOps.java:383-440) on the
@@ -118,20 +141,21 @@ __global__ void rope_store_kernel(float* q, float* k, const float* v, void* kc, 
     }
 }
 
-__global__ void add_kernel(float* x, const float* d, int n) {
+// Tensor-parallel residual join: x += delta (the all-gathered slices), then
+// xn = RMSNorm(x) * norm_w for the next matvec.  One CTA of 1024 threads.
+__global__ void __launch_bounds__(1024) add_norm_kernel(float* x, const float* d, float* xn, const float* norm_w,
+                                                        int n, float eps) {
+    __shared__ float red[32];
     pdl_launch_dependents();
     pdl_wait();
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) x[i] = x[i] + d[i];
-}
-
-// GGUFVectorOps.swiGLU (GGUFVectorOps.java:333-338): silu(g) * u.
-__global__ void swiglu_kernel(float* h, const float* gate, const float* up, int n) {
-    pdl_launch_dependents();
-    pdl_wait();
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        const float g = gate[i];
-        h[i] = g / (1.0f + expf(-g)) * up[i];
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = x[i] + d[i];
+        x[i] = v;
+        ss = fmaf(v, v, ss);
     }
+    const float scale = 1.0f / sqrtf(block_sum_1024(ss, red) / static_cast<float>(n) + eps);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) xn[i] = x[i] * scale * norm_w[i];
 }
 
 // Greedy hand-off inside the graph: the step's argmax becomes the next
@@ -214,7 +238,9 @@ struct DecodeModel {
     float* norms = nullptr;            // [layers][2][H] then [H]
     float2* rope = nullptr;            // [max_ctx][D/2] (cos, sin)
     void *kc = nullptr, *vc = nullptr; // [layers][max_ctx][hkv*D]
-    float *x, *q, *k, *vv, *att_l, *att, *delta_l, *delta, *gate, *up, *h_l, *hh, *logits_l, *logits, *scratch;
+    float *x, *xn, *q, *k, *vv, *att_l, *att, *delta_l, *delta, *h_l, *hh, *logits_l, *logits, *scratch;
+    float* norm_partials = nullptr;    // [matvec_max_ctas()] per-CTA sums of squares
+    unsigned int* norm_counter = nullptr;
     float* act_base = nullptr;
     int* io = nullptr;                 // device {pos, token, argmax}
     int* tokens = nullptr;             // device [max_ctx]: greedy token emitted at each position
@@ -241,17 +267,15 @@ DecodeModel* find(unsigned long long h) {
     return it == g_models.end() ? nullptr : it->second.get();
 }
 
-cudaError_t matvec(const DecodeModel& m, const Nf4* ws, float* const* ys, const int* rows, int n, const float* x, int K,
-                   int prologue, const float* norm_w, const float* gate, const float* residual) {
+// One NF4 matvec launch over 1-3 row segments sharing x.
+cudaError_t matvec(const DecodeModel& m, const Nf4* ws, float* const* ys, const int* rows, int n, const float* x,
+                   int K, int epilogue, const float* residual, float* norm_out, const float* norm_w) {
     MatvecParams p = {};
     p.nseg = n;
     p.K = K;
     p.group = m.group;
     p.x = x;
-    p.prologue = prologue;
-    p.norm_w = norm_w;
-    p.norm_eps = m.eps;
-    p.gate = gate;
+    p.epilogue = epilogue;
     for (int i = 0; i < n; ++i) {
         p.seg[i].w = ws[i].codes;
         p.seg[i].absmax = ws[i].absmax;
@@ -259,6 +283,14 @@ cudaError_t matvec(const DecodeModel& m, const Nf4* ws, float* const* ys, const 
         p.seg[i].rows = rows[i];
         p.seg[i].residual = residual;
         p.total_rows += rows[i];
+    }
+    if (epilogue == EPI_SWIGLU_PAIR) p.total_rows = rows[0];
+    if (norm_out) {
+        p.norm_out = norm_out;
+        p.norm_w = norm_w;
+        p.norm_eps = m.eps;
+        p.norm_partials = m.norm_partials;
+        p.norm_counter = m.norm_counter;
     }
     return launch_matvec(FMT_NF4, p, m.stream, true);
 }
@@ -277,19 +309,20 @@ cudaError_t matvec(const DecodeModel& m, const Nf4* ws, float* const* ys, const 
 cudaError_t record_step(DecodeModel& m) {
     const int D = m.D;
     const int sms = sm_count_for_current_device();
-    REC(launch_small(embed_nf4_kernel, (m.H + 255) / 256, 256, m.stream, m.x, m.embd.codes, m.embd.absmax, m.io,
-                     m.H, m.group));
+    const float* out_norm = m.norms + static_cast<size_t>(m.layers) * 2 * m.H;
+    REC(launch_small(embed_nf4_kernel, 1, 1024, m.stream, m.x, m.xn, m.embd.codes, m.embd.absmax, m.io, m.H, m.group,
+                     static_cast<const float*>(m.norms), m.eps));
     for (int l = 0; l < m.layers; ++l) {
         const auto& w = m.w[l];
-        const float* attn_norm = m.norms + static_cast<size_t>(l) * 2 * m.H;
-        const float* ffn_norm = attn_norm + m.H;
+        const float* ffn_norm = m.norms + static_cast<size_t>(l) * 2 * m.H + m.H;
+        const float* next_norm = l + 1 < m.layers ? m.norms + static_cast<size_t>(l + 1) * 2 * m.H : out_norm;
         void* kc = static_cast<uint8_t*>(m.kc) + static_cast<size_t>(l) * m.kv_layer_elems() * m.kv_elem();
         void* vc = static_cast<uint8_t*>(m.vc) + static_cast<size_t>(l) * m.kv_layer_elems() * m.kv_elem();
-        {   // q, k, v (GgufDecodePass.java:305-309)
+        {   // q, k, v from the normed x (GgufDecodePass.java:305-309)
             const Nf4 ws[3] = {w[W_Q], w[W_K], w[W_V]};
             float* ys[3] = {m.q, m.k, m.vv};
             const int rows[3] = {m.hq * D, m.hkv * D, m.hkv * D};
-            REC(matvec(m, ws, ys, rows, 3, m.x, m.H, PRO_RMSNORM, attn_norm, nullptr, nullptr));
+            REC(matvec(m, ws, ys, rows, 3, m.xn, m.H, EPI_STORE, nullptr, nullptr, nullptr));
         }
         // RoPE on q and k, KV store (GgufDecodePass.java:333-362)
         REC(launch_small(rope_store_kernel, std::max(1, ((m.hq + m.hkv) * D / 2 + 255) / 256), 256, m.stream, m.q,
@@ -317,53 +350,52 @@ cudaError_t record_step(DecodeModel& m) {
             REC(launch_attention(a, m.stream, true));
         }
         if (m.T > 1) RECN(g_nccl.allGather(m.att_l, m.att, static_cast<size_t>(m.hq) * D, ncclFloat, m.comm, m.stream));
-        {   // o-proj + residual (GgufDecodePass.java:475-481)
+        {   // o-proj + residual (GgufDecodePass.java:475-481), then the FFN norm (:485)
             const Nf4 ws[1] = {w[W_O]};
-            float* ys[1] = {m.T > 1 ? m.delta_l : m.x};
             const int rows[1] = {m.h};
-            REC(matvec(m, ws, ys, rows, 1, m.att, m.Hq * D, PRO_NONE, nullptr, nullptr, m.T > 1 ? nullptr : m.x));
-        }
-        if (m.T > 1) {
-            RECN(g_nccl.allGather(m.delta_l, m.delta, m.h, ncclFloat, m.comm, m.stream));
-            REC(launch_small(add_kernel, (m.H + 255) / 256, 256, m.stream, m.x, static_cast<const float*>(m.delta), m.H));
-        }
-        {   // gate / up (GgufDecodePass.java:485-492)
-            const Nf4 ws[2] = {w[W_GATE], w[W_UP]};
-            float* ys[2] = {m.gate, m.up};
-            const int rows[2] = {m.f, m.f};
-            REC(matvec(m, ws, ys, rows, 2, m.x, m.H, PRO_RMSNORM, ffn_norm, nullptr, nullptr));
-        }
-        {   // SwiGLU + down-proj + residual (GgufDecodePass.java:497-511)
-            const Nf4 ws[1] = {w[W_DOWN]};
             if (m.T > 1) {
-                REC(launch_small(swiglu_kernel, (m.f + 255) / 256, 256, m.stream, m.h_l,
-                                 static_cast<const float*>(m.gate), static_cast<const float*>(m.up), m.f));
-                RECN(g_nccl.allGather(m.h_l, m.hh, m.f, ncclFloat, m.comm, m.stream));
                 float* ys[1] = {m.delta_l};
-                const int rows[1] = {m.h};
-                REC(matvec(m, ws, ys, rows, 1, m.hh, m.F, PRO_NONE, nullptr, nullptr, nullptr));
+                REC(matvec(m, ws, ys, rows, 1, m.att, m.Hq * D, EPI_STORE, nullptr, nullptr, nullptr));
                 RECN(g_nccl.allGather(m.delta_l, m.delta, m.h, ncclFloat, m.comm, m.stream));
-                REC(launch_small(add_kernel, (m.H + 255) / 256, 256, m.stream, m.x, static_cast<const float*>(m.delta),
-                                 m.H));
+                REC(launch_small(add_norm_kernel, 1, 1024, m.stream, m.x, static_cast<const float*>(m.delta), m.xn,
+                                 ffn_norm, m.H, m.eps));
             } else {
                 float* ys[1] = {m.x};
-                const int rows[1] = {m.h};
-                REC(matvec(m, ws, ys, rows, 1, m.up, m.F, PRO_SWIGLU, nullptr, m.gate, m.x));
+                REC(matvec(m, ws, ys, rows, 1, m.att, m.Hq * D, EPI_STORE, m.x, m.xn, ffn_norm));
+            }
+        }
+        {   // gate / up with the SwiGLU epilogue (GgufDecodePass.java:492-497)
+            const Nf4 ws[2] = {w[W_GATE], w[W_UP]};
+            float* ys[2] = {m.T > 1 ? m.h_l : m.hh, nullptr};
+            const int rows[2] = {m.f, m.f};
+            REC(matvec(m, ws, ys, rows, 2, m.xn, m.H, EPI_SWIGLU_PAIR, nullptr, nullptr, nullptr));
+        }
+        if (m.T > 1) RECN(g_nccl.allGather(m.h_l, m.hh, m.f, ncclFloat, m.comm, m.stream));
+        {   // down-proj + residual (GgufDecodePass.java:504-511), then the next layer's norm
+            const Nf4 ws[1] = {w[W_DOWN]};
+            const int rows[1] = {m.h};
+            if (m.T > 1) {
+                float* ys[1] = {m.delta_l};
+                REC(matvec(m, ws, ys, rows, 1, m.hh, m.F, EPI_STORE, nullptr, nullptr, nullptr));
+                RECN(g_nccl.allGather(m.delta_l, m.delta, m.h, ncclFloat, m.comm, m.stream));
+                REC(launch_small(add_norm_kernel, 1, 1024, m.stream, m.x, static_cast<const float*>(m.delta), m.xn,
+                                 next_norm, m.H, m.eps));
+            } else {
+                float* ys[1] = {m.x};
+                REC(matvec(m, ws, ys, rows, 1, m.hh, m.F, EPI_STORE, m.x, m.xn, next_norm));
             }
         }
     }
-    {   // output norm + logits (GgufLogitsProcessor.compute)
+    {   // logits from the output-normed x (GgufLogitsProcessor.compute)
         const Nf4 ws[1] = {m.head};
         float* ys[1] = {m.T > 1 ? m.logits_l : m.logits};
         const int rows[1] = {m.v};
-        REC(matvec(m, ws, ys, rows, 1, m.x, m.H, PRO_RMSNORM, m.norms + static_cast<size_t>(m.layers) * 2 * m.H, nullptr,
-                   nullptr));
+        REC(matvec(m, ws, ys, rows, 1, m.xn, m.H, EPI_STORE, nullptr, nullptr, nullptr));
     }
     if (m.T > 1) RECN(g_nccl.allGather(m.logits_l, m.logits, m.v, ncclFloat, m.comm, m.stream));
     REC(launch_small(argmax_kernel, std::max(1, std::min(sms, (m.V + 1023) / 1024)), 1024, m.stream,
                      static_cast<const float*>(m.logits), m.V, m.io));
     REC(launch_small(advance_kernel, 1, 32, m.stream, m.io, m.tokens, m.max_ctx));
-    (void)sms;
     return cudaSuccess;
 }
 
@@ -466,7 +498,7 @@ int aljabr_blackwell_decode_model_create(const int* dims, float eps, float rope_
     auto ok = [&](cudaError_t e) { return e == cudaSuccess; };
     const size_t kvb = static_cast<size_t>(m->layers) * m->kv_layer_elems() * m->kv_elem();
     const size_t acts = static_cast<size_t>(m->H) + m->hq * m->D + 2 * m->hkv * m->D + m->hq * m->D + m->Hq * m->D +
-                        m->h + m->H + 2 * m->f + m->f + m->F + m->v + m->V +
+                        m->h + m->H + m->f + m->F + m->v + m->V + m->H + matvec_max_ctas() + 4 +
                         attention_scratch_floats(m->hq, m->D, m->splits) + 64;
     if (!ok(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking)) || !ok(cudaMalloc(&m->kc, kvb)) ||
         !ok(cudaMalloc(&m->vc, kvb)) || !ok(cudaMalloc(&m->act_base, acts * 4)) ||
@@ -507,8 +539,11 @@ int aljabr_blackwell_decode_model_create(const int* dims, float eps, float rope_
     auto take = [&](size_t n) { float* r = p; p += (n + 3) / 4 * 4; return r; };
     m->x = take(m->H); m->q = take(m->hq * m->D); m->k = take(m->hkv * m->D); m->vv = take(m->hkv * m->D);
     m->att_l = take(m->hq * m->D); m->att = take(m->Hq * m->D); m->delta_l = take(m->h); m->delta = take(m->H);
-    m->gate = take(m->f); m->up = take(m->f); m->h_l = take(m->f); m->hh = take(m->F);
+    m->h_l = take(m->f); m->hh = take(m->F);
     m->logits_l = take(m->v); m->logits = take(m->V);
+    m->xn = take(m->H);
+    m->norm_partials = take(matvec_max_ctas());
+    m->norm_counter = reinterpret_cast<unsigned int*>(take(4));   // zeroed by the memset above
     m->scratch = take(attention_scratch_floats(m->hq, m->D, m->splits));
     if (T > 1) {
         if (!nccl_id) { destroy(m.get()); return decode_fail(ALJ_ERR_BAD_ARG, "TP > 1 needs an NCCL unique id"); }

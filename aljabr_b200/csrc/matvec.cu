@@ -1,27 +1,35 @@
 // Batch-1 dequantise-and-matvec kernels (y = W x) for GGUF Q4_0 / Q8_0 and
 // NF4 weights on B200 (sm_100a), plus the bit-exact dequantisation kernels.
 //
-// Design (HBM-bound streaming, one persistent CTA per SM):
+// Design (HBM-bound streaming; two CTAs per SM so that, under programmatic
+// dependent launch, the next matvec's weight copies start while the
+// previous one finishes):
 //   * rows are handed out in units of 4; each CTA owns a contiguous,
-//     balanced range of units and walks it in tiles of 32 rows x K-chunks;
+//     balanced range of units and walks it in tiles (32 rows NF4, 16 rows
+//     GGUF) x K-chunks;
 //   * one producer thread streams each tile's chunk into shared memory with
-//     2-D TMA tensor copies (one 4-row box per copy, cp.async.bulk.tensor),
+//     2-D TMA tensor copies (one 4-row box per copy, cp.async.bulk.tensor)
 //     completing on an mbarrier, through a multi-stage ring of empty/full
-//     barrier pairs; the boxes land densely, row after row;
-//   * 16 consumer warps each own 2 rows of the tile; inside a warp the lanes
-//     split the chunk's columns, and each lane keeps its column slice of x in
-//     registers for both rows, so shared memory carries only the weights;
-//     per-row partial sums stay in the lane until the tile's last chunk and
-//     are then reduced with 5 shuffles -- no cross-warp reduction;
+//     barrier pairs; boxes land densely, row after row;
+//   * 8 consumer warps each own every 8th row of the tile; inside a warp the
+//     lanes split the chunk's columns, and each lane loads its slice of x
+//     straight from global memory into registers once per chunk and reuses
+//     it for all its rows -- shared memory carries only weights;
+//   * per-row partial sums stay in the lane until the tile's last chunk and
+//     are then reduced with 5 shuffles: no cross-warp reduction;
 //   * 4-bit / 8-bit GGUF codes become exact floats with one LOP3 each (the
 //     code placed in the mantissa of 2^23) and one packed f32x2 add per two
 //     codes; products accumulate with packed f32x2 FMA;
-//   * NF4 bytes index a 256-entry table of value pairs (T[hi], T[lo]),
-//     replicated per lane in shared memory (entry b of lane l at
-//     8 * (32 b + l)): one conflict-free LDS.64 yields both weights of a byte
-//     as an f32x2 operand;
+//   * NF4 bytes index a 256-entry table of value pairs (T[hi], T[lo]) with 16
+//     copies in shared memory (entry b, copy c at 8 * (16 b + c)); an LDS.64
+//     is served per half-warp, so lane l reading copy l % 16 is
+//     conflict-free, and one load yields both weights of a byte;
 //   * block scales (fp16 d for GGUF, fp32 absmax for NF4) are applied once
 //     per block to the block's partial sum.
+// Epilogues: plain store with optional bias / residual; SwiGLU over a
+// gate/up segment pair (both rows of a pair land in the same warp); and an
+// optional RMSNorm of the finished output vector, written by the last CTA
+// to finish (fixed-order reduction of per-CTA partials, deterministic).
 // Shapes the TMA path cannot stage (K not a multiple of 256, segment rows
 // not a multiple of 4, unaligned pointers, other NF4 groups) run a plain
 // one-warp-per-row kernel instead.
@@ -31,6 +39,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 namespace alj {
@@ -47,15 +56,13 @@ __device__ const float kNf4Table[16] = {
 
 __device__ __forceinline__ float nf4_at(int code) { return kNf4Table[code & 15]; }
 
-constexpr int kConsumerWarps = 16;
+constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;
 constexpr int kUnitRows = 4;                      // rows per TMA box
-constexpr int kTileUnits = 8;
-constexpr int kTileRows = kUnitRows * kTileUnits; // 32 = 16 warps x 2 rows
 constexpr int kMaxStages = 8;
-constexpr int kSmemLimit = 232448;                // 227 KB opt-in per CTA on sm_100
-constexpr int kLutBytes = 256 * 32 * 8;           // NF4 byte-pair table, per lane
+constexpr int kCtaSmemBudget = 115712;            // two CTAs per SM (228 KB minus 1 KB each)
+constexpr int kLutBytes = 256 * 16 * 8;           // NF4 byte-pair table, 16 copies
 
 template <int FMT>
 struct Fmt;
@@ -66,6 +73,7 @@ struct Fmt<FMT_Q4_0> {
     static constexpr int kLaneF4 = 16;           // x float4s per lane
     static constexpr int kBoxInner = 144;        // in UINT64 elements
     static constexpr int kElemBytes = 8;
+    static constexpr int kTileRows = 16;
     static size_t row_bytes(int K) { return static_cast<size_t>(K) / 32 * 18; }
 };
 template <>
@@ -75,6 +83,7 @@ struct Fmt<FMT_Q8_0> {
     static constexpr int kLaneF4 = 8;
     static constexpr int kBoxInner = 136;
     static constexpr int kElemBytes = 8;
+    static constexpr int kTileRows = 16;
     static size_t row_bytes(int K) { return static_cast<size_t>(K) / 32 * 34; }
 };
 template <>
@@ -84,6 +93,7 @@ struct Fmt<FMT_NF4> {
     static constexpr int kLaneF4 = 8;
     static constexpr int kBoxInner = 128;        // in UINT32 elements
     static constexpr int kElemBytes = 4;
+    static constexpr int kTileRows = 32;
     static size_t row_bytes(int K) { return static_cast<size_t>(K) / 2; }
 };
 
@@ -102,11 +112,13 @@ struct alignas(64) TmaParams {
     int nseg;
     int K;
     int total_rows;
-    int prologue;
-    float norm_eps;
+    int epilogue;
     const float* x;
+    float* norm_out;
     const float* norm_w;
-    const float* gate;
+    float norm_eps;
+    float* norm_partials;
+    unsigned int* norm_counter;
 };
 
 // Exact magic constants: float(0x4B000000 | (c << s)) = 2^23 + c * 2^s.
@@ -133,47 +145,45 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
 }
 
 // ---- per-format row dots over one chunk (this lane's columns) -------------
-// Q4_0: this lane's two blocks (36 B at 36*lane: word-aligned, conflict-free
-// since 9 is odd).  Block A's fp16 d is word-aligned and its codes 2 bytes
-// off; block B the reverse.  x holds per block eight float4s in the order
-// (x_j, x_{j+16}, x_{j+1}, x_{j+17}), (x_{j+2}, x_{j+18}, x_{j+3}, x_{j+19}),
-// j = 4i, matching ggml's nibble order (low nibble of byte j = element j,
-// high nibble = element j + 16).
+// Q4_0 block with natural-order x (xb[i] = x[4i..4i+3], xb[4+i] =
+// x[16+4i..]): byte j holds element j (low nibble) and j+16 (high nibble).
+// Low nibbles of bytes (j, j+1) sit at bits (0, 8) of a code word and pair
+// with (x_j, x_{j+1}); high nibbles at bits (4, 12) pair with (x_{j+16},
+// x_{j+17}).  Scales per lane of the packed pair: lo (1, 256), hi (16, 4096).
 __device__ __forceinline__ float q4_0_block(uint32_t dbits, const uint32_t (&c)[4], const float4* xb) {
-    const f2 k01 = mk2(-(kTwo23 + 8.0f), -(kTwo23 + 128.0f));
-    const f2 k23 = mk2(-(kTwo23 + 2048.0f), -(kTwo23 + 32768.0f));
-    const f2 fold = mk2(1.0f / 256.0f, 1.0f / 256.0f);   // a23's 256x / 4096x units onto a01's 1x / 16x
-    f2 a01 = mk2(0.0f, 0.0f), a23 = mk2(0.0f, 0.0f);
+    const f2 klo = mk2(-(kTwo23 + 8.0f), -(kTwo23 + 2048.0f));
+    const f2 khi = mk2(-(kTwo23 + 128.0f), -(kTwo23 + 32768.0f));
+    f2 alo = mk2(0.0f, 0.0f), ahi = mk2(0.0f, 0.0f);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const float4 xa = xb[2 * i], xc = xb[2 * i + 1];
+        const float4 xl = xb[i], xh = xb[4 + i];
         const uint32_t w = c[i], w2 = w >> 16;
-        const f2 p0 = add2(mk2u((w & 0xFu) | kMagic, (w & 0xF0u) | kMagic), k01);
-        const f2 p1 = add2(mk2u((w & 0xF00u) | kMagic, (w & 0xF000u) | kMagic), k23);
-        const f2 p2 = add2(mk2u((w2 & 0xFu) | kMagic, (w2 & 0xF0u) | kMagic), k01);
-        const f2 p3 = add2(mk2u((w2 & 0xF00u) | kMagic, (w2 & 0xF000u) | kMagic), k23);
-        a01 = fma2(p0, mk2(xa.x, xa.y), a01);
-        a23 = fma2(p1, mk2(xa.z, xa.w), a23);
-        a01 = fma2(p2, mk2(xc.x, xc.y), a01);
-        a23 = fma2(p3, mk2(xc.z, xc.w), a23);
+        const f2 l0 = add2(mk2u((w & 0xFu) | kMagic, (w & 0xF00u) | kMagic), klo);       // elements 4i, 4i+1
+        const f2 h0 = add2(mk2u((w & 0xF0u) | kMagic, (w & 0xF000u) | kMagic), khi);     // 4i+16, 4i+17
+        const f2 l1 = add2(mk2u((w2 & 0xFu) | kMagic, (w2 & 0xF00u) | kMagic), klo);     // 4i+2, 4i+3
+        const f2 h1 = add2(mk2u((w2 & 0xF0u) | kMagic, (w2 & 0xF000u) | kMagic), khi);   // 4i+18, 4i+19
+        alo = fma2(l0, mk2(xl.x, xl.y), alo);
+        ahi = fma2(h0, mk2(xh.x, xh.y), ahi);
+        alo = fma2(l1, mk2(xl.z, xl.w), alo);
+        ahi = fma2(h1, mk2(xh.z, xh.w), ahi);
     }
-    const f2 t = fma2(a23, fold, a01);
-    const float bs = fmaf(hi(t), 0.0625f, lo(t));
+    // alo = (s1, 256 s1'), ahi = (16 s, 4096 s'): fold to 16x units, then 1x
+    const f2 t = fma2(alo, mk2(16.0f, 1.0f / 16.0f), mk2(hi(ahi) * (1.0f / 256.0f), lo(ahi)));
+    const float bs = (lo(t) + hi(t)) * 0.0625f;
     return __half2float(__ushort_as_half(static_cast<unsigned short>(dbits))) * bs;
 }
 
-__device__ __forceinline__ float q4_0_row(uint32_t row_addr, int lane, const float4* x) {
-    uint32_t W[9];
-    const uint32_t a = row_addr + lane * 36;
+// Block bb (0 or 1) of this lane's two: block 0's fp16 d is word-aligned and
+// its codes 2 bytes off, block 1 the reverse (words 4..8 of the 36 bytes).
+__device__ __forceinline__ float q4_0_half(uint32_t row_addr, int lane, int bb, const float4* x) {
+    const uint32_t a = row_addr + lane * 36 + bb * 16;
+    uint32_t W[5];
 #pragma unroll
-    for (int k = 0; k < 9; ++k) W[k] = lds_u32(a + 4 * k);
-    uint32_t cA[4], cB[4];
+    for (int k = 0; k < 5; ++k) W[k] = lds_u32(a + 4 * k);
+    uint32_t c[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        cA[i] = __funnelshift_r(W[i], W[i + 1], 16);
-        cB[i] = W[5 + i];
-    }
-    return q4_0_block(W[0] & 0xFFFFu, cA, x) + q4_0_block(W[4] >> 16, cB, x + 8);
+    for (int i = 0; i < 4; ++i) c[i] = bb ? W[1 + i] : __funnelshift_r(W[i], W[i + 1], 16);
+    return q4_0_block(bb ? (W[0] >> 16) : (W[0] & 0xFFFFu), c, x);
 }
 
 // Q8_0: this lane's block (34 B at 34*lane).  Even lanes start word-aligned
@@ -209,7 +219,7 @@ __device__ __forceinline__ float q8_0_row(uint32_t row_addr, int lane, const flo
 }
 
 // NF4: this lane's 16 code bytes (32 weights, inside one absmax group) at
-// 16*lane.  lut_lane = shared address of this lane's column of the table.
+// 16*lane.  lut_lane = shared address of copy (lane % 16) of entry 0.
 __device__ __forceinline__ float nf4_row(uint32_t row_addr, float am, uint32_t lane_off, uint32_t lut_lane,
                                          const float4* x) {
     uint32_t w[4];
@@ -220,11 +230,11 @@ __device__ __forceinline__ float nf4_row(uint32_t row_addr, float am, uint32_t l
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         // byte b of word k -> weights 8k+2b (high nibble), 8k+2b+1 (low nibble);
-        // __byte_perm(w, 0, 0x44b4) moves byte b to bits 8..15 = 256 * byte
-        const float2 t0 = lds_f2(lut_lane + __byte_perm(w[k], 0, 0x4404));
-        const float2 t1 = lds_f2(lut_lane + __byte_perm(w[k], 0, 0x4414));
-        const float2 t2 = lds_f2(lut_lane + __byte_perm(w[k], 0, 0x4424));
-        const float2 t3 = lds_f2(lut_lane + __byte_perm(w[k], 0, 0x4434));
+        // entry of byte v: lut_lane + 128 v
+        const float2 t0 = lds_f2(lut_lane + (__byte_perm(w[k], 0, 0x4440) << 7));
+        const float2 t1 = lds_f2(lut_lane + (__byte_perm(w[k], 0, 0x4441) << 7));
+        const float2 t2 = lds_f2(lut_lane + (__byte_perm(w[k], 0, 0x4442) << 7));
+        const float2 t3 = lds_f2(lut_lane + (__byte_perm(w[k], 0, 0x4443) << 7));
         const float4 x0 = x[2 * k], x1 = x[2 * k + 1];
         A = fma2(mk2(t0.x, t0.y), mk2(x0.x, x0.y), A);
         B = fma2(mk2(t1.x, t1.y), mk2(x0.z, x0.w), B);
@@ -233,65 +243,6 @@ __device__ __forceinline__ float nf4_row(uint32_t row_addr, float am, uint32_t l
     }
     const f2 t = add2(A, B);
     return am * (lo(t) + hi(t));
-}
-
-// ---- x staging --------------------------------------------------------------
-// Destination layout: per chunk, per lane float4 slot j, per lane:
-// xs4[(chunk * kLaneF4 + j) * 32 + lane], so that a warp's load of slot j is
-// 32 consecutive float4s (conflict-free).  Elements past K are zero.
-template <int FMT>
-__device__ __forceinline__ int x_source(int q, int comp) {
-    using F = Fmt<FMT>;
-    constexpr int per_chunk = F::kLaneF4 * 32;
-    const int chunk = q / per_chunk;
-    const int rem = q - chunk * per_chunk;
-    const int j = rem >> 5, ln = rem & 31;
-    if (FMT == FMT_Q4_0) {
-        const int bb = j >> 3, f = j & 7;
-        const int base = chunk * F::kChunkElems + (ln * 2 + bb) * 32 + 4 * (f >> 1) + 2 * (f & 1);
-        return base + (comp >> 1) + 16 * (comp & 1);   // (x_j, x_{j+16}, x_{j+1}, x_{j+17})
-    }
-    return chunk * F::kChunkElems + ln * 32 + 4 * j + comp;
-}
-
-template <int FMT>
-__device__ void stage_x(const TmaParams& p, float4* xs4, float* red, int Kp) {
-    const int tid = threadIdx.x;
-    const int K = p.K;
-    float scale = 1.0f;
-    if (p.prologue == PRO_RMSNORM) {
-        float ss = 0.0f;
-        for (int i = tid * 4; i < K; i += kConsumerThreads * 4) {
-            const float4 v = *reinterpret_cast<const float4*>(p.x + i);
-            ss = fmaf(v.x, v.x, ss); ss = fmaf(v.y, v.y, ss); ss = fmaf(v.z, v.z, ss); ss = fmaf(v.w, v.w, ss);
-        }
-        ss = warp_sum(ss);
-        if ((tid & 31) == 0) red[tid >> 5] = ss;
-        named_bar(1, kConsumerThreads);
-        float tot = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) tot += red[w];
-        scale = 1.0f / sqrtf(tot / static_cast<float>(K) + p.norm_eps);
-    }
-    for (int q = tid; q < Kp / 4; q += kConsumerThreads) {
-        float v[4];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const int e = x_source<FMT>(q, c);
-            float a = 0.0f;
-            if (e < K) {
-                a = p.x[e];
-                if (p.prologue == PRO_RMSNORM) {
-                    a = a * scale * p.norm_w[e];
-                } else if (p.prologue == PRO_SWIGLU) {
-                    const float g = p.gate[e];
-                    a = g / (1.0f + expf(-g)) * a;
-                }
-            }
-            v[c] = a;
-        }
-        xs4[q] = make_float4(v[0], v[1], v[2], v[3]);
-    }
 }
 
 __device__ __forceinline__ void locate_row(const TmaParams& p, int row, int& seg, int& lrow) {
@@ -303,51 +254,45 @@ __device__ __forceinline__ void locate_row(const TmaParams& p, int row, int& seg
 
 template <int FMT, int GROUP>
 constexpr int stage_bytes() {
-    return ((kTileRows * Fmt<FMT>::kChunkBytes + (FMT == FMT_NF4 ? kTileRows * (1024 / GROUP) * 4 : 0)) + 1023) &
-           ~1023;
+    return ((Fmt<FMT>::kTileRows * Fmt<FMT>::kChunkBytes +
+             (FMT == FMT_NF4 ? Fmt<FMT>::kTileRows * (1024 / GROUP) * 4 : 0)) + 1023) & ~1023;
 }
 
 template <int FMT, int GROUP>
-__global__ void __launch_bounds__(kThreads, 1) matvec_tma_kernel(const __grid_constant__ TmaParams p, int stages) {
+__global__ void __launch_bounds__(kThreads, 2) matvec_tma_kernel(const __grid_constant__ TmaParams p, int stages) {
     using F = Fmt<FMT>;
+    constexpr int T = F::kTileRows;
+    constexpr int R = T / kConsumerWarps;                    // rows per warp per tile
+    constexpr int kStage = stage_bytes<FMT, GROUP>();
+    constexpr int kAbsPerRow = 1024 / GROUP;                 // NF4 absmax floats per row-chunk
+    constexpr int kCodeTile = T * F::kChunkBytes;            // codes region of a stage
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     pdl_launch_dependents();
 
     const int K = p.K;
     const int nchunks = (K + F::kChunkElems - 1) / F::kChunkElems;
-    const int Kp = nchunks * F::kChunkElems;
-    constexpr int kStage = stage_bytes<FMT, GROUP>();
-    constexpr int kAbsPerRow = 1024 / GROUP;                 // NF4 absmax floats per row-chunk
-    constexpr int kCodeTile = kTileRows * F::kChunkBytes;    // codes region of a stage
+    const bool pair = p.epilogue == EPI_SWIGLU_PAIR;
+    const int unit_rows_per_tile = pair ? T / 2 : T;         // logical rows per tile
+    const int tile_units = unit_rows_per_tile / kUnitRows;
 
     const uint32_t base = smem_u32(smem_raw);
     const uint32_t pad = (1024u - (base & 1023u)) & 1023u;
     uint8_t* sp = smem_raw + pad;
     uint8_t* stage0 = sp;
     sp += static_cast<size_t>(stages) * kStage;
-    float4* xs4 = reinterpret_cast<float4*>(sp);
-    sp += static_cast<size_t>(Kp) * 4;
-    uint32_t lut_lane = 0;
-    if (FMT == FMT_NF4) {
-        float2* lut = reinterpret_cast<float2*>(sp);
-        for (int i = threadIdx.x; i < 256 * 32; i += kThreads) {
-            const int b = i >> 5;
-            lut[i] = make_float2(nf4_at(b >> 4), nf4_at(b & 15));
-        }
-        lut_lane = smem_u32(lut) + (threadIdx.x & 31) * 8;
-        sp += kLutBytes;
-    }
+    float2* lut = reinterpret_cast<float2*>(sp);
+    if (FMT == FMT_NF4) sp += kLutBytes;
     float* red = reinterpret_cast<float*>(sp);
-    sp += kConsumerWarps * 4;
+    sp += 64;
     uint64_t* full = reinterpret_cast<uint64_t*>(sp);
     uint64_t* empty = full + kMaxStages;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kMaxStages);
+    volatile int* flags = reinterpret_cast<volatile int*>(empty + kMaxStages);   // [0] abort, [1] last CTA
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int units = p.total_rows / kUnitRows;
     const int u_begin = static_cast<int>(static_cast<long long>(units) * blockIdx.x / gridDim.x);
     const int u_end = static_cast<int>(static_cast<long long>(units) * (blockIdx.x + 1) / gridDim.x);
-    const int ntiles = (u_end - u_begin + kTileUnits - 1) / kTileUnits;
+    const int ntiles = (u_end - u_begin + tile_units - 1) / tile_units;
     const int items = ntiles * nchunks;
 
     if (threadIdx.x == 0) {
@@ -355,93 +300,177 @@ __global__ void __launch_bounds__(kThreads, 1) matvec_tma_kernel(const __grid_co
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
         }
-        *abort_flag = 0;
+        flags[0] = 0;
+        flags[1] = 0;
         fence_mbar_init();
     }
     __syncthreads();
 
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------------ producer
+        // Weights never depend on the previous kernel, so the copies start
+        // before griddepcontrol.wait.
         if (lane == 0) {
             for (int it = 0; it < items; ++it) {
                 const int t = it / nchunks, c = it - t * nchunks;
                 const int s = it % stages;
                 const uint32_t round = static_cast<uint32_t>(it / stages);
-                const int tu0 = u_begin + t * kTileUnits;
-                const int nunits = min(kTileUnits, u_end - tu0);
-                if (*abort_flag || !mbar_wait(&empty[s], (round & 1u) ^ 1u)) {
-                    *abort_flag = 1;
+                const int tu0 = u_begin + t * tile_units;
+                const int nunits = min(tile_units, u_end - tu0);
+                if (flags[0] || !mbar_wait(&empty[s], (round & 1u) ^ 1u)) {
+                    flags[0] = 1;
                     break;
                 }
-                const uint32_t per_unit = kUnitRows * (F::kChunkBytes + (FMT == FMT_NF4 ? kAbsPerRow * 4 : 0));
-                mbar_arrive_expect_tx(&full[s], per_unit * nunits);
+                const uint32_t per_box = kUnitRows * (F::kChunkBytes + (FMT == FMT_NF4 ? kAbsPerRow * 4 : 0));
+                mbar_arrive_expect_tx(&full[s], per_box * nunits * (pair ? 2 : 1));
                 uint8_t* st = stage0 + static_cast<size_t>(s) * kStage;
                 for (int u = 0; u < nunits; ++u) {
-                    int seg, lrow;
-                    locate_row(p, (tu0 + u) * kUnitRows, seg, lrow);
-                    tma_load_2d(smem_u32(st + u * kUnitRows * F::kChunkBytes), &p.seg[seg].codes, c * F::kBoxInner,
-                                lrow, &full[s]);
-                    if (FMT == FMT_NF4)
-                        tma_load_2d(smem_u32(st + kCodeTile + u * kUnitRows * kAbsPerRow * 4), &p.seg[seg].absmax,
-                                    c * kAbsPerRow, lrow, &full[s]);
+                    const int lrow_g = (tu0 + u) * kUnitRows;
+                    for (int half = 0; half < (pair ? 2 : 1); ++half) {
+                        int seg, lrow;
+                        if (pair) {
+                            seg = half;
+                            lrow = lrow_g;
+                        } else {
+                            locate_row(p, lrow_g, seg, lrow);
+                        }
+                        const int srow = u * kUnitRows + half * (T / 2);
+                        tma_load_2d(smem_u32(st + srow * F::kChunkBytes), &p.seg[seg].codes, c * F::kBoxInner, lrow,
+                                    &full[s]);
+                        if (FMT == FMT_NF4)
+                            tma_load_2d(smem_u32(st + kCodeTile + srow * kAbsPerRow * 4), &p.seg[seg].absmax,
+                                        c * kAbsPerRow, lrow, &full[s]);
+                    }
                 }
             }
         }
     } else {
         // ------------------------------------------------------------ consumers
-        pdl_wait();
-        stage_x<FMT>(p, xs4, red, Kp);
-        named_bar(1, kConsumerThreads);
-        float acc0 = 0.0f, acc1 = 0.0f;
-        const int r0 = warp, r1 = warp + kConsumerWarps;
+        if (FMT == FMT_NF4) {
+            for (int i = threadIdx.x; i < 256 * 16; i += kConsumerThreads) {
+                const int b = i >> 4;
+                lut[i] = make_float2(nf4_at(b >> 4), nf4_at(b & 15));
+            }
+            named_bar(1, kConsumerThreads);
+        }
+        const uint32_t lut_lane = smem_u32(lut) + (lane & 15) * 8;
+        pdl_wait();   // x (and residual) come from the previous kernel
+        float acc[R];
+#pragma unroll
+        for (int k = 0; k < R; ++k) acc[k] = 0.0f;
+        float sq = 0.0f;   // this warp's share of sum(y^2) for the optional norm
         for (int it = 0; it < items; ++it) {
             const int t = it / nchunks, c = it - t * nchunks;
             const int s = it % stages;
             const uint32_t round = static_cast<uint32_t>(it / stages);
-            const int tu0 = u_begin + t * kTileUnits;
-            const int trows = min(kTileUnits, u_end - tu0) * kUnitRows;
-            const bool ok = (*abort_flag == 0) && mbar_wait(&full[s], round & 1u);
-            if (!ok) *abort_flag = 1;
-            if (ok && r0 < trows) {
-                float4 xr[F::kLaneF4];
+            const int tu0 = u_begin + t * tile_units;
+            const int valid = min(tile_units, u_end - tu0) * kUnitRows;   // valid rows per tile half
+            // this lane's slice of x for chunk c: 32 floats (one Q4_0 block at a time)
+            const int e0 = c * F::kChunkElems + lane * (F::kLaneF4 * 4);
+            float4 xr[8];
 #pragma unroll
-                for (int j = 0; j < F::kLaneF4; ++j) xr[j] = xs4[(c * F::kLaneF4 + j) * 32 + lane];
+            for (int j = 0; j < 8; ++j)
+                xr[j] = (e0 + 4 * j < K) ? __ldg(reinterpret_cast<const float4*>(p.x + e0) + j)
+                                         : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            const bool ok = (flags[0] == 0) && mbar_wait(&full[s], round & 1u);
+            if (!ok) flags[0] = 1;
+            if (ok) {
                 const uint32_t st = smem_u32(stage0 + static_cast<size_t>(s) * kStage);
-                if (FMT == FMT_Q4_0) {
-                    acc0 += q4_0_row(st + r0 * F::kChunkBytes, lane, xr);
-                    if (r1 < trows) acc1 += q4_0_row(st + r1 * F::kChunkBytes, lane, xr);
-                } else if (FMT == FMT_Q8_0) {
-                    acc0 += q8_0_row(st + r0 * F::kChunkBytes, lane, xr);
-                    if (r1 < trows) acc1 += q8_0_row(st + r1 * F::kChunkBytes, lane, xr);
-                } else {
-                    const float* am =
-                        reinterpret_cast<const float*>(stage0 + static_cast<size_t>(s) * kStage + kCodeTile);
-                    const int g = (lane * 32) / GROUP;
-                    acc0 += nf4_row(st + r0 * F::kChunkBytes, am[r0 * kAbsPerRow + g], lane * 16, lut_lane, xr);
-                    if (r1 < trows)
-                        acc1 += nf4_row(st + r1 * F::kChunkBytes, am[r1 * kAbsPerRow + g], lane * 16, lut_lane, xr);
+                const float* am = reinterpret_cast<const float*>(stage0 + static_cast<size_t>(s) * kStage + kCodeTile);
+#pragma unroll
+                for (int bb = 0; bb < (FMT == FMT_Q4_0 ? 2 : 1); ++bb) {
+                    if (bb == 1) {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            xr[j] = (e0 + 32 + 4 * j < K)
+                                        ? __ldg(reinterpret_cast<const float4*>(p.x + e0 + 32) + j)
+                                        : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    }
+#pragma unroll
+                    for (int k = 0; k < R; ++k) {
+                        const int r = warp + kConsumerWarps * k;
+                        const int rl = pair ? (r % (T / 2)) : r;
+                        if (rl < valid) {
+                            if (FMT == FMT_Q4_0) {
+                                acc[k] += q4_0_half(st + r * F::kChunkBytes, lane, bb, xr);
+                            } else if (FMT == FMT_Q8_0) {
+                                acc[k] += q8_0_row(st + r * F::kChunkBytes, lane, xr);
+                            } else {
+                                acc[k] += nf4_row(st + r * F::kChunkBytes, am[r * kAbsPerRow + (lane * 32) / GROUP],
+                                                  lane * 16, lut_lane, xr);
+                            }
+                        }
+                    }
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
             if (c == nchunks - 1) {
+                float v[R];
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int r = h ? r1 : r0;
-                    if (r < trows) {
-                        const float v = warp_sum(h ? acc1 : acc0);
-                        if (lane == 0 && *abort_flag == 0) {
-                            int seg, lrow;
-                            locate_row(p, tu0 * kUnitRows + r, seg, lrow);
-                            const TmaSegment& sg = p.seg[seg];
-                            float out = v;
-                            if (sg.bias) out += sg.bias[lrow];
-                            if (sg.residual) out = sg.residual[lrow] + out;
-                            sg.y[lrow] = out;
+                for (int k = 0; k < R; ++k) {
+                    const int r = warp + kConsumerWarps * k;
+                    const int rl = pair ? (r % (T / 2)) : r;
+                    v[k] = rl < valid ? warp_sum(acc[k]) : 0.0f;
+                    acc[k] = 0.0f;
+                }
+                if (lane == 0 && flags[0] == 0) {
+                    if (pair) {
+#pragma unroll
+                        for (int k = 0; k < R / 2; ++k) {
+                            const int r = warp + kConsumerWarps * k;
+                            if (r < valid) {
+                                const float g = v[k], u = v[k + R / 2];
+                                p.seg[0].y[tu0 * kUnitRows + r] = g / (1.0f + expf(-g)) * u;
+                            }
+                        }
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < R; ++k) {
+                            const int r = warp + kConsumerWarps * k;
+                            if (r < valid) {
+                                int seg, lrow;
+                                locate_row(p, tu0 * kUnitRows + r, seg, lrow);
+                                const TmaSegment& sg = p.seg[seg];
+                                float out = v[k];
+                                if (sg.bias) out += sg.bias[lrow];
+                                if (sg.residual) out = sg.residual[lrow] + out;
+                                sg.y[lrow] = out;
+                                sq = fmaf(out, out, sq);
+                            }
                         }
                     }
                 }
-                acc0 = acc1 = 0.0f;
+            }
+        }
+        if (p.norm_out) {
+            // Deterministic RMSNorm of the whole output: per-CTA partials in
+            // fixed order, finished by the last CTA to arrive.
+            __threadfence();
+            if (lane == 0) red[warp] = sq;
+            named_bar(1, kConsumerThreads);
+            if (threadIdx.x == 0) {
+                float cta = 0.0f;
+                for (int w = 0; w < kConsumerWarps; ++w) cta += red[w];
+                p.norm_partials[blockIdx.x] = cta;
+                __threadfence();
+                const unsigned int prev = atomicAdd(p.norm_counter, 1u);
+                flags[1] = prev == gridDim.x - 1;
+            }
+            named_bar(1, kConsumerThreads);
+            if (flags[1]) {
+                __threadfence();
+                if (threadIdx.x == 0) {
+                    float tot = 0.0f;
+                    for (unsigned int b = 0; b < gridDim.x; ++b) tot += __ldcg(p.norm_partials + b);
+                    red[8] = 1.0f / sqrtf(tot / static_cast<float>(p.total_rows) + p.norm_eps);
+                    *p.norm_counter = 0u;
+                }
+                named_bar(1, kConsumerThreads);
+                const float scale = red[8];
+                const float* y = p.seg[0].y;
+                for (int i = threadIdx.x; i < p.total_rows; i += kConsumerThreads)
+                    p.norm_out[i] = __ldcg(y + i) * scale * p.norm_w[i];
             }
         }
     }
@@ -585,11 +614,7 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, cons
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-size_t fixed_smem(int fmt, int K) {
-    const int chunk = fmt == FMT_Q4_0 ? Fmt<FMT_Q4_0>::kChunkElems : 1024;
-    const size_t Kp = (static_cast<size_t>(K) + chunk - 1) / chunk * chunk;
-    return 1024 + Kp * 4 + (fmt == FMT_NF4 ? kLutBytes : 0) + kConsumerWarps * 4 + 2 * kMaxStages * 8 + 64;
-}
+size_t fixed_smem(int fmt) { return 1024 + (fmt == FMT_NF4 ? kLutBytes : 0) + 64 + 2 * kMaxStages * 8 + 64; }
 
 int stage_size(int fmt, int group) {
     switch (fmt) {
@@ -599,8 +624,8 @@ int stage_size(int fmt, int group) {
     }
 }
 
-int stages_for(int fmt, int K, int group) {
-    const long long avail = kSmemLimit - static_cast<long long>(fixed_smem(fmt, K));
+int stages_for(int fmt, int group) {
+    const long long avail = kCtaSmemBudget - static_cast<long long>(fixed_smem(fmt));
     const long long s = avail / stage_size(fmt, group);
     return static_cast<int>(std::min<long long>(s, kMaxStages));
 }
@@ -613,11 +638,13 @@ cudaError_t launch_tma(const MatvecParams& mp, cudaStream_t stream, bool pdl) {
     p.nseg = mp.nseg;
     p.K = mp.K;
     p.total_rows = mp.total_rows;
-    p.prologue = mp.prologue;
-    p.norm_eps = mp.norm_eps;
+    p.epilogue = mp.epilogue;
     p.x = mp.x;
+    p.norm_out = mp.norm_out;
     p.norm_w = mp.norm_w;
-    p.gate = mp.gate;
+    p.norm_eps = mp.norm_eps;
+    p.norm_partials = mp.norm_partials;
+    p.norm_counter = mp.norm_counter;
     const CUtensorMapDataType dt = F::kElemBytes == 8 ? CU_TENSOR_MAP_DATA_TYPE_UINT64 : CU_TENSOR_MAP_DATA_TYPE_UINT32;
     int row0 = 0;
     for (int s = 0; s < mp.nseg; ++s) {
@@ -625,9 +652,8 @@ cudaError_t launch_tma(const MatvecParams& mp, cudaStream_t stream, bool pdl) {
         TmaSegment& ts = p.seg[s];
         if (!encode_2d(&ts.codes, dt, F::kElemBytes, sg.w, F::row_bytes(mp.K), sg.rows, F::kBoxInner))
             return cudaErrorInvalidValue;
-        if (FMT == FMT_NF4 &&
-            !encode_2d(&ts.absmax, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, sg.absmax,
-                       static_cast<size_t>(mp.K) / GROUP * 4, sg.rows, 1024 / GROUP))
+        if (FMT == FMT_NF4 && !encode_2d(&ts.absmax, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, sg.absmax,
+                                         static_cast<size_t>(mp.K) / GROUP * 4, sg.rows, 1024 / GROUP))
             return cudaErrorInvalidValue;
         ts.bias = sg.bias;
         ts.residual = sg.residual;
@@ -636,19 +662,18 @@ cudaError_t launch_tma(const MatvecParams& mp, cudaStream_t stream, bool pdl) {
         ts.row0 = row0;
         row0 += sg.rows;
     }
-    const int stages = stages_for(FMT, mp.K, GROUP);
-    const size_t smem = fixed_smem(FMT, mp.K) + static_cast<size_t>(stages) * stage_bytes<FMT, GROUP>();
+    const int stages = stages_for(FMT, GROUP);
+    const size_t smem = fixed_smem(FMT) + static_cast<size_t>(stages) * stage_bytes<FMT, GROUP>();
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (!configured[dev & 63]) {
         cudaError_t e = cudaFuncSetAttribute(matvec_tma_kernel<FMT, GROUP>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, kCtaSmemBudget);
         if (e != cudaSuccess) return e;
         configured[dev & 63] = true;
     }
-    const int sms = sm_count_for_current_device();
-    const int grid = std::max(1, std::min(sms, mp.total_rows / kUnitRows));
+    const int grid = std::max(1, std::min(matvec_max_ctas(), mp.total_rows / kUnitRows));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
@@ -680,23 +705,27 @@ cudaError_t launch_generic(const MatvecParams& p, cudaStream_t stream, bool pdl)
 
 }  // namespace
 
+int matvec_max_ctas() { return 2 * sm_count_for_current_device(); }
+
 bool matvec_tma_supported(int fmt, int K, int group) {
     if (K <= 0 || K % 256 != 0) return false;
     if (fmt == FMT_NF4 && !(group == 64 || (group == 128 && K % 512 == 0))) return false;
-    if (stages_for(fmt, K, fmt == FMT_NF4 ? group : 32) < 2) return false;
+    if (stages_for(fmt, fmt == FMT_NF4 ? group : 32) < 2) return false;
     return encode_fn() != nullptr;
 }
 
 cudaError_t launch_matvec(int fmt, const MatvecParams& p, cudaStream_t stream, bool pdl) {
     if (p.total_rows <= 0) return cudaSuccess;
     // TMA tensor boxes need 16-byte aligned bases and whole 4-row units per
-    // segment; the x prologue reads float4.
+    // segment; x is read as float4.
     bool ok = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
     for (int s = 0; s < p.nseg; ++s) {
         ok = ok && (reinterpret_cast<uintptr_t>(p.seg[s].w) & 15) == 0 && p.seg[s].rows % kUnitRows == 0;
         if (fmt == FMT_NF4) ok = ok && (reinterpret_cast<uintptr_t>(p.seg[s].absmax) & 15) == 0;
     }
-    if (p.prologue == PRO_RMSNORM) ok = ok && (reinterpret_cast<uintptr_t>(p.norm_w) & 15) == 0;
+    if (p.epilogue == EPI_SWIGLU_PAIR) ok = ok && p.nseg == 2 && p.seg[0].rows == p.seg[1].rows &&
+                                              p.total_rows == p.seg[0].rows;
+    if (p.norm_out) ok = ok && p.nseg == 1 && p.norm_partials && p.norm_counter && p.norm_w;
     if (ok && matvec_tma_supported(fmt, p.K, p.group)) {
         switch (fmt) {
             case FMT_Q4_0: return launch_tma<FMT_Q4_0, 32>(p, stream, pdl);
@@ -707,7 +736,7 @@ cudaError_t launch_matvec(int fmt, const MatvecParams& p, cudaStream_t stream, b
         }
         return cudaErrorInvalidValue;
     }
-    if (p.prologue != PRO_NONE) return cudaErrorNotSupported;
+    if (p.epilogue != EPI_STORE || p.norm_out) return cudaErrorNotSupported;
     switch (fmt) {
         case FMT_Q4_0: return launch_generic<FMT_Q4_0>(p, stream, pdl);
         case FMT_Q8_0: return launch_generic<FMT_Q8_0>(p, stream, pdl);
