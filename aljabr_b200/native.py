@@ -79,6 +79,7 @@ SIGNATURES = {
     "aljabr_blackwell_matvec_dev": (_i, [_i, _p, _p, _p, _p, _i, _i, _i, _p, _p]),
     "aljabr_blackwell_dequantize_dev": (_i, [_i, _p, _p, _p, _ll, _i, _p]),
     "aljabr_blackwell_decode_attention_dev": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _p]),
+    "aljabr_blackwell_decode_attention_noalloc": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _p]),
     "aljabr_blackwell_nccl_unique_id": (_i, [_p, _i]),
     "aljabr_blackwell_decode_model_create": (_i, [ctypes.POINTER(_i), _f, _f, _i, _i, _p,
                                                   ctypes.POINTER(ctypes.c_ulonglong)]),
