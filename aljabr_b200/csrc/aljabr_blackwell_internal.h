@@ -56,6 +56,9 @@ int matvec_max_ctas();
 // programmatic dependent launch on the stream.
 cudaError_t launch_matvec(int fmt, const MatvecParams& p, cudaStream_t stream, bool pdl);
 bool matvec_tma_supported(int fmt, int K, int group);
+// Tensor-core path (Q4_0, K a multiple of 2048); launch_matvec picks it first.
+bool matvec_mma_supported(int fmt, int K);
+cudaError_t launch_matvec_mma(int fmt, const MatvecParams& p, cudaStream_t stream, bool pdl);
 
 cudaError_t launch_dequant(int fmt, float* dst, const uint8_t* src, const float* absmax, int64_t numel,
                            int group, cudaStream_t stream);

@@ -705,6 +705,8 @@ cudaError_t launch_generic(const MatvecParams& p, cudaStream_t stream, bool pdl)
 
 }  // namespace
 
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() { return encode_fn(); }
+
 int matvec_max_ctas() { return 2 * sm_count_for_current_device(); }
 
 bool matvec_tma_supported(int fmt, int K, int group) {
@@ -716,6 +718,10 @@ bool matvec_tma_supported(int fmt, int K, int group) {
 
 cudaError_t launch_matvec(int fmt, const MatvecParams& p, cudaStream_t stream, bool pdl) {
     if (p.total_rows <= 0) return cudaSuccess;
+    if (matvec_mma_supported(fmt, p.K)) {
+        const cudaError_t e = launch_matvec_mma(fmt, p, stream, pdl);
+        if (e != cudaErrorNotSupported) return e;
+    }
     // TMA tensor boxes need 16-byte aligned bases and whole 4-row units per
     // segment; x is read as float4.
     bool ok = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
