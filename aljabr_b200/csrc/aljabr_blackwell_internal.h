@@ -48,6 +48,10 @@ struct MatvecParams {
     float norm_eps;
     float* norm_partials;
     unsigned int* norm_counter;
+    // Optional L2 prefetch of the weights the following launch reads (each CTA
+    // its 1/grid share, after its own copies are issued).
+    const void* prefetch;
+    size_t prefetch_bytes;
 };
 // CTAs a TMA matvec launches (the size norm_partials must have).
 int matvec_max_ctas();
@@ -59,6 +63,9 @@ bool matvec_tma_supported(int fmt, int K, int group);
 // Tensor-core path (Q4_0, K a multiple of 2048); launch_matvec picks it first.
 bool matvec_mma_supported(int fmt, int K);
 cudaError_t launch_matvec_mma(int fmt, const MatvecParams& p, cudaStream_t stream, bool pdl);
+// NF4 table path (K a multiple of 2048, group 64 or 128); picked second.
+bool matvec_lut_supported(int fmt, int K, int group);
+cudaError_t launch_matvec_lut(int fmt, const MatvecParams& p, cudaStream_t stream, bool pdl);
 
 cudaError_t launch_dequant(int fmt, float* dst, const uint8_t* src, const float* absmax, int64_t numel,
                            int group, cudaStream_t stream);

@@ -25,6 +25,8 @@ namespace {
 thread_local std::string t_last_error;
 thread_local int t_device = -1;
 thread_local bool t_pdl = false;
+thread_local const void* t_prefetch = nullptr;   // one-shot L2 prefetch hint (device address)
+thread_local size_t t_prefetch_bytes = 0;
 int g_verbose = 0;
 
 int fail(int code, const char* fmt, ...) {
@@ -217,6 +219,10 @@ int run_matvecs(DeviceState* st, const MatSpec* m, int n, const float* dx, int K
             p.seg[i].rows = m[i].N;
             p.total_rows += m[i].N;
         }
+        p.prefetch = t_prefetch;
+        p.prefetch_bytes = t_prefetch_bytes;
+        t_prefetch = nullptr;
+        t_prefetch_bytes = 0;
         return launch_status(launch_matvec(fmt_of(m[0].type), p, stream, pdl), "matvec");
     }
     for (int i = 0; i < n; ++i) {
@@ -436,6 +442,22 @@ const char* aljabr_blackwell_last_error(void) { return t_last_error.c_str(); }
 
 int aljabr_blackwell_set_pdl(int enable) {
     t_pdl = enable != 0;
+    return ALJ_OK;
+}
+
+int aljabr_blackwell_prefetch_hint(const void* next_weights, size_t bytes) {
+    if (!next_weights || bytes == 0) {
+        t_prefetch = nullptr;
+        t_prefetch_bytes = 0;
+        return ALJ_OK;
+    }
+    int err = 0;
+    DeviceState* st = state(&err);
+    if (!st) return err;
+    const void* d = resolve(st, next_weights);
+    if (!d) return fail(ALJ_ERR_NOT_REGISTERED, "prefetch hint: not device or registered memory");
+    t_prefetch = d;
+    t_prefetch_bytes = bytes;
     return ALJ_OK;
 }
 

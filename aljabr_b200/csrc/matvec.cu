@@ -722,6 +722,10 @@ cudaError_t launch_matvec(int fmt, const MatvecParams& p, cudaStream_t stream, b
         const cudaError_t e = launch_matvec_mma(fmt, p, stream, pdl);
         if (e != cudaErrorNotSupported) return e;
     }
+    if (matvec_lut_supported(fmt, p.K, p.group)) {
+        const cudaError_t e = launch_matvec_lut(fmt, p, stream, pdl);
+        if (e != cudaErrorNotSupported) return e;
+    }
     // TMA tensor boxes need 16-byte aligned bases and whole 4-row units per
     // segment; x is read as float4.
     bool ok = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;

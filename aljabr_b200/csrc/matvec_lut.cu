@@ -1,0 +1,542 @@
+// Batch-1 NF4 dequantise-and-matvec (y = W x, bitsandbytes layout: two codes
+// per byte, high nibble first, one fp32 absmax per `group` elements) on B200
+// (sm_100a), for K a multiple of 2048 and group 64 or 128.
+//
+// NF4 values are 16 arbitrary constants, so a code cannot become a tensor-core
+// operand with bit tricks; the work stays on the CUDA cores and is shaped so
+// that each weight costs ~1.8 instructions:
+//   * a 64 KB table in shared memory maps a code byte b to the float pair
+//     (T[b >> 4], T[b & 15]), 32 copies (entry b, copy c at 256 b + 8 c): lane
+//     l reads copy l, so the 8-byte loads of a half warp hit 16 distinct bank
+//     pairs whatever the bytes are, and one PRMT builds the address
+//     (b << 8 | 8 l) from the code word;
+//   * one packed f32x2 FMA per byte multiplies the pair with (x[2i], x[2i+1]);
+//   * rows are dealt out in balanced units of 4 and walked in slabs of up to
+//     32 rows (pair mode: 16 gate + 16 up rows) x chunks of 2048 columns; a
+//     producer warp streams each slab-chunk with 2-D TMA boxes of 8 or 4 rows
+//     (codes: 1024 B per row; absmax: 2048 / group floats per row) plus the
+//     chunk of x as a 2-D box {32 floats, 64} with 128-byte swizzle, so the
+//     16-byte x loads below are bank-conflict free;
+//   * warp w covers column quarter w % 4 (512 columns, 16 per lane) of the
+//     slab rows r with r % 4 == w / 4: x (16 floats per lane) is loaded once
+//     per chunk and reused for up to 8 rows, each lane applies the absmax of
+//     its 16 columns once per row;
+//   * per-lane row partials are reduced across the warp with a butterfly at
+//     the end of the slab, and the epilogue warp sums the four column quarters
+//     in fixed order (deterministic), applying bias / residual / SwiGLU and
+//     the optional last-CTA RMSNorm, as the tensor-core Q4_0 kernel does.
+// Every mbarrier wait is bounded (ALJ_FAULT_TIMEOUT in the device fault word).
+#include "common.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
+
+namespace alj {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();   // matvec.cu
+
+namespace {
+
+constexpr int kCW = 16;
+constexpr int kConsumers = kCW * 32;
+constexpr int kProducerWarp = kCW;
+constexpr int kEpilogueWarp = kCW + 1;
+constexpr int kThreads = (kCW + 2) * 32;
+constexpr int kUnit = 4;
+constexpr int kSlabRows = 32;
+constexpr int kChunkElems = 2048;
+constexpr int kCodeRowBytes = kChunkElems / 2;             // 1024
+constexpr int kXBytes = kChunkElems * 4;                   // 8 KB
+constexpr int kLutBytes = 256 * 32 * 8;                    // 64 KB
+constexpr int kMaxStages = 4;
+constexpr int kRing = 4;
+constexpr int kSmemMax = 232448;
+
+__constant__ float kNf4[16] = {
+    -1.0f, -0.6961928009986877f, -0.5250730514526367f, -0.39491748809814453f,
+    -0.28444138169288635f, -0.18477343022823334f, -0.09105003625154495f, 0.0f,
+    0.07958029955625534f, 0.16093020141124725f, 0.24611230194568634f, 0.33791524171829224f,
+    0.44070982933044434f, 0.5626170039176941f, 0.7229568362236023f, 1.0f};
+
+struct alignas(64) LutSegment {
+    CUtensorMap codes8, codes4;     // box {128 x 8 B, 8 | 4 rows}
+    CUtensorMap abs8, abs4;         // box {2048 / group floats, 8 | 4 rows}
+    const float* bias;
+    const float* residual;
+    float* y;
+    int rows;
+    int row0;
+};
+
+struct alignas(64) LutParams {
+    LutSegment seg[3];
+    CUtensorMap xmap;               // x as [K / 32][32] floats, box {32, 64}, 128-byte swizzle
+    int nseg;
+    int K;
+    int group;
+    int total_rows;
+    int pair;
+    float* norm_out;
+    const float* norm_w;
+    float norm_eps;
+    float* norm_partials;
+    unsigned int* norm_counter;
+    const uint8_t* prefetch;
+    size_t prefetch_bytes;
+};
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ uint2 lds64u(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ f2 lds_pair(uint32_t a) {
+    unsigned long long v;
+    asm volatile("ld.shared.b64 %0, [%1];" : "=l"(v) : "r"(a));
+    return f2{v};
+}
+__device__ __forceinline__ float4 lds128f(uint32_t a) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ float lds32f(uint32_t a) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+    return v;
+}
+
+__device__ __forceinline__ void prefetch_share(const uint8_t* base, size_t bytes) {
+    const size_t share = bytes / gridDim.x;
+    const uintptr_t b0 = reinterpret_cast<uintptr_t>(base);
+    uintptr_t a = (b0 + share * blockIdx.x + 15) & ~uintptr_t(15);
+    const size_t cap = share < (size_t(128) << 10) ? share : (size_t(128) << 10);
+    const uintptr_t lim = b0 + share * blockIdx.x + cap;
+    const uintptr_t end = (lim < b0 + bytes ? lim : b0 + bytes) & ~uintptr_t(15);
+    for (; a + 16 <= end; a += 16384) {
+        const uintptr_t left = end - a;
+        const uint32_t n = static_cast<uint32_t>(left < 16384 ? left : 16384) & ~15u;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(n) : "memory");
+    }
+}
+
+// norm_out = y * scale * norm_w over the whole output, by the last CTA's
+// consumer warps and epilogue warp (participant index 0 .. 16 * 32 + 31).
+template <typename P>
+__device__ __forceinline__ void norm_pass(const P& p, float scale, int idx) {
+    const float* y = p.seg[0].y;
+    for (int i = idx; i < p.total_rows; i += kCW * 32 + 32) p.norm_out[i] = __ldcg(y + i) * scale * p.norm_w[i];
+}
+
+struct SlabWalk {
+    int u, u_end;
+    __device__ __forceinline__ bool next(const LutParams& p, int& seg, int& su, int& nunits) {
+        if (u >= u_end) return false;
+        seg = 0;
+        int seg_end = p.total_rows / kUnit;
+        if (!p.pair) {
+            if (p.nseg > 1 && u * kUnit >= p.seg[1].row0) seg = 1;
+            if (p.nseg > 2 && u * kUnit >= p.seg[2].row0) seg = 2;
+            seg_end = (p.seg[seg].row0 + p.seg[seg].rows) / kUnit;
+        }
+        su = u;
+        nunits = min(p.pair ? kSlabRows / (2 * kUnit) : kSlabRows / kUnit, min(u_end, seg_end) - u);
+        u += nunits;
+        return true;
+    }
+};
+
+struct StageLayout {
+    int abs_row_bytes;   // 4 * 2048 / group
+    int abs_off;         // codes: 32 rows x 1024 B
+    int x_off;           // 1024-aligned
+    int bytes;
+};
+__host__ __device__ inline StageLayout stage_layout(int group) {
+    StageLayout L;
+    L.abs_row_bytes = 4 * (kChunkElems / group);
+    L.abs_off = kSlabRows * kCodeRowBytes;
+    L.x_off = (L.abs_off + kSlabRows * L.abs_row_bytes + 1023) & ~1023;
+    L.bytes = L.x_off + kXBytes;
+    return L;
+}
+
+// Issue the boxes of `nunits` 4-row units starting at segment row r0 into
+// slab rows [srow, srow + 4 nunits).
+__device__ __forceinline__ void load_rows(const LutSegment& sg, int r0, int nunits, int srow, int chunk,
+                                          uint32_t st, const StageLayout& L, int abs_elems, uint64_t* bar) {
+    for (int u = 0; u < nunits;) {
+        const bool eight = nunits - u >= 2;
+        const int rr = srow + u * kUnit;
+        tma_load_2d(st + rr * kCodeRowBytes, eight ? &sg.codes8 : &sg.codes4, chunk * (kCodeRowBytes / 8),
+                    r0 + u * kUnit, bar);
+        tma_load_2d(st + L.abs_off + rr * L.abs_row_bytes, eight ? &sg.abs8 : &sg.abs4, chunk * abs_elems,
+                    r0 + u * kUnit, bar);
+        u += eight ? 2 : 1;
+    }
+}
+
+template <int GROUP>
+__global__ void __launch_bounds__(kThreads, 1) nf4_lut_kernel(const __grid_constant__ LutParams p, int stages) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    pdl_launch_dependents();
+    const int K = p.K;
+    const int nchunks = K / kChunkElems;
+    const StageLayout L = stage_layout(GROUP);
+    constexpr int kAbsElems = kChunkElems / GROUP;
+    // [0, 64 KB) table | stages (1024-aligned) | ring | misc | barriers
+    const uint32_t lut_s = smem_u32(smem_raw);
+    const uint32_t base = lut_s + kLutBytes;
+    const uint32_t stage_s = (base + 1023u) & ~1023u;
+    uint8_t* after = smem_raw + (stage_s - lut_s) + static_cast<size_t>(stages) * L.bytes;
+    float* red = reinterpret_cast<float*>(after);      // [kRing][kCW][8]
+    float* misc = red + kRing * kCW * 8;
+    uint64_t* full = reinterpret_cast<uint64_t*>(misc + 16);
+    uint64_t* empty = full + kMaxStages;
+    uint64_t* rfull = empty + kMaxStages;
+    uint64_t* rempty = rfull + kRing;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int units = p.total_rows / kUnit;
+    const int u_begin = static_cast<int>(static_cast<long long>(units) * blockIdx.x / gridDim.x);
+    const int u_end = static_cast<int>(static_cast<long long>(units) * (blockIdx.x + 1) / gridDim.x);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kCW);
+        }
+        for (int b = 0; b < kRing; ++b) {
+            mbar_init(&rfull[b], kCW);
+            mbar_init(&rempty[b], 1);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == kProducerWarp) {
+        if (lane == 0) {
+            SlabWalk walk{u_begin, u_end};
+            int seg, su, nunits, s = 0;
+            uint32_t ph = 0;
+            bool alive = true;
+            bool x_waited = false;
+            while (alive && walk.next(p, seg, su, nunits)) {
+                const int rows = nunits * kUnit * (p.pair ? 2 : 1);
+                for (int c = 0; c < nchunks; ++c) {
+                    if (!mbar_wait(&empty[s], ph ^ 1u)) {
+                        alive = false;
+                        break;
+                    }
+                    const uint32_t st = stage_s + s * L.bytes;
+                    mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rows * (kCodeRowBytes + L.abs_row_bytes) + kXBytes));
+                    if (p.pair) {
+                        load_rows(p.seg[0], su * kUnit, nunits, 0, c, st, L, kAbsElems, &full[s]);
+                        load_rows(p.seg[1], su * kUnit, nunits, kSlabRows / 2, c, st, L, kAbsElems, &full[s]);
+                    } else {
+                        load_rows(p.seg[seg], su * kUnit - p.seg[seg].row0, nunits, 0, c, st, L, kAbsElems, &full[s]);
+                    }
+                    // x comes from the previous kernel: its first copy waits for it.
+                    if (!x_waited) {
+                        pdl_wait();
+                        x_waited = true;
+                    }
+                    tma_load_2d(st + L.x_off, &p.xmap, 0, c * (kChunkElems / 32), &full[s]);
+                    if (++s == stages) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+            }
+            if (alive && p.prefetch) prefetch_share(p.prefetch, p.prefetch_bytes);
+        }
+        return;
+    }
+
+    if (warp == kEpilogueWarp) {
+        pdl_wait();
+        SlabWalk walk{u_begin, u_end};
+        int seg, su, nunits, sl = 0;
+        float sq = 0.0f;
+        while (walk.next(p, seg, su, nunits)) {
+            const int b = sl % kRing;
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(&rfull[b], (sl / kRing) & 1));
+            if (ok) {
+                // slab row r: row group r % 4, slot r / 4; the four column quarters in order
+                const int i = lane & 3, j = lane >> 2;
+                float acc = 0.0f;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc += red[(b * kCW + 4 * i + q) * 8 + j];
+                if (p.pair) {
+                    const float up = __shfl_down_sync(0xffffffffu, acc, 16);
+                    if (lane < nunits * kUnit) {
+                        const float out = acc / (1.0f + expf(-acc)) * up;
+                        p.seg[0].y[su * kUnit + lane] = out;
+                        sq = fmaf(out, out, sq);
+                    }
+                } else if (lane < nunits * kUnit) {
+                    const LutSegment& sg = p.seg[seg];
+                    const int lrow = su * kUnit + lane - sg.row0;
+                    float out = acc;
+                    if (sg.bias) out += sg.bias[lrow];
+                    if (sg.residual) out = sg.residual[lrow] + out;
+                    sg.y[lrow] = out;
+                    sq = fmaf(out, out, sq);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&rempty[b]);
+            ++sl;
+        }
+        if (p.norm_out) {
+            // Deterministic RMSNorm of the whole output: per-CTA partials in
+            // fixed order; the last CTA to arrive computes the scale, and all of
+            // its consumer warps plus this warp write norm_out.
+            __threadfence();   // this lane's y stores before the arrival below
+            const float cta = warp_sum(sq);
+            if (lane == 0) {
+                p.norm_partials[blockIdx.x] = cta;
+                __threadfence();
+                const unsigned int prev = atomicAdd(p.norm_counter, 1u);
+                misc[1] = prev == gridDim.x - 1 ? 1.0f : 0.0f;
+            }
+            __syncwarp();
+            if (misc[1] != 0.0f) {
+                __threadfence();
+                float part = 0.0f;
+                for (unsigned int b = lane; b < gridDim.x; b += 32) part += __ldcg(p.norm_partials + b);
+                const float tot = warp_sum(part);
+                if (lane == 0) {
+                    misc[0] = 1.0f / sqrtf(tot / static_cast<float>(p.total_rows) + p.norm_eps);
+                    *p.norm_counter = 0u;
+                }
+            }
+            named_bar(2, kCW * 32 + 32);
+            if (misc[1] != 0.0f) norm_pass(p, misc[0], kCW * 32 + lane);
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------------- consumers
+    {
+        // Byte-pair table, 32 copies: entry b, copy c at 256 b + 8 c.
+        float2* lut = reinterpret_cast<float2*>(smem_raw);
+        for (int e = threadIdx.x; e < 256 * 32; e += kConsumers) {
+            const int b = e >> 5;
+            lut[e] = make_float2(kNf4[b >> 4], kNf4[b & 15]);
+        }
+        named_bar(1, kConsumers);
+    }
+    const int q = warp & 3;                 // column quarter: columns [512 q, 512 q + 512) of a chunk
+    const int rg = warp >> 2;               // rows rg, rg + 4, ... of the slab
+    const uint32_t lane8 = static_cast<uint32_t>(lane) * 8u;
+    const uint32_t code_off = q * 256 + lane * 8;                           // this lane's 8 code bytes
+    const uint32_t abs_off = L.abs_off + ((q * 512 + lane * 16) / GROUP) * 4;
+    uint32_t xoff[4];                                                       // swizzled x granules
+    {
+        const uint32_t xrow = q * 16 + (lane >> 1);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t gran = (lane & 1) * 4 + k;
+            xoff[k] = L.x_off + xrow * 128 + ((gran ^ (xrow & 7)) << 4);
+        }
+    }
+
+    SlabWalk walk{u_begin, u_end};
+    int seg, su, nunits, s = 0, sl = 0;
+    uint32_t ph = 0;
+    while (walk.next(p, seg, su, nunits)) {
+        // slab rows with data: pair mode holds gate rows [0, 4n) and up rows [16, 16 + 4n)
+        const int valid = nunits * kUnit;
+        float acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+        for (int c = 0; c < nchunks; ++c) {
+            if (__all_sync(0xffffffffu, mbar_wait(&full[s], ph))) {
+                const uint32_t st = stage_s + s * L.bytes;
+                float4 xv[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) xv[k] = lds128f(st + xoff[k]);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int r = rg + 4 * j;
+                    const bool live = p.pair ? ((r & 15) < valid) : (r < valid);
+                    if (live) {
+                        const uint2 w = lds64u(st + r * kCodeRowBytes + code_off);
+                        const float am = lds32f(st + abs_off + r * L.abs_row_bytes);
+                        f2 A = mk2(0.0f, 0.0f), B = mk2(0.0f, 0.0f);
+#pragma unroll
+                        for (int m = 0; m < 8; ++m) {
+                            const uint32_t word = m < 4 ? w.x : w.y;
+                            const uint32_t sel = 0x5504u | (static_cast<uint32_t>(m & 3) << 4);
+                            const f2 t = lds_pair(lut_s + __byte_perm(word, lane8, sel));
+                            const float4& xx = xv[m >> 1];
+                            const f2 xp = (m & 1) ? mk2(xx.z, xx.w) : mk2(xx.x, xx.y);
+                            if (m & 1) B = fma2(t, xp, B);
+                            else A = fma2(t, xp, A);
+                        }
+                        const f2 t2 = add2(A, B);
+                        acc[j] = fmaf(am, lo(t2) + hi(t2), acc[j]);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (++s == stages) {
+                s = 0;
+                ph ^= 1u;
+            }
+        }
+        // Butterfly: after it, lane j (j < 8) holds slot j's sum over the warp.
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {   // xor 16: lanes < 16 keep slots 0..3, others 4..7
+            const float mine = lane < 16 ? acc[j] : acc[j + 4];
+            const float other = lane < 16 ? acc[j + 4] : acc[j];
+            acc[j] = mine + __shfl_xor_sync(0xffffffffu, other, 16);
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {   // xor 8
+            const bool up = (lane & 8) != 0;
+            const float mine = up ? acc[j + 2] : acc[j];
+            const float other = up ? acc[j] : acc[j + 2];
+            acc[j] = mine + __shfl_xor_sync(0xffffffffu, other, 8);
+        }
+        {                               // xor 4
+            const bool up = (lane & 4) != 0;
+            const float mine = up ? acc[1] : acc[0];
+            const float other = up ? acc[0] : acc[1];
+            acc[0] = mine + __shfl_xor_sync(0xffffffffu, other, 4);
+        }
+        acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 2);
+        acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 1);
+        // lane L now holds slot (L>>4)*4 + ((L>>3)&1)*2 + ((L>>2)&1); lanes 4m hold distinct slots
+        const int b = sl % kRing;
+        mbar_wait(&rempty[b], ((sl / kRing) & 1) ^ 1u);
+        if ((lane & 3) == 0) {
+            const int slot = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+            red[(b * kCW + warp) * 8 + slot] = acc[0];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&rfull[b]);
+        ++sl;
+    }
+    if (p.norm_out) {
+        named_bar(2, kCW * 32 + 32);
+        if (misc[1] != 0.0f) norm_pass(p, misc[0], threadIdx.x);
+    }
+}
+
+bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, cuuint64_t inner, cuuint64_t rows,
+               cuuint64_t row_bytes, cuuint32_t box_inner, cuuint32_t box_rows, CUtensorMapSwizzle swz) {
+    auto fn = tensor_map_encoder();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {inner, rows};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_inner, box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    return fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+size_t smem_bytes(int group, int stages) {
+    return kLutBytes + 1024 + static_cast<size_t>(stages) * stage_layout(group).bytes + kRing * kCW * 8 * 4 + 16 * 4 +
+           (2 * kMaxStages + 2 * kRing) * 8;
+}
+
+}  // namespace
+
+bool matvec_lut_supported(int fmt, int K, int group) {
+    if (fmt != FMT_NF4 || K <= 0 || K % kChunkElems != 0 || (group != 64 && group != 128)) return false;
+    return tensor_map_encoder() != nullptr && smem_bytes(group, 2) <= static_cast<size_t>(kSmemMax);
+}
+
+cudaError_t launch_matvec_lut(int fmt, const MatvecParams& mp, cudaStream_t stream, bool pdl) {
+    if (!matvec_lut_supported(fmt, mp.K, mp.group)) return cudaErrorNotSupported;
+    const bool pair = mp.epilogue == EPI_SWIGLU_PAIR;
+    if (pair && (mp.nseg != 2 || mp.seg[0].rows != mp.seg[1].rows || mp.total_rows != mp.seg[0].rows))
+        return cudaErrorNotSupported;
+    if ((reinterpret_cast<uintptr_t>(mp.x) & 15) != 0) return cudaErrorNotSupported;
+    for (int s = 0; s < mp.nseg; ++s)
+        if (mp.seg[s].rows % kUnit != 0 || (reinterpret_cast<uintptr_t>(mp.seg[s].w) & 15) != 0 ||
+            (reinterpret_cast<uintptr_t>(mp.seg[s].absmax) & 15) != 0)
+            return cudaErrorNotSupported;
+    LutParams p;
+    memset(&p, 0, sizeof p);
+    p.nseg = mp.nseg;
+    p.K = mp.K;
+    p.group = mp.group;
+    p.total_rows = mp.total_rows;
+    p.pair = pair ? 1 : 0;
+    p.norm_out = mp.norm_out;
+    p.norm_w = mp.norm_w;
+    p.norm_eps = mp.norm_eps;
+    p.norm_partials = mp.norm_partials;
+    p.norm_counter = mp.norm_counter;
+    p.prefetch = static_cast<const uint8_t*>(mp.prefetch);
+    p.prefetch_bytes = mp.prefetch_bytes;
+    const cuuint32_t abs_elems = static_cast<cuuint32_t>(kChunkElems / mp.group);
+    int row0 = 0;
+    for (int s = 0; s < mp.nseg; ++s) {
+        LutSegment& ls = p.seg[s];
+        const MatvecSegment& sg = mp.seg[s];
+        const cuuint64_t rows = static_cast<cuuint64_t>(sg.rows);
+        const cuuint64_t row_bytes = static_cast<cuuint64_t>(mp.K) / 2;
+        const cuuint64_t abs_row = static_cast<cuuint64_t>(mp.K / mp.group);
+        if (!encode_2d(&ls.codes8, CU_TENSOR_MAP_DATA_TYPE_UINT64, sg.w, row_bytes / 8, rows, row_bytes, 128, 8,
+                       CU_TENSOR_MAP_SWIZZLE_NONE) ||
+            !encode_2d(&ls.codes4, CU_TENSOR_MAP_DATA_TYPE_UINT64, sg.w, row_bytes / 8, rows, row_bytes, 128, 4,
+                       CU_TENSOR_MAP_SWIZZLE_NONE) ||
+            !encode_2d(&ls.abs8, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, sg.absmax, abs_row, rows, abs_row * 4, abs_elems, 8,
+                       CU_TENSOR_MAP_SWIZZLE_NONE) ||
+            !encode_2d(&ls.abs4, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, sg.absmax, abs_row, rows, abs_row * 4, abs_elems, 4,
+                       CU_TENSOR_MAP_SWIZZLE_NONE))
+            return cudaErrorInvalidValue;
+        ls.bias = sg.bias;
+        ls.residual = sg.residual;
+        ls.y = sg.y;
+        ls.rows = sg.rows;
+        ls.row0 = pair ? 0 : row0;
+        row0 += sg.rows;
+    }
+    if (!encode_2d(&p.xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, mp.x, 32, static_cast<cuuint64_t>(mp.K / 32), 128, 32, 64,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    int stages = kMaxStages;
+    while (stages > 2 && smem_bytes(mp.group, stages) > static_cast<size_t>(kSmemMax)) --stages;
+    const size_t smem = smem_bytes(mp.group, stages);
+    auto kern = mp.group == 64 ? nf4_lut_kernel<64> : nf4_lut_kernel<128>;
+    static bool configured[2][64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    bool& done = configured[mp.group == 64 ? 0 : 1][dev & 63];
+    if (!done) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+        if (e != cudaSuccess) return e;
+        done = true;
+    }
+    const int units = mp.total_rows / kUnit;
+    const int grid = std::max(1, std::min(sm_count_for_current_device(), units));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, p, stages);
+}
+
+}  // namespace alj

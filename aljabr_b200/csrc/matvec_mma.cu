@@ -58,7 +58,6 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();   // matvec.cu
 namespace {
 
 constexpr int kCW = 16;                        // consumer warps
-constexpr int kConsumers = kCW * 32;
 constexpr int kProducerWarp = kCW;
 constexpr int kEpilogueWarp = kCW + 1;
 constexpr int kThreads = (kCW + 2) * 32;
@@ -98,6 +97,8 @@ struct alignas(64) MmaParams {
     float norm_eps;
     float* norm_partials;
     unsigned int* norm_counter;
+    const uint8_t* prefetch;
+    size_t prefetch_bytes;
 };
 
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
@@ -140,8 +141,33 @@ __device__ __forceinline__ uint32_t land(uint32_t w, uint32_t m) {
     return r;
 }
 
+// L2 prefetch of this CTA's 1/grid share of [base, base + bytes) -- the part
+// the same CTA index of the next launch reads first (rows are contiguous and
+// dealt out in order) -- capped at 128 KB, strictly inside the range.
+__device__ __forceinline__ void prefetch_share(const uint8_t* base, size_t bytes) {
+    const size_t share = bytes / gridDim.x;
+    const uintptr_t b0 = reinterpret_cast<uintptr_t>(base);
+    uintptr_t a = (b0 + share * blockIdx.x + 15) & ~uintptr_t(15);
+    const size_t cap = share < (size_t(128) << 10) ? share : (size_t(128) << 10);
+    const uintptr_t lim = b0 + share * blockIdx.x + cap;
+    const uintptr_t end = (lim < b0 + bytes ? lim : b0 + bytes) & ~uintptr_t(15);
+    for (; a + 16 <= end; a += 16384) {
+        const uintptr_t left = end - a;
+        const uint32_t n = static_cast<uint32_t>(left < 16384 ? left : 16384) & ~15u;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(n) : "memory");
+    }
+}
+
 // Slabs of a CTA's unit range, split at segment boundaries (pair mode: both
 // segments advance together over the logical rows).
+// norm_out = y * scale * norm_w over the whole output, by the last CTA's
+// consumer warps and epilogue warp (participant index 0 .. 16 * 32 + 31).
+template <typename P>
+__device__ __forceinline__ void norm_pass(const P& p, float scale, int idx) {
+    const float* y = p.seg[0].y;
+    for (int i = idx; i < p.total_rows; i += kCW * 32 + 32) p.norm_out[i] = __ldcg(y + i) * scale * p.norm_w[i];
+}
+
 struct SlabWalk {
     int u, u_end;
     __device__ __forceinline__ bool next(const MmaParams& p, int& seg, int& su, int& nunits) {
@@ -238,6 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1) q4_0_mma_kernel(const __grid_cons
                     }
                 }
             }
+            if (alive && p.prefetch) prefetch_share(p.prefetch, p.prefetch_bytes);
         }
         return;
     }
@@ -279,7 +306,8 @@ __global__ void __launch_bounds__(kThreads, 1) q4_0_mma_kernel(const __grid_cons
         }
         if (p.norm_out) {
             // Deterministic RMSNorm of the whole output: per-CTA partials in
-            // fixed order, finished by the last CTA to arrive.
+            // fixed order; the last CTA to arrive computes the scale, and all of
+            // its consumer warps plus this warp write norm_out.
             __threadfence();   // this lane's y stores before the arrival below
             const float cta = warp_sum(sq);
             if (lane == 0) {
@@ -291,17 +319,16 @@ __global__ void __launch_bounds__(kThreads, 1) q4_0_mma_kernel(const __grid_cons
             __syncwarp();
             if (misc[1] != 0.0f) {
                 __threadfence();
-                float tot = 0.0f;
+                float part = 0.0f;
+                for (unsigned int b = lane; b < gridDim.x; b += 32) part += __ldcg(p.norm_partials + b);
+                const float tot = warp_sum(part);
                 if (lane == 0) {
-                    for (unsigned int b = 0; b < gridDim.x; ++b) tot += __ldcg(p.norm_partials + b);
                     misc[0] = 1.0f / sqrtf(tot / static_cast<float>(lrows) + p.norm_eps);
                     *p.norm_counter = 0u;
                 }
-                __syncwarp();
-                const float scale = misc[0];
-                const float* y = p.seg[0].y;
-                for (int i = lane; i < lrows; i += 32) p.norm_out[i] = __ldcg(y + i) * scale * p.norm_w[i];
             }
+            named_bar(2, kCW * 32 + 32);
+            if (misc[1] != 0.0f) norm_pass(p, misc[0], kCW * 32 + lane);
         }
         return;
     }
@@ -458,6 +485,10 @@ __global__ void __launch_bounds__(kThreads, 1) q4_0_mma_kernel(const __grid_cons
         if (lane == 0) mbar_arrive(&rfull[b]);
         ++sl;
     }
+    if (p.norm_out) {
+        named_bar(2, kCW * 32 + 32);
+        if (misc[1] != 0.0f) norm_pass(p, misc[0], threadIdx.x);
+    }
 }
 
 bool encode_q4_0_maps(MmaSegment& ms, const void* w, int K, int rows) {
@@ -512,6 +543,8 @@ cudaError_t launch_matvec_mma(int fmt, const MatvecParams& mp, cudaStream_t stre
     p.norm_eps = mp.norm_eps;
     p.norm_partials = mp.norm_partials;
     p.norm_counter = mp.norm_counter;
+    p.prefetch = static_cast<const uint8_t*>(mp.prefetch);
+    p.prefetch_bytes = mp.prefetch_bytes;
     int row0 = 0;
     for (int s = 0; s < mp.nseg; ++s) {
         MmaSegment& ms = p.seg[s];

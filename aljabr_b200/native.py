@@ -62,6 +62,7 @@ SIGNATURES = {
     "aljabr_blackwell_device_status": (_i, [ctypes.POINTER(ctypes.c_uint)]),
     "aljabr_blackwell_shutdown": (_i, []),
     "aljabr_blackwell_set_pdl": (_i, [_i]),
+    "aljabr_blackwell_prefetch_hint": (_i, [_p, _sz]),
     "aljabr_blackwell_register_model_buffer": (_i, [_p, _sz]),
     "aljabr_blackwell_unregister_model_buffer": (_i, [_p]),
     "aljabr_blackwell_device_address": (_p, [_p]),

@@ -166,8 +166,15 @@ def run_ours(args, rank, world, local_rank):
 
     def step(i):
         j = i % pool
+        # each launch L2-prefetches the weights of the one after it (a hint;
+        # every launch still reads all of its own weights)
+        if not args.no_prefetch:
+            native.check(L.aljabr_blackwell_prefetch_hint(dn_d[j].data_ptr(), dn_d[j].nbytes))
         native.check(L.aljabr_blackwell_matvec_dev(native.TYPE_Q4_0, ys_up[j].data_ptr(), xs_up[j].data_ptr(),
                                                    up_d[j].data_ptr(), None, UP_K, UP_N, 0, None, sh))
+        if not args.no_prefetch:
+            nxt = up_d[(j + 1) % pool]
+            native.check(L.aljabr_blackwell_prefetch_hint(nxt.data_ptr(), nxt.nbytes))
         native.check(L.aljabr_blackwell_matvec_dev(native.TYPE_Q4_0, ys_dn[j].data_ptr(), xs_dn[j].data_ptr(),
                                                    dn_d[j].data_ptr(), None, DOWN_K, DOWN_N, 0, None, sh))
 
@@ -280,7 +287,8 @@ def run_ours(args, rank, world, local_rank):
                    "x": "N(0,1) fp32", "pool_matrices": 2 * pool, "pool_bytes": pool * pair_bytes,
                    "l2_bytes": l2, "l2_policy": "inputs larger than L2: weights rotate through a pool > 2x L2",
                    "parallelism": f"independent replicas x{world} (rows of each matrix on one GPU)",
-                   "launch": "CUDA graphs of 500 steps" + ("" if args.no_pdl else ", programmatic dependent launch")},
+                   "launch": "CUDA graphs of 500 steps" + ("" if args.no_pdl else ", programmatic dependent launch")
+                             + ("" if args.no_prefetch else ", each launch L2-prefetches the next launch's first weights")},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                      "traffic": load_traffic("q4_0_matvec"),
@@ -600,6 +608,7 @@ def main():
     ap.add_argument("--no-extra", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--no-prefetch", action="store_true", help="no L2 prefetch hints between the headline launches")
     ap.add_argument("--only", choices=["nf4", "q8", "attention", "decode"],
                     help="run one secondary workload alone (for profiling); prints its dict")
     ap.add_argument("--decode-tokens", type=int, default=32)

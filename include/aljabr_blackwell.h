@@ -93,6 +93,14 @@ int aljabr_blackwell_shutdown(void);
  * (true for weights loaded once, as in a decode loop). */
 int aljabr_blackwell_set_pdl(int enable);
 
+/* Scheduling hint, no counterpart in the reference: the next matvec launched
+ * from this thread (any entry point) prefetches, once its own weight copies
+ * are issued, the weights the launch after it will read -- [next_weights,
+ * next_weights + bytes), device or registered memory -- into L2, each CTA its
+ * share, so that launch starts on L2 hits while this one drains.  One-shot:
+ * the hint is consumed by that launch.  Pass NULL to clear. */
+int aljabr_blackwell_prefetch_hint(const void* next_weights, size_t bytes);
+
 /* ---- model buffers (aljabr_metal_buffers.h:15) ---------------------------- */
 /* Copy [base, base+bytes) to HBM once; later calls may pass host pointers
  * inside this range as weight pointers.  Re-registering the same base is a

@@ -55,20 +55,29 @@ def _cfg(shape):
                            shape.vocab, shape.max_ctx, shape.group, shape.eps, shape.rope_theta)
 
 
+# "small" runs the plain-kernel fallbacks (K below 2048); "wide" has every K a
+# multiple of 2048, so the projections run the TMA table kernel with its fused
+# epilogues (q/k/v segments, residual + RMSNorm, SwiGLU pair, lm_head).
+SHAPES = {
+    "small": dict(layers=2, hidden=256, q_heads=4, kv_heads=2, head_dim=64, ffn=512, vocab=1024, max_ctx=32),
+    "wide": dict(layers=2, hidden=2048, q_heads=16, kv_heads=4, head_dim=128, ffn=4096, vocab=2048, max_ctx=16),
+}
+
+
 @pytest.mark.parametrize("kv_dtype", [0, 1])
-def test_decode_step_matches_oracle(kv_dtype):
+@pytest.mark.parametrize("which", ["small", "wide"])
+def test_decode_step_matches_oracle(kv_dtype, which):
     from aljabr_b200 import native
     from aljabr_b200.decode import LlamaShape
     native.call("aljabr_blackwell_init", 0)
-    shape = LlamaShape(layers=2, hidden=256, q_heads=4, kv_heads=2, head_dim=64, ffn=512, vocab=1024, max_ctx=32,
-                       kv_dtype=kv_dtype)
+    shape = LlamaShape(**SHAPES[which], kv_dtype=kv_dtype)
     codes, absmax, norms = _model(123, shape)
     dec = _build(shape, codes, absmax, norms)
     cdt = np.uint16 if kv_dtype else np.float32
     kc = np.zeros((shape.layers, shape.max_ctx, shape.kv_heads * shape.head_dim), cdt)
     vc = np.zeros_like(kc)
     cfg = _cfg(shape)
-    tokens = [7, 300, 5, 1023, 64, 64, 0, 811, 2, 999]
+    tokens = [7, 300, 5, 1023, 64, 64, 0, 811, 2, 999] if which == "small" else [7, 1300, 5, 2047, 64]
     try:
         for pos, tok in enumerate(tokens):
             nxt, logits = dec.step(tok, pos, want_logits=True)

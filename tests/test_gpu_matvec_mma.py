@@ -78,3 +78,23 @@ def test_segments_split_slabs(lib):
     d.dispatch_mat_vec_triple(t["s0"], outs[0], t["s1"], outs[1], t["s2"], outs[2], x)
     for w, n, y in zip(ws, rows, outs):
         assert synth.max_rel_err(y, oracle.matvec_q4_0(w, x, n, threads=8)) < TOL
+
+
+def test_prefetch_hint_changes_nothing_but_timing(lib):
+    """The one-shot L2 prefetch hint is consumed by the next launch and does not
+    change its result; a host pointer that is neither registered nor device
+    memory is refused."""
+    import torch
+    from aljabr_b200.native import ProviderError
+    N, K = 4096, 4096
+    w = synth.q4_0(70, N, K)
+    x = synth.activation(71, K)
+    plain = _dev_matvec(lib, w, x, K, N)
+    nxt = torch.from_numpy(synth.q4_0(72, 14336, K)).cuda()
+    lib.call("aljabr_blackwell_prefetch_hint", nxt.data_ptr(), nxt.numel())
+    hinted = _dev_matvec(lib, w, x, K, N)
+    np.testing.assert_array_equal(hinted, plain)
+    host = np.zeros(1024, np.uint8)
+    with pytest.raises(ProviderError):
+        lib.call("aljabr_blackwell_prefetch_hint", host.ctypes.data, host.nbytes)
+    lib.call("aljabr_blackwell_prefetch_hint", None, 0)
