@@ -1,5 +1,5 @@
-// Batch-1 GGUF Q4_0 dequantise-and-matvec (y = W x) on the tensor cores of
-// B200 (sm_100a), for K a multiple of 2048.
+// Batch-1 GGUF Q4_0 and Q8_0 dequantise-and-matvec (y = W x) on the tensor
+// cores of B200 (sm_100a), for K a multiple of 2048.
 //
 // Why tensor cores for a matvec: the kernel is HBM-bound only if the SM can
 // decode 40 Q4_0 weights per cycle (6.5 TB/s / 148 SMs / 0.5625 B per
@@ -22,19 +22,22 @@
 //     with b = 8 (w / 2) + (w % 2) (same parity, so the 2-byte misalignment
 //     of even blocks is warp-uniform); lane (g, t) decodes block t of rows g
 //     and g + 8 straight into the A fragments of 8 MMAs;
-//   * codes enter the MMA as fp16 subnormals: (w & 0x000F000F) is the pair
-//     (c0, c2) * 2^-24 and (w & 0x00F000F0) is (16 c1', 16 c3') * 2^-24 --
-//     exact, no offset, no conversion instruction;
+//   * codes enter the MMA as fp16 subnormals: for Q4_0, (w & 0x000F000F) is
+//     the pair (c0, c2) * 2^-24 and (w & 0x00F000F0) is (16 c1', 16 c3') *
+//     2^-24; for Q8_0, PRMT(w ^ 0x80808080, 0, 0x4140) is (b0 + 128, b1 +
+//     128) * 2^-24 -- exact, one instruction per two codes;
 //   * x is staged once per CTA into shared memory as the B fragments, per
 //     32-element block: x' = x 2^-E (E from the block's max |x|, so
-//     |x'| < 2^11), hi = rint(x') and lo = (x' - hi) on a 2^-11 grid, both
+//     |x'| < 2^11 for Q4_0, 2^10 for Q8_0), hi = rint(x') and lo = (x' - hi)
+//     on a 2^-11 grid, both
 //     exact in fp16.  B column 2t carries block t's hi, 2t + 1 its lo, so one
 //     MMA keeps the four blocks of a span apart and D(row, 2t) + D(row, 2t+1)
 //     is block t's dot product; every partial sum is an exact multiple of a
 //     power of two below 2^24, so the tensor core's accumulation rounds
 //     nothing and the result carries fp32 accuracy;
-//   * the -8 code offset enters as the accumulator's initial value
-//     -8 sum(hi) 2^-24 (hi column) and -8 sum(lo) 2^-24 (lo column);
+//   * the code offset (-8 for Q4_0, -128 for the biased Q8_0 bytes) enters as
+//     the accumulator's initial value -off sum(hi) 2^-24 (hi column) and
+//     -off sum(lo) 2^-24 (lo column);
 //   * the block scale d (fp16, decoded from the fetched words) and 2^(E+24)
 //     are applied once per block in fp32;
 //   * per-warp row partials go through a shared-memory ring to the epilogue
@@ -63,11 +66,55 @@ constexpr int kEpilogueWarp = kCW + 1;
 constexpr int kThreads = (kCW + 2) * 32;
 constexpr int kUnit = 4;                       // rows per balancing unit
 constexpr int kChunkElems = 2048;              // 16 spans of 128 columns
-constexpr int kChunkBytes = 1152;              // Q4_0 bytes per row per chunk
-constexpr int kGroups = kChunkBytes / 128;     // 128-byte column groups per chunk
-constexpr int kBoxBytes = 8 * kChunkBytes;     // one 8-row half slab
-constexpr int kStageBytes = 2 * kBoxBytes;
 constexpr int kMaxStages = 8;
+
+// Per-format geometry.  Both formats store 32-element blocks (fp16 d first),
+// so a chunk of 2048 columns is 64 blocks and an odd number of 128-byte
+// column groups per row (9 for Q4_0, 17 for Q8_0): row r's groups then get
+// pairwise different swizzle keys (9 r + g or 17 r + g mod 8).
+template <int FMT>
+struct MmaFmt;
+template <>
+struct MmaFmt<FMT_Q4_0> {
+    static constexpr int kBlockBytes = 18;
+    static constexpr int kWords = 5;           // 32-bit words a lane fetches per block row
+    static constexpr float kOffset = 8.0f;     // code c stands for c - 8
+    static constexpr int kXBits = 11;          // |x'| < 2^11: 32 products c * hi (c < 16) stay below 2^20
+};
+template <>
+struct MmaFmt<FMT_Q8_0> {
+    static constexpr int kBlockBytes = 34;
+    static constexpr int kWords = 9;
+    static constexpr float kOffset = 128.0f;   // int8 b enters as the unsigned b + 128
+    static constexpr int kXBits = 10;          // |x'| < 2^10: 32 products (b + 128) * hi stay below 2^23
+};
+template <int FMT>
+struct MmaGeom {
+    static constexpr int kChunkBytes = 64 * MmaFmt<FMT>::kBlockBytes;   // 1152 | 2176
+    static constexpr int kGroups = kChunkBytes / 128;                   // 9 | 17
+    static constexpr int kBoxBytes = 8 * kChunkBytes;                   // one 8-row half slab
+    static constexpr int kStageBytes = 2 * kBoxBytes;
+};
+
+// Block element (0..31) that B slot `pos` (0..3) of k-step j carries.  The
+// A side: code word i of a block is (b0 b1 b2 b3) = bytes at code index
+// byte_idx(par, i, .); even blocks start 2 bytes into a word (the word holds
+// d), odd blocks start on a word.
+//   Q4_0: word i feeds k-steps 2i (low nibbles) and 2i + 1 (high nibbles,
+//         elements + 16); slots (0, 1) = bytes (b0, b2), (2, 3) = (b1, b3).
+//   Q8_0: word j feeds k-step j; slots (0, 1) = (b0, b1), (2, 3) = (b2, b3).
+__host__ __device__ constexpr int q4_byte_idx(int par, int i, int q) {
+    return par ? (i == 0 ? 12 + q : 4 * (i - 1) + q) : (i == 0 ? (q < 2 ? q : 12 + q) : 2 + 4 * (i - 1) + q);
+}
+__host__ __device__ constexpr int q8_byte_idx(int par, int i, int q) {
+    return par ? (i == 0 ? 28 + q : 4 * (i - 1) + q) : (i == 0 ? (q < 2 ? q : 28 + q) : 4 * i - 2 + q);
+}
+template <int FMT>
+__host__ __device__ constexpr int slot_elem(int par, int j, int pos) {
+    return FMT == FMT_Q4_0
+               ? q4_byte_idx(par, j >> 1, pos == 0 ? 0 : pos == 1 ? 2 : pos == 2 ? 1 : 3) + 16 * (j & 1)
+               : q8_byte_idx(par, j, pos);
+}
 constexpr int kRecBytes = 128;                 // B fragments of a (span, k-step pair): 8 lane slots of 16 B
 constexpr int kSpanBytes = 4 * kRecBytes;
 constexpr int kBlockInfoBytes = 16;            // per 32-element block: -off_hi, -off_lo, 2^(E+24), 0
@@ -186,7 +233,14 @@ struct SlabWalk {
     }
 };
 
-__global__ void __launch_bounds__(kThreads, 1) q4_0_mma_kernel(const __grid_constant__ MmaParams p, int stages) {
+template <int FMT>
+__global__ void __launch_bounds__(kThreads, 1) quant_mma_kernel(const __grid_constant__ MmaParams p, int stages) {
+    using G = MmaGeom<FMT>;
+    using F = MmaFmt<FMT>;
+    constexpr int kChunkBytes = G::kChunkBytes;
+    constexpr int kGroups = G::kGroups;
+    constexpr int kBoxBytes = G::kBoxBytes;
+    constexpr int kStageBytes = G::kStageBytes;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     pdl_launch_dependents();
     const int K = p.K;
@@ -342,16 +396,10 @@ __global__ void __launch_bounds__(kThreads, 1) q4_0_mma_kernel(const __grid_cons
         // Lane (t, j) = (lane / 8, lane % 8) converts the 4 elements of block
         // blk + 2t that B slots 0..3 of k-step j carry.
         const int st_t = lane >> 3, st_j = lane & 7;
-        const int hs = st_j & 1;
+        const int hs = FMT == FMT_Q4_0 ? (st_j & 1) : 0;   // Q4_0 high nibbles enter the MMA as 16 c
         int e[4];
 #pragma unroll
-        for (int pos = 0; pos < 4; ++pos) {
-            const int q = pos == 0 ? 0 : pos == 1 ? 2 : pos == 2 ? 1 : 3;   // slot -> byte of the code word
-            const int i = st_j >> 1;                                         // code word
-            const int byte = par ? (i == 0 ? 12 + q : 4 * (i - 1) + q)
-                                 : (i == 0 ? (q < 2 ? q : 12 + q) : 2 + 4 * (i - 1) + q);
-            e[pos] = byte + 16 * hs;
-        }
+        for (int pos = 0; pos < 4; ++pos) e[pos] = slot_elem<FMT>(par, st_j, pos);
 #pragma unroll 2
         for (int c = 0; c < nchunks; ++c) {
             const int bg = c * 64 + blk + 2 * st_t;
@@ -364,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1) q4_0_mma_kernel(const __grid_cons
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
             int E = 0;
-            if (mx > 0.0f && mx < INFINITY) E = min(90, max(-90, ilogbf(mx) - 10));
+            if (mx > 0.0f && mx < INFINITY) E = min(90, max(-90, ilogbf(mx) - (F::kXBits - 1)));
             const float xs = __int_as_float((127 - E) << 23);
             float hv[4], lv[4], shi = 0.0f, slo = 0.0f;
 #pragma unroll
@@ -381,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1) q4_0_mma_kernel(const __grid_cons
             slo += __shfl_xor_sync(0xffffffffu, slo, 1);
             slo += __shfl_xor_sync(0xffffffffu, slo, 2);
             slo += __shfl_xor_sync(0xffffffffu, slo, 4);
-            const float hsc = hs ? 0.0625f : 1.0f;   // high nibbles enter the MMA as 16 c
+            const float hsc = hs ? 0.0625f : 1.0f;
             uint32_t hw[2], lw[2];
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
@@ -390,11 +438,12 @@ __global__ void __launch_bounds__(kThreads, 1) q4_0_mma_kernel(const __grid_cons
                 hw[u] = *reinterpret_cast<const uint32_t*>(&h);
                 lw[u] = *reinterpret_cast<const uint32_t*>(&l);
             }
+            // k-steps 2i and 2i + 1 share a 16-byte lane slot: k-step j at 8 (j & 1)
             uint8_t* rec = xfrag + static_cast<size_t>(c * 16 + warp) * kSpanBytes + (st_j >> 1) * kRecBytes;
-            *reinterpret_cast<uint2*>(rec + 32 * st_t + 8 * hs) = make_uint2(hw[0], hw[1]);
-            *reinterpret_cast<uint2*>(rec + 32 * st_t + 16 + 8 * hs) = make_uint2(lw[0], lw[1]);
+            *reinterpret_cast<uint2*>(rec + 32 * st_t + 8 * (st_j & 1)) = make_uint2(hw[0], hw[1]);
+            *reinterpret_cast<uint2*>(rec + 32 * st_t + 16 + 8 * (st_j & 1)) = make_uint2(lw[0], lw[1]);
             if (st_j == 0)
-                binfo[bg] = make_float4(-8.0f * shi * kTwoM24, -8.0f * slo * kTwoM24,
+                binfo[bg] = make_float4(-F::kOffset * shi * kTwoM24, -F::kOffset * slo * kTwoM24,
                                         __int_as_float((127 + E + 24) << 23), 0.0f);
         }
         __syncwarp();
@@ -404,13 +453,14 @@ __global__ void __launch_bounds__(kThreads, 1) q4_0_mma_kernel(const __grid_cons
     const uint32_t bact = (g >> 1) == t ? 1u : 0u;       // lanes whose B column belongs to their quad
     const uint32_t boff = 16u * (2 * t + (g & 1));
     const uint32_t sel_d = par ? 0x4432u : 0x4410u;      // fp16 d: low half (even block) or high half (odd)
-    const uint32_t sel_c0 = par ? 0x7654u : 0x5432u;     // first code word: W4 (odd) or W0.hi:W4.lo (even)
+    const uint32_t sel_c0 = par ? 0x7654u : 0x5432u;     // first code word: W[last] (odd) or W0.hi:W[last].lo
     const int myblk = blk + 2 * t;
-    uint32_t aoff[5];                                    // swizzled offsets of this lane's 5 words in row g
+    constexpr int kW = F::kWords;
+    uint32_t aoff[kW];                                   // swizzled offsets of this lane's words in row g
     {
-        const uint32_t boffs = (18u * myblk) & ~3u;
+        const uint32_t boffs = (static_cast<uint32_t>(F::kBlockBytes) * myblk) & ~3u;
 #pragma unroll
-        for (int k = 0; k < 5; ++k) {
+        for (int k = 0; k < kW; ++k) {
             const uint32_t o = boffs + 4 * k;
             const uint32_t segidx = g * kGroups + (o >> 7);
             aoff[k] = segidx * 128 + ((((o >> 4) & 7) ^ (segidx & 7)) << 4) + (o & 15);
@@ -429,9 +479,9 @@ __global__ void __launch_bounds__(kThreads, 1) q4_0_mma_kernel(const __grid_cons
             // warp-uniform: the MMAs below need all 32 lanes
             if (__all_sync(0xffffffffu, mbar_wait(&full[s], ph))) {
                 const uint32_t st = stage_s + s * kStageBytes;
-                uint32_t W0[5], W1[5];
+                uint32_t W0[kW], W1[kW];
 #pragma unroll
-                for (int k = 0; k < 5; ++k) {
+                for (int k = 0; k < kW; ++k) {
                     W0[k] = lds32(st + aoff[k]);
                     W1[k] = lds32(st + kBoxBytes + aoff[k]);
                 }
@@ -443,23 +493,36 @@ __global__ void __launch_bounds__(kThreads, 1) q4_0_mma_kernel(const __grid_cons
                 const float scale = __uint_as_float(bi.z);
                 const float d0 = __half2float(__ushort_as_half(static_cast<unsigned short>(__byte_perm(W0[0], 0u, sel_d)))) * scale;
                 const float d1 = __half2float(__ushort_as_half(static_cast<unsigned short>(__byte_perm(W1[0], 0u, sel_d)))) * scale;
-                uint32_t cw0[4], cw1[4];
-                cw0[0] = __byte_perm(W0[0], W0[4], sel_c0);
-                cw1[0] = __byte_perm(W1[0], W1[4], sel_c0);
-#pragma unroll
-                for (int i = 1; i < 4; ++i) {
-                    cw0[i] = W0[i];
-                    cw1[i] = W1[i];
-                }
                 float d[4] = {__uint_as_float(bi.x), __uint_as_float(bi.y), __uint_as_float(bi.x), __uint_as_float(bi.y)};
+                if constexpr (FMT == FMT_Q4_0) {
+                    uint32_t cw0[4], cw1[4];
+                    cw0[0] = __byte_perm(W0[0], W0[4], sel_c0);
+                    cw1[0] = __byte_perm(W1[0], W1[4], sel_c0);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const uint32_t s0 = cw0[i] >> 8, s1 = cw1[i] >> 8;
-                    // k-step 2i: low nibbles of bytes (0,2) | (1,3); k-step 2i+1: high nibbles
-                    mma16816(d, land(cw0[i], 0x000F000Fu), land(cw1[i], 0x000F000Fu), land(s0, 0x000F000Fu),
-                             land(s1, 0x000F000Fu), B[i].x, B[i].y);
-                    mma16816(d, land(cw0[i], 0x00F000F0u), land(cw1[i], 0x00F000F0u), land(s0, 0x00F000F0u),
-                             land(s1, 0x00F000F0u), B[i].z, B[i].w);
+                    for (int i = 1; i < 4; ++i) {
+                        cw0[i] = W0[i];
+                        cw1[i] = W1[i];
+                    }
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const uint32_t s0 = cw0[i] >> 8, s1 = cw1[i] >> 8;
+                        // k-step 2i: low nibbles of bytes (0,2) | (1,3); k-step 2i+1: high nibbles
+                        mma16816(d, land(cw0[i], 0x000F000Fu), land(cw1[i], 0x000F000Fu), land(s0, 0x000F000Fu),
+                                 land(s1, 0x000F000Fu), B[i].x, B[i].y);
+                        mma16816(d, land(cw0[i], 0x00F000F0u), land(cw1[i], 0x00F000F0u), land(s0, 0x00F000F0u),
+                                 land(s1, 0x00F000F0u), B[i].z, B[i].w);
+                    }
+                } else {
+                    // int8 b -> (b ^ 0x80) = b + 128 as an fp16 subnormal, two per PRMT
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t c0 = (j == 0 ? __byte_perm(W0[0], W0[8], sel_c0) : W0[j]) ^ 0x80808080u;
+                        const uint32_t c1 = (j == 0 ? __byte_perm(W1[0], W1[8], sel_c0) : W1[j]) ^ 0x80808080u;
+                        const uint4& Bq = B[j >> 1];
+                        mma16816(d, __byte_perm(c0, 0u, 0x4140u), __byte_perm(c1, 0u, 0x4140u),
+                                 __byte_perm(c0, 0u, 0x4342u), __byte_perm(c1, 0u, 0x4342u),
+                                 (j & 1) ? Bq.z : Bq.x, (j & 1) ? Bq.w : Bq.y);
+                    }
                 }
                 y0 = fmaf(d0, d[0] + d[1], y0);
                 y1 = fmaf(d1, d[2] + d[3], y1);
@@ -491,15 +554,16 @@ __global__ void __launch_bounds__(kThreads, 1) q4_0_mma_kernel(const __grid_cons
     }
 }
 
-bool encode_q4_0_maps(MmaSegment& ms, const void* w, int K, int rows) {
+template <int FMT>
+bool encode_maps(MmaSegment& ms, const void* w, int K, int rows) {
     auto fn = tensor_map_encoder();
     if (!fn) return false;
-    const size_t row_bytes = static_cast<size_t>(K) / 32 * 18;
+    const size_t row_bytes = static_cast<size_t>(K) / 32 * MmaFmt<FMT>::kBlockBytes;
     const cuuint64_t dims[3] = {16, row_bytes / 128, static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[2] = {128, row_bytes};
     const cuuint32_t es[3] = {1, 1, 1};
     for (int v = 0; v < 2; ++v) {
-        const cuuint32_t box[3] = {16, static_cast<cuuint32_t>(kGroups), v == 0 ? 8u : 4u};
+        const cuuint32_t box[3] = {16, static_cast<cuuint32_t>(MmaGeom<FMT>::kGroups), v == 0 ? 8u : 4u};
         if (fn(v == 0 ? &ms.map8 : &ms.map4, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(w), dims, strides,
                box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
@@ -507,6 +571,8 @@ bool encode_q4_0_maps(MmaSegment& ms, const void* w, int K, int rows) {
     }
     return true;
 }
+
+int stage_bytes_of(int fmt) { return fmt == FMT_Q4_0 ? MmaGeom<FMT_Q4_0>::kStageBytes : MmaGeom<FMT_Q8_0>::kStageBytes; }
 
 size_t fixed_smem(int K) {
     const size_t nspans = static_cast<size_t>(K / kChunkElems) * 16;
@@ -517,8 +583,8 @@ size_t fixed_smem(int K) {
 }  // namespace
 
 bool matvec_mma_supported(int fmt, int K) {
-    if (fmt != FMT_Q4_0 || K <= 0 || K % kChunkElems != 0) return false;
-    if (static_cast<long long>(fixed_smem(K)) + 2LL * kStageBytes > kSmemMax) return false;
+    if ((fmt != FMT_Q4_0 && fmt != FMT_Q8_0) || K <= 0 || K % kChunkElems != 0) return false;
+    if (static_cast<long long>(fixed_smem(K)) + 2LL * stage_bytes_of(fmt) > kSmemMax) return false;
     return tensor_map_encoder() != nullptr;
 }
 
@@ -548,7 +614,9 @@ cudaError_t launch_matvec_mma(int fmt, const MatvecParams& mp, cudaStream_t stre
     int row0 = 0;
     for (int s = 0; s < mp.nseg; ++s) {
         MmaSegment& ms = p.seg[s];
-        if (!encode_q4_0_maps(ms, mp.seg[s].w, mp.K, mp.seg[s].rows)) return cudaErrorInvalidValue;
+        const bool ok = fmt == FMT_Q4_0 ? encode_maps<FMT_Q4_0>(ms, mp.seg[s].w, mp.K, mp.seg[s].rows)
+                                        : encode_maps<FMT_Q8_0>(ms, mp.seg[s].w, mp.K, mp.seg[s].rows);
+        if (!ok) return cudaErrorInvalidValue;
         ms.bias = mp.seg[s].bias;
         ms.residual = mp.seg[s].residual;
         ms.y = mp.seg[s].y;
@@ -557,15 +625,18 @@ cudaError_t launch_matvec_mma(int fmt, const MatvecParams& mp, cudaStream_t stre
         row0 += mp.seg[s].rows;
     }
     const size_t fixed = fixed_smem(mp.K);
-    const int stages = static_cast<int>(std::min<size_t>(kMaxStages, (kSmemMax - fixed) / kStageBytes));
-    const size_t smem = fixed + static_cast<size_t>(stages) * kStageBytes;
-    static bool configured[64] = {};
+    const int sb = stage_bytes_of(fmt);
+    const int stages = static_cast<int>(std::min<size_t>(kMaxStages, (kSmemMax - fixed) / sb));
+    const size_t smem = fixed + static_cast<size_t>(stages) * sb;
+    auto kern = fmt == FMT_Q4_0 ? quant_mma_kernel<FMT_Q4_0> : quant_mma_kernel<FMT_Q8_0>;
+    static bool configured[2][64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (!configured[dev & 63]) {
-        cudaError_t e = cudaFuncSetAttribute(q4_0_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+    bool& done = configured[fmt == FMT_Q4_0 ? 0 : 1][dev & 63];
+    if (!done) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
         if (e != cudaSuccess) return e;
-        configured[dev & 63] = true;
+        done = true;
     }
     const int units = mp.total_rows / kUnit;
     const int grid = std::max(1, std::min(sm_count_for_current_device(), units));
@@ -579,7 +650,7 @@ cudaError_t launch_matvec_mma(int fmt, const MatvecParams& mp, cudaStream_t stre
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, q4_0_mma_kernel, p, stages);
+    return cudaLaunchKernelEx(&cfg, kern, p, stages);
 }
 
 }  // namespace alj

@@ -98,3 +98,35 @@ def test_prefetch_hint_changes_nothing_but_timing(lib):
     with pytest.raises(ProviderError):
         lib.call("aljabr_blackwell_prefetch_hint", host.ctypes.data, host.nbytes)
     lib.call("aljabr_blackwell_prefetch_hint", None, 0)
+
+
+def _dev_matvec_q8(lib, w, x, K, N):
+    import torch
+    dw = torch.from_numpy(w).cuda()
+    dx = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+    dy = torch.full((N,), float("nan"), dtype=torch.float32, device="cuda")
+    lib.call("aljabr_blackwell_matvec_dev", lib.TYPE_Q8_0, dy.data_ptr(), dx.data_ptr(), dw.data_ptr(), None,
+             K, N, 0, None, None)
+    torch.cuda.synchronize()
+    return dy.cpu().numpy()
+
+
+@pytest.mark.parametrize("N", [4, 12, 36, 596, 2380])
+@pytest.mark.parametrize("K", [2048, 6144])
+def test_q8_0_ragged_rows(lib, N, K):
+    w = synth.q8_0(500 + N, N, K)
+    x = synth.activation(600 + K, K)
+    y = _dev_matvec_q8(lib, w, x, K, N)
+    assert synth.max_rel_err(y, oracle.matvec_q8_0(w, x, N, threads=8)) < TOL
+    assert synth.max_rel_err(y, oracle.matvec_f64(oracle.Q8_0, w, x, N, threads=8)) < TOL
+
+
+@pytest.mark.parametrize("scale", [1.0, 3e4, 1e-6])
+def test_q8_0_activation_outliers_and_scales(lib, scale):
+    N, K = 1024, 8192
+    w = synth.q8_0(17, N, K)
+    x = synth.activation(18, K) * np.float32(scale)
+    x[5::97] *= 50.0
+    x[:32] = 0.0
+    y = _dev_matvec_q8(lib, w, x, K, N)
+    assert synth.max_rel_err(y, oracle.matvec_q8_0(w, x, N, threads=8)) < TOL
