@@ -11,14 +11,14 @@ import oracle
 pytestmark = pytest.mark.gpu
 
 
-def _rank_main(rank, world, nccl_id, q):
+def _rank_main(rank, world, nccl_id, q, which):
     import torch
     torch.cuda.set_device(rank)
     from aljabr_b200 import native
     from aljabr_b200.decode import LlamaNf4Decoder, shard_rows
     from tests.test_gpu_decode import _model
     native.call("aljabr_blackwell_init", rank)
-    shape = _shape()
+    shape = _shape(which)
     codes, absmax, norms = _model(321, shape)
     dec = LlamaNf4Decoder(shape, tp_world=world, tp_rank=rank, nccl_id=nccl_id)
     H = shape.hidden
@@ -44,14 +44,20 @@ def _rank_main(rank, world, nccl_id, q):
         dec.close()
 
 
-def _shape():
+def _shape(which):
+    """"small" runs the plain-kernel fallbacks; "wide" has K a multiple of 2048
+    everywhere, so each rank's shards run the TMA table kernel."""
     from aljabr_b200.decode import LlamaShape
-    return LlamaShape(layers=2, hidden=256, q_heads=4, kv_heads=2, head_dim=64, ffn=512, vocab=1024, max_ctx=16,
+    if which == "small":
+        return LlamaShape(layers=2, hidden=256, q_heads=4, kv_heads=2, head_dim=64, ffn=512, vocab=1024, max_ctx=16,
+                          kv_dtype=0)
+    return LlamaShape(layers=2, hidden=2048, q_heads=16, kv_heads=4, head_dim=128, ffn=4096, vocab=2048, max_ctx=16,
                       kv_dtype=0)
 
 
 @pytest.mark.skipif(int(os.environ.get("ALJ_TEST_GPUS", "0")) < 2, reason="needs 2 GPUs (set ALJ_TEST_GPUS=2)")
-def test_tp2_decode_matches_oracle():
+@pytest.mark.parametrize("which", ["small", "wide"])
+def test_tp2_decode_matches_oracle(which):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -61,14 +67,14 @@ def test_tp2_decode_matches_oracle():
     nid = nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, nid, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, nid, q, which)) for r in range(2)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=300) for _ in range(2))
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    shape = _shape()
+    shape = _shape(which)
     codes, absmax, norms = _model(321, shape)
     kc = np.zeros((shape.layers, shape.max_ctx, shape.kv_heads * shape.head_dim), np.float32)
     vc = np.zeros_like(kc)
