@@ -22,6 +22,26 @@ enum Epilogue : int {
     EPI_SWIGLU_PAIR = 1,   // segments 0 (gate) and 1 (up) of equal rows: seg[0].y = silu(W_g x) * (W_u x)
 };
 
+// Tensor-parallel exchange of a kernel's output slice over NVLink (decode
+// step on 2..8 GPUs).  A kernel with tp > 1 stores each output row into every
+// rank's copy (push_y[r] + row), and the CTA that finishes last publishes,
+// after a system-scope fence, the rank's sum of squares of its rows into
+// push_part[r] (if set) and the flag value (*seq) * push_mul + push_add into
+// push_flag[r] on every rank.  A kernel whose input is such a gathered buffer
+// first waits (bounded) until its local wait_flags[0..tp) all reach
+// (*seq) * wait_mul + wait_add.
+constexpr int kMaxTp = 8;
+struct TpLink {
+    int tp;                              // <= 1: no exchange
+    float* push_y[kMaxTp];
+    float* push_part[kMaxTp];
+    unsigned int* push_flag[kMaxTp];
+    unsigned int* counter;               // local last-CTA counter: 0 before and after
+    const unsigned int* wait_flags;      // local [tp], or null
+    const int* seq;                      // device token counter
+    int push_mul, push_add, wait_mul, wait_add;
+};
+
 struct MatvecSegment {
     const uint8_t* w;        // Q4_0 / Q8_0 blocks, or NF4 packed codes (row-major [rows][K])
     const float* absmax;     // NF4 per-group fp32 scales, else null
@@ -52,6 +72,7 @@ struct MatvecParams {
     // its 1/grid share, after its own copies are issued).
     const void* prefetch;
     size_t prefetch_bytes;
+    TpLink tpl;              // tensor-parallel push / wait (NF4 table kernel only)
 };
 // CTAs a TMA matvec launches (the size norm_partials must have).
 int matvec_max_ctas();
@@ -86,6 +107,7 @@ struct AttnParams {
     float* part_ml;          // scratch [q_heads][splits][2]  (running max, running sum)
     int splits;
     const int* dev_pos;      // if set, seq_len = *dev_pos + 1 is read on the device (graph replay)
+    TpLink tpl;              // tensor-parallel push of `out` (combine kernel; needs splits >= 2)
 };
 int attention_splits(int seq_len, int kv_heads, int sm_count);
 size_t attention_scratch_floats(int q_heads, int head_dim, int splits);

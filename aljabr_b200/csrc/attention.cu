@@ -238,7 +238,29 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnParams p) {
             a3 = fmaf(po[(j + 3) * D + d], s_w[j + 3], a3);
         }
         for (; j < S; ++j) a0 = fmaf(po[j * D + d], s_w[j], a0);
-        p.out[qh * D + d] = ((a0 + a1) + (a2 + a3)) * inv;
+        const float o = ((a0 + a1) + (a2 + a3)) * inv;
+        if (p.tpl.tp > 1) {
+            for (int r = 0; r < p.tpl.tp; ++r) p.tpl.push_y[r][qh * D + d] = o;
+        } else {
+            p.out[qh * D + d] = o;
+        }
+    }
+    if (p.tpl.tp > 1) {
+        // the last CTA publishes this rank's heads on every rank
+        __threadfence_system();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const unsigned int prev = atomicAdd(p.tpl.counter, 1u);
+            s_red[0] = prev == gridDim.x - 1 ? 1.0f : 0.0f;
+        }
+        __syncthreads();
+        if (s_red[0] != 0.0f) {
+            __threadfence_system();
+            if (static_cast<int>(threadIdx.x) < p.tpl.tp)
+                st_release_sys(p.tpl.push_flag[threadIdx.x],
+                               static_cast<unsigned int>(*p.tpl.seq * p.tpl.push_mul + p.tpl.push_add));
+            if (threadIdx.x == 0) *p.tpl.counter = 0u;
+        }
     }
 }
 
@@ -372,6 +394,9 @@ size_t attention_scratch_floats(int q_heads, int head_dim, int splits) {
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl) {
     const int active = p.seq_len - p.start_pos;
     if (active <= 0) return cudaErrorInvalidValue;
+    // the tensor-parallel push lives in the combine kernel
+    if (p.tpl.tp > 1 && (p.splits < 2 || p.tpl.tp > kMaxTp || !p.tpl.counter || !p.tpl.seq || !fast_path(p)))
+        return cudaErrorInvalidValue;
     if (fast_path(p)) {
         dim3 grid(p.kv_heads, p.splits);
         cudaError_t e = p.kv_dtype == ALJ_KV_BF16 ? dispatch_e<ALJ_KV_BF16>(p, grid, stream, pdl)

@@ -74,6 +74,36 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
         : "memory");
 }
 
+// ---------------------------------------------------------------- cross-GPU flags
+// Release / acquire at system scope for the tensor-parallel exchange: a rank
+// writes its output rows into every peer's buffer (NVLink peer mappings),
+// fences, and publishes a monotonically increasing flag value on each peer.
+__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Bounded wait until flags[0..n) all reach `target` (wrap-safe).  Returns
+// false and records ALJ_FAULT_TIMEOUT if a peer never publishes.
+__device__ __forceinline__ bool wait_flags_sys(const unsigned int* flags, int n, unsigned int target) {
+    const long long t0 = clock64();
+    for (int r = 0; r < n; ++r) {
+        while (static_cast<int>(ld_acquire_sys(flags + r) - target) < 0) {
+            if (clock64() - t0 > kSpinLimitCycles) {
+                record_fault(ALJ_FAULT_TIMEOUT);
+                return false;
+            }
+        }
+    }
+    return true;
+}
+// Generic-proxy writes observed above become visible to this thread's later
+// TMA (async-proxy) reads.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
 // Programmatic dependent launch: wait for the producer grid's writes, and let
 // the next grid in the stream begin launching.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

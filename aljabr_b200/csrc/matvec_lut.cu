@@ -86,6 +86,7 @@ struct alignas(64) LutParams {
     unsigned int* norm_counter;
     const uint8_t* prefetch;
     size_t prefetch_bytes;
+    TpLink tpl;
 };
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
@@ -249,6 +250,12 @@ __global__ void __launch_bounds__(kThreads, 1) nf4_lut_kernel(const __grid_const
                     // x comes from the previous kernel: its first copy waits for it.
                     if (!x_waited) {
                         pdl_wait();
+                        // tensor parallel: x is gathered from every rank's push
+                        if (p.tpl.tp > 1 && p.tpl.wait_flags) {
+                            wait_flags_sys(p.tpl.wait_flags, p.tpl.tp,
+                                           static_cast<unsigned int>(*p.tpl.seq * p.tpl.wait_mul + p.tpl.wait_add));
+                            fence_proxy_async_global();
+                        }
                         x_waited = true;
                     }
                     tma_load_2d(st + L.x_off, &p.xmap, 0, c * (kChunkElems / 32), &full[s]);
@@ -281,7 +288,11 @@ __global__ void __launch_bounds__(kThreads, 1) nf4_lut_kernel(const __grid_const
                     const float up = __shfl_down_sync(0xffffffffu, acc, 16);
                     if (lane < nunits * kUnit) {
                         const float out = acc / (1.0f + expf(-acc)) * up;
-                        p.seg[0].y[su * kUnit + lane] = out;
+                        if (p.tpl.tp > 1) {
+                            for (int r = 0; r < p.tpl.tp; ++r) p.tpl.push_y[r][su * kUnit + lane] = out;
+                        } else {
+                            p.seg[0].y[su * kUnit + lane] = out;
+                        }
                         sq = fmaf(out, out, sq);
                     }
                 } else if (lane < nunits * kUnit) {
@@ -290,13 +301,44 @@ __global__ void __launch_bounds__(kThreads, 1) nf4_lut_kernel(const __grid_const
                     float out = acc;
                     if (sg.bias) out += sg.bias[lrow];
                     if (sg.residual) out = sg.residual[lrow] + out;
-                    sg.y[lrow] = out;
+                    if (p.tpl.tp > 1) {
+                        for (int r = 0; r < p.tpl.tp; ++r) p.tpl.push_y[r][lrow] = out;
+                    } else {
+                        sg.y[lrow] = out;
+                    }
                     sq = fmaf(out, out, sq);
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&rempty[b]);
             ++sl;
+        }
+        if (p.tpl.tp > 1) {
+            // Publish this rank's slice: the last CTA to finish writes the
+            // rank's sum of squares (fixed order over the CTAs) and the flag
+            // value on every rank, after a system-scope fence that covers
+            // every CTA's peer stores.
+            __threadfence_system();
+            const float cta = warp_sum(sq);
+            if (lane == 0) {
+                p.norm_partials[blockIdx.x] = cta;
+                __threadfence_system();
+                const unsigned int prev = atomicAdd(p.tpl.counter, 1u);
+                misc[1] = prev == gridDim.x - 1 ? 1.0f : 0.0f;
+            }
+            __syncwarp();
+            if (misc[1] != 0.0f) {
+                __threadfence_system();
+                float part = 0.0f;
+                for (unsigned int b = lane; b < gridDim.x; b += 32) part += __ldcg(p.norm_partials + b);
+                const float tot = warp_sum(part);
+                if (lane < p.tpl.tp && p.tpl.push_part[lane]) *p.tpl.push_part[lane] = tot;
+                __threadfence_system();
+                if (lane < p.tpl.tp)
+                    st_release_sys(p.tpl.push_flag[lane],
+                                   static_cast<unsigned int>(*p.tpl.seq * p.tpl.push_mul + p.tpl.push_add));
+                if (lane == 0) *p.tpl.counter = 0u;
+            }
         }
         if (p.norm_out) {
             // Deterministic RMSNorm of the whole output: per-CTA partials in
@@ -484,6 +526,10 @@ cudaError_t launch_matvec_lut(int fmt, const MatvecParams& mp, cudaStream_t stre
     p.norm_counter = mp.norm_counter;
     p.prefetch = static_cast<const uint8_t*>(mp.prefetch);
     p.prefetch_bytes = mp.prefetch_bytes;
+    p.tpl = mp.tpl;
+    if (p.tpl.tp > 1 && (p.tpl.tp > kMaxTp || !p.tpl.counter || !p.tpl.seq || !p.norm_partials || mp.nseg > 2 ||
+                         (mp.nseg == 2 && !pair) || p.norm_out))
+        return cudaErrorInvalidValue;
     const cuuint32_t abs_elems = static_cast<cuuint32_t>(kChunkElems / mp.group);
     int row0 = 0;
     for (int s = 0; s < mp.nseg; ++s) {

@@ -11,7 +11,8 @@ import oracle
 pytestmark = pytest.mark.gpu
 
 
-def _rank_main(rank, world, nccl_id, q, which):
+def _rank_main(rank, world, nccl_id, q, which, exchange):
+    os.environ["ALJ_TP_EXCHANGE"] = exchange
     import torch
     torch.cuda.set_device(rank)
     from aljabr_b200 import native
@@ -56,8 +57,11 @@ def _shape(which):
 
 
 @pytest.mark.skipif(int(os.environ.get("ALJ_TEST_GPUS", "0")) < 2, reason="needs 2 GPUs (set ALJ_TEST_GPUS=2)")
-@pytest.mark.parametrize("which", ["small", "wide"])
-def test_tp2_decode_matches_oracle(which):
+@pytest.mark.parametrize("which,exchange", [("small", "nccl"), ("wide", "nccl"), ("wide", "p2p")])
+def test_tp2_decode_matches_oracle(which, exchange):
+    """exchange "p2p" joins the slices with NVLink peer stores from the
+    producing kernels (the wide shape runs the table kernel that carries the
+    push); "nccl" with ncclAllGather."""
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -67,7 +71,7 @@ def test_tp2_decode_matches_oracle(which):
     nid = nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, nid, q, which)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, nid, q, which, exchange)) for r in range(2)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=300) for _ in range(2))
