@@ -113,6 +113,27 @@ int attention_splits(int seq_len, int kv_heads, int sm_count);
 size_t attention_scratch_floats(int q_heads, int head_dim, int splits);
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl);
 
+// Batched NF4 GEMM on tcgen05 (gemm_nf4.cu): y_s[m * ldy_s + n] =
+// sum_k x[m][k] * W_s[n][k] for up to 3 weight matrices sharing x (bf16).
+struct GemmNf4Args {
+    int nseg;
+    float* y[3];
+    int ldy[3];
+    const void* packed[3];   // weights packed by launch_gemm_nf4_pack
+    int rows[3];
+    const void* x;           // bf16 [M][K]
+    int M, K, group;
+    void* workspace;
+    size_t workspace_bytes;
+};
+bool gemm_nf4_supported(int M, int K, int group);
+size_t gemm_nf4_packed_bytes(int rows, int K, int group);
+cudaError_t launch_gemm_nf4_pack(void* packed, const void* codes, const void* absmax, int rows, int K, int group,
+                                 cudaStream_t stream);
+int gemm_nf4_tiles(int M, int nseg, const int* rows);
+size_t gemm_nf4_workspace_bytes(int M, int K, int total_tiles, int grid);
+cudaError_t launch_gemm_nf4(const GemmNf4Args& a, cudaStream_t stream);
+
 int sm_count_for_current_device();
 
 }  // namespace alj

@@ -653,6 +653,72 @@ int aljabr_blackwell_matvec_dev(int type, float* y, const float* x, const void* 
     return run_matvecs(st, &m, 1, x, K, group, pick_stream(st, stream), t_pdl);
 }
 
+long long aljabr_blackwell_gemm_nf4_workspace_size(int M, int K, int nseg, const int* rows) {
+    if (M < 1 || K < 1 || nseg < 1 || nseg > 3 || !rows) return fail(ALJ_ERR_BAD_ARG, "bad gemm_nf4 shape");
+    for (int s = 0; s < nseg; ++s)
+        if (rows[s] < 1) return fail(ALJ_ERR_BAD_DIMS, "rows[%d]=%d", s, rows[s]);
+    const int sms = sm_count_for_current_device();
+    return static_cast<long long>(gemm_nf4_workspace_bytes(M, K, gemm_nf4_tiles(M, nseg, rows), sms > 0 ? sms : 1));
+}
+
+long long aljabr_blackwell_gemm_nf4_packed_size(int rows, int K, int blockSize) {
+    if (rows < 1 || !gemm_nf4_supported(1, K, blockSize))
+        return fail(ALJ_ERR_UNSUPPORTED, "gemm_nf4: rows=%d K=%d blockSize=%d (K %% 256, blockSize 64/128)", rows, K,
+                    blockSize);
+    return static_cast<long long>(gemm_nf4_packed_bytes(rows, K, blockSize));
+}
+
+int aljabr_blackwell_gemm_nf4_pack(void* packed, const void* codes, const void* absmax, int rows, int K, int blockSize,
+                                   void* stream) {
+    int err = 0;
+    DeviceState* st = state(&err);
+    if (!st) return err;
+    if (!packed || !codes || !absmax) return fail(ALJ_ERR_BAD_ARG, "gemm_nf4_pack: null pointer");
+    if (rows < 1 || !gemm_nf4_supported(1, K, blockSize))
+        return fail(ALJ_ERR_UNSUPPORTED, "gemm_nf4_pack: rows=%d K=%d blockSize=%d", rows, K, blockSize);
+    if ((reinterpret_cast<uintptr_t>(packed) & 255) || (reinterpret_cast<uintptr_t>(codes) & 15))
+        return fail(ALJ_ERR_BAD_ARG, "gemm_nf4_pack: packed must be 256-byte and codes 16-byte aligned");
+    return launch_status(launch_gemm_nf4_pack(packed, codes, absmax, rows, K, blockSize, pick_stream(st, stream)),
+                         "gemm_nf4_pack");
+}
+
+int aljabr_blackwell_gemm_nf4_dev(int nseg, float* const* y, const int* ldy, const void* const* packed,
+                                  const int* rows, const void* x_bf16, int M, int K, int blockSize, void* workspace,
+                                  long long workspace_bytes, void* stream) {
+    int err = 0;
+    DeviceState* st = state(&err);
+    if (!st) return err;
+    if (nseg < 1 || nseg > 3 || !y || !ldy || !packed || !rows || !x_bf16 || !workspace)
+        return fail(ALJ_ERR_BAD_ARG, "gemm_nf4: null argument or nseg=%d", nseg);
+    if (M < 1 || K < 1) return fail(ALJ_ERR_BAD_DIMS, "gemm_nf4: M=%d K=%d", M, K);
+    if (reinterpret_cast<uintptr_t>(x_bf16) & 15) return fail(ALJ_ERR_BAD_ARG, "gemm_nf4: x not 16-byte aligned");
+    if (!gemm_nf4_supported(M, K, blockSize))
+        return fail(ALJ_ERR_UNSUPPORTED, "gemm_nf4: K=%d blockSize=%d (K %% 256, blockSize 64/128)", K, blockSize);
+    GemmNf4Args a;
+    memset(&a, 0, sizeof a);
+    a.nseg = nseg;
+    for (int s = 0; s < nseg; ++s) {
+        if (!y[s] || !packed[s]) return fail(ALJ_ERR_BAD_ARG, "gemm_nf4: null segment %d", s);
+        if (reinterpret_cast<uintptr_t>(packed[s]) & 255)
+            return fail(ALJ_ERR_BAD_ARG, "gemm_nf4: packed weights %d not 256-byte aligned", s);
+        if (rows[s] < 1 || ldy[s] < rows[s]) return fail(ALJ_ERR_BAD_DIMS, "gemm_nf4: rows=%d ldy=%d", rows[s], ldy[s]);
+        a.y[s] = y[s];
+        a.ldy[s] = ldy[s];
+        a.packed[s] = packed[s];
+        a.rows[s] = rows[s];
+    }
+    a.x = x_bf16;
+    a.M = M;
+    a.K = K;
+    a.group = blockSize;
+    a.workspace = workspace;
+    a.workspace_bytes = workspace_bytes > 0 ? static_cast<size_t>(workspace_bytes) : 0;
+    const size_t need = gemm_nf4_workspace_bytes(M, K, gemm_nf4_tiles(M, nseg, rows), sm_count_for_current_device());
+    if (a.workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
+        return fail(ALJ_ERR_BAD_ARG, "gemm_nf4: workspace %lld bytes (need %zu, 256-byte aligned)", workspace_bytes, need);
+    return launch_status(launch_gemm_nf4(a, pick_stream(st, stream)), "gemm_nf4");
+}
+
 int aljabr_blackwell_dequantize_dev(int type, float* dst, const void* src, const float* absmax, long long numel, int group,
                                     void* stream) {
     int err = 0;

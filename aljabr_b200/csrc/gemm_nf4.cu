@@ -1,0 +1,864 @@
+// Batched NF4 dequantise-and-GEMM on the 5th-generation tensor cores (tcgen05,
+// sm_100a): Y[m][n] = sum_k X[m][k] * W[n][k] for a batch of M >= 2 tokens
+// (prefill, batched decode), the weights in the NF4 layout of the batch-1 path
+// (two codes per byte, high nibble first, one fp32 absmax per `group` = 64 or
+// 128 consecutive elements of a row).  This is AccelOps.linear for M > 1
+// (engine/safetensor/.../tensor/AccelOps.java:453-456: cblas_sgemm NoTrans x
+// Trans on the dequantised fp32 weight), with the activations in bf16.
+//
+// Arithmetic.  The reference multiplies fp32 weights T[c] * s by fp32
+// activations.  Rounding either operand to one 16-bit float costs ~1e-3
+// relative per output, over the 1e-3 element-wise bound, so:
+//   * A operand (weights): the codebook value only, T[c] = Th[c] + Tl[c] with
+//     Th = fp16(T), Tl = fp16(T - Th) (|T - Th - Tl| <= 2^-22 |T|).  Two
+//     tcgen05.mma per k-step (A = Th tile, then A = Tl tile, same B).
+//   * B operand (activations): x' = x * 2^f per token, f chosen so that
+//     max|x'| lies in [2^14, 2^15) -- exact, since a bf16 value has 8
+//     significant bits and fp16 11 (gemm_x_prep_kernel).
+//   * The absmax is not folded into the operands: each NF4 group gets its own
+//     TMEM accumulator D_g = sum_{k in g} T[c_k] x'_k, and the epilogue warps
+//     accumulate acc += s_g * D_g in fp32 on the CUDA cores, then scale by
+//     2^-f.  So the scale enters exactly as in the reference (one fp32
+//     product per group instead of per element) and no per-row exponent or
+//     weight preparation is needed.
+//
+// Weight layout.  The GEMM reads NF4 weights packed once (gemm_nf4_pack_
+// kernel, at weight registration, like the reference's prepared Q4_0 cache):
+// for each 128-row tile and each 256-column unit, the 128 rows x 128 code
+// bytes are one contiguous 16 KB block, and for each 16-group slot the 128
+// rows x 16 absmax one contiguous 8 KB block (rows past the matrix are zero).
+// A tile's codes in the original row-major layout are 128-byte pieces 2 KB
+// to 14 KB apart, and streamed that way DRAM served one 16 KB copy per ~4 us
+// per SM (about 0.5 TB/s in all).
+//
+// Tiles and schedule.  A tile is 128 weight rows (the MMA's M, TMEM lanes) x
+// MT tokens (the MMA's N: 16, 32, 64 or 128; more tokens use several token
+// tiles).  A unit is one tile x 256 columns of K.  Units are dealt out to one
+// CTA per SM in equal contiguous ranges ("stream-K"): a tile whose K range is
+// split between CTAs is finished by the last of them to arrive, which sums
+// the others' fp32 partials in K order (deterministic; a per-tile counter in
+// the workspace is returned to 0).
+//
+// Warp roles (one CTA per SM, up to 227 KB shared memory):
+//   warps 0-3      dequant: thread r owns weight row r of the tile; per stage
+//                  (64 columns) it reads its 32 code bytes and writes the 64
+//                  Th and 64 Tl values of the row into the 128-byte-swizzled
+//                  K-major A tiles (byte b -> (Th, Tl) pairs of its two codes
+//                  via a 64 KB table, 32 bank-private copies, one PRMT + one
+//                  8-byte load per byte);
+//   warps 4..      epilogue (1 or 2 warpgroups): warp w reads TMEM lanes
+//                  32 (w % 4) .. +31 = its 32 rows, a token half each;
+//   next warp      weight stream: TMA copies of the codes (box 128 B x 128
+//                  rows = 4 stages) and the absmax (box 16 groups x 128 rows);
+//   next warp      activation stream: TMA copies of the fp16 activations
+//                  (box 64 x MT, 128-byte swizzle) into their own deeper ring,
+//                  so neither stream waits on the other's consumers;
+//   last warp      TMEM allocation and the MMA issue (one thread).
+// Every mbarrier wait is bounded; the first wait that runs out sets a shared
+// abort flag, records ALJ_FAULT_TIMEOUT, and every role leaves its loop; the
+// MMA thread waits (bounded) for its last commit before TMEM is released.
+#include "common.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
+
+namespace alj {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();   // matvec.cu
+
+namespace {
+
+constexpr int kRows = 128;                  // weight rows per tile
+constexpr int kStageK = 64;                 // K per stage (A tile: 64 fp16 = one 128 B swizzle row)
+constexpr int kUnitK = 256;                 // K per stream-K unit (one codes copy)
+constexpr int kUnitStages = kUnitK / kStageK;
+constexpr int kAbsCols = 16;                // absmax groups per absmax copy
+constexpr int kMaxCodesRing = 4;
+constexpr int kAbsRing = 2;
+constexpr int kTableBytes = 256 * 32 * 8;   // 64 KB
+constexpr int kCodesBytes = kRows * 128;    // 16 KB
+constexpr int kAbsBytes = kRows * kAbsCols * 4;   // 8 KB
+constexpr int kATileBytes = kRows * 128;    // 16 KB (one of Th / Tl)
+constexpr int kMaxSeg = 3;
+constexpr int kSmemMax = 232448;
+constexpr int kMaxARing = 4;                // dequantised A stages
+constexpr int kMaxXRing = 16;               // activation stages
+constexpr int kMaxDBufs = 8;
+
+struct alignas(64) GemmSeg {
+    CUtensorMap codes;     // packed codes: uint8 [tiles * units * 128][128], box {128, 128}, 128 B swizzle
+    CUtensorMap absmax;    // packed absmax: fp32 [tiles * slots * 128][16], box {16, 128}, 64 B swizzle
+    float* y;              // y[m * ldy + n]
+    int rows;
+    int ldy;
+    int tile0;             // first row tile of the segment
+};
+
+struct alignas(64) GemmParams {
+    GemmSeg seg[kMaxSeg];
+    CUtensorMap xmap;      // fp16 [M][K], box {64, MT}, 128 B swizzle
+    const int* tokexp;     // [M]: x' = x * 2^tokexp
+    float* partials;       // [2 * grid][MT][128]
+    unsigned int* counters;   // [tiles], 0 before and after
+    int nseg, M, K, group;
+    int row_tiles, tok_tiles, tiles, units_per_tile, abs_slots;
+    long long units;
+    int grid, codes_ring, a_ring, x_ring, dbufs;
+};
+
+// ------------------------------------------------------------------ PTX
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+__device__ __forceinline__ float lds_f32(uint32_t a) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+// Generic-proxy shared-memory writes (the dequantised A tiles) become visible
+// to the tensor core (async proxy).
+__device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, rows of 128 B,
+// 8-row groups 1024 B apart (SBO), LBO 16 B (unused for swizzled K-major),
+// descriptor version 1, base offset 0 (tiles are 1024-byte aligned).
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
+    return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+// Instruction descriptor, kind::f16: D f32, A/B f16, both K-major, M = 128, N = n.
+__host__ __device__ constexpr uint32_t idesc_f16(int n) {
+    return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(kRows >> 4) << 24);
+}
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+            d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accum)
+        : "memory");
+}
+// Arrive once on `bar` when every tcgen05.mma this thread issued so far has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// 32 lanes x 16 columns of 32 bit from TMEM; the wait is tied to the outputs
+// so no use of them can be scheduled before it.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15])
+                 :
+                 : "memory");
+}
+
+// ------------------------------------------------------------------ waits
+// Bounded wait that also gives up as soon as another role has (abort flag).
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (*abort_flag) return false;
+        if (clock64() - t0 > kSpinLimitCycles) {
+            record_fault(ALJ_FAULT_TIMEOUT);
+            *abort_flag = 1;
+            return false;
+        }
+    }
+    return true;
+}
+
+// The same wait by every lane of a warp, with one verdict for all of them.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+    return __all_sync(0xffffffffu, wait_bar(bar, parity, abort_flag));
+}
+
+// ------------------------------------------------------------------ schedule
+__device__ __forceinline__ long long unit_begin(const GemmParams& p, int c) {
+    return static_cast<long long>(c) * p.units / p.grid;
+}
+// CTA whose unit range holds unit u.
+__device__ __forceinline__ int cta_of(const GemmParams& p, long long u) {
+    int c = static_cast<int>(u * p.grid / p.units);
+    while (c + 1 < p.grid && unit_begin(p, c + 1) <= u) ++c;
+    while (c > 0 && unit_begin(p, c) > u) --c;
+    return c;
+}
+// Partial slot of CTA c's piece of tile t (a CTA has at most two split pieces:
+// its first and its last tile).
+__device__ __forceinline__ int slot_of(const GemmParams& p, int c, int t) {
+    return 2 * c + (t == static_cast<int>(unit_begin(p, c) / p.units_per_tile) ? 0 : 1);
+}
+
+struct Piece {
+    int t, seg, row0, tok0, c0, c1;   // tile, segment, first row in segment, first token, unit range in tile
+};
+__device__ __forceinline__ Piece make_piece(const GemmParams& p, int t, long long u0, long long u1) {
+    Piece pc;
+    pc.t = t;
+    const long long tb = static_cast<long long>(t) * p.units_per_tile;
+    pc.c0 = static_cast<int>((u0 > tb ? u0 : tb) - tb);
+    const long long te = tb + p.units_per_tile;
+    pc.c1 = static_cast<int>((u1 < te ? u1 : te) - tb);
+    const int rt = t / p.tok_tiles;
+    pc.tok0 = (t % p.tok_tiles);
+    int s = 0;
+    while (s + 1 < p.nseg && rt >= p.seg[s + 1].tile0) ++s;
+    pc.seg = s;
+    pc.row0 = (rt - p.seg[s].tile0) * kRows;
+    return pc;
+}
+
+// ------------------------------------------------------------------ kernel
+template <int MT, int EW>
+__global__ void __launch_bounds__(32 * (7 + 4 * EW), 1) nf4_tc_gemm_kernel(const __grid_constant__ GemmParams p) {
+    constexpr int NT = MT / EW;                 // tokens per epilogue thread
+    constexpr int kEpiWarp0 = 4;
+    constexpr int kProdWarp = 4 + 4 * EW;       // codes + absmax stream
+    constexpr int kXWarp = kProdWarp + 1;       // activation tiles
+    constexpr int kMmaWarp = kProdWarp + 2;
+    constexpr int kXBytes = MT * 128;
+    constexpr int kAStageBytes = 2 * kATileBytes;
+    constexpr uint32_t kIdesc = idesc_f16(MT);
+
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int CQ = p.codes_ring;
+    const int SA = p.a_ring;
+    const int SX = p.x_ring;
+    const int NB = p.dbufs;
+    uint8_t* table = smem;
+    uint8_t* codes_ring = table + kTableBytes;
+    uint8_t* abs_ring = codes_ring + static_cast<size_t>(CQ) * kCodesBytes;
+    uint8_t* a_ring = abs_ring + kAbsRing * kAbsBytes;
+    uint8_t* x_ring = a_ring + static_cast<size_t>(SA) * kAStageBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(x_ring + static_cast<size_t>(SX) * kXBytes);
+    uint64_t* codes_full = bars;
+    uint64_t* codes_empty = codes_full + kMaxCodesRing;
+    uint64_t* abs_full = codes_empty + kMaxCodesRing;
+    uint64_t* abs_empty = abs_full + kAbsRing;
+    uint64_t* a_full = abs_empty + kAbsRing;
+    uint64_t* a_empty = a_full + kMaxARing;
+    uint64_t* x_full = a_empty + kMaxARing;
+    uint64_t* x_empty = x_full + kMaxXRing;
+    uint64_t* d_full = x_empty + kMaxXRing;
+    uint64_t* d_empty = d_full + kMaxDBufs;
+    uint64_t* done_bar = d_empty + kMaxDBufs;
+    uint64_t* epi_a = done_bar + 1;             // epilogue warps stored their partials
+    uint64_t* epi_b = epi_a + 1;                // the tile counter was taken (last_flag set)
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(epi_b + 1);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_b + 1) + 1;
+    int* last_flag = reinterpret_cast<int*>(epi_b + 1) + 2;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    // Byte -> (Th pair, Tl pair) table: entry b, copy l at 256 b + 8 l.  The
+    // 16 (Th, Tl) code pairs go to a scratch word array first (in the A ring,
+    // not yet in use), then every thread writes two copies per 16-byte store.
+    uint32_t* pairs = reinterpret_cast<uint32_t*>(a_ring);
+    if (threadIdx.x < 16) {
+        const float t = nf4_value(threadIdx.x);
+        const __half h = __float2half_rn(t);
+        const __half l = __float2half_rn(t - __half2float(h));
+        pairs[threadIdx.x] = static_cast<uint32_t>(__half_as_ushort(h)) |
+                             (static_cast<uint32_t>(__half_as_ushort(l)) << 16);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < 256 * 16; e += blockDim.x) {
+        const int b = e >> 4;
+        const uint32_t p0 = pairs[b >> 4], p1 = pairs[b & 15];
+        const uint32_t hx = (p0 & 0xFFFFu) | (p1 << 16);
+        const uint32_t lx = (p0 >> 16) | (p1 & 0xFFFF0000u);
+        reinterpret_cast<uint4*>(table)[e] = make_uint4(hx, lx, hx, lx);
+    }
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kMaxCodesRing; ++i) {
+            mbar_init(&codes_full[i], 1);
+            mbar_init(&codes_empty[i], 4);
+        }
+        for (int i = 0; i < kAbsRing; ++i) {
+            mbar_init(&abs_full[i], 1);
+            mbar_init(&abs_empty[i], 4 * EW);
+        }
+        for (int i = 0; i < kMaxARing; ++i) {
+            mbar_init(&a_full[i], 4);
+            mbar_init(&a_empty[i], 1);
+        }
+        for (int i = 0; i < kMaxXRing; ++i) {
+            mbar_init(&x_full[i], 1);
+            mbar_init(&x_empty[i], 1);
+        }
+        for (int i = 0; i < kMaxDBufs; ++i) {
+            mbar_init(&d_full[i], 1);
+            mbar_init(&d_empty[i], 4 * EW);
+        }
+        mbar_init(done_bar, 1);
+        mbar_init(epi_a, 4 * EW);
+        mbar_init(epi_b, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(512)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+
+    const long long u0 = unit_begin(p, blockIdx.x);
+    const long long u1 = unit_begin(p, blockIdx.x + 1);
+    const int t_first = static_cast<int>(u0 / p.units_per_tile);
+    const int t_last = static_cast<int>((u1 - 1) / p.units_per_tile);
+    const int gpu = p.group / kStageK;          // stages per group (1 or 2)
+
+    if (warp < 4) {
+        // ---------------------------------------------------------- dequant
+        const int r = threadIdx.x;              // tile row
+        const uint32_t lane8 = static_cast<uint32_t>(lane) * 8u;
+        const uint32_t tab = smem_u32(table);
+        const uint32_t swz = static_cast<uint32_t>(r & 7);
+        int ci = 0, si = 0;
+        bool ok = u1 > u0;
+        for (int t = t_first; ok && t <= t_last; ++t) {
+            const Piece pc = make_piece(p, t, u0, u1);
+            for (int c = pc.c0; ok && c < pc.c1; ++c, ++ci) {
+                const int cs = ci % CQ;
+                if (!warp_wait(&codes_full[cs], (ci / CQ) & 1, abort_flag)) { ok = false; break; }
+                const uint32_t crow = smem_u32(codes_ring + static_cast<size_t>(cs) * kCodesBytes) + r * 128;
+                for (int st = 0; st < kUnitStages; ++st, ++si) {
+                    const int ss = si % SA;
+                    if (!warp_wait(&a_empty[ss], ((si / SA) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                    const uint32_t ahi = smem_u32(a_ring + static_cast<size_t>(ss) * kAStageBytes) + r * 128;
+                    const uint32_t alo = ahi + kATileBytes;
+                    const uint4 w0 = lds128(crow + ((static_cast<uint32_t>(2 * st) ^ swz) << 4));
+                    const uint4 w1 = lds128(crow + ((static_cast<uint32_t>(2 * st + 1) ^ swz) << 4));
+                    const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t w = words[j];
+                        const uint2 e0 = lds64(tab + prmt(w, lane8, 0x5504u));
+                        const uint2 e1 = lds64(tab + prmt(w, lane8, 0x5514u));
+                        const uint2 e2 = lds64(tab + prmt(w, lane8, 0x5524u));
+                        const uint2 e3 = lds64(tab + prmt(w, lane8, 0x5534u));
+                        const uint32_t off = (static_cast<uint32_t>(j) ^ swz) << 4;
+                        sts128(ahi + off, e0.x, e1.x, e2.x, e3.x);
+                        sts128(alo + off, e0.y, e1.y, e2.y, e3.y);
+                    }
+                    fence_async_shared();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&a_full[ss]);
+                }
+                __syncwarp();
+                if (ok && lane == 0) mbar_arrive(&codes_empty[cs]);
+            }
+        }
+    } else if (warp < kProdWarp) {
+        // ---------------------------------------------------------- epilogue
+        const int q = warp & 3;
+        const int eh = (warp - kEpiWarp0) >> 2;
+        const int r = 32 * q + lane;
+        const uint32_t tq = tmem_base + (static_cast<uint32_t>(32 * q) << 16);
+        int ai = 0, di = 0, ep = 0;
+        bool ok = u1 > u0;
+        float acc[NT];
+        for (int t = t_first; ok && t <= t_last; ++t) {
+            const Piece pc = make_piece(p, t, u0, u1);
+            const GemmSeg& sg = p.seg[pc.seg];
+#pragma unroll
+            for (int j = 0; j < NT; ++j) acc[j] = 0.0f;
+            int as = -1;
+            for (int c = pc.c0; ok && c < pc.c1; ++c) {
+                const int kb = c * kUnitK;
+                const int col0 = kb / p.group;
+                if (c == pc.c0 || col0 % kAbsCols == 0) {
+                    if (as >= 0) {
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&abs_empty[as]);
+                    }
+                    as = ai % kAbsRing;
+                    if (!warp_wait(&abs_full[as], (ai / kAbsRing) & 1, abort_flag)) { ok = false; as = -1; break; }
+                    ++ai;
+                }
+                const uint32_t arow = smem_u32(abs_ring + as * kAbsBytes) + r * 64;
+                const uint32_t aswz = static_cast<uint32_t>((r >> 1) & 3);
+                for (int gi = 0; gi < kUnitK / p.group; ++gi, ++di) {
+                    const int ds = di % NB;
+                    if (!warp_wait(&d_full[ds], (di / NB) & 1, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    const int col = (col0 + gi) % kAbsCols;
+                    const float s = lds_f32(arow + (((static_cast<uint32_t>(col >> 2) ^ aswz) << 4) | ((col & 3) << 2)));
+                    const uint32_t ta = tq + static_cast<uint32_t>(ds * MT + eh * NT);
+#pragma unroll
+                    for (int h = 0; h < NT / 16; ++h) {
+                        uint32_t v[16];
+                        tmem_ld16(ta + 16 * h, v);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) acc[16 * h + j] = fmaf(s, __uint_as_float(v[j]), acc[16 * h + j]);
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&d_empty[ds]);
+                }
+            }
+            if (as >= 0) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&abs_empty[as]);
+            }
+            if (!ok) break;
+            // ---- write-out
+            const int n = pc.row0 + r;
+            const int m0 = pc.tok0 * MT + eh * NT;
+            const int cf = cta_of(p, static_cast<long long>(t) * p.units_per_tile);
+            const int cl = cta_of(p, static_cast<long long>(t + 1) * p.units_per_tile - 1);
+            bool write = cf == cl;
+            if (!write) {
+                float* part = p.partials + static_cast<size_t>(slot_of(p, blockIdx.x, t)) * (MT * kRows);
+#pragma unroll
+                for (int j = 0; j < NT; ++j) part[(eh * NT + j) * kRows + r] = acc[j];
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(epi_a);
+                if (warp == kEpiWarp0) {
+                    const bool all = warp_wait(epi_a, ep & 1, abort_flag);
+                    if (lane == 0) {
+                        *last_flag = 0;
+                        if (all) {
+                            const unsigned prev = atomicAdd(&p.counters[t], 1u);
+                            *last_flag = prev == static_cast<unsigned>(cl - cf) ? 1 : 0;
+                        }
+                        mbar_arrive(epi_b);
+                    }
+                    __syncwarp();
+                }
+                const bool got = warp_wait(epi_b, ep & 1, abort_flag);
+                ++ep;
+                if (!got) { ok = false; break; }
+                write = *reinterpret_cast<volatile int*>(last_flag) != 0;
+                if (write) {
+                    __threadfence();
+#pragma unroll
+                    for (int j = 0; j < NT; ++j) acc[j] = 0.0f;
+                    for (int cc = cf; cc <= cl; ++cc) {
+                        const float* pp =
+                            p.partials + static_cast<size_t>(slot_of(p, cc, t)) * (MT * kRows) + eh * NT * kRows + r;
+#pragma unroll
+                        for (int j = 0; j < NT; ++j) acc[j] += __ldcg(pp + j * kRows);
+                    }
+                    if (threadIdx.x == kEpiWarp0 * 32) p.counters[t] = 0u;
+                }
+            }
+            if (write && n < sg.rows) {
+#pragma unroll
+                for (int j = 0; j < NT; ++j) {
+                    const int m = m0 + j;
+                    if (m < p.M) {
+                        const int f = __ldg(p.tokexp + m);
+                        sg.y[static_cast<size_t>(m) * sg.ldy + n] = acc[j] * __int_as_float((127 - f) << 23);
+                    }
+                }
+            }
+        }
+    } else if (warp == kProdWarp) {
+        // ---------------------------------------------------------- codes + absmax stream
+        if (lane == 0) {
+            int ci = 0, ai = 0;
+            bool ok = u1 > u0;
+            for (int t = t_first; ok && t <= t_last; ++t) {
+                const Piece pc = make_piece(p, t, u0, u1);
+                const GemmSeg& sg = p.seg[pc.seg];
+                for (int c = pc.c0; ok && c < pc.c1; ++c) {
+                    const int kb = c * kUnitK;
+                    const int col0 = kb / p.group;
+                    if (c == pc.c0 || col0 % kAbsCols == 0) {
+                        const int as = ai % kAbsRing;
+                        if (!wait_bar(&abs_empty[as], ((ai / kAbsRing) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                        mbar_arrive_expect_tx(&abs_full[as], kAbsBytes);
+                        tma_load_2d(smem_u32(abs_ring + as * kAbsBytes), &sg.absmax, 0,
+                                    ((pc.row0 / kRows) * p.abs_slots + col0 / kAbsCols) * kRows, &abs_full[as]);
+                        ++ai;
+                    }
+                    const int cs = ci % CQ;
+                    if (!wait_bar(&codes_empty[cs], ((ci / CQ) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&codes_full[cs], kCodesBytes);
+                    tma_load_2d(smem_u32(codes_ring + static_cast<size_t>(cs) * kCodesBytes), &sg.codes, 0,
+                                ((pc.row0 / kRows) * p.units_per_tile + c) * kRows, &codes_full[cs]);
+                    ++ci;
+                }
+            }
+        }
+    } else if (warp == kXWarp) {
+        // ---------------------------------------------------------- activation tiles
+        if (lane == 0) {
+            int xi = 0;
+            bool ok = u1 > u0;
+            for (int t = t_first; ok && t <= t_last; ++t) {
+                const Piece pc = make_piece(p, t, u0, u1);
+                for (int c = pc.c0; ok && c < pc.c1; ++c) {
+                    for (int st = 0; st < kUnitStages; ++st, ++xi) {
+                        const int xs = xi % SX;
+                        if (!wait_bar(&x_empty[xs], ((xi / SX) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                        mbar_arrive_expect_tx(&x_full[xs], kXBytes);
+                        tma_load_2d(smem_u32(x_ring + static_cast<size_t>(xs) * kXBytes), &p.xmap,
+                                    c * kUnitK + st * kStageK, pc.tok0 * MT, &x_full[xs]);
+                    }
+                }
+            }
+        }
+    } else {
+        // ---------------------------------------------------------- MMA issue
+        if (lane == 0) {
+            int si = 0, di = 0;
+            bool ok = u1 > u0;
+            for (int t = t_first; ok && t <= t_last; ++t) {
+                const Piece pc = make_piece(p, t, u0, u1);
+                for (int c = pc.c0; ok && c < pc.c1; ++c) {
+                    for (int st = 0; st < kUnitStages; ++st, ++si) {
+                        const int g = st % gpu;       // stage within its group (pieces start on group starts)
+                        const int ds = di % NB;
+                        if (g == 0 && !wait_bar(&d_empty[ds], ((di / NB) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                        const int sa = si % SA;
+                        const int sx = si % SX;
+                        if (!wait_bar(&x_full[sx], (si / SX) & 1, abort_flag) ||
+                            !wait_bar(&a_full[sa], (si / SA) & 1, abort_flag)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint32_t abase = smem_u32(a_ring + static_cast<size_t>(sa) * kAStageBytes);
+                        const uint64_t ah = sdesc(abase), al = sdesc(abase + kATileBytes),
+                                       bx = sdesc(smem_u32(x_ring + static_cast<size_t>(sx) * kXBytes));
+                        const uint32_t d = tmem_base + static_cast<uint32_t>(ds * MT);
+#pragma unroll
+                        for (int kk = 0; kk < kStageK / 16; ++kk) {
+                            tc_mma(d, ah + 2 * kk, bx + 2 * kk, kIdesc, (g > 0 || kk > 0) ? 1u : 0u);
+                            tc_mma(d, al + 2 * kk, bx + 2 * kk, kIdesc, 1u);
+                        }
+                        tc_commit(&a_empty[sa]);
+                        tc_commit(&x_empty[sx]);
+                        if (g == gpu - 1) {
+                            tc_commit(&d_full[ds]);
+                            ++di;
+                        }
+                    }
+                }
+            }
+            // Every MMA issued has completed before TMEM is released.
+            tc_commit(done_bar);
+            mbar_wait(done_bar, 0);
+        }
+        __syncwarp();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(512) : "memory");
+    }
+}
+
+// bf16 activations -> fp16 x * 2^f (per token row), f = 15 - e with
+// max|x| = m * 2^e, m in [0.5, 1): max|x'| in [2^14, 2^15).  Block 0 also
+// clears the stream-K tile counters.
+__global__ void gemm_x_prep_kernel(const __nv_bfloat16* __restrict__ x, int K, __half* __restrict__ xh,
+                                   int* __restrict__ tokexp, unsigned int* __restrict__ counters, int ncounters) {
+    const int m = blockIdx.x;
+    if (m == 0)
+        for (int i = threadIdx.x; i < ncounters; i += blockDim.x) counters[i] = 0u;
+    const uint4* row = reinterpret_cast<const uint4*>(x + static_cast<size_t>(m) * K);
+    const int n8 = K / 8;
+    float mx = 0.0f;
+    for (int i = threadIdx.x; i < n8; i += blockDim.x) {
+        const uint4 v = __ldg(row + i);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            mx = fmaxf(mx, fabsf(__uint_as_float(w[j] << 16)));
+            mx = fmaxf(mx, fabsf(__uint_as_float(w[j] & 0xFFFF0000u)));
+        }
+    }
+    __shared__ float red[32];
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    mx = red[0];
+    int f = 0;
+    if (mx > 0.0f && mx <= 3.4028234663852886e38f) {
+        int e;
+        frexpf(mx, &e);
+        f = 15 - e;
+        f = f < -100 ? -100 : (f > 100 ? 100 : f);
+    }
+    if (threadIdx.x == 0) tokexp[m] = f;
+    // 2^f as two exact factors (|f| <= 100 < 126 would fit one, kept general).
+    const float sc = __int_as_float((127 + f) << 23);
+    uint4* out = reinterpret_cast<uint4*>(xh + static_cast<size_t>(m) * K);
+    for (int i = threadIdx.x; i < n8; i += blockDim.x) {
+        const uint4 v = __ldg(row + i);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const __half lo = __float2half_rn(__uint_as_float(w[j] << 16) * sc);
+            const __half hi = __float2half_rn(__uint_as_float(w[j] & 0xFFFF0000u) * sc);
+            o[j] = static_cast<uint32_t>(__half_as_ushort(lo)) | (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
+        }
+        out[i] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+// One-time repack of an NF4 matrix [rows][K] (codes, absmax in the original
+// layout) into the GEMM's tile-contiguous layout (see the file comment).
+__global__ void gemm_nf4_pack_kernel(uint8_t* __restrict__ pcodes, float* __restrict__ pabs,
+                                     const uint8_t* __restrict__ codes, const float* __restrict__ absmax, int rows,
+                                     int K, int group, int row_tiles, int units, int slots) {
+    const size_t nchunks = static_cast<size_t>(row_tiles) * units * kRows * 8;     // 16-byte pieces
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t q = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; q < nchunks; q += stride) {
+        const int j = static_cast<int>(q & 7);
+        const int rr = static_cast<int>((q >> 3) & (kRows - 1));
+        const size_t tu = q >> 10;                      // rt * units + u
+        const int u = static_cast<int>(tu % units);
+        const int row = static_cast<int>(tu / units) * kRows + rr;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (row < rows)
+            v = __ldg(reinterpret_cast<const uint4*>(codes + static_cast<size_t>(row) * (K / 2) + u * 128 + j * 16));
+        reinterpret_cast<uint4*>(pcodes)[q] = v;
+    }
+    const int ncols = K / group;
+    const size_t nabs = static_cast<size_t>(row_tiles) * slots * kRows * kAbsCols;
+    for (size_t f = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; f < nabs; f += stride) {
+        const int c = static_cast<int>(f & (kAbsCols - 1));
+        const int rr = static_cast<int>((f >> 4) & (kRows - 1));
+        const size_t ts = f >> 11;                      // rt * slots + s
+        const int col = static_cast<int>(ts % slots) * kAbsCols + c;
+        const int row = static_cast<int>(ts / slots) * kRows + rr;
+        pabs[f] = (row < rows && col < ncols) ? __ldg(absmax + static_cast<size_t>(row) * ncols + col) : 0.0f;
+    }
+}
+
+// ------------------------------------------------------------------ host
+int token_tile_for(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+struct WsLayout {
+    size_t xh, tokexp, counters, partials, total;
+};
+WsLayout ws_layout(int M, int K, int tiles, int grid) {
+    const int MT = token_tile_for(M);
+    WsLayout w;
+    w.xh = 0;
+    w.tokexp = align_up(w.xh + static_cast<size_t>(M) * K * 2, 256);
+    w.counters = align_up(w.tokexp + static_cast<size_t>(M) * 4, 256);
+    w.partials = align_up(w.counters + static_cast<size_t>(tiles) * 4, 256);
+    w.total = align_up(w.partials + static_cast<size_t>(2) * grid * MT * kRows * 4, 256);
+    return w;
+}
+
+// Ring depths: two dequantised A stages, a codes ring of 3 units (2 if the
+// activation ring would otherwise hold fewer than 3 stages), and as deep an
+// activation ring (up to 16 stages) as fits.
+struct Rings {
+    int codes, a, x;
+    size_t smem;
+};
+Rings rings_for(int MT) {
+    const size_t fixed = 1024 + kTableBytes + kAbsRing * kAbsBytes + 1024;
+    const size_t xb = static_cast<size_t>(MT) * 128;
+    Rings r{0, 2, 0, 0};
+    for (int cq = 3; cq >= 2; --cq) {
+        const size_t used = fixed + static_cast<size_t>(cq) * kCodesBytes + r.a * 2 * kATileBytes;
+        if (used >= static_cast<size_t>(kSmemMax)) continue;
+        const int sx = static_cast<int>(std::min<size_t>(kMaxXRing, (kSmemMax - used) / xb));
+        if (sx >= 3 || cq == 2) {
+            r.codes = cq;
+            r.x = sx;
+            r.smem = used + sx * xb;
+            break;
+        }
+    }
+    return r;
+}
+
+bool encode(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base, uint64_t inner, uint64_t outer,
+            uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+    auto fn = tensor_map_encoder();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {inner * esize};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t es[2] = {1, 1};
+    return fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int MT, int EW>
+cudaError_t launch_mt(const GemmParams& p, size_t smem, cudaStream_t stream) {
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!configured[dev & 63]) {
+        cudaError_t e = cudaFuncSetAttribute(nf4_tc_gemm_kernel<MT, EW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kSmemMax);
+        if (e != cudaSuccess) return e;
+        configured[dev & 63] = true;
+    }
+    nf4_tc_gemm_kernel<MT, EW><<<p.grid, 32 * (7 + 4 * EW), smem, stream>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+bool gemm_nf4_supported(int M, int K, int group) {
+    return M >= 1 && K > 0 && K % kUnitK == 0 && (group == 64 || group == 128) && tensor_map_encoder() != nullptr;
+}
+
+namespace {
+int abs_slots_of(int K, int group) { return (K / group + kAbsCols - 1) / kAbsCols; }
+size_t packed_codes_bytes(int rows, int K) {
+    return static_cast<size_t>((rows + kRows - 1) / kRows) * (K / kUnitK) * kCodesBytes;
+}
+}  // namespace
+
+size_t gemm_nf4_packed_bytes(int rows, int K, int group) {
+    return packed_codes_bytes(rows, K) + static_cast<size_t>((rows + kRows - 1) / kRows) * abs_slots_of(K, group) * kAbsBytes;
+}
+
+cudaError_t launch_gemm_nf4_pack(void* packed, const void* codes, const void* absmax, int rows, int K, int group,
+                                 cudaStream_t stream) {
+    if (rows < 1 || !gemm_nf4_supported(1, K, group)) return cudaErrorNotSupported;
+    if ((reinterpret_cast<uintptr_t>(packed) & 255) || (reinterpret_cast<uintptr_t>(codes) & 15) || (K / 2) % 16)
+        return cudaErrorInvalidValue;
+    uint8_t* pc = static_cast<uint8_t*>(packed);
+    float* pa = reinterpret_cast<float*>(pc + packed_codes_bytes(rows, K));
+    const int row_tiles = (rows + kRows - 1) / kRows;
+    gemm_nf4_pack_kernel<<<2 * sm_count_for_current_device(), 256, 0, stream>>>(
+        pc, pa, static_cast<const uint8_t*>(codes), static_cast<const float*>(absmax), rows, K, group, row_tiles,
+        K / kUnitK, abs_slots_of(K, group));
+    return cudaGetLastError();
+}
+
+size_t gemm_nf4_workspace_bytes(int M, int K, int total_tiles, int grid) {
+    return ws_layout(M, K, total_tiles, grid).total;
+}
+
+int gemm_nf4_tiles(int M, int nseg, const int* rows) {
+    int rt = 0;
+    for (int s = 0; s < nseg; ++s) rt += (rows[s] + kRows - 1) / kRows;
+    const int MT = token_tile_for(M);
+    return rt * ((M + MT - 1) / MT);
+}
+
+cudaError_t launch_gemm_nf4(const GemmNf4Args& a, cudaStream_t stream) {
+    if (a.nseg < 1 || a.nseg > kMaxSeg || !gemm_nf4_supported(a.M, a.K, a.group)) return cudaErrorNotSupported;
+    const int MT = token_tile_for(a.M);
+    GemmParams p;
+    memset(&p, 0, sizeof p);
+    p.nseg = a.nseg;
+    p.M = a.M;
+    p.K = a.K;
+    p.group = a.group;
+    int rt = 0;
+    p.abs_slots = abs_slots_of(a.K, a.group);
+    for (int s = 0; s < a.nseg; ++s) {
+        GemmSeg& g = p.seg[s];
+        if (a.rows[s] <= 0 || (reinterpret_cast<uintptr_t>(a.packed[s]) & 255)) return cudaErrorInvalidValue;
+        const int tiles_s = (a.rows[s] + kRows - 1) / kRows;
+        const uint8_t* pc = static_cast<const uint8_t*>(a.packed[s]);
+        const void* pa = pc + packed_codes_bytes(a.rows[s], a.K);
+        if (!encode(&g.codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, pc, 128,
+                    static_cast<uint64_t>(tiles_s) * (a.K / kUnitK) * kRows, 128, kRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+            !encode(&g.absmax, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, pa, kAbsCols,
+                    static_cast<uint64_t>(tiles_s) * p.abs_slots * kRows, kAbsCols, kRows, CU_TENSOR_MAP_SWIZZLE_64B))
+            return cudaErrorInvalidValue;
+        g.y = a.y[s];
+        g.rows = a.rows[s];
+        g.ldy = a.ldy[s];
+        g.tile0 = rt;
+        rt += (a.rows[s] + kRows - 1) / kRows;
+    }
+    p.row_tiles = rt;
+    p.tok_tiles = (a.M + MT - 1) / MT;
+    p.tiles = rt * p.tok_tiles;
+    p.units_per_tile = a.K / kUnitK;
+    p.units = static_cast<long long>(p.tiles) * p.units_per_tile;
+    p.grid = static_cast<int>(std::min<long long>(sm_count_for_current_device(), p.units));
+    const WsLayout w = ws_layout(a.M, a.K, p.tiles, p.grid);
+    if (!a.workspace || a.workspace_bytes < w.total || (reinterpret_cast<uintptr_t>(a.workspace) & 255))
+        return cudaErrorInvalidValue;
+    uint8_t* ws = static_cast<uint8_t*>(a.workspace);
+    __half* xh = reinterpret_cast<__half*>(ws + w.xh);
+    p.tokexp = reinterpret_cast<const int*>(ws + w.tokexp);
+    p.counters = reinterpret_cast<unsigned int*>(ws + w.counters);
+    p.partials = reinterpret_cast<float*>(ws + w.partials);
+    if (!encode(&p.xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh, a.K, a.M, kStageK, MT, CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    const Rings rg = rings_for(MT);
+    if (rg.x < 2) return cudaErrorNotSupported;
+    p.codes_ring = rg.codes;
+    p.a_ring = rg.a;
+    p.x_ring = rg.x;
+    p.dbufs = std::min(kMaxDBufs, 512 / MT);
+
+    gemm_x_prep_kernel<<<a.M, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(a.x), a.K, xh,
+                                               reinterpret_cast<int*>(ws + w.tokexp), p.counters, p.tiles);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const size_t smem = rg.smem;
+    switch (MT) {
+        case 16: return launch_mt<16, 1>(p, smem, stream);
+        case 32: return launch_mt<32, 1>(p, smem, stream);
+        case 64: return launch_mt<64, 2>(p, smem, stream);
+        default: return launch_mt<128, 2>(p, smem, stream);
+    }
+}
+
+}  // namespace alj

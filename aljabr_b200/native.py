@@ -81,6 +81,10 @@ SIGNATURES = {
     "aljabr_blackwell_dequantize_dev": (_i, [_i, _p, _p, _p, _ll, _i, _p]),
     "aljabr_blackwell_decode_attention_dev": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _p]),
     "aljabr_blackwell_decode_attention_noalloc": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _p]),
+    "aljabr_blackwell_gemm_nf4_workspace_size": (_ll, [_i, _i, _i, _p]),
+    "aljabr_blackwell_gemm_nf4_packed_size": (_ll, [_i, _i, _i]),
+    "aljabr_blackwell_gemm_nf4_pack": (_i, [_p, _p, _p, _i, _i, _i, _p]),
+    "aljabr_blackwell_gemm_nf4_dev": (_i, [_i, _p, _p, _p, _p, _p, _i, _i, _i, _p, _ll, _p]),
     "aljabr_blackwell_nccl_unique_id": (_i, [_p, _i]),
     "aljabr_blackwell_decode_model_create": (_i, [ctypes.POINTER(_i), _f, _f, _i, _i, _p,
                                                   ctypes.POINTER(ctypes.c_ulonglong)]),
@@ -135,3 +139,38 @@ def check(rc: int) -> int:
 
 def call(name: str, *args) -> int:
     return check(getattr(lib(), name)(*args))
+
+
+def gemm_nf4_workspace_size(M: int, K: int, rows) -> int:
+    """Bytes of device workspace aljabr_blackwell_gemm_nf4_dev needs."""
+    n = len(rows)
+    v = lib().aljabr_blackwell_gemm_nf4_workspace_size(M, K, n, (ctypes.c_int * n)(*rows))
+    if v < 0:
+        check(int(v))
+    return int(v)
+
+
+def gemm_nf4_packed_size(rows: int, K: int, group: int) -> int:
+    """Bytes of the packed form of one NF4 matrix [rows][K]."""
+    v = lib().aljabr_blackwell_gemm_nf4_packed_size(rows, K, group)
+    if v < 0:
+        check(int(v))
+    return int(v)
+
+
+def gemm_nf4_pack(packed: int, codes: int, absmax: int, rows: int, K: int, group: int, stream=None) -> int:
+    """Repack an NF4 matrix (device codes + absmax) for gemm_nf4_dev."""
+    return call("aljabr_blackwell_gemm_nf4_pack", ctypes.c_void_p(packed), ctypes.c_void_p(codes),
+                ctypes.c_void_p(absmax), rows, K, group, None if stream is None else ctypes.c_void_p(stream))
+
+
+def gemm_nf4_dev(y, ldy, packed, rows, x_bf16: int, M: int, K: int, group: int,
+                 workspace: int, workspace_bytes: int, stream=None) -> int:
+    """Batched NF4 linear on device pointers: y[s][m * ldy[s] + n] = sum_k x[m][k] W_s[n][k],
+    W_s packed by gemm_nf4_pack."""
+    n = len(y)
+    P = ctypes.c_void_p * n
+    I = ctypes.c_int * n
+    return call("aljabr_blackwell_gemm_nf4_dev", n, P(*y), I(*ldy), P(*packed), I(*rows),
+                ctypes.c_void_p(x_bf16), M, K, group, ctypes.c_void_p(workspace), workspace_bytes,
+                None if stream is None else ctypes.c_void_p(stream))

@@ -173,6 +173,34 @@ int aljabr_blackwell_decode_attention_dev(float* out, const float* q, const void
                                           int kv_heads, int q_heads, int head_dim, int seq_len,
                                           int start_pos, float scale, void* stream);
 
+/* ---- batched NF4 linear on the tensor cores (prefill / batched decode) ----
+ * AccelOps.linear for M > 1 (engine/safetensor/aljabr-safetensor-core/.../
+ * tensor/AccelOps.java:453-456: cblas_sgemm(RowMajor, NoTrans, Trans, M, N,
+ * K, 1, X, K, W, K, 0, Y, N) on the dequantised weight), bf16 activations:
+ *     y_s[m * ldy_s + n] = sum_k X[m][k] * W_s[n][k]        (fp32 out)
+ * for nseg (1..3) weight matrices W_s sharing X (q/k/v, gate/up).
+ *
+ * The weights are packed once per matrix (at registration, like the
+ * reference's prepared Q4_0 cache, GgufQ32Build): gemm_nf4_pack reads codes
+ * (device NF4 [rows][K/2], two codes per byte, high nibble first; 16-byte
+ * aligned) and absmax (device fp32 [rows][K/blockSize]) and writes `packed`
+ * (device, 256-byte aligned, gemm_nf4_packed_size bytes): each 128-row x
+ * 256-column block of codes and each 128-row x 16-group block of absmax is
+ * contiguous.  K a multiple of 256; blockSize 64 or 128.
+ *
+ * gemm_nf4_dev: x_bf16 device bf16 [M][K] (16-byte aligned); workspace
+ * device memory, 256-byte aligned, at least gemm_nf4_workspace_size bytes,
+ * used by one call at a time (no reference counterpart: the reference's
+ * sgemm runs on the host).  Stream-ordered on `stream` (NULL = the
+ * library's stream). */
+long long aljabr_blackwell_gemm_nf4_packed_size(int rows, int K, int blockSize);
+int aljabr_blackwell_gemm_nf4_pack(void* packed, const void* codes, const void* absmax, int rows, int K,
+                                   int blockSize, void* stream);
+long long aljabr_blackwell_gemm_nf4_workspace_size(int M, int K, int nseg, const int* rows);
+int aljabr_blackwell_gemm_nf4_dev(int nseg, float* const* y, const int* ldy, const void* const* packed,
+                                  const int* rows, const void* x_bf16, int M, int K, int blockSize,
+                                  void* workspace, long long workspace_bytes, void* stream);
+
 /* Same computation as aljabr_blackwell_decode_attention_dev, for callers that
  * may not allocate device memory at call time.  No counterpart in the
  * reference: its attention runs on the host and needs no device scratch.

@@ -88,6 +88,7 @@ def _attention_case(lib, kv_dtype, Hq, Hkv, D, ctx, start, seed, use_fallback_st
     else:
         dk, dv = torch.from_numpy(kf).cuda(), torch.from_numpy(vf).cuda()
     scale = float(np.float32(1.0 / math.sqrt(D)))
+    torch.cuda.synchronize()   # caches written on torch's stream; the library's stream is non-blocking
     out = decode_attention(q, dk.data_ptr(), dv.data_ptr(), kv_dtype, stride, Hkv, Hq, D, ctx, start, scale)
     ref = oracle.gqa_decode_attention(q, kf.ravel(), vf.ravel(), stride, Hkv, Hq, D, ctx, start, scale)
     return out, ref
@@ -117,6 +118,7 @@ def test_attention_golden_known_answers(lib, golden):
             continue
         dk = torch.tensor(fx["k"], dtype=torch.float32, device="cuda")
         dv = torch.tensor(fx["v"], dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()
         out = decode_attention(np.array(fx["q"], np.float32), dk.data_ptr(), dv.data_ptr(), lib.KV_F32, fx["stride"],
                                fx["kv_heads"], fx["q_heads"], fx["head_dim"], fx["seq_len"], fx["start"], fx["scale"])
         np.testing.assert_allclose(out, fx["expected"], atol=fx["tol"], rtol=0, err_msg=fx["name"])

@@ -144,6 +144,7 @@ def test_device_pointer_api_matches_host_api(lib):
     dw = torch.from_numpy(w).cuda()
     dx = torch.from_numpy(x).cuda()
     dy = torch.empty(N, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()   # inputs prepared on torch's stream; the library's stream is non-blocking
     lib.call("aljabr_blackwell_matvec_dev", lib.TYPE_Q4_0, dy.data_ptr(), dx.data_ptr(), dw.data_ptr(), None,
              K, N, 0, None, None)
     torch.cuda.synchronize()   # device-wide: the library's own stream ran the kernel

@@ -27,6 +27,7 @@ def _dev_matvec(lib, w, x, K, N):
     dw = torch.from_numpy(w).cuda()
     dx = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
     dy = torch.full((N,), float("nan"), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()   # inputs from torch's stream; the library's own stream is non-blocking
     lib.call("aljabr_blackwell_matvec_dev", lib.TYPE_Q4_0, dy.data_ptr(), dx.data_ptr(), dw.data_ptr(), None,
              K, N, 0, None, None)
     torch.cuda.synchronize()
@@ -91,6 +92,7 @@ def test_prefetch_hint_changes_nothing_but_timing(lib):
     x = synth.activation(71, K)
     plain = _dev_matvec(lib, w, x, K, N)
     nxt = torch.from_numpy(synth.q4_0(72, 14336, K)).cuda()
+    torch.cuda.synchronize()
     lib.call("aljabr_blackwell_prefetch_hint", nxt.data_ptr(), nxt.numel())
     hinted = _dev_matvec(lib, w, x, K, N)
     np.testing.assert_array_equal(hinted, plain)
@@ -105,6 +107,7 @@ def _dev_matvec_q8(lib, w, x, K, N):
     dw = torch.from_numpy(w).cuda()
     dx = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
     dy = torch.full((N,), float("nan"), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()   # inputs from torch's stream; the library's own stream is non-blocking
     lib.call("aljabr_blackwell_matvec_dev", lib.TYPE_Q8_0, dy.data_ptr(), dx.data_ptr(), dw.data_ptr(), None,
              K, N, 0, None, None)
     torch.cuda.synchronize()

@@ -35,6 +35,7 @@ def _caches(kv_dtype, ctx, stride, seed):
 def _run(native, name, q, k, v, kv_dtype, stride, Hkv, Hq, D, ctx, start, scale, stream):
     import torch
     out = torch.full((Hq * D,), float("nan"), device="cuda", dtype=torch.float32)
+    torch.cuda.synchronize()   # the _dev entry's NULL stream is the library's own, not torch's
     rc = getattr(native.lib(), name)(
         ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(k.data_ptr()),
         ctypes.c_void_p(v.data_ptr()), kv_dtype, stride, Hkv, Hq, D, ctx, start, ctypes.c_float(scale),
