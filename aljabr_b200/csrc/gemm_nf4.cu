@@ -11,7 +11,7 @@
 // relative per output, over the 1e-3 element-wise bound, so:
 //   * A operand (weights): the codebook value only, T[c] = Th[c] + Tl[c] with
 //     Th = fp16(T), Tl = fp16(T - Th) (|T - Th - Tl| <= 2^-22 |T|).  Two
-//     tcgen05.mma per k-step (A = Th tile, then A = Tl tile, same B).
+//     tcgen05.mma per k-step (A = the Th columns, then the Tl columns, same B).
 //   * B operand (activations): x' = x * 2^f per token, f chosen so that
 //     max|x'| lies in [2^14, 2^15) -- exact, since a bf16 value has 8
 //     significant bits and fp16 11 (gemm_x_prep_kernel).
@@ -39,13 +39,17 @@
 // the others' fp32 partials in K order (deterministic; a per-tile counter in
 // the workspace is returned to 0).
 //
-// Warp roles (one CTA per SM, up to 227 KB shared memory):
-//   warps 0-3      dequant: thread r owns weight row r of the tile; per stage
-//                  (64 columns) it reads its 32 code bytes and writes the 64
-//                  Th and 64 Tl values of the row into the 128-byte-swizzled
-//                  K-major A tiles (byte b -> (Th, Tl) pairs of its two codes
-//                  via a 64 KB table, 32 bank-private copies, one PRMT + one
-//                  8-byte load per byte);
+// Warp roles (one CTA per SM, up to 227 KB shared memory, all 512 TMEM
+// columns: 4 A stages x 64 columns, then the accumulators):
+//   warps 0-3      dequant: thread r owns weight row r of the tile = TMEM
+//                  lane r; per stage (64 columns) it reads its 32 code bytes,
+//                  looks up the (Th, Tl) pairs of each byte's two codes in a
+//                  64 KB table (32 bank-private copies: one PRMT + one 8-byte
+//                  load per byte) and stores the 32 Th pairs and 32 Tl pairs
+//                  into the stage's TMEM columns with two tcgen05.st.  The A
+//                  operand never touches shared memory, whose bandwidth a
+//                  shared-memory A tile (written, then read by the MMA) used
+//                  up at about a third of the HBM rate;
 //   warps 4..      epilogue (1 or 2 warpgroups): warp w reads TMEM lanes
 //                  32 (w % 4) .. +31 = its 32 rows, a token half each;
 //   next warp      weight stream: TMA copies of the codes (box 128 B x 128
@@ -53,7 +57,8 @@
 //   next warp      activation stream: TMA copies of the fp16 activations
 //                  (box 64 x MT, 128-byte swizzle) into their own deeper ring,
 //                  so neither stream waits on the other's consumers;
-//   last warp      TMEM allocation and the MMA issue (one thread).
+//   last warp      TMEM allocation and the MMA issue (one thread):
+//                  tcgen05.mma with A from TMEM and B from shared memory.
 // Every mbarrier wait is bounded; the first wait that runs out sets a shared
 // abort flag, records ALJ_FAULT_TIMEOUT, and every role leaves its loop; the
 // MMA thread waits (bounded) for its last commit before TMEM is released.
@@ -81,12 +86,21 @@ constexpr int kAbsRing = 2;
 constexpr int kTableBytes = 256 * 32 * 8;   // 64 KB
 constexpr int kCodesBytes = kRows * 128;    // 16 KB
 constexpr int kAbsBytes = kRows * kAbsCols * 4;   // 8 KB
-constexpr int kATileBytes = kRows * 128;    // 16 KB (one of Th / Tl)
+constexpr int kACols = 64;                  // TMEM columns per A stage: 32 of Th pairs, 32 of Tl pairs
+constexpr int kARing = 4;                   // A stages in TMEM (columns 0 .. 255)
+constexpr int kDCol0 = kARing * kACols;     // first TMEM column of the accumulators
 constexpr int kMaxSeg = 3;
 constexpr int kSmemMax = 232448;
 constexpr int kMaxARing = 4;                // dequantised A stages
 constexpr int kMaxXRing = 16;               // activation stages
 constexpr int kMaxDBufs = 8;
+// One tcgen05.commit per stage, onto sdone[stage % kSDone]: the A slot, the
+// activation slot and (at a group's last stage) the accumulator of that stage
+// are all released by it.  Each waiter lags the MMA by fewer than kSDone
+// stages (A ring 4, activation ring <= 16, accumulators <= 8 groups), so a
+// slot's parity cannot alias.  (A commit costs the issuing thread a few
+// hundred cycles; three per stage paced the whole pipeline.)
+constexpr int kSDone = 32;
 
 struct alignas(64) GemmSeg {
     CUtensorMap codes;     // packed codes: uint8 [tiles * units * 128][128], box {128, 128}, 128 B swizzle
@@ -106,7 +120,7 @@ struct alignas(64) GemmParams {
     int nseg, M, K, group;
     int row_tiles, tok_tiles, tiles, units_per_tile, abs_slots;
     long long units;
-    int grid, codes_ring, a_ring, x_ring, dbufs;
+    int grid, codes_ring, x_ring, dbufs;
 };
 
 // ------------------------------------------------------------------ PTX
@@ -127,9 +141,6 @@ __device__ __forceinline__ uint2 lds64(uint32_t a) {
     asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
     return v;
 }
-__device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
-    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
-}
 __device__ __forceinline__ float lds_f32(uint32_t a) {
     float v;
     asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
@@ -140,9 +151,6 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
     return r;
 }
-// Generic-proxy shared-memory writes (the dequantised A tiles) become visible
-// to the tensor core (async proxy).
-__device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -158,13 +166,43 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
 __host__ __device__ constexpr uint32_t idesc_f16(int n) {
     return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(kRows >> 4) << 24);
 }
-__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+// One stage: 4 k-steps x (Th, Tl) = 8 MMAs into D, then one commit onto `bar`
+// (arrives when they and every earlier MMA of this thread have completed).
+// `accum` = 0 starts a new accumulation group (first MMA overwrites D).
+__device__ __forceinline__ void tc_stage_mma(uint32_t d, uint32_t ah, uint64_t b, uint32_t idesc, uint32_t accum,
+                                             uint64_t* bar) {
+    const uint32_t al = ah + kACols / 2;
     asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
-            d),
-        "l"(a), "l"(b), "r"(idesc), "r"(accum)
+        "{\n .reg .pred p0, p1;\n"
+        " setp.ne.b32 p0, %12, 0;\n"
+        " setp.eq.b32 p1, %12, %12;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %9, %13, p0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%5], %9, %13, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %10, %13, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%6], %10, %13, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%3], %11, %13, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%7], %11, %13, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%4], %14, %13, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%8], %14, %13, p1;\n"
+        " tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%15];\n"
+        "}\n" ::"r"(d),
+        "r"(ah), "r"(ah + 8), "r"(ah + 16), "r"(ah + 24), "r"(al), "r"(al + 8), "r"(al + 16), "r"(al + 24),
+        "l"(b), "l"(b + 2), "l"(b + 4), "r"(accum), "r"(idesc), "l"(b + 6), "r"(smem_u32(bar))
         : "memory");
 }
+
+// 32 lanes x 32 columns of 32 bit to TMEM (this warp's lane quarter).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // Arrive once on `bar` when every tcgen05.mma this thread issued so far has completed.
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -188,11 +226,25 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 
 // ------------------------------------------------------------------ waits
+// try_wait with a suspend-time hint: the thread sleeps in the barrier unit
+// until the phase completes (or ~0.5 ms pass) instead of spinning, so waiting
+// warps do not take issue slots from the dequant and epilogue warps that share
+// their schedulers.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(500000u)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait that also gives up as soon as another role has (abort flag).
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
-    while (!mbar_try_wait(bar, parity)) {
+    while (!mbar_try_wait_sleep(bar, parity)) {
         if (*abort_flag) return false;
         if (clock64() - t0 > kSpinLimitCycles) {
             record_fault(ALJ_FAULT_TIMEOUT);
@@ -207,6 +259,19 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
     return __all_sync(0xffffffffu, wait_bar(bar, parity, abort_flag));
 }
+
+// Position in a ring of mbarriers: the slot and the parity of the phase its
+// next waiter expects, advanced once per use (no division on the issue path).
+struct Cursor {
+    int slot;
+    uint32_t phase;
+    __device__ __forceinline__ void next(int n) {
+        if (++slot == n) {
+            slot = 0;
+            phase ^= 1u;
+        }
+    }
+};
 
 // ------------------------------------------------------------------ schedule
 __device__ __forceinline__ long long unit_begin(const GemmParams& p, int c) {
@@ -245,39 +310,38 @@ __device__ __forceinline__ Piece make_piece(const GemmParams& p, int t, long lon
 }
 
 // ------------------------------------------------------------------ kernel
+constexpr int kIssuers = 2;                 // MMA-issuing warps (alternate NF4 groups)
+
 template <int MT, int EW>
-__global__ void __launch_bounds__(32 * (7 + 4 * EW), 1) nf4_tc_gemm_kernel(const __grid_constant__ GemmParams p) {
+__global__ void __launch_bounds__(32 * (6 + kIssuers + 4 * EW), 1)
+    nf4_tc_gemm_kernel(const __grid_constant__ GemmParams p) {
     constexpr int NT = MT / EW;                 // tokens per epilogue thread
     constexpr int kEpiWarp0 = 4;
     constexpr int kProdWarp = 4 + 4 * EW;       // codes + absmax stream
     constexpr int kXWarp = kProdWarp + 1;       // activation tiles
-    constexpr int kMmaWarp = kProdWarp + 2;
+    constexpr int kMmaWarp = kProdWarp + 2;     // first issuer; also allocates TMEM
     constexpr int kXBytes = MT * 128;
-    constexpr int kAStageBytes = 2 * kATileBytes;
     constexpr uint32_t kIdesc = idesc_f16(MT);
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int CQ = p.codes_ring;
-    const int SA = p.a_ring;
+    constexpr int SA = kARing;
     const int SX = p.x_ring;
     const int NB = p.dbufs;
     uint8_t* table = smem;
     uint8_t* codes_ring = table + kTableBytes;
     uint8_t* abs_ring = codes_ring + static_cast<size_t>(CQ) * kCodesBytes;
-    uint8_t* a_ring = abs_ring + kAbsRing * kAbsBytes;
-    uint8_t* x_ring = a_ring + static_cast<size_t>(SA) * kAStageBytes;
+    uint8_t* x_ring = abs_ring + kAbsRing * kAbsBytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(x_ring + static_cast<size_t>(SX) * kXBytes);
     uint64_t* codes_full = bars;
     uint64_t* codes_empty = codes_full + kMaxCodesRing;
     uint64_t* abs_full = codes_empty + kMaxCodesRing;
     uint64_t* abs_empty = abs_full + kAbsRing;
     uint64_t* a_full = abs_empty + kAbsRing;
-    uint64_t* a_empty = a_full + kMaxARing;
-    uint64_t* x_full = a_empty + kMaxARing;
-    uint64_t* x_empty = x_full + kMaxXRing;
-    uint64_t* d_full = x_empty + kMaxXRing;
-    uint64_t* d_empty = d_full + kMaxDBufs;
+    uint64_t* x_full = a_full + kMaxARing;
+    uint64_t* sdone = x_full + kMaxXRing;
+    uint64_t* d_empty = sdone + kSDone;
     uint64_t* done_bar = d_empty + kMaxDBufs;
     uint64_t* epi_a = done_bar + 1;             // epilogue warps stored their partials
     uint64_t* epi_b = epi_a + 1;                // the tile counter was taken (last_flag set)
@@ -289,9 +353,10 @@ __global__ void __launch_bounds__(32 * (7 + 4 * EW), 1) nf4_tc_gemm_kernel(const
     const int lane = threadIdx.x & 31;
 
     // Byte -> (Th pair, Tl pair) table: entry b, copy l at 256 b + 8 l.  The
-    // 16 (Th, Tl) code pairs go to a scratch word array first (in the A ring,
-    // not yet in use), then every thread writes two copies per 16-byte store.
-    uint32_t* pairs = reinterpret_cast<uint32_t*>(a_ring);
+    // 16 (Th, Tl) code pairs go to a scratch word array first (in the
+    // activation ring, not yet in use), then every thread writes two copies
+    // per 16-byte store.
+    uint32_t* pairs = reinterpret_cast<uint32_t*>(x_ring);
     if (threadIdx.x < 16) {
         const float t = nf4_value(threadIdx.x);
         const __half h = __float2half_rn(t);
@@ -316,19 +381,13 @@ __global__ void __launch_bounds__(32 * (7 + 4 * EW), 1) nf4_tc_gemm_kernel(const
             mbar_init(&abs_full[i], 1);
             mbar_init(&abs_empty[i], 4 * EW);
         }
-        for (int i = 0; i < kMaxARing; ++i) {
-            mbar_init(&a_full[i], 4);
-            mbar_init(&a_empty[i], 1);
-        }
-        for (int i = 0; i < kMaxXRing; ++i) {
-            mbar_init(&x_full[i], 1);
-            mbar_init(&x_empty[i], 1);
-        }
+        for (int i = 0; i < kMaxARing; ++i) mbar_init(&a_full[i], 4);
+        for (int i = 0; i < kMaxXRing; ++i) mbar_init(&x_full[i], 1);
+        for (int i = 0; i < kSDone; ++i) mbar_init(&sdone[i], 1);
         for (int i = 0; i < kMaxDBufs; ++i) {
-            mbar_init(&d_full[i], 1);
             mbar_init(&d_empty[i], 4 * EW);
         }
-        mbar_init(done_bar, 1);
+        mbar_init(done_bar, kIssuers);
         mbar_init(epi_a, 4 * EW);
         mbar_init(epi_b, 1);
         *abort_flag = 0;
@@ -353,43 +412,49 @@ __global__ void __launch_bounds__(32 * (7 + 4 * EW), 1) nf4_tc_gemm_kernel(const
 
     if (warp < 4) {
         // ---------------------------------------------------------- dequant
-        const int r = threadIdx.x;              // tile row
+        const int r = threadIdx.x;              // tile row = TMEM lane
         const uint32_t lane8 = static_cast<uint32_t>(lane) * 8u;
         const uint32_t tab = smem_u32(table);
         const uint32_t swz = static_cast<uint32_t>(r & 7);
-        int ci = 0, si = 0;
+        const uint32_t ta_row = tmem_base + (static_cast<uint32_t>(32 * warp) << 16);   // lanes of this warp
+        Cursor cc{0, 0u}, ac{0, 0u}, rel{0, 0u};
+        int si = 0;
         bool ok = u1 > u0;
         for (int t = t_first; ok && t <= t_last; ++t) {
             const Piece pc = make_piece(p, t, u0, u1);
-            for (int c = pc.c0; ok && c < pc.c1; ++c, ++ci) {
-                const int cs = ci % CQ;
-                if (!warp_wait(&codes_full[cs], (ci / CQ) & 1, abort_flag)) { ok = false; break; }
-                const uint32_t crow = smem_u32(codes_ring + static_cast<size_t>(cs) * kCodesBytes) + r * 128;
+            for (int c = pc.c0; ok && c < pc.c1; ++c) {
+                if (!warp_wait(&codes_full[cc.slot], cc.phase, abort_flag)) { ok = false; break; }
+                const uint32_t crow = smem_u32(codes_ring + static_cast<size_t>(cc.slot) * kCodesBytes) + r * 128;
                 for (int st = 0; st < kUnitStages; ++st, ++si) {
-                    const int ss = si % SA;
-                    if (!warp_wait(&a_empty[ss], ((si / SA) & 1) ^ 1, abort_flag)) { ok = false; break; }
-                    const uint32_t ahi = smem_u32(a_ring + static_cast<size_t>(ss) * kAStageBytes) + r * 128;
-                    const uint32_t alo = ahi + kATileBytes;
+                    if (si >= SA) {   // the MMAs of stage si - SA have released this A slot
+                        if (!warp_wait(&sdone[rel.slot], rel.phase, abort_flag)) { ok = false; break; }
+                        rel.next(kSDone);
+                    }
+                    tc_fence_after();
                     const uint4 w0 = lds128(crow + ((static_cast<uint32_t>(2 * st) ^ swz) << 4));
                     const uint4 w1 = lds128(crow + ((static_cast<uint32_t>(2 * st + 1) ^ swz) << 4));
                     const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                    uint32_t hi[32], lo[32];
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
-                        const uint32_t w = words[j];
-                        const uint2 e0 = lds64(tab + prmt(w, lane8, 0x5504u));
-                        const uint2 e1 = lds64(tab + prmt(w, lane8, 0x5514u));
-                        const uint2 e2 = lds64(tab + prmt(w, lane8, 0x5524u));
-                        const uint2 e3 = lds64(tab + prmt(w, lane8, 0x5534u));
-                        const uint32_t off = (static_cast<uint32_t>(j) ^ swz) << 4;
-                        sts128(ahi + off, e0.x, e1.x, e2.x, e3.x);
-                        sts128(alo + off, e0.y, e1.y, e2.y, e3.y);
+#pragma unroll
+                        for (int b = 0; b < 4; ++b) {
+                            const uint2 e = lds64(tab + prmt(words[j], lane8, 0x5504u | (b << 4)));
+                            hi[4 * j + b] = e.x;
+                            lo[4 * j + b] = e.y;
+                        }
                     }
-                    fence_async_shared();
+                    tmem_st32(ta_row + ac.slot * kACols, hi);
+                    tmem_st32(ta_row + ac.slot * kACols + kACols / 2, lo);
+                    tmem_wait_st();
+                    tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&a_full[ss]);
+                    if (lane == 0) mbar_arrive(&a_full[ac.slot]);
+                    ac.next(SA);
                 }
                 __syncwarp();
-                if (ok && lane == 0) mbar_arrive(&codes_empty[cs]);
+                if (ok && lane == 0) mbar_arrive(&codes_empty[cc.slot]);
+                cc.next(CQ);
             }
         }
     } else if (warp < kProdWarp) {
@@ -398,7 +463,8 @@ __global__ void __launch_bounds__(32 * (7 + 4 * EW), 1) nf4_tc_gemm_kernel(const
         const int eh = (warp - kEpiWarp0) >> 2;
         const int r = 32 * q + lane;
         const uint32_t tq = tmem_base + (static_cast<uint32_t>(32 * q) << 16);
-        int ai = 0, di = 0, ep = 0;
+        Cursor abc{0, 0u}, dc{0, 0u}, sdc{gpu - 1, 0u};
+        int ep = 0;
         bool ok = u1 > u0;
         float acc[NT];
         for (int t = t_first; ok && t <= t_last; ++t) {
@@ -408,26 +474,24 @@ __global__ void __launch_bounds__(32 * (7 + 4 * EW), 1) nf4_tc_gemm_kernel(const
             for (int j = 0; j < NT; ++j) acc[j] = 0.0f;
             int as = -1;
             for (int c = pc.c0; ok && c < pc.c1; ++c) {
-                const int kb = c * kUnitK;
-                const int col0 = kb / p.group;
-                if (c == pc.c0 || col0 % kAbsCols == 0) {
+                const int col0 = c * (kUnitK / p.group);
+                if (c == pc.c0 || (col0 & (kAbsCols - 1)) == 0) {
                     if (as >= 0) {
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&abs_empty[as]);
                     }
-                    as = ai % kAbsRing;
-                    if (!warp_wait(&abs_full[as], (ai / kAbsRing) & 1, abort_flag)) { ok = false; as = -1; break; }
-                    ++ai;
+                    as = abc.slot;
+                    if (!warp_wait(&abs_full[as], abc.phase, abort_flag)) { ok = false; as = -1; break; }
+                    abc.next(kAbsRing);
                 }
                 const uint32_t arow = smem_u32(abs_ring + as * kAbsBytes) + r * 64;
                 const uint32_t aswz = static_cast<uint32_t>((r >> 1) & 3);
-                for (int gi = 0; gi < kUnitK / p.group; ++gi, ++di) {
-                    const int ds = di % NB;
-                    if (!warp_wait(&d_full[ds], (di / NB) & 1, abort_flag)) { ok = false; break; }
+                for (int gi = 0; gi < kUnitK / p.group; ++gi) {
+                    if (!warp_wait(&sdone[sdc.slot], sdc.phase, abort_flag)) { ok = false; break; }
                     tc_fence_after();
-                    const int col = (col0 + gi) % kAbsCols;
+                    const int col = (col0 + gi) & (kAbsCols - 1);
                     const float s = lds_f32(arow + (((static_cast<uint32_t>(col >> 2) ^ aswz) << 4) | ((col & 3) << 2)));
-                    const uint32_t ta = tq + static_cast<uint32_t>(ds * MT + eh * NT);
+                    const uint32_t ta = tq + static_cast<uint32_t>(kDCol0 + dc.slot * MT + eh * NT);
 #pragma unroll
                     for (int h = 0; h < NT / 16; ++h) {
                         uint32_t v[16];
@@ -437,7 +501,9 @@ __global__ void __launch_bounds__(32 * (7 + 4 * EW), 1) nf4_tc_gemm_kernel(const
                     }
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&d_empty[ds]);
+                    if (lane == 0) mbar_arrive(&d_empty[dc.slot]);
+                    dc.next(NB);
+                    for (int k = 0; k < gpu; ++k) sdc.next(kSDone);
                 }
             }
             if (as >= 0) {
@@ -464,6 +530,7 @@ __global__ void __launch_bounds__(32 * (7 + 4 * EW), 1) nf4_tc_gemm_kernel(const
                         *last_flag = 0;
                         if (all) {
                             const unsigned prev = atomicAdd(&p.counters[t], 1u);
+                            __threadfence();
                             *last_flag = prev == static_cast<unsigned>(cl - cf) ? 1 : 0;
                         }
                         mbar_arrive(epi_b);
@@ -501,81 +568,81 @@ __global__ void __launch_bounds__(32 * (7 + 4 * EW), 1) nf4_tc_gemm_kernel(const
     } else if (warp == kProdWarp) {
         // ---------------------------------------------------------- codes + absmax stream
         if (lane == 0) {
-            int ci = 0, ai = 0;
+            Cursor cc{0, 0u}, abc{0, 0u};
             bool ok = u1 > u0;
             for (int t = t_first; ok && t <= t_last; ++t) {
                 const Piece pc = make_piece(p, t, u0, u1);
                 const GemmSeg& sg = p.seg[pc.seg];
+                const int rt = pc.row0 / kRows;
                 for (int c = pc.c0; ok && c < pc.c1; ++c) {
-                    const int kb = c * kUnitK;
-                    const int col0 = kb / p.group;
-                    if (c == pc.c0 || col0 % kAbsCols == 0) {
-                        const int as = ai % kAbsRing;
-                        if (!wait_bar(&abs_empty[as], ((ai / kAbsRing) & 1) ^ 1, abort_flag)) { ok = false; break; }
-                        mbar_arrive_expect_tx(&abs_full[as], kAbsBytes);
-                        tma_load_2d(smem_u32(abs_ring + as * kAbsBytes), &sg.absmax, 0,
-                                    ((pc.row0 / kRows) * p.abs_slots + col0 / kAbsCols) * kRows, &abs_full[as]);
-                        ++ai;
+                    const int col0 = c * (kUnitK / p.group);
+                    if (c == pc.c0 || (col0 & (kAbsCols - 1)) == 0) {
+                        if (!wait_bar(&abs_empty[abc.slot], abc.phase ^ 1u, abort_flag)) { ok = false; break; }
+                        mbar_arrive_expect_tx(&abs_full[abc.slot], kAbsBytes);
+                        tma_load_2d(smem_u32(abs_ring + abc.slot * kAbsBytes), &sg.absmax, 0,
+                                    (rt * p.abs_slots + col0 / kAbsCols) * kRows, &abs_full[abc.slot]);
+                        abc.next(kAbsRing);
                     }
-                    const int cs = ci % CQ;
-                    if (!wait_bar(&codes_empty[cs], ((ci / CQ) & 1) ^ 1, abort_flag)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&codes_full[cs], kCodesBytes);
-                    tma_load_2d(smem_u32(codes_ring + static_cast<size_t>(cs) * kCodesBytes), &sg.codes, 0,
-                                ((pc.row0 / kRows) * p.units_per_tile + c) * kRows, &codes_full[cs]);
-                    ++ci;
+                    if (!wait_bar(&codes_empty[cc.slot], cc.phase ^ 1u, abort_flag)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&codes_full[cc.slot], kCodesBytes);
+                    tma_load_2d(smem_u32(codes_ring + static_cast<size_t>(cc.slot) * kCodesBytes), &sg.codes, 0,
+                                (rt * p.units_per_tile + c) * kRows, &codes_full[cc.slot]);
+                    cc.next(CQ);
                 }
             }
         }
     } else if (warp == kXWarp) {
         // ---------------------------------------------------------- activation tiles
         if (lane == 0) {
+            Cursor xc{0, 0u}, rel{0, 0u};
             int xi = 0;
             bool ok = u1 > u0;
             for (int t = t_first; ok && t <= t_last; ++t) {
                 const Piece pc = make_piece(p, t, u0, u1);
                 for (int c = pc.c0; ok && c < pc.c1; ++c) {
                     for (int st = 0; st < kUnitStages; ++st, ++xi) {
-                        const int xs = xi % SX;
-                        if (!wait_bar(&x_empty[xs], ((xi / SX) & 1) ^ 1, abort_flag)) { ok = false; break; }
-                        mbar_arrive_expect_tx(&x_full[xs], kXBytes);
-                        tma_load_2d(smem_u32(x_ring + static_cast<size_t>(xs) * kXBytes), &p.xmap,
-                                    c * kUnitK + st * kStageK, pc.tok0 * MT, &x_full[xs]);
+                        if (xi >= SX) {   // the MMAs of stage xi - SX have released this slot
+                            if (!wait_bar(&sdone[rel.slot], rel.phase, abort_flag)) { ok = false; break; }
+                            rel.next(kSDone);
+                        }
+                        mbar_arrive_expect_tx(&x_full[xc.slot], kXBytes);
+                        tma_load_2d(smem_u32(x_ring + static_cast<size_t>(xc.slot) * kXBytes), &p.xmap,
+                                    c * kUnitK + st * kStageK, pc.tok0 * MT, &x_full[xc.slot]);
+                        xc.next(SX);
                     }
                 }
             }
         }
     } else {
         // ---------------------------------------------------------- MMA issue
+        // Issuer k takes the NF4 groups whose CTA-local index is k mod
+        // kIssuers; it walks every stage to keep its ring cursors in step.
+        const int issuer = warp - kMmaWarp;
         if (lane == 0) {
-            int si = 0, di = 0;
+            Cursor dc{0, 0u}, xc{0, 0u}, ac{0, 0u}, sd{0, 0u};
+            int g = 0, grp = 0;
             bool ok = u1 > u0;
             for (int t = t_first; ok && t <= t_last; ++t) {
                 const Piece pc = make_piece(p, t, u0, u1);
-                for (int c = pc.c0; ok && c < pc.c1; ++c) {
-                    for (int st = 0; st < kUnitStages; ++st, ++si) {
-                        const int g = st % gpu;       // stage within its group (pieces start on group starts)
-                        const int ds = di % NB;
-                        if (g == 0 && !wait_bar(&d_empty[ds], ((di / NB) & 1) ^ 1, abort_flag)) { ok = false; break; }
-                        const int sa = si % SA;
-                        const int sx = si % SX;
-                        if (!wait_bar(&x_full[sx], (si / SX) & 1, abort_flag) ||
-                            !wait_bar(&a_full[sa], (si / SA) & 1, abort_flag)) { ok = false; break; }
+                const int nst = (pc.c1 - pc.c0) * kUnitStages;
+                for (int i = 0; i < nst; ++i) {
+                    if (grp == issuer) {
+                        if (g == 0 && !wait_bar(&d_empty[dc.slot], dc.phase ^ 1u, abort_flag)) { ok = false; break; }
+                        if (!wait_bar(&x_full[xc.slot], xc.phase, abort_flag) ||
+                            !wait_bar(&a_full[ac.slot], ac.phase, abort_flag)) { ok = false; break; }
                         tc_fence_after();
-                        const uint32_t abase = smem_u32(a_ring + static_cast<size_t>(sa) * kAStageBytes);
-                        const uint64_t ah = sdesc(abase), al = sdesc(abase + kATileBytes),
-                                       bx = sdesc(smem_u32(x_ring + static_cast<size_t>(sx) * kXBytes));
-                        const uint32_t d = tmem_base + static_cast<uint32_t>(ds * MT);
-#pragma unroll
-                        for (int kk = 0; kk < kStageK / 16; ++kk) {
-                            tc_mma(d, ah + 2 * kk, bx + 2 * kk, kIdesc, (g > 0 || kk > 0) ? 1u : 0u);
-                            tc_mma(d, al + 2 * kk, bx + 2 * kk, kIdesc, 1u);
-                        }
-                        tc_commit(&a_empty[sa]);
-                        tc_commit(&x_empty[sx]);
-                        if (g == gpu - 1) {
-                            tc_commit(&d_full[ds]);
-                            ++di;
-                        }
+                        const uint32_t ah = tmem_base + static_cast<uint32_t>(ac.slot * kACols);
+                        const uint64_t bx = sdesc(smem_u32(x_ring + static_cast<size_t>(xc.slot) * kXBytes));
+                        const uint32_t d = tmem_base + static_cast<uint32_t>(kDCol0 + dc.slot * MT);
+                        tc_stage_mma(d, ah, bx, kIdesc, g > 0 ? 1u : 0u, &sdone[sd.slot]);
+                    }
+                    xc.next(SX);
+                    ac.next(SA);
+                    sd.next(kSDone);
+                    if (++g == gpu) {
+                        g = 0;
+                        dc.next(NB);
+                        if (++grp == kIssuers) grp = 0;
                     }
                 }
             }
@@ -703,28 +770,19 @@ WsLayout ws_layout(int M, int K, int tiles, int grid) {
     return w;
 }
 
-// Ring depths: two dequantised A stages, a codes ring of 3 units (2 if the
-// activation ring would otherwise hold fewer than 3 stages), and as deep an
-// activation ring (up to 16 stages) as fits.
+// Ring depths in shared memory: 4 codes units and as deep an activation ring
+// (up to 16 stages) as fits.  The dequantised A stages live in TMEM.
 struct Rings {
-    int codes, a, x;
+    int codes, x;
     size_t smem;
 };
 Rings rings_for(int MT) {
     const size_t fixed = 1024 + kTableBytes + kAbsRing * kAbsBytes + 1024;
     const size_t xb = static_cast<size_t>(MT) * 128;
-    Rings r{0, 2, 0, 0};
-    for (int cq = 3; cq >= 2; --cq) {
-        const size_t used = fixed + static_cast<size_t>(cq) * kCodesBytes + r.a * 2 * kATileBytes;
-        if (used >= static_cast<size_t>(kSmemMax)) continue;
-        const int sx = static_cast<int>(std::min<size_t>(kMaxXRing, (kSmemMax - used) / xb));
-        if (sx >= 3 || cq == 2) {
-            r.codes = cq;
-            r.x = sx;
-            r.smem = used + sx * xb;
-            break;
-        }
-    }
+    Rings r{kMaxCodesRing, 0, 0};
+    const size_t used = fixed + static_cast<size_t>(r.codes) * kCodesBytes;
+    r.x = static_cast<int>(std::min<size_t>(kMaxXRing, (kSmemMax - used) / xb));
+    r.smem = used + r.x * xb;
     return r;
 }
 
@@ -751,7 +809,7 @@ cudaError_t launch_mt(const GemmParams& p, size_t smem, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
         configured[dev & 63] = true;
     }
-    nf4_tc_gemm_kernel<MT, EW><<<p.grid, 32 * (7 + 4 * EW), smem, stream>>>(p);
+    nf4_tc_gemm_kernel<MT, EW><<<p.grid, 32 * (6 + kIssuers + 4 * EW), smem, stream>>>(p);
     return cudaGetLastError();
 }
 
@@ -844,9 +902,8 @@ cudaError_t launch_gemm_nf4(const GemmNf4Args& a, cudaStream_t stream) {
     const Rings rg = rings_for(MT);
     if (rg.x < 2) return cudaErrorNotSupported;
     p.codes_ring = rg.codes;
-    p.a_ring = rg.a;
     p.x_ring = rg.x;
-    p.dbufs = std::min(kMaxDBufs, 512 / MT);
+    p.dbufs = std::min(kMaxDBufs, (512 - kDCol0) / MT);
 
     gemm_x_prep_kernel<<<a.M, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(a.x), a.K, xh,
                                                reinterpret_cast<int*>(ws + w.tokexp), p.counters, p.tiles);

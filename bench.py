@@ -58,6 +58,17 @@ def load_peaks():
     return 6650.0, "fallback"
 
 
+def load_tc_peak():
+    """Dense bf16 tensor peak (TFLOP/s, cuBLAS burst) from MEASURED_PEAKS.json."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        if "bf16_tflops" in d:
+            return float(d["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
 def load_traffic(name):
     p = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(p):
@@ -323,7 +334,7 @@ def capture(torch, stream, record):
 
 def run_extra(args, dev, stream, sh, l2, which=None, reps=200):
     """Secondary configs, each with its own pool > 2 x L2 and device timing.
-    `which` selects a subset of {"nf4", "q8", "attention"} (all if None)."""
+    `which` selects a subset of {"nf4", "q8", "attention", "c5"} (all if None)."""
     import torch
 
     import oracle
@@ -417,7 +428,84 @@ def run_extra(args, dev, stream, sh, l2, which=None, reps=200):
                                                     "us_per_call": round(ms * 1e3, 3), "algorithmic_bytes": alg,
                                                     "launches_per_call": 2}
 
-    for name, fn in (("nf4", nf4_section), ("q8", q8_section), ("attention", attention_section)):
+    def c5_section():
+        # Batched NF4 on the per-GPU tensor-parallel shard (TP 8) of one
+        # Llama-3-70B layer: q 1024x8192, k/v 128x8192, o 1024x8192,
+        # gate/up 3584x8192, down 1024x28672 rows of this GPU; bf16 activations,
+        # M tokens.  M = 1 runs the batch-1 NF4 matvec on the row-major weights,
+        # M > 1 the tcgen05 GEMM on the packed weights (q/k/v and gate/up fused
+        # launches).  Weights: uniform random NF4 codes (the NF4 levels are
+        # equiprobable for normal weights) and absmax ~ |N(0.05, 0.005)|.
+        H, FF, TPW, G = 8192, 28672, 8, 64
+        shp = {"q": (H // TPW, H), "k": (1024 // TPW, H), "v": (1024 // TPW, H), "o": (H // TPW, H),
+               "gate": (FF // TPW, H), "up": (FF // TPW, H), "down": (H // TPW, FF)}
+        nweights = sum(n * k for n, k in shp.values())
+        wbytes = sum(n * k // 2 + n * k // G * 4 for n, k in shp.values())
+        pool5 = max(2, int(np.ceil(2.5 * l2 / wbytes)))
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(5)
+        raw, packed = [], []
+        for _ in range(pool5):
+            lr, lp = {}, {}
+            for name, (n, k) in shp.items():
+                c = torch.randint(0, 256, (n * k // 2,), dtype=torch.uint8, device=dev, generator=gen)
+                a = (0.05 + 0.005 * torch.randn(n * k // G, device=dev, generator=gen)).abs()
+                pk = torch.empty(native.gemm_nf4_packed_size(n, k, G), dtype=torch.uint8, device=dev)
+                torch.cuda.synchronize(dev)
+                native.gemm_nf4_pack(pk.data_ptr(), c.data_ptr(), a.data_ptr(), n, k, G, sh.value)
+                lr[name], lp[name] = (c, a), pk
+            raw.append(lr)
+            packed.append(lp)
+        torch.cuda.synchronize(dev)
+        tc_peak, tc_kind = load_tc_peak()
+        hbm_peak, hbm_kind = load_peaks()
+        res = {}
+        for M in (1, 16, 64, 512):
+            xh = torch.randn(M, H, device=dev).to(torch.bfloat16)
+            xf = torch.randn(M, FF, device=dev).to(torch.bfloat16)
+            ys = {name: torch.empty(M * n, device=dev) for name, (n, _) in shp.items()}
+            if M == 1:
+                xh32, xf32 = xh.float().reshape(-1), xf.float().reshape(-1)
+
+                def layer(i):
+                    lay = raw[i % pool5]
+                    for name, (n, k) in shp.items():
+                        c, a = lay[name]
+                        native.check(L.aljabr_blackwell_matvec_dev(
+                            native.TYPE_NF4, ys[name].data_ptr(), (xf32 if name == "down" else xh32).data_ptr(),
+                            c.data_ptr(), ctypes_ptr(a), k, n, G, None, sh))
+                launches = len(shp)
+            else:
+                wsb = max(native.gemm_nf4_workspace_size(M, H, [shp["q"][0], shp["k"][0], shp["v"][0]]),
+                          native.gemm_nf4_workspace_size(M, H, [shp["gate"][0], shp["up"][0]]),
+                          native.gemm_nf4_workspace_size(M, FF, [shp["down"][0]]))
+                ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+                calls = ((("q", "k", "v"), xh, H), (("o",), xh, H), (("gate", "up"), xh, H), (("down",), xf, FF))
+
+                def layer(i):
+                    lay = packed[i % pool5]
+                    for names, x, k in calls:
+                        native.gemm_nf4_dev([ys[nm].data_ptr() for nm in names], [shp[nm][0] for nm in names],
+                                            [lay[nm].data_ptr() for nm in names], [shp[nm][0] for nm in names],
+                                            x.data_ptr(), M, k, G, ws.data_ptr(), wsb, sh.value)
+                launches = 2 * len(calls)          # activation prep + GEMM per call
+            torch.cuda.synchronize(dev)
+            ms = timed(layer, max(10, reps // 10))
+            flops = 2.0 * M * nweights
+            hbm_floor_us = wbytes / (hbm_peak * 1e3)
+            tc_floor_us = 2.0 * flops / (tc_peak * 1e6)      # two MMAs (Th, Tl) per weight element
+            res[f"M{M}"] = {"us_per_layer_shard": round(ms * 1e3, 2), "TFLOP/s": round(flops / (ms * 1e9), 1),
+                            "weight_GB/s": round(wbytes / (ms * 1e6), 1), "launches": launches,
+                            "floor_us": round(max(hbm_floor_us, tc_floor_us if M > 1 else 0.0), 2),
+                            "bound": "hbm" if M == 1 or hbm_floor_us >= tc_floor_us else "tensor"}
+            del ys
+            torch.cuda.empty_cache()
+        out["c5_nf4_batched_70b_layer_tp8_shard"] = {
+            "per_gpu_weights": nweights, "weight_bytes": wbytes, "pool_layers": pool5,
+            "peaks": {"hbm_GB/s": hbm_peak, "hbm": hbm_kind, "bf16_TFLOP/s": tc_peak, "tensor": tc_kind},
+            "tokens": res}
+
+    for name, fn in (("nf4", nf4_section), ("q8", q8_section), ("attention", attention_section), ("c5", c5_section)):
         if want(name):
             fn()
             torch.cuda.empty_cache()
@@ -609,7 +697,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--no-prefetch", action="store_true", help="no L2 prefetch hints between the headline launches")
-    ap.add_argument("--only", choices=["nf4", "q8", "attention", "decode"],
+    ap.add_argument("--only", choices=["nf4", "q8", "attention", "decode", "c5"],
                     help="run one secondary workload alone (for profiling); prints its dict")
     ap.add_argument("--decode-tokens", type=int, default=32)
     args = ap.parse_args()
