@@ -34,10 +34,11 @@
 // Tiles and schedule.  A tile is 128 weight rows (the MMA's M, TMEM lanes) x
 // MT tokens (the MMA's N: 16, 32, 64 or 128; more tokens use several token
 // tiles).  A unit is one tile x 256 columns of K.  Units are dealt out to one
-// CTA per SM in equal contiguous ranges ("stream-K"): a tile whose K range is
-// split between CTAs is finished by the last of them to arrive, which sums
-// the others' fp32 partials in K order (deterministic; a per-tile counter in
-// the workspace is returned to 0).
+// CTA per SM in equal contiguous ranges ("stream-K").  A piece of a tile whose
+// K range is split between CTAs is written as an fp32 partial; after a grid
+// barrier (cooperative launch, bounded wait) every CTA sums a share of the
+// split tiles' outputs over their pieces in K order (deterministic).  One CTA
+// summing a whole tile's ~18 partials was latency bound at ~15 us.
 //
 // Warp roles (one CTA per SM, up to 227 KB shared memory, all 512 TMEM
 // columns: 4 A stages x 64 columns, then the accumulators):
@@ -90,6 +91,8 @@ constexpr int kACols = 64;                  // TMEM columns per A stage: 32 of T
 constexpr int kARing = 4;                   // A stages in TMEM (columns 0 .. 255)
 constexpr int kDCol0 = kARing * kACols;     // first TMEM column of the accumulators
 constexpr int kMaxSeg = 3;
+constexpr int kMaxSplit = 160;              // >= grid: each CTA boundary splits at most one tile
+constexpr int kMaxPieces = 320;             // >= split tiles + grid
 constexpr int kSmemMax = 232448;
 constexpr int kMaxARing = 4;                // dequantised A stages
 constexpr int kMaxXRing = 16;               // activation stages
@@ -116,11 +119,14 @@ struct alignas(64) GemmParams {
     CUtensorMap xmap;      // fp16 [M][K], box {64, MT}, 128 B swizzle
     const int* tokexp;     // [M]: x' = x * 2^tokexp
     float* partials;       // [2 * grid][MT][128]
-    unsigned int* counters;   // [tiles], 0 before and after
+    unsigned int* gbar;    // grid barrier: one flag per CTA, cleared by gemm_x_prep_kernel
     int nseg, M, K, group;
     int row_tiles, tok_tiles, tiles, units_per_tile, abs_slots;
     long long units;
     int grid, codes_ring, x_ring, dbufs;
+    int nsplit;                                 // tiles whose K range is split between CTAs
+    unsigned short split_tile[kMaxSplit], split_off[kMaxSplit], split_n[kMaxSplit];
+    unsigned short piece_slot[kMaxPieces];      // partial slots of the split tiles' pieces, in K order
 };
 
 // ------------------------------------------------------------------ PTX
@@ -166,28 +172,34 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
 __host__ __device__ constexpr uint32_t idesc_f16(int n) {
     return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(kRows >> 4) << 24);
 }
-// One stage: 4 k-steps x (Th, Tl) = 8 MMAs into D, then one commit onto `bar`
+// One stage: 4 k-steps x (Th, Tl) = 8 MMAs, then one commit onto `bar`
 // (arrives when they and every earlier MMA of this thread have completed).
-// `accum` = 0 starts a new accumulation group (first MMA overwrites D).
-__device__ __forceinline__ void tc_stage_mma(uint32_t d, uint32_t ah, uint64_t b, uint32_t idesc, uint32_t accum,
-                                             uint64_t* bar) {
+// The Th products accumulate in dh and the Tl products in dl: two independent
+// chains of 4, so consecutive MMAs do not wait on each other's accumulator
+// (with dl == dh it is one chain of 8).  `accum` = 0 starts a new group (the
+// first MMA of each chain overwrites it).
+__device__ __forceinline__ void tc_stage_mma(uint32_t dh, uint32_t dl, uint32_t ah, uint64_t b, uint32_t idesc,
+                                             uint32_t accum, uint64_t* bar) {
     const uint32_t al = ah + kACols / 2;
+    const uint32_t accum_l = (dl == dh) ? 1u : accum;
     asm volatile(
-        "{\n .reg .pred p0, p1;\n"
+        "{\n .reg .pred p0, p1, p2;\n"
         " setp.ne.b32 p0, %12, 0;\n"
+        " setp.ne.b32 p2, %17, 0;\n"
         " setp.eq.b32 p1, %12, %12;\n"
         " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %9, %13, p0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%5], %9, %13, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%16], [%5], %9, %13, p2;\n"
         " tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %10, %13, p1;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%6], %10, %13, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%16], [%6], %10, %13, p1;\n"
         " tcgen05.mma.cta_group::1.kind::f16 [%0], [%3], %11, %13, p1;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%7], %11, %13, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%16], [%7], %11, %13, p1;\n"
         " tcgen05.mma.cta_group::1.kind::f16 [%0], [%4], %14, %13, p1;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%8], %14, %13, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%16], [%8], %14, %13, p1;\n"
         " tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%15];\n"
-        "}\n" ::"r"(d),
+        "}\n" ::"r"(dh),
         "r"(ah), "r"(ah + 8), "r"(ah + 16), "r"(ah + 24), "r"(al), "r"(al + 8), "r"(al + 16), "r"(al + 24),
-        "l"(b), "l"(b + 2), "l"(b + 4), "r"(accum), "r"(idesc), "l"(b + 6), "r"(smem_u32(bar))
+        "l"(b), "l"(b + 2), "l"(b + 4), "r"(accum), "r"(idesc), "l"(b + 6), "r"(smem_u32(bar)), "r"(dl),
+        "r"(accum_l)
         : "memory");
 }
 
@@ -255,6 +267,15 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
     return true;
 }
 
+__device__ __forceinline__ void st_release_gpu(unsigned int* p, unsigned int v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // The same wait by every lane of a warp, with one verdict for all of them.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
     return __all_sync(0xffffffffu, wait_bar(bar, parity, abort_flag));
@@ -309,13 +330,97 @@ __device__ __forceinline__ Piece make_piece(const GemmParams& p, int t, long lon
     return pc;
 }
 
+// Sum the split tiles' partials (pieces in K order) into y, a share per thread
+// of the whole grid.  Out of line, so that its registers do not add to the
+// pipeline roles'.
+// Work item = 4 consecutive rows of one token of one split tile (a float4 of
+// every piece's partial).  Q items per iteration and all their loads (B
+// pieces at a time) in flight before the in-order sums, so a thread waits one
+// L2 round trip per batch, not one per piece.
+template <int Q, int B>
+__device__ __forceinline__ void reduce_items(const GemmParams& p, int MT) {
+    const int vpt = MT * kRows / 4;
+    const long long total = static_cast<long long>(p.nsplit) * vpt;
+    const long long nthr = static_cast<long long>(gridDim.x) * blockDim.x;
+    const float4* part4 = reinterpret_cast<const float4*>(p.partials);
+    for (long long e0 = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; e0 < total; e0 += Q * nthr) {
+        int np[Q], off[Q], within[Q], item[Q];
+#pragma unroll
+        for (int q = 0; q < Q; ++q) {
+            const long long e = e0 + q * nthr;
+            const bool live = e < total;
+            item[q] = live ? static_cast<int>(e / vpt) : -1;
+            within[q] = live ? static_cast<int>(e - static_cast<long long>(item[q]) * vpt) : 0;
+            np[q] = live ? p.split_n[item[q]] : 0;
+            off[q] = live ? p.split_off[item[q]] : 0;
+        }
+        float4 acc[Q];
+        int npm = 0;
+#pragma unroll
+        for (int q = 0; q < Q; ++q) {
+            acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+            npm = np[q] > npm ? np[q] : npm;
+        }
+        for (int k0 = 0; k0 < npm; k0 += B) {
+            float4 a[Q][B];
+#pragma unroll
+            for (int q = 0; q < Q; ++q)
+#pragma unroll
+                for (int k = 0; k < B; ++k)
+                    a[q][k] = k0 + k < np[q]
+                                  ? __ldcg(part4 + static_cast<size_t>(p.piece_slot[off[q] + k0 + k]) * vpt + within[q])
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int q = 0; q < Q; ++q)
+#pragma unroll
+                for (int k = 0; k < B; ++k) {
+                    acc[q].x += a[q][k].x;
+                    acc[q].y += a[q][k].y;
+                    acc[q].z += a[q][k].z;
+                    acc[q].w += a[q][k].w;
+                }
+        }
+#pragma unroll
+        for (int q = 0; q < Q; ++q) {
+            if (item[q] < 0) continue;
+            const int m = within[q] * 4 / kRows;            // token within the tile
+            const int rr = within[q] * 4 - m * kRows;       // first of the 4 rows
+            const Piece pc = make_piece(p, p.split_tile[item[q]], 0, p.units);
+            const GemmSeg& sg = p.seg[pc.seg];
+            const int tok = pc.tok0 * MT + m;
+            if (tok >= p.M) continue;
+            const float sc = __int_as_float((127 - __ldg(p.tokexp + tok)) << 23);
+            float* yr = sg.y + static_cast<size_t>(tok) * sg.ldy + pc.row0 + rr;
+            const float v[4] = {acc[q].x, acc[q].y, acc[q].z, acc[q].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (pc.row0 + rr + j < sg.rows) yr[j] = v[j] * sc;
+        }
+    }
+}
+
+// Sum the split tiles' partials into y, a share per thread of the whole grid.
+// Out of line, so that its registers do not add to the pipeline roles'.
+__device__ __noinline__ void reduce_split_tiles(const GemmParams& p, int MT) {
+    const long long items = static_cast<long long>(p.nsplit) * (MT * kRows / 4);
+    if (items <= static_cast<long long>(gridDim.x) * blockDim.x)
+        reduce_items<1, 16>(p, MT);       // few items, many pieces each (small matrices)
+    else
+        reduce_items<2, 8>(p, MT);
+}
+
 // ------------------------------------------------------------------ kernel
-constexpr int kIssuers = 2;                 // MMA-issuing warps (alternate NF4 groups)
+// MMA-issuing warps (round-robin over NF4 groups): the tensor pipe takes a
+// 128-row MMA every ~64 cycles whatever N is, and one thread's issue path
+// (waits, address set-up, 8 MMAs, commit) does not keep it busy.
+__host__ __device__ constexpr int issuers_for(int EW) { return EW == 1 ? 4 : 2; }
 
 template <int MT, int EW>
-__global__ void __launch_bounds__(32 * (6 + kIssuers + 4 * EW), 1)
+__global__ void __launch_bounds__(32 * (6 + issuers_for(EW) + 4 * EW), 1)
     nf4_tc_gemm_kernel(const __grid_constant__ GemmParams p) {
+    constexpr int kIssuers = issuers_for(EW);
     constexpr int NT = MT / EW;                 // tokens per epilogue thread
+    constexpr int CH = MT <= 64 ? 2 : 1;        // accumulator chains per group (Th, Tl)
     constexpr int kEpiWarp0 = 4;
     constexpr int kProdWarp = 4 + 4 * EW;       // codes + absmax stream
     constexpr int kXWarp = kProdWarp + 1;       // activation tiles
@@ -343,11 +448,8 @@ __global__ void __launch_bounds__(32 * (6 + kIssuers + 4 * EW), 1)
     uint64_t* sdone = x_full + kMaxXRing;
     uint64_t* d_empty = sdone + kSDone;
     uint64_t* done_bar = d_empty + kMaxDBufs;
-    uint64_t* epi_a = done_bar + 1;             // epilogue warps stored their partials
-    uint64_t* epi_b = epi_a + 1;                // the tile counter was taken (last_flag set)
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(epi_b + 1);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_b + 1) + 1;
-    int* last_flag = reinterpret_cast<int*>(epi_b + 1) + 2;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(done_bar + 1);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1) + 1;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -388,8 +490,6 @@ __global__ void __launch_bounds__(32 * (6 + kIssuers + 4 * EW), 1)
             mbar_init(&d_empty[i], 4 * EW);
         }
         mbar_init(done_bar, kIssuers);
-        mbar_init(epi_a, 4 * EW);
-        mbar_init(epi_b, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -464,7 +564,6 @@ __global__ void __launch_bounds__(32 * (6 + kIssuers + 4 * EW), 1)
         const int r = 32 * q + lane;
         const uint32_t tq = tmem_base + (static_cast<uint32_t>(32 * q) << 16);
         Cursor abc{0, 0u}, dc{0, 0u}, sdc{gpu - 1, 0u};
-        int ep = 0;
         bool ok = u1 > u0;
         float acc[NT];
         for (int t = t_first; ok && t <= t_last; ++t) {
@@ -491,13 +590,23 @@ __global__ void __launch_bounds__(32 * (6 + kIssuers + 4 * EW), 1)
                     tc_fence_after();
                     const int col = (col0 + gi) & (kAbsCols - 1);
                     const float s = lds_f32(arow + (((static_cast<uint32_t>(col >> 2) ^ aswz) << 4) | ((col & 3) << 2)));
-                    const uint32_t ta = tq + static_cast<uint32_t>(kDCol0 + dc.slot * MT + eh * NT);
+                    const uint32_t ta = tq + static_cast<uint32_t>(kDCol0 + dc.slot * CH * MT + eh * NT);
 #pragma unroll
                     for (int h = 0; h < NT / 16; ++h) {
                         uint32_t v[16];
                         tmem_ld16(ta + 16 * h, v);
+                        if constexpr (CH == 2) {
+                            uint32_t w[16];
+                            tmem_ld16(ta + MT + 16 * h, w);
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) acc[16 * h + j] = fmaf(s, __uint_as_float(v[j]), acc[16 * h + j]);
+                            for (int j = 0; j < 16; ++j)
+                                acc[16 * h + j] =
+                                    fmaf(s, __uint_as_float(v[j]) + __uint_as_float(w[j]), acc[16 * h + j]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                acc[16 * h + j] = fmaf(s, __uint_as_float(v[j]), acc[16 * h + j]);
+                        }
                     }
                     tc_fence_before();
                     __syncwarp();
@@ -511,50 +620,17 @@ __global__ void __launch_bounds__(32 * (6 + kIssuers + 4 * EW), 1)
                 if (lane == 0) mbar_arrive(&abs_empty[as]);
             }
             if (!ok) break;
-            // ---- write-out
+            // ---- write-out: a whole tile goes to y; a piece of a split tile
+            // to its partial slot (summed after the grid barrier below).
             const int n = pc.row0 + r;
             const int m0 = pc.tok0 * MT + eh * NT;
             const int cf = cta_of(p, static_cast<long long>(t) * p.units_per_tile);
             const int cl = cta_of(p, static_cast<long long>(t + 1) * p.units_per_tile - 1);
-            bool write = cf == cl;
-            if (!write) {
+            if (cf != cl) {
                 float* part = p.partials + static_cast<size_t>(slot_of(p, blockIdx.x, t)) * (MT * kRows);
 #pragma unroll
                 for (int j = 0; j < NT; ++j) part[(eh * NT + j) * kRows + r] = acc[j];
-                __threadfence();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(epi_a);
-                if (warp == kEpiWarp0) {
-                    const bool all = warp_wait(epi_a, ep & 1, abort_flag);
-                    if (lane == 0) {
-                        *last_flag = 0;
-                        if (all) {
-                            const unsigned prev = atomicAdd(&p.counters[t], 1u);
-                            __threadfence();
-                            *last_flag = prev == static_cast<unsigned>(cl - cf) ? 1 : 0;
-                        }
-                        mbar_arrive(epi_b);
-                    }
-                    __syncwarp();
-                }
-                const bool got = warp_wait(epi_b, ep & 1, abort_flag);
-                ++ep;
-                if (!got) { ok = false; break; }
-                write = *reinterpret_cast<volatile int*>(last_flag) != 0;
-                if (write) {
-                    __threadfence();
-#pragma unroll
-                    for (int j = 0; j < NT; ++j) acc[j] = 0.0f;
-                    for (int cc = cf; cc <= cl; ++cc) {
-                        const float* pp =
-                            p.partials + static_cast<size_t>(slot_of(p, cc, t)) * (MT * kRows) + eh * NT * kRows + r;
-#pragma unroll
-                        for (int j = 0; j < NT; ++j) acc[j] += __ldcg(pp + j * kRows);
-                    }
-                    if (threadIdx.x == kEpiWarp0 * 32) p.counters[t] = 0u;
-                }
-            }
-            if (write && n < sg.rows) {
+            } else if (n < sg.rows) {
 #pragma unroll
                 for (int j = 0; j < NT; ++j) {
                     const int m = m0 + j;
@@ -633,8 +709,8 @@ __global__ void __launch_bounds__(32 * (6 + kIssuers + 4 * EW), 1)
                         tc_fence_after();
                         const uint32_t ah = tmem_base + static_cast<uint32_t>(ac.slot * kACols);
                         const uint64_t bx = sdesc(smem_u32(x_ring + static_cast<size_t>(xc.slot) * kXBytes));
-                        const uint32_t d = tmem_base + static_cast<uint32_t>(kDCol0 + dc.slot * MT);
-                        tc_stage_mma(d, ah, bx, kIdesc, g > 0 ? 1u : 0u, &sdone[sd.slot]);
+                        const uint32_t d = tmem_base + static_cast<uint32_t>(kDCol0 + dc.slot * CH * MT);
+                        tc_stage_mma(d, d + (CH - 1) * MT, ah, bx, kIdesc, g > 0 ? 1u : 0u, &sdone[sd.slot]);
                     }
                     xc.next(SX);
                     ac.next(SA);
@@ -659,11 +735,36 @@ __global__ void __launch_bounds__(32 * (6 + kIssuers + 4 * EW), 1)
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(512) : "memory");
     }
+    if (p.nsplit == 0) return;
+
+    // ---- split tiles: every CTA sums a share of their outputs over the
+    // pieces in K order (deterministic), after a grid barrier.  The launch is
+    // cooperative, so all CTAs are resident; the wait is bounded.
+    // Grid barrier without a contended atomic: each CTA publishes its own flag
+    // (cleared to 0 by gemm_x_prep_kernel), then thread j polls CTA j's flag.
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        st_release_gpu(p.gbar + blockIdx.x, 1u);
+    }
+    if (threadIdx.x < gridDim.x) {
+        const long long t0 = clock64();
+        while (ld_acquire_gpu(p.gbar + threadIdx.x) == 0u) {
+            if (clock64() - t0 > kSpinLimitCycles) {
+                record_fault(ALJ_FAULT_TIMEOUT);
+                *abort_flag = 1;
+                break;
+            }
+        }
+    }
+    __syncthreads();
+    if (*abort_flag) return;
+    reduce_split_tiles(p, MT);
 }
 
 // bf16 activations -> fp16 x * 2^f (per token row), f = 15 - e with
 // max|x| = m * 2^e, m in [0.5, 1): max|x'| in [2^14, 2^15).  Block 0 also
-// clears the stream-K tile counters.
+// clears the GEMM's grid-barrier flags.
 __global__ void gemm_x_prep_kernel(const __nv_bfloat16* __restrict__ x, int K, __half* __restrict__ xh,
                                    int* __restrict__ tokexp, unsigned int* __restrict__ counters, int ncounters) {
     const int m = blockIdx.x;
@@ -757,15 +858,15 @@ int token_tile_for(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct WsLayout {
-    size_t xh, tokexp, counters, partials, total;
+    size_t xh, tokexp, gbar, partials, total;
 };
 WsLayout ws_layout(int M, int K, int tiles, int grid) {
     const int MT = token_tile_for(M);
     WsLayout w;
     w.xh = 0;
     w.tokexp = align_up(w.xh + static_cast<size_t>(M) * K * 2, 256);
-    w.counters = align_up(w.tokexp + static_cast<size_t>(M) * 4, 256);
-    w.partials = align_up(w.counters + static_cast<size_t>(tiles) * 4, 256);
+    w.gbar = align_up(w.tokexp + static_cast<size_t>(M) * 4, 256);
+    w.partials = align_up(w.gbar + static_cast<size_t>(kMaxSplit) * 4, 256);
     w.total = align_up(w.partials + static_cast<size_t>(2) * grid * MT * kRows * 4, 256);
     return w;
 }
@@ -809,8 +910,19 @@ cudaError_t launch_mt(const GemmParams& p, size_t smem, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
         configured[dev & 63] = true;
     }
-    nf4_tc_gemm_kernel<MT, EW><<<p.grid, 32 * (6 + kIssuers + 4 * EW), smem, stream>>>(p);
-    return cudaGetLastError();
+    // Cooperative when split tiles need the grid barrier (all CTAs resident:
+    // one per SM by shared memory, grid <= SM count).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.grid);
+    cfg.blockDim = dim3(32 * (6 + issuers_for(EW) + 4 * EW));
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = p.nsplit > 0 ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, nf4_tc_gemm_kernel<MT, EW>, p);
 }
 
 }  // namespace
@@ -888,14 +1000,36 @@ cudaError_t launch_gemm_nf4(const GemmNf4Args& a, cudaStream_t stream) {
     p.tiles = rt * p.tok_tiles;
     p.units_per_tile = a.K / kUnitK;
     p.units = static_cast<long long>(p.tiles) * p.units_per_tile;
-    p.grid = static_cast<int>(std::min<long long>(sm_count_for_current_device(), p.units));
+    p.grid = static_cast<int>(std::min<long long>(std::min(sm_count_for_current_device(), kMaxSplit), p.units));
+    // Tiles whose K range is split between CTAs (summed after the grid barrier).
+    auto ub = [&](int c) { return static_cast<long long>(c) * p.units / p.grid; };
+    auto cta_of_h = [&](long long u) {
+        int c = static_cast<int>(u * p.grid / p.units);
+        while (c + 1 < p.grid && ub(c + 1) <= u) ++c;
+        while (c > 0 && ub(c) > u) --c;
+        return c;
+    };
+    p.nsplit = 0;
+    int npieces = 0;
+    for (int t = 0; t < p.tiles; ++t) {
+        const int cf = cta_of_h(static_cast<long long>(t) * p.units_per_tile);
+        const int cl = cta_of_h(static_cast<long long>(t + 1) * p.units_per_tile - 1);
+        if (cf == cl) continue;
+        if (p.nsplit >= kMaxSplit || t > 65535 || npieces + (cl - cf + 1) > kMaxPieces) return cudaErrorNotSupported;
+        p.split_tile[p.nsplit] = static_cast<unsigned short>(t);
+        p.split_off[p.nsplit] = static_cast<unsigned short>(npieces);
+        p.split_n[p.nsplit] = static_cast<unsigned short>(cl - cf + 1);
+        for (int c = cf; c <= cl; ++c)   // slot of CTA c's piece of t: 2c, +1 unless t is c's first tile
+            p.piece_slot[npieces++] = static_cast<unsigned short>(2 * c + (t == ub(c) / p.units_per_tile ? 0 : 1));
+        ++p.nsplit;
+    }
     const WsLayout w = ws_layout(a.M, a.K, p.tiles, p.grid);
     if (!a.workspace || a.workspace_bytes < w.total || (reinterpret_cast<uintptr_t>(a.workspace) & 255))
         return cudaErrorInvalidValue;
     uint8_t* ws = static_cast<uint8_t*>(a.workspace);
     __half* xh = reinterpret_cast<__half*>(ws + w.xh);
     p.tokexp = reinterpret_cast<const int*>(ws + w.tokexp);
-    p.counters = reinterpret_cast<unsigned int*>(ws + w.counters);
+    p.gbar = reinterpret_cast<unsigned int*>(ws + w.gbar);
     p.partials = reinterpret_cast<float*>(ws + w.partials);
     if (!encode(&p.xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh, a.K, a.M, kStageK, MT, CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
@@ -903,10 +1037,10 @@ cudaError_t launch_gemm_nf4(const GemmNf4Args& a, cudaStream_t stream) {
     if (rg.x < 2) return cudaErrorNotSupported;
     p.codes_ring = rg.codes;
     p.x_ring = rg.x;
-    p.dbufs = std::min(kMaxDBufs, (512 - kDCol0) / MT);
+    p.dbufs = std::min(kMaxDBufs, (512 - kDCol0) / (MT <= 64 ? 2 * MT : MT));
 
     gemm_x_prep_kernel<<<a.M, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(a.x), a.K, xh,
-                                               reinterpret_cast<int*>(ws + w.tokexp), p.counters, p.tiles);
+                                               reinterpret_cast<int*>(ws + w.tokexp), p.gbar, p.grid);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const size_t smem = rg.smem;
