@@ -563,6 +563,7 @@ __global__ void __launch_bounds__(32 * (6 + issuers_for(EW) + 4 * EW), 1)
         const int eh = (warp - kEpiWarp0) >> 2;
         const int r = 32 * q + lane;
         const uint32_t tq = tmem_base + (static_cast<uint32_t>(32 * q) << 16);
+        pdl_wait();       // token exponents (read at write-out)
         Cursor abc{0, 0u}, dc{0, 0u}, sdc{gpu - 1, 0u};
         bool ok = u1 > u0;
         float acc[NT];
@@ -670,6 +671,7 @@ __global__ void __launch_bounds__(32 * (6 + issuers_for(EW) + 4 * EW), 1)
     } else if (warp == kXWarp) {
         // ---------------------------------------------------------- activation tiles
         if (lane == 0) {
+            pdl_wait();   // fp16 activations and token exponents come from gemm_x_prep_kernel
             Cursor xc{0, 0u}, rel{0, 0u};
             int xi = 0;
             bool ok = u1 > u0;
@@ -741,7 +743,9 @@ __global__ void __launch_bounds__(32 * (6 + issuers_for(EW) + 4 * EW), 1)
     // pieces in K order (deterministic), after a grid barrier.  The launch is
     // cooperative, so all CTAs are resident; the wait is bounded.
     // Grid barrier without a contended atomic: each CTA publishes its own flag
-    // (cleared to 0 by gemm_x_prep_kernel), then thread j polls CTA j's flag.
+    // (cleared to 0 by gemm_x_prep_kernel, hence the wait for it), then thread
+    // j polls CTA j's flag.
+    pdl_wait();
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
@@ -762,38 +766,71 @@ __global__ void __launch_bounds__(32 * (6 + issuers_for(EW) + 4 * EW), 1)
     reduce_split_tiles(p, MT);
 }
 
+constexpr int kPrepThreads = 1024;
+constexpr int kPrepVecs = 4;                // uint4 (8 bf16) a thread keeps in registers: K <= 32768
+
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+__device__ __forceinline__ uint4 to_f16x8(uint4 v, float sc) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const __half lo = __float2half_rn(bf16_lo(w[j]) * sc);
+        const __half hi = __float2half_rn(bf16_hi(w[j]) * sc);
+        o[j] = static_cast<uint32_t>(__half_as_ushort(lo)) | (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 // bf16 activations -> fp16 x * 2^f (per token row), f = 15 - e with
-// max|x| = m * 2^e, m in [0.5, 1): max|x'| in [2^14, 2^15).  Block 0 also
-// clears the GEMM's grid-barrier flags.
-__global__ void gemm_x_prep_kernel(const __nv_bfloat16* __restrict__ x, int K, __half* __restrict__ xh,
-                                   int* __restrict__ tokexp, unsigned int* __restrict__ counters, int ncounters) {
+// max|x| = m * 2^e, m in [0.5, 1): max|x'| in [2^14, 2^15).  One block per
+// token, sized so that a row of K <= 32768 is read once and kept in registers
+// (4 x 8 values a thread).  Block 0 also clears the GEMM's grid-barrier flags.  Each block
+// lets the dependent GEMM launch as soon as it is resident.
+__global__ void __launch_bounds__(kPrepThreads) gemm_x_prep_kernel(const __nv_bfloat16* __restrict__ x, int K,
+                                                                   __half* __restrict__ xh, int* __restrict__ tokexp,
+                                                                   unsigned int* __restrict__ flags, int nflags) {
+    pdl_launch_dependents();
     const int m = blockIdx.x;
     if (m == 0)
-        for (int i = threadIdx.x; i < ncounters; i += blockDim.x) counters[i] = 0u;
+        for (int i = threadIdx.x; i < nflags; i += blockDim.x) flags[i] = 0u;
     const uint4* row = reinterpret_cast<const uint4*>(x + static_cast<size_t>(m) * K);
     const int n8 = K / 8;
+    const int nt = blockDim.x;
+    const bool in_regs = n8 <= kPrepVecs * nt;
+    uint4 v[kPrepVecs];
     float mx = 0.0f;
-    for (int i = threadIdx.x; i < n8; i += blockDim.x) {
-        const uint4 v = __ldg(row + i);
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    if (in_regs) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            mx = fmaxf(mx, fabsf(__uint_as_float(w[j] << 16)));
-            mx = fmaxf(mx, fabsf(__uint_as_float(w[j] & 0xFFFF0000u)));
+        for (int k = 0; k < kPrepVecs; ++k) {
+            const int i = threadIdx.x + k * nt;
+            v[k] = i < n8 ? __ldg(row + i) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int k = 0; k < kPrepVecs; ++k) {
+            const uint32_t w[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) mx = fmaxf(mx, fmaxf(fabsf(bf16_lo(w[j])), fabsf(bf16_hi(w[j]))));
+        }
+    } else {
+        for (int i = threadIdx.x; i < n8; i += blockDim.x) {
+            const uint4 u = __ldg(row + i);
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) mx = fmaxf(mx, fmaxf(fabsf(bf16_lo(w[j])), fabsf(bf16_hi(w[j]))));
         }
     }
     __shared__ float red[32];
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
     __syncthreads();
     if (threadIdx.x < 32) {
-        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
-        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-        if (threadIdx.x == 0) red[0] = v;
+        float r = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) r = fmaxf(r, __shfl_xor_sync(0xffffffffu, r, o));
+        if (threadIdx.x == 0) red[0] = r;
     }
     __syncthreads();
     mx = red[0];
@@ -805,20 +842,16 @@ __global__ void gemm_x_prep_kernel(const __nv_bfloat16* __restrict__ x, int K, _
         f = f < -100 ? -100 : (f > 100 ? 100 : f);
     }
     if (threadIdx.x == 0) tokexp[m] = f;
-    // 2^f as two exact factors (|f| <= 100 < 126 would fit one, kept general).
-    const float sc = __int_as_float((127 + f) << 23);
+    const float sc = __int_as_float((127 + f) << 23);    // 2^f, |f| <= 100
     uint4* out = reinterpret_cast<uint4*>(xh + static_cast<size_t>(m) * K);
-    for (int i = threadIdx.x; i < n8; i += blockDim.x) {
-        const uint4 v = __ldg(row + i);
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-        uint32_t o[4];
+    if (in_regs) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const __half lo = __float2half_rn(__uint_as_float(w[j] << 16) * sc);
-            const __half hi = __float2half_rn(__uint_as_float(w[j] & 0xFFFF0000u) * sc);
-            o[j] = static_cast<uint32_t>(__half_as_ushort(lo)) | (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
+        for (int k = 0; k < kPrepVecs; ++k) {
+            const int i = threadIdx.x + k * nt;
+            if (i < n8) out[i] = to_f16x8(v[k], sc);
         }
-        out[i] = make_uint4(o[0], o[1], o[2], o[3]);
+    } else {
+        for (int i = threadIdx.x; i < n8; i += blockDim.x) out[i] = to_f16x8(__ldg(row + i), sc);
     }
 }
 
@@ -917,11 +950,16 @@ cudaError_t launch_mt(const GemmParams& p, size_t smem, cudaStream_t stream) {
     cfg.blockDim = dim3(32 * (6 + issuers_for(EW) + 4 * EW));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
+    // Programmatic dependent launch on the activation prep just before it:
+    // set-up, the table, TMEM and the weight stream overlap it; the roles that
+    // read its output wait with griddepcontrol.wait.
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeCooperative;
+    attr[1].val.cooperative = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = p.nsplit > 0 ? 1 : 0;
+    cfg.numAttrs = p.nsplit > 0 ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, nf4_tc_gemm_kernel<MT, EW>, p);
 }
 
@@ -1039,7 +1077,8 @@ cudaError_t launch_gemm_nf4(const GemmNf4Args& a, cudaStream_t stream) {
     p.x_ring = rg.x;
     p.dbufs = std::min(kMaxDBufs, (512 - kDCol0) / (MT <= 64 ? 2 * MT : MT));
 
-    gemm_x_prep_kernel<<<a.M, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(a.x), a.K, xh,
+    const int prep_threads = std::min(kPrepThreads, std::max(128, (a.K / 8 / kPrepVecs + 31) / 32 * 32));
+    gemm_x_prep_kernel<<<a.M, prep_threads, 0, stream>>>(static_cast<const __nv_bfloat16*>(a.x), a.K, xh,
                                                reinterpret_cast<int*>(ws + w.tokexp), p.gbar, p.grid);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
