@@ -420,7 +420,8 @@ __global__ void __launch_bounds__(32 * (6 + issuers_for(EW) + 4 * EW), 1)
     nf4_tc_gemm_kernel(const __grid_constant__ GemmParams p) {
     constexpr int kIssuers = issuers_for(EW);
     constexpr int NT = MT / EW;                 // tokens per epilogue thread
-    constexpr int CH = MT <= 64 ? 2 : 1;        // accumulator chains per group (Th, Tl)
+    constexpr int CH = MT <= 16 ? 2 : 1;        // accumulator chains per group (Th, Tl); more TMEM per group
+                                                // leaves fewer accumulator buffers for wider token tiles
     constexpr int kEpiWarp0 = 4;
     constexpr int kProdWarp = 4 + 4 * EW;       // codes + absmax stream
     constexpr int kXWarp = kProdWarp + 1;       // activation tiles
@@ -1075,7 +1076,7 @@ cudaError_t launch_gemm_nf4(const GemmNf4Args& a, cudaStream_t stream) {
     if (rg.x < 2) return cudaErrorNotSupported;
     p.codes_ring = rg.codes;
     p.x_ring = rg.x;
-    p.dbufs = std::min(kMaxDBufs, (512 - kDCol0) / (MT <= 64 ? 2 * MT : MT));
+    p.dbufs = std::min(kMaxDBufs, (512 - kDCol0) / (MT <= 16 ? 2 * MT : MT));
 
     const int prep_threads = std::min(kPrepThreads, std::max(128, (a.K / 8 / kPrepVecs + 31) / 32 * 32));
     gemm_x_prep_kernel<<<a.M, prep_threads, 0, stream>>>(static_cast<const __nv_bfloat16*>(a.x), a.K, xh,
