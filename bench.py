@@ -333,6 +333,7 @@ def capture(torch, stream, record):
 
 
 def run_extra(args, dev, stream, sh, l2, which=None, reps=200):
+    c5_tokens = [int(v) for v in getattr(args, "c5_tokens", "1,16,64,512").split(",")]
     """Secondary configs, each with its own pool > 2 x L2 and device timing.
     `which` selects a subset of {"nf4", "q8", "attention", "c5"} (all if None)."""
     import torch
@@ -460,7 +461,7 @@ def run_extra(args, dev, stream, sh, l2, which=None, reps=200):
         tc_peak, tc_kind = load_tc_peak()
         hbm_peak, hbm_kind = load_peaks()
         res = {}
-        for M in (1, 16, 64, 512):
+        for M in c5_tokens:
             xh = torch.randn(M, H, device=dev).to(torch.bfloat16)
             xf = torch.randn(M, FF, device=dev).to(torch.bfloat16)
             ys = {name: torch.empty(M * n, device=dev) for name, (n, _) in shp.items()}
@@ -700,6 +701,8 @@ def main():
     ap.add_argument("--only", choices=["nf4", "q8", "attention", "decode", "c5"],
                     help="run one secondary workload alone (for profiling); prints its dict")
     ap.add_argument("--decode-tokens", type=int, default=32)
+    ap.add_argument("--c5-tokens", default="1,16,64,512",
+                    help="token counts of the batched-NF4 (C5) section, comma separated")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
