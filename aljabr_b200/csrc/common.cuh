@@ -50,11 +50,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// try_wait with a suspend-time hint: the thread sleeps in the barrier unit
+// until the phase completes (or ~0.5 ms pass) instead of spinning, so a
+// waiting warp does not take issue slots from the warps sharing its scheduler.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(500000u)
+        : "memory");
+    return ok != 0;
+}
 // Bounded wait: returns false (and records the fault) if the phase never flips.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     long long t0 = clock64();
-    while (!mbar_try_wait(bar, parity)) {
+    while (!mbar_try_wait_sleep(bar, parity)) {
         if (clock64() - t0 > kSpinLimitCycles) {
             record_fault(ALJ_FAULT_TIMEOUT);
             return false;

@@ -238,20 +238,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 
 // ------------------------------------------------------------------ waits
-// try_wait with a suspend-time hint: the thread sleeps in the barrier unit
-// until the phase completes (or ~0.5 ms pass) instead of spinning, so waiting
-// warps do not take issue slots from the dequant and epilogue warps that share
-// their schedulers.
-__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(500000u)
-        : "memory");
-    return ok != 0;
-}
-
 // Bounded wait that also gives up as soon as another role has (abort flag).
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
     if (mbar_try_wait(bar, parity)) return true;
