@@ -107,10 +107,15 @@ struct AttnParams {
     float* part_ml;          // scratch [q_heads][splits][2]  (running max, running sum)
     int splits;
     const int* dev_pos;      // if set, seq_len = *dev_pos + 1 is read on the device (graph replay)
-    TpLink tpl;              // tensor-parallel push of `out` (combine kernel; needs splits >= 2)
+    TpLink tpl;              // tensor-parallel push of `out` (split merge; needs splits >= 2)
+    unsigned int* split_counter;   // [kv_heads] arrival counters of the fused split merge: 0 before and after
 };
 int attention_splits(int seq_len, int kv_heads, int sm_count);
+// Scratch of attention_scratch_floats() floats, zeroed once when allocated
+// and then owned by one stream: attention_bind_scratch points part_o,
+// part_ml and split_counter into it for p.q_heads / p.head_dim / p.splits.
 size_t attention_scratch_floats(int q_heads, int head_dim, int splits);
+void attention_bind_scratch(AttnParams& p, float* scratch);
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl);
 
 // Batched NF4 GEMM on tcgen05 (gemm_nf4.cu): y_s[m * ldy_s + n] =

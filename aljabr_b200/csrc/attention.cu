@@ -18,9 +18,15 @@
 // Other shapes run a plain three-pass kernel (one CTA per query head).
 #include "common.cuh"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 
 namespace alj {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();   // matvec.cu
+
 namespace {
 
 constexpr float kLog2e = 1.4426950408889634f;
@@ -73,6 +79,39 @@ __device__ __forceinline__ void reduce_scatter32(float (&v)[32], int lane) {
             const float send = upper ? v[i] : v[i + h];
             const float keep = upper ? v[i + h] : v[i];
             v[i] = keep + __shfl_xor_sync(0xffffffffu, send, h);
+        }
+    }
+}
+
+// Merge the per-warp softmax state of one CTA -- running max (natural-log
+// units), running sum and unnormalised output, in shared memory as
+// [warp][head slot] with `gs` slots per warp -- and store the split's
+// partials, or the normalised output when there is a single split.
+template <int D>
+__device__ __forceinline__ void merge_warps_store(const AttnParams& p, const float* s_ml, const float* s_o, int gs, int G,
+                                                  int kvh, int split) {
+    for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+        const int g = idx / D, d = idx - g * D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, s_ml[(w * gs + g) * 2]);
+        float L = 0.0f, acc = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) {
+            const float mw = s_ml[(w * gs + g) * 2];
+            const float f = mw == -INFINITY ? 0.0f : exp2f((mw - M) * kLog2e);
+            L = fmaf(s_ml[(w * gs + g) * 2 + 1], f, L);
+            acc = fmaf(s_o[(w * gs + g) * D + d], f, acc);
+        }
+        const int qh = kvh * G + g;
+        if (p.splits == 1) {
+            p.out[qh * D + d] = L > 0.0f ? acc / L : 0.0f;
+        } else {
+            p.part_o[(static_cast<long long>(qh) * p.splits + split) * D + d] = acc;
+            if (d == 0) {
+                p.part_ml[(static_cast<long long>(qh) * p.splits + split) * 2] = M;
+                p.part_ml[(static_cast<long long>(qh) * p.splits + split) * 2 + 1] = L;
+            }
         }
     }
 }
@@ -168,36 +207,452 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_split_kernel(const AttnP
 #pragma unroll
         for (int e = 0; e < E; ++e) s_o[warp][g][lane * E + e] = o[g][e];
     __syncthreads();
-    for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
-        const int g = idx / D, d = idx - g * D;
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, s_ml[w][g][0]);
-        float L = 0.0f, acc = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kAttnWarps; ++w) {
-            const float mw = s_ml[w][g][0];
-            const float f = mw == -INFINITY ? 0.0f : exp2f((mw - M) * kLog2e);
-            L = fmaf(s_ml[w][g][1], f, L);
-            acc = fmaf(s_o[w][g][d], f, acc);
+    merge_warps_store<D>(p, &s_ml[0][0][0], &s_o[0][0][0], G, G, kvh, split);
+}
+
+// ---------------------------------------------------------------- tensor-core split kernel
+// bf16 caches with head_dim 64 or 128 and up to 8 query heads per kv head.
+// The shuffle formulation above spends ~15 warp instructions per (position,
+// head) pair, which leaves it issue-bound well below the HBM rate; here both
+// products run on mma.sync.m16n8k16 (bf16 operands, f32 accumulation):
+//   * the split's K/V rows arrive by TMA as 32-row boxes of 64-element
+//     halves (128-byte swizzle, so the ldmatrix reads below are free of bank
+//     conflicts), each box completing on its own mbarrier;
+//   * fp32 accuracy from bf16 operands: the query (times scale * log2 e) and
+//     the probabilities are each split into three bf16 parts x = h + m + l
+//     (|x - h - m - l| <= 2^-26 |x|) while K and V are exact in bf16.  With
+//     G <= 4 heads the three parts share one A operand (rows [0, G) = h,
+//     [G, 2G) = m, [8, 8 + G) = l), and a shuffle joins the m rows to the
+//     others; with 5..8 heads two MMAs run per step, [h ; m] and [l ; 0];
+//   * scores: B = 8 cached positions of K straight from shared memory; the
+//     accumulator of a lane holds its head's score for two positions;
+//   * a warp owns every 4th 16-position chunk of the split and keeps all its
+//     scores in registers, so its softmax needs no rescaling; the score
+//     accumulator layout is the A-operand layout of the next product;
+//   * output: B = V rows through ldmatrix.trans, accumulated over the warp's
+//     chunks in 64 (head_dim 128) registers;
+//   * the warps merge through shared memory into the split's partials; the
+//     last CTA of a kv head (a per-head arrival counter) merges the splits
+//     and writes the output -- no second kernel.
+constexpr int kMaxSplits = 256;
+constexpr int kBoxRows = 32;     // positions per TMA box and per staging barrier
+constexpr int kMaxBoxes = 6;     // at most 192 positions per split
+constexpr int kChunkRows = 16;
+constexpr int kMaxWarpChunks = (kMaxBoxes * kBoxRows / kChunkRows + kAttnWarps - 1) / kAttnWarps;
+constexpr int kMmaSmemMax = 2 * kMaxBoxes * kBoxRows * 128 * 2 + 1024;   // K + V at head_dim 128, + alignment
+
+struct AttnMmaParams {
+    CUtensorMap kmap;   // bf16 cache viewed as [rows][kv_heads][head_dim / 64][64]
+    CUtensorMap vmap;
+    AttnParams a;
+    int cap_rows;       // staged rows per split: a multiple of kBoxRows, >= the longest split
+    int merge_smem;     // the split merge copies the partial outputs into shared memory
+};
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+        "[%6];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t a, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(a)
+                 : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t a, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(a)
+                 : "memory");
+}
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ unsigned int atom_add_acq_rel_gpu(unsigned int* p, unsigned int v) {
+    unsigned int old;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ uint32_t bf16x2_bits(__nv_bfloat162 v) { return *reinterpret_cast<const uint32_t*>(&v); }
+// Three-part bf16 split of (x0, x1): pairs packed as MMA operands (x0 low).
+struct Split3 {
+    uint32_t h, m, l;
+};
+__device__ __forceinline__ Split3 split3(float x0, float x1) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+    const float r0 = x0 - __low2float(h), r1 = x1 - __high2float(h);
+    const __nv_bfloat162 m = __floats2bfloat162_rn(r0, r1);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(r0 - __low2float(m), r1 - __high2float(m));
+    return {bf16x2_bits(h), bf16x2_bits(m), bf16x2_bits(l)};
+}
+// Byte offset of (row, element d) in a staged region [d / 64][cap rows][128 B]
+// written by TMA with the 128-byte swizzle (16-byte unit ^= row % 8).
+__device__ __forceinline__ uint32_t swz(int row, int d, int cap) {
+    return static_cast<uint32_t>(((d >> 6) * cap + row) * 128 + ((((d >> 3) & 7) ^ (row & 7)) << 4));
+}
+
+// A operands of one k16 step from the lane's (x0, x1) at k = kq + {0,1} and
+// (x2, x3) at k = kq + 8 + {0,1}, for the lane's row r = lane / 4.
+// PACK (G <= 4): r < G carries head r's h (row r) and l (row r + 8);
+// G <= r < 2G carries head r - G's m (row r).  Otherwise a0 = [h ; m] and
+// a1 = [l ; 0] with r < G the head.  `role`: 0 = h/l rows, 1 = m rows,
+// 2 = no head.
+template <bool PACK>
+__device__ __forceinline__ void a_operands(float x0, float x1, float x2, float x3, int role, uint32_t (&a0)[4],
+                                           uint32_t (&a1)[4]) {
+    const Split3 lo = split3(x0, x1), hi = split3(x2, x3);
+    if (PACK) {
+        a0[0] = role == 0 ? lo.h : role == 1 ? lo.m : 0u;
+        a0[1] = role == 0 ? lo.l : 0u;
+        a0[2] = role == 0 ? hi.h : role == 1 ? hi.m : 0u;
+        a0[3] = role == 0 ? hi.l : 0u;
+    } else {
+        const bool on = role == 0;
+        a0[0] = on ? lo.h : 0u;
+        a0[1] = on ? lo.m : 0u;
+        a0[2] = on ? hi.h : 0u;
+        a0[3] = on ? hi.m : 0u;
+        a1[0] = on ? lo.l : 0u;
+        a1[1] = 0u;
+        a1[2] = on ? hi.l : 0u;
+        a1[3] = 0u;
+    }
+}
+
+// The last CTA of kv head `kvh`: merge the splits of its G query heads
+// (partials in natural-log units) and write the output, or push it to every
+// tensor-parallel rank and publish when the last kv head is done.  Each
+// thread owns float4 items (head, 4 outputs).  When the G heads' partial
+// outputs fit in shared memory (`bulk`) they arrive by one bulk copy per
+// head while the split weights are formed; otherwise each thread's first
+// loads go out before the weights are formed and the rest in batches.
+template <int D>
+__device__ __forceinline__ void merge_splits(const AttnParams& p, int kvh, int G, bool bulk, float* sm, float* s_scale,
+                                             uint64_t* bar) {
+    constexpr int kBatch = 16;
+    const int S = p.splits;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int items = G * D / 4;
+    float* const s_w = bulk ? sm + static_cast<size_t>(G) * S * D : sm;
+    float4 v[kBatch];
+    if (bulk) {
+        if (threadIdx.x == 0) {
+            fence_proxy_async_global();   // other CTAs' generic stores, read by the async proxy
+            mbar_arrive_expect_tx(bar, static_cast<uint32_t>(G * S * D * 4));
+            for (int g = 0; g < G; ++g)
+                bulk_g2s(sm + static_cast<size_t>(g) * S * D, p.part_o + static_cast<long long>(kvh * G + g) * S * D,
+                         static_cast<uint32_t>(S * D * 4), bar);
         }
+    } else {
+        const int it = threadIdx.x, g = it / (D / 4), d = (it - g * (D / 4)) * 4;
+        const float4* po = reinterpret_cast<const float4*>(p.part_o + static_cast<long long>(kvh * G + g) * S * D + d);
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u)
+            v[u] = it < items && u < S ? __ldcg(po + u * (D / 4)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+    // split weights: warp w forms those of heads w, w + 4, ...
+    for (int g = warp; g < G; g += kAttnWarps) {
+        const float2* ml = reinterpret_cast<const float2*>(p.part_ml + static_cast<long long>(kvh * G + g) * S * 2);
+        float2 e[kMaxSplits / 32];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < kMaxSplits / 32; ++k) {
+            e[k] = lane + 32 * k < S ? __ldcg(ml + lane + 32 * k) : make_float2(-INFINITY, 0.0f);
+            mx = fmaxf(mx, e[k].x);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float l = 0.0f;
+#pragma unroll
+        for (int k = 0; k < kMaxSplits / 32; ++k) {
+            const float w = e[k].x == -INFINITY ? 0.0f : exp2f((e[k].x - mx) * kLog2e);
+            if (lane + 32 * k < S) s_w[g * S + lane + 32 * k] = w;
+            l = fmaf(e[k].y, w, l);
+        }
+        l = warp_sum(l);
+        if (lane == 0) s_scale[g] = l > 0.0f ? 1.0f / l : 0.0f;
+    }
+    __syncthreads();
+    if (bulk) mbar_wait(bar, 0);   // a timeout is recorded in the fault word
+    for (int it = threadIdx.x; it < items; it += blockDim.x) {
+        const int g = it / (D / 4), d = (it - g * (D / 4)) * 4;
         const int qh = kvh * G + g;
-        if (p.splits == 1) {
-            p.out[qh * D + d] = L > 0.0f ? acc / L : 0.0f;
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (bulk) {
+            const float4* so = reinterpret_cast<const float4*>(sm + static_cast<size_t>(g) * S * D + d);
+            for (int j0 = 0; j0 < S; j0 += 8) {   // 8 independent shared loads per step
+                float4 x[8];
+                float w[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const bool in = j0 + u < S;
+                    x[u] = in ? so[(j0 + u) * (D / 4)] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    w[u] = in ? s_w[g * S + j0 + u] : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    acc.x = fmaf(x[u].x, w[u], acc.x);
+                    acc.y = fmaf(x[u].y, w[u], acc.y);
+                    acc.z = fmaf(x[u].z, w[u], acc.z);
+                    acc.w = fmaf(x[u].w, w[u], acc.w);
+                }
+            }
         } else {
-            p.part_o[(static_cast<long long>(qh) * p.splits + split) * D + d] = acc;
-            if (d == 0) {
-                p.part_ml[(static_cast<long long>(qh) * p.splits + split) * 2] = M;
-                p.part_ml[(static_cast<long long>(qh) * p.splits + split) * 2 + 1] = L;
+            const float4* po = reinterpret_cast<const float4*>(p.part_o + static_cast<long long>(qh) * S * D + d);
+            for (int j0 = 0; j0 < S; j0 += kBatch) {
+                if (it != static_cast<int>(threadIdx.x) || j0 > 0) {
+#pragma unroll
+                    for (int u = 0; u < kBatch; ++u)
+                        v[u] = j0 + u < S ? __ldcg(po + (j0 + u) * (D / 4)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                }
+#pragma unroll
+                for (int u = 0; u < kBatch; ++u) {
+                    const float w = j0 + u < S ? s_w[g * S + j0 + u] : 0.0f;
+                    acc.x = fmaf(v[u].x, w, acc.x);
+                    acc.y = fmaf(v[u].y, w, acc.y);
+                    acc.z = fmaf(v[u].z, w, acc.z);
+                    acc.w = fmaf(v[u].w, w, acc.w);
+                }
+            }
+        }
+        const float inv = s_scale[g];
+        const float4 o = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        if (p.tpl.tp > 1) {
+            for (int r = 0; r < p.tpl.tp; ++r) *reinterpret_cast<float4*>(p.tpl.push_y[r] + qh * D + d) = o;
+        } else {
+            *reinterpret_cast<float4*>(p.out + qh * D + d) = o;
+        }
+    }
+    if (p.tpl.tp > 1) {
+        // the last kv head publishes this rank's heads on every rank
+        __threadfence_system();
+        __syncthreads();
+        if (threadIdx.x == 0)
+            s_scale[0] = atomicAdd(p.tpl.counter, 1u) == static_cast<unsigned int>(p.kv_heads - 1) ? 1.0f : 0.0f;
+        __syncthreads();
+        if (s_scale[0] != 0.0f) {
+            __threadfence_system();
+            if (static_cast<int>(threadIdx.x) < p.tpl.tp)
+                st_release_sys(p.tpl.push_flag[threadIdx.x],
+                               static_cast<unsigned int>(*p.tpl.seq * p.tpl.push_mul + p.tpl.push_add));
+            if (threadIdx.x == 0) *p.tpl.counter = 0u;
+        }
+    }
+}
+
+template <int D, bool PACK>
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const __grid_constant__ AttnMmaParams mp) {
+    const AttnParams& p = mp.a;
+    pdl_launch_dependents();
+    pdl_wait();
+    constexpr int NH = D / 64;   // 128-byte halves of a row
+    constexpr int KS = D / 16;   // k16 steps of q.k
+    constexpr int NT = D / 8;    // n8 tiles of the output
+    const int kvh = blockIdx.x, split = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = p.q_heads / p.kv_heads;
+    const int cap = mp.cap_rows;
+    const int seq_len = p.dev_pos ? *p.dev_pos + 1 : p.seq_len;
+    const int active = seq_len - p.start_pos;
+    const int c0 = p.start_pos + static_cast<int>(static_cast<long long>(active) * split / p.splits);
+    const int c1 = p.start_pos + static_cast<int>(static_cast<long long>(active) * (split + 1) / p.splits);
+    int n = c1 - c0;
+    if (n > cap) {   // a device position past the length the launch was sized for
+        if (threadIdx.x == 0) record_fault(ALJ_FAULT_BOUNDS);
+        n = cap;
+    }
+
+    extern __shared__ unsigned char smem_raw[];
+    __shared__ uint64_t s_bar[kMaxBoxes + 1];   // K/V boxes, then the split merge's bulk copy
+    __shared__ float s_ml[kAttnWarps * 8 * 2];
+    __shared__ float s_scale[8];
+    __shared__ unsigned int s_last;
+    const uint32_t sk = (smem_u32(smem_raw) + 1023u) & ~1023u;
+    const uint32_t sv = sk + static_cast<uint32_t>(cap) * D * 2;
+    float* const stage_f = reinterpret_cast<float*>(smem_raw + (sk - smem_u32(smem_raw)));
+    // the lane's row r = lane / 4 of the A / C fragments and its head; the
+    // query loads go out ahead of the bulk traffic of the whole grid
+    const int r = lane >> 2, kq = (lane & 3) * 2;
+    const int role = r < G ? 0 : (PACK && r < 2 * G) ? 1 : 2;
+    const int head = role == 0 ? r : role == 1 ? r - G : 0;
+    const int partner = role == 0 ? lane + 4 * G : lane - 4 * G;   // PACK: the lane with the other part rows
+    if (threadIdx.x == 0) {   // before the query loads: the fence would wait for them
+        for (int b = 0; b < kMaxBoxes + 1; ++b) mbar_init(&s_bar[b], 1);
+        fence_mbar_init();
+    }
+    float qv[KS][4];
+    {
+        const float* qrow = p.q + static_cast<long long>(kvh * G + head) * D;
+#pragma unroll
+        for (int s = 0; s < KS; ++s) {
+            qv[s][0] = qv[s][1] = qv[s][2] = qv[s][3] = 0.0f;
+            if (role != 2) {
+                qv[s][0] = qrow[16 * s + kq];
+                qv[s][1] = qrow[16 * s + kq + 1];
+                qv[s][2] = qrow[16 * s + 8 + kq];
+                qv[s][3] = qrow[16 * s + 8 + kq + 1];
             }
         }
     }
+    const int nboxes = (n + kBoxRows - 1) / kBoxRows;
+    if (threadIdx.x == 0) {
+        for (int b = 0; b < nboxes; ++b) {
+            mbar_arrive_expect_tx(&s_bar[b], 2u * NH * kBoxRows * 128u);
+            for (int h = 0; h < NH; ++h) {
+                const uint32_t off = static_cast<uint32_t>((h * cap + b * kBoxRows) * 128);
+                tma_load_4d(sk + off, &mp.kmap, 0, h, kvh, c0 + b * kBoxRows, &s_bar[b]);
+                tma_load_4d(sv + off, &mp.vmap, 0, h, kvh, c0 + b * kBoxRows, &s_bar[b]);
+            }
+        }
+    }
+    uint32_t qa[KS][4], qb[PACK ? 1 : KS][4];
+    {
+        const float qs = p.scale * kLog2e;
+#pragma unroll
+        for (int s = 0; s < KS; ++s)
+            a_operands<PACK>(qv[s][0] * qs, qv[s][1] * qs, qv[s][2] * qs, qv[s][3] * qs, role, qa[s], qb[PACK ? 0 : s]);
+    }
+    __syncthreads();   // barrier initialisation visible to every waiter
+
+    // scores (log2 units) of this warp's chunks: sc[ci][t][j] is position
+    // 16c + 8t + kq + j of chunk c = warp + 4 ci, for the lane's head
+    const int nchunks = (n + kChunkRows - 1) / kChunkRows;
+    float sc[kMaxWarpChunks][2][2];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int ci = 0; ci < kMaxWarpChunks; ++ci) {
+        const int c = warp + ci * kAttnWarps;
+        sc[ci][0][0] = sc[ci][0][1] = sc[ci][1][0] = sc[ci][1][1] = -INFINITY;
+        if (c >= nchunks) continue;
+        mbar_wait(&s_bar[c >> 1], 0);   // a timeout is recorded in the fault word
+        float acc[2][4] = {};
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+            const int row = kChunkRows * c + 8 * t + (lane & 7);
+#pragma unroll
+            for (int s2 = 0; s2 < KS / 2; ++s2) {
+                uint32_t kb[4];
+                ldsm_x4(sk + swz(row, 32 * s2 + 8 * (lane >> 3), cap), kb);
+                mma_bf16(acc[t], qa[2 * s2], kb[0], kb[1]);
+                mma_bf16(acc[t], qa[2 * s2 + 1], kb[2], kb[3]);
+                if (!PACK) {
+                    mma_bf16(acc[t], qb[2 * s2], kb[0], kb[1]);
+                    mma_bf16(acc[t], qb[2 * s2 + 1], kb[2], kb[3]);
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                float v = acc[t][j] + acc[t][j + 2];
+                if (PACK) v += __shfl_sync(0xffffffffu, v, partner & 31);
+                const int pos = kChunkRows * c + 8 * t + kq + j;
+                sc[ci][t][j] = pos < n ? v : -INFINITY;
+                mx = fmaxf(mx, sc[ci][t][j]);
+            }
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+
+    // probabilities as A operands, split like the query
+    uint32_t pa[kMaxWarpChunks][4], pb[PACK ? 1 : kMaxWarpChunks][4];
+    float l = 0.0f;
+#pragma unroll
+    for (int ci = 0; ci < kMaxWarpChunks; ++ci) {
+        float e[2][2];
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                e[t][j] = sc[ci][t][j] == -INFINITY ? 0.0f : exp2f(sc[ci][t][j] - mx);
+                l += e[t][j];
+            }
+        a_operands<PACK>(e[0][0], e[0][1], e[1][0], e[1][1], role, pa[ci], pb[PACK ? 0 : ci]);
+    }
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+
+    float o[NT][4];
+#pragma unroll
+    for (int i = 0; i < NT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+#pragma unroll
+    for (int ci = 0; ci < kMaxWarpChunks; ++ci) {
+        const int c = warp + ci * kAttnWarps;
+        if (c >= nchunks) break;
+        if (c == nchunks - 1 && (n & (kChunkRows - 1))) {
+            // rows past the split hold other positions (or unwritten cache):
+            // zero them so that probability 0 never meets a NaN
+            const int nz = kChunkRows * nchunks - n;
+            for (int i = lane; i < nz * NH * 8; i += 32) {
+                const int row = n + i / (NH * 8), h = (i / 8) % NH, u = i & 7;
+                asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(sv + static_cast<uint32_t>((h * cap + row) * 128 + u * 16)),
+                             "r"(0u)
+                             : "memory");
+            }
+            __syncwarp();
+        }
+        const int row = kChunkRows * c + ((lane >> 3) & 1) * 8 + (lane & 7);
+#pragma unroll
+        for (int u = 0; u < NT / 2; ++u) {
+            uint32_t vb[4];
+            ldsm_x4_trans(sv + swz(row, 16 * u + (lane >> 4) * 8, cap), vb);
+            mma_bf16(o[2 * u], pa[ci], vb[0], vb[1]);
+            mma_bf16(o[2 * u + 1], pa[ci], vb[2], vb[3]);
+            if (!PACK) {
+                mma_bf16(o[2 * u], pb[ci], vb[0], vb[1]);
+                mma_bf16(o[2 * u + 1], pb[ci], vb[2], vb[3]);
+            }
+        }
+    }
+
+    // per-warp state to shared memory (the output part reuses the staging
+    // buffer once every warp is done reading it), then the CTA merge
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < NT; ++i)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            o[i][j] += o[i][j + 2];
+            if (PACK) o[i][j] += __shfl_sync(0xffffffffu, o[i][j], partner & 31);
+        }
+    if (role == 0) {
+        if ((lane & 3) == 0) {
+            s_ml[(warp * 8 + r) * 2] = mx == -INFINITY ? -INFINITY : mx * (1.0f / kLog2e);
+            s_ml[(warp * 8 + r) * 2 + 1] = l;
+        }
+#pragma unroll
+        for (int i = 0; i < NT; ++i) {
+            stage_f[(warp * 8 + r) * D + 8 * i + kq] = o[i][0];
+            stage_f[(warp * 8 + r) * D + 8 * i + kq + 1] = o[i][1];
+        }
+    }
+    __syncthreads();
+    merge_warps_store<D>(p, s_ml, stage_f, 8, G, kvh, split);
+    if (p.splits == 1) return;
+
+    // the last CTA of this kv head to finish merges the splits: the CTA
+    // barrier orders every thread's partial stores before thread 0's
+    // acquire-release arrival (release is cumulative), and the winner's
+    // acquire orders the other CTAs' partials before its reads
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atom_add_acq_rel_gpu(&p.split_counter[kvh], 1u) == static_cast<unsigned int>(p.splits - 1);
+    __syncthreads();
+    if (!s_last) return;
+    merge_splits<D>(p, kvh, G, mp.merge_smem, stage_f, s_scale, &s_bar[kMaxBoxes]);
+    if (threadIdx.x == 0) p.split_counter[kvh] = 0u;
 }
 
 // Merge the splits of one query head: the per-split (max, sum) pairs are
 // staged in shared memory and turned into weights once, then each thread
 // sums its head-dim element over the splits with independent loads.
-constexpr int kMaxSplits = 256;
 
 __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnParams p) {
     pdl_launch_dependents();
@@ -324,8 +779,9 @@ __global__ void attn_fallback_kernel(const AttnParams p) {
     }
 }
 
-cudaError_t launch_pdl(void (*kernel)(AttnParams), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
-                       const AttnParams& p) {
+template <typename Params>
+cudaError_t launch_pdl(void (*kernel)(Params), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                       const Params& p) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
@@ -337,6 +793,69 @@ cudaError_t launch_pdl(void (*kernel)(AttnParams), dim3 grid, dim3 block, size_t
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
+// Shared memory of the bulk split merge: the kv head's partial outputs and
+// their weights.
+size_t merge_bytes(const AttnParams& p) {
+    const size_t gs = static_cast<size_t>(p.q_heads / p.kv_heads) * p.splits;
+    return gs * p.head_dim * 4 + gs * 4;
+}
+
+// Tensor maps and staging rows for the tensor-core kernel; false when the
+// cache type, shape or layout is outside it (the shuffle kernel runs then).
+bool mma_params(const AttnParams& p, AttnMmaParams& mp) {
+    if (p.kv_dtype != ALJ_KV_BF16 || !(p.head_dim == 64 || p.head_dim == 128)) return false;
+    if (p.kv_heads <= 0 || p.q_heads % p.kv_heads || p.q_heads / p.kv_heads > 8) return false;
+    const uintptr_t mis = reinterpret_cast<uintptr_t>(p.k) | reinterpret_cast<uintptr_t>(p.v);
+    if (mis % 16 || (static_cast<long long>(p.stride) * 2) % 16 || (p.head_stride * 2) % 16) return false;
+    const int active = p.seq_len - p.start_pos;
+    const int rows = (active + p.splits - 1) / p.splits;
+    const int cap = (rows + kBoxRows - 1) / kBoxRows * kBoxRows;
+    if (cap > kMaxBoxes * kBoxRows) return false;
+    if (p.splits > 1 && (!p.split_counter || reinterpret_cast<uintptr_t>(p.part_o) % 16 ||
+                         reinterpret_cast<uintptr_t>(p.part_ml) % 8 || p.splits > kMaxSplits))
+        return false;
+    auto fn = tensor_map_encoder();
+    if (!fn) return false;
+    const cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(p.head_dim / 64), static_cast<cuuint64_t>(p.kv_heads),
+                                static_cast<cuuint64_t>(p.seq_len)};
+    const cuuint64_t strides[3] = {128, static_cast<cuuint64_t>(p.head_stride) * 2,
+                                   static_cast<cuuint64_t>(p.stride) * 2};
+    const cuuint32_t box[4] = {64, 1, 1, kBoxRows};
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    for (int t = 0; t < 2; ++t)
+        if (fn(t == 0 ? &mp.kmap : &mp.vmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(t == 0 ? p.k : p.v),
+               dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    mp.a = p;
+    mp.cap_rows = cap;
+    mp.merge_smem = p.splits > 1 && merge_bytes(p) + 1024 <= static_cast<size_t>(kMmaSmemMax);
+    return true;
+}
+
+template <int D, bool PACK>
+cudaError_t launch_mma(const AttnMmaParams& mp, dim3 grid, cudaStream_t stream, bool pdl) {
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!configured[dev & 63]) {
+        cudaError_t e =
+            cudaFuncSetAttribute(attn_mma_kernel<D, PACK>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaSmemMax);
+        if (e != cudaSuccess) return e;
+        configured[dev & 63] = true;
+    }
+    const size_t stage = 2ull * mp.cap_rows * D * 2;
+    const size_t smem = (mp.merge_smem ? std::max(stage, merge_bytes(mp.a)) : stage) + 1024;
+    return launch_pdl(attn_mma_kernel<D, PACK>, grid, dim3(kAttnWarps * 32), smem, stream, pdl, mp);
+}
+
+cudaError_t dispatch_mma(const AttnMmaParams& mp, dim3 grid, cudaStream_t stream, bool pdl) {
+    const bool pack = mp.a.q_heads / mp.a.kv_heads <= 4;
+    if (mp.a.head_dim == 64)
+        return pack ? launch_mma<64, true>(mp, grid, stream, pdl) : launch_mma<64, false>(mp, grid, stream, pdl);
+    return pack ? launch_mma<128, true>(mp, grid, stream, pdl) : launch_mma<128, false>(mp, grid, stream, pdl);
 }
 
 bool fast_path(const AttnParams& p) {
@@ -381,24 +900,42 @@ cudaError_t dispatch_e(const AttnParams& p, dim3 grid, cudaStream_t stream, bool
 }  // namespace
 
 int attention_splits(int seq_len, int kv_heads, int sm_count) {
-    // ~2 CTAs per SM in total, at least 64 positions per split
+    // ~2 CTAs per SM in total and at least 64 positions per split; long
+    // caches take more splits so that a split stays within the tensor-core
+    // kernel's staging (kMaxBoxes * kBoxRows positions)
     const int want = std::max(1, (2 * sm_count + kv_heads - 1) / std::max(kv_heads, 1));
     const int cap = std::max(1, seq_len / 64);
-    return std::min(std::min(want, cap), kMaxSplits);
+    const int need = (seq_len + kMaxBoxes * kBoxRows - 1) / (kMaxBoxes * kBoxRows);
+    return std::min(std::max(std::min(want, cap), need), kMaxSplits);
 }
 
+// [arrival counters: q_heads words, rounded to 16 bytes][partial outputs][partial (max, sum)]:
+// the counters sit at a fixed place whatever the split count, so the zeros
+// they return to after every launch stay zeros for the next shape.
+static size_t counter_floats(int q_heads) { return (static_cast<size_t>(q_heads) + 3) / 4 * 4; }
+
 size_t attention_scratch_floats(int q_heads, int head_dim, int splits) {
-    return static_cast<size_t>(q_heads) * splits * (head_dim + 2);
+    return counter_floats(q_heads) + static_cast<size_t>(q_heads) * splits * (head_dim + 2);
+}
+
+void attention_bind_scratch(AttnParams& p, float* scratch) {
+    p.split_counter = reinterpret_cast<unsigned int*>(scratch);
+    p.part_o = scratch + counter_floats(p.q_heads);
+    p.part_ml = p.part_o + static_cast<size_t>(p.q_heads) * p.splits * p.head_dim;
 }
 
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl) {
     const int active = p.seq_len - p.start_pos;
     if (active <= 0) return cudaErrorInvalidValue;
     // the tensor-parallel push lives in the combine kernel
-    if (p.tpl.tp > 1 && (p.splits < 2 || p.tpl.tp > kMaxTp || !p.tpl.counter || !p.tpl.seq || !fast_path(p)))
+    AttnMmaParams mp{};
+    const bool tc = mma_params(p, mp);
+    const bool split_path = tc || fast_path(p);
+    if (p.tpl.tp > 1 && (p.splits < 2 || p.tpl.tp > kMaxTp || !p.tpl.counter || !p.tpl.seq || !split_path))
         return cudaErrorInvalidValue;
-    if (fast_path(p)) {
+    if (split_path) {
         dim3 grid(p.kv_heads, p.splits);
+        if (tc) return dispatch_mma(mp, grid, stream, pdl);   // merges its splits itself
         cudaError_t e = p.kv_dtype == ALJ_KV_BF16 ? dispatch_e<ALJ_KV_BF16>(p, grid, stream, pdl)
                                                   : dispatch_e<ALJ_KV_F32>(p, grid, stream, pdl);
         if (e != cudaSuccess || p.splits == 1) return e;

@@ -62,6 +62,7 @@ struct DevBuf {
         p = nullptr;
         cap = 0;
         cudaError_t e = cudaMalloc(&p, bytes);
+        if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);   // counters inside scratch start at zero
         if (e == cudaSuccess) cap = bytes;
         return e;
     }
@@ -360,8 +361,7 @@ int run_attention(DeviceState* st, float* dout, const float* dq, const void* k, 
     p.splits = attention_splits(seq_len - start_pos, kv_heads, st->sms);
     if (p.splits > 1) {
         ALJ_CUDA(scratch->ensure(attention_scratch_floats(q_heads, head_dim, p.splits) * 4));
-        p.part_o = static_cast<float*>(scratch->p);
-        p.part_ml = p.part_o + static_cast<size_t>(q_heads) * p.splits * head_dim;
+        attention_bind_scratch(p, static_cast<float*>(scratch->p));
     }
     return launch_status(launch_attention(p, stream, false), "decode attention");
 }

@@ -400,8 +400,7 @@ cudaError_t record_step(DecodeModel& m) {
             a.start_pos = 0;
             a.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)));
             a.splits = m.splits;
-            a.part_o = m.scratch;
-            a.part_ml = m.scratch + static_cast<size_t>(m.hq) * m.splits * D;
+            attention_bind_scratch(a, m.scratch);
             a.dev_pos = m.io;
             REC(launch_attention(a, m.stream, true));
         }
@@ -522,8 +521,7 @@ cudaError_t record_step_p2p(DecodeModel& m) {
             a.start_pos = 0;
             a.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)));
             a.splits = m.splits;
-            a.part_o = m.scratch;
-            a.part_ml = m.scratch + static_cast<size_t>(m.hq) * m.splits * D;
+            attention_bind_scratch(a, m.scratch);
             a.dev_pos = m.io;
             a.tpl = link(m.off_att, R * m.hq * D, 0, FL_ATT, L, l + 1);
             REC(launch_attention(a, m.stream, true));

@@ -94,10 +94,10 @@ extern "C" int aljabr_blackwell_decode_attention_noalloc(float* out, const float
     if (p.splits > 1) {
         if (attention_scratch_floats(q_heads, head_dim, p.splits) > kNoAllocScratchFloats)
             return decode_fail(ALJ_ERR_BAD_DIMS,
-                               "q_heads * splits * (head_dim + 2) exceeds the 1,048,576-float static scratch of "
+                               "the split scratch (q_heads * splits * (head_dim + 2) floats and counters) exceeds the "
+                               "1,048,576-float static scratch of "
                                "aljabr_blackwell_decode_attention_noalloc");
-        p.part_o = scratch;
-        p.part_ml = scratch + static_cast<size_t>(q_heads) * p.splits * head_dim;
+        attention_bind_scratch(p, scratch);
     }
     const cudaError_t e = launch_attention(p, static_cast<cudaStream_t>(stream), false);
     if (e == cudaErrorNotSupported) return decode_fail(ALJ_ERR_UNSUPPORTED, "decode attention: shape not supported");

@@ -104,6 +104,21 @@ def test_gqa_decode_attention_parity(lib, kv_dtype, Hq, Hkv, D, ctx, start):
     assert synth.normwise_rel_err(out, ref) < 1e-5
 
 
+@pytest.mark.parametrize("kv_dtype,Hq,Hkv,D,ctx,start,pad", [
+    (1, 32, 8, 128, 32768, 0, 0),   # long cache: 171 splits of <= 192 rows on the tensor-core kernel
+    (1, 32, 8, 128, 130, 0, 0),     # two splits of 65 rows: partial TMA box and partial 16-row chunk
+    (1, 24, 8, 128, 999, 7, 0),     # 3 query heads per kv head, ragged start
+    (1, 64, 8, 64, 2049, 0, 0),     # 8 query heads per kv head, head_dim 64
+    (1, 8, 8, 128, 5000, 4000, 0),  # one query head per kv head, window past the start
+    (1, 32, 8, 128, 1000, 0, 4),    # rows 8-byte but not 16-byte aligned: shuffle kernel
+    (0, 16, 4, 64, 2500, 0, 0),     # f32 cache: shuffle kernel
+])
+def test_gqa_decode_attention_kernel_paths(lib, kv_dtype, Hq, Hkv, D, ctx, start, pad):
+    out, ref = _attention_case(lib, kv_dtype, Hq, Hkv, D, ctx, start, seed=ctx + pad, use_fallback_stride=pad > 0)
+    assert synth.max_rel_err(out, ref) < 1e-3
+    assert synth.normwise_rel_err(out, ref) < 1e-5
+
+
 @pytest.mark.parametrize("Hq,Hkv,D,ctx", [(6, 3, 40, 129), (32, 8, 128, 333)])
 def test_gqa_decode_attention_generic_layouts(lib, Hq, Hkv, D, ctx):
     out, ref = _attention_case(lib, 0, Hq, Hkv, D, ctx, 0, seed=ctx, use_fallback_stride=True)
