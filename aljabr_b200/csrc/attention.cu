@@ -241,9 +241,12 @@ constexpr int kChunkRows = 16;
 constexpr int kMaxWarpChunks = (kMaxBoxes * kBoxRows / kChunkRows + kAttnWarps - 1) / kAttnWarps;
 constexpr int kMmaSmemMax = 2 * kMaxBoxes * kBoxRows * 128 * 2 + 1024;   // K + V at head_dim 128, + alignment
 
-struct AttnMmaParams {
-    CUtensorMap kmap;   // bf16 cache viewed as [rows][kv_heads][head_dim / 64][64]
-    CUtensorMap vmap;
+struct KvMaps {
+    CUtensorMap k;      // bf16 cache viewed as [rows][kv_heads][head_dim / 64][64]
+    CUtensorMap v;
+};
+struct AttnMmaParams {  // host side: what one launch of the kernel takes
+    KvMaps maps;
     AttnParams a;
     int cap_rows;       // staged rows per split: a multiple of kBoxRows, >= the longest split
     int merge_smem;     // the split merge copies the partial outputs into shared memory
@@ -448,8 +451,15 @@ __device__ __forceinline__ void merge_splits(const AttnParams& p, int kvh, int G
 }
 
 template <int D, bool PACK>
-__global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const __grid_constant__ AttnMmaParams mp) {
-    const AttnParams& p = mp.a;
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const __grid_constant__ KvMaps maps, const AttnParams p,
+                                                                  const int cap, const int merge_smem) {
+    __shared__ uint64_t s_bar[kMaxBoxes + 1];   // K/V boxes, then the split merge's bulk copy
+    if (threadIdx.x == 0) {   // ahead of the previous kernel's completion
+        prefetch_tensormap(&maps.k);
+        prefetch_tensormap(&maps.v);
+        for (int b = 0; b < kMaxBoxes + 1; ++b) mbar_init(&s_bar[b], 1);
+        fence_mbar_init();
+    }
     pdl_launch_dependents();
     pdl_wait();
     constexpr int NH = D / 64;   // 128-byte halves of a row
@@ -458,7 +468,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const __grid_
     const int kvh = blockIdx.x, split = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = p.q_heads / p.kv_heads;
-    const int cap = mp.cap_rows;
     const int seq_len = p.dev_pos ? *p.dev_pos + 1 : p.seq_len;
     const int active = seq_len - p.start_pos;
     const int c0 = p.start_pos + static_cast<int>(static_cast<long long>(active) * split / p.splits);
@@ -470,7 +479,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const __grid_
     }
 
     extern __shared__ unsigned char smem_raw[];
-    __shared__ uint64_t s_bar[kMaxBoxes + 1];   // K/V boxes, then the split merge's bulk copy
     __shared__ float s_ml[kAttnWarps * 8 * 2];
     __shared__ float s_scale[8];
     __shared__ unsigned int s_last;
@@ -483,10 +491,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const __grid_
     const int role = r < G ? 0 : (PACK && r < 2 * G) ? 1 : 2;
     const int head = role == 0 ? r : role == 1 ? r - G : 0;
     const int partner = role == 0 ? lane + 4 * G : lane - 4 * G;   // PACK: the lane with the other part rows
-    if (threadIdx.x == 0) {   // before the query loads: the fence would wait for them
-        for (int b = 0; b < kMaxBoxes + 1; ++b) mbar_init(&s_bar[b], 1);
-        fence_mbar_init();
-    }
     float qv[KS][4];
     {
         const float* qrow = p.q + static_cast<long long>(kvh * G + head) * D;
@@ -507,8 +511,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const __grid_
             mbar_arrive_expect_tx(&s_bar[b], 2u * NH * kBoxRows * 128u);
             for (int h = 0; h < NH; ++h) {
                 const uint32_t off = static_cast<uint32_t>((h * cap + b * kBoxRows) * 128);
-                tma_load_4d(sk + off, &mp.kmap, 0, h, kvh, c0 + b * kBoxRows, &s_bar[b]);
-                tma_load_4d(sv + off, &mp.vmap, 0, h, kvh, c0 + b * kBoxRows, &s_bar[b]);
+                tma_load_4d(sk + off, &maps.k, 0, h, kvh, c0 + b * kBoxRows, &s_bar[b]);
+                tma_load_4d(sv + off, &maps.v, 0, h, kvh, c0 + b * kBoxRows, &s_bar[b]);
             }
         }
     }
@@ -646,7 +650,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const __grid_
     if (threadIdx.x == 0) s_last = atom_add_acq_rel_gpu(&p.split_counter[kvh], 1u) == static_cast<unsigned int>(p.splits - 1);
     __syncthreads();
     if (!s_last) return;
-    merge_splits<D>(p, kvh, G, mp.merge_smem, stage_f, s_scale, &s_bar[kMaxBoxes]);
+    merge_splits<D>(p, kvh, G, merge_smem != 0, stage_f, s_scale, &s_bar[kMaxBoxes]);
     if (threadIdx.x == 0) p.split_counter[kvh] = 0u;
 }
 
@@ -779,9 +783,9 @@ __global__ void attn_fallback_kernel(const AttnParams p) {
     }
 }
 
-template <typename Params>
-cudaError_t launch_pdl(void (*kernel)(Params), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
-                       const Params& p) {
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                       const Args&... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
@@ -792,7 +796,7 @@ cudaError_t launch_pdl(void (*kernel)(Params), dim3 grid, dim3 block, size_t sme
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kernel, p);
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
 // Shared memory of the bulk split merge: the kv head's partial outputs and
@@ -825,7 +829,7 @@ bool mma_params(const AttnParams& p, AttnMmaParams& mp) {
     const cuuint32_t box[4] = {64, 1, 1, kBoxRows};
     const cuuint32_t es[4] = {1, 1, 1, 1};
     for (int t = 0; t < 2; ++t)
-        if (fn(t == 0 ? &mp.kmap : &mp.vmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(t == 0 ? p.k : p.v),
+        if (fn(t == 0 ? &mp.maps.k : &mp.maps.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(t == 0 ? p.k : p.v),
                dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return false;
@@ -848,7 +852,8 @@ cudaError_t launch_mma(const AttnMmaParams& mp, dim3 grid, cudaStream_t stream, 
     }
     const size_t stage = 2ull * mp.cap_rows * D * 2;
     const size_t smem = (mp.merge_smem ? std::max(stage, merge_bytes(mp.a)) : stage) + 1024;
-    return launch_pdl(attn_mma_kernel<D, PACK>, grid, dim3(kAttnWarps * 32), smem, stream, pdl, mp);
+    return launch_pdl(attn_mma_kernel<D, PACK>, grid, dim3(kAttnWarps * 32), smem, stream, pdl, mp.maps, mp.a,
+                      mp.cap_rows, mp.merge_smem);
 }
 
 cudaError_t dispatch_mma(const AttnMmaParams& mp, dim3 grid, cudaStream_t stream, bool pdl) {

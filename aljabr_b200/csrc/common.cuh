@@ -114,6 +114,10 @@ __device__ __forceinline__ bool wait_flags_sys(const unsigned int* flags, int n,
 }
 // Generic-proxy writes observed above become visible to this thread's later
 // TMA (async-proxy) reads.
+// Fetch a TMA descriptor (a kernel parameter) ahead of its first use.
+__device__ __forceinline__ void prefetch_tensormap(const void* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
 __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
 // Programmatic dependent launch: wait for the producer grid's writes, and let

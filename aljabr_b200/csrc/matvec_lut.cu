@@ -5,11 +5,13 @@
 // NF4 values are 16 arbitrary constants, so a code cannot become a tensor-core
 // operand with bit tricks; the work stays on the CUDA cores and is shaped so
 // that each weight costs ~1.8 instructions:
-//   * a 64 KB table in shared memory maps a code byte b to the float pair
-//     (T[b >> 4], T[b & 15]), 32 copies (entry b, copy c at 256 b + 8 c): lane
-//     l reads copy l, so the 8-byte loads of a half warp hit 16 distinct bank
-//     pairs whatever the bytes are, and one PRMT builds the address
-//     (b << 8 | 8 l) from the code word;
+//   * a 32 KB table in shared memory maps a code byte b to the float pair
+//     (T[b >> 4], T[b & 15]), 16 copies (entry b, copy c at 128 b + 8 c): lane
+//     l reads copy l % 16, so the 8-byte loads of a half warp (the unit in
+//     which 8-byte shared loads are served) hit 16 distinct bank pairs
+//     whatever the bytes are; a PRMT and a shift build the address
+//     (b << 7 | 8 (l % 16)) from the code word.  The 32 KB the table does not
+//     take (against one copy per lane) hold a fourth TMA stage;
 //   * one packed f32x2 FMA per byte multiplies the pair with (x[2i], x[2i+1]);
 //   * rows are dealt out in balanced units of 4 and walked in slabs of up to
 //     32 rows (pair mode: 16 gate + 16 up rows) x chunks of 2048 columns; a
@@ -50,7 +52,8 @@ constexpr int kSlabRows = 32;
 constexpr int kChunkElems = 2048;
 constexpr int kCodeRowBytes = kChunkElems / 2;             // 1024
 constexpr int kXBytes = kChunkElems * 4;                   // 8 KB
-constexpr int kLutBytes = 256 * 32 * 8;                    // 64 KB
+constexpr int kLutCopies = 16;                             // one per lane of a half warp
+constexpr int kLutBytes = 256 * kLutCopies * 8;            // 32 KB
 constexpr int kMaxStages = 4;
 constexpr int kRing = 4;
 constexpr int kSmemMax = 232448;
@@ -106,10 +109,14 @@ __device__ __forceinline__ f2 lds_pair(uint32_t a) {
     asm volatile("ld.shared.b64 %0, [%1];" : "=l"(v) : "r"(a));
     return f2{v};
 }
-__device__ __forceinline__ float4 lds128f(uint32_t a) {
-    float4 v;
-    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
-    return v;
+// Two packed f32x2 operands from 16 bytes of shared memory.
+__device__ __forceinline__ void lds_pairs2(uint32_t a, f2& p0, f2& p1) {
+    asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(p0.v), "=l"(p1.v) : "r"(a));
+}
+__device__ __forceinline__ f2 mul2f(f2 a, f2 b) {
+    f2 r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+    return r;
 }
 __device__ __forceinline__ float lds32f(uint32_t a) {
     float v;
@@ -139,16 +146,35 @@ __device__ __forceinline__ void norm_pass(const P& p, float scale, int idx) {
     for (int i = idx; i < p.total_rows; i += kCW * 32 + 32) p.norm_out[i] = __ldcg(y + i) * scale * p.norm_w[i];
 }
 
+// Row geometry of a launch, read from the parameters once at kernel start
+// (independent loads, one round trip) instead of by each walk step.
+struct SlabGeom {
+    int total_rows, pair, nseg;
+    int row0[3], rows[3];
+};
+__device__ __forceinline__ SlabGeom slab_geom(const LutParams& p) {
+    SlabGeom g;
+    g.total_rows = p.total_rows;
+    g.pair = p.pair;
+    g.nseg = p.nseg;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+        g.row0[i] = p.seg[i].row0;
+        g.rows[i] = p.seg[i].rows;
+    }
+    return g;
+}
+
 struct SlabWalk {
     int u, u_end;
-    __device__ __forceinline__ bool next(const LutParams& p, int& seg, int& su, int& nunits) {
+    __device__ __forceinline__ bool next(const SlabGeom& p, int& seg, int& su, int& nunits) {
         if (u >= u_end) return false;
         seg = 0;
         int seg_end = p.total_rows / kUnit;
         if (!p.pair) {
-            if (p.nseg > 1 && u * kUnit >= p.seg[1].row0) seg = 1;
-            if (p.nseg > 2 && u * kUnit >= p.seg[2].row0) seg = 2;
-            seg_end = (p.seg[seg].row0 + p.seg[seg].rows) / kUnit;
+            if (p.nseg > 1 && u * kUnit >= p.row0[1]) seg = 1;
+            if (p.nseg > 2 && u * kUnit >= p.row0[2]) seg = 2;
+            seg_end = (p.row0[seg] + p.rows[seg]) / kUnit;
         }
         su = u;
         nunits = min(p.pair ? kSlabRows / (2 * kUnit) : kSlabRows / kUnit, min(u_end, seg_end) - u);
@@ -190,12 +216,22 @@ __device__ __forceinline__ void load_rows(const LutSegment& sg, int r0, int nuni
 template <int GROUP>
 __global__ void __launch_bounds__(kThreads, 1) nf4_lut_kernel(const __grid_constant__ LutParams p, int stages) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
+    if (threadIdx.x == (kProducerWarp << 5)) {   // descriptors on their way before the first copies
+        for (int g = 0; g < p.nseg; ++g) {
+            prefetch_tensormap(&p.seg[g].codes8);
+            prefetch_tensormap(&p.seg[g].codes4);
+            prefetch_tensormap(&p.seg[g].abs8);
+            prefetch_tensormap(&p.seg[g].abs4);
+        }
+        prefetch_tensormap(&p.xmap);
+    }
     pdl_launch_dependents();
+    const SlabGeom geo = slab_geom(p);
     const int K = p.K;
     const int nchunks = K / kChunkElems;
     const StageLayout L = stage_layout(GROUP);
     constexpr int kAbsElems = kChunkElems / GROUP;
-    // [0, 64 KB) table | stages (1024-aligned) | ring | misc | barriers
+    // [0, 32 KB) table | stages (1024-aligned) | ring | misc | barriers
     const uint32_t lut_s = smem_u32(smem_raw);
     const uint32_t base = lut_s + kLutBytes;
     const uint32_t stage_s = (base + 1023u) & ~1023u;
@@ -208,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1) nf4_lut_kernel(const __grid_const
     uint64_t* rempty = rfull + kRing;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int units = p.total_rows / kUnit;
+    const int units = geo.total_rows / kUnit;
     const int u_begin = static_cast<int>(static_cast<long long>(units) * blockIdx.x / gridDim.x);
     const int u_end = static_cast<int>(static_cast<long long>(units) * (blockIdx.x + 1) / gridDim.x);
 
@@ -232,7 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1) nf4_lut_kernel(const __grid_const
             uint32_t ph = 0;
             bool alive = true;
             bool x_waited = false;
-            while (alive && walk.next(p, seg, su, nunits)) {
+            while (alive && walk.next(geo, seg, su, nunits)) {
                 const int rows = nunits * kUnit * (p.pair ? 2 : 1);
                 for (int c = 0; c < nchunks; ++c) {
                     if (!mbar_wait(&empty[s], ph ^ 1u)) {
@@ -275,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1) nf4_lut_kernel(const __grid_const
         SlabWalk walk{u_begin, u_end};
         int seg, su, nunits, sl = 0;
         float sq = 0.0f;
-        while (walk.next(p, seg, su, nunits)) {
+        while (walk.next(geo, seg, su, nunits)) {
             const int b = sl % kRing;
             const bool ok = __all_sync(0xffffffffu, mbar_wait(&rfull[b], (sl / kRing) & 1));
             if (ok) {
@@ -371,17 +407,20 @@ __global__ void __launch_bounds__(kThreads, 1) nf4_lut_kernel(const __grid_const
 
     // ---------------------------------------------------------------- consumers
     {
-        // Byte-pair table, 32 copies: entry b, copy c at 256 b + 8 c.
+        // Byte-pair table, 16 copies: entry b, copy c at 128 b + 8 c.
         float2* lut = reinterpret_cast<float2*>(smem_raw);
-        for (int e = threadIdx.x; e < 256 * 32; e += kConsumers) {
-            const int b = e >> 5;
-            lut[e] = make_float2(kNf4[b >> 4], kNf4[b & 15]);
+        // lane l holds T[l % 16]; the pair of entry b comes from two shuffles
+        const float tl = kNf4[lane & 15];
+        for (int e = threadIdx.x; e < 256 * kLutCopies; e += kConsumers) {
+            const int b = e >> 4;
+            lut[e] = make_float2(__shfl_sync(0xffffffffu, tl, b >> 4), __shfl_sync(0xffffffffu, tl, b & 15));
         }
         named_bar(1, kConsumers);
     }
     const int q = warp & 3;                 // column quarter: columns [512 q, 512 q + 512) of a chunk
     const int rg = warp >> 2;               // rows rg, rg + 4, ... of the slab
-    const uint32_t lane8 = static_cast<uint32_t>(lane) * 8u;
+    // table address (b << 7 | (lane % 16) << 3) = PRMT(b << 8 | (lane % 16) << 4) >> 1
+    const uint32_t lane16 = static_cast<uint32_t>(lane & 15) * 16u;
     const uint32_t code_off = q * 256 + lane * 8;                           // this lane's 8 code bytes
     const uint32_t abs_off = L.abs_off + ((q * 512 + lane * 16) / GROUP) * 4;
     uint32_t xoff[4];                                                       // swizzled x granules
@@ -394,41 +433,60 @@ __global__ void __launch_bounds__(kThreads, 1) nf4_lut_kernel(const __grid_const
         }
     }
 
+    constexpr int kAbsRowBytes = 4 * (kChunkElems / GROUP);
     SlabWalk walk{u_begin, u_end};
     int seg, su, nunits, s = 0, sl = 0;
     uint32_t ph = 0;
-    while (walk.next(p, seg, su, nunits)) {
+    while (walk.next(geo, seg, su, nunits)) {
         // slab rows with data: pair mode holds gate rows [0, 4n) and up rows [16, 16 + 4n)
         const int valid = nunits * kUnit;
+        const bool all_live = p.pair ? rg + 12 < valid : rg + 28 < valid;   // warp-uniform
         float acc[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
         for (int c = 0; c < nchunks; ++c) {
             if (__all_sync(0xffffffffu, mbar_wait(&full[s], ph))) {
                 const uint32_t st = stage_s + s * L.bytes;
-                float4 xv[4];
+                // x of this lane's 16 columns as 8 packed pairs, loaded once for all rows
+                f2 xp[8];
 #pragma unroll
-                for (int k = 0; k < 4; ++k) xv[k] = lds128f(st + xoff[k]);
+                for (int k = 0; k < 4; ++k) lds_pairs2(st + xoff[k], xp[2 * k], xp[2 * k + 1]);
+                const uint32_t code_base = st + rg * kCodeRowBytes + code_off;      // row rg; row rg + 4j at + 4096 j
+                const uint32_t abs_base = st + abs_off + rg * kAbsRowBytes;
+                // one row: 8 code bytes -> 8 table pairs -> 8 packed multiply-adds
+                auto row_dot = [&](uint2 w, float am, float a) {
+                    f2 t[8];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int r = rg + 4 * j;
-                    const bool live = p.pair ? ((r & 15) < valid) : (r < valid);
-                    if (live) {
-                        const uint2 w = lds64u(st + r * kCodeRowBytes + code_off);
-                        const float am = lds32f(st + abs_off + r * L.abs_row_bytes);
-                        f2 A = mk2(0.0f, 0.0f), B = mk2(0.0f, 0.0f);
+                    for (int m = 0; m < 8; ++m) {
+                        const uint32_t word = m < 4 ? w.x : w.y;
+                        t[m] = lds_pair(lut_s + (__byte_perm(word, lane16, 0x5504u | (static_cast<uint32_t>(m & 3) << 4)) >> 1));
+                    }
+                    f2 A = mul2f(t[0], xp[0]), B = mul2f(t[1], xp[1]);
 #pragma unroll
-                        for (int m = 0; m < 8; ++m) {
-                            const uint32_t word = m < 4 ? w.x : w.y;
-                            const uint32_t sel = 0x5504u | (static_cast<uint32_t>(m & 3) << 4);
-                            const f2 t = lds_pair(lut_s + __byte_perm(word, lane8, sel));
-                            const float4& xx = xv[m >> 1];
-                            const f2 xp = (m & 1) ? mk2(xx.z, xx.w) : mk2(xx.x, xx.y);
-                            if (m & 1) B = fma2(t, xp, B);
-                            else A = fma2(t, xp, A);
-                        }
-                        const f2 t2 = add2(A, B);
-                        acc[j] = fmaf(am, lo(t2) + hi(t2), acc[j]);
+                    for (int m = 2; m < 8; m += 2) {
+                        A = fma2(t[m], xp[m], A);
+                        B = fma2(t[m + 1], xp[m + 1], B);
+                    }
+                    const f2 t2 = add2(A, B);
+                    return fmaf(am, lo(t2) + hi(t2), a);
+                };
+                if (all_live) {
+                    // the next row's code word is read before this row's table loads
+                    uint2 w = lds64u(code_base);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const uint2 wj = w;
+                        if (j < 7) w = lds64u(code_base + (j + 1) * 4 * kCodeRowBytes);
+                        const float am = lds32f(abs_base + j * 4 * kAbsRowBytes);
+                        acc[j] = row_dot(wj, am, acc[j]);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const int r = rg + 4 * j;
+                        if (p.pair ? ((r & 15) < valid) : (r < valid))
+                            acc[j] = row_dot(lds64u(code_base + j * 4 * kCodeRowBytes),
+                                             lds32f(abs_base + j * 4 * kAbsRowBytes), acc[j]);
                     }
                 }
             }
