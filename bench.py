@@ -427,7 +427,7 @@ def run_extra(args, dev, stream, sh, l2, which=None, reps=200):
         alg = 2 * kvb + 8 * Hq * D
         out["gqa_decode_attention_ctx4096_bf16"] = {"GB/s": round(alg / (ms * 1e-3) / 1e9, 1),
                                                     "us_per_call": round(ms * 1e3, 3), "algorithmic_bytes": alg,
-                                                    "launches_per_call": 2}
+                                                    "launches_per_call": 1}
 
     def c5_section():
         # Batched NF4 on the per-GPU tensor-parallel shard (TP 8) of one
