@@ -68,6 +68,17 @@ struct MatvecParams {
     float norm_eps;
     float* norm_partials;
     unsigned int* norm_counter;
+    // Deferred RMSNorm (NF4 table kernel only).  norm_defer: instead of the
+    // last-CTA pass, write norm_out = y * norm_w (unscaled) and this CTA's sum
+    // of squares of y to norm_partials[CTA]; the consuming launch applies the
+    // scale.  in_parts (consuming side): x is such an unscaled vector whose
+    // producer left in_nparts partials; every output is multiplied by
+    // rsqrt(sum(partials) / in_rows + in_eps) before the epilogue.
+    int norm_defer;
+    const float* in_parts;
+    int in_nparts;
+    int in_rows;
+    float in_eps;
     // Optional L2 prefetch of the weights the following launch reads (each CTA
     // its 1/grid share, after its own copies are issued).
     const void* prefetch;
@@ -87,6 +98,7 @@ cudaError_t launch_matvec_mma(int fmt, const MatvecParams& p, cudaStream_t strea
 // NF4 table path (K a multiple of 2048, group 64 or 128); picked second.
 bool matvec_lut_supported(int fmt, int K, int group);
 cudaError_t launch_matvec_lut(int fmt, const MatvecParams& p, cudaStream_t stream, bool pdl);
+int matvec_lut_grid(int total_rows);   // CTAs (and norm partials) of a table-kernel launch
 
 cudaError_t launch_dequant(int fmt, float* dst, const uint8_t* src, const float* absmax, int64_t numel,
                            int group, cudaStream_t stream);

@@ -282,6 +282,7 @@ struct DecodeModel {
     void *kc = nullptr, *vc = nullptr; // [layers][max_ctx][hkv*D]
     float *x, *xn, *q, *k, *vv, *att_l, *att, *delta_l, *delta, *h_l, *hh, *logits_l, *logits, *scratch;
     float* norm_partials = nullptr;    // [matvec_max_ctas()] per-CTA sums of squares
+    bool defer_norm = false;           // RMSNorm scale applied by the consuming matvec (one GPU)
     unsigned int* norm_counter = nullptr;
     float* act_base = nullptr;
     int* io = nullptr;                 // device {pos, token, argmax}
@@ -319,9 +320,13 @@ DecodeModel* find(unsigned long long h) {
 }
 
 // One NF4 matvec launch over 1-3 row segments sharing x.
+// With m.defer_norm (one GPU, every K on the NF4 table kernel), a launch
+// given norm_out leaves x * norm_w and its per-CTA sums of squares, and
+// `scaled_x` marks a launch whose x is such a vector: it applies the
+// RMSNorm scale to its outputs from those partials.
 cudaError_t matvec(const DecodeModel& m, const Nf4* ws, float* const* ys, const int* rows, int n, const float* x,
                    int K, int epilogue, const float* residual, float* norm_out, const float* norm_w,
-                   const TpLink* tpl = nullptr) {
+                   const TpLink* tpl = nullptr, bool scaled_x = false) {
     MatvecParams p = {};
     if (tpl) {
         p.tpl = *tpl;
@@ -347,6 +352,13 @@ cudaError_t matvec(const DecodeModel& m, const Nf4* ws, float* const* ys, const 
         p.norm_eps = m.eps;
         p.norm_partials = m.norm_partials;
         p.norm_counter = m.norm_counter;
+        p.norm_defer = m.defer_norm ? 1 : 0;
+    }
+    if (scaled_x && m.defer_norm) {
+        p.in_parts = m.norm_partials;
+        p.in_nparts = matvec_lut_grid(m.H);   // the producing o / down launch has H rows
+        p.in_rows = m.H;
+        p.in_eps = m.eps;
     }
     return launch_matvec(FMT_NF4, p, m.stream, true);
 }
@@ -378,7 +390,8 @@ cudaError_t record_step(DecodeModel& m) {
             const Nf4 ws[3] = {w[W_Q], w[W_K], w[W_V]};
             float* ys[3] = {m.q, m.k, m.vv};
             const int rows[3] = {m.hq * D, m.hkv * D, m.hkv * D};
-            REC(matvec(m, ws, ys, rows, 3, m.xn, m.H, EPI_STORE, nullptr, nullptr, nullptr));
+            // layer 0's x comes normed from the embedding kernel
+            REC(matvec(m, ws, ys, rows, 3, m.xn, m.H, EPI_STORE, nullptr, nullptr, nullptr, nullptr, l > 0));
         }
         // RoPE on q and k, KV store (GgufDecodePass.java:333-362)
         REC(launch_small(rope_store_kernel, std::max(1, ((m.hq + m.hkv) * D / 2 + 255) / 256), 256, m.stream, m.q,
@@ -423,7 +436,7 @@ cudaError_t record_step(DecodeModel& m) {
             const Nf4 ws[2] = {w[W_GATE], w[W_UP]};
             float* ys[2] = {m.T > 1 ? m.h_l : m.hh, nullptr};
             const int rows[2] = {m.f, m.f};
-            REC(matvec(m, ws, ys, rows, 2, m.xn, m.H, EPI_SWIGLU_PAIR, nullptr, nullptr, nullptr));
+            REC(matvec(m, ws, ys, rows, 2, m.xn, m.H, EPI_SWIGLU_PAIR, nullptr, nullptr, nullptr, nullptr, true));
         }
         if (m.T > 1) RECN(g_nccl.allGather(m.h_l, m.hh, m.f, ncclFloat, m.comm, m.stream));
         {   // down-proj + residual (GgufDecodePass.java:504-511), then the next layer's norm
@@ -445,7 +458,7 @@ cudaError_t record_step(DecodeModel& m) {
         const Nf4 ws[1] = {m.head};
         float* ys[1] = {m.T > 1 ? m.logits_l : m.logits};
         const int rows[1] = {m.v};
-        REC(matvec(m, ws, ys, rows, 1, m.xn, m.H, EPI_STORE, nullptr, nullptr, nullptr));
+        REC(matvec(m, ws, ys, rows, 1, m.xn, m.H, EPI_STORE, nullptr, nullptr, nullptr, nullptr, true));
     }
     if (m.T > 1) RECN(g_nccl.allGather(m.logits_l, m.logits, m.v, ncclFloat, m.comm, m.stream));
     REC(launch_small(argmax_kernel, std::max(1, std::min(sms, (m.V + 1023) / 1024)), 1024, m.stream,
@@ -743,7 +756,12 @@ int aljabr_blackwell_decode_model_create(const int* dims, float eps, float rope_
     m->w.resize(m->layers);
     m->layer_set.assign(m->layers, false);
     m->splits = attention_splits(m->max_ctx, m->hkv, sm_count_for_current_device());
-    if (T > 1) m->splits = std::max(m->splits, 2);   // the tensor-parallel push lives in the combine kernel
+    if (T > 1) m->splits = std::max(m->splits, 2);   // the tensor-parallel push lives in the split merge
+    // The RMSNorm scale moves to the consuming matvec when every launch that
+    // produces or consumes a normed vector runs on the NF4 table kernel.
+    m->defer_norm = T == 1 && matvec_lut_supported(FMT_NF4, m->H, m->group) &&
+                    matvec_lut_supported(FMT_NF4, m->Hq * m->D, m->group) &&
+                    matvec_lut_supported(FMT_NF4, m->F, m->group);
 
     auto ok = [&](cudaError_t e) { return e == cudaSuccess; };
     const size_t kvb = static_cast<size_t>(m->layers) * m->kv_layer_elems() * m->kv_elem();

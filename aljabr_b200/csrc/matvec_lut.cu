@@ -87,6 +87,11 @@ struct alignas(64) LutParams {
     float norm_eps;
     float* norm_partials;
     unsigned int* norm_counter;
+    int norm_defer;
+    const float* in_parts;
+    int in_nparts;
+    int in_rows;
+    float in_eps;
     const uint8_t* prefetch;
     size_t prefetch_bytes;
     TpLink tpl;
@@ -248,18 +253,26 @@ __global__ void __launch_bounds__(kThreads, 1) nf4_lut_kernel(const __grid_const
     const int u_begin = static_cast<int>(static_cast<long long>(units) * blockIdx.x / gridDim.x);
     const int u_end = static_cast<int>(static_cast<long long>(units) * (blockIdx.x + 1) / gridDim.x);
 
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < stages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kCW);
+    // The producer warp initialises the barriers and goes straight on to its
+    // first copies; the other warps wait on named barrier 3 (all threads)
+    // before they touch a barrier.
+    if (warp == kProducerWarp) {
+        if (lane == 0) {
+            for (int s = 0; s < stages; ++s) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], kCW);
+            }
+            for (int b = 0; b < kRing; ++b) {
+                mbar_init(&rfull[b], kCW);
+                mbar_init(&rempty[b], 1);
+            }
+            fence_mbar_init();
         }
-        for (int b = 0; b < kRing; ++b) {
-            mbar_init(&rfull[b], kCW);
-            mbar_init(&rempty[b], 1);
-        }
-        fence_mbar_init();
+        __syncwarp();
+        named_bar_arrive(3, kThreads);
+    } else {
+        named_bar(3, kThreads);
     }
-    __syncthreads();
 
     if (warp == kProducerWarp) {
         if (lane == 0) {
@@ -308,6 +321,13 @@ __global__ void __launch_bounds__(kThreads, 1) nf4_lut_kernel(const __grid_const
 
     if (warp == kEpilogueWarp) {
         pdl_wait();
+        // deferred RMSNorm of x: its scale from the producer's partials (fixed order)
+        float in_s = 1.0f;
+        if (p.in_parts) {
+            float part = 0.0f;
+            for (int b = lane; b < p.in_nparts; b += 32) part += __ldcg(p.in_parts + b);
+            in_s = 1.0f / sqrtf(warp_sum(part) / static_cast<float>(p.in_rows) + p.in_eps);
+        }
         SlabWalk walk{u_begin, u_end};
         int seg, su, nunits, sl = 0;
         float sq = 0.0f;
@@ -320,6 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1) nf4_lut_kernel(const __grid_const
                 float acc = 0.0f;
 #pragma unroll
                 for (int q = 0; q < 4; ++q) acc += red[(b * kCW + 4 * i + q) * 8 + j];
+                acc *= in_s;
                 if (p.pair) {
                     const float up = __shfl_down_sync(0xffffffffu, acc, 16);
                     if (lane < nunits * kUnit) {
@@ -342,6 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1) nf4_lut_kernel(const __grid_const
                     } else {
                         sg.y[lrow] = out;
                     }
+                    if (p.norm_defer) p.norm_out[lrow] = out * p.norm_w[lrow];
                     sq = fmaf(out, out, sq);
                 }
             }
@@ -376,7 +398,11 @@ __global__ void __launch_bounds__(kThreads, 1) nf4_lut_kernel(const __grid_const
                 if (lane == 0) *p.tpl.counter = 0u;
             }
         }
-        if (p.norm_out) {
+        if (p.norm_out && p.norm_defer) {
+            // the consuming launch sums the partials and applies the scale
+            const float cta = warp_sum(sq);
+            if (lane == 0) p.norm_partials[blockIdx.x] = cta;
+        } else if (p.norm_out) {
             // Deterministic RMSNorm of the whole output: per-CTA partials in
             // fixed order; the last CTA to arrive computes the scale, and all of
             // its consumer warps plus this warp write norm_out.
@@ -530,7 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1) nf4_lut_kernel(const __grid_const
         if (lane == 0) mbar_arrive(&rfull[b]);
         ++sl;
     }
-    if (p.norm_out) {
+    if (p.norm_out && !p.norm_defer) {
         named_bar(2, kCW * 32 + 32);
         if (misc[1] != 0.0f) norm_pass(p, misc[0], threadIdx.x);
     }
@@ -554,6 +580,10 @@ size_t smem_bytes(int group, int stages) {
 }
 
 }  // namespace
+
+int matvec_lut_grid(int total_rows) {
+    return std::max(1, std::min(sm_count_for_current_device(), total_rows / kUnit));
+}
 
 bool matvec_lut_supported(int fmt, int K, int group) {
     if (fmt != FMT_NF4 || K <= 0 || K % kChunkElems != 0 || (group != 64 && group != 128)) return false;
@@ -582,6 +612,14 @@ cudaError_t launch_matvec_lut(int fmt, const MatvecParams& mp, cudaStream_t stre
     p.norm_eps = mp.norm_eps;
     p.norm_partials = mp.norm_partials;
     p.norm_counter = mp.norm_counter;
+    p.norm_defer = mp.norm_defer;
+    p.in_parts = mp.in_parts;
+    p.in_nparts = mp.in_nparts;
+    p.in_rows = mp.in_rows;
+    p.in_eps = mp.in_eps;
+    if ((p.norm_defer && (!p.norm_out || !p.norm_w || !p.norm_partials || mp.nseg != 1)) ||
+        (p.in_parts && (p.in_nparts <= 0 || p.in_rows <= 0)))
+        return cudaErrorInvalidValue;
     p.prefetch = static_cast<const uint8_t*>(mp.prefetch);
     p.prefetch_bytes = mp.prefetch_bytes;
     p.tpl = mp.tpl;
@@ -628,8 +666,7 @@ cudaError_t launch_matvec_lut(int fmt, const MatvecParams& mp, cudaStream_t stre
         if (e != cudaSuccess) return e;
         done = true;
     }
-    const int units = mp.total_rows / kUnit;
-    const int grid = std::max(1, std::min(sm_count_for_current_device(), units));
+    const int grid = matvec_lut_grid(mp.total_rows);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
