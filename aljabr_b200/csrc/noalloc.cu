@@ -16,10 +16,12 @@
 // that device (so make that first call before any stream capture).  The
 // entry point calls no cudaMalloc, cudaFree, stream or allocating library
 // routine.  All calls share the array and it keeps the last call's
-// contents; every split writes its whole slot before the merge reads it, so
-// nothing needs clearing, but calls whose kernels overlap on the GPU (on
-// different streams, or from several threads) race on it and must be
-// ordered by the caller.
+// contents.  Every split writes its whole slot before the merge reads it;
+// the only words that must start at zero are the per-kv-head arrival
+// counters at the head of the array, which each call clears on its stream
+// (cudaMemsetAsync) before its kernel runs.  Calls whose kernels overlap on
+// the GPU (on different streams, or from several threads) race on the array
+// and must be ordered by the caller.
 #include "common.cuh"
 
 #include <mutex>
@@ -98,6 +100,11 @@ extern "C" int aljabr_blackwell_decode_attention_noalloc(float* out, const float
                                "1,048,576-float static scratch of "
                                "aljabr_blackwell_decode_attention_noalloc");
         attention_bind_scratch(p, scratch);
+        if (cudaMemsetAsync(p.split_counter, 0, static_cast<size_t>(q_heads) * sizeof(unsigned int),
+                            static_cast<cudaStream_t>(stream)) != cudaSuccess) {
+            cudaGetLastError();
+            return decode_fail(ALJ_ERR_CUDA, "clearing the split counters failed");
+        }
     }
     const cudaError_t e = launch_attention(p, static_cast<cudaStream_t>(stream), false);
     if (e == cudaErrorNotSupported) return decode_fail(ALJ_ERR_UNSUPPORTED, "decode attention: shape not supported");

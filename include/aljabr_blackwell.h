@@ -206,14 +206,15 @@ int aljabr_blackwell_gemm_nf4_dev(int nseg, float* const* y, const int* ldy, con
  * reference: its attention runs on the host and needs no device scratch.
  * The split partials live in a static device array of 1,048,576 floats
  * (4 MiB) compiled into the library; shapes whose scratch,
- * q_heads * splits * (head_dim + 2) floats, exceeds it are rejected with
- * ALJ_ERR_BAD_DIMS.  Calls no cudaMalloc / cudaFree and needs no prior
+ * q_heads * splits * (head_dim + 2) floats plus one counter word per query
+ * head (rounded up to 4), exceeds it are rejected with ALJ_ERR_BAD_DIMS.  Calls no cudaMalloc / cudaFree and needs no prior
  * aljabr_blackwell_init: it runs on the current device and on `stream`
  * (NULL = the legacy default stream).  The first call on a device looks up
  * the array's device address (cudaGetSymbolAddress) with that device
  * current; make it before any stream capture.  All calls share the array,
  * so calls whose kernels may overlap (other streams, other threads) race
- * and must be ordered by the caller.  Nothing needs to start at zero. */
+ * and must be ordered by the caller.  The split merge's arrival counters
+ * must start at zero; each call clears them on `stream` before its kernel. */
 int aljabr_blackwell_decode_attention_noalloc(float* out, const float* q, const void* k_cache,
                                               const void* v_cache, int kv_dtype, int cache_head_stride,
                                               int kv_heads, int q_heads, int head_dim, int seq_len,
