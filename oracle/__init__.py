@@ -5,8 +5,8 @@ Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
 legs use this package, and only as the checker or the timed CPU baseline.
 The product path (``aljabr_b200``) never imports it.
 
-Parity status: Q4_0 / Q8_0 / fp16 / attention restatements are pinned by the
-reference's known-answer tests (``tests/golden/``).  The NF4 fp32 GEMV (Apple
+Parity status: Q4_0 / Q8_0 / Q4_K / Q6_K / fp16 / attention restatements are
+pinned by the reference's known-answer tests (``tests/golden/``).  The NF4 fp32 GEMV (Apple
 Accelerate ``cblas_sgemv`` in the reference) and the NF4 quantizer (external
 project) are "parity unpinned"; NF4 dequantisation is pinned by its table and
 nibble order.
@@ -26,7 +26,8 @@ _LIB = os.path.join(_HERE, "liboracle.so")
 
 CFLAGS = ["-O2", "-std=c11", "-fPIC", "-shared", "-ffp-contract=off", "-fno-fast-math", "-pthread"]
 
-Q4_0, Q8_0, NF4 = 2, 8, 100
+Q4_0, Q8_0, Q4_K, Q6_K, NF4 = 2, 8, 12, 14, 100
+K_BLOCK_BYTES = {Q4_K: 144, Q6_K: 210}   # per 256-value super-block
 
 
 def build(force: bool = False) -> str:
@@ -77,6 +78,11 @@ def _declare(L):
         getattr(L, name).restype = _f
     L.orc_matvec_q4_0.argtypes = [_p, _p, _p, _i, _i, _i]
     L.orc_matvec_q8_0.argtypes = [_p, _p, _p, _i, _i, _i, _i]
+    for name in ("orc_dot_row_q4_k", "orc_dot_row_q6_k"):
+        getattr(L, name).argtypes = [_p, _i, _p]
+        getattr(L, name).restype = _f
+    L.orc_dequantize_k_row.argtypes = [_i, _p, _i, _p]
+    L.orc_matvec_k.argtypes = [_i, _p, _p, _p, _i, _i, _i]
     L.orc_matvec_nf4.argtypes = [_p, _p, _p, _p, _i, _i, _i, _p, _i]
     L.orc_matvec_f64.argtypes = [_i, _p, _p, _p, _p, _i, _i, _i, _i]
     L.orc_gqa_decode_attention.argtypes = [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _f]
@@ -212,6 +218,28 @@ def matvec_q8_0(w, x, N: int, vector_order: bool = True, threads: int = 1) -> np
     w, x = _c(w, np.uint8), _c(x, np.float32)
     y = np.empty(N, dtype=np.float32)
     lib().orc_matvec_q8_0(_ptr(w), _ptr(x), _ptr(y), x.size, N, int(vector_order), threads)
+    return y
+
+
+def dot_row_k(kind: int, row, x) -> float:
+    """One Q4_K / Q6_K row dot in the reference's float order."""
+    row, x = _c(row, np.uint8), _c(x, np.float32)
+    fn = lib().orc_dot_row_q4_k if kind == Q4_K else lib().orc_dot_row_q6_k
+    return fn(_ptr(row), x.size, _ptr(x))
+
+
+def dequantize_k_row(kind: int, row, columns: int) -> np.ndarray:
+    """The values of one Q4_K / Q6_K row (fp64, from the element formulas)."""
+    row = _c(row, np.uint8)
+    out = np.empty(columns, dtype=np.float64)
+    lib().orc_dequantize_k_row(kind, _ptr(row), columns, _ptr(out))
+    return out
+
+
+def matvec_k(kind: int, w, x, N: int, threads: int = 1) -> np.ndarray:
+    w, x = _c(w, np.uint8), _c(x, np.float32)
+    y = np.empty(N, dtype=np.float32)
+    lib().orc_matvec_k(kind, _ptr(w), _ptr(x), _ptr(y), x.size, N, threads)
     return y
 
 

@@ -296,6 +296,159 @@ float orc_dot_row_q8_0_vector(const uint8_t* row, int columns, const float* x) {
 }
 
 /* ------------------------------------------------------------------------ */
+/* K-quants: 256-value super-blocks.
+ * Q4_K (144 B): fp16 d, fp16 dmin, 12 bytes of packed 6-bit (scale, min)
+ * pairs for 8 sub-blocks of 32, 128 bytes of nibbles; the 64 values of
+ * chunk j take the low nibbles (sub-block 2j) then the high nibbles
+ * (sub-block 2j+1) of bytes [32j, 32j+32).  value = d*scale*q - dmin*min.
+ * Q6_K (210 B): ql[128] low nibbles, qh[64] two-bit high parts, int8
+ * scales[16] (one per 16 values), fp16 d at byte 208.  In each 128-value
+ * half h, value 32k + i (k < 4, i < 32) is ql[64h + 32(k&1) + i] nibble
+ * (k >> 1) with bits 2k..2k+1 of qh[32h + i] on top, minus 32, times
+ * d * scales[8h + 2k + i/16]. */
+
+/* RT/GgufKQuantLayout.java:37-50 (scaleMinK4PackedCode) and :60-66 (scaleK4Packed). */
+static void q4k_scale_min(const uint8_t* sc, int index, int* scale, int* min) {
+    if (index < 4) {
+        *scale = sc[index] & 63;
+        *min = sc[index + 4] & 63;
+    } else {
+        *scale = (sc[index + 4] & 0x0F) | ((sc[index - 4] >> 6) << 4);
+        *min = (sc[index + 4] >> 4) | ((sc[index] >> 6) << 4);
+    }
+}
+
+/* RT/GgufQ4RawDot.java:38-141 (dotRowQ4K): per 64-value chunk two 8-wide
+ * left-to-right product sums per step, the vector sums only where a min is
+ * non-zero, then sum += d1*dot1 + d2*dot2 and the min corrections. */
+float orc_dot_row_q4_k(const uint8_t* row, int columns, const float* x) {
+    float sum = 0.0f;
+    for (int b = 0; b < columns / 256; b++) {
+        const uint8_t* blk = row + (int64_t)b * 144;
+        const float d = orc_f16_to_f32(le16(blk));
+        const float dmin = orc_f16_to_f32(le16(blk + 2));
+        const int block_mins = dmin != 0.0f;
+        const uint8_t* qs = blk + 16;
+        const float* v = x + (int64_t)b * 256;
+        for (int j = 0; j < 4; j++) {
+            int s1, m1, s2, m2;
+            q4k_scale_min(blk + 4, 2 * j, &s1, &m1);
+            q4k_scale_min(blk + 4, 2 * j + 1, &s2, &m2);
+            const float d1 = d * (float)s1, d2 = d * (float)s2;
+            const int min1 = block_mins ? m1 : 0, min2 = block_mins ? m2 : 0;
+            const int has1 = block_mins && min1 != 0, has2 = block_mins && min2 != 0;
+            float vs1 = 0.0f, vs2 = 0.0f, dot1 = 0.0f, dot2 = 0.0f;
+            for (int i = 0; i < 32; i += 8) {
+                float t1 = (float)(qs[i] & 0x0F) * v[i];
+                float t2 = (float)((qs[i] >> 4) & 0x0F) * v[32 + i];
+                for (int k = 1; k < 8; k++) {
+                    t1 = t1 + (float)(qs[i + k] & 0x0F) * v[i + k];
+                    t2 = t2 + (float)((qs[i + k] >> 4) & 0x0F) * v[32 + i + k];
+                }
+                dot1 += t1;
+                dot2 += t2;
+                if (has1) {
+                    float u = v[i];
+                    for (int k = 1; k < 8; k++) u = u + v[i + k];
+                    vs1 += u;
+                }
+                if (has2) {
+                    float u = v[32 + i];
+                    for (int k = 1; k < 8; k++) u = u + v[32 + i + k];
+                    vs2 += u;
+                }
+            }
+            sum += d1 * dot1 + d2 * dot2;
+            if (has1) sum -= dmin * (float)min1 * vs1;
+            if (has2) sum -= dmin * (float)min2 * vs2;
+            qs += 32;
+            v += 64;
+        }
+    }
+    return sum;
+}
+
+/* RT/GgufQ6RawDot.java:403-513 (dotRowQ6KHalf): 16 values of each of the
+ * four 32-value quarters of a half, 8-wide left-to-right product sums. */
+static float q6k_half(const uint8_t* ql, const uint8_t* qh, const float* v, int off,
+                      float s1, float s2, float s3, float s4) {
+    float dot1 = 0.0f, dot2 = 0.0f, dot3 = 0.0f, dot4 = 0.0f;
+    for (int i = off; i < off + 16; i += 8) {
+        float t[4] = {0, 0, 0, 0};
+        for (int k = 0; k < 8; k++) {
+            const int a = ql[i + k], c = ql[32 + i + k], h = qh[i + k];
+            const float p1 = (float)(((a & 0x0F) | ((h & 3) << 4)) - 32) * v[i + k];
+            const float p2 = (float)(((c & 0x0F) | (((h >> 2) & 3) << 4)) - 32) * v[32 + i + k];
+            const float p3 = (float)(((a >> 4) | (((h >> 4) & 3) << 4)) - 32) * v[64 + i + k];
+            const float p4 = (float)(((c >> 4) | (((h >> 6) & 3) << 4)) - 32) * v[96 + i + k];
+            if (k == 0) { t[0] = p1; t[1] = p2; t[2] = p3; t[3] = p4; }
+            else { t[0] = t[0] + p1; t[1] = t[1] + p2; t[2] = t[2] + p3; t[3] = t[3] + p4; }
+        }
+        dot1 += t[0];
+        dot2 += t[1];
+        dot3 += t[2];
+        dot4 += t[3];
+    }
+    return s1 * dot1 + s2 * dot2 + s3 * dot3 + s4 * dot4;
+}
+
+/* RT/GgufQ6RawDot.java:77-133 (dotRowQ6KBlock). */
+static float q6k_block(const uint8_t* blk, const float* v) {
+    const float d = orc_f16_to_f32(le16(blk + 208));
+    const int8_t* sc = (const int8_t*)(blk + 192);
+    const float s0 = q6k_half(blk, blk + 128, v, 0, d * sc[0], d * sc[2], d * sc[4], d * sc[6]);
+    const float s1 = q6k_half(blk, blk + 128, v, 16, d * sc[1], d * sc[3], d * sc[5], d * sc[7]);
+    const float s2 = q6k_half(blk + 64, blk + 160, v + 128, 0, d * sc[8], d * sc[10], d * sc[12], d * sc[14]);
+    const float s3 = q6k_half(blk + 64, blk + 160, v + 128, 16, d * sc[9], d * sc[11], d * sc[13], d * sc[15]);
+    return s0 + s1 + s2 + s3;
+}
+
+/* RT/GgufQ6RawDot.java:33-75 (dotRowQ6K): four running block sums, then the tail. */
+float orc_dot_row_q6_k(const uint8_t* row, int columns, const float* x) {
+    const int blocks = columns / 256;
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+    int b = 0;
+    for (; b <= blocks - 4; b += 4) {
+        a0 += q6k_block(row + (int64_t)b * 210, x + (int64_t)b * 256);
+        a1 += q6k_block(row + (int64_t)(b + 1) * 210, x + (int64_t)(b + 1) * 256);
+        a2 += q6k_block(row + (int64_t)(b + 2) * 210, x + (int64_t)(b + 2) * 256);
+        a3 += q6k_block(row + (int64_t)(b + 3) * 210, x + (int64_t)(b + 3) * 256);
+    }
+    float sum = a0 + a1 + a2 + a3;
+    for (; b < blocks; b++) sum += q6k_block(row + (int64_t)b * 210, x + (int64_t)b * 256);
+    return sum;
+}
+
+/* Values of one K-quant row (element formulas above), for fp64 sums and tests. */
+void orc_dequantize_k_row(int type, const uint8_t* row, int columns, double* out) {
+    for (int b = 0; b < columns / 256; b++) {
+        double* o = out + (int64_t)b * 256;
+        if (type == ORC_Q4_K) {
+            const uint8_t* blk = row + (int64_t)b * 144;
+            const double d = orc_f16_to_f32(le16(blk)), dmin = orc_f16_to_f32(le16(blk + 2));
+            for (int e = 0; e < 256; e++) {
+                const int j = e / 64, t = e % 64, sb = 2 * j + (t >= 32);
+                const int byte = blk[16 + 32 * j + (t & 31)];
+                const int q = t < 32 ? (byte & 15) : (byte >> 4);
+                int sc, mn;
+                q4k_scale_min(blk + 4, sb, &sc, &mn);
+                o[e] = d * sc * q - dmin * mn;
+            }
+        } else {
+            const uint8_t* blk = row + (int64_t)b * 210;
+            const double d = orc_f16_to_f32(le16(blk + 208));
+            for (int e = 0; e < 256; e++) {
+                const int h = e / 128, w = e % 128, k = w / 32, i = w % 32;
+                const int lo = blk[64 * h + 32 * (k & 1) + i];
+                const int hb = blk[128 + 32 * h + i];
+                const int q = (((k >> 1) ? (lo >> 4) : (lo & 15)) | (((hb >> (2 * k)) & 3) << 4)) - 32;
+                o[e] = d * (int8_t)blk[192 + 8 * h + 2 * k + i / 16] * q;
+            }
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------ */
 /* Row parallelism: rows split into 2 chunks per thread, chunks pulled from a
  * shared counter (RT/GgufParallelConfig.java:14-15,56-73, GgufRows.java:133). */
 typedef struct {
@@ -346,6 +499,13 @@ static double f64_row_dot(const job_t* j, int64_t row) {
             double d = orc_f16_to_f32(le16(r + b * 34));
             for (int t = 0; t < 32; t++) s += d * (int8_t)r[b * 34 + 2 + t] * (double)j->x[b * 32 + t];
         }
+    } else if (j->type == ORC_Q4_K || j->type == ORC_Q6_K) {
+        const int bb = j->type == ORC_Q4_K ? 144 : 210;
+        double vals[256];
+        for (int b = 0; b < K / 256; b++) {
+            orc_dequantize_k_row(j->type, j->w + row * (int64_t)(K / 256) * bb + (int64_t)b * bb, 256, vals);
+            for (int e = 0; e < 256; e++) s += vals[e] * (double)j->x[b * 256 + e];
+        }
     } else {
         int64_t base = row * (int64_t)K;
         for (int k = 0; k < K; k++) {
@@ -370,6 +530,8 @@ static void* worker(void* arg) {
             if (j->y64) { j->y64[r] = f64_row_dot(j, r); continue; }
             float v;
             if (j->type == ORC_Q4_0) v = orc_dot_row_q4_0(j->w + r * (int64_t)(j->K / 32) * 18, j->K, j->x);
+            else if (j->type == ORC_Q4_K) v = orc_dot_row_q4_k(j->w + r * (int64_t)(j->K / 256) * 144, j->K, j->x);
+            else if (j->type == ORC_Q6_K) v = orc_dot_row_q6_k(j->w + r * (int64_t)(j->K / 256) * 210, j->K, j->x);
             else if (j->type == ORC_Q8_0)
                 v = j->vector_order ? orc_dot_row_q8_0_vector(j->w + r * (int64_t)(j->K / 32) * 34, j->K, j->x)
                                     : orc_dot_row_q8_0_scalar(j->w + r * (int64_t)(j->K / 32) * 34, j->K, j->x);
@@ -406,6 +568,12 @@ void orc_matvec_q4_0(const uint8_t* w, const float* x, float* y, int K, int N, i
 void orc_matvec_q8_0(const uint8_t* w, const float* x, float* y, int K, int N, int vector_order, int threads) {
     job_t j; memset(&j, 0, sizeof j);
     j.type = ORC_Q8_0; j.K = K; j.N = N; j.w = w; j.x = x; j.y = y; j.vector_order = vector_order;
+    run_job(&j, threads);
+}
+
+void orc_matvec_k(int type, const uint8_t* w, const float* x, float* y, int K, int N, int threads) {
+    job_t j; memset(&j, 0, sizeof j);
+    j.type = type; j.K = K; j.N = N; j.w = w; j.x = x; j.y = y;
     run_job(&j, threads);
 }
 

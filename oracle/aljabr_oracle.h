@@ -56,11 +56,15 @@ void orc_dequantize_q8_0(const uint8_t* blocks, float* dst, int64_t numel); /* R
 float orc_dot_row_q4_0(const uint8_t* row, int columns, const float* x);          /* RT/GgufQ32RawDot.java:34-67 */
 float orc_dot_row_q8_0_scalar(const uint8_t* row, int columns, const float* x);   /* RT/GgufQ8RawDot.java:138-185 */
 float orc_dot_row_q8_0_vector(const uint8_t* row, int columns, const float* x);   /* RT/GgufQ8RawDot.java:63-121 */
+float orc_dot_row_q4_k(const uint8_t* row, int columns, const float* x);          /* RT/GgufQ4RawDot.java:38-141 */
+float orc_dot_row_q6_k(const uint8_t* row, int columns, const float* x);          /* RT/GgufQ6RawDot.java:33-133,403-513 */
+void  orc_dequantize_k_row(int type, const uint8_t* row, int columns, double* out); /* element formulas, fp64 */
 
 /* ---- matvec (rows parallel over `threads` host threads, 2 chunks each) -- */
-enum { ORC_Q4_0 = 2, ORC_Q8_0 = 8, ORC_NF4 = 100 };
+enum { ORC_Q4_0 = 2, ORC_Q8_0 = 8, ORC_Q4_K = 12, ORC_Q6_K = 14, ORC_NF4 = 100 };
 void orc_matvec_q4_0(const uint8_t* w, const float* x, float* y, int K, int N, int threads);
 void orc_matvec_q8_0(const uint8_t* w, const float* x, float* y, int K, int N, int vector_order, int threads);
+void orc_matvec_k(int type, const uint8_t* w, const float* x, float* y, int K, int N, int threads);   /* Q4_K / Q6_K */
 /* NF4: dequantise (DK:84-102) then a plain fp32 row dot (stands in for the
  * closed cblas_sgemv at engine/safetensor/.../AccelOps.java:444-451). */
 void orc_matvec_nf4(const uint8_t* codes, const float* absmax, const float* x, float* y,

@@ -179,6 +179,69 @@ def main():
         numel=16, group=8, codes=codes, absmax=[2.0, -0.5],
         expected=[float(f32(nf4[i]) * f32(2.0 if i < 8 else -0.5)) for i in range(16)], tol=0.0))
 
+    # --- Q4_K / Q6_K (256-value super-blocks) -------------------------------
+    def lane_packed(i):           # GgufQ4CalcFx.packedQuant / GgufQ6Fx.laneOrderLowBits
+        low = i & 0x0F
+        return low | ((15 - low) << 4)
+
+    def q4k_block(with_mins):     # GgufQ4Fx.writeSimpleBlock / writeBlockWithAllScalesAndMins + lane-order quants
+        dmin = 0x3800 if with_mins else 0
+        scales = [1, 1, 1, 1, 2, 2, 2, 2, 0x21, 0x21, 0x21, 0x21] if with_mins else \
+                 [1, 1, 1, 1, 0, 0, 0, 0, 1, 1, 1, 1]
+        return [0x00, 0x3C, dmin & 0xFF, dmin >> 8] + scales + [lane_packed(i) for i in range(128)]
+
+    def q4k_expected_dot(x, with_mins):   # GgufQ4CalcFx.expectedDot, float32 accumulation
+        acc = f32(0)
+        for sb in range(0, 256, 64):
+            qb = (sb // 64) * 32
+            for i in range(32):
+                low = (qb + i) & 0x0F
+                high = 15 - low
+                lv = f32(low - 1.0) if with_mins else f32(low)
+                hv = f32(high - 1.0) if with_mins else f32(high)
+                acc = f32(acc + lv * f32(x[sb + i]))
+                acc = f32(acc + hv * f32(x[sb + 32 + i]))
+        return float(acc)
+
+    for with_mins, lines in ((False, "20-43"), (True, "45-68")):
+        fx.append(dict(
+            name=f"q4_k_lane_order_{'mins' if with_mins else 'no_mins'}_ramp", kind="k_matvec",
+            source=f"{RT_TEST}/GgufQ4KRawTest.java:{lines}, GgufQ4Fx.java, GgufQ4CalcFx.java",
+            type=12, K=256, N=1, weights=q4k_block(with_mins), x=ramp(256),
+            expected=[q4k_expected_dot(ramp(256), with_mins)], tol=0.0))
+
+    def q6k_block(low, high, scale):      # GgufQ6Fx.writeBlock
+        return [low] * 128 + [high] * 64 + [scale & 0xFF] * 16 + [0x00, 0x3C]
+
+    fx.append(dict(
+        name="q6_k_uniform_blocks_ones", kind="k_matvec",
+        source=f"{RT_TEST}/GgufQ6KRawTest.java:20-45, GgufQ6Fx.java",
+        type=14, K=256, N=2, weights=q6k_block(0x11, 0xAA, 1) + q6k_block(0x22, 0xAA, 1), x=ones(256),
+        expected=[256.0, 512.0], tol=0.0))
+
+    def q6_high(i):               # GgufQ6Fx.laneOrderHighBits
+        return (i * 53 + 0xA7) & 0xFF
+
+    q6_lane = [lane_packed(i) for i in range(128)] + [q6_high(i) for i in range(64)] + [1] * 16 + [0x00, 0x3C]
+
+    def q6k_expected_dot(x):      # GgufQ6LaneFx.expectedDot, float32 accumulation
+        acc = f32(0)
+        for sb in range(0, 256, 128):
+            lb, hb = (sb // 128) * 64, (sb // 128) * 32
+            for i in range(32):
+                a, c, h = lane_packed(lb + i), lane_packed(lb + 32 + i), q6_high(hb + i)
+                vals = [((a & 15) | ((h & 3) << 4)) - 32, ((c & 15) | (((h >> 2) & 3) << 4)) - 32,
+                        ((a >> 4) | (((h >> 4) & 3) << 4)) - 32, ((c >> 4) | (((h >> 6) & 3) << 4)) - 32]
+                for q, off in zip(vals, (0, 32, 64, 96)):
+                    acc = f32(acc + f32(q) * f32(x[sb + off + i]))
+        return float(acc)
+
+    fx.append(dict(
+        name="q6_k_lane_order_ramp", kind="k_matvec",
+        source=f"{RT_TEST}/GgufQ6KRawTest.java:47-75, GgufQ6Fx.java, GgufQ6LaneFx.java",
+        type=14, K=256, N=2, weights=q6_lane + q6_lane, x=ramp(256),
+        expected=[q6k_expected_dot(ramp(256))] * 2, tol=0.0))
+
     out = os.path.join(os.path.dirname(os.path.abspath(__file__)), "known_answers.json")
     with open(out, "w") as f:
         json.dump({"generator": "tests/golden/make_golden.py", "fixtures": fx}, f, indent=1)

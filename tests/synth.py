@@ -31,6 +31,23 @@ def nf4(seed: int, n: int, k: int, group: int = 64):
     return oracle.quantize_nf4(weights(seed, n, k), group)
 
 
+def k_quant(kind: int, seed: int, n: int, k: int) -> np.ndarray:
+    """n rows of k values as random Q4_K / Q6_K super-blocks: random code,
+    scale and min bytes (every pattern is a valid block) with small positive
+    fp16 super-block scales, the magnitudes GGUF files carry."""
+    g = np.random.default_rng(seed)
+    bb = oracle.K_BLOCK_BYTES[kind]
+    blocks = g.integers(0, 256, size=(n * (k // 256), bb), dtype=np.uint8)
+    f16 = lambda v: np.array([oracle.f32_to_f16_bits(float(t)) for t in v], dtype=np.uint16).view(np.uint8).reshape(-1, 2)
+    nb = blocks.shape[0]
+    if kind == oracle.Q4_K:
+        blocks[:, 0:2] = f16(g.uniform(2e-4, 1e-3, nb))
+        blocks[:, 2:4] = f16(g.uniform(1e-4, 5e-4, nb))
+    else:
+        blocks[:, 208:210] = f16(g.uniform(5e-5, 3e-4, nb))
+    return blocks.reshape(-1)
+
+
 def max_rel_err(got, ref) -> float:
     """max_i |got_i - ref_i| / max(|ref_i|, 1e-3 * max|ref|): the north-star
     metric (element-wise relative error, guarded where ref_i is near zero)."""

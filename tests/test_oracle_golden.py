@@ -147,3 +147,30 @@ def test_rope_rotation_preserves_pair_norm():
     yr = y.reshape(4, 2, 64)
     np.testing.assert_allclose(np.hypot(xr[:, 0], xr[:, 1]), np.hypot(yr[:, 0], yr[:, 1]), rtol=1e-5)
     np.testing.assert_array_equal(oracle.rope(x, 4, 128, 0, 500000.0), x)
+
+
+def test_k_quant_matvec_known_answers(golden):
+    """Q4_K / Q6_K row dots (GgufQ4RawDot.dotRowQ4K, GgufQ6RawDot.dotRowQ6K
+    restated) against the values the reference's raw K-quant tests assert."""
+    fxs = _fixtures(golden, "k_matvec")
+    assert {fx["type"] for fx in fxs} == {oracle.Q4_K, oracle.Q6_K}
+    for fx in fxs:
+        w = np.array(fx["weights"], dtype=np.uint8)
+        x = np.array(fx["x"], dtype=np.float32)
+        y = oracle.matvec_k(fx["type"], w, x, fx["N"])
+        np.testing.assert_array_equal(y, np.array(fx["expected"], dtype=np.float32), err_msg=fx["name"])
+        # the fp64 element formulas give the same value on these exact cases
+        y64 = oracle.matvec_f64(fx["type"], w, x, fx["N"])
+        np.testing.assert_allclose(y64, fx["expected"], rtol=0, atol=0, err_msg=fx["name"])
+
+
+def test_k_quant_dot_matches_fp64_on_random_rows():
+    """The float-order restatement stays within float rounding of the fp64
+    element sums on random super-blocks (every byte pattern is a valid block)."""
+    from tests import synth
+    for kind in (oracle.Q4_K, oracle.Q6_K):
+        w = synth.k_quant(kind, 11 + kind, 4, 2048)
+        x = np.random.default_rng(kind).normal(0, 1, 2048).astype(np.float32)
+        y = oracle.matvec_k(kind, w, x, 4, threads=2)
+        y64 = oracle.matvec_f64(kind, w, x, 4)
+        assert synth.normwise_rel_err(y, y64) < 1e-6
