@@ -14,7 +14,7 @@
 
 namespace alj {
 
-enum WeightFormat : int { FMT_Q4_0 = 0, FMT_Q8_0 = 1, FMT_NF4 = 2 };
+enum WeightFormat : int { FMT_Q4_0 = 0, FMT_Q8_0 = 1, FMT_NF4 = 2, FMT_Q4_K = 3, FMT_Q6_K = 4 };
 
 // Output-side fusions of a matvec (decode-step fusion).
 enum Epilogue : int {
@@ -99,6 +99,10 @@ cudaError_t launch_matvec_mma(int fmt, const MatvecParams& p, cudaStream_t strea
 bool matvec_lut_supported(int fmt, int K, int group);
 cudaError_t launch_matvec_lut(int fmt, const MatvecParams& p, cudaStream_t stream, bool pdl);
 int matvec_lut_grid(int total_rows);   // CTAs (and norm partials) of a table-kernel launch
+// GGUF K-quants (Q4_K / Q6_K, K a multiple of 256): one warp per row, plain
+// store epilogue (+ bias / residual).
+bool matvec_k_supported(int fmt, int K);
+cudaError_t launch_matvec_k(int fmt, const MatvecParams& p, cudaStream_t stream, bool pdl);
 
 cudaError_t launch_dequant(int fmt, float* dst, const uint8_t* src, const float* absmax, int64_t numel,
                            int group, cudaStream_t stream);

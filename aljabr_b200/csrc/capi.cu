@@ -169,6 +169,8 @@ int fmt_of(int type) {
         case ALJ_TYPE_Q4_0: return FMT_Q4_0;
         case ALJ_TYPE_Q8_0: return FMT_Q8_0;
         case ALJ_TYPE_NF4: return FMT_NF4;
+        case ALJ_TYPE_Q4_K: return FMT_Q4_K;
+        case ALJ_TYPE_Q6_K: return FMT_Q6_K;
     }
     return -1;
 }
@@ -178,6 +180,8 @@ int check_dims(int type, long long K, long long N) {
     if (K > (1 << 24) || N > (1 << 28)) return fail(ALJ_ERR_BAD_DIMS, "K=%lld N=%lld too large", K, N);
     if ((type == ALJ_TYPE_Q4_0 || type == ALJ_TYPE_Q8_0) && K % 32 != 0)
         return fail(ALJ_ERR_BAD_DIMS, "K=%lld is not a multiple of the 32-value block", K);
+    if ((type == ALJ_TYPE_Q4_K || type == ALJ_TYPE_Q6_K) && K % 256 != 0)
+        return fail(ALJ_ERR_BAD_DIMS, "K=%lld is not a multiple of the 256-value super-block", K);
     if (fmt_of(type) < 0) return fail(ALJ_ERR_UNSUPPORTED, "weight type %d has no Blackwell kernel", type);
     return ALJ_OK;
 }
@@ -551,6 +555,22 @@ int aljabr_blackwell_matvec_tb_q4_0(void* C, const void* A, const void* B, int K
 
 int aljabr_blackwell_matvec_tb_q8_0(void* C, const void* A, const void* B, int K, int N) {
     const int t = ALJ_TYPE_Q8_0;
+    const void* b[1] = {B};
+    const float* am[1] = {nullptr};
+    HostOut o[1] = {{C, N}};
+    return tb_matvec(1, &t, b, am, nullptr, o, A, K, 0, 1);
+}
+
+int aljabr_blackwell_matvec_tb_q4_k(void* C, const void* A, const void* B, int K, int N) {
+    const int t = ALJ_TYPE_Q4_K;
+    const void* b[1] = {B};
+    const float* am[1] = {nullptr};
+    HostOut o[1] = {{C, N}};
+    return tb_matvec(1, &t, b, am, nullptr, o, A, K, 0, 1);
+}
+
+int aljabr_blackwell_matvec_tb_q6_k(void* C, const void* A, const void* B, int K, int N) {
+    const int t = ALJ_TYPE_Q6_K;
     const void* b[1] = {B};
     const float* am[1] = {nullptr};
     HostOut o[1] = {{C, N}};

@@ -28,6 +28,8 @@ ALJ_ERR_NO_MEMORY = -8
 TYPE_Q4_0 = 2
 TYPE_Q8_0 = 8
 TYPE_NF4 = 100
+TYPE_Q4_K = 12
+TYPE_Q6_K = 14
 KV_F32 = 0
 KV_BF16 = 1
 
@@ -68,6 +70,8 @@ SIGNATURES = {
     "aljabr_blackwell_device_address": (_p, [_p]),
     "aljabr_blackwell_matvec_tb_q4_0": (_i, [_p, _p, _p, _i, _i]),
     "aljabr_blackwell_matvec_tb_q8_0": (_i, [_p, _p, _p, _i, _i]),
+    "aljabr_blackwell_matvec_tb_q4_k": (_i, [_p, _p, _p, _i, _i]),
+    "aljabr_blackwell_matvec_tb_q6_k": (_i, [_p, _p, _p, _i, _i]),
     "aljabr_blackwell_matvec_tb_nf4": (_i, [_p, _p, _p, _p, _i, _i, _i]),
     "aljabr_blackwell_linear_nf4": (_i, [_p, _p, _p, _p, _p, _i, _i, _i]),
     "aljabr_blackwell_matvec_tb_pair": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i]),

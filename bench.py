@@ -335,7 +335,7 @@ def capture(torch, stream, record):
 def run_extra(args, dev, stream, sh, l2, which=None, reps=200):
     c5_tokens = [int(v) for v in getattr(args, "c5_tokens", "1,16,64,512").split(",")]
     """Secondary configs, each with its own pool > 2 x L2 and device timing.
-    `which` selects a subset of {"nf4", "q8", "attention", "c5"} (all if None)."""
+    `which` selects a subset of {"nf4", "q8", "attention", "c5", "kquant"} (all if None)."""
     import torch
 
     import oracle
@@ -429,6 +429,42 @@ def run_extra(args, dev, stream, sh, l2, which=None, reps=200):
                                                     "us_per_call": round(ms * 1e3, 3), "algorithmic_bytes": alg,
                                                     "launches_per_call": 1}
 
+    def kquant_section():
+        # GGUF Q4_K / Q6_K (SURVEY next row 1) at the Llama FFN shapes of the
+        # headline: up 14336x4096 + down 4096x14336 per step.  Synthetic
+        # super-blocks: random code / scale bytes with fixed small fp16 super
+        # scales (every byte pattern is a valid block).
+        g8 = torch.Generator(device=dev).manual_seed(5)
+        for name, kind, bb in (("q4_k", native.TYPE_Q4_K, 144), ("q6_k", native.TYPE_Q6_K, 210)):
+            shapes = ((14336, 4096), (4096, 14336))
+            mats = []
+            for n, k in shapes:
+                w = torch.randint(0, 256, (n * k // 256 * bb,), dtype=torch.uint8, device=dev, generator=g8)
+                v = w.view(-1, bb)
+                if kind == native.TYPE_Q4_K:
+                    v[:, 0], v[:, 1], v[:, 2], v[:, 3] = 0x00, 0x10, 0x00, 0x0C   # d ~ 6e-5, dmin ~ 2e-4
+                else:
+                    v[:, 208], v[:, 209] = 0x00, 0x10
+                mats.append(w)
+            pair = sum(m.numel() for m in mats)
+            poolk = max(2, int(np.ceil(2.5 * l2 / pair)))
+            ws = [[m.clone() for m in mats] for _ in range(poolk)]
+            xk = [[torch.randn(k, device=dev) for _, k in shapes] for _ in range(poolk)]
+            yk = [[torch.empty(n, device=dev) for n, _ in shapes] for _ in range(poolk)]
+            torch.cuda.synchronize(dev)
+
+            def kstep(i, kind=kind, ws=ws, xk=xk, yk=yk, poolk=poolk, shapes=shapes):
+                j = i % poolk
+                for m, (n, k) in enumerate(shapes):
+                    native.check(L.aljabr_blackwell_matvec_dev(kind, yk[j][m].data_ptr(), xk[j][m].data_ptr(),
+                                                               ws[j][m].data_ptr(), None, k, n, 0, None, sh))
+            ms = timed(kstep, reps)
+            alg = pair + sum(4 * (n + k) for n, k in shapes)
+            out[f"{name}_llama_ffn"] = {"GB/s": round(alg / (ms * 1e-3) / 1e9, 1), "us_per_step": round(ms * 1e3, 3),
+                                        "launches_per_step": 2, "algorithmic_bytes": alg,
+                                        "kernel": f"{name[:2]}k_matvec_kernel (4 rows per CTA, K split over 8 warps)"}
+            del ws, xk, yk
+
     def c5_section():
         # Batched NF4 on the per-GPU tensor-parallel shard (TP 8) of one
         # Llama-3-70B layer: q 1024x8192, k/v 128x8192, o 1024x8192,
@@ -506,7 +542,8 @@ def run_extra(args, dev, stream, sh, l2, which=None, reps=200):
             "peaks": {"hbm_GB/s": hbm_peak, "hbm": hbm_kind, "bf16_TFLOP/s": tc_peak, "tensor": tc_kind},
             "tokens": res}
 
-    for name, fn in (("nf4", nf4_section), ("q8", q8_section), ("attention", attention_section), ("c5", c5_section)):
+    for name, fn in (("nf4", nf4_section), ("q8", q8_section), ("attention", attention_section),
+                     ("kquant", kquant_section), ("c5", c5_section)):
         if want(name):
             fn()
             torch.cuda.empty_cache()
@@ -698,7 +735,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--no-prefetch", action="store_true", help="no L2 prefetch hints between the headline launches")
-    ap.add_argument("--only", choices=["nf4", "q8", "attention", "decode", "c5"],
+    ap.add_argument("--only", choices=["nf4", "q8", "attention", "decode", "c5", "kquant"],
                     help="run one secondary workload alone (for profiling); prints its dict")
     ap.add_argument("--decode-tokens", type=int, default=32)
     ap.add_argument("--c5-tokens", default="1,16,64,512",

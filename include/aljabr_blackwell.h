@@ -60,6 +60,14 @@ extern "C" {
 #define ALJ_TYPE_Q4_0 2
 #define ALJ_TYPE_Q8_0 8
 #define ALJ_TYPE_NF4  100
+/* GGUF K-quants, 256-value super-blocks (GgmlType ids; block sizes in
+ * engine/gguf/aljabr-gguf-core/.../runtime/GgufQuantFormats.java:51-53):
+ * Q4_K 144 B (GgufQ4RawDot.dotRowQ4K, GgufQ4RawDot.java:38-141), Q6_K 210 B
+ * (GgufQ6RawDot.dotRowQ6K, GgufQ6RawDot.java:33-133).  Accepted by the typed
+ * matvec entry points (aljabr_blackwell_matvec_dev, _tb_pair, _tb_triple) and
+ * by aljabr_blackwell_matvec_tb_q4_k / _q6_k; K a multiple of 256. */
+#define ALJ_TYPE_Q4_K 12
+#define ALJ_TYPE_Q6_K 14
 
 /* ---- KV-cache element types --------------------------------------------- */
 #define ALJ_KV_F32  0   /* the reference's fp32 cache (KVCache.java:22-23)  */
@@ -118,6 +126,12 @@ int aljabr_blackwell_matvec_tb_q4_0(void* C, const void* A, const void* B, int K
 /* Q8_0 (GgufQ8RawDot.dotRowQ8_0, .../runtime/GgufQ8RawDot.java:40-50);
  * same shape as aljabr_metal_matvec_tb_q8_0. */
 int aljabr_blackwell_matvec_tb_q8_0(void* C, const void* A, const void* B, int K, int N);
+/* Q4_K / Q6_K (GgufRawDot.q4K / q6K, .../runtime/GgufRawDot.java:79-149);
+ * same shapes as aljabr_metal_matvec_tb_q4_k / _q6_k
+ * (backend/metal/.../cpp/metal/aljabr_metal_matvec_api.h:48-53).
+ * B: N rows of K/256 super-blocks (144 / 210 bytes); K a multiple of 256. */
+int aljabr_blackwell_matvec_tb_q4_k(void* C, const void* A, const void* B, int K, int N);
+int aljabr_blackwell_matvec_tb_q6_k(void* C, const void* A, const void* B, int K, int N);
 /* NF4: AccelOps.linear's dequantise-then-sgemv for M == 1
  * (engine/safetensor/.../tensor/AccelOps.java:392-451); same shape as
  * aljabr_metal_matvec_tb_nf4.  absmax: float[N*K/blockSize]. */

@@ -164,7 +164,7 @@ def test_errors_are_reported_not_fallen_back(lib):
         lib.call("aljabr_blackwell_matvec_tb_q4_0", y.ctypes.data, x.ctypes.data, w.ctypes.data, 250, 4)
     assert e.value.code == lib.ALJ_ERR_BAD_DIMS
     with pytest.raises(UnsupportedOperation):
-        lib.call("aljabr_blackwell_matvec_tb_batch", y.ctypes.data, x.ctypes.data, w.ctypes.data, 256, 4, 12, 1)
+        lib.call("aljabr_blackwell_matvec_tb_batch", y.ctypes.data, x.ctypes.data, w.ctypes.data, 256, 4, 13, 1)
     bits = ctypes.c_uint(0)
     lib.call("aljabr_blackwell_device_status", ctypes.byref(bits))
     assert bits.value == 0
