@@ -68,6 +68,20 @@ __device__ __forceinline__ void nibbles4(uint32_t w, int sh, f2& p01, f2& p23) {
     p23 = add2(p23, off);
 }
 
+// L2 prefetch of the 16-byte-aligned inside of [base, base + bytes), in
+// 16 KB bulk requests: the CTA's rows are one contiguous range, and one
+// thread puts all of it in flight at once, so the warps' own loads find it
+// in L2 instead of each paying the HBM round trip in turn.
+__device__ __forceinline__ void prefetch_rows_l2(const uint8_t* base, size_t bytes) {
+    uintptr_t a = (reinterpret_cast<uintptr_t>(base) + 15) & ~uintptr_t(15);
+    const uintptr_t end = (reinterpret_cast<uintptr_t>(base) + bytes) & ~uintptr_t(15);
+    for (; a + 16 <= end; a += 16384) {
+        const uintptr_t left = end - a;
+        const uint32_t n = static_cast<uint32_t>(left < 16384 ? left : 16384) & ~15u;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(n) : "memory");
+    }
+}
+
 struct KRows {
     const uint8_t* w;
     const float* x;
@@ -107,6 +121,7 @@ __global__ void __launch_bounds__(kKWarps * 32, 3) q4k_matvec_kernel(const KRows
     const int row0 = blockIdx.x * kKGroups * kKRows;
     const int nb = p.K / 256;
     const size_t row_bytes = static_cast<size_t>(nb) * 144;
+    if (threadIdx.x == 0) prefetch_rows_l2(p.w + row0 * row_bytes, min(kKGroups * kKRows, p.N - row0) * row_bytes);
     const int j = lane >> 3, t = (lane * 4) & 31;
     float acc[kKGroups][kKRows];
 #pragma unroll
@@ -152,6 +167,7 @@ __global__ void __launch_bounds__(kKWarps * 32, 3) q6k_matvec_kernel(const KRows
     const int row0 = blockIdx.x * kKGroups * kKRows;
     const int nb = p.K / 256;
     const size_t row_bytes = static_cast<size_t>(nb) * 210;
+    if (threadIdx.x == 0) prefetch_rows_l2(p.w + row0 * row_bytes, min(kKGroups * kKRows, p.N - row0) * row_bytes);
     // byte position p = 2 lane + e of a 64-byte ql half: quarter k0 = p / 32
     // (low nibble) or 2 + k0 (high nibble), value index i0 + e = p % 32
     const int k0 = lane >> 4, i0 = (lane * 2) & 31, g = i0 >> 4;
