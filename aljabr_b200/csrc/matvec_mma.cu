@@ -400,13 +400,26 @@ __global__ void __launch_bounds__(kThreads, 1) quant_mma_kernel(const __grid_con
         int e[4];
 #pragma unroll
         for (int pos = 0; pos < 4; ++pos) e[pos] = slot_elem<FMT>(par, st_j, pos);
-#pragma unroll 2
-        for (int c = 0; c < nchunks; ++c) {
+        // x reads of up to kXBatch chunks go out together: one L2 round trip
+        // per batch instead of one per chunk (every CTA reads all of x, so
+        // these lines are contended)
+        constexpr int kXBatch = 8;
+        for (int c0 = 0; c0 < nchunks; c0 += kXBatch) {
+            float vb[kXBatch][4];
+#pragma unroll
+            for (int cb = 0; cb < kXBatch; ++cb) {
+                const float* xb = p.x + static_cast<size_t>((c0 + cb) * 64 + blk + 2 * st_t) * 32;
+#pragma unroll
+                for (int pos = 0; pos < 4; ++pos) vb[cb][pos] = c0 + cb < nchunks ? __ldg(xb + e[pos]) : 0.0f;
+            }
+#pragma unroll
+            for (int cb = 0; cb < kXBatch; ++cb) {
+            const int c = c0 + cb;
+            if (c >= nchunks) break;
             const int bg = c * 64 + blk + 2 * st_t;
-            const float* xb = p.x + static_cast<size_t>(bg) * 32;
             float v[4];
 #pragma unroll
-            for (int pos = 0; pos < 4; ++pos) v[pos] = __ldg(xb + e[pos]);
+            for (int pos = 0; pos < 4; ++pos) v[pos] = vb[cb][pos];
             float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
@@ -445,6 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1) quant_mma_kernel(const __grid_con
             if (st_j == 0)
                 binfo[bg] = make_float4(-F::kOffset * shi * kTwoM24, -F::kOffset * slo * kTwoM24,
                                         __int_as_float((127 + E + 24) << 23), 0.0f);
+            }
         }
         __syncwarp();
     }
