@@ -166,15 +166,6 @@ __device__ __forceinline__ uint4 lds128(uint32_t a) {
     asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
     return v;
 }
-// Load only where `pred` is set (no shared access otherwise); zeros elsewhere.
-__device__ __forceinline__ uint4 lds128_if(uint32_t a, uint32_t pred) {
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    asm volatile(
-        "{\n .reg .pred q;\n setp.ne.u32 q, %5, 0;\n @q ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];\n}\n"
-        : "+r"(v.x), "+r"(v.y), "+r"(v.z), "+r"(v.w)
-        : "r"(a), "r"(pred));
-    return v;
-}
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -256,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1) quant_mma_kernel(const __grid_con
     sp += static_cast<size_t>(nspans) * 4 * kBlockInfoBytes;
     float* red = reinterpret_cast<float*>(sp);           // [kRing][kCW][16]
     sp += kRing * kCW * 16 * 4;
-    float* misc = reinterpret_cast<float*>(sp);          // [0] norm scale, [1] last-CTA flag
+    float* misc = reinterpret_cast<float*>(sp);          // [0] norm scale, [1] last-CTA flag, [12..15] zeros
     sp += 16 * 4;
     uint64_t* full = reinterpret_cast<uint64_t*>(sp);
     uint64_t* empty = full + kMaxStages;
@@ -279,6 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1) quant_mma_kernel(const __grid_con
             mbar_init(&rempty[b], 1);
         }
         fence_mbar_init();
+        *reinterpret_cast<float4*>(misc + 12) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
     __syncthreads();
 
@@ -483,6 +475,9 @@ __global__ void __launch_bounds__(kThreads, 1) quant_mma_kernel(const __grid_con
     const uint32_t stage_s = smem_u32(stage0);
     const uint32_t brec0 = smem_u32(xfrag) + warp * kSpanBytes + boff;
     const uint32_t binfo0 = smem_u32(binfo) + myblk * kBlockInfoBytes;
+    // lanes whose B slots stay zero read them from a 16-byte zero slot (a
+    // broadcast load) instead of zero-filling registers and predicating
+    const uint32_t zero16 = smem_u32(misc + 12);
 
     SlabWalk walk{u_begin, u_end};
     int seg, su, nunits, s = 0, sl = 0;
@@ -503,7 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1) quant_mma_kernel(const __grid_con
                 const uint32_t rb = brec0 + c * (16 * kSpanBytes);
                 uint4 B[4];
 #pragma unroll
-                for (int jp = 0; jp < 4; ++jp) B[jp] = lds128_if(rb + jp * kRecBytes, bact);
+                for (int jp = 0; jp < 4; ++jp) B[jp] = lds128(bact ? rb + jp * kRecBytes : zero16);
                 const float scale = __uint_as_float(bi.z);
                 const float d0 = __half2float(__ushort_as_half(static_cast<unsigned short>(__byte_perm(W0[0], 0u, sel_d)))) * scale;
                 const float d1 = __half2float(__ushort_as_half(static_cast<unsigned short>(__byte_perm(W1[0], 0u, sel_d)))) * scale;
