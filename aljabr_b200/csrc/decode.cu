@@ -113,6 +113,81 @@ __global__ void __launch_bounds__(1024) embed_nf4_kernel(float* x, float* xn, co
     if (threadIdx.x == 0) *reinterpret_cast<unsigned long long*>(io + 4) = 0ull;
 }
 
+// One value of a GGUF row, in the reference's dequantiser float order:
+// Q4_0 / Q8_0 as GgufBlockDequantizer (q - 8) * d + 0.0f and q * d; Q4_K as
+// GgufKBlockDequantizer.dequantizeQ4KBlock (:32-75), d1 = d * scale,
+// m1 = dmin * min, d1 * q - m1; Q6_K as dequantizeQ6KBlock (:320-360),
+// (d * scale) * (q - 32).  Bytes are read one at a time (rows of 18- and
+// 210-byte blocks are only 2-byte aligned).
+__device__ float gguf_value(int fmt, const uint8_t* row, int i) {
+    auto f16 = [](const uint8_t* b) { return f16_bits_to_f32(static_cast<uint32_t>(b[0]) | (b[1] << 8)); };
+    if (fmt == FMT_Q4_0 || fmt == FMT_Q8_0) {
+        const int j = i & 31;
+        const uint8_t* blk = row + (i >> 5) * (fmt == FMT_Q4_0 ? 18 : 34);
+        const float d = f16(blk);
+        if (fmt == FMT_Q8_0) return __fmul_rn(static_cast<float>(static_cast<signed char>(blk[2 + j])), d);
+        const int byte = blk[2 + (j & 15)];
+        const int q = j < 16 ? (byte & 15) : (byte >> 4);
+        return __fadd_rn(__fmul_rn(static_cast<float>(q - 8), d), 0.0f);
+    }
+    const int e = i & 255;
+    if (fmt == FMT_Q4_K) {
+        const uint8_t* blk = row + (i >> 8) * 144;
+        const int j = e >> 6, t = e & 63, sb = 2 * j + (t >= 32);
+        const int byte = blk[16 + 32 * j + (t & 31)];
+        const int q = t < 32 ? (byte & 15) : (byte >> 4);
+        const uint8_t* sc = blk + 4;
+        int s, mn;
+        if (sb < 4) {
+            s = sc[sb] & 63;
+            mn = sc[sb + 4] & 63;
+        } else {
+            s = (sc[sb + 4] & 15) | ((sc[sb - 4] >> 6) << 4);
+            mn = (sc[sb + 4] >> 4) | ((sc[sb] >> 6) << 4);
+        }
+        const float d1 = __fmul_rn(f16(blk), static_cast<float>(s));
+        const float m1 = __fmul_rn(f16(blk + 2), static_cast<float>(mn));
+        return __fsub_rn(__fmul_rn(d1, static_cast<float>(q)), m1);
+    }
+    const uint8_t* blk = row + (i >> 8) * 210;   // Q6_K
+    const int h = e >> 7, w = e & 127, k = w >> 5, ii = w & 31;
+    const int lo = blk[64 * h + 32 * (k & 1) + ii];
+    const int hb = blk[128 + 32 * h + ii];
+    const int q = (((k >> 1) ? (lo >> 4) : (lo & 15)) | (((hb >> (2 * k)) & 3) << 4)) - 32;
+    const float s = __fmul_rn(f16(blk + 208), static_cast<float>(static_cast<signed char>(blk[192 + 8 * h + 2 * k + ii / 16])));
+    return __fmul_rn(s, static_cast<float>(q));
+}
+
+// embed_nf4_kernel for a GGUF-typed embedding table (row_bytes per token row).
+__global__ void __launch_bounds__(1024) embed_gguf_kernel(float* x, float* xn, const uint8_t* table, int fmt,
+                                                          long long row_bytes, int* io, int H, const float* norm_w,
+                                                          float eps) {
+    __shared__ float red[32];
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint8_t* row = table + static_cast<long long>(io[1]) * row_bytes;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+        const float v = gguf_value(fmt, row, i);
+        x[i] = v;
+        ss = fmaf(v, v, ss);
+    }
+    const float scale = 1.0f / sqrtf(block_sum_1024(ss, red) / static_cast<float>(H) + eps);
+    for (int i = threadIdx.x; i < H; i += blockDim.x) xn[i] = x[i] * scale * norm_w[i];
+    if (threadIdx.x == 0) *reinterpret_cast<unsigned long long*>(io + 4) = 0ull;
+}
+
+// h = SiLU(gate) * up (GGUFVectorOps.swiglu, the matvec epilogues' formula),
+// in place over `up`, for projections whose kernel has no SwiGLU epilogue.
+__global__ void swiglu_kernel(const float* gate, float* up, int n) {
+    pdl_launch_dependents();
+    pdl_wait();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float g = gate[i];
+        up[i] = g / (1.0f + expf(-g)) * up[i];
+    }
+}
+
 // Split-half RoPE (GGUFVectorOps.rope, GGUFVectorOps.java:383-440) on the
 // rank's q and k heads, then the KV store at `pos`
 // (GgufKvCacheWriteExecution.storeToken).  rope[pos * D/2 + i] holds
@@ -259,10 +334,24 @@ cudaError_t launch_small(void (*kernel)(Args...), int grid, int block, cudaStrea
     return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
+// Bytes of one row of `cols` values in a GGUF block format (NF4: packed codes).
+long long gguf_row_bytes(int fmt, int cols) {
+    switch (fmt) {
+        case FMT_Q4_0: return cols / 32 * 18LL;
+        case FMT_Q8_0: return cols / 32 * 34LL;
+        case FMT_Q4_K: return cols / 256 * 144LL;
+        case FMT_Q6_K: return cols / 256 * 210LL;
+        default: return cols / 2;
+    }
+}
+
 // ------------------------------------------------------------------ model
-struct Nf4 {
+// One registered weight matrix: row-major ggml blocks of `fmt` (WeightFormat),
+// or NF4 codes with their absmax scales.
+struct Weight {
     const uint8_t* codes = nullptr;
     const float* absmax = nullptr;
+    int fmt = FMT_NF4;
 };
 
 enum { W_Q = 0, W_K, W_V, W_O, W_GATE, W_UP, W_DOWN, W_COUNT };
@@ -273,9 +362,9 @@ struct DecodeModel {
     float eps, theta;
     int T = 1, rank = 0;
     int hq, hkv, f, h, v;              // this rank's shard sizes
-    std::vector<std::array<Nf4, W_COUNT>> w;
+    std::vector<std::array<Weight, W_COUNT>> w;
     std::vector<bool> layer_set;
-    Nf4 embd, head;
+    Weight embd, head;
     bool output_set = false;
     float* norms = nullptr;            // [layers][2][H] then [H]
     float2* rope = nullptr;            // [max_ctx][D/2] (cos, sin)
@@ -283,6 +372,7 @@ struct DecodeModel {
     float *x, *xn, *q, *k, *vv, *att_l, *att, *delta_l, *delta, *h_l, *hh, *logits_l, *logits, *scratch;
     float* norm_partials = nullptr;    // [matvec_max_ctas()] per-CTA sums of squares
     bool defer_norm = false;           // RMSNorm scale applied by the consuming matvec (one GPU)
+    bool typed = false;                // some tensor is not NF4: unfused residual / norm / SwiGLU launches
     unsigned int* norm_counter = nullptr;
     float* act_base = nullptr;
     int* io = nullptr;                 // device {pos, token, argmax}
@@ -324,7 +414,7 @@ DecodeModel* find(unsigned long long h) {
 // given norm_out leaves x * norm_w and its per-CTA sums of squares, and
 // `scaled_x` marks a launch whose x is such a vector: it applies the
 // RMSNorm scale to its outputs from those partials.
-cudaError_t matvec(const DecodeModel& m, const Nf4* ws, float* const* ys, const int* rows, int n, const float* x,
+cudaError_t matvec(const DecodeModel& m, const Weight* ws, float* const* ys, const int* rows, int n, const float* x,
                    int K, int epilogue, const float* residual, float* norm_out, const float* norm_w,
                    const TpLink* tpl = nullptr, bool scaled_x = false) {
     MatvecParams p = {};
@@ -360,7 +450,20 @@ cudaError_t matvec(const DecodeModel& m, const Nf4* ws, float* const* ys, const 
         p.in_rows = m.H;
         p.in_eps = m.eps;
     }
-    return launch_matvec(FMT_NF4, p, m.stream, true);
+    bool same = true;
+    for (int i = 1; i < n; ++i) same = same && ws[i].fmt == ws[0].fmt;
+    if (same) return launch_matvec(ws[0].fmt, p, m.stream, true);
+    // q/k/v of mixed GGUF types (e.g. Q4_K q/k with a Q6_K v): one launch per segment
+    if (epilogue != EPI_STORE || norm_out) return cudaErrorNotSupported;
+    for (int i = 0; i < n; ++i) {
+        MatvecParams one = p;
+        one.nseg = 1;
+        one.seg[0] = p.seg[i];
+        one.total_rows = rows[i];
+        const cudaError_t e = launch_matvec(ws[i].fmt, one, m.stream, true);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 #define REC(expr)                                  \
@@ -378,8 +481,12 @@ cudaError_t record_step(DecodeModel& m) {
     const int D = m.D;
     const int sms = sm_count_for_current_device();
     const float* out_norm = m.norms + static_cast<size_t>(m.layers) * 2 * m.H;
-    REC(launch_small(embed_nf4_kernel, 1, 1024, m.stream, m.x, m.xn, m.embd.codes, m.embd.absmax, m.io, m.H, m.group,
-                     static_cast<const float*>(m.norms), m.eps));
+    if (m.embd.fmt == FMT_NF4)
+        REC(launch_small(embed_nf4_kernel, 1, 1024, m.stream, m.x, m.xn, m.embd.codes, m.embd.absmax, m.io, m.H,
+                         m.group, static_cast<const float*>(m.norms), m.eps));
+    else
+        REC(launch_small(embed_gguf_kernel, 1, 1024, m.stream, m.x, m.xn, m.embd.codes, m.embd.fmt,
+                         gguf_row_bytes(m.embd.fmt, m.H), m.io, m.H, static_cast<const float*>(m.norms), m.eps));
     for (int l = 0; l < m.layers; ++l) {
         const auto& w = m.w[l];
         const float* ffn_norm = m.norms + static_cast<size_t>(l) * 2 * m.H + m.H;
@@ -387,7 +494,7 @@ cudaError_t record_step(DecodeModel& m) {
         void* kc = static_cast<uint8_t*>(m.kc) + static_cast<size_t>(l) * m.kv_layer_elems() * m.kv_elem();
         void* vc = static_cast<uint8_t*>(m.vc) + static_cast<size_t>(l) * m.kv_layer_elems() * m.kv_elem();
         {   // q, k, v from the normed x (GgufDecodePass.java:305-309)
-            const Nf4 ws[3] = {w[W_Q], w[W_K], w[W_V]};
+            const Weight ws[3] = {w[W_Q], w[W_K], w[W_V]};
             float* ys[3] = {m.q, m.k, m.vv};
             const int rows[3] = {m.hq * D, m.hkv * D, m.hkv * D};
             // layer 0's x comes normed from the embedding kernel
@@ -419,12 +526,17 @@ cudaError_t record_step(DecodeModel& m) {
         }
         if (m.T > 1) RECN(g_nccl.allGather(m.att_l, m.att, static_cast<size_t>(m.hq) * D, ncclFloat, m.comm, m.stream));
         {   // o-proj + residual (GgufDecodePass.java:475-481), then the FFN norm (:485)
-            const Nf4 ws[1] = {w[W_O]};
+            const Weight ws[1] = {w[W_O]};
             const int rows[1] = {m.h};
             if (m.T > 1) {
                 float* ys[1] = {m.delta_l};
                 REC(matvec(m, ws, ys, rows, 1, m.att, m.Hq * D, EPI_STORE, nullptr, nullptr, nullptr));
                 RECN(g_nccl.allGather(m.delta_l, m.delta, m.h, ncclFloat, m.comm, m.stream));
+                REC(launch_small(add_norm_kernel, 1, 1024, m.stream, m.x, static_cast<const float*>(m.delta), m.xn,
+                                 ffn_norm, m.H, m.eps));
+            } else if (m.typed) {
+                float* ys[1] = {m.delta};
+                REC(matvec(m, ws, ys, rows, 1, m.att, m.Hq * D, EPI_STORE, nullptr, nullptr, nullptr));
                 REC(launch_small(add_norm_kernel, 1, 1024, m.stream, m.x, static_cast<const float*>(m.delta), m.xn,
                                  ffn_norm, m.H, m.eps));
             } else {
@@ -433,19 +545,31 @@ cudaError_t record_step(DecodeModel& m) {
             }
         }
         {   // gate / up with the SwiGLU epilogue (GgufDecodePass.java:492-497)
-            const Nf4 ws[2] = {w[W_GATE], w[W_UP]};
-            float* ys[2] = {m.T > 1 ? m.h_l : m.hh, nullptr};
+            const Weight ws[2] = {w[W_GATE], w[W_UP]};
             const int rows[2] = {m.f, m.f};
-            REC(matvec(m, ws, ys, rows, 2, m.xn, m.H, EPI_SWIGLU_PAIR, nullptr, nullptr, nullptr, nullptr, true));
+            if (m.typed) {   // one GPU: gate -> h_l, up -> hh, then hh = SiLU(h_l) * hh
+                float* ys[2] = {m.h_l, m.hh};
+                REC(matvec(m, ws, ys, rows, 2, m.xn, m.H, EPI_STORE, nullptr, nullptr, nullptr));
+                REC(launch_small(swiglu_kernel, std::max(1, std::min(sms, (m.F + 255) / 256)), 256, m.stream,
+                                 static_cast<const float*>(m.h_l), m.hh, m.F));
+            } else {
+                float* ys[2] = {m.T > 1 ? m.h_l : m.hh, nullptr};
+                REC(matvec(m, ws, ys, rows, 2, m.xn, m.H, EPI_SWIGLU_PAIR, nullptr, nullptr, nullptr, nullptr, true));
+            }
         }
         if (m.T > 1) RECN(g_nccl.allGather(m.h_l, m.hh, m.f, ncclFloat, m.comm, m.stream));
         {   // down-proj + residual (GgufDecodePass.java:504-511), then the next layer's norm
-            const Nf4 ws[1] = {w[W_DOWN]};
+            const Weight ws[1] = {w[W_DOWN]};
             const int rows[1] = {m.h};
             if (m.T > 1) {
                 float* ys[1] = {m.delta_l};
                 REC(matvec(m, ws, ys, rows, 1, m.hh, m.F, EPI_STORE, nullptr, nullptr, nullptr));
                 RECN(g_nccl.allGather(m.delta_l, m.delta, m.h, ncclFloat, m.comm, m.stream));
+                REC(launch_small(add_norm_kernel, 1, 1024, m.stream, m.x, static_cast<const float*>(m.delta), m.xn,
+                                 next_norm, m.H, m.eps));
+            } else if (m.typed) {
+                float* ys[1] = {m.delta};
+                REC(matvec(m, ws, ys, rows, 1, m.hh, m.F, EPI_STORE, nullptr, nullptr, nullptr));
                 REC(launch_small(add_norm_kernel, 1, 1024, m.stream, m.x, static_cast<const float*>(m.delta), m.xn,
                                  next_norm, m.H, m.eps));
             } else {
@@ -455,7 +579,7 @@ cudaError_t record_step(DecodeModel& m) {
         }
     }
     {   // logits from the output-normed x (GgufLogitsProcessor.compute)
-        const Nf4 ws[1] = {m.head};
+        const Weight ws[1] = {m.head};
         float* ys[1] = {m.T > 1 ? m.logits_l : m.logits};
         const int rows[1] = {m.v};
         REC(matvec(m, ws, ys, rows, 1, m.xn, m.H, EPI_STORE, nullptr, nullptr, nullptr, nullptr, true));
@@ -510,7 +634,7 @@ cudaError_t record_step_p2p(DecodeModel& m) {
         void* kc = static_cast<uint8_t*>(m.kc) + static_cast<size_t>(l) * m.kv_layer_elems() * m.kv_elem();
         void* vc = static_cast<uint8_t*>(m.vc) + static_cast<size_t>(l) * m.kv_layer_elems() * m.kv_elem();
         {   // q, k, v of this rank's heads
-            const Nf4 ws[3] = {w[W_Q], w[W_K], w[W_V]};
+            const Weight ws[3] = {w[W_Q], w[W_K], w[W_V]};
             float* ys[3] = {m.q, m.k, m.vv};
             const int rows[3] = {m.hq * D, m.hkv * D, m.hkv * D};
             REC(matvec(m, ws, ys, rows, 3, m.xn, m.H, EPI_STORE, nullptr, nullptr, nullptr));
@@ -540,7 +664,7 @@ cudaError_t record_step_p2p(DecodeModel& m) {
             REC(launch_attention(a, m.stream, true));
         }
         {   // o-proj: x rows += W_o att, pushed with this rank's sum of squares; then the FFN norm
-            const Nf4 ws[1] = {w[W_O]};
+            const Weight ws[1] = {w[W_O]};
             const int rows[1] = {m.h};
             float* ys[1] = {x + R * m.h};
             TpLink t = link(m.off_x, R * m.h, m.off_part_o, FL_XO, L, l + 1);
@@ -553,14 +677,14 @@ cudaError_t record_step_p2p(DecodeModel& m) {
                              static_cast<const int*>(m.io + 6), L, l + 1));
         }
         {   // gate / up with the SwiGLU epilogue, pushed into every rank's hh
-            const Nf4 ws[2] = {w[W_GATE], w[W_UP]};
+            const Weight ws[2] = {w[W_GATE], w[W_UP]};
             float* ys[2] = {hh + R * m.f, nullptr};
             const int rows[2] = {m.f, m.f};
             TpLink t = link(m.off_hh, R * m.f, 0, FL_H, L, l + 1);
             REC(matvec(m, ws, ys, rows, 2, m.xn, m.H, EPI_SWIGLU_PAIR, nullptr, nullptr, nullptr, &t));
         }
         {   // down-proj: x rows += W_down hh, pushed; then the next norm
-            const Nf4 ws[1] = {w[W_DOWN]};
+            const Weight ws[1] = {w[W_DOWN]};
             const int rows[1] = {m.h};
             float* ys[1] = {x + R * m.h};
             TpLink t = link(m.off_x, R * m.h, m.off_part_d, FL_XD, L, l + 1);
@@ -574,7 +698,7 @@ cudaError_t record_step_p2p(DecodeModel& m) {
         }
     }
     {   // logits of this rank's vocabulary rows, pushed into every rank's logits
-        const Nf4 ws[1] = {m.head};
+        const Weight ws[1] = {m.head};
         float* ys[1] = {peer(R, m.off_logits) + R * m.v};
         const int rows[1] = {m.v};
         TpLink t = link(m.off_logits, R * m.v, 0, FL_LOGITS, 1, 1);
@@ -839,20 +963,59 @@ int aljabr_blackwell_decode_model_create(const int* dims, float eps, float rope_
     return ALJ_OK;
 }
 
-int aljabr_blackwell_register_decode_layer(unsigned long long handle, int layer, const void* const* codes,
-                                           const void* const* absmax, const float* attn_norm, const float* ffn_norm) {
+}  // extern "C"
+
+namespace {
+// ALJ_TYPE_* of a decode-step weight -> WeightFormat, or -1.
+int decode_fmt(int type) {
+    switch (type) {
+        case ALJ_TYPE_Q4_0: return FMT_Q4_0;
+        case ALJ_TYPE_Q8_0: return FMT_Q8_0;
+        case ALJ_TYPE_Q4_K: return FMT_Q4_K;
+        case ALJ_TYPE_Q6_K: return FMT_Q6_K;
+        case ALJ_TYPE_NF4: return FMT_NF4;
+        default: return -1;
+    }
+}
+
+// Resolve one weight (and, for NF4, its absmax) into `out`; marks the model
+// typed for a GGUF format (one GPU only: the tensor-parallel exchange fuses
+// the NF4 kernels' epilogues).
+int bind_weight(DecodeModel* m, Weight& out, const void* w, int type, const void* absmax) {
+    const int fmt = decode_fmt(type);
+    if (fmt < 0) return decode_fail(ALJ_ERR_UNSUPPORTED, "decode weights must be Q4_0, Q8_0, Q4_K, Q6_K or NF4");
+    if (fmt != FMT_NF4 && m->T > 1)
+        return decode_fail(ALJ_ERR_UNSUPPORTED, "GGUF-typed decode weights need tp_world 1 (NF4 for tensor parallel)");
+    Weight r;
+    r.fmt = fmt;
+    r.codes = static_cast<const uint8_t*>(decode_resolve(w));
+    r.absmax = fmt == FMT_NF4 ? static_cast<const float*>(decode_resolve(absmax)) : nullptr;
+    if (!r.codes || (fmt == FMT_NF4 && !r.absmax))
+        return decode_fail(ALJ_ERR_NOT_REGISTERED, "decode weights must be device or registered memory");
+    out = r;
+    if (fmt != FMT_NF4) {
+        m->typed = true;
+        m->defer_norm = false;
+    }
+    return ALJ_OK;
+}
+
+int register_layer(unsigned long long handle, int layer, const void* const* w, const int* types,
+                   const void* const* absmax, const float* attn_norm, const float* ffn_norm) {
     DecodeModel* m = find(handle);
     if (!m) return decode_fail(ALJ_ERR_BAD_ARG, "unknown decode model handle");
     if (layer < 0 || layer >= m->layers) return decode_fail(ALJ_ERR_BAD_DIMS, "layer index out of range");
-    if (!codes || !absmax || !attn_norm || !ffn_norm) return decode_fail(ALJ_ERR_BAD_ARG, "null layer pointer");
+    if (!w || !attn_norm || !ffn_norm) return decode_fail(ALJ_ERR_BAD_ARG, "null layer pointer");
     std::lock_guard<std::mutex> g(m->mu);
     cudaSetDevice(m->device);
+    std::array<Weight, W_COUNT> ws;
     for (int i = 0; i < W_COUNT; ++i) {
-        m->w[layer][i].codes = static_cast<const uint8_t*>(decode_resolve(codes[i]));
-        m->w[layer][i].absmax = static_cast<const float*>(decode_resolve(absmax[i]));
-        if (!m->w[layer][i].codes || !m->w[layer][i].absmax)
-            return decode_fail(ALJ_ERR_NOT_REGISTERED, "layer weights must be device or registered memory");
+        const int type = types ? types[i] : ALJ_TYPE_NF4;
+        if (type == ALJ_TYPE_NF4 && !absmax) return decode_fail(ALJ_ERR_BAD_ARG, "NF4 weights need absmax");
+        const int rc = bind_weight(m, ws[i], w[i], type, absmax ? absmax[i] : nullptr);
+        if (rc != ALJ_OK) return rc;
     }
+    m->w[layer] = ws;
     float* dst = m->norms + static_cast<size_t>(layer) * 2 * m->H;
     if (cudaMemcpy(dst, attn_norm, m->H * 4, cudaMemcpyDefault) != cudaSuccess ||
         cudaMemcpy(dst + m->H, ffn_norm, m->H * 4, cudaMemcpyDefault) != cudaSuccess)
@@ -862,25 +1025,53 @@ int aljabr_blackwell_register_decode_layer(unsigned long long handle, int layer,
     return ALJ_OK;
 }
 
-int aljabr_blackwell_register_output(unsigned long long handle, const void* embd_codes, const void* embd_absmax,
-                                     const void* head_codes, const void* head_absmax, const float* output_norm) {
+int register_output(unsigned long long handle, const void* embd, int embd_type, const void* embd_absmax,
+                    const void* head, int head_type, const void* head_absmax, const float* output_norm) {
     DecodeModel* m = find(handle);
     if (!m) return decode_fail(ALJ_ERR_BAD_ARG, "unknown decode model handle");
     if (!output_norm) return decode_fail(ALJ_ERR_BAD_ARG, "null output norm");
     std::lock_guard<std::mutex> g(m->mu);
     cudaSetDevice(m->device);
-    m->embd.codes = static_cast<const uint8_t*>(decode_resolve(embd_codes));
-    m->embd.absmax = static_cast<const float*>(decode_resolve(embd_absmax));
-    m->head.codes = static_cast<const uint8_t*>(decode_resolve(head_codes));
-    m->head.absmax = static_cast<const float*>(decode_resolve(head_absmax));
-    if (!m->embd.codes || !m->embd.absmax || !m->head.codes || !m->head.absmax)
-        return decode_fail(ALJ_ERR_NOT_REGISTERED, "output weights must be device or registered memory");
+    Weight e, h;
+    int rc = bind_weight(m, e, embd, embd_type, embd_absmax);
+    if (rc == ALJ_OK) rc = bind_weight(m, h, head, head_type, head_absmax);
+    if (rc != ALJ_OK) return rc;
+    m->embd = e;
+    m->head = h;
     if (cudaMemcpy(m->norms + static_cast<size_t>(m->layers) * 2 * m->H, output_norm, m->H * 4, cudaMemcpyDefault) !=
         cudaSuccess)
         return decode_fail(ALJ_ERR_CUDA, "copying the output norm failed");
     m->output_set = true;
     if (m->exec) { cudaGraphExecDestroy(m->exec); m->exec = nullptr; }
     return ALJ_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int aljabr_blackwell_register_decode_layer(unsigned long long handle, int layer, const void* const* codes,
+                                           const void* const* absmax, const float* attn_norm, const float* ffn_norm) {
+    if (!codes || !absmax) return decode_fail(ALJ_ERR_BAD_ARG, "null layer pointer");
+    return register_layer(handle, layer, codes, nullptr, absmax, attn_norm, ffn_norm);
+}
+
+int aljabr_blackwell_register_decode_layer_typed(unsigned long long handle, int layer, const void* const* weights,
+                                                 const int* types, const void* const* absmax, const float* attn_norm,
+                                                 const float* ffn_norm) {
+    if (!types) return decode_fail(ALJ_ERR_BAD_ARG, "null type list");
+    return register_layer(handle, layer, weights, types, absmax, attn_norm, ffn_norm);
+}
+
+int aljabr_blackwell_register_output(unsigned long long handle, const void* embd_codes, const void* embd_absmax,
+                                     const void* head_codes, const void* head_absmax, const float* output_norm) {
+    return register_output(handle, embd_codes, ALJ_TYPE_NF4, embd_absmax, head_codes, ALJ_TYPE_NF4, head_absmax,
+                           output_norm);
+}
+
+int aljabr_blackwell_register_output_typed(unsigned long long handle, const void* embd, int embd_type,
+                                           const void* embd_absmax, const void* head, int head_type,
+                                           const void* head_absmax, const float* output_norm) {
+    return register_output(handle, embd, embd_type, embd_absmax, head, head_type, head_absmax, output_norm);
 }
 
 int aljabr_blackwell_decode_step_token(unsigned long long handle, int token, int pos, float* logits_out,

@@ -3,7 +3,9 @@
 Mirrors the reference's decode-step registration seam (the Metal bridge's
 registerDecodeLayer / registerOutput / decodeStepToken,
 engine/gguf/aljabr-gguf-java/.../javabackend/GgufMetalBridge.java:1879-2053)
-for a Llama-shaped model whose linear weights are NF4.
+for a Llama-shaped model whose linear weights are NF4 or, through
+register_layer_typed / register_output_typed, GGUF Q4_0 / Q8_0 / Q4_K / Q6_K
+with one type per tensor (registerDecodeLayer's typeQ .. typeDown).
 
 Weights may be given as numpy arrays (registered as model buffers: copied to
 HBM once, kept alive by this object) or as device addresses (ints, e.g.
@@ -93,6 +95,25 @@ class LlamaNf4Decoder:
         native.call("aljabr_blackwell_register_output", ctypes.c_ulonglong(self.handle),
                     ctypes.c_void_p(self._addr(embd_codes)), ctypes.c_void_p(self._addr(embd_absmax)),
                     ctypes.c_void_p(self._addr(head_codes)), ctypes.c_void_p(self._addr(head_absmax)), on.ctypes.data)
+
+    def register_layer_typed(self, layer: int, weights: list, types: list, attn_norm, ffn_norm, absmax=None):
+        """One GGUF type per tensor (native.TYPE_Q4_0 / Q8_0 / Q4_K / Q6_K / NF4),
+        as registerDecodeLayer's typeQ .. typeDown; absmax[i] only for NF4."""
+        w = (ctypes.c_void_p * 7)(*[self._addr(x) for x in weights])
+        t = (ctypes.c_int * 7)(*types)
+        a = None if absmax is None else (ctypes.c_void_p * 7)(*[None if x is None else self._addr(x) for x in absmax])
+        an = np.ascontiguousarray(attn_norm, dtype=np.float32)
+        fn = np.ascontiguousarray(ffn_norm, dtype=np.float32)
+        native.call("aljabr_blackwell_register_decode_layer_typed", ctypes.c_ulonglong(self.handle), layer, w, t, a,
+                    an.ctypes.data, fn.ctypes.data)
+
+    def register_output_typed(self, embd, embd_type: int, head, head_type: int, output_norm, embd_absmax=None,
+                              head_absmax=None):
+        on = np.ascontiguousarray(output_norm, dtype=np.float32)
+        ptr = (lambda a: None if a is None else ctypes.c_void_p(self._addr(a)))
+        native.call("aljabr_blackwell_register_output_typed", ctypes.c_ulonglong(self.handle),
+                    ctypes.c_void_p(self._addr(embd)), embd_type, ptr(embd_absmax), ctypes.c_void_p(self._addr(head)),
+                    head_type, ptr(head_absmax), on.ctypes.data)
 
     def sync_kv_cache(self, layer: int, seq_len: int, k, v):
         native.call("aljabr_blackwell_sync_kv_cache", ctypes.c_ulonglong(self.handle), layer, seq_len,

@@ -94,6 +94,8 @@ SIGNATURES = {
                                                   ctypes.POINTER(ctypes.c_ulonglong)]),
     "aljabr_blackwell_register_decode_layer": (_i, [ctypes.c_ulonglong, _i, _p, _p, _p, _p]),
     "aljabr_blackwell_register_output": (_i, [ctypes.c_ulonglong, _p, _p, _p, _p, _p]),
+    "aljabr_blackwell_register_decode_layer_typed": (_i, [ctypes.c_ulonglong, _i, _p, _p, _p, _p, _p]),
+    "aljabr_blackwell_register_output_typed": (_i, [ctypes.c_ulonglong, _p, _i, _p, _p, _i, _p, _p]),
     "aljabr_blackwell_decode_step_token": (_i, [ctypes.c_ulonglong, _i, _i, _p, _p]),
     "aljabr_blackwell_decode_run": (_i, [ctypes.c_ulonglong, _i, _i, _i, _p]),
     "aljabr_blackwell_sync_kv_cache": (_i, [ctypes.c_ulonglong, _i, _i, _p, _p]),

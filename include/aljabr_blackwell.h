@@ -234,7 +234,7 @@ int aljabr_blackwell_decode_attention_noalloc(float* out, const float* q, const 
                                               int kv_heads, int q_heads, int head_dim, int seq_len,
                                               int start_pos, float scale, void* stream);
 
-/* ---- full decode step (Llama-shaped, NF4 weights, one CUDA graph/token) ---
+/* ---- full decode step (Llama-shaped, NF4 or GGUF weights, one CUDA graph/token) ---
  * The device-resident form of GgufDecodePass.forward's layer loop
  * (engine/gguf/aljabr-gguf-java/.../GgufDecodePass.java:297-545), shaped like
  * the Metal provider's registered decode step (aljabr_metal_matvec_api.h:
@@ -258,6 +258,21 @@ int aljabr_blackwell_register_decode_layer(unsigned long long handle, int layer,
 /* Token embedding [vocab][hidden] (full on every rank) and lm_head rows. */
 int aljabr_blackwell_register_output(unsigned long long handle, const void* embd_codes, const void* embd_absmax,
                                      const void* head_codes, const void* head_absmax, const float* output_norm);
+/* The same two registrations with one GGUF type per tensor, as the Metal
+ * provider's aljabr_metal_register_decode_layer (typeQ .. typeDown) and
+ * aljabr_metal_register_output / register_token_embd (typeOutputW,
+ * typeEmbdW) take them (aljabr_metal_matvec_api.h:244-268).
+ * types[7] / embd_type / head_type: ALJ_TYPE_Q4_0, _Q8_0, _Q4_K, _Q6_K or
+ * _NF4; weights are row-major ggml blocks (NF4: packed codes); absmax may be
+ * NULL, its entries are read only for NF4 tensors.  Any GGUF-typed tensor
+ * makes the step run its residual adds, RMSNorms and SwiGLU as separate
+ * small launches; it needs tp_world 1 (ALJ_ERR_UNSUPPORTED otherwise). */
+int aljabr_blackwell_register_decode_layer_typed(unsigned long long handle, int layer, const void* const* weights,
+                                                 const int* types, const void* const* absmax, const float* attn_norm,
+                                                 const float* ffn_norm);
+int aljabr_blackwell_register_output_typed(unsigned long long handle, const void* embd, int embd_type,
+                                           const void* embd_absmax, const void* head, int head_type,
+                                           const void* head_absmax, const float* output_norm);
 /* One token at position `pos` (its K/V are written at pos; attention covers
  * [0, pos]).  logits_out: host float[vocab] or NULL; argmax_out: host int or
  * NULL (greedy next token). */

@@ -93,6 +93,7 @@ def _declare(L):
     L.orc_swiglu.argtypes = [_p, _p, _p, _i]
     L.orc_softmax.argtypes = [_p, _i]
     L.orc_decode_step_nf4.argtypes = [_p, _p, _p, _p, _p, _p, _i, _i, _i, _p, _p]
+    L.orc_decode_step_typed.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _p, _p]
 
 
 def _ptr(a):
@@ -315,4 +316,24 @@ def decode_step_nf4(cfg: LlamaCfg, codes: list, absmax: list, norms, k_cache, v_
     logits = np.empty(cfg.vocab, dtype=np.float32) if want_logits else None
     lib().orc_decode_step_nf4(ctypes.byref(cfg), cp, ap, _ptr(norms), _ptr(k_cache), _ptr(v_cache),
                               kv_bf16, token, pos, _ptr(x), _ptr(logits))
+    return x, logits
+
+
+def decode_step_typed(cfg: LlamaCfg, weights: list, types: list, absmax: list, norms, k_cache, v_cache,
+                      token: int, pos: int, want_logits: bool = True):
+    """decode_step_nf4 with one GGUF type per tensor (Q4_0 / Q8_0 / Q4_K /
+    Q6_K / NF4; absmax[i] is used only for NF4 tensors and may be None)."""
+    weights = [_c(w, np.uint8) for w in weights]
+    absmax = [None if a is None else _c(a, np.float32) for a in absmax]
+    wp = (ctypes.c_void_p * len(weights))(*[w.ctypes.data for w in weights])
+    ap = (ctypes.c_void_p * len(absmax))(*[None if a is None else a.ctypes.data for a in absmax])
+    tp = (ctypes.c_int * len(types))(*types)
+    norms = _c(norms, np.float32)
+    assert k_cache.dtype in (np.uint16, np.float32) and k_cache.flags.c_contiguous
+    assert v_cache.dtype == k_cache.dtype and v_cache.flags.c_contiguous
+    kv_bf16 = int(k_cache.dtype == np.uint16)
+    x = np.empty(cfg.hidden, dtype=np.float32)
+    logits = np.empty(cfg.vocab, dtype=np.float32) if want_logits else None
+    lib().orc_decode_step_typed(ctypes.byref(cfg), wp, tp, ap, _ptr(norms), _ptr(k_cache), _ptr(v_cache),
+                                kv_bf16, token, pos, _ptr(x), _ptr(logits))
     return x, logits

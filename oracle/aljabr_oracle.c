@@ -679,13 +679,87 @@ void orc_swiglu(const float* gate, const float* up, float* dst, int len) {   /* 
 }
 
 /* ------------------------------------------------------------------------ */
-static void nf4_matvec_seq(const uint8_t* codes, const float* absmax, const float* x, float* y, int K, int N, int g) {
-    for (int r = 0; r < N; r++) y[r] = nf4_row_dot(codes, absmax, x, K, g, r);
+static int64_t typed_row_bytes(int type, int K) {
+    switch (type) {
+        case ORC_Q4_0: return (int64_t)K / 32 * 18;
+        case ORC_Q8_0: return (int64_t)K / 32 * 34;
+        case ORC_Q4_K: return (int64_t)K / 256 * 144;
+        case ORC_Q6_K: return (int64_t)K / 256 * 210;
+        default: return (int64_t)K / 2;
+    }
 }
 
-void orc_decode_step_nf4(const orc_llama_cfg* c, const uint8_t* const* codes, const float* const* absmax,
-                         const float* norms, void* k_cache_v, void* v_cache_v, int kv_bf16,
-                         int token, int pos, float* x_out, float* logits) {
+/* y = W x with each row dotted in the reference's raw-row float order for
+ * the tensor's GGUF type (GgufRawDot's q4_0 / q8_0 / q4K / q6K routes), or
+ * AccelOps.linear's NF4 order. */
+static void typed_matvec_seq(int type, const uint8_t* w, const float* absmax, const float* x, float* y, int K, int N,
+                             int g) {
+    const int64_t rb = typed_row_bytes(type, K);
+    for (int r = 0; r < N; r++) {
+        const uint8_t* row = w + (int64_t)r * rb;
+        switch (type) {
+            case ORC_Q4_0: y[r] = orc_dot_row_q4_0(row, K, x); break;
+            case ORC_Q8_0: y[r] = orc_dot_row_q8_0_scalar(row, K, x); break;
+            case ORC_Q4_K: y[r] = orc_dot_row_q4_k(row, K, x); break;
+            case ORC_Q6_K: y[r] = orc_dot_row_q6_k(row, K, x); break;
+            default: y[r] = nf4_row_dot(w, absmax, x, K, g, r); break;
+        }
+    }
+}
+
+/* Row `token` of an embedding table as floats, in the reference's dequantiser
+ * order: Q4_0 / Q8_0 as GgufBlockDequantizer (orc_dequantize_q4_0 / _q8_0),
+ * Q4_K as GgufKBlockDequantizer.dequantizeQ4KBlock (:32-75: d1 = d * scale,
+ * m1 = dmin * min, value = d1 * q - m1), Q6_K as dequantizeQ6KBlock
+ * (:320-360: s = d * scale, value = s * (q - 32)), NF4 as
+ * DequantizationKernel.dequantizeNf4. */
+static void typed_embed_row(int type, const uint8_t* w, const float* absmax, int token, int H, int g, float* x) {
+    const uint8_t* row = w + (int64_t)token * typed_row_bytes(type, H);
+    if (type == ORC_Q4_0) {
+        orc_dequantize_q4_0(row, x, H);
+    } else if (type == ORC_Q8_0) {
+        orc_dequantize_q8_0(row, x, H);
+    } else if (type == ORC_Q4_K) {
+        for (int b = 0; b < H / 256; b++) {
+            const uint8_t* blk = row + (int64_t)b * 144;
+            const float d = orc_f16_to_f32(le16(blk)), dmin = orc_f16_to_f32(le16(blk + 2));
+            for (int e = 0; e < 256; e++) {
+                const int j = e / 64, t = e % 64, sb = 2 * j + (t >= 32);
+                const int byte = blk[16 + 32 * j + (t & 31)];
+                const int q = t < 32 ? (byte & 15) : (byte >> 4);
+                int sc, mn;
+                q4k_scale_min(blk + 4, sb, &sc, &mn);
+                const float d1 = d * (float)sc, m1 = dmin * (float)mn;
+                x[b * 256 + e] = d1 * (float)q - m1;
+            }
+        }
+    } else if (type == ORC_Q6_K) {
+        for (int b = 0; b < H / 256; b++) {
+            const uint8_t* blk = row + (int64_t)b * 210;
+            const float d = orc_f16_to_f32(le16(blk + 208));
+            for (int e = 0; e < 256; e++) {
+                const int h = e / 128, w2 = e % 128, k = w2 / 32, i = w2 % 32;
+                const int lo = blk[64 * h + 32 * (k & 1) + i];
+                const int hb = blk[128 + 32 * h + i];
+                const int q = (((k >> 1) ? (lo >> 4) : (lo & 15)) | (((hb >> (2 * k)) & 3) << 4)) - 32;
+                const float s = d * (float)(int8_t)blk[192 + 8 * h + 2 * k + i / 16];
+                x[b * 256 + e] = s * (float)q;
+            }
+        }
+    } else {
+        const int64_t base = (int64_t)token * H;
+        for (int k2 = 0; k2 < H; k2++) {
+            const int64_t e = base + k2;
+            const int bb = w[e >> 1];
+            const int code = (e & 1) ? (bb & 15) : ((bb >> 4) & 15);
+            x[k2] = NF4_TABLE[code] * absmax[((e >> 1) * 2) / g];
+        }
+    }
+}
+
+void orc_decode_step_typed(const orc_llama_cfg* c, const uint8_t* const* codes, const int* types,
+                           const float* const* absmax, const float* norms, void* k_cache_v, void* v_cache_v,
+                           int kv_bf16, int token, int pos, float* x_out, float* logits) {
     int H = c->hidden, D = c->head_dim, Hq = c->q_heads, Hkv = c->kv_heads, F = c->ffn;
     int QD = Hq * D, KVD = Hkv * D, L = c->layers, g = c->group;
     float* x = (float*)calloc((size_t)H, 4);
@@ -701,24 +775,17 @@ void orc_decode_step_nf4(const orc_llama_cfg* c, const uint8_t* const* codes, co
     float* kf = (float*)calloc((size_t)(pos + 1) * KVD, 4);
     float* vf = (float*)calloc((size_t)(pos + 1) * KVD, 4);
 
-    /* embedding row: NF4 dequantisation of row `token` (tensor 7*L) */
-    {
-        int64_t base = (int64_t)token * H;
-        for (int k2 = 0; k2 < H; k2++) {
-            int64_t e = base + k2;
-            int b = codes[7 * L][e >> 1];
-            int code = (e & 1) ? (b & 15) : ((b >> 4) & 15);
-            x[k2] = NF4_TABLE[code] * absmax[7 * L][((e >> 1) * 2) / g];
-        }
-    }
+    /* embedding row `token` (tensor 7*L) */
+    typed_embed_row(types[7 * L], codes[7 * L], absmax[7 * L], token, H, g, x);
     float scale = (float)(1.0 / sqrt((double)D));                           /* DP:368-377 */
     for (int l = 0; l < L; l++) {
         const uint8_t* const* cw = codes + 7 * l;
         const float* const* aw = absmax + 7 * l;
+        const int* tw = types + 7 * l;
         orc_rms_norm(x, norms + (size_t)l * 2 * H, xb, H, c->eps);             /* DP:305 */
-        nf4_matvec_seq(cw[0], aw[0], xb, q, H, QD, g);                           /* DP:309 */
-        nf4_matvec_seq(cw[1], aw[1], xb, k, H, KVD, g);
-        nf4_matvec_seq(cw[2], aw[2], xb, v, H, KVD, g);
+        typed_matvec_seq(tw[0], cw[0], aw[0], xb, q, H, QD, g);                           /* DP:309 */
+        typed_matvec_seq(tw[1], cw[1], aw[1], xb, k, H, KVD, g);
+        typed_matvec_seq(tw[2], cw[2], aw[2], xb, v, H, KVD, g);
         orc_rope(q, Hq, D, D, pos, c->rope_theta);                               /* DP:333 */
         orc_rope(k, Hkv, D, D, pos, c->rope_theta);                              /* DP:360 */
         size_t lbase = (size_t)l * c->max_ctx * KVD;
@@ -742,20 +809,30 @@ void orc_decode_step_nf4(const orc_llama_cfg* c, const uint8_t* const* codes, co
             memcpy(vf, vc + lbase, sizeof(float) * (size_t)(pos + 1) * KVD);
         }
         orc_gqa_decode_attention(q, att, scores, kf, vf, KVD, Hkv, Hq, D, pos + 1, 0, scale);   /* DP:386 */
-        nf4_matvec_seq(cw[3], aw[3], att, xb, QD, H, g);                         /* DP:475 */
+        typed_matvec_seq(tw[3], cw[3], aw[3], att, xb, QD, H, g);                         /* DP:475 */
         for (int i = 0; i < H; i++) x[i] += xb[i];                               /* DP:481 */
         orc_rms_norm(x, norms + (size_t)l * 2 * H + H, xb, H, c->eps);           /* DP:485 */
-        nf4_matvec_seq(cw[4], aw[4], xb, gate, H, F, g);                         /* DP:492 */
-        nf4_matvec_seq(cw[5], aw[5], xb, up, H, F, g);
+        typed_matvec_seq(tw[4], cw[4], aw[4], xb, gate, H, F, g);                         /* DP:492 */
+        typed_matvec_seq(tw[5], cw[5], aw[5], xb, up, H, F, g);
         orc_swiglu(gate, up, hb, F);                                             /* DP:497 */
-        nf4_matvec_seq(cw[6], aw[6], hb, xb, F, H, g);                           /* DP:504 */
+        typed_matvec_seq(tw[6], cw[6], aw[6], hb, xb, F, H, g);                           /* DP:504 */
         for (int i = 0; i < H; i++) x[i] += xb[i];                               /* DP:511 */
     }
     memcpy(x_out, x, sizeof(float) * H);
     if (logits) {
         orc_rms_norm(x, norms + (size_t)L * 2 * H, xb, H, c->eps);
-        nf4_matvec_seq(codes[7 * L + 1], absmax[7 * L + 1], xb, logits, H, c->vocab, g);
+        typed_matvec_seq(types[7 * L + 1], codes[7 * L + 1], absmax[7 * L + 1], xb, logits, H, c->vocab, g);
     }
     free(x); free(xb); free(q); free(k); free(v); free(att); free(gate); free(up); free(hb);
     free(scores); free(kf); free(vf);
+}
+
+void orc_decode_step_nf4(const orc_llama_cfg* c, const uint8_t* const* codes, const float* const* absmax,
+                         const float* norms, void* k_cache_v, void* v_cache_v, int kv_bf16,
+                         int token, int pos, float* x_out, float* logits) {
+    const int n = 7 * c->layers + 2;
+    int* types = (int*)malloc(sizeof(int) * (size_t)n);
+    for (int i = 0; i < n; i++) types[i] = ORC_NF4;
+    orc_decode_step_typed(c, codes, types, absmax, norms, k_cache_v, v_cache_v, kv_bf16, token, pos, x_out, logits);
+    free(types);
 }

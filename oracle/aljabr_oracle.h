@@ -109,6 +109,12 @@ void orc_decode_step_nf4(const orc_llama_cfg* cfg,
                          const float* norms,   /* [layers][2][H] (attn, ffn) then [H] output norm */
                          void* k_cache, void* v_cache, int kv_bf16,
                          int token, int pos, float* x_out, float* logits);
+/* The same step with one GGUF type per tensor (types[7*layers + 2], ORC_*;
+ * absmax entries only for ORC_NF4 tensors): RawDot row order per type, the
+ * reference's dequantiser order for the embedding row. */
+void orc_decode_step_typed(const orc_llama_cfg* cfg, const uint8_t* const* w, const int* types,
+                           const float* const* absmax, const float* norms, void* k_cache, void* v_cache,
+                           int kv_bf16, int token, int pos, float* x_out, float* logits);
 
 #ifdef __cplusplus
 }
