@@ -573,10 +573,36 @@ def run_decode(args, rank, world, dev, tokens_per_run=32, runs=4):
         obj = [nccl_unique_id() if rank == 0 else None]
         torch.distributed.broadcast_object_list(obj, src=0)
         nid = obj[0]
+    from aljabr_b200 import native
+    wkind = getattr(args, "decode_weights", "nf4")
+    if wkind != "nf4" and world > 1:
+        raise SystemExit("GGUF-typed decode weights run on one GPU (tensor parallel decode is NF4)")
     dec = LlamaNf4Decoder(s, tp_world=world, tp_rank=rank, nccl_id=nid)
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
     keep = []
+    # GGUF blocks: (bytes, values, [(byte offset of an fp16 scale, its bits)]);
+    # random code bytes, fixed small scales (every code pattern is valid).
+    gguf_layout = {native.TYPE_Q4_0: (18, 32, [(0, 0x1C00)]), native.TYPE_Q8_0: (34, 32, [(0, 0x1400)]),
+                   native.TYPE_Q4_K: (144, 256, [(0, 0x0800), (2, 0x0C00)]),
+                   native.TYPE_Q6_K: (210, 256, [(208, 0x0200)])}
+    if wkind == "q4_0":
+        layer_types = [native.TYPE_Q4_0] * 7
+        embd_type = head_type = native.TYPE_Q4_0
+    else:   # llama.cpp's Q4_K_M mix: Q4_K, with Q6_K for attn_v, ffn_down and the output matrix
+        T4, T6 = native.TYPE_Q4_K, native.TYPE_Q6_K
+        layer_types = [T4, T4, T6, T4, T4, T4, T6]
+        embd_type, head_type = T4, T6
+
+    def gguf(t, rows, cols):
+        bb, per, scales = gguf_layout[t]
+        nblk = rows * cols // per
+        w = torch.randint(0, 256, (nblk * bb,), dtype=torch.uint8, device=dev, generator=g)
+        v = w.view(nblk, bb)
+        for off, bits in scales:
+            v[:, off], v[:, off + 1] = bits & 0xFF, bits >> 8
+        keep.append(w)
+        return w.data_ptr(), w.numel()
 
     def nf4(rows, cols):
         c = torch.randint(0, 256, (rows * cols // 2,), dtype=torch.uint8, device=dev, generator=g)
@@ -586,7 +612,20 @@ def run_decode(args, rank, world, dev, tokens_per_run=32, runs=4):
 
     H = s.hidden
     weight_bytes = 0
-    for layer in range(s.layers):
+    for layer in range(s.layers if wkind != "nf4" else 0):
+        ws = []
+        for n, t in zip(("q", "k", "v", "o", "gate", "up", "down"), layer_types):
+            p, nb = gguf(t, s.rows(n), s.cols(n))
+            ws.append(p)
+            weight_bytes += nb
+        norm = np.ones(H, np.float32)
+        dec.register_layer_typed(layer, ws, layer_types, norm, norm)
+    if wkind != "nf4":
+        ep, _ = gguf(embd_type, s.vocab, H)
+        hp, nb = gguf(head_type, s.vocab, H)
+        weight_bytes += nb
+        dec.register_output_typed(ep, embd_type, hp, head_type, np.ones(H, np.float32))
+    for layer in range(s.layers if wkind == "nf4" else 0):
         cs, As = [], []
         for n in ("q", "k", "v", "o", "gate", "up", "down"):
             rows = s.rows(n) // world
@@ -596,10 +635,11 @@ def run_decode(args, rank, world, dev, tokens_per_run=32, runs=4):
             As.append(a)
         norm = np.ones(H, np.float32)
         dec.register_layer(layer, cs, As, norm, norm)
-    ec, ea = nf4(s.vocab, H)
-    hc, ha = nf4(s.vocab // world, H)
-    weight_bytes += (s.vocab // world) * H // 2 + (s.vocab // world) * H // s.group * 4
-    dec.register_output(ec, ea, hc, ha, np.ones(H, np.float32))
+    if wkind == "nf4":
+        ec, ea = nf4(s.vocab, H)
+        hc, ha = nf4(s.vocab // world, H)
+        weight_bytes += (s.vocab // world) * H // 2 + (s.vocab // world) * H // s.group * 4
+        dec.register_output(ec, ea, hc, ha, np.ones(H, np.float32))
     kvd = s.kv_heads // world * s.head_dim
     for layer in range(s.layers):
         k = torch.randn(s.max_ctx, kvd, device=dev, generator=g).to(torch.bfloat16)
@@ -641,7 +681,12 @@ def run_decode(args, rank, world, dev, tokens_per_run=32, runs=4):
             "hbm_frac_of_measured_peak": round(per_gpu * tok_s / 1e9 / peak, 4),
             "e2e_tok_per_s": round(tokens_per_run / dt_e2e, 1),
             "timer": "host wall clock around decode_run (32-token greedy runs, one sync each); max over ranks",
-            "config": "Llama-3-8B shape, NF4 b64 linear + lm_head + embedding, bf16 KV ctx 4096, random weights"}
+            "weights": wkind,
+            "config": "Llama-3-8B shape, " + {"nf4": "NF4 b64 linear + lm_head + embedding",
+                                               "q4_0": "GGUF Q4_0 linear + lm_head + embedding",
+                                               "q4_k_m": "GGUF Q4_K linear + embedding, Q6_K attn_v / ffn_down / "
+                                                         "lm_head (llama.cpp Q4_K_M mix)"}[wkind]
+                      + ", bf16 KV ctx 4096, random weights"}
 
 
 # ----------------------------------------------------------------- CPU legs
@@ -738,6 +783,8 @@ def main():
     ap.add_argument("--only", choices=["nf4", "q8", "attention", "decode", "c5", "kquant"],
                     help="run one secondary workload alone (for profiling); prints its dict")
     ap.add_argument("--decode-tokens", type=int, default=32)
+    ap.add_argument("--decode-weights", default="nf4", choices=["nf4", "q4_0", "q4_k_m"],
+                    help="weight formats of the --only decode model (GGUF types on one GPU only)")
     ap.add_argument("--c5-tokens", default="1,16,64,512",
                     help="token counts of the batched-NF4 (C5) section, comma separated")
     args = ap.parse_args()
