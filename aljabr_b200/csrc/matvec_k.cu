@@ -14,7 +14,7 @@
 // bits 2k..2k+1 of qh[32h + i] above it, minus 32, times
 // d*scales[8h + 2k + i/16].
 //
-// A CTA serves kKRows consecutive rows; its 8 warps deal out "tasks" (a few
+// A CTA serves 4 consecutive rows (8 for Q4_K with K <= 4096); its 8 warps deal out "tasks" (a few
 // blocks of one row subset) and meet in shared memory at the end, summed in
 // fixed order (deterministic).  Within a task consecutive lanes read
 // consecutive code bytes, and each lane loads its x values once for all the
@@ -86,16 +86,16 @@ __device__ __forceinline__ void q4k_pair_scales(const uint4& hd, int j, uint32_t
 // (and their two sums) are loaded once per task and serve the task's RS rows.
 // Each nibble becomes a float with one LOP3 into the mantissa of 2^(23 - p) at
 // its own bit position p (no shifts for bytes 0..2) and one packed subtract.
-template <int RS>
+template <int R, int RS>
 __global__ void __launch_bounds__(kKWarps * 32, 3) q4k_matvec_kernel(const KRows p) {
     pdl_launch_dependents();
     pdl_wait();   // x may come from the previous kernel
-    constexpr int kSub = kKRows / RS;   // row subsets; warp w always serves subset w % kSub
+    constexpr int kSub = R / RS;   // row subsets; warp w always serves subset w % kSub
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row0 = blockIdx.x * kKRows;
+    const int row0 = blockIdx.x * R;
     const int nb = p.K / 256;
     const size_t row_bytes = static_cast<size_t>(nb) * 144;
-    if (threadIdx.x == 0) prefetch_rows_l2(p.w + row0 * row_bytes, min(kKRows, p.N - row0) * row_bytes);
+    if (threadIdx.x == 0) prefetch_rows_l2(p.w + row0 * row_bytes, min(R, p.N - row0) * row_bytes);
     const int bl = lane >> 3, c = lane & 7, j = c >> 1;
     const int sub = warp % kSub;
     const uint8_t* rowp[RS];
@@ -161,9 +161,9 @@ __global__ void __launch_bounds__(kKWarps * 32, 3) q4k_matvec_kernel(const KRows
         }
     }
     // warp sums into this warp's row subset, then the 8 warps in fixed order
-    __shared__ float red[kKWarps][kKRows];
+    __shared__ float red[kKWarps][R];
 #pragma unroll
-    for (int r = 0; r < kKRows; ++r) {
+    for (int r = 0; r < R; ++r) {
         const int rs = r - sub * RS;
         float v = 0.0f;
 #pragma unroll
@@ -173,7 +173,7 @@ __global__ void __launch_bounds__(kKWarps * 32, 3) q4k_matvec_kernel(const KRows
         if (lane == 0) red[warp][r] = v;
     }
     __syncthreads();
-    if (warp == 0 && lane < kKRows && row0 + lane < p.N) {
+    if (warp == 0 && lane < R && row0 + lane < p.N) {
         float out = 0.0f;
 #pragma unroll
         for (int w = 0; w < kKWarps; ++w) out += red[w][lane];
@@ -328,7 +328,6 @@ cudaError_t launch_matvec_k(int fmt, const MatvecParams& mp, cudaStream_t stream
         if (reinterpret_cast<uintptr_t>(sg.w) & (fmt == FMT_Q4_K ? 15 : 1)) return cudaErrorNotSupported;
         KRows p{sg.w, mp.x, sg.y, sg.bias, sg.residual, mp.K, sg.rows};
         cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((sg.rows + kKRows - 1) / kKRows);
         cfg.blockDim = dim3(kKWarps * 32);
         cfg.stream = stream;
         cudaLaunchAttribute attr[1];
@@ -337,12 +336,18 @@ cudaError_t launch_matvec_k(int fmt, const MatvecParams& mp, cudaStream_t stream
         cfg.attrs = attr;
         cfg.numAttrs = pdl ? 1 : 0;
         void (*kern)(const KRows);
-        if (fmt == FMT_Q4_K) {
+        int cta_rows = kKRows;
+        if (fmt == FMT_Q4_K && mp.K <= 4096) {
+            // short rows: 8-row CTAs, each lane walking 4 rows (x loads shared over 4)
+            cta_rows = 8;
+            kern = q4k_matvec_kernel<8, 4>;
+        } else if (fmt == FMT_Q4_K) {
             const int rs = q4k_rows_per_lane(mp.K / 256);
-            kern = rs == 4 ? q4k_matvec_kernel<4> : rs == 2 ? q4k_matvec_kernel<2> : q4k_matvec_kernel<1>;
+            kern = rs == 4 ? q4k_matvec_kernel<4, 4> : rs == 2 ? q4k_matvec_kernel<4, 2> : q4k_matvec_kernel<4, 1>;
         } else {
             kern = q6k_rows_per_lane(mp.K / 256) == 2 ? q6k_matvec_kernel<2> : q6k_matvec_kernel<1>;
         }
+        cfg.gridDim = dim3((sg.rows + cta_rows - 1) / cta_rows);
         const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
         if (e != cudaSuccess) return e;
     }

@@ -63,7 +63,7 @@ def test_golden_known_answers(lib, golden):
 
 @pytest.mark.parametrize("kind", [oracle.Q4_K, oracle.Q6_K])
 @pytest.mark.parametrize("N,K", [(1, 256), (7, 512), (37, 2816), (300, 2048), (4096, 4096), (1024, 14336),
-                                 (14336, 4096)])
+                                 (14336, 4096), (33, 5120), (40, 11264)])
 def test_matches_oracle_and_fp64(lib, kind, N, K):
     w = synth.k_quant(kind, 100 + N + kind, N, K)
     x = synth.activation(200 + K, K)
