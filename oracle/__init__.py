@@ -45,8 +45,7 @@ _lib = None
 def lib():
     global _lib
     if _lib is None:
-        if not os.path.exists(_LIB):
-            build()
+        build()   # compiles only when the library is missing or older than the sources
         _lib = ctypes.CDLL(_LIB)
         _declare(_lib)
     return _lib
@@ -94,6 +93,7 @@ def _declare(L):
     L.orc_softmax.argtypes = [_p, _i]
     L.orc_decode_step_nf4.argtypes = [_p, _p, _p, _p, _p, _p, _i, _i, _i, _p, _p]
     L.orc_decode_step_typed.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _p, _p]
+    L.orc_dequantize_row_ref.argtypes = [_i, _p, _i, _p]
 
 
 def _ptr(a):
@@ -234,6 +234,16 @@ def dequantize_k_row(kind: int, row, columns: int) -> np.ndarray:
     row = _c(row, np.uint8)
     out = np.empty(columns, dtype=np.float64)
     lib().orc_dequantize_k_row(kind, _ptr(row), columns, _ptr(out))
+    return out
+
+
+def dequantize_row_ref(kind: int, row, columns: int) -> np.ndarray:
+    """One GGUF row as float32 in the reference's dequantiser order
+    (GgufBlockDequantizer / GgufKBlockDequantizer), as the typed decode
+    step's embedding lookup uses it."""
+    row = _c(row, np.uint8)
+    out = np.empty(columns, dtype=np.float32)
+    lib().orc_dequantize_row_ref(kind, _ptr(row), columns, _ptr(out))
     return out
 
 

@@ -707,20 +707,18 @@ static void typed_matvec_seq(int type, const uint8_t* w, const float* absmax, co
     }
 }
 
-/* Row `token` of an embedding table as floats, in the reference's dequantiser
+/* One GGUF row (`cols` values) as floats, in the reference's dequantiser
  * order: Q4_0 / Q8_0 as GgufBlockDequantizer (orc_dequantize_q4_0 / _q8_0),
  * Q4_K as GgufKBlockDequantizer.dequantizeQ4KBlock (:32-75: d1 = d * scale,
  * m1 = dmin * min, value = d1 * q - m1), Q6_K as dequantizeQ6KBlock
- * (:320-360: s = d * scale, value = s * (q - 32)), NF4 as
- * DequantizationKernel.dequantizeNf4. */
-static void typed_embed_row(int type, const uint8_t* w, const float* absmax, int token, int H, int g, float* x) {
-    const uint8_t* row = w + (int64_t)token * typed_row_bytes(type, H);
+ * (:320-360: s = d * scale, value = s * (q - 32)). */
+void orc_dequantize_row_ref(int type, const uint8_t* row, int cols, float* x) {
     if (type == ORC_Q4_0) {
-        orc_dequantize_q4_0(row, x, H);
+        orc_dequantize_q4_0(row, x, cols);
     } else if (type == ORC_Q8_0) {
-        orc_dequantize_q8_0(row, x, H);
+        orc_dequantize_q8_0(row, x, cols);
     } else if (type == ORC_Q4_K) {
-        for (int b = 0; b < H / 256; b++) {
+        for (int b = 0; b < cols / 256; b++) {
             const uint8_t* blk = row + (int64_t)b * 144;
             const float d = orc_f16_to_f32(le16(blk)), dmin = orc_f16_to_f32(le16(blk + 2));
             for (int e = 0; e < 256; e++) {
@@ -734,7 +732,7 @@ static void typed_embed_row(int type, const uint8_t* w, const float* absmax, int
             }
         }
     } else if (type == ORC_Q6_K) {
-        for (int b = 0; b < H / 256; b++) {
+        for (int b = 0; b < cols / 256; b++) {
             const uint8_t* blk = row + (int64_t)b * 210;
             const float d = orc_f16_to_f32(le16(blk + 208));
             for (int e = 0; e < 256; e++) {
@@ -746,14 +744,22 @@ static void typed_embed_row(int type, const uint8_t* w, const float* absmax, int
                 x[b * 256 + e] = s * (float)q;
             }
         }
-    } else {
-        const int64_t base = (int64_t)token * H;
-        for (int k2 = 0; k2 < H; k2++) {
-            const int64_t e = base + k2;
-            const int bb = w[e >> 1];
-            const int code = (e & 1) ? (bb & 15) : ((bb >> 4) & 15);
-            x[k2] = NF4_TABLE[code] * absmax[((e >> 1) * 2) / g];
-        }
+    }
+}
+
+/* Row `token` of an embedding table as floats: orc_dequantize_row_ref for the
+ * GGUF types, DequantizationKernel.dequantizeNf4 for NF4. */
+static void typed_embed_row(int type, const uint8_t* w, const float* absmax, int token, int H, int g, float* x) {
+    if (type != ORC_NF4) {
+        orc_dequantize_row_ref(type, w + (int64_t)token * typed_row_bytes(type, H), H, x);
+        return;
+    }
+    const int64_t base = (int64_t)token * H;
+    for (int k2 = 0; k2 < H; k2++) {
+        const int64_t e = base + k2;
+        const int bb = w[e >> 1];
+        const int code = (e & 1) ? (bb & 15) : ((bb >> 4) & 15);
+        x[k2] = NF4_TABLE[code] * absmax[((e >> 1) * 2) / g];
     }
 }
 

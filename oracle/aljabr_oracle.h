@@ -109,6 +109,10 @@ void orc_decode_step_nf4(const orc_llama_cfg* cfg,
                          const float* norms,   /* [layers][2][H] (attn, ffn) then [H] output norm */
                          void* k_cache, void* v_cache, int kv_bf16,
                          int token, int pos, float* x_out, float* logits);
+/* One GGUF row (Q4_0 / Q8_0 / Q4_K / Q6_K) in the reference's dequantiser
+ * float order (GgufBlockDequantizer, GgufKBlockDequantizer). */
+void orc_dequantize_row_ref(int type, const uint8_t* row, int cols, float* out);
+
 /* The same step with one GGUF type per tensor (types[7*layers + 2], ORC_*;
  * absmax entries only for ORC_NF4 tensors): RawDot row order per type, the
  * reference's dequantiser order for the embedding row. */

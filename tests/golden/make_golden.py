@@ -242,6 +242,17 @@ def main():
         type=14, K=256, N=2, weights=q6_lane + q6_lane, x=ramp(256),
         expected=[q6k_expected_dot(ramp(256))] * 2, tol=0.0))
 
+    # K-quant row dequantisation (GgufKBlockDequantizer, the embedding-row path)
+    fx.append(dict(
+        name="q4_k_simple_block_dequant", kind="k_dequant",
+        source=f"{RT_TEST}/GgufQ4KTest.java:17-35, GgufQ4Fx.java:13-24",
+        type=12, K=256, weights=[0x00, 0x3C, 0x00, 0x00] + [1, 1, 1, 1, 0, 0, 0, 0, 1, 1, 1, 1] + [0x21] * 128,
+        expected=([1.0] * 32 + [2.0] * 32) * 4, tol=0.0))
+    fx.append(dict(
+        name="q6_k_uniform_block_dequant", kind="k_dequant",
+        source=f"{RT_TEST}/GgufQ6KTest.java:18-32, GgufQ6Fx.java:13-28",
+        type=14, K=256, weights=q6k_block(0x11, 0xAA, 1), expected=[1.0] * 256, tol=0.0))
+
     out = os.path.join(os.path.dirname(os.path.abspath(__file__)), "known_answers.json")
     with open(out, "w") as f:
         json.dump({"generator": "tests/golden/make_golden.py", "fixtures": fx}, f, indent=1)

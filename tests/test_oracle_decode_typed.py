@@ -51,3 +51,32 @@ def test_typed_step_logits_use_the_row_dots():
     head = weights[8].reshape(64, -1)
     ref = np.array([oracle.dot_row_q4_0(head[r], xn) for r in range(64)], np.float32)
     np.testing.assert_array_equal(logits.view(np.uint32), ref.view(np.uint32))
+
+
+def test_row_dequantiser_known_answers(golden):
+    """orc_dequantize_row_ref (the typed step's embedding lookup) reproduces the
+    reference's GgufQ4KTest / GgufQ6KTest dequantised rows exactly."""
+    seen = set()
+    for fx in golden.values():
+        if fx["kind"] != "k_dequant":
+            continue
+        seen.add(fx["type"])
+        got = oracle.dequantize_row_ref(fx["type"], np.array(fx["weights"], np.uint8), fx["K"])
+        np.testing.assert_array_equal(got, np.array(fx["expected"], np.float32), err_msg=fx["name"])
+    assert seen == {oracle.Q4_K, oracle.Q6_K}
+
+
+def test_row_dequantiser_matches_element_formulas():
+    """Random K-quant rows: the float-order dequantiser is within float
+    rounding of the fp64 element formulas; Q4_0 / Q8_0 are the block
+    dequantisers themselves."""
+    from tests import synth
+    for kind in (oracle.Q4_K, oracle.Q6_K):
+        row = synth.k_quant(kind, 17 + kind, 1, 1024)
+        got = oracle.dequantize_row_ref(kind, row, 1024).astype(np.float64)
+        ref = oracle.dequantize_k_row(kind, row, 1024)
+        assert np.max(np.abs(got - ref) / np.maximum(np.abs(ref), 1e-6)) < 1e-6
+    vals = np.random.default_rng(2).normal(0, 1, 256).astype(np.float32)
+    w4, w8 = oracle.encode_q4_0(vals), oracle.encode_q8_0(vals)
+    np.testing.assert_array_equal(oracle.dequantize_row_ref(oracle.Q4_0, w4, 256), oracle.dequantize_q4_0(w4, 256))
+    np.testing.assert_array_equal(oracle.dequantize_row_ref(oracle.Q8_0, w8, 256), oracle.dequantize_q8_0(w8, 256))
