@@ -26,9 +26,18 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import native
-from .native import TYPE_NF4, TYPE_Q4_0, TYPE_Q8_0, UnsupportedOperation
+from .native import TYPE_NF4, TYPE_Q4_0, TYPE_Q4_K, TYPE_Q6_K, TYPE_Q8_0, UnsupportedOperation
 
 BLOCK_BYTES = {TYPE_Q4_0: 18, TYPE_Q8_0: 34}
+# Types whose matvec the bridge routes, as GgufMetalBridge.matVec routes Q4_K,
+# Q6_K and Q8_0 (GgufMetalBridge.java:701-716) -- plus Q4_0, which this
+# provider serves natively where the Metal bridge leaves it to the CPU.
+MATVEC_ENTRY = {
+    TYPE_Q4_0: "aljabr_blackwell_matvec_tb_q4_0",
+    TYPE_Q8_0: "aljabr_blackwell_matvec_tb_q8_0",
+    TYPE_Q4_K: "aljabr_blackwell_matvec_tb_q4_k",
+    TYPE_Q6_K: "aljabr_blackwell_matvec_tb_q6_k",
+}
 
 
 @dataclass(frozen=True)
@@ -102,7 +111,9 @@ class GgufBlackwellBridge:
 
     @staticmethod
     def is_type_supported(type_id: int) -> bool:
-        return type_id in (TYPE_Q4_0, TYPE_Q8_0)
+        """GgufMetalBridge.isTypeSupported (GgufMetalBridge.java:604-606) for the
+        types this provider has kernels for."""
+        return type_id in MATVEC_ENTRY
 
     @classmethod
     def mat_vec(cls, model: GgufModel, tensor: GgufTensor, vector: np.ndarray, output: np.ndarray) -> bool:
@@ -110,7 +121,7 @@ class GgufBlackwellBridge:
         K, N = tensor.columns, tensor.rows
         if vector.size < K or output.size < N:
             raise ValueError("vector/output shorter than the tensor's columns/rows")
-        fn = {TYPE_Q4_0: "aljabr_blackwell_matvec_tb_q4_0", TYPE_Q8_0: "aljabr_blackwell_matvec_tb_q8_0"}.get(tensor.type_id)
+        fn = MATVEC_ENTRY.get(tensor.type_id)
         if fn is None:
             raise UnsupportedOperation(native.ALJ_ERR_UNSUPPORTED, f"GGUF type {tensor.type_id} ({tensor.name})")
         native.call(fn, _fptr(output), _fptr(vector), ctypes.c_void_p(model.address(tensor)), K, N)

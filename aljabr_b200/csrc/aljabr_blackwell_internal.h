@@ -155,6 +155,11 @@ int gemm_nf4_tiles(int M, int nseg, const int* rows);
 size_t gemm_nf4_workspace_bytes(int M, int K, int total_tiles, int grid);
 cudaError_t launch_gemm_nf4(const GemmNf4Args& a, cudaStream_t stream);
 
+// Decode glue of the FFM binding (glue.cu): one-CTA RMSNorm and the
+// elementwise SiLU-gated product.
+cudaError_t launch_rmsnorm(float* out, const float* x, const float* w, int n, float eps, cudaStream_t stream);
+cudaError_t launch_silu_ffn(float* out, const float* gate, const float* up, int n, int sms, cudaStream_t stream);
+
 int sm_count_for_current_device();
 
 }  // namespace alj

@@ -366,8 +366,48 @@ int run_attention(DeviceState* st, float* dout, const float* dq, const void* k, 
     if (p.splits > 1) {
         ALJ_CUDA(scratch->ensure(attention_scratch_floats(q_heads, head_dim, p.splits) * 4));
         attention_bind_scratch(p, static_cast<float*>(scratch->p));
+        // The split merge's arrival counters must start at zero.  Clear them on
+        // the launch stream itself: the stream may be non-blocking (the
+        // library's own) or the caller's, so a memset on any other stream
+        // would not be ordered before the kernel.
+        ALJ_CUDA(cudaMemsetAsync(p.split_counter, 0, static_cast<size_t>(q_heads) * sizeof(unsigned int), stream));
     }
     return launch_status(launch_attention(p, stream, false), "decode attention");
+}
+
+// The binding's elementwise glue (rmsnorm, silu_ffn): operands that are
+// device, managed or registered memory are used in place; plain host
+// operands are staged through the device scratch.  Blocks until out is
+// written.  kind 0: out = rmsnorm(a; weight b, eps); kind 1: out = silu(a) * b.
+int glue_call(int kind, float* out, const float* a, const float* b, int n, float eps) {
+    int err = 0;
+    DeviceState* st = state(&err);
+    if (!st) return err;
+    if (!out || !a || !b) return fail(ALJ_ERR_BAD_ARG, "null pointer argument");
+    if (n <= 0 || n > (1 << 24)) return fail(ALJ_ERR_BAD_DIMS, "N=%d must be in [1, 2^24]", n);
+    const float* da = static_cast<const float*>(resolve(st, a));
+    const float* db = static_cast<const float*>(resolve(st, b));
+    float* dout = const_cast<float*>(static_cast<const float*>(resolve(st, out)));
+    std::lock_guard<std::mutex> g(st->mu);
+    const size_t bytes = static_cast<size_t>(n) * 4;
+    ALJ_CUDA(st->dtmp.ensure(3 * bytes));
+    float* slot = static_cast<float*>(st->dtmp.p);
+    if (!da) {
+        ALJ_CUDA(cudaMemcpyAsync(slot, a, bytes, cudaMemcpyHostToDevice, st->stream));
+        da = slot;
+    }
+    if (!db) {
+        ALJ_CUDA(cudaMemcpyAsync(slot + n, b, bytes, cudaMemcpyHostToDevice, st->stream));
+        db = slot + n;
+    }
+    float* dst = dout ? dout : slot + 2 * static_cast<size_t>(n);
+    const cudaError_t e = kind == 0 ? launch_rmsnorm(dst, da, db, n, eps, st->stream)
+                                    : launch_silu_ffn(dst, da, db, n, st->sms, st->stream);
+    int rc = launch_status(e, kind == 0 ? "rmsnorm" : "silu_ffn");
+    if (rc) return rc;
+    if (!dout) ALJ_CUDA(cudaMemcpyAsync(out, dst, bytes, cudaMemcpyDeviceToHost, st->stream));
+    ALJ_CUDA(cudaStreamSynchronize(st->stream));
+    return ALJ_OK;
 }
 
 }  // namespace
@@ -379,6 +419,7 @@ int sm_count_for_current_device() {
 }
 
 int decode_fail(int code, const char* msg) { return fail(code, "%s", msg); }
+void noalloc_forget_scratch();   // noalloc.cu
 
 const void* decode_resolve(const void* p) {
     int err = 0;
@@ -419,12 +460,45 @@ int aljabr_blackwell_device_count(void) {
     return count;
 }
 
-int aljabr_blackwell_device_name(int device_id, char* buf, int buf_len) {
+int aljabr_blackwell_device_get(int device_id) {
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+        cudaGetLastError();
+        return fail(ALJ_ERR_NOT_INITIALIZED, "no CUDA device visible");
+    }
+    if (device_id < 0 || device_id >= count) return fail(ALJ_ERR_BAD_ARG, "device %d out of range (%d devices)", device_id, count);
+    t_device = device_id;
+    int err = 0;
+    return state(&err) ? ALJ_OK : err;
+}
+
+int aljabr_blackwell_device_name(char* buf, int buf_len, int device_id) {
     if (!buf || buf_len <= 0) return fail(ALJ_ERR_BAD_ARG, "null buffer");
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+        cudaGetLastError();
+        buf[0] = '\0';
+        return fail(ALJ_ERR_NOT_INITIALIZED, "no CUDA device visible");
+    }
+    if (device_id < 0 || device_id >= count) return fail(ALJ_ERR_BAD_ARG, "device %d out of range (%d devices)", device_id, count);
     cudaDeviceProp prop;
     ALJ_CUDA(cudaGetDeviceProperties(&prop, device_id));
     snprintf(buf, static_cast<size_t>(buf_len), "%s", prop.name);
     return ALJ_OK;
+}
+
+long long aljabr_blackwell_tmem_size(int device_id) {
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+        cudaGetLastError();
+        return fail(ALJ_ERR_NOT_INITIALIZED, "no CUDA device visible");
+    }
+    if (device_id < 0 || device_id >= count) return fail(ALJ_ERR_BAD_ARG, "device %d out of range (%d devices)", device_id, count);
+    int major = 0, sms = 0;
+    ALJ_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device_id));
+    ALJ_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device_id));
+    if (major != 10) return fail(ALJ_ERR_UNSUPPORTED, "device %d has no tensor memory (sm_%d)", device_id, major);
+    return static_cast<long long>(sms) * 128 * 512 * 4;   // 128 lanes x 512 columns x 32 bit per SM
 }
 
 int aljabr_blackwell_compute_capability(int device_id) {
@@ -479,6 +553,7 @@ int aljabr_blackwell_device_status(unsigned int* fault_bits) {
 }
 
 int aljabr_blackwell_shutdown(void) {
+    noalloc_forget_scratch();
     std::lock_guard<std::mutex> g(g_mu);
     for (auto& s : g_dev) {
         if (!s) continue;
@@ -765,6 +840,14 @@ int aljabr_blackwell_decode_attention_dev(float* out, const float* q, const void
     std::lock_guard<std::mutex> g(st->mu);   // the split scratch is shared per device
     return run_attention(st, out, q, k_cache, v_cache, kv_dtype, cache_head_stride, head_dim, kv_heads, q_heads, head_dim,
                          seq_len, start_pos, scale, pick_stream(st, stream), &st->dscratch);
+}
+
+int aljabr_blackwell_rmsnorm(float* out, const float* x, const float* weight, int N, float eps) {
+    return glue_call(0, out, x, weight, N, eps);
+}
+
+int aljabr_blackwell_silu_ffn(float* out, const float* gate, const float* up, int N) {
+    return glue_call(1, out, gate, up, N, 0.0f);
 }
 
 }  // extern "C"

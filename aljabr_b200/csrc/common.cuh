@@ -100,10 +100,17 @@ __device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
 }
 // Bounded wait until flags[0..n) all reach `target` (wrap-safe).  Returns
 // false and records ALJ_FAULT_TIMEOUT if a peer never publishes.
+// If an earlier wait has already timed out (a peer is gone), return at once:
+// the rest of a token's exchanges then fail fast instead of each spending
+// the full limit.
+__device__ __forceinline__ bool fault_timeout_recorded() {
+    return (*static_cast<volatile unsigned int*>(&g_fault_word) & ALJ_FAULT_TIMEOUT) != 0u;
+}
 __device__ __forceinline__ bool wait_flags_sys(const unsigned int* flags, int n, unsigned int target) {
     const long long t0 = clock64();
     for (int r = 0; r < n; ++r) {
         while (static_cast<int>(ld_acquire_sys(flags + r) - target) < 0) {
+            if (fault_timeout_recorded()) return false;
             if (clock64() - t0 > kSpinLimitCycles) {
                 record_fault(ALJ_FAULT_TIMEOUT);
                 return false;

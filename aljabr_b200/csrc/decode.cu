@@ -5,12 +5,15 @@
 // Metal provider's registered-layer decode step (aljabr_metal_matvec_api.h:
 // aljabr_metal_register_decode_layer / aljabr_metal_decode_step_token).
 //
-// Per layer (one GPU): q/k/v triple matvec on the normed x -> RoPE + KV
-// store -> split-K attention (+ combine) -> o-proj whose epilogue adds the
-// residual and, in its last CTA, writes RMSNorm(x) for the FFN -> gate/up
-// pair whose epilogue applies SwiGLU -> down-proj whose epilogue adds the
-// residual and writes the next layer's normed x.  Seven launches per layer,
-// chained with programmatic dependent launch inside one CUDA graph.
+// Per layer (one GPU, NF4 weights): q/k/v triple matvec that scales its
+// input by the deferred RMSNorm -> RoPE + KV store -> attention (one launch,
+// split merge fused into its last CTAs) -> o-proj whose epilogue adds the
+// residual and writes x, x * norm_w and one sum of squares per CTA (the
+// RMSNorm scale is applied by the consumer) -> gate/up pair whose epilogue
+// applies SwiGLU -> down-proj whose epilogue does as the o-proj's for the
+// next layer.  Six launches per layer, chained with programmatic dependent
+// launch inside one CUDA graph.  GGUF-typed weights run the residual +
+// RMSNorm and SwiGLU as separate small launches instead.
 //
 // Tensor parallelism (2/4/8 GPUs, one process per GPU): every weight is
 // row-sharded (the caller passes each rank's contiguous row block) and

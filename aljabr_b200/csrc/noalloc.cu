@@ -40,6 +40,14 @@ std::mutex g_scratch_mu;
 
 int decode_fail(int code, const char* msg);
 
+// Forget the looked-up device addresses (aljabr_blackwell_shutdown): after a
+// device reset the array may sit at a new address, so the next call looks
+// it up again.
+void noalloc_forget_scratch() {
+    std::lock_guard<std::mutex> g(g_scratch_mu);
+    for (int d = 0; d < kMaxDevices; ++d) g_scratch_ptr[d] = nullptr;
+}
+
 }  // namespace alj
 
 using namespace alj;

@@ -56,8 +56,10 @@ _sz = ctypes.c_size_t
 SIGNATURES = {
     "aljabr_blackwell_init": (_i, [_i]),
     "aljabr_blackwell_device_count": (_i, []),
-    "aljabr_blackwell_device_name": (_i, [_i, ctypes.c_char_p, _i]),
+    "aljabr_blackwell_device_get": (_i, [_i]),
+    "aljabr_blackwell_device_name": (_i, [ctypes.c_char_p, _i, _i]),
     "aljabr_blackwell_compute_capability": (_i, [_i]),
+    "aljabr_blackwell_tmem_size": (_ll, [_i]),
     "aljabr_blackwell_free_memory": (_ll, []),
     "aljabr_blackwell_last_error": (ctypes.c_char_p, []),
     "aljabr_blackwell_set_verbose": (None, [_i]),
@@ -80,6 +82,8 @@ SIGNATURES = {
     "aljabr_blackwell_dequantize_nf4": (_i, [_p, _p, _p, _ll, _i]),
     "aljabr_blackwell_dequantize_q4_0": (_i, [_p, _p, _ll]),
     "aljabr_blackwell_dequantize_q8_0": (_i, [_p, _p, _ll]),
+    "aljabr_blackwell_rmsnorm": (_i, [_p, _p, _p, _i, _f]),
+    "aljabr_blackwell_silu_ffn": (_i, [_p, _p, _p, _i]),
     "aljabr_blackwell_decode_attention": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _f]),
     "aljabr_blackwell_matvec_dev": (_i, [_i, _p, _p, _p, _p, _i, _i, _i, _p, _p]),
     "aljabr_blackwell_dequantize_dev": (_i, [_i, _p, _p, _p, _ll, _i, _p]),

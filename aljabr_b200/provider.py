@@ -21,10 +21,10 @@ BACKEND_ID = "blackwell"
 
 # operation id -> supported constraint sets (NATIVE) ; everything else UNSUPPORTED
 NATIVE_OPERATIONS = {
-    "matvec": {"q4_0", "q8_0", "nf4"},
-    "matvec.pair": {"q4_0", "q8_0"},
-    "matvec.triple": {"q4_0", "q8_0"},
-    "matvec.batch": {"q4_0", "q8_0"},
+    "matvec": {"q4_0", "q8_0", "nf4", "q4_k", "q6_k"},
+    "matvec.pair": {"q4_0", "q8_0", "q4_k", "q6_k"},
+    "matvec.triple": {"q4_0", "q8_0", "q4_k", "q6_k"},
+    "matvec.batch": {"q4_0", "q8_0", "q4_k", "q6_k"},
     "dequantize": {"q4_0", "q8_0", "nf4"},
     "attention.gqa.decode": {"f32", "bf16"},
 }
@@ -109,7 +109,7 @@ class BlackwellComputeProvider:
         out = []
         for d in range(L.aljabr_blackwell_device_count()):
             buf = ctypes.create_string_buffer(256)
-            native.check(L.aljabr_blackwell_device_name(d, buf, 256))
+            native.check(L.aljabr_blackwell_device_name(buf, 256, d))
             cc = L.aljabr_blackwell_compute_capability(d)
             out.append(DeviceDescriptor(PROVIDER_ID, d, "GPU", buf.value.decode(), cc))
         return out

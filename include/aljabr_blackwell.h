@@ -79,10 +79,21 @@ extern "C" {
 int aljabr_blackwell_init(int device_id);
 /* Number of CUDA devices (FN_DEVICE_COUNT). */
 int aljabr_blackwell_device_count(void);
-/* Device name into buf (FN_DEVICE_NAME); returns 0 or an error. */
-int aljabr_blackwell_device_name(int device_id, char* buf, int buf_len);
+/* Select `device_id` for the calling thread's later calls, like
+ * aljabr_blackwell_init (FN_DEVICE_GET, BlackwellBinding.java:153-157,
+ * bound at :465-466 as (JAVA_INT) -> JAVA_INT).  Returns 0 or an error. */
+int aljabr_blackwell_device_get(int device_id);
+/* Device name into buf, NUL-terminated and truncated to buf_len bytes
+ * (FN_DEVICE_NAME; argument order as bound at BlackwellBinding.java:469-470:
+ * (ADDRESS buf, JAVA_INT bufSz, JAVA_INT deviceId)).  Returns 0 or an error. */
+int aljabr_blackwell_device_name(char* buf, int buf_len, int device_id);
 /* major*10+minor, e.g. 100 for B200 (FN_COMPUTE_CAP). */
 int aljabr_blackwell_compute_capability(int device_id);
+/* Tensor memory of the device in bytes (FN_TMEM_SIZE,
+ * BlackwellBinding.java:185-189, bound at :477-478): 128 lanes x 512
+ * columns x 4 bytes = 256 KiB per SM, times the SM count (37,879,808 on a
+ * 148-SM B200).  Negative error code on a device without TMEM (not sm_100). */
+long long aljabr_blackwell_tmem_size(int device_id);
 /* Free device memory in bytes for the current device (FN_FREE_MEM). */
 long long aljabr_blackwell_free_memory(void);
 /* Message for the last failing call on this thread ("" if none). */
@@ -164,6 +175,23 @@ int aljabr_blackwell_dequantize_q4_0(void* dst, const void* blocks, long long nu
 /* Q8_0 rows (.../runtime/GgufRowDequantizer.java:142-151). */
 int aljabr_blackwell_dequantize_q8_0(void* dst, const void* blocks, long long numel);
 
+/* ---- decode glue bound by the FFM class (BlackwellBinding.java:574-583) ---
+ * Both take float buffers that are device memory, registered memory, or
+ * plain host memory (staged through the library's buffers), may alias
+ * elementwise (out == x, out == gate == up as BlackwellRunner.java:586
+ * calls it), and block until `out` is written.
+ *
+ * aljabr_blackwell_rmsnorm: out[i] = (x[i] / rms) * weight[i] with
+ * rms = sqrt(sum(x^2) / N + eps), the arithmetic of the binding's own
+ * contract (BlackwellCpuFallback.rmsNorm, BlackwellCpuFallback.java:50-64);
+ * fp32 throughout, IEEE division and square root; the sum of squares is a
+ * fixed-order tree, not the Java loop's sequential order.  1 <= N <= 2^24. */
+int aljabr_blackwell_rmsnorm(float* out, const float* x, const float* weight, int N, float eps);
+/* aljabr_blackwell_silu_ffn: out[i] = gate[i] / (1 + exp(-gate[i])) * up[i]
+ * (BlackwellCpuFallback.siluFfn, BlackwellCpuFallback.java:70-79); exp is
+ * the CUDA single-precision expf, within 2 ulp of the Java double exp. */
+int aljabr_blackwell_silu_ffn(float* out, const float* gate, const float* up, int N);
+
 /* ---- GQA decode attention ------------------------------------------------ */
 /* GgufDecodeAttentionExecution.execute(query, output, scores, keyCache,
  * valueCache, cacheHeadStride, kvHeads, queryHeads, headDimension,
@@ -182,6 +210,12 @@ int aljabr_blackwell_matvec_dev(int type, float* y, const float* x, const void* 
                                 int K, int N, int group, const float* bias, void* stream);
 int aljabr_blackwell_dequantize_dev(int type, float* dst, const void* src, const float* absmax,
                                     long long numel, int group, void* stream);
+/* Decode attention on device pointers.  Its split partials live in one
+ * scratch buffer per device that the library allocates on first use and
+ * reuses; each call clears the buffer's arrival counters on `stream` before
+ * its kernel.  Calls whose kernels may overlap on the GPU (different
+ * streams, or several threads) share that buffer and must be ordered by the
+ * caller (an event or one stream). */
 int aljabr_blackwell_decode_attention_dev(float* out, const float* q, const void* k_cache,
                                           const void* v_cache, int kv_dtype, int cache_head_stride,
                                           int kv_heads, int q_heads, int head_dim, int seq_len,
@@ -225,7 +259,9 @@ int aljabr_blackwell_gemm_nf4_dev(int nseg, float* const* y, const int* ldy, con
  * aljabr_blackwell_init: it runs on the current device and on `stream`
  * (NULL = the legacy default stream).  The first call on a device looks up
  * the array's device address (cudaGetSymbolAddress) with that device
- * current; make it before any stream capture.  All calls share the array,
+ * current; make it before any stream capture.  A device reset may move the
+ * array: call aljabr_blackwell_shutdown after one, so the next call looks
+ * the address up again.  All calls share the array,
  * so calls whose kernels may overlap (other streams, other threads) race
  * and must be ordered by the caller.  The split merge's arrival counters
  * must start at zero; each call clears them on `stream` before its kernel. */

@@ -5,8 +5,9 @@ Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
 legs use this package, and only as the checker or the timed CPU baseline.
 The product path (``aljabr_b200``) never imports it.
 
-Parity status: Q4_0 / Q8_0 / Q4_K / Q6_K / fp16 / attention restatements are
-pinned by the reference's known-answer tests (``tests/golden/``).  The NF4 fp32 GEMV (Apple
+Parity status: Q4_0 (raw and prepared-cache order) / Q8_0 / Q4_K / Q6_K /
+fp16 / attention restatements are pinned by the reference's known-answer
+tests (``tests/golden/``).  The NF4 fp32 GEMV (Apple
 Accelerate ``cblas_sgemv`` in the reference) and the NF4 quantizer (external
 project) are "parity unpinned"; NF4 dequantisation is pinned by its table and
 nibble order.
@@ -76,6 +77,11 @@ def _declare(L):
         getattr(L, name).argtypes = [_p, _i, _p]
         getattr(L, name).restype = _f
     L.orc_matvec_q4_0.argtypes = [_p, _p, _p, _i, _i, _i]
+    L.orc_matvec_q4_0_prepared.argtypes = [_p, _p, _p, _i, _i, _i]
+    L.orc_dot_row_q4_0_prepared.argtypes = [_p, _i, _p]
+    L.orc_dot_row_q4_0_prepared.restype = _f
+    L.orc_rmsnorm_binding.argtypes = [_p, _p, _p, _i, _f]
+    L.orc_silu_ffn_binding.argtypes = [_p, _p, _p, _i]
     L.orc_matvec_q8_0.argtypes = [_p, _p, _p, _i, _i, _i, _i]
     for name in ("orc_dot_row_q4_k", "orc_dot_row_q6_k"):
         getattr(L, name).argtypes = [_p, _i, _p]
@@ -202,6 +208,11 @@ def dot_row_q4_0(row, x) -> float:
     return lib().orc_dot_row_q4_0(_ptr(row), x.size, _ptr(x))
 
 
+def dot_row_q4_0_prepared(row, x) -> float:
+    row, x = _c(row, np.uint8), _c(x, np.float32)
+    return lib().orc_dot_row_q4_0_prepared(_ptr(row), x.size, _ptr(x))
+
+
 def dot_row_q8_0(row, x, vector_order: bool = True) -> float:
     row, x = _c(row, np.uint8), _c(x, np.float32)
     fn = lib().orc_dot_row_q8_0_vector if vector_order else lib().orc_dot_row_q8_0_scalar
@@ -212,6 +223,14 @@ def matvec_q4_0(w, x, N: int, threads: int = 1) -> np.ndarray:
     w, x = _c(w, np.uint8), _c(x, np.float32)
     y = np.empty(N, dtype=np.float32)
     lib().orc_matvec_q4_0(_ptr(w), _ptr(x), _ptr(y), x.size, N, threads)
+    return y
+
+
+def matvec_q4_0_prepared(w, x, N: int, threads: int = 1) -> np.ndarray:
+    """Q4_0 in the prepared-cache order, the reference's default for >= 32 rows."""
+    w, x = _c(w, np.uint8), _c(x, np.float32)
+    y = np.empty(N, dtype=np.float32)
+    lib().orc_matvec_q4_0_prepared(_ptr(w), _ptr(x), _ptr(y), x.size, N, threads)
     return y
 
 
@@ -287,6 +306,22 @@ def rms_norm(x, w, eps: float) -> np.ndarray:
     x, w = _c(x, np.float32), _c(w, np.float32)
     out = np.empty_like(x)
     lib().orc_rms_norm(_ptr(x), _ptr(w), _ptr(out), x.size, eps)
+    return out
+
+
+def rmsnorm_binding(x, w, eps: float) -> np.ndarray:
+    """BlackwellCpuFallback.rmsNorm: the FFM binding's RMSNorm contract."""
+    x, w = _c(x, np.float32), _c(w, np.float32)
+    out = np.empty_like(x)
+    lib().orc_rmsnorm_binding(_ptr(x), _ptr(w), _ptr(out), x.size, eps)
+    return out
+
+
+def silu_ffn_binding(gate, up) -> np.ndarray:
+    """BlackwellCpuFallback.siluFfn: out = silu(gate) * up."""
+    gate, up = _c(gate, np.float32), _c(up, np.float32)
+    out = np.empty_like(gate)
+    lib().orc_silu_ffn_binding(_ptr(gate), _ptr(up), _ptr(out), gate.size)
     return out
 
 

@@ -448,6 +448,69 @@ void orc_dequantize_k_row(int type, const uint8_t* row, int columns, double* out
     }
 }
 
+/* ---- Q4_0 prepared path: the reference's default for >= 32 rows --------
+ * RT/GgufPreparedCachePolicy.java:66-75 (cache_min_rows 32) selects the
+ * prepared matrix built by RT/GgufQ32Build.java:78-91 (fillQ4_0Blocks: fp32
+ * block scale f16ToF32(d); codes unpacked by RT/GgufQuantUnpacker.java:
+ * 365-367,414-433,445-448 to int8 (q & 15) - 8 at index i and (q >> 4) - 8
+ * at index 16 + i), then dotted by RT/GgufQ32Dot.java:627-670
+ * (dotRowQ32PreparedNoBiasScalar: four interleaved Math.fma accumulators
+ * over blocks, sum0 + sum1 + sum2 + sum3, fma tail) with the per-block dot
+ * RT/GgufDot.java:1046-1058 (dotSignedByte32Scalar: four lane partial sums
+ * of int8 * float, lane sum left to right). */
+static float q4_0_prepared_block_dot(const uint8_t* blk, const float* v) {
+    int8_t q[32];
+    for (int i = 0; i < 16; i++) {
+        const int b = blk[2 + i];
+        q[i] = (int8_t)((b & 0x0F) - 8);
+        q[16 + i] = (int8_t)((b >> 4) - 8);
+    }
+    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+    for (int i = 0; i < 32; i += 4) {
+        s0 += (float)q[i] * v[i];
+        s1 += (float)q[i + 1] * v[i + 1];
+        s2 += (float)q[i + 2] * v[i + 2];
+        s3 += (float)q[i + 3] * v[i + 3];
+    }
+    return s0 + s1 + s2 + s3;
+}
+float orc_dot_row_q4_0_prepared(const uint8_t* row, int columns, const float* x) {
+    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+    int blocks = columns / 32, block = 0, unrolled_limit = blocks - 4;
+    for (; block <= unrolled_limit; block += 4) {
+        const uint8_t* b = row + (size_t)block * 18;
+        s0 = fmaf(orc_f16_to_f32(le16(b)), q4_0_prepared_block_dot(b, x + block * 32), s0);
+        s1 = fmaf(orc_f16_to_f32(le16(b + 18)), q4_0_prepared_block_dot(b + 18, x + (block + 1) * 32), s1);
+        s2 = fmaf(orc_f16_to_f32(le16(b + 36)), q4_0_prepared_block_dot(b + 36, x + (block + 2) * 32), s2);
+        s3 = fmaf(orc_f16_to_f32(le16(b + 54)), q4_0_prepared_block_dot(b + 54, x + (block + 3) * 32), s3);
+    }
+    float sum = s0 + s1 + s2 + s3;
+    for (; block < blocks; block++) {
+        const uint8_t* b = row + (size_t)block * 18;
+        sum = fmaf(orc_f16_to_f32(le16(b)), q4_0_prepared_block_dot(b, x + block * 32), sum);
+    }
+    return sum;
+}
+
+/* ---- the FFM binding's decode glue (BlackwellCpuFallback.java:50-79) ----
+ * Path: backend/blackwell/aljabr-kernel-blackwell/src/main/java/tech/kayys/
+ * aljabr/blackwell/binding/BlackwellCpuFallback.java.  rmsNorm: sequential
+ * float sum of squares, rms = (float) Math.sqrt(sum / N + eps),
+ * out = (x / rms) * w.  siluFfn: g / (1 + (float) Math.exp(-g)) * u. */
+void orc_rmsnorm_binding(const float* x, const float* w, float* out, int n, float eps) {
+    float sum = 0.0f;
+    for (int i = 0; i < n; i++) sum += x[i] * x[i];
+    const float rms = (float)sqrt((double)(sum / (float)n + eps));
+    for (int i = 0; i < n; i++) out[i] = (x[i] / rms) * w[i];
+}
+void orc_silu_ffn_binding(const float* gate, const float* up, float* out, int n) {
+    for (int i = 0; i < n; i++) {
+        const float g = gate[i];
+        const float silu = g / (1.0f + (float)exp(-(double)g));
+        out[i] = silu * up[i];
+    }
+}
+
 /* ------------------------------------------------------------------------ */
 /* Row parallelism: rows split into 2 chunks per thread, chunks pulled from a
  * shared counter (RT/GgufParallelConfig.java:14-15,56-73, GgufRows.java:133). */
@@ -530,6 +593,8 @@ static void* worker(void* arg) {
             if (j->y64) { j->y64[r] = f64_row_dot(j, r); continue; }
             float v;
             if (j->type == ORC_Q4_0) v = orc_dot_row_q4_0(j->w + r * (int64_t)(j->K / 32) * 18, j->K, j->x);
+            else if (j->type == ORC_Q4_0_PREPARED)
+                v = orc_dot_row_q4_0_prepared(j->w + r * (int64_t)(j->K / 32) * 18, j->K, j->x);
             else if (j->type == ORC_Q4_K) v = orc_dot_row_q4_k(j->w + r * (int64_t)(j->K / 256) * 144, j->K, j->x);
             else if (j->type == ORC_Q6_K) v = orc_dot_row_q6_k(j->w + r * (int64_t)(j->K / 256) * 210, j->K, j->x);
             else if (j->type == ORC_Q8_0)
@@ -562,6 +627,12 @@ static void run_job(job_t* j, int threads) {
 void orc_matvec_q4_0(const uint8_t* w, const float* x, float* y, int K, int N, int threads) {
     job_t j; memset(&j, 0, sizeof j);
     j.type = ORC_Q4_0; j.K = K; j.N = N; j.w = w; j.x = x; j.y = y;
+    run_job(&j, threads);
+}
+
+void orc_matvec_q4_0_prepared(const uint8_t* w, const float* x, float* y, int K, int N, int threads) {
+    job_t j; memset(&j, 0, sizeof j);
+    j.type = ORC_Q4_0_PREPARED; j.K = K; j.N = N; j.w = w; j.x = x; j.y = y;
     run_job(&j, threads);
 }
 

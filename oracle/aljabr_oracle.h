@@ -54,6 +54,10 @@ void orc_dequantize_q8_0(const uint8_t* blocks, float* dst, int64_t numel); /* R
 
 /* ---- row dots in the reference's summation order ------------------------ */
 float orc_dot_row_q4_0(const uint8_t* row, int columns, const float* x);          /* RT/GgufQ32RawDot.java:34-67 */
+/* Q4_0 in the prepared-cache order (the reference's default for >= 32 rows):
+ * RT/GgufQ32Build.java:78-91, RT/GgufQuantUnpacker.java:365-367,414-448,
+ * RT/GgufQ32Dot.java:627-670, RT/GgufDot.java:1046-1058. */
+float orc_dot_row_q4_0_prepared(const uint8_t* row, int columns, const float* x);
 float orc_dot_row_q8_0_scalar(const uint8_t* row, int columns, const float* x);   /* RT/GgufQ8RawDot.java:138-185 */
 float orc_dot_row_q8_0_vector(const uint8_t* row, int columns, const float* x);   /* RT/GgufQ8RawDot.java:63-121 */
 float orc_dot_row_q4_k(const uint8_t* row, int columns, const float* x);          /* RT/GgufQ4RawDot.java:38-141 */
@@ -61,8 +65,9 @@ float orc_dot_row_q6_k(const uint8_t* row, int columns, const float* x);        
 void  orc_dequantize_k_row(int type, const uint8_t* row, int columns, double* out); /* element formulas, fp64 */
 
 /* ---- matvec (rows parallel over `threads` host threads, 2 chunks each) -- */
-enum { ORC_Q4_0 = 2, ORC_Q8_0 = 8, ORC_Q4_K = 12, ORC_Q6_K = 14, ORC_NF4 = 100 };
+enum { ORC_Q4_0 = 2, ORC_Q8_0 = 8, ORC_Q4_K = 12, ORC_Q6_K = 14, ORC_NF4 = 100, ORC_Q4_0_PREPARED = 1002 };
 void orc_matvec_q4_0(const uint8_t* w, const float* x, float* y, int K, int N, int threads);
+void orc_matvec_q4_0_prepared(const uint8_t* w, const float* x, float* y, int K, int N, int threads);
 void orc_matvec_q8_0(const uint8_t* w, const float* x, float* y, int K, int N, int vector_order, int threads);
 void orc_matvec_k(int type, const uint8_t* w, const float* x, float* y, int K, int N, int threads);   /* Q4_K / Q6_K */
 /* NF4: dequantise (DK:84-102) then a plain fp32 row dot (stands in for the
@@ -87,6 +92,10 @@ void  orc_rms_norm(const float* x, const float* w, float* out, int len, float ep
 void  orc_rope(float* x, int n_heads, int head_dim, int rotary_dim, int pos, float freq_base); /* VO:383-440 */
 void  orc_swiglu(const float* gate, const float* up, float* dst, int len);       /* VO:333-338 */
 void  orc_softmax(float* a, int len);                                            /* VO:302-317 */
+/* The FFM binding's own glue contract (backend/blackwell/aljabr-kernel-
+ * blackwell/.../binding/BlackwellCpuFallback.java:50-64 and :70-79). */
+void  orc_rmsnorm_binding(const float* x, const float* w, float* out, int n, float eps);
+void  orc_silu_ffn_binding(const float* gate, const float* up, float* out, int n);
 
 /* One batch-1 decode step of a Llama-shaped model with NF4 linear weights,
  * following DP:297-545 (pre-norm, q/k/v, split-half RoPE, KV store,

@@ -67,6 +67,11 @@ def test_q4_0_matvec_parity(lib, N, K):
     assert synth.max_rel_err(y, ref) < TOL
     assert synth.max_rel_err(y, g) < TOL
     assert synth.normwise_rel_err(y, g) < 1e-5
+    if N >= 32:
+        # the reference's default order at >= 32 rows: the prepared cache
+        # (GgufPreparedCachePolicy.java:66-75, GgufQ32Dot.java:627-670)
+        prep = oracle.matvec_q4_0_prepared(w, x, N, threads=8)
+        assert synth.max_rel_err(y, prep) < TOL
 
 
 @pytest.mark.parametrize("N,K", [(7, 256), (1024, 4096), (4096, 4096), (14336, 4096), (4096, 14336), (5, 160),

@@ -28,6 +28,53 @@ def test_q4_0_matvec_known_answers(golden):
             np.testing.assert_array_equal(oracle.matvec_q4_0(w, x, fx["N"], threads=threads), y)
 
 
+def test_q4_0_prepared_order_known_answers(golden):
+    # The prepared-cache order (GgufQ32Dot.dotRowQ32PreparedNoBiasScalar) is
+    # the reference's default for >= 32 rows; the same known answers hold
+    # (GgufQ32Test.java:18-42 asserts 16 / 48 through matVecRows, whichever
+    # order the cache policy picks).
+    for fx in _fixtures(golden, "q4_0_matvec"):
+        w = np.array(fx["weights"], dtype=np.uint8)
+        x = np.array(fx["x"], dtype=np.float32)
+        y = oracle.matvec_q4_0_prepared(w, x, fx["N"])
+        np.testing.assert_allclose(y, fx["expected"], rtol=0, atol=fx["tol"] * max(1.0, np.abs(fx["expected"]).max()),
+                                   err_msg=fx["name"])
+        for threads in (2, 3):
+            np.testing.assert_array_equal(oracle.matvec_q4_0_prepared(w, x, fx["N"], threads=threads), y)
+
+
+def test_q4_0_prepared_and_raw_orders_agree_with_fp64():
+    rng = np.random.default_rng(13)
+    for K, N in ((4096, 64), (14336, 32), (4128, 40)):   # 4128: 129 blocks, exercises the fma tail
+        w = oracle.encode_q4_0(rng.normal(0, 0.02, size=K * N).astype(np.float32))
+        x = rng.normal(0, 1, size=K).astype(np.float32)
+        raw = oracle.matvec_q4_0(w, x, N)
+        prep = oracle.matvec_q4_0_prepared(w, x, N)
+        g = oracle.matvec_f64(oracle.Q4_0, w, x, N)
+        scale = np.abs(g).max()
+        assert np.max(np.abs(raw - g)) / scale < 1e-5
+        assert np.max(np.abs(prep - g)) / scale < 1e-5
+        # the orders differ (fma vs separate rounding), so they are close but not equal
+        assert np.max(np.abs(prep - raw)) / scale < 1e-5
+        row = w[:(K // 32) * 18]
+        assert oracle.dot_row_q4_0_prepared(row, x) == prep[0]
+
+
+def test_binding_glue_restatement():
+    rng = np.random.default_rng(14)
+    x = rng.normal(0, 1, size=4096).astype(np.float32)
+    w = rng.normal(1, 0.1, size=4096).astype(np.float32)
+    out = oracle.rmsnorm_binding(x, w, 1e-6)
+    x64 = x.astype(np.float64)
+    ref = x64 / np.sqrt(np.mean(x64 * x64) + 1e-6) * w
+    assert np.max(np.abs(out - ref)) < 1e-5
+    g = rng.normal(0, 2, size=1000).astype(np.float32)
+    u = rng.normal(0, 1, size=1000).astype(np.float32)
+    s = oracle.silu_ffn_binding(g, u)
+    g64 = g.astype(np.float64)
+    np.testing.assert_allclose(s, g64 / (1 + np.exp(-g64)) * u, rtol=1e-6, atol=1e-7)
+
+
 def test_q4_0_dequant_known_answers(golden):
     for fx in _fixtures(golden, "q4_0_dequant"):
         y = oracle.dequantize_q4_0(np.array(fx["weights"], dtype=np.uint8), fx["numel"])

@@ -9,9 +9,20 @@ from aljabr_b200.bridge import GgufModel
 def test_operation_support_native_only_for_implemented_kernels():
     assert provider.operation_support("matvec", {"type": "q4_0"}).support == "NATIVE"
     assert provider.operation_support("matvec", {"type": "nf4"}).support == "NATIVE"
-    assert provider.operation_support("matvec", {"type": "q4_k"}).support == "UNSUPPORTED"
+    assert provider.operation_support("matvec", {"type": "q4_k"}).support == "NATIVE"
+    assert provider.operation_support("matvec", {"type": "q6_k"}).support == "NATIVE"
+    assert provider.operation_support("matvec", {"type": "q5_k"}).support == "UNSUPPORTED"
     assert provider.operation_support("attention.gqa.decode", {"dtype": "bf16"}).support == "NATIVE"
     assert provider.operation_support("softmax", {}).support == "UNSUPPORTED"
+
+
+def test_bridge_routes_the_types_the_metal_seam_routes():
+    # GgufMetalBridge.matVec routes Q4_K (12), Q6_K (14) and Q8_0 (8)
+    from aljabr_b200.bridge import GgufBlackwellBridge
+    for t in (2, 8, 12, 14):
+        assert GgufBlackwellBridge.is_type_supported(t)
+    for t in (0, 1, 3, 13, 30):
+        assert not GgufBlackwellBridge.is_type_supported(t)
 
 
 def test_operation_support_requires_constraints():
