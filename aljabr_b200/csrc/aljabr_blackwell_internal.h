@@ -92,7 +92,12 @@ int matvec_max_ctas();
 // programmatic dependent launch on the stream.
 cudaError_t launch_matvec(int fmt, const MatvecParams& p, cudaStream_t stream, bool pdl);
 bool matvec_tma_supported(int fmt, int K, int group);
-// Tensor-core path (Q4_0, K a multiple of 2048); launch_matvec picks it first.
+// Integer tensor-core path (Q4_0 / Q8_0, K a multiple of 2048, plain store
+// epilogue with bias / residual); launch_matvec picks it first.
+bool matvec_imma_supported(int fmt, int K);
+cudaError_t launch_matvec_imma(int fmt, const MatvecParams& p, cudaStream_t stream, bool pdl);
+// fp16 tensor-core path (Q4_0 / Q8_0, K a multiple of 2048) with the fused
+// SwiGLU-pair and RMSNorm epilogues; picked when the integer path declines.
 bool matvec_mma_supported(int fmt, int K);
 cudaError_t launch_matvec_mma(int fmt, const MatvecParams& p, cudaStream_t stream, bool pdl);
 // NF4 table path (K a multiple of 2048, group 64 or 128); picked second.

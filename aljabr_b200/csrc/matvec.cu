@@ -722,6 +722,10 @@ cudaError_t launch_matvec(int fmt, const MatvecParams& p, cudaStream_t stream, b
     if (p.norm_defer || p.in_parts)   // only the NF4 table kernel splits the RMSNorm across launches
         return fmt == FMT_NF4 && matvec_lut_supported(fmt, p.K, p.group) ? launch_matvec_lut(fmt, p, stream, pdl)
                                                                          : cudaErrorNotSupported;
+    if (matvec_imma_supported(fmt, p.K)) {
+        const cudaError_t e = launch_matvec_imma(fmt, p, stream, pdl);
+        if (e != cudaErrorNotSupported) return e;
+    }
     if (matvec_mma_supported(fmt, p.K)) {
         const cudaError_t e = launch_matvec_mma(fmt, p, stream, pdl);
         if (e != cudaErrorNotSupported) return e;

@@ -1,0 +1,574 @@
+// Batch-1 GGUF Q4_0 and Q8_0 dequantise-and-matvec (y = W x) on the integer
+// tensor-core path of B200 (sm_100a): mma.sync.m16n8k32 with s8 operands and
+// s32 accumulation, for K a multiple of 2048.
+//
+// Why this shape.  At batch 1 the kernel is HBM-bound only if an SM retires
+// ~40 Q4_0 weights per cycle.  The multiply-adds go to the tensor cores; what
+// is left on the issue ports is moving and decoding codes, so this kernel is
+// built around the fewest instructions per weight:
+//   * A operand = the codes themselves.  Q8_0 bytes are s8 as stored (no
+//     decode).  A Q4_0 code word gives its eight codes in two LOP3s (plus one
+//     shift): (w & 0xF0F0F0F0) ^ 0x80808080 is the four high nibbles as the
+//     s8 values 16 (c - 8), and the same on w << 4 gives the low nibbles.
+//   * B operand = x, split exactly into three balanced int8 digits per
+//     32-element block: X = rint(x 2^F) with F chosen from the block's max
+//     |x| so that |X| <= 2^22, X = h 2^16 + m 2^8 + l, l, m in [-128, 127],
+//     h in [-64, 64].  One MMA column per digit, so every product and every
+//     partial sum is an exact integer (|sum| < 2^19 per column): the tensor
+//     core rounds nothing.  The block value d 2^-F (h 2^16 + m 2^8 + l) is
+//     formed in fp32 once per block, which is the only rounding besides the
+//     fp32 sums over blocks.  x keeps 22 bits relative to its block maximum.
+//   * One k32 MMA covers two blocks of 16 rows: k-slots of quad lanes 0-1
+//     carry the even block of a block pair, lanes 2-3 the odd block, and
+//     columns 0-2 / 4-6 hold the digits of the even / odd block.  So every
+//     lane's accumulator columns belong to one block and one fp16 scale.
+//
+// Data flow per CTA (one CTA per SM; 16 consumer warps, a TMA producer warp
+// and an epilogue warp; up to 8 stages of ~18 KB in flight):
+//   * rows are dealt out in balanced units of 4 and walked in slabs of <= 16
+//     rows (a slab never straddles a weight segment) x chunks of 2048 (Q4_0)
+//     or 1024 (Q8_0) columns;
+//   * the producer copies each slab-chunk with 2-D TMA boxes of 8 or 4 rows
+//     whose inner extent is the chunk plus 16 bytes: smem rows are padded by
+//     16 bytes (a 4- or 20-word bank shift per row), which makes every
+//     fragment load of a quad (four distinct words mod 4) conflict-free;
+//   * warp w owns a fixed run of block pairs in every chunk (2 for Q4_0, 1
+//     for Q8_0), converts their x into B-fragment records once per launch
+//     (read by no other warp), and for each stage loads its code words, runs
+//     two MMAs per block pair and folds d 2^-F per block into fp32 row sums;
+//   * per-warp row sums go through a shared-memory ring to the epilogue
+//     warp, which adds them in fixed warp order (bit-identical repeat calls)
+//     and applies bias / residual.
+// Every mbarrier wait is bounded (ALJ_FAULT_TIMEOUT in the device fault word).
+#include "common.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
+
+namespace alj {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();   // matvec.cu
+
+namespace {
+
+constexpr int kCW = 16;                      // consumer warps
+constexpr int kProducerWarp = kCW;
+constexpr int kEpilogueWarp = kCW + 1;
+constexpr int kThreads = (kCW + 2) * 32;
+constexpr int kUnit = 4;                     // rows per balancing unit
+constexpr int kMaxStages = 8;
+constexpr int kRing = 4;                     // slab partial buffers
+constexpr int kRecBytes = 192;               // B fragments of one block pair: 12 active lanes x 16 B
+constexpr int kSmemMax = 232448;             // 227 KB opt-in per CTA
+constexpr uint32_t kMagic = 0x4B400000u;     // bits of 1.5 * 2^23: fma(x, s, magic) = magic + rint(x s)
+
+template <int FMT>
+struct IFmt;
+template <>
+struct IFmt<FMT_Q4_0> {
+    static constexpr int kPairBytes = 36;    // two 18-byte blocks
+    static constexpr int kChunkPairs = 32;   // 2048 columns
+    static constexpr int kWordsPerRow = 2;   // code words a lane decodes per row and pair
+};
+template <>
+struct IFmt<FMT_Q8_0> {
+    static constexpr int kPairBytes = 68;    // two 34-byte blocks
+    static constexpr int kChunkPairs = 16;   // 1024 columns
+    static constexpr int kWordsPerRow = 4;
+};
+template <int FMT>
+struct IGeom {
+    static constexpr int kChunkCols = IFmt<FMT>::kChunkPairs * 64;
+    static constexpr int kChunkBytes = IFmt<FMT>::kChunkPairs * IFmt<FMT>::kPairBytes;   // 1152 | 1088
+    static constexpr int kRowStride = kChunkBytes + 16;                                  // 1168 | 1104
+    static constexpr int kBoxElems = kRowStride / 8;                                     // uint64 elements
+    static constexpr int kStageBytes = 16 * kRowStride;
+    static constexpr int kPairsPerWarp = IFmt<FMT>::kChunkPairs / kCW;                   // 2 | 1
+};
+
+// Source word (index into the pair's 32-bit words) of code word `w` of quad
+// lane t.  -1 marks the word the even block splits across its scale words:
+// bytes 2-3 of word 0 and bytes 0-1 of word 4 (Q4_0) or word 8 (Q8_0).
+// Quad lanes 0-1 take the even block's code bytes, lanes 2-3 the odd block's;
+// each load instruction of a quad reads four words that are distinct mod 4.
+__host__ __device__ constexpr int src_word(int fmt, int t, int w) {
+    return fmt == FMT_Q4_0 ? (t == 0 ? (w == 0 ? 1 : 2) : t == 1 ? (w == 0 ? 3 : -1) : t == 2 ? (w == 0 ? 8 : 5)
+                                                                                                : (w == 0 ? 6 : 7))
+                           : (t == 0 ? 1 + 2 * w
+                              : t == 1 ? (w < 3 ? 2 + 2 * w : -1)
+                              : t == 2 ? (w == 0 ? 11 : w == 1 ? 9 : w == 2 ? 15 : 13)
+                                       : (w == 0 ? 12 : w == 1 ? 10 : w == 2 ? 16 : 14));
+}
+// Byte of the pair that byte q of lane t's code word w holds.
+__host__ __device__ constexpr int word_byte(int fmt, int t, int w, int q) {
+    return src_word(fmt, t, w) >= 0 ? 4 * src_word(fmt, t, w) + q
+                                    : (q < 2 ? 2 + q : (fmt == FMT_Q4_0 ? 14 : 30) + q);
+}
+// Block element (0..31, within the lane's block) multiplied at k-slot byte q
+// of operand register r (0 = a0/a1, 1 = a2/a3) in MMA m of a block pair.
+__host__ __device__ constexpr int slot_elem(int fmt, int t, int m, int r, int q) {
+    return fmt == FMT_Q4_0 ? (word_byte(fmt, t, r, q) - (t < 2 ? 2 : 20)) + 16 * m
+                           : (word_byte(fmt, t, 2 * m + r, q) - (t < 2 ? 2 : 36));
+}
+
+struct alignas(64) ImmaSegment {
+    CUtensorMap map8;                        // box {row chunk + 16 B, 8 rows}
+    CUtensorMap map4;                        // box {row chunk + 16 B, 4 rows}
+    const float* bias;
+    const float* residual;
+    float* y;
+    int rows;
+    int row0;
+};
+
+struct alignas(64) ImmaParams {
+    ImmaSegment seg[3];
+    int nseg;
+    int K;
+    int total_rows;
+    const float* x;
+    const uint8_t* prefetch;
+    size_t prefetch_bytes;
+};
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void imma(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                     uint32_t b1) {
+    asm(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+// High nibbles as s8 16 (c - 8); the same on (w << 4) gives the low nibbles.
+__device__ __forceinline__ uint32_t nib_s8(uint32_t w) { return lop3_and_xor(w, 0xF0F0F0F0u, 0x80808080u); }
+
+// Slabs of <= 16 rows of a CTA's unit range, split at segment boundaries.
+struct SlabWalk {
+    int u, u_end;
+    __device__ __forceinline__ bool next(const ImmaParams& p, int& seg, int& su, int& nunits) {
+        if (u >= u_end) return false;
+        seg = 0;
+        if (p.nseg > 1 && u * kUnit >= p.seg[1].row0) seg = 1;
+        if (p.nseg > 2 && u * kUnit >= p.seg[2].row0) seg = 2;
+        const int seg_end = (p.seg[seg].row0 + p.seg[seg].rows) / kUnit;
+        su = u;
+        nunits = min(4, min(u_end, seg_end) - u);
+        u += nunits;
+        return true;
+    }
+};
+
+// x digits of every block pair this warp owns (its run of kPPW pairs in each
+// chunk) into B-fragment records and per-block scales, in units of two
+// pairs.  The x loads of up to kXBatch units go out together (every CTA reads
+// all of x, so those lines are contended in L2: one round trip per batch).
+//   pass A: lane l holds x[4 (l % 16) ..] of unit pair j = l / 16; 8-lane
+//           groups form each block's max |x| and scale 2^F; each lane writes
+//           the three digit bytes of its four elements, in element order,
+//           into the warp's scratch (one word per digit);
+//   pass B: lane (pair j, group (t, m, r)) gathers the four digit bytes that
+//           k-slot bytes 0..3 of operand r of MMA m carry for quad lane t
+//           (two words and a PRMT per digit) and writes the three record
+//           words of lanes (g, t), g = digit (t < 2) or 4 + digit (t >= 2).
+constexpr int kXBatch = 8;
+constexpr int kScratchBytes = 3 * 128;      // per warp: digit planes h, m, l of a unit's 128 elements
+
+template <int FMT>
+__device__ __forceinline__ int unit_pair(int u, int j, int warp) {
+    constexpr int kPPW = IGeom<FMT>::kPairsPerWarp;
+    constexpr int kCP = IFmt<FMT>::kChunkPairs;
+    return kPPW == 2 ? u * kCP + warp * 2 + j : (2 * u + j) * kCP + warp;
+}
+
+template <int FMT>
+__device__ __forceinline__ void stage_x(const float* __restrict__ x, int nunits, uint8_t* rec, float* xs,
+                                        uint8_t* scratch, int warp, int lane) {
+    const int ja = lane >> 4;                                  // pass A: unit pair of this lane
+    const int jb = lane >> 4, gi = lane & 15;                  // pass B: (pair, t, m, r)
+    const int t = gi >> 2, m = (gi >> 1) & 1, r = gi & 1;
+    const int e0 = slot_elem(FMT, t, m, r, 0), e2 = slot_elem(FMT, t, m, r, 2);
+    const int bbase = jb * 64 + (t < 2 ? 0 : 32);
+    const int wa = (bbase + e0) >> 2, wb = (bbase + e2) >> 2;  // scratch words holding bytes e0, e0+1 / e2, e2+1
+    const uint32_t gsel = static_cast<uint32_t>((e0 & 3) | ((e0 & 3) + 1) << 4 | (4 + (e2 & 3)) << 8 |
+                                                (5 + (e2 & 3)) << 12);
+    const uint32_t* sw = reinterpret_cast<const uint32_t*>(scratch);
+    uint32_t* swr = reinterpret_cast<uint32_t*>(scratch);
+    for (int u0 = 0; u0 < nunits; u0 += kXBatch) {
+        float4 v[kXBatch];
+#pragma unroll
+        for (int b = 0; b < kXBatch; ++b)
+            if (u0 + b < nunits)
+                v[b] = __ldg(reinterpret_cast<const float4*>(x + static_cast<size_t>(unit_pair<FMT>(u0 + b, ja, warp)) * 64) +
+                             (lane & 15));
+#pragma unroll
+        for (int b = 0; b < kXBatch; ++b) {
+            const int u = u0 + b;
+            if (u >= nunits) break;
+            // ---- pass A
+            float mx = fmaxf(fmaxf(fabsf(v[b].x), fabsf(v[b].y)), fmaxf(fabsf(v[b].z), fabsf(v[b].w)));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            // exponent field E of the max: scale 2^F, F = 148 - E (max 2^F in
+            // [2^21, 2^22)); E clamped below so that 2^-F / 16 stays normal;
+            // a block holding Inf or NaN gets a NaN scale (its rows become NaN).
+            const uint32_t eb = (__float_as_uint(mx) >> 23) & 0xFFu;
+            const uint32_t ec = eb < 26u ? 26u : eb;
+            const float sc = eb == 0xFFu ? 0.0f : __uint_as_float((275u - ec) << 23);
+            const float inv = eb == 0xFFu ? __uint_as_float(0x7FC00000u)
+                                          : __uint_as_float((ec - 21u - (FMT == FMT_Q4_0 ? 4u : 0u)) << 23);
+            if ((lane & 7) == 0) xs[2 * unit_pair<FMT>(u, ja, warp) + ((lane >> 3) & 1)] = inv;
+            const float xv[4] = {v[b].x, v[b].y, v[b].z, v[b].w};
+            uint32_t bits[4], mid[4], hig[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                bits[q] = __float_as_uint(__fmaf_rn(xv[q], sc, __uint_as_float(kMagic)));   // magic + X
+                mid[q] = bits[q] + 0x80u;                 // byte 1 = m digit of X
+                hig[q] = bits[q] - 0x3F7F80u;             // byte 2 = h digit of X
+            }
+            __syncwarp();                                 // the previous unit's pass B has read the scratch
+            swr[0 * 32 + lane] = prmt(prmt(hig[0], hig[1], 0x0062u), prmt(hig[2], hig[3], 0x6200u), 0x7610u);
+            swr[1 * 32 + lane] = prmt(prmt(mid[0], mid[1], 0x0051u), prmt(mid[2], mid[3], 0x5100u), 0x7610u);
+            swr[2 * 32 + lane] = prmt(prmt(bits[0], bits[1], 0x0040u), prmt(bits[2], bits[3], 0x4000u), 0x7610u);
+            __syncwarp();
+            // ---- pass B: record slot of lane (g, t) is 2 g + t (t < 2) or 6 + 2 (g - 4) + t - 2
+            uint8_t* slot = rec + static_cast<size_t>(unit_pair<FMT>(u, jb, warp)) * kRecBytes + (t < 2 ? t : 4 + t) * 16 +
+                            4 * (2 * m + r);
+#pragma unroll
+            for (int d = 0; d < 3; ++d)
+                *reinterpret_cast<uint32_t*>(slot + 32 * d) = prmt(sw[d * 32 + wa], sw[d * 32 + wb], gsel);
+        }
+    }
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_constant__ ImmaParams p, int stages) {
+    using G = IGeom<FMT>;
+    constexpr int kRS = G::kRowStride;
+    constexpr int kStageBytes = G::kStageBytes;
+    constexpr int kPPW = G::kPairsPerWarp;
+    constexpr int kChunkPairs = IFmt<FMT>::kChunkPairs;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    pdl_launch_dependents();
+    const int K = p.K;
+    const int nchunks = K / G::kChunkCols;
+    const int npairs = K / 64;
+    const uint32_t base = smem_u32(smem_raw);
+    uint8_t* sp = smem_raw + ((1024u - (base & 1023u)) & 1023u);
+    uint8_t* stage0 = sp;
+    sp += static_cast<size_t>(stages) * kStageBytes;
+    uint8_t* rec = sp;                                    // [npairs][12 slots][16 B]
+    sp += static_cast<size_t>(npairs) * kRecBytes;
+    float* xs = reinterpret_cast<float*>(sp);             // [2 * npairs]
+    sp += static_cast<size_t>(npairs) * 8;
+    float* red = reinterpret_cast<float*>(sp);            // [kRing][kCW][16]
+    sp += kRing * kCW * 16 * 4;
+    uint8_t* scratch = sp;                                // [kCW][kScratchBytes]: x staging
+    sp += kCW * kScratchBytes;
+    uint32_t* zero16 = reinterpret_cast<uint32_t*>(sp);   // B fragments of inactive lanes
+    sp += 16;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sp);
+    uint64_t* empty = full + kMaxStages;
+    uint64_t* rfull = empty + kMaxStages;
+    uint64_t* rempty = rfull + kRing;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int units = p.total_rows / kUnit;
+    const int u_begin = static_cast<int>(static_cast<long long>(units) * blockIdx.x / gridDim.x);
+    const int u_end = static_cast<int>(static_cast<long long>(units) * (blockIdx.x + 1) / gridDim.x);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kCW);
+        }
+        for (int b = 0; b < kRing; ++b) {
+            mbar_init(&rfull[b], kCW);
+            mbar_init(&rempty[b], 1);
+        }
+        fence_mbar_init();
+        zero16[0] = zero16[1] = zero16[2] = zero16[3] = 0u;
+    }
+    __syncthreads();
+
+    if (warp == kProducerWarp) {
+        // Weights never depend on the previous kernel: copies start before
+        // griddepcontrol.wait.
+        if (lane == 0) {
+            for (int s = 0; s < p.nseg; ++s) {
+                prefetch_tensormap(&p.seg[s].map8);
+                prefetch_tensormap(&p.seg[s].map4);
+            }
+            SlabWalk walk{u_begin, u_end};
+            int seg, su, nunits, s = 0;
+            uint32_t ph = 0;
+            bool alive = true;
+            while (alive && walk.next(p, seg, su, nunits)) {
+                const ImmaSegment& sg = p.seg[seg];
+                const int r0 = su * kUnit - sg.row0;
+                for (int c = 0; c < nchunks; ++c) {
+                    if (!mbar_wait(&empty[s], ph ^ 1u)) {
+                        alive = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nunits * kUnit * kRS));
+                    const uint32_t st = smem_u32(stage0) + s * kStageBytes;
+                    const int cx = c * (G::kChunkBytes / 8);
+                    tma_load_2d(st, nunits >= 2 ? &sg.map8 : &sg.map4, cx, r0, &full[s]);
+                    if (nunits > 2) tma_load_2d(st + 8 * kRS, nunits == 4 ? &sg.map8 : &sg.map4, cx, r0 + 8, &full[s]);
+                    if (++s == stages) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+            }
+            if (alive && p.prefetch) prefetch_share(p.prefetch, p.prefetch_bytes);
+        }
+        return;
+    }
+
+    if (warp == kEpilogueWarp) {
+        // Fixed-order sum of the consumer warps' partials per slab, then bias /
+        // residual and the store.
+        pdl_wait();
+        SlabWalk walk{u_begin, u_end};
+        int seg, su, nunits, sl = 0;
+        while (walk.next(p, seg, su, nunits)) {
+            const int b = sl % kRing;
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(&rfull[b], (sl / kRing) & 1));
+            if (ok && lane < nunits * kUnit) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int w = 0; w < kCW; ++w) acc += red[(b * kCW + w) * 16 + lane];
+                const ImmaSegment& sg = p.seg[seg];
+                const int lrow = su * kUnit + lane - sg.row0;
+                float out = acc;
+                if (sg.bias) out += sg.bias[lrow];
+                if (sg.residual) out = sg.residual[lrow] + out;
+                sg.y[lrow] = out;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&rempty[b]);
+            ++sl;
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------------- consumers
+    pdl_wait();   // x comes from the previous kernel
+    const int g = lane >> 2, t = lane & 3;
+    const int pair_first = warp * kPPW;                   // this warp's pairs in every chunk
+    // Per-lane constants: smem offsets of the words this lane loads from a
+    // pair (row g; row g + 8 is 8 row strides further), PRMT selectors.
+    int woff[IFmt<FMT>::kWordsPerRow];                    // word index of each code word in row g
+#pragma unroll
+    for (int w = 0; w < IFmt<FMT>::kWordsPerRow; ++w) {
+        const int sw = src_word(FMT, t, w);
+        woff[w] = g * (kRS / 4) + (sw >= 0 ? sw : (FMT == FMT_Q4_0 ? 4 : 8));
+    }
+    const int off_v0 = g * (kRS / 4);
+    const int off_vd = off_v0 + (FMT == FMT_Q4_0 ? 4 : 8);             // the word holding the odd block's d
+    const uint32_t sel_fix = t == 1 ? 0x1076u : 0x3210u;               // the split word of lane 1
+    const uint32_t sel_d = t < 2 ? 0x3210u : 0x7676u;                  // even block's d: V0 low; odd: Vd high
+    const bool bact = t < 2 ? g < 3 : (g >= 4 && g < 7);
+    const int slot = t < 2 ? 2 * g + t : 6 + 2 * (g - 4) + (t - 2);
+    const uint8_t* bptr = bact ? rec + slot * 16 : reinterpret_cast<const uint8_t*>(zero16);
+    const int bstride = bact ? kRecBytes : 0;
+    const float* xsp = xs + (t >> 1);
+    const f2 kd0 = mk2((t & 1) ? 1.0f : 65536.0f, (t & 1) ? 1.0f : 65536.0f);   // digit weights of columns 2t, 2t + 1
+    const f2 kd1 = mk2((t & 1) ? 0.0f : 256.0f, (t & 1) ? 0.0f : 256.0f);
+
+    if (u_begin < u_end) {
+        // digits of this warp's pairs for the whole launch (read by no other warp)
+        stage_x<FMT>(p.x, nchunks * kPPW / 2, rec, xs, scratch + warp * kScratchBytes, warp, lane);
+        __syncwarp();
+    }
+    SlabWalk walk{u_begin, u_end};
+    int seg, su, nunits, s = 0, sl = 0;
+    uint32_t ph = 0;
+    while (walk.next(p, seg, su, nunits)) {
+        f2 y = mk2(0.0f, 0.0f);                           // (row g, row g + 8)
+        for (int c = 0; c < nchunks; ++c) {
+            const int P0 = c * kChunkPairs + pair_first;
+            // warp-uniform: the MMAs below need all 32 lanes
+            if (__all_sync(0xffffffffu, mbar_wait(&full[s], ph))) {
+                const uint8_t* st = stage0 + s * kStageBytes + pair_first * IFmt<FMT>::kPairBytes;
+#pragma unroll
+                for (int j = 0; j < kPPW; ++j) {
+                    const uint32_t* r0 = reinterpret_cast<const uint32_t*>(st + j * IFmt<FMT>::kPairBytes);
+                    const uint32_t* r8 = r0 + 2 * kRS;           // row g + 8
+                    const int P = P0 + j;
+                    uint32_t W0[IFmt<FMT>::kWordsPerRow], W1[IFmt<FMT>::kWordsPerRow];
+#pragma unroll
+                    for (int w = 0; w < IFmt<FMT>::kWordsPerRow; ++w) {
+                        W0[w] = r0[woff[w]];
+                        W1[w] = r8[woff[w]];
+                    }
+                    const uint32_t v00 = r0[off_v0], v01 = r8[off_v0];
+                    const uint32_t vd0 = r0[off_vd], vd1 = r8[off_vd];
+                    constexpr int kLast = IFmt<FMT>::kWordsPerRow - 1;
+                    W0[kLast] = prmt(W0[kLast], v00, sel_fix);
+                    W1[kLast] = prmt(W1[kLast], v01, sel_fix);
+                    const uint32_t d0 = prmt(v00, vd0, sel_d), d1 = prmt(v01, vd1, sel_d);
+                    const uint4 B = *reinterpret_cast<const uint4*>(bptr + P * bstride);
+                    const float xsv = xsp[2 * P];
+                    int acc[4] = {0, 0, 0, 0};
+                    if constexpr (FMT == FMT_Q4_0) {
+                        imma(acc, nib_s8(W0[0] << 4), nib_s8(W1[0] << 4), nib_s8(W0[1] << 4), nib_s8(W1[1] << 4),
+                             B.x, B.y);
+                        imma(acc, nib_s8(W0[0]), nib_s8(W1[0]), nib_s8(W0[1]), nib_s8(W1[1]), B.z, B.w);
+                    } else {
+                        imma(acc, W0[0], W1[0], W0[1], W1[1], B.x, B.y);
+                        imma(acc, W0[2], W1[2], W0[3], W1[3], B.z, B.w);
+                    }
+                    const float dg = __half2float(__ushort_as_half(static_cast<unsigned short>(d0 & 0xFFFFu)));
+                    const float dg8 = __half2float(__ushort_as_half(static_cast<unsigned short>(d1 & 0xFFFFu)));
+                    const f2 c0 = mk2(static_cast<float>(acc[0]), static_cast<float>(acc[2]));
+                    const f2 c1 = mk2(static_cast<float>(acc[1]), static_cast<float>(acc[3]));
+                    const f2 v = fma2(c1, kd1, mul2(c0, kd0));
+                    y = fma2(mul2(mk2(dg, dg8), mk2(xsv, xsv)), v, y);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (++s == stages) {
+                s = 0;
+                ph ^= 1u;
+            }
+        }
+        float y0 = lo(y), y1 = hi(y);
+        y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
+        y1 += __shfl_xor_sync(0xffffffffu, y1, 1);
+        y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
+        y1 += __shfl_xor_sync(0xffffffffu, y1, 2);
+        const int b = sl % kRing;
+        mbar_wait(&rempty[b], ((sl / kRing) & 1) ^ 1u);
+        if (t == 0) {
+            red[(b * kCW + warp) * 16 + g] = y0;
+            red[(b * kCW + warp) * 16 + g + 8] = y1;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&rfull[b]);
+        ++sl;
+    }
+}
+
+template <int FMT>
+bool encode_maps(ImmaSegment& ms, const void* w, int K, int rows) {
+    auto fn = tensor_map_encoder();
+    if (!fn) return false;
+    const size_t row_bytes = static_cast<size_t>(K) / 32 * (FMT == FMT_Q4_0 ? 18 : 34);
+    const cuuint64_t dims[2] = {row_bytes / 8, static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t es[2] = {1, 1};
+    for (int v = 0; v < 2; ++v) {
+        const cuuint32_t box[2] = {static_cast<cuuint32_t>(IGeom<FMT>::kBoxElems), v == 0 ? 8u : 4u};
+        if (fn(v == 0 ? &ms.map8 : &ms.map4, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(w), dims, strides,
+               box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    return true;
+}
+
+int stage_bytes_of(int fmt) {
+    return fmt == FMT_Q4_0 ? IGeom<FMT_Q4_0>::kStageBytes : IGeom<FMT_Q8_0>::kStageBytes;
+}
+
+size_t fixed_smem(int K) {
+    const size_t npairs = static_cast<size_t>(K / 64);
+    return 1024 + npairs * (kRecBytes + 8) + kRing * kCW * 16 * 4 + kCW * kScratchBytes + 16 +
+           (2 * kMaxStages + 2 * kRing) * 8;
+}
+
+// Stages (at most kMaxStages) that fit beside the fixed part in 227 KB.
+void plan_smem(int fmt, int K, int* stages, size_t* smem) {
+    const size_t fixed = fixed_smem(K);
+    const int sb = stage_bytes_of(fmt);
+    *stages = static_cast<int>(std::min<size_t>(kMaxStages, kSmemMax > fixed ? (kSmemMax - fixed) / sb : 0));
+    *smem = fixed + static_cast<size_t>(*stages) * sb;
+}
+
+}  // namespace
+
+bool matvec_imma_supported(int fmt, int K) {
+    if ((fmt != FMT_Q4_0 && fmt != FMT_Q8_0) || K <= 0 || K % 2048 != 0) return false;
+    int stages = 0;
+    size_t smem = 0;
+    plan_smem(fmt, K, &stages, &smem);
+    if (stages < 2) return false;
+    return tensor_map_encoder() != nullptr;
+}
+
+cudaError_t launch_matvec_imma(int fmt, const MatvecParams& mp, cudaStream_t stream, bool pdl) {
+    if (!matvec_imma_supported(fmt, mp.K)) return cudaErrorNotSupported;
+    if (mp.epilogue != EPI_STORE || mp.norm_out || mp.norm_defer || mp.in_parts || mp.tpl.tp > 1)
+        return cudaErrorNotSupported;
+    if ((reinterpret_cast<uintptr_t>(mp.x) & 15) != 0) return cudaErrorNotSupported;
+    for (int s = 0; s < mp.nseg; ++s)
+        if (mp.seg[s].rows % kUnit != 0 || (reinterpret_cast<uintptr_t>(mp.seg[s].w) & 15) != 0)
+            return cudaErrorNotSupported;
+    ImmaParams p;
+    memset(&p, 0, sizeof p);
+    p.nseg = mp.nseg;
+    p.K = mp.K;
+    p.total_rows = mp.total_rows;
+    p.x = mp.x;
+    p.prefetch = static_cast<const uint8_t*>(mp.prefetch);
+    p.prefetch_bytes = mp.prefetch_bytes;
+    int row0 = 0;
+    for (int s = 0; s < mp.nseg; ++s) {
+        ImmaSegment& ms = p.seg[s];
+        const bool ok = fmt == FMT_Q4_0 ? encode_maps<FMT_Q4_0>(ms, mp.seg[s].w, mp.K, mp.seg[s].rows)
+                                        : encode_maps<FMT_Q8_0>(ms, mp.seg[s].w, mp.K, mp.seg[s].rows);
+        if (!ok) return cudaErrorInvalidValue;
+        ms.bias = mp.seg[s].bias;
+        ms.residual = mp.seg[s].residual;
+        ms.y = mp.seg[s].y;
+        ms.rows = mp.seg[s].rows;
+        ms.row0 = row0;
+        row0 += mp.seg[s].rows;
+    }
+    int stages = 0;
+    size_t smem = 0;
+    plan_smem(fmt, mp.K, &stages, &smem);
+    auto kern = fmt == FMT_Q4_0 ? quant_imma_kernel<FMT_Q4_0> : quant_imma_kernel<FMT_Q8_0>;
+    static bool configured[2][64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    bool& done = configured[fmt == FMT_Q4_0 ? 0 : 1][dev & 63];
+    if (!done) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+        if (e != cudaSuccess) return e;
+        done = true;
+    }
+    const int units = mp.total_rows / kUnit;
+    const int grid = std::max(1, std::min(sm_count_for_current_device(), units));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, p, stages);
+}
+
+}  // namespace alj

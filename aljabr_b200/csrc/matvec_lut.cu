@@ -129,20 +129,6 @@ __device__ __forceinline__ float lds32f(uint32_t a) {
     return v;
 }
 
-__device__ __forceinline__ void prefetch_share(const uint8_t* base, size_t bytes) {
-    const size_t share = bytes / gridDim.x;
-    const uintptr_t b0 = reinterpret_cast<uintptr_t>(base);
-    uintptr_t a = (b0 + share * blockIdx.x + 15) & ~uintptr_t(15);
-    const size_t cap = share < (size_t(128) << 10) ? share : (size_t(128) << 10);
-    const uintptr_t lim = b0 + share * blockIdx.x + cap;
-    const uintptr_t end = (lim < b0 + bytes ? lim : b0 + bytes) & ~uintptr_t(15);
-    for (; a + 16 <= end; a += 16384) {
-        const uintptr_t left = end - a;
-        const uint32_t n = static_cast<uint32_t>(left < 16384 ? left : 16384) & ~15u;
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(n) : "memory");
-    }
-}
-
 // norm_out = y * scale * norm_w over the whole output, by the last CTA's
 // consumer warps and epilogue warp (participant index 0 .. 16 * 32 + 31).
 template <typename P>

@@ -179,23 +179,6 @@ __device__ __forceinline__ uint32_t land(uint32_t w, uint32_t m) {
     return r;
 }
 
-// L2 prefetch of this CTA's 1/grid share of [base, base + bytes) -- the part
-// the same CTA index of the next launch reads first (rows are contiguous and
-// dealt out in order) -- capped at 128 KB, strictly inside the range.
-__device__ __forceinline__ void prefetch_share(const uint8_t* base, size_t bytes) {
-    const size_t share = bytes / gridDim.x;
-    const uintptr_t b0 = reinterpret_cast<uintptr_t>(base);
-    uintptr_t a = (b0 + share * blockIdx.x + 15) & ~uintptr_t(15);
-    const size_t cap = share < (size_t(128) << 10) ? share : (size_t(128) << 10);
-    const uintptr_t lim = b0 + share * blockIdx.x + cap;
-    const uintptr_t end = (lim < b0 + bytes ? lim : b0 + bytes) & ~uintptr_t(15);
-    for (; a + 16 <= end; a += 16384) {
-        const uintptr_t left = end - a;
-        const uint32_t n = static_cast<uint32_t>(left < 16384 ? left : 16384) & ~15u;
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(n) : "memory");
-    }
-}
-
 // Slabs of a CTA's unit range, split at segment boundaries (pair mode: both
 // segments advance together over the logical rows).
 // norm_out = y * scale * norm_w over the whole output, by the last CTA's

@@ -80,6 +80,7 @@ def _declare(L):
     L.orc_matvec_q4_0_prepared.argtypes = [_p, _p, _p, _i, _i, _i]
     L.orc_dot_row_q4_0_prepared.argtypes = [_p, _i, _p]
     L.orc_dot_row_q4_0_prepared.restype = _f
+    L.orc_set_decode_threads.argtypes = [_i]
     L.orc_rmsnorm_binding.argtypes = [_p, _p, _p, _i, _f]
     L.orc_silu_ffn_binding.argtypes = [_p, _p, _p, _i]
     L.orc_matvec_q8_0.argtypes = [_p, _p, _p, _i, _i, _i, _i]
@@ -342,6 +343,11 @@ class LlamaCfg(ctypes.Structure):
     _fields_ = [("layers", _i), ("hidden", _i), ("q_heads", _i), ("kv_heads", _i),
                 ("head_dim", _i), ("ffn", _i), ("vocab", _i), ("max_ctx", _i), ("group", _i),
                 ("eps", _f), ("rope_theta", _f)]
+
+
+def set_decode_threads(threads: int) -> None:
+    """Host threads for the decode-step restatements' matvecs (speed only)."""
+    lib().orc_set_decode_threads(int(threads))
 
 
 def decode_step_nf4(cfg: LlamaCfg, codes: list, absmax: list, norms, k_cache, v_cache,

@@ -763,11 +763,11 @@ static int64_t typed_row_bytes(int type, int K) {
 /* y = W x with each row dotted in the reference's raw-row float order for
  * the tensor's GGUF type (GgufRawDot's q4_0 / q8_0 / q4K / q6K routes), or
  * AccelOps.linear's NF4 order. */
-static void typed_matvec_seq(int type, const uint8_t* w, const float* absmax, const float* x, float* y, int K, int N,
-                             int g) {
+static void typed_rows(int type, const uint8_t* w, const float* absmax, const float* x, float* y, int K, int g,
+                       int64_t r0, int64_t r1) {
     const int64_t rb = typed_row_bytes(type, K);
-    for (int r = 0; r < N; r++) {
-        const uint8_t* row = w + (int64_t)r * rb;
+    for (int64_t r = r0; r < r1; r++) {
+        const uint8_t* row = w + r * rb;
         switch (type) {
             case ORC_Q4_0: y[r] = orc_dot_row_q4_0(row, K, x); break;
             case ORC_Q8_0: y[r] = orc_dot_row_q8_0_scalar(row, K, x); break;
@@ -776,6 +776,39 @@ static void typed_matvec_seq(int type, const uint8_t* w, const float* absmax, co
             default: y[r] = nf4_row_dot(w, absmax, x, K, g, r); break;
         }
     }
+}
+
+/* Host threads for the decode-step restatement's matvecs (each row is
+ * computed by one thread in its own fixed order, so the result does not
+ * depend on the count; only the checker's speed does). */
+static int g_decode_threads = 1;
+void orc_set_decode_threads(int threads) { g_decode_threads = threads < 1 ? 1 : (threads > 256 ? 256 : threads); }
+
+typedef struct {
+    int type, K, N, g;
+    const uint8_t* w; const float* absmax; const float* x; float* y;
+    int part, parts;
+} typed_job_t;
+static void* typed_worker(void* arg) {
+    typed_job_t* j = (typed_job_t*)arg;
+    typed_rows(j->type, j->w, j->absmax, j->x, j->y, j->K, j->g, (int64_t)j->N * j->part / j->parts,
+               (int64_t)j->N * (j->part + 1) / j->parts);
+    return NULL;
+}
+static void typed_matvec_seq(int type, const uint8_t* w, const float* absmax, const float* x, float* y, int K, int N,
+                             int g) {
+    const int parts = N >= 64 * g_decode_threads ? g_decode_threads : 1;
+    if (parts == 1) {
+        typed_rows(type, w, absmax, x, y, K, g, 0, N);
+        return;
+    }
+    pthread_t tid[256];
+    typed_job_t jobs[256];
+    for (int p = 0; p < parts; p++) {
+        jobs[p] = (typed_job_t){type, K, N, g, w, absmax, x, y, p, parts};
+        pthread_create(&tid[p], NULL, typed_worker, &jobs[p]);
+    }
+    for (int p = 0; p < parts; p++) pthread_join(tid[p], NULL);
 }
 
 /* One GGUF row (`cols` values) as floats, in the reference's dequantiser

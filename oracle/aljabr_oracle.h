@@ -118,6 +118,9 @@ void orc_decode_step_nf4(const orc_llama_cfg* cfg,
                          const float* norms,   /* [layers][2][H] (attn, ffn) then [H] output norm */
                          void* k_cache, void* v_cache, int kv_bf16,
                          int token, int pos, float* x_out, float* logits);
+/* Host threads the two decode-step restatements use for their matvecs
+ * (rows split among threads; results do not depend on the count). */
+void orc_set_decode_threads(int threads);
 /* One GGUF row (Q4_0 / Q8_0 / Q4_K / Q6_K) in the reference's dequantiser
  * float order (GgufBlockDequantizer, GgufKBlockDequantizer). */
 void orc_dequantize_row_ref(int type, const uint8_t* row, int cols, float* out);

@@ -196,3 +196,31 @@ def test_unsupported_shapes_are_refused(lib):
     with pytest.raises(ProviderError):      # workspace too small
         lib.gemm_nf4_dev([z.data_ptr()], [N], [z.data_ptr()], [N], z.data_ptr(), M, 256, 64,
                          z.data_ptr(), 256)
+
+
+# one rank's TP8 row shard of a Llama-3-70B layer (hidden
+# 8192, 64 query heads, 8 KV heads, head_dim 128, FFN 28672): q/k/v = 1024 +
+# 128 + 128 rows (one launch, three segments), o = 1024 rows, gate/up = 3584
+# + 3584 rows, down = 1024 rows of K = 28672.
+C5_SHARDS = {"qkv": ((1024, 128, 128), 8192), "o": ((1024,), 8192), "gate_up": ((3584, 3584), 8192),
+             "down": ((1024,), 28672)}
+
+
+def _ref64_dense(codes, absmax, xv, n, K, group):
+    """fp64 X W^T on the bit-exact dequantised weight (DequantizationKernel order)."""
+    w = oracle.dequantize_nf4(codes, absmax, n * K, group).reshape(n, K).astype(np.float64)
+    return xv.astype(np.float64) @ w.T
+
+
+@pytest.mark.parametrize("M", [16, 64, 512])
+@pytest.mark.parametrize("shard", sorted(C5_SHARDS))
+def test_c5_tp8_shard_shapes(lib, shard, M):
+    rows, K = C5_SHARDS[shard]
+    g = 64
+    segs = [(*synth.nf4(900 + 17 * i + K // 1024, r, K, g), r) for i, r in enumerate(rows)]
+    xbits, xv = _bf16(np.random.default_rng(M + K).normal(0, 1, (M, K)).astype(np.float32))
+    ys = _run(lib, segs, xbits, M, K, g)
+    pick = np.unique(np.linspace(0, M - 1, min(M, 8)).astype(int))   # tokens checked in the reference order
+    for (c, a, r), y in zip(segs, ys):
+        _check(y, _ref64_dense(c, a, xv, r, K, g))
+        _check(y[pick], _ref(c, a, xv[pick], r, g))
