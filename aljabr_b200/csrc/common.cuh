@@ -129,12 +129,13 @@ __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence
 
 // L2 prefetch of this CTA's 1/grid share of [base, base + bytes) -- the part
 // the same CTA index of the next launch reads first (rows are contiguous and
-// dealt out in order) -- capped at 128 KB, strictly inside the range.
-__device__ __forceinline__ void prefetch_share(const uint8_t* base, size_t bytes) {
+// dealt out in order) -- capped at `limit` bytes (128 KB by default),
+// strictly inside the range.
+__device__ __forceinline__ void prefetch_share(const uint8_t* base, size_t bytes, size_t limit = size_t(128) << 10) {
     const size_t share = bytes / gridDim.x;
     const uintptr_t b0 = reinterpret_cast<uintptr_t>(base);
     uintptr_t a = (b0 + share * blockIdx.x + 15) & ~uintptr_t(15);
-    const size_t cap = share < (size_t(128) << 10) ? share : (size_t(128) << 10);
+    const size_t cap = share < limit ? share : limit;
     const uintptr_t lim = b0 + share * blockIdx.x + cap;
     const uintptr_t end = (lim < b0 + bytes ? lim : b0 + bytes) & ~uintptr_t(15);
     for (; a + 16 <= end; a += 16384) {

@@ -61,8 +61,11 @@ constexpr int kThreads = (kCW + 2) * 32;
 constexpr int kUnit = 4;                     // rows per balancing unit
 constexpr int kMaxStages = 8;
 constexpr int kRing = 4;                     // slab partial buffers
-constexpr int kRecBytes = 192;               // B fragments of one block pair: 12 active lanes x 16 B
+constexpr int kRecBytes = 208;               // B fragments of one block pair: 12 active lanes x 16 B + a zero slot
+constexpr int kZeroSlot = 12;                // the slot that lanes with no B operand read
+constexpr int kSlabUnits = 8;                // a slab is up to 32 rows: two 16-row MMA tiles
 constexpr int kSmemMax = 232448;             // 227 KB opt-in per CTA
+constexpr int kSmemBudget = 220 * 1024;      // planned use: leaves room beside it for small kernels
 constexpr uint32_t kMagic = 0x4B400000u;     // bits of 1.5 * 2^23: fma(x, s, magic) = magic + rint(x s)
 
 template <int FMT>
@@ -85,7 +88,7 @@ struct IGeom {
     static constexpr int kChunkBytes = IFmt<FMT>::kChunkPairs * IFmt<FMT>::kPairBytes;   // 1152 | 1088
     static constexpr int kRowStride = kChunkBytes + 16;                                  // 1168 | 1104
     static constexpr int kBoxElems = kRowStride / 8;                                     // uint64 elements
-    static constexpr int kStageBytes = 16 * kRowStride;
+    static constexpr int kStageBytes = kUnit * kSlabUnits * kRowStride;                 // 32 rows
     static constexpr int kPairsPerWarp = IFmt<FMT>::kChunkPairs / kCW;                   // 2 | 1
 };
 
@@ -129,6 +132,7 @@ struct alignas(64) ImmaParams {
     int nseg;
     int K;
     int total_rows;
+    int slab_units;                          // units per slab (at most kSlabUnits)
     const float* x;
     const uint8_t* prefetch;
     size_t prefetch_bytes;
@@ -156,7 +160,7 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 // High nibbles as s8 16 (c - 8); the same on (w << 4) gives the low nibbles.
 __device__ __forceinline__ uint32_t nib_s8(uint32_t w) { return lop3_and_xor(w, 0xF0F0F0F0u, 0x80808080u); }
 
-// Slabs of <= 16 rows of a CTA's unit range, split at segment boundaries.
+// Slabs of <= 32 rows of a CTA's unit range, split at segment boundaries.
 struct SlabWalk {
     int u, u_end;
     __device__ __forceinline__ bool next(const ImmaParams& p, int& seg, int& su, int& nunits) {
@@ -166,11 +170,87 @@ struct SlabWalk {
         if (p.nseg > 2 && u * kUnit >= p.seg[2].row0) seg = 2;
         const int seg_end = (p.seg[seg].row0 + p.seg[seg].rows) / kUnit;
         su = u;
-        nunits = min(4, min(u_end, seg_end) - u);
+        nunits = min(p.slab_units, min(u_end, seg_end) - u);
         u += nunits;
         return true;
     }
 };
+
+// Shared-memory loads at a 32-bit address plus a compile-time byte offset
+// (folded into the instruction).
+template <int OFF>
+__device__ __forceinline__ uint32_t lds_at(uint32_t a) {
+    uint32_t v;
+    asm("ld.shared.u32 %0, [%1+%2];" : "=r"(v) : "r"(a), "n"(OFF));
+    return v;
+}
+template <int OFF>
+__device__ __forceinline__ uint4 lds4_at(uint32_t a) {
+    uint4 v;
+    asm("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4+%5];"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+        : "r"(a), "n"(OFF));
+    return v;
+}
+
+// Per-lane constants of the consumer loop (lane (g, t) of the MMA).
+struct LaneCtx {
+    uint32_t woff[4];     // smem byte offsets of this lane's code words in row g, pair 0 of the warp
+    uint32_t v0, vd;      // the pair's word 0 (even block's d) and the word holding the odd block's d
+    uint32_t sel_fix;     // PRMT joining the even block's split code word (lane 1)
+    uint32_t sel_d;       // PRMT picking this lane's block scale
+    uint32_t brec;        // smem address of this lane's B record slot, block pair 0
+    uint32_t xsl;         // smem address of this lane's block scale 2^-F, block pair 0
+    f2 kd0, kd1;          // digit weights of accumulator columns 2t, 2t + 1
+};
+
+// One 16-row tile (RT) of block pair J of a stage: 2 MMAs and the fp32 fold.
+// st[w] = stage base + woff[w]; every offset below is a compile-time constant.
+template <int FMT, int J, int RT>
+__device__ __forceinline__ void pair_tile(const LaneCtx& L, const uint32_t (&st)[4], uint32_t sv0, uint32_t svd,
+                                          const uint4& B, const f2& xs2, f2& y) {
+    constexpr int kRS = IGeom<FMT>::kRowStride;
+    constexpr int kNW = IFmt<FMT>::kWordsPerRow;
+    constexpr int O = RT * 16 * kRS + J * IFmt<FMT>::kPairBytes;
+    constexpr int O8 = O + 8 * kRS;                    // row g + 8
+    uint32_t W0[kNW], W1[kNW];
+#pragma unroll
+    for (int w = 0; w < kNW; ++w) {
+        W0[w] = lds_at<O>(st[w]);
+        W1[w] = lds_at<O8>(st[w]);
+    }
+    const uint32_t v00 = lds_at<O>(sv0), v01 = lds_at<O8>(sv0);
+    const uint32_t vd0 = lds_at<O>(svd), vd1 = lds_at<O8>(svd);
+    W0[kNW - 1] = prmt(W0[kNW - 1], v00, L.sel_fix);
+    W1[kNW - 1] = prmt(W1[kNW - 1], v01, L.sel_fix);
+    const uint32_t d0 = prmt(v00, vd0, L.sel_d), d1 = prmt(v01, vd1, L.sel_d);
+    int acc[4] = {0, 0, 0, 0};
+    if constexpr (FMT == FMT_Q4_0) {
+        imma(acc, nib_s8(W0[0] << 4), nib_s8(W1[0] << 4), nib_s8(W0[1] << 4), nib_s8(W1[1] << 4), B.x, B.y);
+        imma(acc, nib_s8(W0[0]), nib_s8(W1[0]), nib_s8(W0[1]), nib_s8(W1[1]), B.z, B.w);
+    } else {
+        imma(acc, W0[0], W1[0], W0[1], W1[1], B.x, B.y);
+        imma(acc, W0[2], W1[2], W0[3], W1[3], B.z, B.w);
+    }
+    const f2 dd = mk2(__half2float(__ushort_as_half(static_cast<unsigned short>(d0 & 0xFFFFu))),
+                      __half2float(__ushort_as_half(static_cast<unsigned short>(d1 & 0xFFFFu))));
+    const f2 c0 = mk2(static_cast<float>(acc[0]), static_cast<float>(acc[2]));
+    const f2 c1 = mk2(static_cast<float>(acc[1]), static_cast<float>(acc[3]));
+    y = fma2(mul2(dd, xs2), fma2(c1, L.kd1, mul2(c0, L.kd0)), y);
+}
+
+// All of a stage's work for one warp: kPPW block pairs x NRT row tiles.
+template <int FMT, int NRT, int J = 0>
+__device__ __forceinline__ void stage_pairs(const LaneCtx& L, const uint32_t (&st)[4], uint32_t sv0, uint32_t svd,
+                                            uint32_t pb, uint32_t px, f2& y0, f2& y1) {
+    constexpr int kRecBytesT = kRecBytes;
+    const uint4 B = lds4_at<J * kRecBytesT>(pb);
+    const float xsv = __uint_as_float(lds_at<J * 8>(px));
+    const f2 xs2 = mk2(xsv, xsv);
+    pair_tile<FMT, J, 0>(L, st, sv0, svd, B, xs2, y0);
+    if constexpr (NRT == 2) pair_tile<FMT, J, 1>(L, st, sv0, svd, B, xs2, y1);
+    if constexpr (J + 1 < IGeom<FMT>::kPairsPerWarp) stage_pairs<FMT, NRT, J + 1>(L, st, sv0, svd, pb, px, y0, y1);
+}
 
 // x digits of every block pair this warp owns (its run of kPPW pairs in each
 // chunk) into B-fragment records and per-block scales, in units of two
@@ -251,6 +331,9 @@ __device__ __forceinline__ void stage_x(const float* __restrict__ x, int nunits,
 #pragma unroll
             for (int d = 0; d < 3; ++d)
                 *reinterpret_cast<uint32_t*>(slot + 32 * d) = prmt(sw[d * 32 + wa], sw[d * 32 + wb], gsel);
+            if (gi < 4)
+                reinterpret_cast<uint32_t*>(rec + static_cast<size_t>(unit_pair<FMT>(u, jb, warp)) * kRecBytes +
+                                            kZeroSlot * 16)[gi] = 0u;
         }
     }
 }
@@ -261,7 +344,10 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
     constexpr int kRS = G::kRowStride;
     constexpr int kStageBytes = G::kStageBytes;
     constexpr int kPPW = G::kPairsPerWarp;
+    constexpr int kPB = IFmt<FMT>::kPairBytes;
+    constexpr int kNW = IFmt<FMT>::kWordsPerRow;
     constexpr int kChunkPairs = IFmt<FMT>::kChunkPairs;
+    constexpr int kRows = kUnit * kSlabUnits;             // 32
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     pdl_launch_dependents();
     const int K = p.K;
@@ -271,16 +357,14 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
     uint8_t* sp = smem_raw + ((1024u - (base & 1023u)) & 1023u);
     uint8_t* stage0 = sp;
     sp += static_cast<size_t>(stages) * kStageBytes;
-    uint8_t* rec = sp;                                    // [npairs][12 slots][16 B]
+    uint8_t* rec = sp;                                    // [npairs][13 slots][16 B]
     sp += static_cast<size_t>(npairs) * kRecBytes;
     float* xs = reinterpret_cast<float*>(sp);             // [2 * npairs]
     sp += static_cast<size_t>(npairs) * 8;
-    float* red = reinterpret_cast<float*>(sp);            // [kRing][kCW][16]
-    sp += kRing * kCW * 16 * 4;
+    float* red = reinterpret_cast<float*>(sp);            // [kRing][kCW][32]
+    sp += kRing * kCW * kRows * 4;
     uint8_t* scratch = sp;                                // [kCW][kScratchBytes]: x staging
     sp += kCW * kScratchBytes;
-    uint32_t* zero16 = reinterpret_cast<uint32_t*>(sp);   // B fragments of inactive lanes
-    sp += 16;
     uint64_t* full = reinterpret_cast<uint64_t*>(sp);
     uint64_t* empty = full + kMaxStages;
     uint64_t* rfull = empty + kMaxStages;
@@ -291,20 +375,10 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
     const int u_begin = static_cast<int>(static_cast<long long>(units) * blockIdx.x / gridDim.x);
     const int u_end = static_cast<int>(static_cast<long long>(units) * (blockIdx.x + 1) / gridDim.x);
 
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < stages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kCW);
-        }
-        for (int b = 0; b < kRing; ++b) {
-            mbar_init(&rfull[b], kCW);
-            mbar_init(&rempty[b], 1);
-        }
-        fence_mbar_init();
-        zero16[0] = zero16[1] = zero16[2] = zero16[3] = 0u;
-    }
-    __syncthreads();
-
+    // The producer and epilogue warps initialise their own barriers and go
+    // (bar.arrive); consumers wait for both (bar.sync) before touching them.
+    // So the first weight copies leave before the rest of the CTA is set up.
+    constexpr int kSetupBar = 1, kSetupThreads = kThreads;
     if (warp == kProducerWarp) {
         // Weights never depend on the previous kernel: copies start before
         // griddepcontrol.wait.
@@ -313,37 +387,59 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
                 prefetch_tensormap(&p.seg[s].map8);
                 prefetch_tensormap(&p.seg[s].map4);
             }
+            for (int s = 0; s < stages; ++s) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], kCW);
+            }
+            fence_mbar_init();
+        }
+        __syncwarp();
+        named_bar_arrive(kSetupBar, kSetupThreads);
+        if (lane == 0) {
             SlabWalk walk{u_begin, u_end};
-            int seg, su, nunits, s = 0;
+            int seg, su, nunits, s = 0, issued = 0;
             uint32_t ph = 0;
             bool alive = true;
             while (alive && walk.next(p, seg, su, nunits)) {
                 const ImmaSegment& sg = p.seg[seg];
                 const int r0 = su * kUnit - sg.row0;
+                const int rows = nunits * kUnit;
                 for (int c = 0; c < nchunks; ++c) {
                     if (!mbar_wait(&empty[s], ph ^ 1u)) {
                         alive = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nunits * kUnit * kRS));
+                    mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rows * kRS));
                     const uint32_t st = smem_u32(stage0) + s * kStageBytes;
                     const int cx = c * (G::kChunkBytes / 8);
-                    tma_load_2d(st, nunits >= 2 ? &sg.map8 : &sg.map4, cx, r0, &full[s]);
-                    if (nunits > 2) tma_load_2d(st + 8 * kRS, nunits == 4 ? &sg.map8 : &sg.map4, cx, r0 + 8, &full[s]);
+                    for (int r = 0; r < rows; r += 8)   // 8-row boxes, a 4-row box for the last 4
+                        tma_load_2d(st + r * kRS, rows - r >= 8 ? &sg.map8 : &sg.map4, cx, r0 + r, &full[s]);
+                    ++issued;
                     if (++s == stages) {
                         s = 0;
                         ph ^= 1u;
                     }
                 }
             }
-            if (alive && p.prefetch) prefetch_share(p.prefetch, p.prefetch_bytes);
+            // the next launch's share of weights into L2 (all of it: this
+            // keeps HBM busy across the launch boundary)
+            if (alive && p.prefetch) prefetch_share(p.prefetch, p.prefetch_bytes, p.prefetch_bytes);
         }
         return;
     }
 
     if (warp == kEpilogueWarp) {
         // Fixed-order sum of the consumer warps' partials per slab, then bias /
-        // residual and the store.
+        // residual and the store; lane r owns slab row r.
+        if (lane == 0) {
+            for (int b = 0; b < kRing; ++b) {
+                mbar_init(&rfull[b], kCW);
+                mbar_init(&rempty[b], 1);
+            }
+            fence_mbar_init();
+        }
+        __syncwarp();
+        named_bar_arrive(kSetupBar, kSetupThreads);
         pdl_wait();
         SlabWalk walk{u_begin, u_end};
         int seg, su, nunits, sl = 0;
@@ -353,7 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
             if (ok && lane < nunits * kUnit) {
                 float acc = 0.0f;
 #pragma unroll
-                for (int w = 0; w < kCW; ++w) acc += red[(b * kCW + w) * 16 + lane];
+                for (int w = 0; w < kCW; ++w) acc += red[(b * kCW + w) * kRows + lane];
                 const ImmaSegment& sg = p.seg[seg];
                 const int lrow = su * kUnit + lane - sg.row0;
                 float out = acc;
@@ -369,79 +465,52 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
     }
 
     // ---------------------------------------------------------------- consumers
+    named_bar(kSetupBar, kSetupThreads);
     pdl_wait();   // x comes from the previous kernel
     const int g = lane >> 2, t = lane & 3;
     const int pair_first = warp * kPPW;                   // this warp's pairs in every chunk
-    // Per-lane constants: smem offsets of the words this lane loads from a
-    // pair (row g; row g + 8 is 8 row strides further), PRMT selectors.
-    int woff[IFmt<FMT>::kWordsPerRow];                    // word index of each code word in row g
-#pragma unroll
-    for (int w = 0; w < IFmt<FMT>::kWordsPerRow; ++w) {
-        const int sw = src_word(FMT, t, w);
-        woff[w] = g * (kRS / 4) + (sw >= 0 ? sw : (FMT == FMT_Q4_0 ? 4 : 8));
-    }
-    const int off_v0 = g * (kRS / 4);
-    const int off_vd = off_v0 + (FMT == FMT_Q4_0 ? 4 : 8);             // the word holding the odd block's d
-    const uint32_t sel_fix = t == 1 ? 0x1076u : 0x3210u;               // the split word of lane 1
-    const uint32_t sel_d = t < 2 ? 0x3210u : 0x7676u;                  // even block's d: V0 low; odd: Vd high
-    const bool bact = t < 2 ? g < 3 : (g >= 4 && g < 7);
-    const int slot = t < 2 ? 2 * g + t : 6 + 2 * (g - 4) + (t - 2);
-    const uint8_t* bptr = bact ? rec + slot * 16 : reinterpret_cast<const uint8_t*>(zero16);
-    const int bstride = bact ? kRecBytes : 0;
-    const float* xsp = xs + (t >> 1);
-    const f2 kd0 = mk2((t & 1) ? 1.0f : 65536.0f, (t & 1) ? 1.0f : 65536.0f);   // digit weights of columns 2t, 2t + 1
-    const f2 kd1 = mk2((t & 1) ? 0.0f : 256.0f, (t & 1) ? 0.0f : 256.0f);
-
     if (u_begin < u_end) {
         // digits of this warp's pairs for the whole launch (read by no other warp)
         stage_x<FMT>(p.x, nchunks * kPPW / 2, rec, xs, scratch + warp * kScratchBytes, warp, lane);
         __syncwarp();
     }
+    // Per-lane constants: offsets within a stage (row g of tile 0, pair 0 of
+    // this warp); rows g + 8, tile 1 and later pairs are constant offsets.
+    LaneCtx L;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        const int sw = w < kNW ? src_word(FMT, t, w) : 0;
+        L.woff[w] = static_cast<uint32_t>(pair_first * kPB + g * kRS + 4 * (sw >= 0 ? sw : (FMT == FMT_Q4_0 ? 4 : 8)));
+    }
+    L.v0 = static_cast<uint32_t>(pair_first * kPB + g * kRS);
+    L.vd = L.v0 + (FMT == FMT_Q4_0 ? 16u : 32u);
+    L.sel_fix = t == 1 ? 0x1076u : 0x3210u;
+    L.sel_d = t < 2 ? 0x3210u : 0x7676u;
+    const bool bact = t < 2 ? g < 3 : (g >= 4 && g < 7);
+    const int slot = bact ? (t < 2 ? 2 * g + t : 6 + 2 * (g - 4) + (t - 2)) : kZeroSlot;
+    L.brec = smem_u32(rec) + slot * 16;
+    L.xsl = smem_u32(xs) + 4u * (t >> 1);
+    L.kd0 = mk2((t & 1) ? 1.0f : 65536.0f, (t & 1) ? 1.0f : 65536.0f);
+    L.kd1 = mk2((t & 1) ? 0.0f : 256.0f, (t & 1) ? 0.0f : 256.0f);
+    const uint32_t stage_s = smem_u32(stage0);
+
     SlabWalk walk{u_begin, u_end};
     int seg, su, nunits, s = 0, sl = 0;
     uint32_t ph = 0;
     while (walk.next(p, seg, su, nunits)) {
-        f2 y = mk2(0.0f, 0.0f);                           // (row g, row g + 8)
+        const bool two = nunits > kSlabUnits / 2;         // rows 16..31 hold data (warp-uniform)
+        f2 y0 = mk2(0.0f, 0.0f), y1 = mk2(0.0f, 0.0f);    // rows (g, g + 8), (g + 16, g + 24)
         for (int c = 0; c < nchunks; ++c) {
             const int P0 = c * kChunkPairs + pair_first;
             // warp-uniform: the MMAs below need all 32 lanes
             if (__all_sync(0xffffffffu, mbar_wait(&full[s], ph))) {
-                const uint8_t* st = stage0 + s * kStageBytes + pair_first * IFmt<FMT>::kPairBytes;
-#pragma unroll
-                for (int j = 0; j < kPPW; ++j) {
-                    const uint32_t* r0 = reinterpret_cast<const uint32_t*>(st + j * IFmt<FMT>::kPairBytes);
-                    const uint32_t* r8 = r0 + 2 * kRS;           // row g + 8
-                    const int P = P0 + j;
-                    uint32_t W0[IFmt<FMT>::kWordsPerRow], W1[IFmt<FMT>::kWordsPerRow];
-#pragma unroll
-                    for (int w = 0; w < IFmt<FMT>::kWordsPerRow; ++w) {
-                        W0[w] = r0[woff[w]];
-                        W1[w] = r8[woff[w]];
-                    }
-                    const uint32_t v00 = r0[off_v0], v01 = r8[off_v0];
-                    const uint32_t vd0 = r0[off_vd], vd1 = r8[off_vd];
-                    constexpr int kLast = IFmt<FMT>::kWordsPerRow - 1;
-                    W0[kLast] = prmt(W0[kLast], v00, sel_fix);
-                    W1[kLast] = prmt(W1[kLast], v01, sel_fix);
-                    const uint32_t d0 = prmt(v00, vd0, sel_d), d1 = prmt(v01, vd1, sel_d);
-                    const uint4 B = *reinterpret_cast<const uint4*>(bptr + P * bstride);
-                    const float xsv = xsp[2 * P];
-                    int acc[4] = {0, 0, 0, 0};
-                    if constexpr (FMT == FMT_Q4_0) {
-                        imma(acc, nib_s8(W0[0] << 4), nib_s8(W1[0] << 4), nib_s8(W0[1] << 4), nib_s8(W1[1] << 4),
-                             B.x, B.y);
-                        imma(acc, nib_s8(W0[0]), nib_s8(W1[0]), nib_s8(W0[1]), nib_s8(W1[1]), B.z, B.w);
-                    } else {
-                        imma(acc, W0[0], W1[0], W0[1], W1[1], B.x, B.y);
-                        imma(acc, W0[2], W1[2], W0[3], W1[3], B.z, B.w);
-                    }
-                    const float dg = __half2float(__ushort_as_half(static_cast<unsigned short>(d0 & 0xFFFFu)));
-                    const float dg8 = __half2float(__ushort_as_half(static_cast<unsigned short>(d1 & 0xFFFFu)));
-                    const f2 c0 = mk2(static_cast<float>(acc[0]), static_cast<float>(acc[2]));
-                    const f2 c1 = mk2(static_cast<float>(acc[1]), static_cast<float>(acc[3]));
-                    const f2 v = fma2(c1, kd1, mul2(c0, kd0));
-                    y = fma2(mul2(mk2(dg, dg8), mk2(xsv, xsv)), v, y);
-                }
+                const uint32_t sb = stage_s + s * kStageBytes;
+                const uint32_t st[4] = {sb + L.woff[0], sb + L.woff[1], sb + L.woff[2], sb + L.woff[3]};
+                const uint32_t pb = L.brec + P0 * kRecBytes, px = L.xsl + 8u * P0;
+                if (two)
+                    stage_pairs<FMT, 2>(L, st, sb + L.v0, sb + L.vd, pb, px, y0, y1);
+                else
+                    stage_pairs<FMT, 1>(L, st, sb + L.v0, sb + L.vd, pb, px, y0, y1);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
@@ -450,16 +519,20 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
                 ph ^= 1u;
             }
         }
-        float y0 = lo(y), y1 = hi(y);
-        y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
-        y1 += __shfl_xor_sync(0xffffffffu, y1, 1);
-        y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
-        y1 += __shfl_xor_sync(0xffffffffu, y1, 2);
+        float r[4] = {lo(y0), hi(y0), lo(y1), hi(y1)};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            r[i] += __shfl_xor_sync(0xffffffffu, r[i], 1);
+            r[i] += __shfl_xor_sync(0xffffffffu, r[i], 2);
+        }
         const int b = sl % kRing;
         mbar_wait(&rempty[b], ((sl / kRing) & 1) ^ 1u);
         if (t == 0) {
-            red[(b * kCW + warp) * 16 + g] = y0;
-            red[(b * kCW + warp) * 16 + g + 8] = y1;
+            float* rr = red + (b * kCW + warp) * kRows;
+            rr[g] = r[0];
+            rr[g + 8] = r[1];
+            rr[g + 16] = r[2];
+            rr[g + 24] = r[3];
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&rfull[b]);
@@ -491,15 +564,17 @@ int stage_bytes_of(int fmt) {
 
 size_t fixed_smem(int K) {
     const size_t npairs = static_cast<size_t>(K / 64);
-    return 1024 + npairs * (kRecBytes + 8) + kRing * kCW * 16 * 4 + kCW * kScratchBytes + 16 +
+    return 1024 + npairs * (kRecBytes + 8) + kRing * kCW * kUnit * kSlabUnits * 4 + kCW * kScratchBytes +
            (2 * kMaxStages + 2 * kRing) * 8;
 }
 
-// Stages (at most kMaxStages) that fit beside the fixed part in 227 KB.
+// Stages (at most kMaxStages) that fit beside the fixed part in the budget
+// (227 KB only when the budget would hold fewer than two stages).
 void plan_smem(int fmt, int K, int* stages, size_t* smem) {
     const size_t fixed = fixed_smem(K);
     const int sb = stage_bytes_of(fmt);
-    *stages = static_cast<int>(std::min<size_t>(kMaxStages, kSmemMax > fixed ? (kSmemMax - fixed) / sb : 0));
+    const size_t budget = fixed + 2 * static_cast<size_t>(sb) <= kSmemBudget ? kSmemBudget : kSmemMax;
+    *stages = static_cast<int>(std::min<size_t>(kMaxStages, budget > fixed ? (budget - fixed) / sb : 0));
     *smem = fixed + static_cast<size_t>(*stages) * sb;
 }
 
@@ -558,6 +633,7 @@ cudaError_t launch_matvec_imma(int fmt, const MatvecParams& mp, cudaStream_t str
     }
     const int units = mp.total_rows / kUnit;
     const int grid = std::max(1, std::min(sm_count_for_current_device(), units));
+    p.slab_units = kSlabUnits;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
