@@ -63,9 +63,12 @@ constexpr int kMaxStages = 8;
 constexpr int kRing = 4;                     // slab partial buffers
 constexpr int kRecBytes = 208;               // B fragments of one block pair: 12 active lanes x 16 B + a zero slot
 constexpr int kZeroSlot = 12;                // the slot that lanes with no B operand read
-constexpr int kSlabUnits = 8;                // a slab is up to 32 rows: two 16-row MMA tiles
+constexpr int kSlabUnits = 8;                // a slab is 32 rows (two 16-row MMA tiles) ...
+constexpr int kMaxSlabUnits = 9;             // ... or 36 when it absorbs a CTA's one leftover unit
+constexpr int kStageRows = 36;               // stage capacity (a third tile's reads of rows 36..39 fall
+                                             // into the next stage or the records: garbage rows, never stored)
+constexpr int kRedRows = kUnit * kMaxSlabUnits;
 constexpr int kSmemMax = 232448;             // 227 KB opt-in per CTA
-constexpr int kSmemBudget = 220 * 1024;      // planned use: leaves room beside it for small kernels
 constexpr uint32_t kMagic = 0x4B400000u;     // bits of 1.5 * 2^23: fma(x, s, magic) = magic + rint(x s)
 
 template <int FMT>
@@ -88,7 +91,10 @@ struct IGeom {
     static constexpr int kChunkBytes = IFmt<FMT>::kChunkPairs * IFmt<FMT>::kPairBytes;   // 1152 | 1088
     static constexpr int kRowStride = kChunkBytes + 16;                                  // 1168 | 1104
     static constexpr int kBoxElems = kRowStride / 8;                                     // uint64 elements
-    static constexpr int kStageBytes = kUnit * kSlabUnits * kRowStride;                 // 32 rows
+    // TMA destinations (stage base + 8-row box offsets) must be 128-byte aligned
+    static constexpr int kStageBytes = (kStageRows * kRowStride + 127) / 128 * 128;
+    static_assert((8 * kRowStride) % 128 == 0, "8-row box offsets must stay 128-byte aligned");
+    static_assert(kStageBytes % 128 == 0, "stage bases must stay 128-byte aligned");
     static constexpr int kPairsPerWarp = IFmt<FMT>::kChunkPairs / kCW;                   // 2 | 1
 };
 
@@ -132,7 +138,6 @@ struct alignas(64) ImmaParams {
     int nseg;
     int K;
     int total_rows;
-    int slab_units;                          // units per slab (at most kSlabUnits)
     const float* x;
     const uint8_t* prefetch;
     size_t prefetch_bytes;
@@ -160,7 +165,9 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 // High nibbles as s8 16 (c - 8); the same on (w << 4) gives the low nibbles.
 __device__ __forceinline__ uint32_t nib_s8(uint32_t w) { return lop3_and_xor(w, 0xF0F0F0F0u, 0x80808080u); }
 
-// Slabs of <= 32 rows of a CTA's unit range, split at segment boundaries.
+// Slabs of 32 rows of a CTA's unit range, split at segment boundaries; a
+// single unit left over at the end joins the last slab (36 rows), so CTAs
+// that hold one unit more than others walk the same number of stages.
 struct SlabWalk {
     int u, u_end;
     __device__ __forceinline__ bool next(const ImmaParams& p, int& seg, int& su, int& nunits) {
@@ -170,7 +177,8 @@ struct SlabWalk {
         if (p.nseg > 2 && u * kUnit >= p.seg[2].row0) seg = 2;
         const int seg_end = (p.seg[seg].row0 + p.seg[seg].rows) / kUnit;
         su = u;
-        nunits = min(p.slab_units, min(u_end, seg_end) - u);
+        const int avail = min(u_end, seg_end) - u;
+        nunits = avail == kSlabUnits + 1 ? avail : min(kSlabUnits, avail);
         u += nunits;
         return true;
     }
@@ -212,7 +220,7 @@ __device__ __forceinline__ void pair_tile(const LaneCtx& L, const uint32_t (&st)
     constexpr int kRS = IGeom<FMT>::kRowStride;
     constexpr int kNW = IFmt<FMT>::kWordsPerRow;
     constexpr int O = RT * 16 * kRS + J * IFmt<FMT>::kPairBytes;
-    constexpr int O8 = O + 8 * kRS;                    // row g + 8
+    constexpr int O8 = RT < 2 ? O + 8 * kRS : O;       // row g + 8 (tile 2: rows 32..35 only)
     uint32_t W0[kNW], W1[kNW];
 #pragma unroll
     for (int w = 0; w < kNW; ++w) {
@@ -242,14 +250,16 @@ __device__ __forceinline__ void pair_tile(const LaneCtx& L, const uint32_t (&st)
 // All of a stage's work for one warp: kPPW block pairs x NRT row tiles.
 template <int FMT, int NRT, int J = 0>
 __device__ __forceinline__ void stage_pairs(const LaneCtx& L, const uint32_t (&st)[4], uint32_t sv0, uint32_t svd,
-                                            uint32_t pb, uint32_t px, f2& y0, f2& y1) {
+                                            uint32_t pb, uint32_t px, f2& y0, f2& y1, f2& y2) {
     constexpr int kRecBytesT = kRecBytes;
     const uint4 B = lds4_at<J * kRecBytesT>(pb);
     const float xsv = __uint_as_float(lds_at<J * 8>(px));
     const f2 xs2 = mk2(xsv, xsv);
     pair_tile<FMT, J, 0>(L, st, sv0, svd, B, xs2, y0);
-    if constexpr (NRT == 2) pair_tile<FMT, J, 1>(L, st, sv0, svd, B, xs2, y1);
-    if constexpr (J + 1 < IGeom<FMT>::kPairsPerWarp) stage_pairs<FMT, NRT, J + 1>(L, st, sv0, svd, pb, px, y0, y1);
+    if constexpr (NRT >= 2) pair_tile<FMT, J, 1>(L, st, sv0, svd, B, xs2, y1);
+    if constexpr (NRT >= 3) pair_tile<FMT, J, 2>(L, st, sv0, svd, B, xs2, y2);
+    if constexpr (J + 1 < IGeom<FMT>::kPairsPerWarp)
+        stage_pairs<FMT, NRT, J + 1>(L, st, sv0, svd, pb, px, y0, y1, y2);
 }
 
 // x digits of every block pair this warp owns (its run of kPPW pairs in each
@@ -265,7 +275,7 @@ __device__ __forceinline__ void stage_pairs(const LaneCtx& L, const uint32_t (&s
 //           (two words and a PRMT per digit) and writes the three record
 //           words of lanes (g, t), g = digit (t < 2) or 4 + digit (t >= 2).
 constexpr int kXBatch = 8;
-constexpr int kScratchBytes = 3 * 128;      // per warp: digit planes h, m, l of a unit's 128 elements
+constexpr int kScratchBytes = 2 * 3 * 128;  // per warp: digit planes h, m, l of two units' 128 elements
 
 template <int FMT>
 __device__ __forceinline__ int unit_pair(int u, int j, int warp) {
@@ -274,10 +284,39 @@ __device__ __forceinline__ int unit_pair(int u, int j, int warp) {
     return kPPW == 2 ? u * kCP + warp * 2 + j : (2 * u + j) * kCP + warp;
 }
 
+// Pass A for one unit: lane l's four elements of unit pair l / 16 into the
+// three digit-plane words of `scratch`, and the block scales.
+template <int FMT>
+__device__ __forceinline__ void stage_pass_a(const float4& v, int u, int warp, int lane, float* xs, uint32_t* swr) {
+    float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    // exponent field E of the max: scale 2^F, F = 148 - E (max 2^F in
+    // [2^21, 2^22)); E clamped below so that 2^-F / 16 stays normal;
+    // a block holding Inf or NaN gets a NaN scale (its rows become NaN).
+    const uint32_t eb = (__float_as_uint(mx) >> 23) & 0xFFu;
+    const uint32_t ec = eb < 26u ? 26u : eb;
+    const float sc = eb == 0xFFu ? 0.0f : __uint_as_float((275u - ec) << 23);
+    const float inv = eb == 0xFFu ? __uint_as_float(0x7FC00000u)
+                                  : __uint_as_float((ec - 21u - (FMT == FMT_Q4_0 ? 4u : 0u)) << 23);
+    if ((lane & 7) == 0) xs[2 * unit_pair<FMT>(u, lane >> 4, warp) + ((lane >> 3) & 1)] = inv;
+    const float xv[4] = {v.x, v.y, v.z, v.w};
+    uint32_t bits[4], mid[4], hig[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        bits[q] = __float_as_uint(__fmaf_rn(xv[q], sc, __uint_as_float(kMagic)));   // magic + X
+        mid[q] = bits[q] + 0x80u;                 // byte 1 = m digit of X
+        hig[q] = bits[q] - 0x3F7F80u;             // byte 2 = h digit of X
+    }
+    swr[0 * 32 + lane] = prmt(prmt(hig[0], hig[1], 0x0062u), prmt(hig[2], hig[3], 0x6200u), 0x7610u);
+    swr[1 * 32 + lane] = prmt(prmt(mid[0], mid[1], 0x0051u), prmt(mid[2], mid[3], 0x5100u), 0x7610u);
+    swr[2 * 32 + lane] = prmt(prmt(bits[0], bits[1], 0x0040u), prmt(bits[2], bits[3], 0x4000u), 0x7610u);
+}
+
 template <int FMT>
 __device__ __forceinline__ void stage_x(const float* __restrict__ x, int nunits, uint8_t* rec, float* xs,
                                         uint8_t* scratch, int warp, int lane) {
-    const int ja = lane >> 4;                                  // pass A: unit pair of this lane
     const int jb = lane >> 4, gi = lane & 15;                  // pass B: (pair, t, m, r)
     const int t = gi >> 2, m = (gi >> 1) & 1, r = gi & 1;
     const int e0 = slot_elem(FMT, t, m, r, 0), e2 = slot_elem(FMT, t, m, r, 2);
@@ -285,55 +324,36 @@ __device__ __forceinline__ void stage_x(const float* __restrict__ x, int nunits,
     const int wa = (bbase + e0) >> 2, wb = (bbase + e2) >> 2;  // scratch words holding bytes e0, e0+1 / e2, e2+1
     const uint32_t gsel = static_cast<uint32_t>((e0 & 3) | ((e0 & 3) + 1) << 4 | (4 + (e2 & 3)) << 8 |
                                                 (5 + (e2 & 3)) << 12);
-    const uint32_t* sw = reinterpret_cast<const uint32_t*>(scratch);
-    uint32_t* swr = reinterpret_cast<uint32_t*>(scratch);
+    uint32_t* sw = reinterpret_cast<uint32_t*>(scratch);      // two units: [2][3 planes][32 words]
+    // pass B of one unit from scratch half h
+    auto pass_b = [&](int u, int h) {
+        const uint32_t* s = sw + h * 96;
+        uint8_t* prec = rec + static_cast<size_t>(unit_pair<FMT>(u, jb, warp)) * kRecBytes;
+        uint8_t* slot = prec + (t < 2 ? t : 4 + t) * 16 + 4 * (2 * m + r);
+#pragma unroll
+        for (int d = 0; d < 3; ++d)
+            *reinterpret_cast<uint32_t*>(slot + 32 * d) = prmt(s[d * 32 + wa], s[d * 32 + wb], gsel);
+        if (gi < 4) reinterpret_cast<uint32_t*>(prec + kZeroSlot * 16)[gi] = 0u;
+    };
     for (int u0 = 0; u0 < nunits; u0 += kXBatch) {
         float4 v[kXBatch];
 #pragma unroll
         for (int b = 0; b < kXBatch; ++b)
             if (u0 + b < nunits)
-                v[b] = __ldg(reinterpret_cast<const float4*>(x + static_cast<size_t>(unit_pair<FMT>(u0 + b, ja, warp)) * 64) +
+                v[b] = __ldg(reinterpret_cast<const float4*>(x + static_cast<size_t>(unit_pair<FMT>(u0 + b, lane >> 4, warp)) * 64) +
                              (lane & 15));
+        // two units per round: their shuffle / PRMT chains overlap
 #pragma unroll
-        for (int b = 0; b < kXBatch; ++b) {
+        for (int b = 0; b < kXBatch; b += 2) {
             const int u = u0 + b;
             if (u >= nunits) break;
-            // ---- pass A
-            float mx = fmaxf(fmaxf(fabsf(v[b].x), fabsf(v[b].y)), fmaxf(fabsf(v[b].z), fabsf(v[b].w)));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-            // exponent field E of the max: scale 2^F, F = 148 - E (max 2^F in
-            // [2^21, 2^22)); E clamped below so that 2^-F / 16 stays normal;
-            // a block holding Inf or NaN gets a NaN scale (its rows become NaN).
-            const uint32_t eb = (__float_as_uint(mx) >> 23) & 0xFFu;
-            const uint32_t ec = eb < 26u ? 26u : eb;
-            const float sc = eb == 0xFFu ? 0.0f : __uint_as_float((275u - ec) << 23);
-            const float inv = eb == 0xFFu ? __uint_as_float(0x7FC00000u)
-                                          : __uint_as_float((ec - 21u - (FMT == FMT_Q4_0 ? 4u : 0u)) << 23);
-            if ((lane & 7) == 0) xs[2 * unit_pair<FMT>(u, ja, warp) + ((lane >> 3) & 1)] = inv;
-            const float xv[4] = {v[b].x, v[b].y, v[b].z, v[b].w};
-            uint32_t bits[4], mid[4], hig[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                bits[q] = __float_as_uint(__fmaf_rn(xv[q], sc, __uint_as_float(kMagic)));   // magic + X
-                mid[q] = bits[q] + 0x80u;                 // byte 1 = m digit of X
-                hig[q] = bits[q] - 0x3F7F80u;             // byte 2 = h digit of X
-            }
-            __syncwarp();                                 // the previous unit's pass B has read the scratch
-            swr[0 * 32 + lane] = prmt(prmt(hig[0], hig[1], 0x0062u), prmt(hig[2], hig[3], 0x6200u), 0x7610u);
-            swr[1 * 32 + lane] = prmt(prmt(mid[0], mid[1], 0x0051u), prmt(mid[2], mid[3], 0x5100u), 0x7610u);
-            swr[2 * 32 + lane] = prmt(prmt(bits[0], bits[1], 0x0040u), prmt(bits[2], bits[3], 0x4000u), 0x7610u);
+            const bool two = u + 1 < nunits;
+            __syncwarp();                                 // the previous round's pass B has read the scratch
+            stage_pass_a<FMT>(v[b], u, warp, lane, xs, sw);
+            if (two) stage_pass_a<FMT>(v[b + 1], u + 1, warp, lane, xs, sw + 96);
             __syncwarp();
-            // ---- pass B: record slot of lane (g, t) is 2 g + t (t < 2) or 6 + 2 (g - 4) + t - 2
-            uint8_t* slot = rec + static_cast<size_t>(unit_pair<FMT>(u, jb, warp)) * kRecBytes + (t < 2 ? t : 4 + t) * 16 +
-                            4 * (2 * m + r);
-#pragma unroll
-            for (int d = 0; d < 3; ++d)
-                *reinterpret_cast<uint32_t*>(slot + 32 * d) = prmt(sw[d * 32 + wa], sw[d * 32 + wb], gsel);
-            if (gi < 4)
-                reinterpret_cast<uint32_t*>(rec + static_cast<size_t>(unit_pair<FMT>(u, jb, warp)) * kRecBytes +
-                                            kZeroSlot * 16)[gi] = 0u;
+            pass_b(u, 0);
+            if (two) pass_b(u + 1, 1);
         }
     }
 }
@@ -347,7 +367,6 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
     constexpr int kPB = IFmt<FMT>::kPairBytes;
     constexpr int kNW = IFmt<FMT>::kWordsPerRow;
     constexpr int kChunkPairs = IFmt<FMT>::kChunkPairs;
-    constexpr int kRows = kUnit * kSlabUnits;             // 32
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     pdl_launch_dependents();
     const int K = p.K;
@@ -361,8 +380,8 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
     sp += static_cast<size_t>(npairs) * kRecBytes;
     float* xs = reinterpret_cast<float*>(sp);             // [2 * npairs]
     sp += static_cast<size_t>(npairs) * 8;
-    float* red = reinterpret_cast<float*>(sp);            // [kRing][kCW][32]
-    sp += kRing * kCW * kRows * 4;
+    float* red = reinterpret_cast<float*>(sp);            // [kRing][kCW][kRedRows]
+    sp += kRing * kCW * kRedRows * 4;
     uint8_t* scratch = sp;                                // [kCW][kScratchBytes]: x staging
     sp += kCW * kScratchBytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(sp);
@@ -446,12 +465,12 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
         while (walk.next(p, seg, su, nunits)) {
             const int b = sl % kRing;
             const bool ok = __all_sync(0xffffffffu, mbar_wait(&rfull[b], (sl / kRing) & 1));
-            if (ok && lane < nunits * kUnit) {
+            for (int r = lane; ok && r < nunits * kUnit; r += 32) {
                 float acc = 0.0f;
 #pragma unroll
-                for (int w = 0; w < kCW; ++w) acc += red[(b * kCW + w) * kRows + lane];
+                for (int w = 0; w < kCW; ++w) acc += red[(b * kCW + w) * kRedRows + r];
                 const ImmaSegment& sg = p.seg[seg];
-                const int lrow = su * kUnit + lane - sg.row0;
+                const int lrow = su * kUnit + r - sg.row0;
                 float out = acc;
                 if (sg.bias) out += sg.bias[lrow];
                 if (sg.residual) out = sg.residual[lrow] + out;
@@ -498,8 +517,8 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
     int seg, su, nunits, s = 0, sl = 0;
     uint32_t ph = 0;
     while (walk.next(p, seg, su, nunits)) {
-        const bool two = nunits > kSlabUnits / 2;         // rows 16..31 hold data (warp-uniform)
-        f2 y0 = mk2(0.0f, 0.0f), y1 = mk2(0.0f, 0.0f);    // rows (g, g + 8), (g + 16, g + 24)
+        const int ntiles = (nunits * kUnit + 15) / 16;    // 1, 2 or 3 (warp-uniform)
+        f2 y0 = mk2(0.0f, 0.0f), y1 = mk2(0.0f, 0.0f), y2 = mk2(0.0f, 0.0f);   // rows (g, g+8), (g+16, g+24), (g+32, -)
         for (int c = 0; c < nchunks; ++c) {
             const int P0 = c * kChunkPairs + pair_first;
             // warp-uniform: the MMAs below need all 32 lanes
@@ -507,10 +526,12 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
                 const uint32_t sb = stage_s + s * kStageBytes;
                 const uint32_t st[4] = {sb + L.woff[0], sb + L.woff[1], sb + L.woff[2], sb + L.woff[3]};
                 const uint32_t pb = L.brec + P0 * kRecBytes, px = L.xsl + 8u * P0;
-                if (two)
-                    stage_pairs<FMT, 2>(L, st, sb + L.v0, sb + L.vd, pb, px, y0, y1);
+                if (ntiles == 2)
+                    stage_pairs<FMT, 2>(L, st, sb + L.v0, sb + L.vd, pb, px, y0, y1, y2);
+                else if (ntiles == 1)
+                    stage_pairs<FMT, 1>(L, st, sb + L.v0, sb + L.vd, pb, px, y0, y1, y2);
                 else
-                    stage_pairs<FMT, 1>(L, st, sb + L.v0, sb + L.vd, pb, px, y0, y1);
+                    stage_pairs<FMT, 3>(L, st, sb + L.v0, sb + L.vd, pb, px, y0, y1, y2);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
@@ -519,20 +540,21 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
                 ph ^= 1u;
             }
         }
-        float r[4] = {lo(y0), hi(y0), lo(y1), hi(y1)};
+        float r[5] = {lo(y0), hi(y0), lo(y1), hi(y1), lo(y2)};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 5; ++i) {
             r[i] += __shfl_xor_sync(0xffffffffu, r[i], 1);
             r[i] += __shfl_xor_sync(0xffffffffu, r[i], 2);
         }
         const int b = sl % kRing;
         mbar_wait(&rempty[b], ((sl / kRing) & 1) ^ 1u);
         if (t == 0) {
-            float* rr = red + (b * kCW + warp) * kRows;
+            float* rr = red + (b * kCW + warp) * kRedRows;
             rr[g] = r[0];
             rr[g + 8] = r[1];
             rr[g + 16] = r[2];
             rr[g + 24] = r[3];
+            if (g < 4) rr[g + 32] = r[4];
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&rfull[b]);
@@ -564,17 +586,15 @@ int stage_bytes_of(int fmt) {
 
 size_t fixed_smem(int K) {
     const size_t npairs = static_cast<size_t>(K / 64);
-    return 1024 + npairs * (kRecBytes + 8) + kRing * kCW * kUnit * kSlabUnits * 4 + kCW * kScratchBytes +
+    return 1024 + npairs * (kRecBytes + 8) + kRing * kCW * kRedRows * 4 + kCW * kScratchBytes +
            (2 * kMaxStages + 2 * kRing) * 8;
 }
 
-// Stages (at most kMaxStages) that fit beside the fixed part in the budget
-// (227 KB only when the budget would hold fewer than two stages).
+// Stages (at most kMaxStages) that fit beside the fixed part in 227 KB.
 void plan_smem(int fmt, int K, int* stages, size_t* smem) {
     const size_t fixed = fixed_smem(K);
     const int sb = stage_bytes_of(fmt);
-    const size_t budget = fixed + 2 * static_cast<size_t>(sb) <= kSmemBudget ? kSmemBudget : kSmemMax;
-    *stages = static_cast<int>(std::min<size_t>(kMaxStages, budget > fixed ? (budget - fixed) / sb : 0));
+    *stages = static_cast<int>(std::min<size_t>(kMaxStages, kSmemMax > fixed ? (kSmemMax - fixed) / sb : 0));
     *smem = fixed + static_cast<size_t>(*stages) * sb;
 }
 
@@ -633,7 +653,6 @@ cudaError_t launch_matvec_imma(int fmt, const MatvecParams& mp, cudaStream_t str
     }
     const int units = mp.total_rows / kUnit;
     const int grid = std::max(1, std::min(sm_count_for_current_device(), units));
-    p.slab_units = kSlabUnits;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
