@@ -303,7 +303,7 @@ def run_ours(args, rank, world, local_rank):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                      "traffic": load_traffic("q4_0_matvec"),
-                     "kernel": "quant_mma_kernel<Q4_0> (avg of 14336x4096 and 4096x14336 launches)",
+                     "kernel": "quant_imma_kernel<Q4_0> (avg of 14336x4096 and 4096x14336 launches)",
                      "algorithmic_bytes_per_launch": STEP_BYTES // 2},
         "gpu_launches": 2 * args.steps,
         "e2e": e2e,
