@@ -163,6 +163,10 @@ cudaError_t launch_gemm_nf4(const GemmNf4Args& a, cudaStream_t stream);
 // Decode glue of the FFM binding (glue.cu): one-CTA RMSNorm and the
 // elementwise SiLU-gated product.
 cudaError_t launch_rmsnorm(float* out, const float* x, const float* w, int n, float eps, cudaStream_t stream);
+// Copies n floats from mapped pinned host memory (its device address) into
+// device memory with a small kernel that releases its programmatic
+// dependent launch at once (glue.cu).
+cudaError_t launch_host_pull(float* dst, const float* src_mapped, size_t n, int sms, cudaStream_t stream);
 cudaError_t launch_silu_ffn(float* out, const float* gate, const float* up, int n, int sms, cudaStream_t stream);
 
 int sm_count_for_current_device();

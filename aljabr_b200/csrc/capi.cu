@@ -72,21 +72,30 @@ struct DevBuf {
         cap = 0;
     }
 };
+// Grow-only pinned host staging buffer, mapped into the device's address
+// space: kernels read inputs from it and store results into it directly.
 struct HostBuf {
     void* p = nullptr;
+    void* dev = nullptr;   // the device address of p
     size_t cap = 0;
     cudaError_t ensure(size_t bytes) {
         if (bytes <= cap) return cudaSuccess;
         if (p) cudaFreeHost(p);
-        p = nullptr;
+        p = dev = nullptr;
         cap = 0;
-        cudaError_t e = cudaMallocHost(&p, bytes);
-        if (e == cudaSuccess) cap = bytes;
+        cudaError_t e = cudaHostAlloc(&p, bytes, cudaHostAllocMapped | cudaHostAllocPortable);
+        if (e == cudaSuccess) e = cudaHostGetDevicePointer(&dev, p, 0);
+        if (e == cudaSuccess) {
+            cap = bytes;
+        } else if (p) {
+            cudaFreeHost(p);
+            p = dev = nullptr;
+        }
         return e;
     }
     void release() {
         if (p) cudaFreeHost(p);
-        p = nullptr;
+        p = dev = nullptr;
         cap = 0;
     }
 };
@@ -269,35 +278,33 @@ int tb_matvec(int nmat, const int* types, const void* const* B, const float* con
         spec[i].N = outs[i].N;
         ytotal += static_cast<size_t>(outs[i].N);
     }
+    // x (and the bias) go to the device through a pull kernel that reads the
+    // mapped staging buffer; the matvecs store y straight into the mapped
+    // output buffer.  No copy-engine transfer: at these sizes its set-up
+    // (several µs each way) costs more than the PCIe traffic.
     std::lock_guard<std::mutex> g(st->mu);
-    const size_t xbytes = static_cast<size_t>(K) * batch * 4;
+    const size_t xfloats = static_cast<size_t>(K) * batch;
     const size_t nb = nmat == 1 && bias_host ? static_cast<size_t>(outs[0].N) : 0;
-    const size_t ybytes = (ytotal * batch + nb) * 4;
-    ALJ_CUDA(st->dx.ensure(xbytes));
-    ALJ_CUDA(st->dy.ensure(ybytes));
-    ALJ_CUDA(st->hx.ensure(xbytes > (nb * 4) ? xbytes : nb * 4));
+    const size_t ybytes = ytotal * batch * 4;
+    ALJ_CUDA(st->dx.ensure((xfloats + nb) * 4));
+    ALJ_CUDA(st->hx.ensure((xfloats + nb) * 4));
     ALJ_CUDA(st->hy.ensure(ybytes));
-    memcpy(st->hx.p, A, xbytes);
-    ALJ_CUDA(cudaMemcpyAsync(st->dx.p, st->hx.p, xbytes, cudaMemcpyHostToDevice, st->stream));
-    float* dbias = nullptr;
-    if (nb) {
-        dbias = static_cast<float*>(st->dy.p) + ytotal * batch;
-        ALJ_CUDA(cudaStreamSynchronize(st->stream));   // hx is reused for the bias below
-        memcpy(st->hx.p, bias_host, nb * 4);
-        ALJ_CUDA(cudaMemcpyAsync(dbias, st->hx.p, nb * 4, cudaMemcpyHostToDevice, st->stream));
-    }
+    memcpy(st->hx.p, A, xfloats * 4);
+    if (nb) memcpy(static_cast<float*>(st->hx.p) + xfloats, bias_host, nb * 4);
+    float* dx = static_cast<float*>(st->dx.p);
+    ALJ_CUDA(launch_host_pull(dx, static_cast<const float*>(st->hx.dev), xfloats + nb, st->sms, st->stream));
+    const float* dbias = nb ? dx + xfloats : nullptr;
+    float* ydev = static_cast<float*>(st->hy.dev);
     for (int b = 0; b < batch; ++b) {
         size_t off = 0;
         for (int i = 0; i < nmat; ++i) {
-            spec[i].y = static_cast<float*>(st->dy.p) + static_cast<size_t>(b) * ytotal + off;
+            spec[i].y = ydev + static_cast<size_t>(b) * ytotal + off;
             spec[i].bias = (i == 0) ? dbias : nullptr;
             off += static_cast<size_t>(outs[i].N);
         }
-        int rc = run_matvecs(st, spec, nmat, static_cast<const float*>(st->dx.p) + static_cast<size_t>(b) * K, K,
-                             group, st->stream);
+        int rc = run_matvecs(st, spec, nmat, dx + static_cast<size_t>(b) * K, K, group, st->stream, true);
         if (rc) return rc;
     }
-    ALJ_CUDA(cudaMemcpyAsync(st->hy.p, st->dy.p, ytotal * batch * 4, cudaMemcpyDeviceToHost, st->stream));
     ALJ_CUDA(cudaStreamSynchronize(st->stream));
     // scatter [b][matrix][N] staging into the callers' buffers
     for (int i = 0, off = 0; i < nmat; off += outs[i].N, ++i)
@@ -721,15 +728,15 @@ int aljabr_blackwell_decode_attention(float* out, const float* q, const void* k_
     std::lock_guard<std::mutex> g(st->mu);
     const size_t n = static_cast<size_t>(q_heads) * head_dim;
     ALJ_CUDA(st->dx.ensure(n * 4));
-    ALJ_CUDA(st->dy.ensure(n * 4));
     ALJ_CUDA(st->hx.ensure(n * 4));
     ALJ_CUDA(st->hy.ensure(n * 4));
     memcpy(st->hx.p, q, n * 4);
-    ALJ_CUDA(cudaMemcpyAsync(st->dx.p, st->hx.p, n * 4, cudaMemcpyHostToDevice, st->stream));
-    rc = run_attention(st, static_cast<float*>(st->dy.p), static_cast<const float*>(st->dx.p), dk, dv, kv_dtype,
+    // q through the pull kernel, the output stored straight into the mapped buffer
+    ALJ_CUDA(launch_host_pull(static_cast<float*>(st->dx.p), static_cast<const float*>(st->hx.dev), n, st->sms,
+                              st->stream));
+    rc = run_attention(st, static_cast<float*>(st->hy.dev), static_cast<const float*>(st->dx.p), dk, dv, kv_dtype,
                        cache_head_stride, head_dim, kv_heads, q_heads, head_dim, seq_len, start_pos, scale, st->stream, &st->dscratch);
     if (rc) return rc;
-    ALJ_CUDA(cudaMemcpyAsync(st->hy.p, st->dy.p, n * 4, cudaMemcpyDeviceToHost, st->stream));
     ALJ_CUDA(cudaStreamSynchronize(st->stream));
     memcpy(out, st->hy.p, n * 4);
     return ALJ_OK;

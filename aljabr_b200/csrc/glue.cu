@@ -45,7 +45,51 @@ __global__ void silu_ffn_kernel(float* out, const float* gate, const float* up, 
     }
 }
 
+constexpr int kPullThreads = 256;
+constexpr int kPullPerThread = 4;                           // float4 loads in flight per thread
+constexpr int kPullCtaElems = kPullThreads * kPullPerThread;   // float4s per CTA round
+
+// Pulls n floats from mapped pinned host memory into device memory.  The
+// host-buffer entry points stage their inputs this way rather than with a
+// copy-engine transfer, whose set-up costs more than the PCIe read itself
+// at these sizes (KB to a few MB).  The kernel releases its dependent launch
+// at once, so a consumer launched with programmatic dependent launch does
+// its set-up and first weight copies while the reads are in flight (its
+// griddepcontrol.wait still waits for this grid to finish).  dst and src
+// are 16-byte aligned.
+__global__ void __launch_bounds__(kPullThreads) host_pull_kernel(float* __restrict__ dst,
+                                                                 const float* __restrict__ src, size_t n) {
+    pdl_launch_dependents();
+    const size_t n4 = n / 4;
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    float4* d4 = reinterpret_cast<float4*>(dst);
+    for (size_t base = static_cast<size_t>(blockIdx.x) * kPullCtaElems; base < n4;
+         base += static_cast<size_t>(gridDim.x) * kPullCtaElems) {
+        float4 v[kPullPerThread];
+#pragma unroll
+        for (int k = 0; k < kPullPerThread; ++k) {
+            const size_t i = base + k * kPullThreads + threadIdx.x;
+            if (i < n4) v[k] = s4[i];
+        }
+#pragma unroll
+        for (int k = 0; k < kPullPerThread; ++k) {
+            const size_t i = base + k * kPullThreads + threadIdx.x;
+            if (i < n4) d4[i] = v[k];
+        }
+    }
+    if (blockIdx.x == 0)
+        for (size_t j = n4 * 4 + threadIdx.x; j < n; j += kPullThreads) dst[j] = src[j];
+}
+
 }  // namespace
+
+cudaError_t launch_host_pull(float* dst, const float* src_mapped, size_t n, int sms, cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    const size_t rounds = (n / 4 + kPullCtaElems - 1) / kPullCtaElems;
+    const int blocks = static_cast<int>(std::max<size_t>(1, std::min<size_t>(rounds, 2 * std::max(1, sms))));
+    host_pull_kernel<<<blocks, kPullThreads, 0, stream>>>(dst, src_mapped, n);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_rmsnorm(float* out, const float* x, const float* w, int n, float eps, cudaStream_t stream) {
     rmsnorm_kernel<<<1, kNormThreads, 0, stream>>>(out, x, w, n, eps);
