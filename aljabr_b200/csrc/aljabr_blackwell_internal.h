@@ -160,6 +160,28 @@ int gemm_nf4_tiles(int M, int nseg, const int* rows);
 size_t gemm_nf4_workspace_bytes(int M, int K, int total_tiles, int grid);
 cudaError_t launch_gemm_nf4(const GemmNf4Args& a, cudaStream_t stream);
 
+// Batched GGUF Q4_0 / Q8_0 GEMM on tcgen05 (gemm_q.cu): y_s[m * ldy_s + n] =
+// sum_k x[m * K + k] * W_s[n][k] for fp32 x, every segment one format, the
+// weights packed by launch_gemm_q_pack.
+struct GemmQArgs {
+    int fmt;                 // FMT_Q4_0 or FMT_Q8_0
+    int nseg;
+    float* y[3];
+    int ldy[3];
+    const void* packed[3];
+    int rows[3];
+    const float* x;          // [M][K] fp32, 16-byte aligned
+    int M, K;
+    void* workspace;
+    size_t workspace_bytes;
+};
+bool gemm_q_supported(int fmt, int M, int K);
+size_t gemm_q_packed_bytes(int fmt, int rows, int K);
+cudaError_t launch_gemm_q_pack(int fmt, void* packed, const void* w, int rows, int K, cudaStream_t stream);
+int gemm_q_tiles(int M, int nseg, const int* rows);
+size_t gemm_q_workspace_bytes(int M, int K);
+cudaError_t launch_gemm_q(const GemmQArgs& a, cudaStream_t stream);
+
 // Decode glue of the FFM binding (glue.cu): one-CTA RMSNorm and the
 // elementwise SiLU-gated product.
 cudaError_t launch_rmsnorm(float* out, const float* x, const float* w, int n, float eps, cudaStream_t stream);

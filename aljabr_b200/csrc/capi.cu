@@ -12,6 +12,7 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include "aljabr_blackwell_internal.h"
@@ -100,6 +101,13 @@ struct HostBuf {
     }
 };
 
+// A Q4_0 / Q8_0 matrix packed for the batched GEMM (gemm_q.cu).
+struct PackedQ {
+    void* p = nullptr;
+    bool finite = true;       // every block scale finite (else the batch runs per row)
+};
+using PackKey = std::tuple<uintptr_t, int, int, int>;   // device weights, type, rows, K
+
 struct DeviceState {
     int device = 0;
     int sms = 0;
@@ -107,8 +115,9 @@ struct DeviceState {
     std::mutex mu;                          // serialises the staging buffers of tb calls
     std::map<uintptr_t, Registered> reg;    // host base -> HBM copy
     std::mutex reg_mu;
-    DevBuf dx, dy, dtmp, dscratch;
+    DevBuf dx, dy, dtmp, dscratch, dgemm;
     HostBuf hx, hy;
+    std::map<PackKey, PackedQ> qpack;       // guarded by mu
 };
 
 std::mutex g_mu;
@@ -251,6 +260,87 @@ struct HostOut {
     void* C;
     int N;
 };
+
+// Packed copy of a Q4_0 / Q8_0 matrix for the batched GEMM: made on first use
+// (on st->stream, with one blocking read of its max-scale word) and kept until
+// the model buffer holding the matrix is unregistered.  Caller holds st->mu.
+int packed_q(DeviceState* st, int type, const void* w, int rows, int K, const PackedQ** out) {
+    const PackKey key{reinterpret_cast<uintptr_t>(w), type, rows, K};
+    auto it = st->qpack.find(key);
+    if (it == st->qpack.end()) {
+        const int fmt = fmt_of(type);
+        PackedQ pq;
+        ALJ_CUDA(cudaMalloc(&pq.p, gemm_q_packed_bytes(fmt, rows, K)));
+        unsigned int maxbits = 0u;
+        cudaError_t e = launch_gemm_q_pack(fmt, pq.p, w, rows, K, st->stream);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(&maxbits, static_cast<const uint8_t*>(pq.p) + 4, 4, cudaMemcpyDeviceToHost, st->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st->stream);
+        if (e != cudaSuccess) {
+            cudaFree(pq.p);
+            return fail(ALJ_ERR_CUDA, "gemm_q_pack: %s", cudaGetErrorString(e));
+        }
+        pq.finite = maxbits < 0x7F800000u;
+        it = st->qpack.emplace(key, pq).first;
+    }
+    *out = &it->second;
+    return ALJ_OK;
+}
+
+// A batch of Q4_0 / Q8_0 rows through the tcgen05 GEMM, every matrix at once:
+// x through the pull kernel, outputs [matrix][b][N] straight into the mapped
+// buffer.  *ran stays false when a matrix has a non-finite block scale (the
+// caller then runs the rows one at a time, as the reference would).  Caller
+// holds st->mu.
+int tb_gemm_q(DeviceState* st, int nmat, int type, const MatSpec* spec, const HostOut* outs, const void* A, int K,
+              int batch, bool* ran) {
+    *ran = false;
+    GemmQArgs a;
+    memset(&a, 0, sizeof a);
+    size_t ytotal = 0;
+    for (int i = 0; i < nmat; ++i) {
+        const PackedQ* pq = nullptr;
+        const int rc = packed_q(st, type, spec[i].w, outs[i].N, K, &pq);
+        if (rc) return rc;
+        if (!pq->finite) return ALJ_OK;
+        a.packed[i] = pq->p;
+        a.rows[i] = outs[i].N;
+        a.ldy[i] = outs[i].N;
+        ytotal += static_cast<size_t>(outs[i].N) * batch;
+    }
+    const size_t xfloats = static_cast<size_t>(K) * batch;
+    const size_t ws = gemm_q_workspace_bytes(batch, K);
+    ALJ_CUDA(st->dx.ensure(xfloats * 4));
+    ALJ_CUDA(st->hx.ensure(xfloats * 4));
+    ALJ_CUDA(st->hy.ensure(ytotal * 4));
+    ALJ_CUDA(st->dgemm.ensure(ws));
+    memcpy(st->hx.p, A, xfloats * 4);
+    float* dx = static_cast<float*>(st->dx.p);
+    ALJ_CUDA(launch_host_pull(dx, static_cast<const float*>(st->hx.dev), xfloats, st->sms, st->stream));
+    size_t off = 0;
+    for (int i = 0; i < nmat; ++i) {
+        a.y[i] = static_cast<float*>(st->hy.dev) + off;
+        off += static_cast<size_t>(outs[i].N) * batch;
+    }
+    a.fmt = fmt_of(type);
+    a.nseg = nmat;
+    a.x = dx;
+    a.M = batch;
+    a.K = K;
+    a.workspace = st->dgemm.p;
+    a.workspace_bytes = ws;
+    const int rc = launch_status(launch_gemm_q(a, st->stream), "gemm_q");
+    if (rc) return rc;
+    ALJ_CUDA(cudaStreamSynchronize(st->stream));
+    off = 0;
+    for (int i = 0; i < nmat; ++i) {
+        const size_t n = static_cast<size_t>(outs[i].N) * batch;
+        memcpy(outs[i].C, static_cast<const float*>(st->hy.p) + off, n * 4);
+        off += n;
+    }
+    *ran = true;
+    return ALJ_OK;
+}
 int tb_matvec(int nmat, const int* types, const void* const* B, const float* const* absmax_host, const float* bias_host,
               const HostOut* outs, const void* A, int K, int group, int batch) {
     int err = 0;
@@ -278,11 +368,21 @@ int tb_matvec(int nmat, const int* types, const void* const* B, const float* con
         spec[i].N = outs[i].N;
         ytotal += static_cast<size_t>(outs[i].N);
     }
+    std::lock_guard<std::mutex> g(st->mu);
+    if (batch >= 2 && !bias_host) {
+        bool same = true;
+        for (int i = 1; i < nmat; ++i) same = same && types[i] == types[0];
+        const int f0 = fmt_of(types[0]);
+        if (same && (f0 == FMT_Q4_0 || f0 == FMT_Q8_0) && gemm_q_supported(f0, batch, K)) {
+            bool ran = false;
+            const int rc = tb_gemm_q(st, nmat, types[0], spec, outs, A, K, batch, &ran);
+            if (rc || ran) return rc;
+        }
+    }
     // x (and the bias) go to the device through a pull kernel that reads the
     // mapped staging buffer; the matvecs store y straight into the mapped
     // output buffer.  No copy-engine transfer: at these sizes its set-up
     // (several µs each way) costs more than the PCIe traffic.
-    std::lock_guard<std::mutex> g(st->mu);
     const size_t xfloats = static_cast<size_t>(K) * batch;
     const size_t nb = nmat == 1 && bias_host ? static_cast<size_t>(outs[0].N) : 0;
     const size_t ybytes = ytotal * batch * 4;
@@ -568,8 +668,10 @@ int aljabr_blackwell_shutdown(void) {
         cudaStreamSynchronize(s->stream);
         for (auto& kv : s->reg) cudaFree(kv.second.dev);
         s->reg.clear();
-        s->dx.release(); s->dy.release(); s->dtmp.release(); s->dscratch.release();
+        s->dx.release(); s->dy.release(); s->dtmp.release(); s->dscratch.release(); s->dgemm.release();
         s->hx.release(); s->hy.release();
+        for (auto& kv : s->qpack) cudaFree(kv.second.p);
+        s->qpack.clear();
         cudaStreamDestroy(s->stream);
         s.reset();
     }
@@ -615,6 +717,20 @@ int aljabr_blackwell_unregister_model_buffer(const void* base_ptr) {
     auto it = st->reg.find(reinterpret_cast<uintptr_t>(base_ptr));
     if (it == st->reg.end()) return fail(ALJ_ERR_NOT_REGISTERED, "buffer %p is not registered", base_ptr);
     cudaStreamSynchronize(st->stream);
+    {
+        // packed GEMM copies of matrices inside this buffer
+        std::lock_guard<std::mutex> gm(st->mu);
+        const uintptr_t lo = reinterpret_cast<uintptr_t>(it->second.dev), hi = lo + it->second.bytes;
+        for (auto q = st->qpack.begin(); q != st->qpack.end();) {
+            const uintptr_t w = std::get<0>(q->first);
+            if (w >= lo && w < hi) {
+                cudaFree(q->second.p);
+                q = st->qpack.erase(q);
+            } else {
+                ++q;
+            }
+        }
+    }
     cudaFree(it->second.dev);
     st->reg.erase(it);
     return ALJ_OK;
@@ -701,6 +817,19 @@ int aljabr_blackwell_matvec_tb_batch(void* C, const void* A, const void* B, int 
     const float* am[1] = {nullptr};
     HostOut o[1] = {{C, N}};
     return tb_matvec(1, &type, b, am, nullptr, o, A, K, 0, batchSize);
+}
+
+int aljabr_blackwell_matvec_tb_triple_batch(void* C0, void* C1, void* C2, const void* A, const void* B0,
+                                            const void* B1, const void* B2, int K, int N0, int N1, int N2,
+                                            int type0, int type1, int type2, int batchSize) {
+    if (batchSize <= 0) return fail(ALJ_ERR_BAD_DIMS, "batchSize=%d", batchSize);
+    const int types[3] = {type0, type1, type2};
+    for (int i = 0; i < 3; ++i)
+        if (types[i] == ALJ_TYPE_NF4) return fail(ALJ_ERR_UNSUPPORTED, "NF4 batches need absmax: use linear_nf4");
+    const void* b[3] = {B0, B1, B2};
+    const float* am[3] = {nullptr, nullptr, nullptr};
+    HostOut o[3] = {{C0, N0}, {C1, N1}, {C2, N2}};
+    return tb_matvec(3, types, b, am, nullptr, o, A, K, 0, batchSize);
 }
 
 int aljabr_blackwell_dequantize_nf4(void* dst, const void* src, const void* scales, long long numel, int groupSize) {
@@ -819,6 +948,68 @@ int aljabr_blackwell_gemm_nf4_dev(int nseg, float* const* y, const int* ldy, con
     if (a.workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
         return fail(ALJ_ERR_BAD_ARG, "gemm_nf4: workspace %lld bytes (need %zu, 256-byte aligned)", workspace_bytes, need);
     return launch_status(launch_gemm_nf4(a, pick_stream(st, stream)), "gemm_nf4");
+}
+
+long long aljabr_blackwell_gemm_q_packed_size(int type, int rows, int K) {
+    const int fmt = fmt_of(type);
+    if (rows < 1 || !gemm_q_supported(fmt, 2, K))
+        return fail(ALJ_ERR_UNSUPPORTED, "gemm_q: type=%d rows=%d K=%d (Q4_0/Q8_0, K %% 256, K <= 32768)", type, rows, K);
+    return static_cast<long long>(gemm_q_packed_bytes(fmt, rows, K));
+}
+
+int aljabr_blackwell_gemm_q_pack(int type, void* packed, const void* weights, int rows, int K, void* stream) {
+    int err = 0;
+    DeviceState* st = state(&err);
+    if (!st) return err;
+    if (!packed || !weights) return fail(ALJ_ERR_BAD_ARG, "gemm_q_pack: null pointer");
+    const int fmt = fmt_of(type);
+    if (rows < 1 || !gemm_q_supported(fmt, 2, K))
+        return fail(ALJ_ERR_UNSUPPORTED, "gemm_q_pack: type=%d rows=%d K=%d", type, rows, K);
+    if (reinterpret_cast<uintptr_t>(packed) & 255) return fail(ALJ_ERR_BAD_ARG, "gemm_q_pack: packed not 256-byte aligned");
+    return launch_status(launch_gemm_q_pack(fmt, packed, weights, rows, K, pick_stream(st, stream)), "gemm_q_pack");
+}
+
+long long aljabr_blackwell_gemm_q_workspace_size(int M, int K) {
+    if (M < 1 || K < 1) return fail(ALJ_ERR_BAD_ARG, "bad gemm_q shape");
+    return static_cast<long long>(gemm_q_workspace_bytes(M, K));
+}
+
+int aljabr_blackwell_gemm_q_dev(int type, int nseg, float* const* y, const int* ldy, const void* const* packed,
+                                const int* rows, const float* x, int M, int K, void* workspace,
+                                long long workspace_bytes, void* stream) {
+    int err = 0;
+    DeviceState* st = state(&err);
+    if (!st) return err;
+    if (nseg < 1 || nseg > 3 || !y || !ldy || !packed || !rows || !x || !workspace)
+        return fail(ALJ_ERR_BAD_ARG, "gemm_q: null argument or nseg=%d", nseg);
+    if (M < 1 || K < 1) return fail(ALJ_ERR_BAD_DIMS, "gemm_q: M=%d K=%d", M, K);
+    if (reinterpret_cast<uintptr_t>(x) & 15) return fail(ALJ_ERR_BAD_ARG, "gemm_q: x not 16-byte aligned");
+    const int fmt = fmt_of(type);
+    if (!gemm_q_supported(fmt, M, K))
+        return fail(ALJ_ERR_UNSUPPORTED, "gemm_q: type=%d K=%d (Q4_0/Q8_0, K %% 256, K <= 32768)", type, K);
+    GemmQArgs a;
+    memset(&a, 0, sizeof a);
+    a.fmt = fmt;
+    a.nseg = nseg;
+    for (int s = 0; s < nseg; ++s) {
+        if (!y[s] || !packed[s]) return fail(ALJ_ERR_BAD_ARG, "gemm_q: null segment %d", s);
+        if (reinterpret_cast<uintptr_t>(packed[s]) & 255)
+            return fail(ALJ_ERR_BAD_ARG, "gemm_q: packed weights %d not 256-byte aligned", s);
+        if (rows[s] < 1 || ldy[s] < rows[s]) return fail(ALJ_ERR_BAD_DIMS, "gemm_q: rows=%d ldy=%d", rows[s], ldy[s]);
+        a.y[s] = y[s];
+        a.ldy[s] = ldy[s];
+        a.packed[s] = packed[s];
+        a.rows[s] = rows[s];
+    }
+    a.x = x;
+    a.M = M;
+    a.K = K;
+    a.workspace = workspace;
+    a.workspace_bytes = workspace_bytes > 0 ? static_cast<size_t>(workspace_bytes) : 0;
+    const size_t need = gemm_q_workspace_bytes(M, K);
+    if (a.workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
+        return fail(ALJ_ERR_BAD_ARG, "gemm_q: workspace %lld bytes (need %zu, 256-byte aligned)", workspace_bytes, need);
+    return launch_status(launch_gemm_q(a, pick_stream(st, stream)), "gemm_q");
 }
 
 int aljabr_blackwell_dequantize_dev(int type, float* dst, const void* src, const float* absmax, long long numel, int group,

@@ -79,6 +79,7 @@ SIGNATURES = {
     "aljabr_blackwell_matvec_tb_pair": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i]),
     "aljabr_blackwell_matvec_tb_triple": (_i, [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i]),
     "aljabr_blackwell_matvec_tb_batch": (_i, [_p, _p, _p, _i, _i, _i, _i]),
+    "aljabr_blackwell_matvec_tb_triple_batch": (_i, [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _i]),
     "aljabr_blackwell_dequantize_nf4": (_i, [_p, _p, _p, _ll, _i]),
     "aljabr_blackwell_dequantize_q4_0": (_i, [_p, _p, _ll]),
     "aljabr_blackwell_dequantize_q8_0": (_i, [_p, _p, _ll]),
@@ -93,6 +94,10 @@ SIGNATURES = {
     "aljabr_blackwell_gemm_nf4_packed_size": (_ll, [_i, _i, _i]),
     "aljabr_blackwell_gemm_nf4_pack": (_i, [_p, _p, _p, _i, _i, _i, _p]),
     "aljabr_blackwell_gemm_nf4_dev": (_i, [_i, _p, _p, _p, _p, _p, _i, _i, _i, _p, _ll, _p]),
+    "aljabr_blackwell_gemm_q_packed_size": (_ll, [_i, _i, _i]),
+    "aljabr_blackwell_gemm_q_pack": (_i, [_i, _p, _p, _i, _i, _p]),
+    "aljabr_blackwell_gemm_q_workspace_size": (_ll, [_i, _i]),
+    "aljabr_blackwell_gemm_q_dev": (_i, [_i, _i, _p, _p, _p, _p, _p, _i, _i, _p, _ll, _p]),
     "aljabr_blackwell_nccl_unique_id": (_i, [_p, _i]),
     "aljabr_blackwell_decode_model_create": (_i, [ctypes.POINTER(_i), _f, _f, _i, _i, _p,
                                                   ctypes.POINTER(ctypes.c_ulonglong)]),
@@ -184,3 +189,36 @@ def gemm_nf4_dev(y, ldy, packed, rows, x_bf16: int, M: int, K: int, group: int,
     return call("aljabr_blackwell_gemm_nf4_dev", n, P(*y), I(*ldy), P(*packed), I(*rows),
                 ctypes.c_void_p(x_bf16), M, K, group, ctypes.c_void_p(workspace), workspace_bytes,
                 None if stream is None else ctypes.c_void_p(stream))
+
+
+def gemm_q_packed_size(type_id: int, rows: int, K: int) -> int:
+    """Bytes of the packed form of one Q4_0 / Q8_0 matrix [rows][K]."""
+    v = lib().aljabr_blackwell_gemm_q_packed_size(type_id, rows, K)
+    if v < 0:
+        check(int(v))
+    return int(v)
+
+
+def gemm_q_workspace_size(M: int, K: int) -> int:
+    """Workspace bytes of one gemm_q_dev call with M tokens."""
+    v = lib().aljabr_blackwell_gemm_q_workspace_size(M, K)
+    if v < 0:
+        check(int(v))
+    return int(v)
+
+
+def gemm_q_pack(type_id: int, packed: int, weights: int, rows: int, K: int, stream=None) -> int:
+    """Repack a Q4_0 / Q8_0 matrix (device GGUF blocks) for gemm_q_dev."""
+    return call("aljabr_blackwell_gemm_q_pack", type_id, ctypes.c_void_p(packed), ctypes.c_void_p(weights), rows, K,
+                None if stream is None else ctypes.c_void_p(stream))
+
+
+def gemm_q_dev(type_id: int, y, ldy, packed, rows, x: int, M: int, K: int, workspace: int, workspace_bytes: int,
+               stream=None) -> int:
+    """Batched Q4_0 / Q8_0 linear on device pointers: y[s][m * ldy[s] + n] = sum_k x[m][k] W_s[n][k]
+    for fp32 x, W_s packed by gemm_q_pack."""
+    n = len(y)
+    P = ctypes.c_void_p * n
+    I = ctypes.c_int * n
+    return call("aljabr_blackwell_gemm_q_dev", type_id, n, P(*y), I(*ldy), P(*packed), I(*rows), ctypes.c_void_p(x),
+                M, K, ctypes.c_void_p(workspace), workspace_bytes, None if stream is None else ctypes.c_void_p(stream))

@@ -163,6 +163,15 @@ int aljabr_blackwell_matvec_tb_triple(void* C0, void* C1, void* C2, const void* 
  * GgufExecutionDispatcher.java:57-72; aljabr_metal_matvec_tb_batch). */
 int aljabr_blackwell_matvec_tb_batch(void* C, const void* A, const void* B, int K, int N, int type,
                                      int batchSize);
+/* batchSize inputs A[b][K] against three matrices: Cs[b][Ns]
+ * (dispatchMatVecTripleBatch, GgufExecutionDispatcher.java:74-98;
+ * aljabr_metal_matvec_tb_triple_batch).  For Q4_0 / Q8_0 with batchSize >= 2
+ * and K a multiple of 256 both batch entry points run the tcgen05 GEMM
+ * (weights packed on first use and cached until their model buffer is
+ * unregistered); other types and shapes run one matvec per input row. */
+int aljabr_blackwell_matvec_tb_triple_batch(void* C0, void* C1, void* C2, const void* A, const void* B0,
+                                            const void* B1, const void* B2, int K, int N0, int N1, int N2,
+                                            int type0, int type1, int type2, int batchSize);
 
 /* ---- host-buffer dequantisation (bit-exact with the reference) ----------- */
 /* DequantizationKernel.dequantizeNf4(src, dst, scales, numel, groupSize),
@@ -248,6 +257,34 @@ long long aljabr_blackwell_gemm_nf4_workspace_size(int M, int K, int nseg, const
 int aljabr_blackwell_gemm_nf4_dev(int nseg, float* const* y, const int* ldy, const void* const* packed,
                                   const int* rows, const void* x_bf16, int M, int K, int blockSize,
                                   void* workspace, long long workspace_bytes, void* stream);
+
+/* ---- batched GGUF Q4_0 / Q8_0 GEMM on tcgen05 (prefill projections) -------
+ * dispatchMatVecBatch / dispatchMatVecTripleBatch for batchSize >= 2
+ * (engine/gguf/aljabr-gguf-java/.../javabackend/GgufExecutionDispatcher.java:
+ * 57-98; the Metal seam's aljabr_metal_matvec_tb_batch / _tb_triple_batch,
+ * backend/metal/.../cpp/metal/aljabr_metal_matvec_api.h:93-106), fp32
+ * activations:
+ *     y_s[m * ldy_s + n] = sum_k X[m][k] * W_s[n][k]        (fp32 out)
+ * for nseg (1..3) matrices W_s of one type sharing X (q/k/v, gate/up).
+ *
+ * gemm_q_pack reads `weights` (device GGUF blocks of `type`, ALJ_TYPE_Q4_0
+ * or ALJ_TYPE_Q8_0, [rows][K/32]) and writes `packed` (device, 256-byte
+ * aligned, gemm_q_packed_size bytes): a header with the matrix's scale
+ * exponent, then per 128-row x 256-column block the codes and the block
+ * scales contiguous.  K a multiple of 256, at most 32768.
+ *
+ * gemm_q_dev: x device fp32 [M][K] (16-byte aligned); workspace device
+ * memory, 256-byte aligned, at least gemm_q_workspace_size bytes, used by one
+ * call at a time.  Stream-ordered on `stream` (NULL = the library's stream).
+ * Block scales that are Inf or NaN make the whole matrix's outputs NaN here;
+ * the host-buffer batch entry points route such matrices to the per-row
+ * matvec instead. */
+long long aljabr_blackwell_gemm_q_packed_size(int type, int rows, int K);
+int aljabr_blackwell_gemm_q_pack(int type, void* packed, const void* weights, int rows, int K, void* stream);
+long long aljabr_blackwell_gemm_q_workspace_size(int M, int K);
+int aljabr_blackwell_gemm_q_dev(int type, int nseg, float* const* y, const int* ldy, const void* const* packed,
+                                const int* rows, const float* x, int M, int K, void* workspace,
+                                long long workspace_bytes, void* stream);
 
 /* Same computation as aljabr_blackwell_decode_attention_dev, for callers that
  * may not allocate device memory at call time.  No counterpart in the

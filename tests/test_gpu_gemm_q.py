@@ -1,0 +1,222 @@
+"""GPU parity of the tcgen05 batched Q4_0 / Q8_0 GEMM (the prefill projections
+that GgufExecutionDispatcher.dispatchMatVecBatch / dispatchMatVecTripleBatch
+run per token, engine/gguf/aljabr-gguf-java/.../javabackend/
+GgufExecutionDispatcher.java:57-98) against the oracle: output row m is the
+reference's fp32 matvec of token m -- GgufQ32Dot's prepared order for Q4_0
+(the reference's default for >= 32 rows), GgufQ32RawDot's raw order, and
+GgufQ8RawDot's vector order for Q8_0 -- and an fp64 ground truth.
+
+Covers token counts on and off the 16/32/64/128 token tiles and several token
+tiles, ragged weight rows, three segments sharing one input (q/k/v), an
+output stride wider than the rows, long K split between CTAs (stream-K
+partials), activations with outliers, very small and large block scales (the
+per-matrix and per-token power-of-two scaling), bit-identical repeats, and the
+host-buffer batch entry points (matvec_tb_batch / _tb_triple_batch),
+including a matrix with a non-finite block scale, which they run per row.
+Tolerance: max element-wise relative error 1e-3, denominator guarded by
+1e-3 * max|ref|."""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from tests import synth
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
+THREADS = os.cpu_count() or 8
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from aljabr_b200 import native
+    native.call("aljabr_blackwell_init", 0)
+    return native
+
+
+def _enc(kind, w):
+    return oracle.encode_q4_0(w) if kind == "q4_0" else oracle.encode_q8_0(w)
+
+
+def _type(lib, kind):
+    return lib.TYPE_Q4_0 if kind == "q4_0" else lib.TYPE_Q8_0
+
+
+def _pack(lib, kind, blocks, rows, K):
+    import torch
+    dw = torch.from_numpy(np.ascontiguousarray(blocks).view(np.uint8).ravel()).cuda()
+    pk = torch.empty(lib.gemm_q_packed_size(_type(lib, kind), rows, K), dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    lib.gemm_q_pack(_type(lib, kind), pk.data_ptr(), dw.data_ptr(), rows, K)
+    torch.cuda.synchronize()
+    return pk
+
+
+def _run(lib, kind, segs, x, ldy=None, repeat=1):
+    """segs: [(gguf blocks, rows)]; x fp32 [M][K].  Returns [y_s [M][rows_s]]."""
+    import torch
+    M, K = x.shape
+    rows = [r for _, r in segs]
+    ldy = ldy or rows
+    dx = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+    pks = [_pack(lib, kind, b, r, K) for b, r in segs]
+    dy = [torch.full((M * l,), float("nan"), dtype=torch.float32, device="cuda") for l in ldy]
+    ws_bytes = lib.gemm_q_workspace_size(M, K)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    outs = []
+    for _ in range(repeat):
+        torch.cuda.synchronize()
+        lib.gemm_q_dev(_type(lib, kind), [y.data_ptr() for y in dy], ldy, [p.data_ptr() for p in pks], rows,
+                       dx.data_ptr(), M, K, ws.data_ptr(), ws_bytes)
+        torch.cuda.synchronize()
+        outs.append([y.cpu().numpy().reshape(M, l)[:, :r].copy() for y, l, r in zip(dy, ldy, rows)])
+    st = ctypes.c_uint(0)
+    lib.call("aljabr_blackwell_device_status", ctypes.byref(st))
+    assert st.value == 0, f"device fault word {st.value:#x}"
+    return outs if repeat > 1 else outs[0]
+
+
+def _refs(kind, blocks, x, N):
+    """Reference-order oracles, one matvec per token."""
+    if kind == "q4_0":
+        return [np.stack([oracle.matvec_q4_0_prepared(blocks, t, N, threads=THREADS) for t in x]),
+                np.stack([oracle.matvec_q4_0(blocks, t, N, threads=THREADS) for t in x])]
+    return [np.stack([oracle.matvec_q8_0(blocks, t, N, vector_order=True, threads=THREADS) for t in x])]
+
+
+def _f64(kind, blocks, x, N):
+    k = oracle.Q4_0 if kind == "q4_0" else oracle.Q8_0
+    return np.stack([oracle.matvec_f64(k, blocks, t, N, threads=THREADS) for t in x])
+
+
+def _check(y, ref, tol=TOL):
+    err = synth.max_rel_err(y, ref)
+    if not err < tol:
+        y64, r64 = np.asarray(y, np.float64), np.asarray(ref, np.float64)
+        rel = np.abs(y64 - r64) / np.maximum(np.abs(r64), 1e-3 * np.abs(r64).max())
+        bad = np.argwhere(~(rel < tol))
+        pts = ", ".join(f"({t},{n}) {y64[t, n]:.4g}/{r64[t, n]:.4g}" for t, n in bad[:8])
+        raise AssertionError(f"max rel err {err:.3g}: {len(bad)} bad of {y64.size}; first: {pts}")
+
+
+def _case(lib, kind, N, K, M, seed, wscale=1.0, xfn=None):
+    w = synth.weights(seed, N, K) * np.float32(wscale)
+    blocks = _enc(kind, w)
+    x = np.stack([synth.activation(seed * 1000 + m, K) for m in range(M)]).astype(np.float32)
+    if xfn is not None:
+        x = xfn(x)
+    (y,) = _run(lib, kind, [(blocks, N)], x)
+    for ref in _refs(kind, blocks, x, N):
+        _check(y, ref)
+    _check(y, _f64(kind, blocks, x, N))
+    return y
+
+
+@pytest.mark.parametrize("kind", ["q4_0", "q8_0"])
+@pytest.mark.parametrize("M", [2, 16, 17, 64, 100, 128, 200])
+def test_token_counts(lib, kind, M):
+    _case(lib, kind, 256, 2048, M, seed=M)
+
+
+@pytest.mark.parametrize("kind", ["q4_0", "q8_0"])
+def test_ragged_rows_and_long_k(lib, kind):
+    _case(lib, kind, 300, 4096, 33, seed=3)             # last row tile partly outside the matrix
+    _case(lib, kind, 256, 14336, 16, seed=4)            # few tiles, long K: tiles split between CTAs
+
+
+@pytest.mark.parametrize("kind", ["q4_0", "q8_0"])
+def test_three_segments_wide_ldy(lib, kind):
+    K, M = 4096, 24
+    rows = [512, 128, 128]
+    blocks = [_enc(kind, synth.weights(10 + i, r, K)) for i, r in enumerate(rows)]
+    x = np.stack([synth.activation(500 + m, K) for m in range(M)]).astype(np.float32)
+    ys = _run(lib, kind, list(zip(blocks, rows)), x, ldy=[r + 37 for r in rows])
+    for y, b, r in zip(ys, blocks, rows):
+        _check(y, _refs(kind, b, x, r)[0])
+
+
+@pytest.mark.parametrize("kind", ["q4_0", "q8_0"])
+def test_outliers_and_scales(lib, kind):
+    def spikes(x):
+        x = x.copy()
+        x[:, ::97] *= 300.0
+        x[3] *= 1e-6                                     # a near-silent token
+        return x
+    _case(lib, kind, 256, 2048, 20, seed=7, xfn=spikes)
+    _case(lib, kind, 256, 2048, 20, seed=8, wscale=1e-4)   # tiny block scales
+    _case(lib, kind, 256, 2048, 20, seed=9, wscale=300.0)  # large block scales
+
+
+def test_repeat_bit_identical(lib):
+    K, M, N = 14336, 40, 384
+    blocks = _enc("q4_0", synth.weights(21, N, K))
+    x = np.stack([synth.activation(900 + m, K) for m in range(M)]).astype(np.float32)
+    outs = _run(lib, "q4_0", [(blocks, N)], x, repeat=3)
+    assert all(np.array_equal(outs[0][0], o[0]) for o in outs[1:])
+
+
+def test_llama_ffn_shape_q4_0(lib):
+    """Up projection of the Llama-3-8B FFN (14336 x 4096) at 64 tokens; the
+    oracle checks a sample of tokens."""
+    N, K, M = 14336, 4096, 64
+    blocks = _enc("q4_0", synth.weights(31, N, K))
+    x = np.stack([synth.activation(1300 + m, K) for m in range(M)]).astype(np.float32)
+    (y,) = _run(lib, "q4_0", [(blocks, N)], x)
+    pick = [0, 17, 63]
+    ref = np.stack([oracle.matvec_q4_0_prepared(blocks, x[m], N, threads=THREADS) for m in pick])
+    _check(y[pick], ref)
+
+
+def _host(lib, arr):
+    return ctypes.c_void_p(arr.ctypes.data)
+
+
+@pytest.mark.parametrize("kind", ["q4_0", "q8_0"])
+def test_tb_batch_and_triple_batch(lib, kind):
+    """Host-buffer batch entry points against the per-token oracle."""
+    K, M = 2048, 8
+    rows = [384, 128, 256]
+    blocks = [np.ascontiguousarray(_enc(kind, synth.weights(40 + i, r, K))) for i, r in enumerate(rows)]
+    for b in blocks:
+        lib.call("aljabr_blackwell_register_model_buffer", _host(lib, b), b.nbytes)
+    try:
+        x = np.ascontiguousarray(np.stack([synth.activation(700 + m, K) for m in range(M)]).astype(np.float32))
+        t = _type(lib, kind)
+        y = np.full((M, rows[0]), np.nan, np.float32)
+        lib.call("aljabr_blackwell_matvec_tb_batch", _host(lib, y), _host(lib, x), _host(lib, blocks[0]), K, rows[0],
+                 t, M)
+        _check(y, _refs(kind, blocks[0], x, rows[0])[0])
+        ys = [np.full((M, r), np.nan, np.float32) for r in rows]
+        lib.call("aljabr_blackwell_matvec_tb_triple_batch", *[_host(lib, v) for v in ys], _host(lib, x),
+                 *[_host(lib, b) for b in blocks], K, *rows, t, t, t, M)
+        for v, b, r in zip(ys, blocks, rows):
+            _check(v, _refs(kind, b, x, r)[0])
+    finally:
+        for b in blocks:
+            lib.call("aljabr_blackwell_unregister_model_buffer", _host(lib, b))
+
+
+def test_tb_batch_nonfinite_scale_runs_per_row(lib):
+    """A matrix with an Inf block scale: the batch entry point returns what the
+    per-row matvec returns for every token."""
+    K, M, N = 2048, 4, 128
+    blocks = np.ascontiguousarray(_enc("q4_0", synth.weights(50, N, K)))
+    raw = blocks.view(np.uint8).reshape(N, -1)
+    raw[5, 18 * 3:18 * 3 + 2] = np.frombuffer(np.float16(np.inf).tobytes(), np.uint8)   # block 3 of row 5
+    lib.call("aljabr_blackwell_register_model_buffer", _host(lib, blocks), blocks.nbytes)
+    try:
+        x = np.ascontiguousarray(np.stack([synth.activation(800 + m, K) for m in range(M)]).astype(np.float32))
+        y = np.zeros((M, N), np.float32)
+        lib.call("aljabr_blackwell_matvec_tb_batch", _host(lib, y), _host(lib, x), _host(lib, blocks), K, N,
+                 lib.TYPE_Q4_0, M)
+        for m in range(M):
+            r = np.zeros(N, np.float32)
+            xm = np.ascontiguousarray(x[m])
+            lib.call("aljabr_blackwell_matvec_tb_q4_0", _host(lib, r), _host(lib, xm), _host(lib, blocks), K, N)
+            np.testing.assert_array_equal(y[m], r)
+        assert not np.isfinite(y[:, 5]).any()
+    finally:
+        lib.call("aljabr_blackwell_unregister_model_buffer", _host(lib, blocks))
