@@ -182,6 +182,22 @@ int gemm_q_tiles(int M, int nseg, const int* rows);
 size_t gemm_q_workspace_bytes(int M, int K);
 cudaError_t launch_gemm_q(const GemmQArgs& a, cudaStream_t stream);
 
+// Prefill attention (prefill_attention.cu): q / out [B][T][Hq][D], k / v
+// [B][S][kv_stride floats per position] with KV head h at h * D; fp32, all
+// 16-byte aligned.  Token t sees keys [max(0, hi - window + 1), hi] with
+// hi = causal ? min(S - 1, t + causal_offset) : S - 1 (window 0: from 0).
+struct PrefillArgs {
+    float* out;
+    const float* q;
+    const float* k;
+    const float* v;
+    int B, T, S, Hq, Hkv, D, kv_stride;
+    int causal, causal_offset, window;
+    float scale, soft_cap;
+};
+bool prefill_attention_supported(int Hq, int Hkv, int D);
+cudaError_t launch_prefill_attention(const PrefillArgs& a, cudaStream_t stream);
+
 // Decode glue of the FFM binding (glue.cu): one-CTA RMSNorm and the
 // elementwise SiLU-gated product.
 cudaError_t launch_rmsnorm(float* out, const float* x, const float* w, int n, float eps, cudaStream_t stream);

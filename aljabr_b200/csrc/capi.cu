@@ -538,6 +538,62 @@ const void* decode_resolve(const void* p) {
 
 using namespace alj;
 
+namespace {
+// Shared host-buffer path of the prefill attention entry points: q, then k
+// and v compacted to kv_heads * head_dim floats per position, through the
+// mapped staging buffer and the pull kernel; the output is stored straight
+// into the mapped output buffer.
+int run_prefill_host(float* out, const float* q, const float* k, const float* v, int B, int T, int S, int Hq, int Hkv,
+                     int D, int kv_stride, float scale, int causal, int causal_offset, int window, float soft_cap) {
+    int err = 0;
+    DeviceState* st = state(&err);
+    if (!st) return err;
+    if (!out || !q || !k || !v) return fail(ALJ_ERR_BAD_ARG, "prefill attention: null pointer");
+    if (B < 1 || T < 1 || S < 1 || !prefill_attention_supported(Hq, Hkv, D) || kv_stride < Hkv * D)
+        return fail(ALJ_ERR_BAD_DIMS, "prefill attention: B=%d T=%d S=%d H=%d H_kv=%d D=%d kv_stride=%d (D %% 32, D <= 256)",
+                    B, T, S, Hq, Hkv, D, kv_stride);
+    const size_t nq = static_cast<size_t>(B) * T * Hq * D;
+    const size_t row = static_cast<size_t>(Hkv) * D;
+    const size_t nk = static_cast<size_t>(B) * S * row;
+    std::lock_guard<std::mutex> g(st->mu);
+    ALJ_CUDA(st->dx.ensure((nq + 2 * nk) * 4));
+    ALJ_CUDA(st->hx.ensure((nq + 2 * nk) * 4));
+    ALJ_CUDA(st->hy.ensure(nq * 4));
+    float* hq = static_cast<float*>(st->hx.p);
+    memcpy(hq, q, nq * 4);
+    float* hk = hq + nq;
+    float* hv = hk + nk;
+    for (size_t p = 0; p < static_cast<size_t>(B) * S; ++p) {
+        memcpy(hk + p * row, k + p * kv_stride, row * 4);
+        memcpy(hv + p * row, v + p * kv_stride, row * 4);
+    }
+    float* d = static_cast<float*>(st->dx.p);
+    ALJ_CUDA(launch_host_pull(d, static_cast<const float*>(st->hx.dev), nq + 2 * nk, st->sms, st->stream));
+    PrefillArgs a;
+    a.out = static_cast<float*>(st->hy.dev);
+    a.q = d;
+    a.k = d + nq;
+    a.v = d + nq + nk;
+    a.B = B;
+    a.T = T;
+    a.S = S;
+    a.Hq = Hq;
+    a.Hkv = Hkv;
+    a.D = D;
+    a.kv_stride = static_cast<int>(row);
+    a.causal = causal;
+    a.causal_offset = causal_offset;
+    a.window = window;
+    a.scale = scale;
+    a.soft_cap = soft_cap;
+    const int rc = launch_status(launch_prefill_attention(a, st->stream), "prefill attention");
+    if (rc) return rc;
+    ALJ_CUDA(cudaStreamSynchronize(st->stream));
+    memcpy(out, st->hy.p, nq * 4);
+    return ALJ_OK;
+}
+}  // namespace
+
 extern "C" {
 
 int aljabr_blackwell_init(int device_id) {
@@ -869,6 +925,59 @@ int aljabr_blackwell_decode_attention(float* out, const float* q, const void* k_
     ALJ_CUDA(cudaStreamSynchronize(st->stream));
     memcpy(out, st->hy.p, n * 4);
     return ALJ_OK;
+}
+
+
+int aljabr_blackwell_prefill_attention(float* out, const float* q, const float* k, const float* v, int tokens,
+                                       int q_heads, int kv_heads, int head_dim, float scale, int sliding_window,
+                                       int kv_stride) {
+    return run_prefill_host(out, q, k, v, 1, tokens, tokens, q_heads, kv_heads, head_dim, kv_stride, scale, 1, 0,
+                            sliding_window > 0 ? sliding_window : 0, 0.0f);
+}
+
+int aljabr_blackwell_fa4_attention(void* output, void* query, void* key, void* value, int B, int T, int S, int H,
+                                   int H_kv, int D, float scale, int is_causal, int use_bf16, float soft_cap) {
+    (void)use_bf16;   // the arithmetic is fp32 either way
+    return run_prefill_host(static_cast<float*>(output), static_cast<const float*>(query),
+                            static_cast<const float*>(key), static_cast<const float*>(value), B, T, S, H, H_kv, D,
+                            H_kv * D, scale, is_causal ? 1 : 0, S > T ? S - T : 0, 0, soft_cap > 0.0f ? soft_cap : 0.0f);
+}
+
+int aljabr_blackwell_fa4_sdpa_available(void) { return 1; }
+int aljabr_blackwell_fa4_bf16_available(void) { return 0; }
+
+int aljabr_blackwell_prefill_attention_dev(float* out, const float* q, const float* k, const float* v, int B, int T,
+                                           int S, int q_heads, int kv_heads, int head_dim, int kv_stride, float scale,
+                                           int causal, int window, float soft_cap, void* stream) {
+    int err = 0;
+    DeviceState* st = state(&err);
+    if (!st) return err;
+    if (!out || !q || !k || !v) return fail(ALJ_ERR_BAD_ARG, "prefill attention: null pointer");
+    if (B < 1 || T < 1 || S < 1 || !prefill_attention_supported(q_heads, kv_heads, head_dim) ||
+        kv_stride < kv_heads * head_dim || kv_stride % 4)
+        return fail(ALJ_ERR_BAD_DIMS, "prefill attention: B=%d T=%d S=%d H=%d H_kv=%d D=%d kv_stride=%d", B, T, S,
+                    q_heads, kv_heads, head_dim, kv_stride);
+    if ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+         reinterpret_cast<uintptr_t>(v)) & 15)
+        return fail(ALJ_ERR_BAD_ARG, "prefill attention: pointers must be 16-byte aligned");
+    PrefillArgs a;
+    a.out = out;
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.B = B;
+    a.T = T;
+    a.S = S;
+    a.Hq = q_heads;
+    a.Hkv = kv_heads;
+    a.D = head_dim;
+    a.kv_stride = kv_stride;
+    a.causal = causal ? 1 : 0;
+    a.causal_offset = S > T ? S - T : 0;
+    a.window = window > 0 ? window : 0;
+    a.scale = scale;
+    a.soft_cap = soft_cap > 0.0f ? soft_cap : 0.0f;
+    return launch_status(launch_prefill_attention(a, pick_stream(st, stream)), "prefill attention");
 }
 
 int aljabr_blackwell_matvec_dev(int type, float* y, const float* x, const void* w, const float* absmax, int K, int N,

@@ -21,13 +21,15 @@
 //     A_lo B_hi (the A_lo B_lo term is below 2^-22 relative) -- into a TMEM
 //     accumulator (two, alternating, for 16-token tiles, so consecutive
 //     small MMAs do not chain);
-//   * the accumulator covers one 256-column unit: the epilogue drains it
-//     after every unit into fp32 registers (round-to-nearest adds) and the
-//     next unit starts a fresh one.  The tensor core's fp32 accumulation
-//     truncates, and over a whole 4096-column row its error reached ~5e-6 of
-//     the row's scale -- a few times the reference's own fp32 rounding, and
-//     over 1e-3 of the smallest outputs; 24 adds per chain keep it well
-//     below that.  The output is scaled by 2^-(f + s) at the end.
+//   * the accumulator covers one 64-column stage: the epilogue drains it
+//     after every stage into fp32 registers (round-to-nearest adds) and the
+//     next stage starts a fresh one.  The tensor core's fp32 accumulation
+//     truncates: over a whole 4096-column row its error reached ~5e-6 of the
+//     row's scale (over 1e-3 of the smallest outputs), and over 256-column
+//     units it still reached 2e-3 where a row's partial sums are large
+//     against its result (constant weights against a periodic input); 12
+//     adds per chain keep it at the level of fp32 summation.  The output is
+//     scaled by 2^-(f + s) at the end.
 // The products are exact in the tensor core; what rounds is the fp32
 // accumulation and the dropped lo x lo term (~2^-22 relative per product).
 //
@@ -47,15 +49,15 @@
 // streamed at a fraction of the HBM rate in the NF4 GEMM.
 //
 // Warp roles (one CTA per SM, all 512 TMEM columns: 4 A stages x 64 columns,
-// then the accumulator buffers of CH x MT columns, one per unit in flight):
+// then the accumulator buffers of CH x MT columns, one per stage in flight):
 //   warps 0-3      dequant: thread r owns weight row r = TMEM lane r; per
 //                  64-column stage it reads its 32 (Q4_0) or 64 (Q8_0) code
 //                  bytes and 2 block scales, forms the 32 fp16 (hi, hi) and 32
 //                  (lo, lo) column pairs and stores them into the stage's
 //                  TMEM columns with two tcgen05.st;
-//   warps 4..      epilogue (1 or 2 warpgroups): after every unit warp w
+//   warps 4..      epilogue (1 or 2 warpgroups): after every stage warp w
 //                  reads TMEM lanes 32 (w % 4) .. +31, a token half each, and
-//                  adds the unit's accumulators into its registers; at the
+//                  adds the stage's accumulators into its registers; at the
 //                  end of a tile piece it writes y (or the piece's partial,
 //                  for a tile split between CTAs);
 //   next warp      weight stream: one TMA copy (two for Q8_0) of a unit's
@@ -311,8 +313,8 @@ __device__ __forceinline__ void split_pair(uint32_t q, uint32_t dd, uint32_t& hi
 
 // One stage: 4 k-steps x (A_hi B_hi, A_hi B_lo, A_lo B_hi) = 12 MMAs, each
 // into the other accumulator than the one before (d1 == d0: one chain), then
-// one commit onto `bar`.  `accum` = 0 starts a unit: the first MMA into d0
-// overwrites it, and the first into d1 too unless d1 is d0.
+// one commit onto `bar`.  `accum` = 0 starts a fresh accumulator: the first
+// MMA into d0 overwrites it, and the first into d1 too unless d1 is d0.
 __device__ __forceinline__ void q_stage_mma(uint32_t d0, uint32_t d1, uint32_t ah, uint64_t bh, uint64_t bl,
                                             uint32_t idesc, uint32_t accum, uint64_t* bar) {
     const uint32_t al = ah + kACols / 2;
@@ -419,8 +421,7 @@ __global__ void __launch_bounds__(32 * (7 + 4 * EW), 1) q_tc_gemm_kernel(const _
     uint64_t* a_full = codes_empty + kMaxCodesRing;
     uint64_t* x_full = a_full + kARing;
     uint64_t* sdone = x_full + kMaxXRing;
-    uint64_t* d_full = sdone + kSDone;
-    uint64_t* d_empty = d_full + kMaxDBufs;
+    uint64_t* d_empty = sdone + kSDone;
     uint64_t* done_bar = d_empty + kMaxDBufs;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(done_bar + 1);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1) + 1;
@@ -436,10 +437,7 @@ __global__ void __launch_bounds__(32 * (7 + 4 * EW), 1) q_tc_gemm_kernel(const _
         for (int i = 0; i < kARing; ++i) mbar_init(&a_full[i], 4);
         for (int i = 0; i < kMaxXRing; ++i) mbar_init(&x_full[i], 1);
         for (int i = 0; i < kSDone; ++i) mbar_init(&sdone[i], 1);
-        for (int i = 0; i < kMaxDBufs; ++i) {
-            mbar_init(&d_full[i], 1);
-            mbar_init(&d_empty[i], 4 * EW);
-        }
+        for (int i = 0; i < kMaxDBufs; ++i) mbar_init(&d_empty[i], 4 * EW);
         mbar_init(done_bar, 1);
         *abort_flag = 0;
         fence_mbar_init();
@@ -502,7 +500,9 @@ __global__ void __launch_bounds__(32 * (7 + 4 * EW), 1) q_tc_gemm_kernel(const _
         const int r = 32 * q + lane;
         const uint32_t tq = tmem_base + (static_cast<uint32_t>(32 * q) << 16);
         pdl_wait();       // token exponents (read at write-out)
-        Cursor dc{0, 0u};
+        // The MMA thread is at most NB stages ahead (it waits for d_empty), so
+        // a stage's sdone slot is not reused before this wait (NB < kSDone).
+        Cursor dc{0, 0u}, sdc{0, 0u};
         bool ok = u1 > u0;
         for (int t = t_first; ok && t <= t_last; ++t) {
             const Piece pc = make_piece(p, t, u0, u1);
@@ -510,8 +510,9 @@ __global__ void __launch_bounds__(32 * (7 + 4 * EW), 1) q_tc_gemm_kernel(const _
             float acc[NT];
 #pragma unroll
             for (int j = 0; j < NT; ++j) acc[j] = 0.0f;
-            for (int c = pc.c0; c < pc.c1; ++c) {
-                if (!warp_wait(&d_full[dc.slot], dc.phase, abort_flag)) { ok = false; break; }
+            for (int i = 0; i < (pc.c1 - pc.c0) * kUnitStages; ++i) {
+                if (!warp_wait(&sdone[sdc.slot], sdc.phase, abort_flag)) { ok = false; break; }
+                sdc.next(kSDone);
                 tc_fence_after();
                 const uint32_t ta = tq + static_cast<uint32_t>(kDCol0 + dc.slot * CH * MT + eh * NT);
 #pragma unroll
@@ -608,23 +609,20 @@ __global__ void __launch_bounds__(32 * (7 + 4 * EW), 1) q_tc_gemm_kernel(const _
             bool ok = u1 > u0;
             for (int t = t_first; ok && t <= t_last; ++t) {
                 const Piece pc = make_piece(p, t, u0, u1);
-                for (int c = pc.c0; ok && c < pc.c1; ++c) {
-                    if (!wait_bar(&d_empty[dc.slot], dc.phase ^ 1u, abort_flag)) { ok = false; break; }
+                for (int i = 0; i < (pc.c1 - pc.c0) * kUnitStages; ++i) {
+                    if (!wait_bar(&d_empty[dc.slot], dc.phase ^ 1u, abort_flag) ||
+                        !wait_bar(&x_full[xc.slot], xc.phase, abort_flag) ||
+                        !wait_bar(&a_full[ac.slot], ac.phase, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
                     const uint32_t d0 = tmem_base + static_cast<uint32_t>(kDCol0 + dc.slot * CH * MT);
-                    for (int st = 0; st < kUnitStages; ++st) {
-                        if (!wait_bar(&x_full[xc.slot], xc.phase, abort_flag) ||
-                            !wait_bar(&a_full[ac.slot], ac.phase, abort_flag)) { ok = false; break; }
-                        tc_fence_after();
-                        const uint32_t ah = tmem_base + static_cast<uint32_t>(ac.slot * kACols);
-                        const uint32_t xs = smem_u32(x_ring + static_cast<size_t>(xc.slot) * kXBytes);
-                        q_stage_mma(d0, d0 + (CH - 1) * MT, ah, sdesc(xs), sdesc(xs + kXPlane), kIdesc,
-                                    st > 0 ? 1u : 0u, &sdone[sd.slot]);
-                        xc.next(SX);
-                        ac.next(SA);
-                        sd.next(kSDone);
-                    }
-                    if (!ok) break;
-                    tc_commit(&d_full[dc.slot]);    // the unit's accumulator is complete
+                    const uint32_t ah = tmem_base + static_cast<uint32_t>(ac.slot * kACols);
+                    const uint32_t xs = smem_u32(x_ring + static_cast<size_t>(xc.slot) * kXBytes);
+                    // a fresh accumulator per stage; sdone reports it complete
+                    q_stage_mma(d0, d0 + (CH - 1) * MT, ah, sdesc(xs), sdesc(xs + kXPlane), kIdesc, 0u,
+                                &sdone[sd.slot]);
+                    xc.next(SX);
+                    ac.next(SA);
+                    sd.next(kSDone);
                     dc.next(NB);
                 }
             }

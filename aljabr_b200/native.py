@@ -90,6 +90,11 @@ SIGNATURES = {
     "aljabr_blackwell_dequantize_dev": (_i, [_i, _p, _p, _p, _ll, _i, _p]),
     "aljabr_blackwell_decode_attention_dev": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _p]),
     "aljabr_blackwell_decode_attention_noalloc": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _p]),
+    "aljabr_blackwell_prefill_attention": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _f, _i, _i]),
+    "aljabr_blackwell_fa4_attention": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _f, _i, _i, _f]),
+    "aljabr_blackwell_fa4_sdpa_available": (_i, []),
+    "aljabr_blackwell_fa4_bf16_available": (_i, []),
+    "aljabr_blackwell_prefill_attention_dev": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _i, _i, _f, _p]),
     "aljabr_blackwell_gemm_nf4_workspace_size": (_ll, [_i, _i, _i, _p]),
     "aljabr_blackwell_gemm_nf4_packed_size": (_ll, [_i, _i, _i]),
     "aljabr_blackwell_gemm_nf4_pack": (_i, [_p, _p, _p, _i, _i, _i, _p]),

@@ -339,6 +339,7 @@ def capture(torch, stream, record):
 
 def run_extra(args, dev, stream, sh, l2, which=None, reps=200):
     c5_tokens = [int(v) for v in getattr(args, "c5_tokens", "1,16,64,512").split(",")]
+    prefill_tokens = [int(v) for v in getattr(args, "prefill_tokens", "16,64,512").split(",")]
     """Secondary configs, each with its own pool > 2 x L2 and device timing.
     `which` selects a subset of {"nf4", "q8", "attention", "c5", "kquant"} (all if None)."""
     import torch
@@ -547,8 +548,106 @@ def run_extra(args, dev, stream, sh, l2, which=None, reps=200):
             "peaks": {"hbm_GB/s": hbm_peak, "hbm": hbm_kind, "bf16_TFLOP/s": tc_peak, "tensor": tc_kind},
             "tokens": res}
 
+    def prefill_section():
+        # Prefill of one Llama-3-8B layer with GGUF Q4_0 weights (the format of
+        # configs[1]): the seven projections through the batched tcgen05 GEMM
+        # (q/k/v and gate/up as multi-segment calls, fp32 activations) and the
+        # causal GQA attention (32 / 8 heads, head_dim 128) over T prompt
+        # tokens.  Weights: uniform random Q4_0 codes, block scales
+        # |N(0.002, 0.0005)| in fp16; packed once per matrix (not timed).
+        H, FF, HQ, HKV, D = 4096, 14336, 32, 8, 128
+        shp = {"q": (HQ * D, H), "k": (HKV * D, H), "v": (HKV * D, H), "o": (H, HQ * D),
+               "gate": (FF, H), "up": (FF, H), "down": (H, FF)}
+        nweights = sum(n * k for n, k in shp.values())
+        wbytes = sum(n * k // 32 * 18 for n, k in shp.values())
+        poolp = max(2, int(np.ceil(2.5 * l2 / wbytes)))
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(9)
+        packed, raw_o = [], None
+        for li in range(poolp):
+            lp = {}
+            for name, (n, k) in shp.items():
+                blk = torch.randint(0, 256, (n * k // 32, 18), dtype=torch.uint8, device=dev, generator=gen)
+                d = (0.002 + 0.0005 * torch.randn(n * k // 32, device=dev, generator=gen)).abs().half()
+                blk[:, 0:2] = d.view(torch.uint8).reshape(-1, 2)
+                pk = torch.empty(native.gemm_q_packed_size(native.TYPE_Q4_0, n, k), dtype=torch.uint8, device=dev)
+                torch.cuda.synchronize(dev)
+                native.gemm_q_pack(native.TYPE_Q4_0, pk.data_ptr(), blk.data_ptr(), n, k, sh.value)
+                lp[name] = pk
+                if li == 0 and name == "o":
+                    raw_o = blk.cpu().numpy().reshape(-1)
+                del blk, d
+            packed.append(lp)
+        torch.cuda.synchronize(dev)
+        tc_peak, tc_kind = load_tc_peak()
+        hbm_peak, hbm_kind = load_peaks()
+        res = {}
+        for T in prefill_tokens:
+            xh = torch.randn(T, H, device=dev)
+            xf = torch.randn(T, FF, device=dev)
+            ys = {name: torch.empty(T * n, device=dev) for name, (n, _) in shp.items()}
+            wsb = native.gemm_q_workspace_size(T, FF)
+            ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+            calls = ((("q", "k", "v"), xh, H), (("o",), xh, H), (("gate", "up"), xh, H), (("down",), xf, FF))
+
+            def gemm_layer(i):
+                lay = packed[i % poolp]
+                for names, x, k in calls:
+                    native.gemm_q_dev(native.TYPE_Q4_0, [ys[nm].data_ptr() for nm in names],
+                                      [shp[nm][0] for nm in names], [lay[nm].data_ptr() for nm in names],
+                                      [shp[nm][0] for nm in names], x.data_ptr(), T, k, ws.data_ptr(), wsb, sh.value)
+            qa = torch.randn(T, HQ * D, device=dev)
+            ka = torch.randn(T, HKV * D, device=dev)
+            va = torch.randn(T, HKV * D, device=dev)
+            oa = torch.empty(T, HQ * D, device=dev)
+            scale = float(1.0 / np.sqrt(D))
+
+            def attention(i):
+                native.check(L.aljabr_blackwell_prefill_attention_dev(
+                    oa.data_ptr(), qa.data_ptr(), ka.data_ptr(), va.data_ptr(), 1, T, T, HQ, HKV, D, HKV * D,
+                    scale, 1, 0, 0.0, sh))
+            torch.cuda.synchronize(dev)
+            reps_t = max(5, min(50, 20000 // T))
+            ms_g = timed(gemm_layer, reps_t)
+            ms_a = timed(attention, reps_t)
+            # spot checks: token 0 of the o projection (pool slot 0), the attention at T = 64
+            gemm_layer(0)
+            torch.cuda.synchronize(dev)
+            x0 = xh[0].cpu().numpy()
+            ref_o = oracle.matvec_q4_0_prepared(raw_o, x0, H, threads=os.cpu_count() or 8)
+            err_g = float(np.max(np.abs(ys["o"][:H].cpu().numpy() - ref_o) /
+                                 np.maximum(np.abs(ref_o), 1e-3 * np.abs(ref_o).max())))
+            err_a = None
+            if T == 64:
+                attention(0)
+                torch.cuda.synchronize(dev)
+                ref_a = oracle.prefill_attention(qa.cpu().numpy(), ka.cpu().numpy(), va.cpu().numpy(), T, HQ, HKV,
+                                                 D, scale)
+                got = oa.cpu().numpy()
+                err_a = float(np.max(np.abs(got - ref_a) / np.maximum(np.abs(ref_a), 1e-3 * np.abs(ref_a).max())))
+            flops_g = 2.0 * T * nweights
+            flops_a = 2.0 * 2.0 * HQ * D * T * (T + 1) / 2
+            hbm_floor_us = wbytes / (hbm_peak * 1e3)
+            tc_floor_us = 3.0 * flops_g / (tc_peak * 1e6)       # three MMAs per weight x token (hi/lo split)
+            us = (ms_g + ms_a) * 1e3
+            res[f"T{T}"] = {"layer_us": round(us, 2), "tokens_per_s_per_layer": round(T / (us * 1e-6), 1),
+                            "gemm_us": round(ms_g * 1e3, 2), "gemm_TFLOP/s": round(flops_g / (ms_g * 1e9), 1),
+                            "gemm_weight_GB/s": round(wbytes / (ms_g * 1e6), 1),
+                            "gemm_floor_us": round(max(hbm_floor_us, tc_floor_us), 2),
+                            "gemm_bound": "hbm" if hbm_floor_us >= tc_floor_us else "tensor",
+                            "gemm_frac_of_floor": round(max(hbm_floor_us, tc_floor_us) / (ms_g * 1e3), 3),
+                            "attention_us": round(ms_a * 1e3, 2),
+                            "attention_TFLOP/s": round(flops_a / (ms_a * 1e9), 2),
+                            "gemm_max_rel_err_token0_o": err_g, "attention_max_rel_err": err_a}
+            del ys, ws, xh, xf, qa, ka, va, oa
+            torch.cuda.empty_cache()
+        out["prefill_q4_0_llama3_8b_layer"] = {
+            "weights": nweights, "weight_bytes": wbytes, "pool_layers": poolp,
+            "peaks": {"hbm_GB/s": hbm_peak, "hbm": hbm_kind, "bf16_TFLOP/s": tc_peak, "tensor": tc_kind},
+            "tokens": res}
+
     for name, fn in (("nf4", nf4_section), ("q8", q8_section), ("attention", attention_section),
-                     ("kquant", kquant_section), ("c5", c5_section)):
+                     ("kquant", kquant_section), ("c5", c5_section), ("prefill", prefill_section)):
         if want(name):
             fn()
             torch.cuda.empty_cache()
@@ -785,13 +884,15 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--no-prefetch", action="store_true", help="no L2 prefetch hints between the headline launches")
-    ap.add_argument("--only", choices=["nf4", "q8", "attention", "decode", "c5", "kquant"],
+    ap.add_argument("--only", choices=["nf4", "q8", "attention", "decode", "c5", "kquant", "prefill"],
                     help="run one secondary workload alone (for profiling); prints its dict")
     ap.add_argument("--decode-tokens", type=int, default=32)
     ap.add_argument("--decode-weights", default="nf4", choices=["nf4", "q4_0", "q4_k_m"],
                     help="weight formats of the --only decode model (GGUF types on one GPU only)")
     ap.add_argument("--c5-tokens", default="1,16,64,512",
                     help="token counts of the batched-NF4 (C5) section, comma separated")
+    ap.add_argument("--prefill-tokens", default="16,64,512",
+                    help="prompt lengths of the Q4_0 prefill section, comma separated")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

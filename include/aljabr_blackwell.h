@@ -213,6 +213,35 @@ int aljabr_blackwell_decode_attention(float* out, const float* q, const void* k_
                                       int kv_dtype, int cache_head_stride, int kv_heads, int q_heads,
                                       int head_dim, int seq_len, int start_pos, float scale);
 
+/* ---- prefill attention (fp32, GQA) ----------------------------------------
+ * GgufPrefillAttentionExecution.execute's Java loop
+ * (engine/gguf/aljabr-gguf-java/.../javabackend/GgufPrefillAttentionExecution.java:44-82):
+ * out, q: host float[tokens][q_heads*head_dim]; k, v: host
+ * float[tokens][kv_stride] with KV head h at h*head_dim.  Token t attends
+ * positions [t - sliding_window + 1, t] (sliding_window > 0) or [0, t]. */
+int aljabr_blackwell_prefill_attention(float* out, const float* q, const float* k, const float* v, int tokens,
+                                       int q_heads, int kv_heads, int head_dim, float scale, int sliding_window,
+                                       int kv_stride);
+/* The FlashAttention-4 seam (aljabr_metal_fa4_attention, backend/metal/
+ * aljabr-backend-metal/.../binding/MetalFlashAttentionBinding.java:221-285;
+ * CPU contract MetalFlashAttentionCpuFallback.java:46-104): output, query:
+ * host float[B][T][H][D]; key, value: host float[B][S][H_kv][D].  Causal
+ * masks keys s > max(0, S - T) + t; soft_cap > 0 applies tanh(x/cap)*cap.
+ * use_bf16 is accepted and ignored: the arithmetic is fp32.  head_dim D a
+ * multiple of 32 up to 256, H a multiple of H_kv with H / H_kv <= 64.
+ * Returns 0 on success. */
+int aljabr_blackwell_fa4_attention(void* output, void* query, void* key, void* value, int B, int T, int S, int H,
+                                   int H_kv, int D, float scale, int is_causal, int use_bf16, float soft_cap);
+/* aljabr_metal_fa4_sdpa_available / _bf16_available: 1 / 0 here. */
+int aljabr_blackwell_fa4_sdpa_available(void);
+int aljabr_blackwell_fa4_bf16_available(void);
+/* Device pointers, stream-ordered: q / out [B][T][q_heads*head_dim], k / v
+ * [B][S][kv_stride] (kv_stride a multiple of 4), all 16-byte aligned; the
+ * causal limit of token t is t + max(0, S - T); window 0 = none. */
+int aljabr_blackwell_prefill_attention_dev(float* out, const float* q, const float* k, const float* v, int B, int T,
+                                           int S, int q_heads, int kv_heads, int head_dim, int kv_stride, float scale,
+                                           int causal, int window, float soft_cap, void* stream);
+
 /* ---- device-pointer, stream-ordered variants ----------------------------- */
 /* y[N] = W x (+ bias); type ALJ_TYPE_*; absmax/group only for NF4. */
 int aljabr_blackwell_matvec_dev(int type, float* y, const float* x, const void* w, const float* absmax,

@@ -92,6 +92,8 @@ def _declare(L):
     L.orc_matvec_nf4.argtypes = [_p, _p, _p, _p, _i, _i, _i, _p, _i]
     L.orc_matvec_f64.argtypes = [_i, _p, _p, _p, _p, _i, _i, _i, _i]
     L.orc_gqa_decode_attention.argtypes = [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _f]
+    L.orc_prefill_attention.argtypes = [_p, _p, _p, _p, _p, _i, _i, _i, _i, _f, _i, _i]
+    L.orc_fa4_attention.argtypes = [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _f, _i, _f]
     L.orc_vec_dot.argtypes = [_p, _p, _i]
     L.orc_vec_dot.restype = _f
     L.orc_rms_norm.argtypes = [_p, _p, _p, _i, _f]
@@ -300,6 +302,32 @@ def gqa_decode_attention(q, k_cache, v_cache, stride: int, kv_heads: int, q_head
     scores = np.empty(max(seq_len - start_pos, 1), dtype=np.float32)
     lib().orc_gqa_decode_attention(_ptr(q), _ptr(out), _ptr(scores), _ptr(k_cache), _ptr(v_cache),
                                    stride, kv_heads, q_heads, head_dim, seq_len, start_pos, scale)
+    return out
+
+
+def prefill_attention(q, k, v, tokens: int, q_heads: int, kv_heads: int, head_dim: int, scale: float,
+                      window: int = 0, kv_stride: int = 0) -> np.ndarray:
+    """GgufPrefillAttentionExecution's Java loop: q [tokens][q_heads*head_dim],
+    k / v [tokens][kv_stride] (kv_stride 0: kv_heads*head_dim); returns
+    [tokens][q_heads*head_dim]."""
+    kv_stride = kv_stride or kv_heads * head_dim
+    q, k, v = _c(q, np.float32), _c(k, np.float32), _c(v, np.float32)
+    out = np.empty(tokens * q_heads * head_dim, dtype=np.float32)
+    scores = np.empty(max(tokens, 1), dtype=np.float32)
+    lib().orc_prefill_attention(_ptr(out), _ptr(q), _ptr(k), _ptr(v), _ptr(scores), tokens, q_heads, kv_heads,
+                                head_dim, scale, window, kv_stride)
+    return out.reshape(tokens, q_heads * head_dim)
+
+
+def fa4_attention(q, k, v, B: int, T: int, S: int, H: int, H_kv: int, D: int, scale: float,
+                  causal: bool = True, soft_cap: float = 0.0) -> np.ndarray:
+    """The FlashAttention-4 seam's CPU contract (MetalFlashAttentionCpuFallback):
+    q [B][T][H][D], k / v [B][S][H_kv][D]; returns [B][T][H][D] flat."""
+    q, k, v = _c(q, np.float32), _c(k, np.float32), _c(v, np.float32)
+    out = np.empty(B * T * H * D, dtype=np.float32)
+    scores = np.empty(max(S, 1), dtype=np.float32)
+    lib().orc_fa4_attention(_ptr(out), _ptr(q), _ptr(k), _ptr(v), _ptr(scores), B, T, S, H, H_kv, D, scale,
+                            1 if causal else 0, soft_cap)
     return out
 
 

@@ -709,6 +709,75 @@ void orc_gqa_decode_attention(const float* q, float* out, float* scores,
     }
 }
 
+void orc_prefill_attention(float* out, const float* q, const float* k, const float* v, float* scores, int tokens,
+                           int q_heads, int kv_heads, int head_dim, float scale, int window, int kv_stride) {
+    for (int t = 0; t < tokens; t++) {                                        /* PA:44-82 */
+        int start = window > 0 ? (t - window + 1 > 0 ? t - window + 1 : 0) : 0;
+        int end = t;
+        int active = end - start + 1;
+        for (int head = 0; head < q_heads; head++) {
+            int kv_head = head / (q_heads / kv_heads);
+            const float* qh = q + (size_t)t * q_heads * head_dim + (size_t)head * head_dim;
+            for (int p = start; p <= end; p++) {
+                const float* kr = k + (size_t)p * kv_stride + (size_t)kv_head * head_dim;
+                float dot = 0.0f;
+                for (int d = 0; d < head_dim; d++) dot += qh[d] * kr[d];
+                scores[p - start] = dot * scale;
+            }
+            orc_softmax(scores, active);
+            float* oh = out + (size_t)t * q_heads * head_dim + (size_t)head * head_dim;
+            for (int d = 0; d < head_dim; d++) oh[d] = 0.0f;
+            for (int p = start; p <= end; p++) {
+                float w = scores[p - start];
+                const float* vr = v + (size_t)p * kv_stride + (size_t)kv_head * head_dim;
+                for (int d = 0; d < head_dim; d++) oh[d] += w * vr[d];
+            }
+        }
+    }
+}
+
+void orc_fa4_attention(float* out, const float* q, const float* k, const float* v, float* scores, int B, int T,
+                       int S, int H, int H_kv, int D, float scale, int causal, float soft_cap) {
+    int group = H / H_kv;                                                     /* FA:46-104 */
+    int off = S - T > 0 ? S - T : 0;
+    for (int b = 0; b < B; b++)
+        for (int h = 0; h < H; h++) {
+            int hk = h / group;
+            for (int t = 0; t < T; t++) {
+                float mx = -INFINITY;
+                const float* qr = q + ((size_t)(b * T * H + t * H + h)) * D;
+                for (int s = 0; s < S; s++) {
+                    if (causal && s > off + t) { scores[s] = -INFINITY; continue; }
+                    const float* kr = k + ((size_t)(b * S * H_kv + s * H_kv + hk)) * D;
+                    float dot = 0.0f;
+                    for (int d = 0; d < D; d++) dot += qr[d] * kr[d];
+                    float score = dot * scale;
+                    if (soft_cap > 0.0f) score = (float)(tanh((double)(score / soft_cap)) * (double)soft_cap);
+                    scores[s] = score;
+                    if (scores[s] > mx) mx = scores[s];
+                }
+                float sum = 0.0f;
+                for (int s = 0; s < S; s++) {
+                    if (!causal || s <= off + t) {
+                        scores[s] = (float)exp((double)(scores[s] - mx));
+                        sum += scores[s];
+                    } else {
+                        scores[s] = 0.0f;
+                    }
+                }
+                if (sum > 0.0f)
+                    for (int s = 0; s < S; s++) scores[s] /= sum;
+                float* orow = out + ((size_t)(b * T * H + t * H + h)) * D;
+                for (int d = 0; d < D; d++) {
+                    float acc = 0.0f;
+                    for (int s = 0; s < S; s++)
+                        acc += scores[s] * v[((size_t)(b * S * H_kv + s * H_kv + hk)) * D + d];
+                    orow[d] = acc;
+                }
+            }
+        }
+}
+
 void orc_rms_norm(const float* x, const float* w, float* out, int len, float eps) {   /* VO:211-234 */
     float acc[VLANES] = {0};
     int i = 0, bound = len - len % VLANES;

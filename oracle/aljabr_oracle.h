@@ -14,6 +14,8 @@
  *   DK  = engine/safetensor/aljabr-safetensor-core/src/main/java/tech/kayys/aljabr/safetensor/core/tensor/DequantizationKernel.java
  *   AT  = engine/gguf/aljabr-gguf-java/src/main/java/tech/kayys/aljabr/gguf/javabackend/GgufDecodeAttentionExecution.java
  *   DP  = engine/gguf/aljabr-gguf-java/src/main/java/tech/kayys/aljabr/gguf/javabackend/GgufDecodePass.java
+ *   PA  = engine/gguf/aljabr-gguf-java/src/main/java/tech/kayys/aljabr/gguf/javabackend/GgufPrefillAttentionExecution.java
+ *   FA  = backend/metal/aljabr-backend-metal/src/main/java/tech/kayys/aljabr/backend/metal/binding/MetalFlashAttentionCpuFallback.java
  *
  * Parity status: the GGUF and attention restatements are pinned by the
  * reference's own known-answer tests (restated as fixtures under
@@ -85,6 +87,22 @@ void orc_gqa_decode_attention(const float* q, float* out, float* scores,
                               const float* k_cache, const float* v_cache, int stride,
                               int kv_heads, int q_heads, int head_dim,
                               int seq_len, int start_pos, float scale);
+
+/* ---- prefill attention --------------------------------------------------- */
+/* PA:44-82: causal (or sliding-window) attention of `tokens` queries
+ * [token][q_heads*head_dim] over the same tokens' keys / values
+ * [position][kv_stride] (head h at (h / (q_heads/kv_heads)) * head_dim),
+ * with VO:302-317 (softmax); sequential fp32 dots and axpys as written
+ * there.  window > 0 limits token t to positions [t - window + 1, t]
+ * (PA:48-51, slidingWindowAttention && slidingWindow > 0).  `scores` holds
+ * `tokens` floats. */
+void orc_prefill_attention(float* out, const float* q, const float* k, const float* v, float* scores, int tokens,
+                           int q_heads, int kv_heads, int head_dim, float scale, int window, int kv_stride);
+/* FA:46-104, the FlashAttention-4 seam's CPU contract: q / out [B][T][H][D],
+ * k / v [B][S][H_kv][D]; causal masks s > max(0, S - T) + t; soft_cap > 0
+ * applies tanh(score / cap) * cap.  `scores` holds S floats. */
+void orc_fa4_attention(float* out, const float* q, const float* k, const float* v, float* scores, int B, int T,
+                       int S, int H, int H_kv, int D, float scale, int causal, float soft_cap);
 
 /* ---- decode-step glue --------------------------------------------------- */
 float orc_vec_dot(const float* a, const float* b, int len);                      /* VO:43-55   */
