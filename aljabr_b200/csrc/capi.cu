@@ -53,17 +53,20 @@ struct Registered {
     void* dev;
 };
 
-// Grow-only device / pinned host staging buffer.
+// Grow-only device staging buffer.
 struct DevBuf {
     void* p = nullptr;
     size_t cap = 0;
+    // Attention scratch: how many leading counter words are known to be zero
+    // on every stream (0 after an allocation or a reported device fault).
+    int zeroed_words = 0;
     cudaError_t ensure(size_t bytes) {
         if (bytes <= cap) return cudaSuccess;
         if (p) cudaFree(p);
         p = nullptr;
         cap = 0;
+        zeroed_words = 0;
         cudaError_t e = cudaMalloc(&p, bytes);
-        if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);   // counters inside scratch start at zero
         if (e == cudaSuccess) cap = bytes;
         return e;
     }
@@ -71,6 +74,7 @@ struct DevBuf {
         if (p) cudaFree(p);
         p = nullptr;
         cap = 0;
+        zeroed_words = 0;
     }
 };
 // Grow-only pinned host staging buffer, mapped into the device's address
@@ -473,11 +477,17 @@ int run_attention(DeviceState* st, float* dout, const float* dq, const void* k, 
     if (p.splits > 1) {
         ALJ_CUDA(scratch->ensure(attention_scratch_floats(q_heads, head_dim, p.splits) * 4));
         attention_bind_scratch(p, static_cast<float*>(scratch->p));
-        // The split merge's arrival counters must start at zero.  Clear them on
-        // the launch stream itself: the stream may be non-blocking (the
-        // library's own) or the caller's, so a memset on any other stream
-        // would not be ordered before the kernel.
-        ALJ_CUDA(cudaMemsetAsync(p.split_counter, 0, static_cast<size_t>(q_heads) * sizeof(unsigned int), stream));
+        // The split merge's arrival counters must start at zero.  Each merge
+        // returns its counter to zero, so after a call the first q_heads words
+        // stay zero -- but a call with fewer heads lays partials over the
+        // words past its own counters.  Clear them when this call needs more
+        // than that (or the buffer is new, or a fault was reported), on the
+        // launch stream itself: the stream may be non-blocking (the library's
+        // own) or the caller's, so a memset on any other stream would not be
+        // ordered before the kernel.
+        if (q_heads > scratch->zeroed_words)
+            ALJ_CUDA(cudaMemsetAsync(p.split_counter, 0, static_cast<size_t>(q_heads) * sizeof(unsigned int), stream));
+        scratch->zeroed_words = q_heads;
     }
     return launch_status(launch_attention(p, stream, false), "decode attention");
 }
@@ -712,6 +722,11 @@ int aljabr_blackwell_device_status(unsigned int* fault_bits) {
     ALJ_CUDA(cudaMemcpyFromSymbol(&v, g_fault_word, sizeof v));
     ALJ_CUDA(cudaMemcpyToSymbol(g_fault_word, &zero, sizeof zero));
     if (fault_bits) *fault_bits = v;
+    if (v) {
+        // a kernel that gave up may have left split-merge counters non-zero
+        std::lock_guard<std::mutex> g(st->mu);
+        st->dscratch.zeroed_words = 0;
+    }
     return v & ALJ_FAULT_TIMEOUT ? ALJ_ERR_TIMEOUT : ALJ_OK;
 }
 

@@ -17,10 +17,15 @@
 //     below fp16's normal range;
 //   * B: x' = x 2^f per token (max |x'| in [2^14, 2^15)), split the same way
 //     into fp16 hi / lo planes by gemm_q_x_prep_kernel;
-//   * three tcgen05.mma per 16-column k-step -- A_hi B_hi, A_hi B_lo,
-//     A_lo B_hi (the A_lo B_lo term is below 2^-22 relative) -- into a TMEM
-//     accumulator (two, alternating, for 16-token tiles, so consecutive
-//     small MMAs do not chain);
+//   * token tiles of up to 64: the hi and lo activation tiles lie back to
+//     back in shared memory, so one B operand of N = 2 MT tokens covers both
+//     and two tcgen05.mma per 16-column k-step (A_hi and A_lo against it) form
+//     all four products, the accumulator's two halves holding the x_hi and
+//     x_lo sums (a small MMA costs about the same issue time whatever its N,
+//     so two wide ones beat three narrow ones);
+//   * 128-token tiles: three tcgen05.mma per k-step -- A_hi B_hi, A_hi B_lo,
+//     A_lo B_hi (the A_lo B_lo term is below 2^-22 relative) -- into one
+//     accumulator of MT columns;
 //   * the accumulator covers one 64-column stage: the epilogue drains it
 //     after every stage into fp32 registers (round-to-nearest adds) and the
 //     next stage starts a fresh one.  The tensor core's fp32 accumulation
@@ -315,6 +320,30 @@ __device__ __forceinline__ void split_pair(uint32_t q, uint32_t dd, uint32_t& hi
 // into the other accumulator than the one before (d1 == d0: one chain), then
 // one commit onto `bar`.  `accum` = 0 starts a fresh accumulator: the first
 // MMA into d0 overwrites it, and the first into d1 too unless d1 is d0.
+// Token tiles <= 64: one stage as 4 k-steps x (A_hi, A_lo) x [x_hi | x_lo]
+// (N = 2 MT) = 8 MMAs into one accumulator, then one commit onto `bar`; the
+// first MMA overwrites the accumulator.
+__device__ __forceinline__ void q_stage_mma_wide(uint32_t d, uint32_t ah, uint64_t b, uint32_t idesc, uint64_t* bar) {
+    const uint32_t al = ah + kACols / 2;
+    asm volatile(
+        "{\n .reg .pred p0, p1;\n"
+        " setp.ne.b32 p0, %0, %0;\n"
+        " setp.eq.b32 p1, %0, %0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %9, %13, p0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%5], %9, %13, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %10, %13, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%6], %10, %13, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%3], %11, %13, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%7], %11, %13, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%4], %12, %13, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%8], %12, %13, p1;\n"
+        " tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%14];\n"
+        "}\n" ::"r"(d),
+        "r"(ah), "r"(ah + 8), "r"(ah + 16), "r"(ah + 24), "r"(al), "r"(al + 8), "r"(al + 16), "r"(al + 24),
+        "l"(b), "l"(b + 2), "l"(b + 4), "l"(b + 6), "r"(idesc), "r"(smem_u32(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ void q_stage_mma(uint32_t d0, uint32_t d1, uint32_t ah, uint64_t bh, uint64_t bl,
                                             uint32_t idesc, uint32_t accum, uint64_t* bar) {
     const uint32_t al = ah + kACols / 2;
@@ -396,7 +425,8 @@ __device__ __forceinline__ void dequant_stage(uint32_t slot, int r, int st, uint
 template <int FMT, int MT, int EW>
 __global__ void __launch_bounds__(32 * (7 + 4 * EW), 1) q_tc_gemm_kernel(const __grid_constant__ QParams p) {
     constexpr int NT = MT / EW;                 // tokens per epilogue thread
-    constexpr int CH = MT <= 16 ? 2 : 1;        // accumulator chains per unit
+    constexpr bool WIDE = MT <= 64;             // one B operand of 2 MT tokens (x hi | x lo)
+    constexpr int CH = WIDE ? 2 : 1;            // accumulator width in MT columns
     constexpr int kEpiWarp0 = 4;
     constexpr int kProdWarp = 4 + 4 * EW;       // codes + scales stream
     constexpr int kXWarp = kProdWarp + 1;       // activation tiles
@@ -405,7 +435,7 @@ __global__ void __launch_bounds__(32 * (7 + 4 * EW), 1) q_tc_gemm_kernel(const _
     constexpr int SB = slot_bytes(FMT);
     constexpr int kXPlane = MT * 128;
     constexpr int kXBytes = 2 * kXPlane;        // hi then lo tile
-    constexpr uint32_t kIdesc = idesc_f16(MT);
+    constexpr uint32_t kIdesc = idesc_f16(WIDE ? 2 * MT : MT);
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -618,8 +648,10 @@ __global__ void __launch_bounds__(32 * (7 + 4 * EW), 1) q_tc_gemm_kernel(const _
                     const uint32_t ah = tmem_base + static_cast<uint32_t>(ac.slot * kACols);
                     const uint32_t xs = smem_u32(x_ring + static_cast<size_t>(xc.slot) * kXBytes);
                     // a fresh accumulator per stage; sdone reports it complete
-                    q_stage_mma(d0, d0 + (CH - 1) * MT, ah, sdesc(xs), sdesc(xs + kXPlane), kIdesc, 0u,
-                                &sdone[sd.slot]);
+                    if constexpr (WIDE)
+                        q_stage_mma_wide(d0, ah, sdesc(xs), kIdesc, &sdone[sd.slot]);
+                    else
+                        q_stage_mma(d0, d0, ah, sdesc(xs), sdesc(xs + kXPlane), kIdesc, 0u, &sdone[sd.slot]);
                     xc.next(SX);
                     ac.next(SA);
                     sd.next(kSDone);
@@ -814,7 +846,7 @@ cudaError_t launch_gemm_q(const GemmQArgs& a, cudaStream_t stream) {
     if (rg.x < 2) return cudaErrorNotSupported;
     p.codes_ring = rg.codes;
     p.x_ring = rg.x;
-    p.dbufs = std::min(kMaxDBufs, (512 - kDCol0) / ((MT <= 16 ? 2 : 1) * MT));
+    p.dbufs = std::min(kMaxDBufs, (512 - kDCol0) / ((MT <= 64 ? 2 : 1) * MT));
 
     const int prep_threads = std::min(kPrepThreads, std::max(128, (a.K / 4 / kPrepVecs + 31) / 32 * 32));
     gemm_q_x_prep_kernel<<<a.M, prep_threads, 0, stream>>>(a.x, a.K, xh, xl, reinterpret_cast<int*>(ws + w.tokexp),

@@ -250,10 +250,13 @@ int aljabr_blackwell_dequantize_dev(int type, float* dst, const void* src, const
                                     long long numel, int group, void* stream);
 /* Decode attention on device pointers.  Its split partials live in one
  * scratch buffer per device that the library allocates on first use and
- * reuses; each call clears the buffer's arrival counters on `stream` before
- * its kernel.  Calls whose kernels may overlap on the GPU (different
- * streams, or several threads) share that buffer and must be ordered by the
- * caller (an event or one stream). */
+ * reuses.  The split merge's arrival counters sit at the head of that
+ * buffer; every merge returns its counter to zero, and a call clears them on
+ * `stream` before its kernel when they may not be zero (a new buffer, more
+ * query heads than the previous call, or a fault reported by
+ * aljabr_blackwell_device_status).  Calls whose kernels may overlap on the
+ * GPU (different streams, or several threads) share that buffer and must be
+ * ordered by the caller (an event or one stream). */
 int aljabr_blackwell_decode_attention_dev(float* out, const float* q, const void* k_cache,
                                           const void* v_cache, int kv_dtype, int cache_head_stride,
                                           int kv_heads, int q_heads, int head_dim, int seq_len,

@@ -134,9 +134,11 @@ def test_bridge_pair_triple_batch(lib):
     d.dispatch_mat_vec_batch(t["k"], xb, yb, 3)
     for b in range(3):
         assert synth.max_rel_err(yb[b], oracle.matvec_q4_0(wk, xb[b], 1024, threads=8)) < TOL
+    # batches of Q4_0 run on the tensor-core GEMM, single rows on the matvec:
+    # the two agree to the tolerance, not bit for bit
     y1 = np.zeros(1024, np.float32)
     d.dispatch_mat_vec(t["k"], xb[1], y1)
-    np.testing.assert_array_equal(y1, yb[1])
+    assert synth.max_rel_err(yb[1], y1) < TOL
     GgufBlackwellBridge.release_model(model)
 
 
