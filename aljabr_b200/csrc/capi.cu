@@ -12,6 +12,7 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <tuple>
 #include <vector>
 
@@ -122,6 +123,9 @@ struct DeviceState {
     DevBuf dx, dy, dtmp, dscratch, dgemm;
     HostBuf hx, hy;
     std::map<PackKey, PackedQ> qpack;       // guarded by mu
+    void* upload_bounce[2] = {nullptr, nullptr};   // pinned, for model uploads (guarded by upload_mu)
+    cudaEvent_t upload_done[2] = {nullptr, nullptr};
+    std::mutex upload_mu;
 };
 
 std::mutex g_mu;
@@ -604,6 +608,73 @@ int run_prefill_host(float* out, const float* q, const float* k, const float* v,
 }
 }  // namespace
 
+namespace {
+// memcpy spread over host threads (the mapped file's pages are read by
+// several cores at once; one core's copy runs well below the PCIe rate).
+void parallel_copy(void* dst, const void* src, size_t n) {
+    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    const size_t nthr = std::min<size_t>(std::min(4u, hw), std::max<size_t>(1, n >> 22));   // >= 4 MB each
+    if (nthr <= 1) {
+        memcpy(dst, src, n);
+        return;
+    }
+    std::vector<std::thread> th;
+    const size_t part = (n / nthr + 4095) & ~size_t(4095);
+    for (size_t t = 0; t < nthr; ++t) {
+        const size_t off = t * part;
+        if (off >= n) break;
+        const size_t len = std::min(part, n - off);
+        th.emplace_back([=] { memcpy(static_cast<uint8_t*>(dst) + off, static_cast<const uint8_t*>(src) + off, len); });
+    }
+    for (auto& x : th) x.join();
+}
+
+// Copies a (mapped, pageable) model file to HBM.  Up to 64 MB: one pageable
+// cudaMemcpy.  Larger: 32 MB chunks through two pinned bounce buffers kept
+// per device (pinning costs ~0.4 ms per MB, paid once), the host copy of a
+// chunk spread over host threads while the DMA of the previous chunk runs on
+// `stream`.  Measured on B200 hosts: pageable copies ~10 GB/s, one host thread
+// into pinned memory ~14 GB/s, pinned DMA ~55 GB/s.
+int upload_model(DeviceState* st, void* dev, const void* src, size_t bytes) {
+    constexpr size_t kSmall = size_t(64) << 20;
+    constexpr size_t kChunk = size_t(32) << 20;
+    if (bytes <= kSmall) {
+        const cudaError_t e = cudaMemcpy(dev, src, bytes, cudaMemcpyHostToDevice);
+        return e == cudaSuccess ? ALJ_OK : fail(ALJ_ERR_CUDA, "model upload: %s", cudaGetErrorString(e));
+    }
+    std::lock_guard<std::mutex> g(st->upload_mu);
+    for (int b = 0; b < 2; ++b) {
+        if (!st->upload_bounce[b] && cudaHostAlloc(&st->upload_bounce[b], kChunk, cudaHostAllocPortable) != cudaSuccess) {
+            st->upload_bounce[b] = nullptr;
+            cudaGetLastError();
+            return fail(ALJ_ERR_NO_MEMORY, "pinned bounce buffers for the model upload (2 x %zu bytes)", kChunk);
+        }
+        if (!st->upload_done[b] && cudaEventCreateWithFlags(&st->upload_done[b], cudaEventDisableTiming) != cudaSuccess) {
+            st->upload_done[b] = nullptr;
+            cudaGetLastError();
+            return fail(ALJ_ERR_CUDA, "model upload: event creation failed");
+        }
+    }
+    int rc = ALJ_OK;
+    size_t i = 0;
+    for (size_t off = 0; off < bytes && rc == ALJ_OK; off += kChunk, ++i) {
+        const int b = static_cast<int>(i & 1);
+        const size_t n = std::min(kChunk, bytes - off);
+        cudaError_t e = i >= 2 ? cudaEventSynchronize(st->upload_done[b]) : cudaSuccess;   // its previous DMA is done
+        if (e == cudaSuccess) {
+            parallel_copy(st->upload_bounce[b], static_cast<const uint8_t*>(src) + off, n);
+            e = cudaMemcpyAsync(static_cast<uint8_t*>(dev) + off, st->upload_bounce[b], n, cudaMemcpyHostToDevice,
+                                st->stream);
+        }
+        if (e == cudaSuccess) e = cudaEventRecord(st->upload_done[b], st->stream);
+        if (e != cudaSuccess) rc = fail(ALJ_ERR_CUDA, "model upload at byte %zu: %s", off, cudaGetErrorString(e));
+    }
+    const cudaError_t e = cudaStreamSynchronize(st->stream);
+    if (rc == ALJ_OK && e != cudaSuccess) rc = fail(ALJ_ERR_CUDA, "model upload: %s", cudaGetErrorString(e));
+    return rc;
+}
+}  // namespace
+
 extern "C" {
 
 int aljabr_blackwell_init(int device_id) {
@@ -743,6 +814,10 @@ int aljabr_blackwell_shutdown(void) {
         s->hx.release(); s->hy.release();
         for (auto& kv : s->qpack) cudaFree(kv.second.p);
         s->qpack.clear();
+        for (int b = 0; b < 2; ++b) {
+            if (s->upload_bounce[b]) cudaFreeHost(s->upload_bounce[b]);
+            if (s->upload_done[b]) cudaEventDestroy(s->upload_done[b]);
+        }
         cudaStreamDestroy(s->stream);
         s.reset();
     }
@@ -770,10 +845,10 @@ int aljabr_blackwell_register_model_buffer(const void* base_ptr, size_t total_by
         cudaGetLastError();
         return fail(ALJ_ERR_NO_MEMORY, "cudaMalloc(%zu) for the model buffer: %s", total_bytes, cudaGetErrorString(e));
     }
-    e = cudaMemcpy(dev, base_ptr, total_bytes, cudaMemcpyHostToDevice);
-    if (e != cudaSuccess) {
+    const int rc = upload_model(st, dev, base_ptr, total_bytes);
+    if (rc != ALJ_OK) {
         cudaFree(dev);
-        return fail(ALJ_ERR_CUDA, "copying the model buffer to HBM: %s", cudaGetErrorString(e));
+        return rc;
     }
     std::lock_guard<std::mutex> g(st->reg_mu);
     st->reg[reinterpret_cast<uintptr_t>(base_ptr)] = Registered{total_bytes, dev};

@@ -646,8 +646,28 @@ def run_extra(args, dev, stream, sh, l2, which=None, reps=200):
             "peaks": {"hbm_GB/s": hbm_peak, "hbm": hbm_kind, "bf16_TFLOP/s": tc_peak, "tensor": tc_kind},
             "tokens": res}
 
+    def upload_section():
+        # register_model_buffer of a 1 GiB host buffer (the reference's mmap'd
+        # model registration): host wall clock, first call in the process (it
+        # pins the bounce buffers) and a repeat.
+        import ctypes
+        import time
+        buf = np.random.default_rng(3).integers(0, 256, size=1 << 30, dtype=np.uint8)
+        times = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            native.call("aljabr_blackwell_register_model_buffer", ctypes.c_void_p(buf.ctypes.data), buf.nbytes)
+            times.append(time.perf_counter() - t0)
+            native.call("aljabr_blackwell_unregister_model_buffer", ctypes.c_void_p(buf.ctypes.data))
+        out["model_upload_1gib"] = {"first_GB/s": round(buf.nbytes / times[0] / 1e9, 1),
+                                    "repeat_GB/s": round(buf.nbytes / min(times[1:]) / 1e9, 1),
+                                    "how": "register_model_buffer: 32 MB chunks via two pinned bounce buffers, "
+                                           "host copies on 4 threads overlapping the DMA"}
+        del buf
+
     for name, fn in (("nf4", nf4_section), ("q8", q8_section), ("attention", attention_section),
-                     ("kquant", kquant_section), ("c5", c5_section), ("prefill", prefill_section)):
+                     ("kquant", kquant_section), ("c5", c5_section), ("prefill", prefill_section),
+                     ("upload", upload_section)):
         if want(name):
             fn()
             torch.cuda.empty_cache()
@@ -884,7 +904,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--no-prefetch", action="store_true", help="no L2 prefetch hints between the headline launches")
-    ap.add_argument("--only", choices=["nf4", "q8", "attention", "decode", "c5", "kquant", "prefill"],
+    ap.add_argument("--only", choices=["nf4", "q8", "attention", "decode", "c5", "kquant", "prefill", "upload"],
                     help="run one secondary workload alone (for profiling); prints its dict")
     ap.add_argument("--decode-tokens", type=int, default=32)
     ap.add_argument("--decode-weights", default="nf4", choices=["nf4", "q4_0", "q4_k_m"],

@@ -2,6 +2,9 @@
 (weights N(0, 0.02), activations N(0, 1)); used by tests and smoke."""
 from __future__ import annotations
 
+import json
+import struct
+
 import numpy as np
 
 import oracle
@@ -61,3 +64,27 @@ def normwise_rel_err(got, ref) -> float:
     got = np.asarray(got, dtype=np.float64)
     ref = np.asarray(ref, dtype=np.float64)
     return float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30))
+
+
+_ST_TAGS = {np.dtype(np.float32): "F32", np.dtype(np.float16): "F16", np.dtype(np.uint8): "U8",
+            np.dtype(np.int8): "I8", np.dtype(np.int32): "I32", np.dtype(np.uint32): "U32",
+            np.dtype(np.int64): "I64", np.dtype(np.float64): "F64"}
+
+
+def write_safetensors(path: str, tensors: dict, align: int = 8) -> None:
+    """Minimal safetensors writer (test fixture): name -> numpy array, or
+    name -> ("BF16", uint16 array).  Header padded with spaces to `align`."""
+    header, blobs, off = {}, [], 0
+    for name, v in tensors.items():
+        tag, arr = v if isinstance(v, tuple) else (_ST_TAGS[np.asarray(v).dtype], v)
+        raw = np.ascontiguousarray(arr).tobytes()
+        header[name] = {"dtype": tag, "shape": list(np.asarray(arr).shape), "data_offsets": [off, off + len(raw)]}
+        blobs.append(raw)
+        off += len(raw)
+    hb = json.dumps(header).encode()
+    hb += b" " * ((-(8 + len(hb))) % align)
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(hb)))
+        f.write(hb)
+        for b in blobs:
+            f.write(b)
