@@ -89,13 +89,15 @@ __device__ __forceinline__ void q4k_pair_scales(const uint4& hd, int j, uint32_t
 template <int R, int RS>
 __global__ void __launch_bounds__(kKWarps * 32, 3) q4k_matvec_kernel(const KRows p) {
     pdl_launch_dependents();
-    pdl_wait();   // x may come from the previous kernel
     constexpr int kSub = R / RS;   // row subsets; warp w always serves subset w % kSub
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row0 = blockIdx.x * R;
     const int nb = p.K / 256;
     const size_t row_bytes = static_cast<size_t>(nb) * 144;
+    // the weights never depend on the previous kernel: their L2 prefetch goes
+    // out before the wait for x
     if (threadIdx.x == 0) prefetch_rows_l2(p.w + row0 * row_bytes, min(R, p.N - row0) * row_bytes);
+    pdl_wait();   // x may come from the previous kernel
     const int bl = lane >> 3, c = lane & 7, j = c >> 1;
     const int sub = warp % kSub;
     const uint8_t* rowp[RS];
@@ -207,13 +209,14 @@ __device__ __forceinline__ uint32_t ld_word_a2(const uint8_t* a, bool odd) {
 template <int RS>
 __global__ void __launch_bounds__(kKWarps * 32, 3) q6k_matvec_kernel(const KRows p) {
     pdl_launch_dependents();
-    pdl_wait();
     constexpr int kSub = kKRows / (2 * RS);   // row subsets; warp w always serves subset w % kSub
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row0 = blockIdx.x * kKRows;
     const int nb = p.K / 256;
     const size_t row_bytes = static_cast<size_t>(nb) * 210;
+    // weights before the wait for x, as in the Q4_K kernel
     if (threadIdx.x == 0) prefetch_rows_l2(p.w + row0 * row_bytes, min(kKRows, p.N - row0) * row_bytes);
+    pdl_wait();
     const int rh = lane >> 4, h = (lane >> 3) & 1, i0 = 4 * (lane & 7), gsh = 8 * (i0 >> 4);
     const int sub = warp % kSub;
     const uint8_t* rowp[RS];
