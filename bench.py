@@ -288,6 +288,11 @@ def run_ours(args, rank, world, local_rank):
             extra["nf4_decode_llama3_8b"] = run_decode(args, rank, world, dev)
         except Exception as e:  # reported, never hidden: the line says what failed
             extra["nf4_decode_llama3_8b"] = {"error": f"{type(e).__name__}: {e}"}
+        if world > 1:   # BASELINE config 5 with the weights sharded over these GPUs
+            try:
+                extra["c5_nf4_70b_layer_tp"] = run_c5_tp(args, rank, world, dev)
+            except Exception as e:
+                extra["c5_nf4_70b_layer_tp"] = {"error": f"{type(e).__name__}: {e}"}
 
     bits = ctypes.c_uint(0)
     native.check(L.aljabr_blackwell_device_status(ctypes.byref(bits)))
@@ -674,6 +679,121 @@ def run_extra(args, dev, stream, sh, l2, which=None, reps=200):
     return out
 
 
+def run_c5_tp(args, rank, world, dev, reps=20):
+    """BASELINE config 5 at TP = world: one Llama-3-70B layer's NF4 weights
+    (block 64) row-sharded over the ranks, each rank's batched NF4 GEMM on
+    its rows (the batch-1 matvec at M = 1), and every projection's outputs
+    all-gathered in rank order (tp_gemm.gather_token_rows: NCCL over NVLink).
+    Device time per layer (CUDA events on the shared stream), max over
+    ranks; weights rotate through a pool larger than 2 x L2 per rank."""
+    import ctypes
+
+    import torch
+
+    from aljabr_b200 import native
+    from aljabr_b200.tp_gemm import gather_token_rows
+
+    L = native.lib()
+    H, FF, G = 8192, 28672, 64
+    full = {"q": (H, H), "k": (1024, H), "v": (1024, H), "o": (H, H), "gate": (FF, H), "up": (FF, H),
+            "down": (H, FF)}
+    shp = {n: (r // world, k) for n, (r, k) in full.items()}
+    nweights = sum(r * k for r, k in full.values())
+    wbytes = sum(n * k // 2 + n * k // G * 4 for n, k in shp.values())
+    props = torch.cuda.get_device_properties(dev)
+    l2 = getattr(props, "L2_cache_size", 126 * 2 ** 20) or 126 * 2 ** 20
+    pool = max(1, int(np.ceil(2.5 * l2 / wbytes)))
+    st = torch.cuda.Stream(device=dev)
+    sh = ctypes.c_void_p(st.cuda_stream)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(50 + rank)
+    raw, packed = [], []
+    for _ in range(pool):
+        lr, lp = {}, {}
+        for name, (n, k) in shp.items():
+            c = torch.randint(0, 256, (n * k // 2,), dtype=torch.uint8, device=dev, generator=gen)
+            a = (0.05 + 0.005 * torch.randn(n * k // G, device=dev, generator=gen)).abs()
+            pk = torch.empty(native.gemm_nf4_packed_size(n, k, G), dtype=torch.uint8, device=dev)
+            torch.cuda.synchronize(dev)
+            native.gemm_nf4_pack(pk.data_ptr(), c.data_ptr(), a.data_ptr(), n, k, G, sh.value)
+            lr[name], lp[name] = (c, a), pk
+        raw.append(lr)
+        packed.append(lp)
+    torch.cuda.synchronize(dev)
+    groups = (("q", "k", "v"), ("o",), ("gate", "up"), ("down",))
+    res = {}
+    for M in [int(v) for v in getattr(args, "c5_tokens", "1,16,64,512").split(",")]:
+        xh = torch.randn(M, H, device=dev).to(torch.bfloat16)
+        xf = torch.randn(M, FF, device=dev).to(torch.bfloat16)
+        ys = {name: torch.empty(M * n, device=dev) for name, (n, _) in shp.items()}
+        wsb = max(native.gemm_nf4_workspace_size(M, H, [shp["q"][0], shp["k"][0], shp["v"][0]]),
+                  native.gemm_nf4_workspace_size(M, H, [shp["gate"][0], shp["up"][0]]),
+                  native.gemm_nf4_workspace_size(M, FF, [shp["down"][0]]))
+        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        xh32, xf32 = xh.float().reshape(-1), xf.float().reshape(-1)
+
+        def layer(i):
+            lay = packed[i % pool]
+            for names in groups:
+                x, k = (xf, FF) if names == ("down",) else (xh, H)
+                if M == 1:
+                    for nm in names:
+                        c, a = raw[i % pool][nm]
+                        native.check(L.aljabr_blackwell_matvec_dev(
+                            native.TYPE_NF4, ys[nm].data_ptr(), (xf32 if k == FF else xh32).data_ptr(), c.data_ptr(),
+                            ctypes.c_void_p(a.data_ptr()), k, shp[nm][0], G, None, sh))
+                else:
+                    native.gemm_nf4_dev([ys[nm].data_ptr() for nm in names], [shp[nm][0] for nm in names],
+                                        [lay[nm].data_ptr() for nm in names], [shp[nm][0] for nm in names],
+                                        x.data_ptr(), M, k, G, ws.data_ptr(), wsb, sh.value)
+                for nm in names:
+                    gather_token_rows(ys[nm].view(M, shp[nm][0]), world)
+
+        with torch.cuda.stream(st):
+            for i in range(3):
+                layer(i)
+        torch.cuda.synchronize(dev)
+        # one CUDA graph of `pool` layers (GEMMs and NCCL gathers), replayed;
+        # eager launches if this torch / NCCL cannot capture the collectives
+        graph, graphed = None, False
+        try:
+            torch.distributed.barrier()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=st):
+                for i in range(pool):
+                    layer(i)
+            graphed = True
+        except Exception:
+            graph = None
+        torch.cuda.synchronize(dev)
+        torch.distributed.barrier()
+        n = max(1, reps // pool) if graphed else reps
+        with torch.cuda.stream(st):
+            if graphed:
+                graph.replay()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(st)
+            for i in range(n):
+                if graphed:
+                    graph.replay()
+                else:
+                    layer(i)
+            e.record(st)
+        torch.cuda.synchronize(dev)
+        layers = n * pool if graphed else n
+        t = torch.tensor([s.elapsed_time(e) / layers], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+        res[f"M{M}"] = {"us_per_layer": round(ms * 1e3, 2), "TFLOP/s_whole_job": round(2.0 * M * nweights / (ms * 1e9), 1),
+                        "weight_GB/s_per_gpu": round(wbytes / (ms * 1e6), 1), "all_gathers_per_layer": 7,
+                        "launch": "CUDA graph" if graphed else "eager (graph capture of the collectives failed)"}
+        del graph   # graphs holding NCCL calls go before the process group does
+        del ys, ws
+        torch.cuda.empty_cache()
+    return {"tp": world, "per_gpu_weight_bytes": wbytes, "pool_layers": pool,
+            "exchange": "torch.distributed.all_gather (NCCL) of every projection's outputs", "tokens": res}
+
+
 def ctypes_ptr(t):
     import ctypes
     return ctypes.c_void_p(t.data_ptr())
@@ -886,6 +1006,10 @@ def run_only(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     if args.only == "decode":
         return {"only": "decode", **run_decode(args, rank, world, dev, tokens_per_run=args.decode_tokens, runs=1)}
+    if args.only == "c5tp":
+        if world < 2:
+            return {"only": "c5tp", "skipped": "needs torchrun with 2 or more ranks"}
+        return {"only": "c5tp", **run_c5_tp(args, rank, world, dev)}
     props = torch.cuda.get_device_properties(local_rank)
     l2 = getattr(props, "L2_cache_size", 126 * 2 ** 20) or 126 * 2 ** 20
     stream = torch.cuda.Stream(device=dev)
@@ -904,7 +1028,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--no-prefetch", action="store_true", help="no L2 prefetch hints between the headline launches")
-    ap.add_argument("--only", choices=["nf4", "q8", "attention", "decode", "c5", "kquant", "prefill", "upload"],
+    ap.add_argument("--only", choices=["nf4", "q8", "attention", "decode", "c5", "kquant", "prefill", "upload",
+                                       "c5tp"],
                     help="run one secondary workload alone (for profiling); prints its dict")
     ap.add_argument("--decode-tokens", type=int, default=32)
     ap.add_argument("--decode-weights", default="nf4", choices=["nf4", "q4_0", "q4_k_m"],

@@ -88,3 +88,44 @@ def test_shard_sizes_cover_every_row():
     np.testing.assert_array_equal(np.concatenate(parts), a)
     with pytest.raises(ValueError):
         a.reshape(7, -1)
+
+
+def _gemm_worker(rank, world, port, result_q):
+    """Batched NF4 linear row-sharded over `world` gloo ranks: each rank's
+    oracle outputs for its row block, joined by tp_gemm.gather_token_rows,
+    equal the unsharded outputs for every token."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from aljabr_b200.decode import shard_rows
+        from aljabr_b200.tp_gemm import gather_token_rows, shard_extent
+        g = np.random.default_rng(9)
+        N, K, G, M = 128, 512, 64, 5
+        w = g.normal(0, 0.02, size=(N, K)).astype(np.float32)
+        x = g.normal(size=(M, K)).astype(np.float32)
+        codes, absmax = oracle.quantize_nf4(w, G)
+        row0, rows = shard_extent(N, world, rank)
+        c_r = shard_rows(codes, N, K, world, rank)
+        a_r = shard_rows(absmax, N, K, world, rank)
+        y_r = np.stack([oracle.matvec_nf4(c_r, a_r, x[m], rows, G) for m in range(M)])
+        y_tp = gather_token_rows(torch.from_numpy(y_r), world).numpy()
+        y_full = np.stack([oracle.matvec_nf4(codes, absmax, x[m], N, G) for m in range(M)])
+        ok = y_tp.shape == (M, N) and np.array_equal(y_tp, y_full) and row0 == rank * (N // world)
+        result_q.put((rank, bool(ok)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_batched_gather_reproduces_unsharded_gloo():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29640 + os.getpid() % 200
+    procs = [ctx.Process(target=_gemm_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    assert res == {0: True, 1: True}
