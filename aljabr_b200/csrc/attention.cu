@@ -226,20 +226,30 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_split_kernel(const AttnP
 //     others; with 5..8 heads two MMAs run per step, [h ; m] and [l ; 0];
 //   * scores: B = 8 cached positions of K straight from shared memory; the
 //     accumulator of a lane holds its head's score for two positions;
-//   * a warp owns every 4th 16-position chunk of the split and keeps all its
-//     scores in registers, so its softmax needs no rescaling; the score
+//   * a warp owns every W-th 16-position chunk of the split and keeps all
+//     its scores in registers; the warps agree on each head's CTA-wide
+//     maximum once, so their partial sums add without rescaling; the score
 //     accumulator layout is the A-operand layout of the next product;
 //   * output: B = V rows through ldmatrix.trans, accumulated over the warp's
 //     chunks in 64 (head_dim 128) registers;
-//   * the warps merge through shared memory into the split's partials; the
-//     last CTA of a kv head (a per-head arrival counter) merges the splits
-//     and writes the output -- no second kernel.
+//   * the warps' sums add in shared memory into the split's partial; then
+//     either the splits of a kv head form one thread-block cluster and merge
+//     over distributed shared memory, or the last CTA of a kv head (a
+//     per-head arrival counter) merges them from global memory -- no second
+//     kernel either way.
 constexpr int kMaxSplits = 256;
 constexpr int kBoxRows = 32;     // positions per TMA box and per staging barrier
 constexpr int kMaxBoxes = 6;     // at most 192 positions per split
 constexpr int kChunkRows = 16;
-constexpr int kMaxWarpChunks = (kMaxBoxes * kBoxRows / kChunkRows + kAttnWarps - 1) / kAttnWarps;
 constexpr int kMmaSmemMax = 2 * kMaxBoxes * kBoxRows * 128 * 2 + 1024;   // K + V at head_dim 128, + alignment
+// The cluster variant: the splits of one kv head form one thread-block
+// cluster (up to 16 CTAs, one SM each) and merge over distributed shared
+// memory -- no partials in global memory, no arrival counter.
+constexpr int kClusterMax = 16;
+constexpr int kClusterBoxes = 13;   // at most 416 positions per split
+constexpr int kClusterWarps = 8;
+constexpr int kPartFloats = 1536;   // pushed partials: [splits][items / splits] float4 + [splits][8] (max, sum)
+constexpr int kClusterSmemMax = 2 * kClusterBoxes * kBoxRows * 128 * 2 + kPartFloats * 4 + 1024;
 
 struct KvMaps {
     CUtensorMap k;      // bf16 cache viewed as [rows][kv_heads][head_dim / 64][64]
@@ -283,6 +293,43 @@ __device__ __forceinline__ unsigned int atom_add_acq_rel_gpu(unsigned int* p, un
     asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
     return old;
 }
+// Distributed shared memory: this CTA's shared address `a` in cluster CTA
+// `rank`, and stores there.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t a, int rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void st_cluster_f2(uint32_t a, float2 v) {
+    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(a), "f"(v.x), "f"(v.y) : "memory");
+}
+__device__ __forceinline__ void st_cluster_f4(uint32_t a, float4 v) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+// The value, held in a register from here on: the compiler otherwise reads
+// kernel parameters again where they are used, and a late read of the
+// parameter bank can miss its cache.
+__device__ __forceinline__ int pin_reg(int v) {
+    asm volatile("" : "+r"(v));
+    return v;
+}
+template <typename T>
+__device__ __forceinline__ T* pin_reg(T* v) {
+    asm volatile("" : "+l"(v));
+    return v;
+}
+// Split cluster barrier without ordering: arrive early, wait before the
+// first access to another CTA's shared memory (all CTAs have started then).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+// Every thread of every CTA of the cluster: stores before it are visible to
+// loads after it anywhere in the cluster (a hardware barrier, no spin).
+__device__ __forceinline__ void cluster_barrier() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 __device__ __forceinline__ uint32_t bf16x2_bits(__nv_bfloat162 v) { return *reinterpret_cast<const uint32_t*>(&v); }
 // Three-part bf16 split of (x0, x1): pairs packed as MMA operands (x0 low).
 struct Split3 {
@@ -295,10 +342,13 @@ __device__ __forceinline__ Split3 split3(float x0, float x1) {
     const __nv_bfloat162 l = __floats2bfloat162_rn(r0 - __low2float(m), r1 - __high2float(m));
     return {bf16x2_bits(h), bf16x2_bits(m), bf16x2_bits(l)};
 }
-// Byte offset of (row, element d) in a staged region [d / 64][cap rows][128 B]
-// written by TMA with the 128-byte swizzle (16-byte unit ^= row % 8).
-__device__ __forceinline__ uint32_t swz(int row, int d, int cap) {
-    return static_cast<uint32_t>(((d >> 6) * cap + row) * 128 + ((((d >> 3) & 7) ^ (row & 7)) << 4));
+// Byte offset of (row, element d) in a staged region of 32-row boxes, each
+// [head-dim half][32 rows][128 B], written by TMA with the 128-byte swizzle
+// (16-byte unit ^= row % 8).
+template <int NH>
+__device__ __forceinline__ uint32_t swz(int row, int d) {
+    return static_cast<uint32_t>((((row >> 5) * NH + (d >> 6)) * 32 + (row & 31)) * 128 +
+                                 ((((d >> 3) & 7) ^ (row & 7)) << 4));
 }
 
 // A operands of one k16 step from the lane's (x0, x1) at k = kq + {0,1} and
@@ -450,28 +500,51 @@ __device__ __forceinline__ void merge_splits(const AttnParams& p, int kvh, int G
     }
 }
 
-template <int D, bool PACK>
-__global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const __grid_constant__ KvMaps maps, const AttnParams p,
-                                                                  const int cap, const int merge_smem) {
-    __shared__ uint64_t s_bar[kMaxBoxes + 1];   // K/V boxes, then the split merge's bulk copy
-    if (threadIdx.x == 0) {   // ahead of the previous kernel's completion
-        prefetch_tensormap(&maps.k);
-        prefetch_tensormap(&maps.v);
-        for (int b = 0; b < kMaxBoxes + 1; ++b) mbar_init(&s_bar[b], 1);
-        fence_mbar_init();
-    }
-    pdl_launch_dependents();
-    pdl_wait();
+// CL: the launch is a grid of clusters (1, splits, 1), one per kv head, and
+// the splits merge over distributed shared memory; otherwise the last CTA of
+// a kv head merges the partials from global memory.
+//
+// Staging: box b (32 positions) of K sits at sk + b * NH * 4096 as
+// [head-dim half][32 rows][128 B] (one copy fetches both halves), V likewise
+// at sv.  Every warp takes the scores of its own 16-row chunks; the CTA-wide
+// running max of each head is agreed once (one barrier), so the warps'
+// probability-weighted V sums and their sums of probabilities simply add.
+template <int D, bool PACK, bool CL>
+__global__ void __launch_bounds__((CL ? kClusterWarps : kAttnWarps) * 32)
+    attn_mma_kernel(const __grid_constant__ KvMaps maps, const AttnParams p, const int cap, const int merge_smem) {
+    constexpr int W = CL ? kClusterWarps : kAttnWarps;
+    constexpr int MB = CL ? kClusterBoxes : kMaxBoxes;
+    constexpr int MWC = (MB * kBoxRows / kChunkRows + W - 1) / W;   // 16-row chunks per warp
     constexpr int NH = D / 64;   // 128-byte halves of a row
     constexpr int KS = D / 16;   // k16 steps of q.k
     constexpr int NT = D / 8;    // n8 tiles of the output
+    constexpr uint32_t kBoxBytes = NH * kBoxRows * 128;
+    static_assert(MB <= 16, "one lane arms each box a warp issues");
+    __shared__ uint64_t s_bar[MB + 1];   // K/V boxes, then the split merge's bulk copy
+    __shared__ float s_wmax[W][8];       // per warp and head: running max (log2 units)
+    __shared__ float s_wl[W][8];         // per warp and head: sum of probabilities
+    __shared__ float s_scale[8];
+    __shared__ unsigned int s_last;
+    if (threadIdx.x == 0) {   // ahead of the previous kernel's completion
+        prefetch_tensormap(&maps.k);
+        prefetch_tensormap(&maps.v);
+        for (int b = 0; b < MB + 1; ++b) mbar_init(&s_bar[b], 1);
+        fence_mbar_init();
+    }
+    if constexpr (CL) cluster_arrive_relaxed();   // this CTA has started (waited on before any remote store)
+    pdl_launch_dependents();
+    pdl_wait();
     const int kvh = blockIdx.x, split = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int G = p.q_heads / p.kv_heads;
+    const int G = pin_reg(p.q_heads / p.kv_heads);
+    const int S = pin_reg(p.splits);
+    float* const out = pin_reg(p.out);
+    float* const part_o = CL ? nullptr : pin_reg(p.part_o);
+    float* const part_ml = CL ? nullptr : pin_reg(p.part_ml);
     const int seq_len = p.dev_pos ? *p.dev_pos + 1 : p.seq_len;
     const int active = seq_len - p.start_pos;
-    const int c0 = p.start_pos + static_cast<int>(static_cast<long long>(active) * split / p.splits);
-    const int c1 = p.start_pos + static_cast<int>(static_cast<long long>(active) * (split + 1) / p.splits);
+    const int c0 = p.start_pos + static_cast<int>(static_cast<long long>(active) * split / S);
+    const int c1 = p.start_pos + static_cast<int>(static_cast<long long>(active) * (split + 1) / S);
     int n = c1 - c0;
     if (n > cap) {   // a device position past the length the launch was sized for
         if (threadIdx.x == 0) record_fault(ALJ_FAULT_BOUNDS);
@@ -479,9 +552,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const __grid_
     }
 
     extern __shared__ unsigned char smem_raw[];
-    __shared__ float s_ml[kAttnWarps * 8 * 2];
-    __shared__ float s_scale[8];
-    __shared__ unsigned int s_last;
     const uint32_t sk = (smem_u32(smem_raw) + 1023u) & ~1023u;
     const uint32_t sv = sk + static_cast<uint32_t>(cap) * D * 2;
     float* const stage_f = reinterpret_cast<float*>(smem_raw + (sk - smem_u32(smem_raw)));
@@ -505,15 +575,21 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const __grid_
             }
         }
     }
+    __syncthreads();   // barrier initialisation visible to every warp
+    // The copies: box b goes out from warp 2 (b mod W/2), whose first chunk
+    // it holds -- lane j arms its j-th box, then lanes j and 16 + j issue
+    // that box's K and V copies.
     const int nboxes = (n + kBoxRows - 1) / kBoxRows;
-    if (threadIdx.x == 0) {
-        for (int b = 0; b < nboxes; ++b) {
-            mbar_arrive_expect_tx(&s_bar[b], 2u * NH * kBoxRows * 128u);
-            for (int h = 0; h < NH; ++h) {
-                const uint32_t off = static_cast<uint32_t>((h * cap + b * kBoxRows) * 128);
-                tma_load_4d(sk + off, &maps.k, 0, h, kvh, c0 + b * kBoxRows, &s_bar[b]);
-                tma_load_4d(sv + off, &maps.v, 0, h, kvh, c0 + b * kBoxRows, &s_bar[b]);
-            }
+    if ((warp & 1) == 0) {
+        const int b = (lane & 15) * (W / 2) + (warp >> 1);
+        if (lane < 16 && b < nboxes) mbar_arrive_expect_tx(&s_bar[b], 2u * kBoxBytes);
+        __syncwarp();
+        if (b < nboxes) {
+            const uint32_t off = static_cast<uint32_t>(b) * kBoxBytes;
+            if (lane < 16)
+                tma_load_4d(sk + off, &maps.k, 0, c0 + b * kBoxRows, 0, kvh, &s_bar[b]);
+            else
+                tma_load_4d(sv + off, &maps.v, 0, c0 + b * kBoxRows, 0, kvh, &s_bar[b]);
         }
     }
     uint32_t qa[KS][4], qb[PACK ? 1 : KS][4];
@@ -523,16 +599,15 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const __grid_
         for (int s = 0; s < KS; ++s)
             a_operands<PACK>(qv[s][0] * qs, qv[s][1] * qs, qv[s][2] * qs, qv[s][3] * qs, role, qa[s], qb[PACK ? 0 : s]);
     }
-    __syncthreads();   // barrier initialisation visible to every waiter
 
     // scores (log2 units) of this warp's chunks: sc[ci][t][j] is position
-    // 16c + 8t + kq + j of chunk c = warp + 4 ci, for the lane's head
+    // 16c + 8t + kq + j of chunk c = warp + W ci, for the lane's head
     const int nchunks = (n + kChunkRows - 1) / kChunkRows;
-    float sc[kMaxWarpChunks][2][2];
+    float sc[MWC][2][2];
     float mx = -INFINITY;
 #pragma unroll
-    for (int ci = 0; ci < kMaxWarpChunks; ++ci) {
-        const int c = warp + ci * kAttnWarps;
+    for (int ci = 0; ci < MWC; ++ci) {
+        const int c = warp + ci * W;
         sc[ci][0][0] = sc[ci][0][1] = sc[ci][1][0] = sc[ci][1][1] = -INFINITY;
         if (c >= nchunks) continue;
         mbar_wait(&s_bar[c >> 1], 0);   // a timeout is recorded in the fault word
@@ -543,7 +618,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const __grid_
 #pragma unroll
             for (int s2 = 0; s2 < KS / 2; ++s2) {
                 uint32_t kb[4];
-                ldsm_x4(sk + swz(row, 32 * s2 + 8 * (lane >> 3), cap), kb);
+                ldsm_x4(sk + swz<NH>(row, 32 * s2 + 8 * (lane >> 3)), kb);
                 mma_bf16(acc[t], qa[2 * s2], kb[0], kb[1]);
                 mma_bf16(acc[t], qa[2 * s2 + 1], kb[2], kb[3]);
                 if (!PACK) {
@@ -565,12 +640,18 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const __grid_
     }
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    if (role == 0 && (lane & 3) == 0) s_wmax[warp][r] = mx;
+    __syncthreads();
+    // the CTA-wide max of the lane's head
+    mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < W; ++w) mx = fmaxf(mx, s_wmax[w][head]);
 
     // probabilities as A operands, split like the query
-    uint32_t pa[kMaxWarpChunks][4], pb[PACK ? 1 : kMaxWarpChunks][4];
+    uint32_t pa[MWC][4], pb[PACK ? 1 : MWC][4];
     float l = 0.0f;
 #pragma unroll
-    for (int ci = 0; ci < kMaxWarpChunks; ++ci) {
+    for (int ci = 0; ci < MWC; ++ci) {
         float e[2][2];
 #pragma unroll
         for (int t = 0; t < 2; ++t)
@@ -588,8 +669,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const __grid_
 #pragma unroll
     for (int i = 0; i < NT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
 #pragma unroll
-    for (int ci = 0; ci < kMaxWarpChunks; ++ci) {
-        const int c = warp + ci * kAttnWarps;
+    for (int ci = 0; ci < MWC; ++ci) {
+        const int c = warp + ci * W;
         if (c >= nchunks) break;
         if (c == nchunks - 1 && (n & (kChunkRows - 1))) {
             // rows past the split hold other positions (or unwritten cache):
@@ -597,9 +678,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const __grid_
             const int nz = kChunkRows * nchunks - n;
             for (int i = lane; i < nz * NH * 8; i += 32) {
                 const int row = n + i / (NH * 8), h = (i / 8) % NH, u = i & 7;
-                asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(sv + static_cast<uint32_t>((h * cap + row) * 128 + u * 16)),
-                             "r"(0u)
-                             : "memory");
+                const uint32_t a = sv + static_cast<uint32_t>((((row >> 5) * NH + h) * kBoxRows + (row & 31)) * 128 + u * 16);
+                asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0u) : "memory");
             }
             __syncwarp();
         }
@@ -607,7 +687,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const __grid_
 #pragma unroll
         for (int u = 0; u < NT / 2; ++u) {
             uint32_t vb[4];
-            ldsm_x4_trans(sv + swz(row, 16 * u + (lane >> 4) * 8, cap), vb);
+            ldsm_x4_trans(sv + swz<NH>(row, 16 * u + (lane >> 4) * 8), vb);
             mma_bf16(o[2 * u], pa[ci], vb[0], vb[1]);
             mma_bf16(o[2 * u + 1], pa[ci], vb[2], vb[3]);
             if (!PACK) {
@@ -617,8 +697,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const __grid_
         }
     }
 
-    // per-warp state to shared memory (the output part reuses the staging
-    // buffer once every warp is done reading it), then the CTA merge
+    // per-warp sums to shared memory (the output part reuses the staging
+    // buffer once every warp is done reading it), then their CTA sum
     __syncthreads();
 #pragma unroll
     for (int i = 0; i < NT; ++i)
@@ -628,30 +708,108 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const __grid_
             if (PACK) o[i][j] += __shfl_sync(0xffffffffu, o[i][j], partner & 31);
         }
     if (role == 0) {
-        if ((lane & 3) == 0) {
-            s_ml[(warp * 8 + r) * 2] = mx == -INFINITY ? -INFINITY : mx * (1.0f / kLog2e);
-            s_ml[(warp * 8 + r) * 2 + 1] = l;
-        }
+        if ((lane & 3) == 0) s_wl[warp][r] = l;
 #pragma unroll
-        for (int i = 0; i < NT; ++i) {
-            stage_f[(warp * 8 + r) * D + 8 * i + kq] = o[i][0];
-            stage_f[(warp * 8 + r) * D + 8 * i + kq + 1] = o[i][1];
-        }
+        for (int i = 0; i < NT; ++i)
+            *reinterpret_cast<float2*>(stage_f + (warp * 8 + r) * D + 8 * i + kq) = make_float2(o[i][0], o[i][1]);
     }
     __syncthreads();
-    merge_warps_store<D>(p, s_ml, stage_f, 8, G, kvh, split);
-    if (p.splits == 1) return;
+    const int items = G * D / 4;
+    if constexpr (CL) {
+        // Push: each item (head, 4 outputs) of this split goes to the shared
+        // memory of the CTA that owns it (a 1 / splits share of the kv
+        // head's items, in rank order), the (max, sum) of every head to every
+        // CTA; one cluster barrier later each CTA merges its items locally.
+        const int ipo = (items + S - 1) / S;   // items per owner
+        float4* const recv = reinterpret_cast<float4*>(stage_f + max(cap * D, W * 8 * D));   // [S][ipo]
+        float2* const recv_ml = reinterpret_cast<float2*>(recv + S * ipo);                     // [S][8]
+        cluster_wait();   // every CTA of the cluster has started
+        for (int it = threadIdx.x; it < items; it += blockDim.x) {
+            const int g = it / (D / 4), d = (it - g * (D / 4)) * 4;
+            float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+            for (int w = 0; w < W; ++w) {
+                const float4 x = *reinterpret_cast<const float4*>(stage_f + (w * 8 + g) * D + d);
+                acc.x += x.x;
+                acc.y += x.y;
+                acc.z += x.z;
+                acc.w += x.w;
+            }
+            const int owner = it / ipo;
+            st_cluster_f4(cluster_map(smem_u32(recv + split * ipo + (it - owner * ipo)), owner), acc);
+        }
+        if (static_cast<int>(threadIdx.x) < S * G) {
+            const int g = threadIdx.x % G, dst = threadIdx.x / G;
+            float M = -INFINITY, L = 0.0f;
+#pragma unroll
+            for (int w = 0; w < W; ++w) {
+                M = fmaxf(M, s_wmax[w][g]);
+                L += s_wl[w][g];
+            }
+            st_cluster_f2(cluster_map(smem_u32(recv_ml + split * 8 + g), dst), make_float2(M, L));
+        }
+        cluster_barrier();   // release / acquire: every pushed partial visible to its owner
+        const int it = split * ipo + static_cast<int>(threadIdx.x);
+        if (static_cast<int>(threadIdx.x) < ipo && it < items) {
+            const int g = it / (D / 4), d = (it - g * (D / 4)) * 4;
+            float Mx = -INFINITY;
+            for (int j = 0; j < S; ++j) Mx = fmaxf(Mx, recv_ml[j * 8 + g].x);
+            float L = 0.0f;
+            float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            for (int j = 0; j < S; ++j) {
+                const float2 ml = recv_ml[j * 8 + g];
+                const float w = ml.x == -INFINITY ? 0.0f : exp2f(ml.x - Mx);
+                const float4 x = recv[j * ipo + threadIdx.x];
+                L = fmaf(ml.y, w, L);
+                acc.x = fmaf(x.x, w, acc.x);
+                acc.y = fmaf(x.y, w, acc.y);
+                acc.z = fmaf(x.z, w, acc.z);
+                acc.w = fmaf(x.w, w, acc.w);
+            }
+            const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+            *reinterpret_cast<float4*>(out + (kvh * G + g) * D + d) =
+                make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        }
+    } else {
+        for (int it = threadIdx.x; it < items; it += blockDim.x) {
+            const int g = it / (D / 4), d = (it - g * (D / 4)) * 4;
+            float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            float M = -INFINITY, L = 0.0f;
+#pragma unroll
+            for (int w = 0; w < W; ++w) {
+                const float4 x = *reinterpret_cast<const float4*>(stage_f + (w * 8 + g) * D + d);
+                acc.x += x.x;
+                acc.y += x.y;
+                acc.z += x.z;
+                acc.w += x.w;
+                M = fmaxf(M, s_wmax[w][g]);
+                L += s_wl[w][g];
+            }
+            const int qh = kvh * G + g;
+            if (S == 1) {
+                const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+                *reinterpret_cast<float4*>(out + qh * D + d) =
+                    make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+            } else {
+                *reinterpret_cast<float4*>(part_o + (static_cast<long long>(qh) * S + split) * D + d) = acc;
+                if (d == 0)   // natural-log units for the merge
+                    *reinterpret_cast<float2*>(part_ml + (static_cast<long long>(qh) * S + split) * 2) =
+                        make_float2(M == -INFINITY ? -INFINITY : M * (1.0f / kLog2e), L);
+            }
+        }
+        if (S == 1) return;
 
-    // the last CTA of this kv head to finish merges the splits: the CTA
-    // barrier orders every thread's partial stores before thread 0's
-    // acquire-release arrival (release is cumulative), and the winner's
-    // acquire orders the other CTAs' partials before its reads
-    __syncthreads();
-    if (threadIdx.x == 0) s_last = atom_add_acq_rel_gpu(&p.split_counter[kvh], 1u) == static_cast<unsigned int>(p.splits - 1);
-    __syncthreads();
-    if (!s_last) return;
-    merge_splits<D>(p, kvh, G, merge_smem != 0, stage_f, s_scale, &s_bar[kMaxBoxes]);
-    if (threadIdx.x == 0) p.split_counter[kvh] = 0u;
+        // the last CTA of this kv head to finish merges the splits: the CTA
+        // barrier orders every thread's partial stores before thread 0's
+        // acquire-release arrival (release is cumulative), and the winner's
+        // acquire orders the other CTAs' partials before its reads
+        __syncthreads();
+        if (threadIdx.x == 0) s_last = atom_add_acq_rel_gpu(&p.split_counter[kvh], 1u) == static_cast<unsigned int>(S - 1);
+        __syncthreads();
+        if (!s_last) return;
+        merge_splits<D>(p, kvh, G, merge_smem != 0, stage_f, s_scale, &s_bar[MB]);
+        if (threadIdx.x == 0) p.split_counter[kvh] = 0u;
+    }
 }
 
 // Merge the splits of one query head: the per-split (max, sum) pairs are
@@ -808,7 +966,7 @@ size_t merge_bytes(const AttnParams& p) {
 
 // Tensor maps and staging rows for the tensor-core kernel; false when the
 // cache type, shape or layout is outside it (the shuffle kernel runs then).
-bool mma_params(const AttnParams& p, AttnMmaParams& mp) {
+bool mma_params(const AttnParams& p, AttnMmaParams& mp, int max_boxes = kMaxBoxes) {
     if (p.kv_dtype != ALJ_KV_BF16 || !(p.head_dim == 64 || p.head_dim == 128)) return false;
     if (p.kv_heads <= 0 || p.q_heads % p.kv_heads || p.q_heads / p.kv_heads > 8) return false;
     const uintptr_t mis = reinterpret_cast<uintptr_t>(p.k) | reinterpret_cast<uintptr_t>(p.v);
@@ -816,17 +974,19 @@ bool mma_params(const AttnParams& p, AttnMmaParams& mp) {
     const int active = p.seq_len - p.start_pos;
     const int rows = (active + p.splits - 1) / p.splits;
     const int cap = (rows + kBoxRows - 1) / kBoxRows * kBoxRows;
-    if (cap > kMaxBoxes * kBoxRows) return false;
+    if (cap > max_boxes * kBoxRows) return false;
     if (p.splits > 1 && (!p.split_counter || reinterpret_cast<uintptr_t>(p.part_o) % 16 ||
                          reinterpret_cast<uintptr_t>(p.part_ml) % 8 || p.splits > kMaxSplits))
         return false;
     auto fn = tensor_map_encoder();
     if (!fn) return false;
-    const cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(p.head_dim / 64), static_cast<cuuint64_t>(p.kv_heads),
-                                static_cast<cuuint64_t>(p.seq_len)};
-    const cuuint64_t strides[3] = {128, static_cast<cuuint64_t>(p.head_stride) * 2,
-                                   static_cast<cuuint64_t>(p.stride) * 2};
-    const cuuint32_t box[4] = {64, 1, 1, kBoxRows};
+    // [64 elements][positions][head-dim halves][kv heads]: one box is both
+    // halves of 32 positions of one kv head, staged half-major
+    const cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(p.seq_len), static_cast<cuuint64_t>(p.head_dim / 64),
+                                static_cast<cuuint64_t>(p.kv_heads)};
+    const cuuint64_t strides[3] = {static_cast<cuuint64_t>(p.stride) * 2, 128,
+                                   static_cast<cuuint64_t>(p.head_stride) * 2};
+    const cuuint32_t box[4] = {64, kBoxRows, static_cast<cuuint32_t>(p.head_dim / 64), 1};
     const cuuint32_t es[4] = {1, 1, 1, 1};
     for (int t = 0; t < 2; ++t)
         if (fn(t == 0 ? &mp.maps.k : &mp.maps.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(t == 0 ? p.k : p.v),
@@ -845,14 +1005,14 @@ cudaError_t launch_mma(const AttnMmaParams& mp, dim3 grid, cudaStream_t stream, 
     int dev = 0;
     cudaGetDevice(&dev);
     if (!configured[dev & 63]) {
-        cudaError_t e =
-            cudaFuncSetAttribute(attn_mma_kernel<D, PACK>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaSmemMax);
+        cudaError_t e = cudaFuncSetAttribute(attn_mma_kernel<D, PACK, false>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaSmemMax);
         if (e != cudaSuccess) return e;
         configured[dev & 63] = true;
     }
     const size_t stage = 2ull * mp.cap_rows * D * 2;
     const size_t smem = (mp.merge_smem ? std::max(stage, merge_bytes(mp.a)) : stage) + 1024;
-    return launch_pdl(attn_mma_kernel<D, PACK>, grid, dim3(kAttnWarps * 32), smem, stream, pdl, mp.maps, mp.a,
+    return launch_pdl(attn_mma_kernel<D, PACK, false>, grid, dim3(kAttnWarps * 32), smem, stream, pdl, mp.maps, mp.a,
                       mp.cap_rows, mp.merge_smem);
 }
 
@@ -861,6 +1021,103 @@ cudaError_t dispatch_mma(const AttnMmaParams& mp, dim3 grid, cudaStream_t stream
     if (mp.a.head_dim == 64)
         return pack ? launch_mma<64, true>(mp, grid, stream, pdl) : launch_mma<64, false>(mp, grid, stream, pdl);
     return pack ? launch_mma<128, true>(mp, grid, stream, pdl) : launch_mma<128, false>(mp, grid, stream, pdl);
+}
+
+// Dynamic shared memory of the cluster variant: K + V staging (the per-warp
+// state reuses it), one CTA's partials, alignment.
+size_t cluster_smem(int cap, int D) {
+    return static_cast<size_t>(std::max(cap * D, kClusterWarps * 8 * D) + kPartFloats) * 4 + 1024;
+}
+
+// Clusters of `splits` CTAs the device holds at once with the largest
+// staging (0 when it cannot run the cluster variant); asked once per device
+// and split count.
+template <int D, bool PACK>
+int cluster_capacity(int splits) {
+    static int known[64][kClusterMax + 1];
+    static bool asked[64][kClusterMax + 1];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    dev &= 63;
+    if (asked[dev][splits]) return known[dev][splits];
+    asked[dev][splits] = true;
+    auto kern = attn_mma_kernel<D, PACK, true>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kClusterSmemMax) != cudaSuccess ||
+        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, splits);
+    cfg.blockDim = dim3(kClusterWarps * 32);
+    cfg.dynamicSmemBytes = cluster_smem(kClusterBoxes * kBoxRows, D);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = splits;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+    }
+    known[dev][splits] = n;
+    return n;
+}
+
+template <int D, bool PACK>
+cudaError_t launch_mma_cluster(const AttnMmaParams& mp, cudaStream_t stream, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(mp.a.kv_heads, mp.a.splits);
+    cfg.blockDim = dim3(kClusterWarps * 32);
+    cfg.dynamicSmemBytes = cluster_smem(mp.cap_rows, D);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = mp.a.splits;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, attn_mma_kernel<D, PACK, true>, mp.maps, mp.a, mp.cap_rows, 0);
+}
+
+// The cluster variant when it applies: single-rank output, a tensor-core
+// shape, a split count (<= 16, >= 64 positions a split where the cache
+// allows) whose clusters the device holds all at once, one per kv head, with
+// every split within the staging -- and either enough CTAs to cover a good
+// part of the SMs or no fewer splits than the global-merge launch would
+// take.  Returns false (nothing launched) otherwise.
+bool try_cluster(const AttnParams& p, cudaStream_t stream, bool pdl, cudaError_t* err) {
+    if (p.tpl.tp > 1 || p.kv_dtype != ALJ_KV_BF16 || !(p.head_dim == 64 || p.head_dim == 128)) return false;
+    if (p.kv_heads <= 0 || p.q_heads % p.kv_heads || p.q_heads / p.kv_heads > 8) return false;
+    const int active = p.seq_len - p.start_pos;
+    const bool pack = p.q_heads / p.kv_heads <= 4;
+    int S = 0;
+    for (int s = std::min(kClusterMax, std::max(2, (active + 63) / 64)); s >= 2; --s) {
+        if ((active + s - 1) / s > kClusterBoxes * kBoxRows) break;   // fewer splits are only longer
+        const int have = p.head_dim == 64 ? (pack ? cluster_capacity<64, true>(s) : cluster_capacity<64, false>(s))
+                                          : (pack ? cluster_capacity<128, true>(s) : cluster_capacity<128, false>(s));
+        if (have >= p.kv_heads) {
+            S = s;
+            break;
+        }
+    }
+    if (S == 0 || (p.kv_heads * S < 64 && S < p.splits)) return false;
+    AttnParams q = p;
+    q.splits = S;
+    AttnMmaParams mp{};
+    if (!mma_params(q, mp, kClusterBoxes)) return false;
+    mp.merge_smem = 0;
+    if (q.head_dim == 64)
+        *err = pack ? launch_mma_cluster<64, true>(mp, stream, pdl) : launch_mma_cluster<64, false>(mp, stream, pdl);
+    else
+        *err = pack ? launch_mma_cluster<128, true>(mp, stream, pdl) : launch_mma_cluster<128, false>(mp, stream, pdl);
+    return true;
 }
 
 bool fast_path(const AttnParams& p) {
@@ -939,6 +1196,8 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl)
     if (p.tpl.tp > 1 && (p.splits < 2 || p.tpl.tp > kMaxTp || !p.tpl.counter || !p.tpl.seq || !split_path))
         return cudaErrorInvalidValue;
     if (split_path) {
+        cudaError_t ce = cudaSuccess;
+        if (tc && try_cluster(p, stream, pdl, &ce)) return ce;
         dim3 grid(p.kv_heads, p.splits);
         if (tc) return dispatch_mma(mp, grid, stream, pdl);   // merges its splits itself
         cudaError_t e = p.kv_dtype == ALJ_KV_BF16 ? dispatch_e<ALJ_KV_BF16>(p, grid, stream, pdl)

@@ -493,7 +493,10 @@ int run_attention(DeviceState* st, float* dout, const float* dq, const void* k, 
             ALJ_CUDA(cudaMemsetAsync(p.split_counter, 0, static_cast<size_t>(q_heads) * sizeof(unsigned int), stream));
         scratch->zeroed_words = q_heads;
     }
-    return launch_status(launch_attention(p, stream, false), "decode attention");
+    // Programmatic dependent launch: the kernel reads q, the cache and its
+    // scratch only after the previous kernel on the stream has completed, so
+    // only its launch and set-up overlap that kernel's tail.
+    return launch_status(launch_attention(p, stream, true), "decode attention");
 }
 
 // The binding's elementwise glue (rmsnorm, silu_ffn): operands that are

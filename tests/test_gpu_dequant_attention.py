@@ -105,7 +105,10 @@ def test_gqa_decode_attention_parity(lib, kv_dtype, Hq, Hkv, D, ctx, start):
 
 
 @pytest.mark.parametrize("kv_dtype,Hq,Hkv,D,ctx,start,pad", [
-    (1, 32, 8, 128, 32768, 0, 0),   # long cache: 171 splits of <= 192 rows on the tensor-core kernel
+    (1, 32, 8, 128, 32768, 0, 0),   # long cache: 171 splits of <= 192 rows, merged through global memory
+    (1, 16, 2, 128, 4096, 0, 0),    # 2 kv heads: 64 splits merged through global memory
+    (1, 32, 8, 128, 4096, 0, 0),    # one cluster per kv head, merged over distributed shared memory
+    (1, 32, 8, 128, 4090, 0, 0),    # clusters with a partial last box
     (1, 32, 8, 128, 130, 0, 0),     # two splits of 65 rows: partial TMA box and partial 16-row chunk
     (1, 24, 8, 128, 999, 7, 0),     # 3 query heads per kv head, ragged start
     (1, 64, 8, 64, 2049, 0, 0),     # 8 query heads per kv head, head_dim 64
