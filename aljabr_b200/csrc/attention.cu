@@ -519,6 +519,7 @@ __global__ void __launch_bounds__((CL ? kClusterWarps : kAttnWarps) * 32)
     constexpr int KS = D / 16;   // k16 steps of q.k
     constexpr int NT = D / 8;    // n8 tiles of the output
     constexpr uint32_t kBoxBytes = NH * kBoxRows * 128;
+    constexpr int kOStride = D + 8;   // per-warp sum rows, padded so that 4 head rows of a store hit distinct banks
     static_assert(MB <= 16, "one lane arms each box a warp issues");
     __shared__ uint64_t s_bar[MB + 1];   // K/V boxes, then the split merge's bulk copy
     __shared__ float s_wmax[W][8];       // per warp and head: running max (log2 units)
@@ -711,7 +712,7 @@ __global__ void __launch_bounds__((CL ? kClusterWarps : kAttnWarps) * 32)
         if ((lane & 3) == 0) s_wl[warp][r] = l;
 #pragma unroll
         for (int i = 0; i < NT; ++i)
-            *reinterpret_cast<float2*>(stage_f + (warp * 8 + r) * D + 8 * i + kq) = make_float2(o[i][0], o[i][1]);
+            *reinterpret_cast<float2*>(stage_f + (warp * 8 + r) * kOStride + 8 * i + kq) = make_float2(o[i][0], o[i][1]);
     }
     __syncthreads();
     const int items = G * D / 4;
@@ -721,7 +722,7 @@ __global__ void __launch_bounds__((CL ? kClusterWarps : kAttnWarps) * 32)
         // head's items, in rank order), the (max, sum) of every head to every
         // CTA; one cluster barrier later each CTA merges its items locally.
         const int ipo = (items + S - 1) / S;   // items per owner
-        float4* const recv = reinterpret_cast<float4*>(stage_f + max(cap * D, W * 8 * D));   // [S][ipo]
+        float4* const recv = reinterpret_cast<float4*>(stage_f + max(cap * D, W * 8 * kOStride));   // [S][ipo]
         float2* const recv_ml = reinterpret_cast<float2*>(recv + S * ipo);                     // [S][8]
         cluster_wait();   // every CTA of the cluster has started
         for (int it = threadIdx.x; it < items; it += blockDim.x) {
@@ -729,7 +730,7 @@ __global__ void __launch_bounds__((CL ? kClusterWarps : kAttnWarps) * 32)
             float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
             for (int w = 0; w < W; ++w) {
-                const float4 x = *reinterpret_cast<const float4*>(stage_f + (w * 8 + g) * D + d);
+                const float4 x = *reinterpret_cast<const float4*>(stage_f + (w * 8 + g) * kOStride + d);
                 acc.x += x.x;
                 acc.y += x.y;
                 acc.z += x.z;
@@ -777,7 +778,7 @@ __global__ void __launch_bounds__((CL ? kClusterWarps : kAttnWarps) * 32)
             float M = -INFINITY, L = 0.0f;
 #pragma unroll
             for (int w = 0; w < W; ++w) {
-                const float4 x = *reinterpret_cast<const float4*>(stage_f + (w * 8 + g) * D + d);
+                const float4 x = *reinterpret_cast<const float4*>(stage_f + (w * 8 + g) * kOStride + d);
                 acc.x += x.x;
                 acc.y += x.y;
                 acc.z += x.z;
@@ -1011,7 +1012,8 @@ cudaError_t launch_mma(const AttnMmaParams& mp, dim3 grid, cudaStream_t stream, 
         configured[dev & 63] = true;
     }
     const size_t stage = 2ull * mp.cap_rows * D * 2;
-    const size_t smem = (mp.merge_smem ? std::max(stage, merge_bytes(mp.a)) : stage) + 1024;
+    const size_t sums = static_cast<size_t>(kAttnWarps) * 8 * (D + 8) * 4;   // the per-warp sums reuse the staging
+    const size_t smem = std::max(mp.merge_smem ? std::max(stage, merge_bytes(mp.a)) : stage, sums) + 1024;
     return launch_pdl(attn_mma_kernel<D, PACK, false>, grid, dim3(kAttnWarps * 32), smem, stream, pdl, mp.maps, mp.a,
                       mp.cap_rows, mp.merge_smem);
 }
@@ -1026,7 +1028,7 @@ cudaError_t dispatch_mma(const AttnMmaParams& mp, dim3 grid, cudaStream_t stream
 // Dynamic shared memory of the cluster variant: K + V staging (the per-warp
 // state reuses it), one CTA's partials, alignment.
 size_t cluster_smem(int cap, int D) {
-    return static_cast<size_t>(std::max(cap * D, kClusterWarps * 8 * D) + kPartFloats) * 4 + 1024;
+    return static_cast<size_t>(std::max(cap * D, kClusterWarps * 8 * (D + 8)) + kPartFloats) * 4 + 1024;
 }
 
 // Clusters of `splits` CTAs the device holds at once with the largest
