@@ -718,6 +718,10 @@ bool matvec_tma_supported(int fmt, int K, int group) {
 
 cudaError_t launch_matvec(int fmt, const MatvecParams& p, cudaStream_t stream, bool pdl) {
     if (p.total_rows <= 0) return cudaSuccess;
+    if (fmt == FMT_Q4_K && matvec_imma_supported(fmt, p.K)) {   // K a multiple of 2048: integer tensor cores
+        const cudaError_t e = launch_matvec_imma(fmt, p, stream, pdl);
+        if (e != cudaErrorNotSupported) return e;
+    }
     if (fmt == FMT_Q4_K || fmt == FMT_Q6_K) return launch_matvec_k(fmt, p, stream, pdl);
     if (p.norm_defer || p.in_parts)   // only the NF4 table kernel splits the RMSNorm across launches
         return fmt == FMT_NF4 && matvec_lut_supported(fmt, p.K, p.group) ? launch_matvec_lut(fmt, p, stream, pdl)

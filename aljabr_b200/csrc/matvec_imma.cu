@@ -1,4 +1,4 @@
-// Batch-1 GGUF Q4_0 and Q8_0 dequantise-and-matvec (y = W x) on the integer
+// Batch-1 GGUF Q4_0, Q8_0 and Q4_K dequantise-and-matvec (y = W x) on the integer
 // tensor-core path of B200 (sm_100a): mma.sync.m16n8k32 with s8 operands and
 // s32 accumulation, for K a multiple of 2048.
 //
@@ -10,6 +10,10 @@
 //     decode).  A Q4_0 code word gives its eight codes in two LOP3s (plus one
 //     shift): (w & 0xF0F0F0F0) ^ 0x80808080 is the four high nibbles as the
 //     s8 values 16 (c - 8), and the same on w << 4 gives the low nibbles.
+//     Q4_K (GgufQ4RawDot.dotRowQ4K): a 32-byte run of a super-block holds
+//     sub-block 2j in its low and 2j + 1 in its high nibbles; quad lanes 0-1
+//     take the low, 2-3 the high nibbles of the same bytes, unsigned, and
+//     each row adds d scale 2^-F (digits) - dmin min sum(x) per sub-block.
 //   * B operand = x, split exactly into three balanced int8 digits per
 //     32-element block: X = rint(x 2^F) with F chosen from the block's max
 //     |x| so that |X| <= 2^22, X = h 2^16 + m 2^8 + l, l, m in [-128, 127],
@@ -77,18 +81,31 @@ template <>
 struct IFmt<FMT_Q4_0> {
     static constexpr int kPairBytes = 36;    // two 18-byte blocks
     static constexpr int kChunkPairs = 32;   // 2048 columns
+    static constexpr int kChunkBytes = 1152;
     static constexpr int kWordsPerRow = 2;   // code words a lane decodes per row and pair
 };
 template <>
 struct IFmt<FMT_Q8_0> {
     static constexpr int kPairBytes = 68;    // two 34-byte blocks
     static constexpr int kChunkPairs = 16;   // 1024 columns
+    static constexpr int kChunkBytes = 1088;
     static constexpr int kWordsPerRow = 4;
+};
+// Q4_K: a "pair" is the 64 values of one 32-byte code run of a 144-byte
+// super-block (sub-blocks 2j and 2j + 1: low and high nibbles of the same
+// bytes); a warp's two pairs are the adjacent runs 2(w & 1), 2(w & 1) + 1 of
+// super-block w / 2 of the chunk, 32 bytes apart.
+template <>
+struct IFmt<FMT_Q4_K> {
+    static constexpr int kPairBytes = 32;    // step between a warp's two code runs
+    static constexpr int kChunkPairs = 32;   // 2048 columns = 8 super-blocks
+    static constexpr int kChunkBytes = 1152;
+    static constexpr int kWordsPerRow = 4;   // a lane takes one nibble of 16 code bytes per row and pair
 };
 template <int FMT>
 struct IGeom {
     static constexpr int kChunkCols = IFmt<FMT>::kChunkPairs * 64;
-    static constexpr int kChunkBytes = IFmt<FMT>::kChunkPairs * IFmt<FMT>::kPairBytes;   // 1152 | 1088
+    static constexpr int kChunkBytes = IFmt<FMT>::kChunkBytes;   // 1152 | 1088 | 1152
     static constexpr int kRowStride = kChunkBytes + 16;                                  // 1168 | 1104
     static constexpr int kBoxElems = kRowStride / 8;                                     // uint64 elements
     // TMA destinations (stage base + 8-row box offsets) must be 128-byte aligned
@@ -118,9 +135,14 @@ __host__ __device__ constexpr int word_byte(int fmt, int t, int w, int q) {
 }
 // Block element (0..31, within the lane's block) multiplied at k-slot byte q
 // of operand register r (0 = a0/a1, 1 = a2/a3) in MMA m of a block pair.
+// Q4_K: quad lanes 0-1 take the low nibbles (sub-block 2j), lanes 2-3 the
+// high nibbles (sub-block 2j + 1) of the same 16 bytes per lane: byte
+// 16 (t % 2) + 4 w + q of the run holds element 16 (t % 2) + 4 w + q of
+// both, and code word w = 2 m + r feeds operand r of MMA m.
 __host__ __device__ constexpr int slot_elem(int fmt, int t, int m, int r, int q) {
-    return fmt == FMT_Q4_0 ? (word_byte(fmt, t, r, q) - (t < 2 ? 2 : 20)) + 16 * m
-                           : (word_byte(fmt, t, 2 * m + r, q) - (t < 2 ? 2 : 36));
+    return fmt == FMT_Q4_K ? 16 * (t & 1) + 4 * (2 * m + r) + q
+           : fmt == FMT_Q4_0 ? (word_byte(fmt, t, r, q) - (t < 2 ? 2 : 20)) + 16 * m
+                             : (word_byte(fmt, t, 2 * m + r, q) - (t < 2 ? 2 : 36));
 }
 
 struct alignas(64) ImmaSegment {
@@ -210,7 +232,35 @@ struct LaneCtx {
     uint32_t brec;        // smem address of this lane's B record slot, block pair 0
     uint32_t xsl;         // smem address of this lane's block scale 2^-F, block pair 0
     f2 kd0, kd1;          // digit weights of accumulator columns 2t, 2t + 1
+    // Q4_K only
+    uint32_t nsh;         // 0: this lane's sub-block is the low nibbles, 4: the high ones
+    uint32_t oddw;        // the warp's runs are sub-blocks 4..7 of their super-block
+    uint32_t ksel[2];     // PRMT gathering the (scale, min) bytes of the lane's sub-block, run J
+    uint32_t xsum_off;    // bytes from a block scale to the block's sum of x
+    float kmin;           // 1 on the quad lane that adds its sub-block's min term, else 0
 };
+
+__device__ __forceinline__ float f16_lo(uint32_t v) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(v & 0xFFFFu)));
+}
+__device__ __forceinline__ float f16_hi(uint32_t v) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(v >> 16)));
+}
+// 6-bit scale and min of the lane's sub-block s (GGUF's packed 12 bytes q in
+// header words h.y, h.z, h.w): s < 4: q[s] & 63, q[s + 4] & 63; s >= 4:
+// (q[s + 4] & 15) | (q[s - 4] >> 6) << 4, (q[s + 4] >> 4) | (q[s] >> 6) << 4.
+__device__ __forceinline__ void k_scale_min(const LaneCtx& L, uint32_t sel, const uint4& h, float& sc, float& mn) {
+    if (L.oddw) {
+        const uint32_t v = prmt(h.y, h.w, sel);         // byte 0 = q[s - 4], byte 1 = q[s + 4]
+        const uint32_t v2 = prmt(h.z, h.z, sel & 0xFu);  // byte 0 = q[s]
+        sc = static_cast<float>(((v >> 8) & 15u) | ((v >> 2) & 0x30u));
+        mn = static_cast<float>(((v >> 12) & 15u) | ((v2 >> 2) & 0x30u));
+    } else {
+        const uint32_t v = prmt(h.y, h.z, sel);         // byte 0 = q[s], byte 1 = q[s + 4]
+        sc = static_cast<float>(v & 63u);
+        mn = static_cast<float>((v >> 8) & 63u);
+    }
+}
 
 // One 16-row tile (RT) of block pair J of a stage: 2 MMAs and the fp32 fold.
 // st[w] = stage base + woff[w]; every offset below is a compile-time constant.
@@ -247,6 +297,40 @@ __device__ __forceinline__ void pair_tile(const LaneCtx& L, const uint32_t (&st)
     y = fma2(mul2(dd, xs2), fma2(c1, L.kd1, mul2(c0, L.kd0)), y);
 }
 
+// Q4_K, one 16-row tile (RT) of code run J: the lane's nibbles as unsigned
+// s8 codes (no offset), 2 MMAs, then per row d * scale * 2^-F * (digits)
+// - dmin * min * sum(x) for the lane's sub-block (the min once per quad).
+template <int J, int RT>
+__device__ __forceinline__ void pair_tile_k(const LaneCtx& L, const uint32_t (&st)[4], uint32_t sh, const uint4& B,
+                                            const f2& xs2, const f2& xm2, f2& y) {
+    constexpr int kRS = IGeom<FMT_Q4_K>::kRowStride;
+    constexpr int O = RT * 16 * kRS + J * IFmt<FMT_Q4_K>::kPairBytes;
+    constexpr int O8 = RT < 2 ? O + 8 * kRS : O;       // row g + 8 (tile 2: rows 32..35 only)
+    constexpr int H = RT * 16 * kRS;                    // the super-block header of row g
+    constexpr int H8 = RT < 2 ? H + 8 * kRS : H;
+    // the lane's 16 code bytes of rows g and g + 8: one 16-byte load each
+    // (rows are 1168 bytes apart, so the 16 distinct addresses of a warp
+    // fall two per 16-byte bank group: two wavefronts, no conflict)
+    const uint4 q0 = lds4_at<O>(st[0]), q1 = lds4_at<O8>(st[0]);
+    const uint32_t W0[4] = {(q0.x >> L.nsh) & 0x0F0F0F0Fu, (q0.y >> L.nsh) & 0x0F0F0F0Fu,
+                            (q0.z >> L.nsh) & 0x0F0F0F0Fu, (q0.w >> L.nsh) & 0x0F0F0F0Fu};
+    const uint32_t W1[4] = {(q1.x >> L.nsh) & 0x0F0F0F0Fu, (q1.y >> L.nsh) & 0x0F0F0F0Fu,
+                            (q1.z >> L.nsh) & 0x0F0F0F0Fu, (q1.w >> L.nsh) & 0x0F0F0F0Fu};
+    const uint4 h0 = lds4_at<H>(sh), h1 = lds4_at<H8>(sh);
+    int acc[4] = {0, 0, 0, 0};
+    imma(acc, W0[0], W1[0], W0[1], W1[1], B.x, B.y);
+    imma(acc, W0[2], W1[2], W0[3], W1[3], B.z, B.w);
+    float sc0, mn0, sc1, mn1;
+    k_scale_min(L, L.ksel[J], h0, sc0, mn0);
+    k_scale_min(L, L.ksel[J], h1, sc1, mn1);
+    const f2 dd = mk2(f16_lo(h0.x) * sc0, f16_lo(h1.x) * sc1);
+    const f2 mm = mk2(f16_hi(h0.x) * mn0, f16_hi(h1.x) * mn1);
+    const f2 c0 = mk2(static_cast<float>(acc[0]), static_cast<float>(acc[2]));
+    const f2 c1 = mk2(static_cast<float>(acc[1]), static_cast<float>(acc[3]));
+    y = fma2(mul2(dd, xs2), fma2(c1, L.kd1, mul2(c0, L.kd0)), y);
+    y = fma2(mm, xm2, y);
+}
+
 // All of a stage's work for one warp: kPPW block pairs x NRT row tiles.
 template <int FMT, int NRT, int J = 0>
 __device__ __forceinline__ void stage_pairs(const LaneCtx& L, const uint32_t (&st)[4], uint32_t sv0, uint32_t svd,
@@ -255,9 +339,17 @@ __device__ __forceinline__ void stage_pairs(const LaneCtx& L, const uint32_t (&s
     const uint4 B = lds4_at<J * kRecBytesT>(pb);
     const float xsv = __uint_as_float(lds_at<J * 8>(px));
     const f2 xs2 = mk2(xsv, xsv);
-    pair_tile<FMT, J, 0>(L, st, sv0, svd, B, xs2, y0);
-    if constexpr (NRT >= 2) pair_tile<FMT, J, 1>(L, st, sv0, svd, B, xs2, y1);
-    if constexpr (NRT >= 3) pair_tile<FMT, J, 2>(L, st, sv0, svd, B, xs2, y2);
+    if constexpr (FMT == FMT_Q4_K) {
+        const float xmv = -L.kmin * __uint_as_float(lds_at<J * 8>(px + L.xsum_off));
+        const f2 xm2 = mk2(xmv, xmv);
+        pair_tile_k<J, 0>(L, st, sv0, B, xs2, xm2, y0);
+        if constexpr (NRT >= 2) pair_tile_k<J, 1>(L, st, sv0, B, xs2, xm2, y1);
+        if constexpr (NRT >= 3) pair_tile_k<J, 2>(L, st, sv0, B, xs2, xm2, y2);
+    } else {
+        pair_tile<FMT, J, 0>(L, st, sv0, svd, B, xs2, y0);
+        if constexpr (NRT >= 2) pair_tile<FMT, J, 1>(L, st, sv0, svd, B, xs2, y1);
+        if constexpr (NRT >= 3) pair_tile<FMT, J, 2>(L, st, sv0, svd, B, xs2, y2);
+    }
     if constexpr (J + 1 < IGeom<FMT>::kPairsPerWarp)
         stage_pairs<FMT, NRT, J + 1>(L, st, sv0, svd, pb, px, y0, y1, y2);
 }
@@ -287,7 +379,8 @@ __device__ __forceinline__ int unit_pair(int u, int j, int warp) {
 // Pass A for one unit: lane l's four elements of unit pair l / 16 into the
 // three digit-plane words of `scratch`, and the block scales.
 template <int FMT>
-__device__ __forceinline__ void stage_pass_a(const float4& v, int u, int warp, int lane, float* xs, uint32_t* swr) {
+__device__ __forceinline__ void stage_pass_a(const float4& v, int u, int warp, int lane, float* xs, uint32_t* swr,
+                                             float* xsum) {
     float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
@@ -301,6 +394,13 @@ __device__ __forceinline__ void stage_pass_a(const float4& v, int u, int warp, i
     const float inv = eb == 0xFFu ? __uint_as_float(0x7FC00000u)
                                   : __uint_as_float((ec - 21u - (FMT == FMT_Q4_0 ? 4u : 0u)) << 23);
     if ((lane & 7) == 0) xs[2 * unit_pair<FMT>(u, lane >> 4, warp) + ((lane >> 3) & 1)] = inv;
+    if constexpr (FMT == FMT_Q4_K) {   // the block's sum of x, for the min term
+        float sm = (v.x + v.y) + (v.z + v.w);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 4);
+        if ((lane & 7) == 0) xsum[2 * unit_pair<FMT>(u, lane >> 4, warp) + ((lane >> 3) & 1)] = sm;
+    }
     const float xv[4] = {v.x, v.y, v.z, v.w};
     uint32_t bits[4], mid[4], hig[4];
 #pragma unroll
@@ -316,7 +416,7 @@ __device__ __forceinline__ void stage_pass_a(const float4& v, int u, int warp, i
 
 template <int FMT>
 __device__ __forceinline__ void stage_x(const float* __restrict__ x, int nunits, uint8_t* rec, float* xs,
-                                        uint8_t* scratch, int warp, int lane) {
+                                        uint8_t* scratch, int warp, int lane, float* xsum) {
     const int jb = lane >> 4, gi = lane & 15;                  // pass B: (pair, t, m, r)
     const int t = gi >> 2, m = (gi >> 1) & 1, r = gi & 1;
     const int e0 = slot_elem(FMT, t, m, r, 0), e2 = slot_elem(FMT, t, m, r, 2);
@@ -349,8 +449,8 @@ __device__ __forceinline__ void stage_x(const float* __restrict__ x, int nunits,
             if (u >= nunits) break;
             const bool two = u + 1 < nunits;
             __syncwarp();                                 // the previous round's pass B has read the scratch
-            stage_pass_a<FMT>(v[b], u, warp, lane, xs, sw);
-            if (two) stage_pass_a<FMT>(v[b + 1], u + 1, warp, lane, xs, sw + 96);
+            stage_pass_a<FMT>(v[b], u, warp, lane, xs, sw, xsum);
+            if (two) stage_pass_a<FMT>(v[b + 1], u + 1, warp, lane, xs, sw + 96, xsum);
             __syncwarp();
             pass_b(u, 0);
             if (two) pass_b(u + 1, 1);
@@ -380,6 +480,8 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
     sp += static_cast<size_t>(npairs) * kRecBytes;
     float* xs = reinterpret_cast<float*>(sp);             // [2 * npairs]
     sp += static_cast<size_t>(npairs) * 8;
+    float* xsum = reinterpret_cast<float*>(sp);           // Q4_K: [2 * npairs], each block's sum of x
+    if (FMT == FMT_Q4_K) sp += static_cast<size_t>(npairs) * 8;
     float* red = reinterpret_cast<float*>(sp);            // [kRing][kCW][kRedRows]
     sp += kRing * kCW * kRedRows * 4;
     uint8_t* scratch = sp;                                // [kCW][kScratchBytes]: x staging
@@ -490,19 +592,45 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
     const int pair_first = warp * kPPW;                   // this warp's pairs in every chunk
     if (u_begin < u_end) {
         // digits of this warp's pairs for the whole launch (read by no other warp)
-        stage_x<FMT>(p.x, nchunks * kPPW / 2, rec, xs, scratch + warp * kScratchBytes, warp, lane);
+        stage_x<FMT>(p.x, nchunks * kPPW / 2, rec, xs, scratch + warp * kScratchBytes, warp, lane, xsum);
         __syncwarp();
     }
     // Per-lane constants: offsets within a stage (row g of tile 0, pair 0 of
     // this warp); rows g + 8, tile 1 and later pairs are constant offsets.
     LaneCtx L;
+    if constexpr (FMT == FMT_Q4_K) {
+        // runs 2 (w % 2), 2 (w % 2) + 1 of super-block w / 2; the header
+        // (d, dmin, packed scales) at the super-block's first 16 bytes
+        const int sblk = (warp >> 1) * 144;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
-        const int sw = w < kNW ? src_word(FMT, t, w) : 0;
-        L.woff[w] = static_cast<uint32_t>(pair_first * kPB + g * kRS + 4 * (sw >= 0 ? sw : (FMT == FMT_Q4_0 ? 4 : 8)));
+        for (int w = 0; w < 4; ++w)
+            L.woff[w] = static_cast<uint32_t>(sblk + 16 + 64 * (warp & 1) + g * kRS + 16 * (t & 1) + 4 * w);
+        L.v0 = static_cast<uint32_t>(sblk + g * kRS);
+        L.vd = L.v0;
+        L.nsh = t < 2 ? 0u : 4u;
+        L.oddw = static_cast<uint32_t>(warp & 1);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const uint32_t sl = static_cast<uint32_t>(2 * j + (t >= 2 ? 1 : 0));   // sub-block mod 4
+            L.ksel[j] = sl | (sl + 4u) << 4;
+        }
+        L.xsum_off = static_cast<uint32_t>(npairs) * 8u;
+        L.kmin = (t & 1) ? 0.0f : 1.0f;
+    } else {
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const int sw = w < kNW ? src_word(FMT, t, w) : 0;
+            L.woff[w] =
+                static_cast<uint32_t>(pair_first * kPB + g * kRS + 4 * (sw >= 0 ? sw : (FMT == FMT_Q4_0 ? 4 : 8)));
+        }
+        L.v0 = static_cast<uint32_t>(pair_first * kPB + g * kRS);
+        L.vd = L.v0 + (FMT == FMT_Q4_0 ? 16u : 32u);
+        L.nsh = 0u;
+        L.oddw = 0u;
+        L.ksel[0] = L.ksel[1] = 0u;
+        L.xsum_off = 0u;
+        L.kmin = 0.0f;
     }
-    L.v0 = static_cast<uint32_t>(pair_first * kPB + g * kRS);
-    L.vd = L.v0 + (FMT == FMT_Q4_0 ? 16u : 32u);
     L.sel_fix = t == 1 ? 0x1076u : 0x3210u;
     L.sel_d = t < 2 ? 0x3210u : 0x7676u;
     const bool bact = t < 2 ? g < 3 : (g >= 4 && g < 7);
@@ -566,7 +694,7 @@ template <int FMT>
 bool encode_maps(ImmaSegment& ms, const void* w, int K, int rows) {
     auto fn = tensor_map_encoder();
     if (!fn) return false;
-    const size_t row_bytes = static_cast<size_t>(K) / 32 * (FMT == FMT_Q4_0 ? 18 : 34);
+    const size_t row_bytes = static_cast<size_t>(K) / 32 * (FMT == FMT_Q8_0 ? 34 : 18);   // Q4_K: K / 256 * 144
     const cuuint64_t dims[2] = {row_bytes / 8, static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {row_bytes};
     const cuuint32_t es[2] = {1, 1};
@@ -581,18 +709,20 @@ bool encode_maps(ImmaSegment& ms, const void* w, int K, int rows) {
 }
 
 int stage_bytes_of(int fmt) {
-    return fmt == FMT_Q4_0 ? IGeom<FMT_Q4_0>::kStageBytes : IGeom<FMT_Q8_0>::kStageBytes;
+    return fmt == FMT_Q4_0 ? IGeom<FMT_Q4_0>::kStageBytes
+           : fmt == FMT_Q4_K ? IGeom<FMT_Q4_K>::kStageBytes
+                             : IGeom<FMT_Q8_0>::kStageBytes;
 }
 
-size_t fixed_smem(int K) {
+size_t fixed_smem(int fmt, int K) {
     const size_t npairs = static_cast<size_t>(K / 64);
-    return 1024 + npairs * (kRecBytes + 8) + kRing * kCW * kRedRows * 4 + kCW * kScratchBytes +
+    return 1024 + npairs * (kRecBytes + (fmt == FMT_Q4_K ? 16 : 8)) + kRing * kCW * kRedRows * 4 + kCW * kScratchBytes +
            (2 * kMaxStages + 2 * kRing) * 8;
 }
 
 // Stages (at most kMaxStages) that fit beside the fixed part in 227 KB.
 void plan_smem(int fmt, int K, int* stages, size_t* smem) {
-    const size_t fixed = fixed_smem(K);
+    const size_t fixed = fixed_smem(fmt, K);
     const int sb = stage_bytes_of(fmt);
     *stages = static_cast<int>(std::min<size_t>(kMaxStages, kSmemMax > fixed ? (kSmemMax - fixed) / sb : 0));
     *smem = fixed + static_cast<size_t>(*stages) * sb;
@@ -601,7 +731,7 @@ void plan_smem(int fmt, int K, int* stages, size_t* smem) {
 }  // namespace
 
 bool matvec_imma_supported(int fmt, int K) {
-    if ((fmt != FMT_Q4_0 && fmt != FMT_Q8_0) || K <= 0 || K % 2048 != 0) return false;
+    if ((fmt != FMT_Q4_0 && fmt != FMT_Q8_0 && fmt != FMT_Q4_K) || K <= 0 || K % 2048 != 0) return false;
     int stages = 0;
     size_t smem = 0;
     plan_smem(fmt, K, &stages, &smem);
@@ -628,8 +758,9 @@ cudaError_t launch_matvec_imma(int fmt, const MatvecParams& mp, cudaStream_t str
     int row0 = 0;
     for (int s = 0; s < mp.nseg; ++s) {
         ImmaSegment& ms = p.seg[s];
-        const bool ok = fmt == FMT_Q4_0 ? encode_maps<FMT_Q4_0>(ms, mp.seg[s].w, mp.K, mp.seg[s].rows)
-                                        : encode_maps<FMT_Q8_0>(ms, mp.seg[s].w, mp.K, mp.seg[s].rows);
+        const bool ok = fmt == FMT_Q4_0   ? encode_maps<FMT_Q4_0>(ms, mp.seg[s].w, mp.K, mp.seg[s].rows)
+                        : fmt == FMT_Q4_K ? encode_maps<FMT_Q4_K>(ms, mp.seg[s].w, mp.K, mp.seg[s].rows)
+                                          : encode_maps<FMT_Q8_0>(ms, mp.seg[s].w, mp.K, mp.seg[s].rows);
         if (!ok) return cudaErrorInvalidValue;
         ms.bias = mp.seg[s].bias;
         ms.residual = mp.seg[s].residual;
@@ -641,11 +772,13 @@ cudaError_t launch_matvec_imma(int fmt, const MatvecParams& mp, cudaStream_t str
     int stages = 0;
     size_t smem = 0;
     plan_smem(fmt, mp.K, &stages, &smem);
-    auto kern = fmt == FMT_Q4_0 ? quant_imma_kernel<FMT_Q4_0> : quant_imma_kernel<FMT_Q8_0>;
-    static bool configured[2][64] = {};
+    auto kern = fmt == FMT_Q4_0   ? quant_imma_kernel<FMT_Q4_0>
+                : fmt == FMT_Q4_K ? quant_imma_kernel<FMT_Q4_K>
+                                  : quant_imma_kernel<FMT_Q8_0>;
+    static bool configured[3][64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    bool& done = configured[fmt == FMT_Q4_0 ? 0 : 1][dev & 63];
+    bool& done = configured[fmt == FMT_Q4_0 ? 0 : fmt == FMT_Q4_K ? 2 : 1][dev & 63];
     if (!done) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
         if (e != cudaSuccess) return e;

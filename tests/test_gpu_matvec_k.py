@@ -63,7 +63,10 @@ def test_golden_known_answers(lib, golden):
 
 @pytest.mark.parametrize("kind", [oracle.Q4_K, oracle.Q6_K])
 @pytest.mark.parametrize("N,K", [(1, 256), (7, 512), (37, 2816), (300, 2048), (4096, 4096), (1024, 14336),
-                                 (14336, 4096), (33, 5120), (40, 11264)])
+                                 (14336, 4096), (33, 5120), (40, 11264),
+                                 # Q4_K on integer tensor cores (K a multiple of 2048, rows in 4s):
+                                 # ragged 16-row tiles and a 36-row slab
+                                 (100, 2048), (516, 6144)])
 def test_matches_oracle_and_fp64(lib, kind, N, K):
     w = synth.k_quant(kind, 100 + N + kind, N, K)
     x = synth.activation(200 + K, K)
