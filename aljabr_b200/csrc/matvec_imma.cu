@@ -233,7 +233,7 @@ struct LaneCtx {
     uint32_t xsl;         // smem address of this lane's block scale 2^-F, block pair 0
     f2 kd0, kd1;          // digit weights of accumulator columns 2t, 2t + 1
     // Q4_K only
-    uint32_t nsh;         // 0: this lane's sub-block is the low nibbles, 4: the high ones
+    uint32_t nmask;       // 0x0F0F0F0F: this lane's sub-block is the low nibbles, 0xF0F0F0F0: the high ones
     uint32_t oddw;        // the warp's runs are sub-blocks 4..7 of their super-block
     uint32_t ksel[2];     // PRMT gathering the (scale, min) bytes of the lane's sub-block, run J
     uint32_t xsum_off;    // bytes from a block scale to the block's sum of x
@@ -297,38 +297,60 @@ __device__ __forceinline__ void pair_tile(const LaneCtx& L, const uint32_t (&st)
     y = fma2(mul2(dd, xs2), fma2(c1, L.kd1, mul2(c0, L.kd0)), y);
 }
 
-// Q4_K, one 16-row tile (RT) of code run J: the lane's nibbles as unsigned
-// s8 codes (no offset), 2 MMAs, then per row d * scale * 2^-F * (digits)
-// - dmin * min * sum(x) for the lane's sub-block (the min once per quad).
-template <int J, int RT>
-__device__ __forceinline__ void pair_tile_k(const LaneCtx& L, const uint32_t (&st)[4], uint32_t sh, const uint4& B,
-                                            const f2& xs2, const f2& xm2, f2& y) {
+// Q4_K, one 16-row tile RT of a warp's stage work: the super-block header of
+// rows g and g + 8 is read and its d / dmin decoded once for both code runs
+// J; per run, the lane's 16 code bytes per row (one 16-byte load each: rows
+// are 1168 bytes apart, so the 16 distinct addresses of a warp fall two per
+// 16-byte bank group), one AND keeps its nibbles -- c (low) or 16 c (high,
+// within u8) -- and two u8 x s8 MMAs give the sub-block dot; per row
+// d * scale * 2^-F * (digits) - dmin * min * sum(x), the min once per quad.
+__device__ __forceinline__ void immau(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                      uint32_t b1) {
+    asm(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+template <int RT>
+__device__ __forceinline__ void tile_k(const LaneCtx& L, uint32_t sc0, uint32_t sh, const uint4 (&B)[2],
+                                       const f2 (&xs2)[2], const f2 (&xm2)[2], f2& y) {
     constexpr int kRS = IGeom<FMT_Q4_K>::kRowStride;
-    constexpr int O = RT * 16 * kRS + J * IFmt<FMT_Q4_K>::kPairBytes;
-    constexpr int O8 = RT < 2 ? O + 8 * kRS : O;       // row g + 8 (tile 2: rows 32..35 only)
-    constexpr int H = RT * 16 * kRS;                    // the super-block header of row g
-    constexpr int H8 = RT < 2 ? H + 8 * kRS : H;
-    // the lane's 16 code bytes of rows g and g + 8: one 16-byte load each
-    // (rows are 1168 bytes apart, so the 16 distinct addresses of a warp
-    // fall two per 16-byte bank group: two wavefronts, no conflict)
-    const uint4 q0 = lds4_at<O>(st[0]), q1 = lds4_at<O8>(st[0]);
-    const uint32_t W0[4] = {(q0.x >> L.nsh) & 0x0F0F0F0Fu, (q0.y >> L.nsh) & 0x0F0F0F0Fu,
-                            (q0.z >> L.nsh) & 0x0F0F0F0Fu, (q0.w >> L.nsh) & 0x0F0F0F0Fu};
-    const uint32_t W1[4] = {(q1.x >> L.nsh) & 0x0F0F0F0Fu, (q1.y >> L.nsh) & 0x0F0F0F0Fu,
-                            (q1.z >> L.nsh) & 0x0F0F0F0Fu, (q1.w >> L.nsh) & 0x0F0F0F0Fu};
+    constexpr int H = RT * 16 * kRS;                    // row g of the tile
+    constexpr int H8 = RT < 2 ? H + 8 * kRS : H;        // row g + 8 (tile 2: rows 32..35 only)
     const uint4 h0 = lds4_at<H>(sh), h1 = lds4_at<H8>(sh);
-    int acc[4] = {0, 0, 0, 0};
-    imma(acc, W0[0], W1[0], W0[1], W1[1], B.x, B.y);
-    imma(acc, W0[2], W1[2], W0[3], W1[3], B.z, B.w);
-    float sc0, mn0, sc1, mn1;
-    k_scale_min(L, L.ksel[J], h0, sc0, mn0);
-    k_scale_min(L, L.ksel[J], h1, sc1, mn1);
-    const f2 dd = mk2(f16_lo(h0.x) * sc0, f16_lo(h1.x) * sc1);
-    const f2 mm = mk2(f16_hi(h0.x) * mn0, f16_hi(h1.x) * mn1);
-    const f2 c0 = mk2(static_cast<float>(acc[0]), static_cast<float>(acc[2]));
-    const f2 c1 = mk2(static_cast<float>(acc[1]), static_cast<float>(acc[3]));
-    y = fma2(mul2(dd, xs2), fma2(c1, L.kd1, mul2(c0, L.kd0)), y);
-    y = fma2(mm, xm2, y);
+    const f2 dv = mk2(f16_lo(h0.x), f16_lo(h1.x));
+    const f2 dmv = mk2(f16_hi(h0.x), f16_hi(h1.x));
+#pragma unroll
+    for (int J = 0; J < 2; ++J) {
+        constexpr int kPB = IFmt<FMT_Q4_K>::kPairBytes;
+        const uint4 q0 = J == 0 ? lds4_at<H>(sc0) : lds4_at<H + kPB>(sc0);
+        const uint4 q1 = J == 0 ? lds4_at<H8>(sc0) : lds4_at<H8 + kPB>(sc0);
+        int acc[4] = {0, 0, 0, 0};
+        immau(acc, q0.x & L.nmask, q1.x & L.nmask, q0.y & L.nmask, q1.y & L.nmask, B[J].x, B[J].y);
+        immau(acc, q0.z & L.nmask, q1.z & L.nmask, q0.w & L.nmask, q1.w & L.nmask, B[J].z, B[J].w);
+        float s0, m0, s1, m1;
+        k_scale_min(L, L.ksel[J], h0, s0, m0);
+        k_scale_min(L, L.ksel[J], h1, s1, m1);
+        const f2 dd = mul2(dv, mk2(s0, s1));
+        const f2 mm = mul2(dmv, mk2(m0, m1));
+        const f2 c0 = mk2(static_cast<float>(acc[0]), static_cast<float>(acc[2]));
+        const f2 c1 = mk2(static_cast<float>(acc[1]), static_cast<float>(acc[3]));
+        y = fma2(mul2(dd, xs2[J]), fma2(c1, L.kd1, mul2(c0, L.kd0)), y);
+        y = fma2(mm, xm2[J], y);
+    }
+}
+template <int NRT>
+__device__ __forceinline__ void stage_pairs_k(const LaneCtx& L, uint32_t sc0, uint32_t sh, uint32_t pb, uint32_t px,
+                                              f2& y0, f2& y1, f2& y2) {
+    const uint4 B[2] = {lds4_at<0>(pb), lds4_at<kRecBytes>(pb)};
+    const float xa = __uint_as_float(lds_at<0>(px)), xb = __uint_as_float(lds_at<8>(px));
+    const float ma = -L.kmin * __uint_as_float(lds_at<0>(px + L.xsum_off));
+    const float mb = -L.kmin * __uint_as_float(lds_at<8>(px + L.xsum_off));
+    const f2 xs2[2] = {mk2(xa, xa), mk2(xb, xb)};
+    const f2 xm2[2] = {mk2(ma, ma), mk2(mb, mb)};
+    tile_k<0>(L, sc0, sh, B, xs2, xm2, y0);
+    if constexpr (NRT >= 2) tile_k<1>(L, sc0, sh, B, xs2, xm2, y1);
+    if constexpr (NRT >= 3) tile_k<2>(L, sc0, sh, B, xs2, xm2, y2);
 }
 
 // All of a stage's work for one warp: kPPW block pairs x NRT row tiles.
@@ -339,17 +361,9 @@ __device__ __forceinline__ void stage_pairs(const LaneCtx& L, const uint32_t (&s
     const uint4 B = lds4_at<J * kRecBytesT>(pb);
     const float xsv = __uint_as_float(lds_at<J * 8>(px));
     const f2 xs2 = mk2(xsv, xsv);
-    if constexpr (FMT == FMT_Q4_K) {
-        const float xmv = -L.kmin * __uint_as_float(lds_at<J * 8>(px + L.xsum_off));
-        const f2 xm2 = mk2(xmv, xmv);
-        pair_tile_k<J, 0>(L, st, sv0, B, xs2, xm2, y0);
-        if constexpr (NRT >= 2) pair_tile_k<J, 1>(L, st, sv0, B, xs2, xm2, y1);
-        if constexpr (NRT >= 3) pair_tile_k<J, 2>(L, st, sv0, B, xs2, xm2, y2);
-    } else {
-        pair_tile<FMT, J, 0>(L, st, sv0, svd, B, xs2, y0);
-        if constexpr (NRT >= 2) pair_tile<FMT, J, 1>(L, st, sv0, svd, B, xs2, y1);
-        if constexpr (NRT >= 3) pair_tile<FMT, J, 2>(L, st, sv0, svd, B, xs2, y2);
-    }
+    pair_tile<FMT, J, 0>(L, st, sv0, svd, B, xs2, y0);
+    if constexpr (NRT >= 2) pair_tile<FMT, J, 1>(L, st, sv0, svd, B, xs2, y1);
+    if constexpr (NRT >= 3) pair_tile<FMT, J, 2>(L, st, sv0, svd, B, xs2, y2);
     if constexpr (J + 1 < IGeom<FMT>::kPairsPerWarp)
         stage_pairs<FMT, NRT, J + 1>(L, st, sv0, svd, pb, px, y0, y1, y2);
 }
@@ -607,7 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
             L.woff[w] = static_cast<uint32_t>(sblk + 16 + 64 * (warp & 1) + g * kRS + 16 * (t & 1) + 4 * w);
         L.v0 = static_cast<uint32_t>(sblk + g * kRS);
         L.vd = L.v0;
-        L.nsh = t < 2 ? 0u : 4u;
+        L.nmask = t < 2 ? 0x0F0F0F0Fu : 0xF0F0F0F0u;
         L.oddw = static_cast<uint32_t>(warp & 1);
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
@@ -625,7 +639,7 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
         }
         L.v0 = static_cast<uint32_t>(pair_first * kPB + g * kRS);
         L.vd = L.v0 + (FMT == FMT_Q4_0 ? 16u : 32u);
-        L.nsh = 0u;
+        L.nmask = 0u;
         L.oddw = 0u;
         L.ksel[0] = L.ksel[1] = 0u;
         L.xsum_off = 0u;
@@ -639,6 +653,10 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
     L.xsl = smem_u32(xs) + 4u * (t >> 1);
     L.kd0 = mk2((t & 1) ? 1.0f : 65536.0f, (t & 1) ? 1.0f : 65536.0f);
     L.kd1 = mk2((t & 1) ? 0.0f : 256.0f, (t & 1) ? 0.0f : 256.0f);
+    if (FMT == FMT_Q4_K && t >= 2) {   // high nibbles enter as 16 c
+        L.kd0 = mul2(L.kd0, mk2(0.0625f, 0.0625f));
+        L.kd1 = mul2(L.kd1, mk2(0.0625f, 0.0625f));
+    }
     const uint32_t stage_s = smem_u32(stage0);
 
     SlabWalk walk{u_begin, u_end};
@@ -654,12 +672,21 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
                 const uint32_t sb = stage_s + s * kStageBytes;
                 const uint32_t st[4] = {sb + L.woff[0], sb + L.woff[1], sb + L.woff[2], sb + L.woff[3]};
                 const uint32_t pb = L.brec + P0 * kRecBytes, px = L.xsl + 8u * P0;
-                if (ntiles == 2)
-                    stage_pairs<FMT, 2>(L, st, sb + L.v0, sb + L.vd, pb, px, y0, y1, y2);
-                else if (ntiles == 1)
-                    stage_pairs<FMT, 1>(L, st, sb + L.v0, sb + L.vd, pb, px, y0, y1, y2);
-                else
-                    stage_pairs<FMT, 3>(L, st, sb + L.v0, sb + L.vd, pb, px, y0, y1, y2);
+                if constexpr (FMT == FMT_Q4_K) {
+                    if (ntiles == 2)
+                        stage_pairs_k<2>(L, st[0], sb + L.v0, pb, px, y0, y1, y2);
+                    else if (ntiles == 1)
+                        stage_pairs_k<1>(L, st[0], sb + L.v0, pb, px, y0, y1, y2);
+                    else
+                        stage_pairs_k<3>(L, st[0], sb + L.v0, pb, px, y0, y1, y2);
+                } else {
+                    if (ntiles == 2)
+                        stage_pairs<FMT, 2>(L, st, sb + L.v0, sb + L.vd, pb, px, y0, y1, y2);
+                    else if (ntiles == 1)
+                        stage_pairs<FMT, 1>(L, st, sb + L.v0, sb + L.vd, pb, px, y0, y1, y2);
+                    else
+                        stage_pairs<FMT, 3>(L, st, sb + L.v0, sb + L.vd, pb, px, y0, y1, y2);
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);

@@ -34,7 +34,10 @@
 //     MMA keeps the four blocks of a span apart and D(row, 2t) + D(row, 2t+1)
 //     is block t's dot product; every partial sum is an exact multiple of a
 //     power of two below 2^24, so the tensor core's accumulation rounds
-//     nothing and the result carries fp32 accuracy;
+//     nothing.  What is not exact is the split itself: x keeps 22 bits
+//     relative to its block's largest |x| (hi on the integer grid, lo on the
+//     2^-11 grid), so an element far below its block maximum loses low bits;
+//     the other roundings are the fp32 sums over blocks;
 //   * the code offset (-8 for Q4_0, -128 for the biased Q8_0 bytes) enters as
 //     the accumulator's initial value -off sum(hi) 2^-24 (hi column) and
 //     -off sum(lo) 2^-24 (lo column);

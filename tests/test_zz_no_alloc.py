@@ -66,6 +66,13 @@ def test_noalloc_matches_dev_entry_twice(lib, kv_dtype, Hq, Hkv, D, ctx, start):
         floor = 1e-3 * np.abs(w).max()
         rel = (np.abs(o - w) / np.maximum(np.abs(w), floor)).max()
         assert rel < 1e-3, (call, rel)
+        if ctx == 4096:   # and on its own against the CPU restatement of the reference
+            import oracle
+            kf, vf = k.float().cpu().numpy(), v.float().cpu().numpy()
+            ref = oracle.gqa_decode_attention(q.cpu().numpy(), kf.ravel(), vf.ravel(), stride, Hkv, Hq, D, ctx,
+                                              start, scale)
+            rel = (np.abs(o - ref) / np.maximum(np.abs(ref), 1e-3 * np.abs(ref).max())).max()
+            assert rel < 1e-3, (call, rel)
 
 
 def test_noalloc_rejects_scratch_beyond_static_array(lib):
