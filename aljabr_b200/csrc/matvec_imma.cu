@@ -82,6 +82,7 @@ struct IFmt<FMT_Q4_0> {
     static constexpr int kPairBytes = 36;    // two 18-byte blocks
     static constexpr int kChunkPairs = 32;   // 2048 columns
     static constexpr int kChunkBytes = 1152;
+    static constexpr int kRowPad = 16;       // a 4-word bank shift per row
     static constexpr int kWordsPerRow = 2;   // code words a lane decodes per row and pair
 };
 template <>
@@ -89,6 +90,7 @@ struct IFmt<FMT_Q8_0> {
     static constexpr int kPairBytes = 68;    // two 34-byte blocks
     static constexpr int kChunkPairs = 16;   // 1024 columns
     static constexpr int kChunkBytes = 1088;
+    static constexpr int kRowPad = 16;
     static constexpr int kWordsPerRow = 4;
 };
 // Q4_K: a "pair" is the 64 values of one 32-byte code run of a 144-byte
@@ -100,13 +102,16 @@ struct IFmt<FMT_Q4_K> {
     static constexpr int kPairBytes = 32;    // step between a warp's two code runs
     static constexpr int kChunkPairs = 32;   // 2048 columns = 8 super-blocks
     static constexpr int kChunkBytes = 1152;
+    // an 8-word bank shift per row: the 16-byte code loads of a quarter warp
+    // (rows g, g + 1, both 16-byte halves of a run) hit four distinct groups
+    static constexpr int kRowPad = 32;
     static constexpr int kWordsPerRow = 4;   // a lane takes one nibble of 16 code bytes per row and pair
 };
 template <int FMT>
 struct IGeom {
     static constexpr int kChunkCols = IFmt<FMT>::kChunkPairs * 64;
     static constexpr int kChunkBytes = IFmt<FMT>::kChunkBytes;   // 1152 | 1088 | 1152
-    static constexpr int kRowStride = kChunkBytes + 16;                                  // 1168 | 1104
+    static constexpr int kRowStride = kChunkBytes + IFmt<FMT>::kRowPad;                  // 1168 | 1104 | 1184
     static constexpr int kBoxElems = kRowStride / 8;                                     // uint64 elements
     // TMA destinations (stage base + 8-row box offsets) must be 128-byte aligned
     static constexpr int kStageBytes = (kStageRows * kRowStride + 127) / 128 * 128;
@@ -299,9 +304,9 @@ __device__ __forceinline__ void pair_tile(const LaneCtx& L, const uint32_t (&st)
 
 // Q4_K, one 16-row tile RT of a warp's stage work: the super-block header of
 // rows g and g + 8 is read and its d / dmin decoded once for both code runs
-// J; per run, the lane's 16 code bytes per row (one 16-byte load each: rows
-// are 1168 bytes apart, so the 16 distinct addresses of a warp fall two per
-// 16-byte bank group), one AND keeps its nibbles -- c (low) or 16 c (high,
+// J; per run, the lane's 16 code bytes per row (one 16-byte load each; rows
+// are 1184 bytes apart, so a quarter warp's four addresses hit distinct
+// 16-byte bank groups), one AND keeps its nibbles -- c (low) or 16 c (high,
 // within u8) -- and two u8 x s8 MMAs give the sub-block dot; per row
 // d * scale * 2^-F * (digits) - dmin * min * sum(x), the min once per quad.
 __device__ __forceinline__ void immau(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
