@@ -12,6 +12,7 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <array>
 #include <thread>
 #include <tuple>
 #include <vector>
@@ -123,6 +124,9 @@ struct DeviceState {
     DevBuf dx, dy, dtmp, dscratch, dgemm;
     HostBuf hx, hy;
     std::map<PackKey, PackedQ> qpack;       // guarded by mu
+    // host-buffer matvec calls replayed as one CUDA graph (x pull + matvecs)
+    // per shape, weights and staging buffers; guarded by mu
+    std::map<std::array<uintptr_t, 20>, std::pair<int, cudaGraphExec_t>> tb_graphs;
     void* upload_bounce[2] = {nullptr, nullptr};   // pinned, for model uploads (guarded by upload_mu)
     cudaEvent_t upload_done[2] = {nullptr, nullptr};
     std::mutex upload_mu;
@@ -400,17 +404,73 @@ int tb_matvec(int nmat, const int* types, const void* const* B, const float* con
     memcpy(st->hx.p, A, xfloats * 4);
     if (nb) memcpy(static_cast<float*>(st->hx.p) + xfloats, bias_host, nb * 4);
     float* dx = static_cast<float*>(st->dx.p);
-    ALJ_CUDA(launch_host_pull(dx, static_cast<const float*>(st->hx.dev), xfloats + nb, st->sms, st->stream));
     const float* dbias = nb ? dx + xfloats : nullptr;
     float* ydev = static_cast<float*>(st->hy.dev);
-    for (int b = 0; b < batch; ++b) {
-        size_t off = 0;
-        for (int i = 0; i < nmat; ++i) {
-            spec[i].y = ydev + static_cast<size_t>(b) * ytotal + off;
-            spec[i].bias = (i == 0) ? dbias : nullptr;
-            off += static_cast<size_t>(outs[i].N);
+    // the x pull and the matvecs, as launched on st->stream
+    auto enqueue = [&]() -> int {
+        if (launch_host_pull(dx, static_cast<const float*>(st->hx.dev), xfloats + nb, st->sms, st->stream) !=
+            cudaSuccess)
+            return fail(ALJ_ERR_CUDA, "x pull launch failed");
+        for (int b = 0; b < batch; ++b) {
+            size_t off = 0;
+            for (int i = 0; i < nmat; ++i) {
+                spec[i].y = ydev + static_cast<size_t>(b) * ytotal + off;
+                spec[i].bias = (i == 0) ? dbias : nullptr;
+                off += static_cast<size_t>(outs[i].N);
+            }
+            int rc = run_matvecs(st, spec, nmat, dx + static_cast<size_t>(b) * K, K, group, st->stream, true);
+            if (rc) return rc;
         }
-        int rc = run_matvecs(st, spec, nmat, dx + static_cast<size_t>(b) * K, K, group, st->stream, true);
+        return ALJ_OK;
+    };
+    // A shape seen before (same matrices, sizes and staging buffers) is
+    // replayed as one CUDA graph: one launch instead of two or more, with
+    // the tensor maps encoded once.  Captured on its second call (the first
+    // sets the kernels' attributes); not while a prefetch hint is pending,
+    // which belongs to the next launch only.
+    std::array<uintptr_t, 20> key{};
+    key[0] = static_cast<uintptr_t>(nmat);
+    key[1] = static_cast<uintptr_t>(K);
+    key[2] = static_cast<uintptr_t>(group);
+    key[3] = static_cast<uintptr_t>(batch);
+    key[4] = static_cast<uintptr_t>(nb);
+    for (int i = 0; i < nmat; ++i) {
+        key[5 + i] = reinterpret_cast<uintptr_t>(spec[i].w);
+        key[8 + i] = reinterpret_cast<uintptr_t>(spec[i].absmax);
+        key[11 + i] = static_cast<uintptr_t>(spec[i].N);
+        key[14 + i] = static_cast<uintptr_t>(spec[i].type);
+    }
+    key[17] = reinterpret_cast<uintptr_t>(st->hx.dev);
+    key[18] = reinterpret_cast<uintptr_t>(st->dx.p);
+    key[19] = reinterpret_cast<uintptr_t>(st->hy.dev);
+    cudaGraphExec_t ge = nullptr;
+    if (!t_prefetch) {
+        auto it = st->tb_graphs.find(key);
+        if (it == st->tb_graphs.end()) {
+            if (st->tb_graphs.size() < 256) st->tb_graphs.emplace(key, std::make_pair(1, nullptr));
+        } else if (it->second.second) {
+            ge = it->second.second;
+        } else if (++it->second.first >= 2) {
+            cudaGraph_t graph = nullptr;
+            if (cudaStreamBeginCapture(st->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+                const int rc = enqueue();
+                const cudaError_t e = cudaStreamEndCapture(st->stream, &graph);
+                if (rc == ALJ_OK && e == cudaSuccess && graph &&
+                    cudaGraphInstantiate(&ge, graph, 0) == cudaSuccess) {
+                    it->second.second = ge;
+                } else {
+                    ge = nullptr;
+                    it->second.first = -(1 << 30);   // this shape runs direct from now on
+                }
+                if (graph) cudaGraphDestroy(graph);
+            }
+            cudaGetLastError();   // a failed capture leaves no error behind; the direct path runs
+        }
+    }
+    if (ge) {
+        ALJ_CUDA(cudaGraphLaunch(ge, st->stream));
+    } else {
+        const int rc = enqueue();
         if (rc) return rc;
     }
     ALJ_CUDA(cudaStreamSynchronize(st->stream));
@@ -817,6 +877,9 @@ int aljabr_blackwell_shutdown(void) {
         s->hx.release(); s->hy.release();
         for (auto& kv : s->qpack) cudaFree(kv.second.p);
         s->qpack.clear();
+        for (auto& kv : s->tb_graphs)
+            if (kv.second.second) cudaGraphExecDestroy(kv.second.second);
+        s->tb_graphs.clear();
         for (int b = 0; b < 2; ++b) {
             if (s->upload_bounce[b]) cudaFreeHost(s->upload_bounce[b]);
             if (s->upload_done[b]) cudaEventDestroy(s->upload_done[b]);
@@ -875,6 +938,17 @@ int aljabr_blackwell_unregister_model_buffer(const void* base_ptr) {
             if (w >= lo && w < hi) {
                 cudaFree(q->second.p);
                 q = st->qpack.erase(q);
+            } else {
+                ++q;
+            }
+        }
+        // replay graphs of host-buffer calls on matrices inside this buffer
+        for (auto q = st->tb_graphs.begin(); q != st->tb_graphs.end();) {
+            bool inside = false;
+            for (int i = 0; i < 3; ++i) inside = inside || (q->first[5 + i] >= lo && q->first[5 + i] < hi);
+            if (inside) {
+                if (q->second.second) cudaGraphExecDestroy(q->second.second);
+                q = st->tb_graphs.erase(q);
             } else {
                 ++q;
             }
