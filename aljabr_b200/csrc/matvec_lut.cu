@@ -189,33 +189,30 @@ __host__ __device__ inline StageLayout stage_layout(int group) {
     return L;
 }
 
-// Issue the boxes of `nunits` 4-row units starting at segment row r0 into
-// slab rows [srow, srow + 4 nunits).
-__device__ __forceinline__ void load_rows(const LutSegment& sg, int r0, int nunits, int srow, int chunk,
-                                          uint32_t st, const StageLayout& L, int abs_elems, uint64_t* bar) {
-    for (int u = 0; u < nunits;) {
-        const bool eight = nunits - u >= 2;
-        const int rr = srow + u * kUnit;
+// The boxes of `nunits` 4-row units starting at segment row r0, into slab
+// rows [srow, srow + 4 nunits), one per lane: lane 2b takes the code box of
+// units 2b, 2b + 1 (8 rows, or 4 for a last single unit), lane 2b + 1 its
+// absmax box.  Lanes past the slab's boxes issue nothing.
+__device__ __forceinline__ void load_rows_lane(int lane, const LutSegment& sg, int r0, int nunits, int srow,
+                                               int chunk, uint32_t st, const StageLayout& L, int abs_elems,
+                                               uint64_t* bar) {
+    const int u = 2 * (lane >> 1);
+    if (u >= nunits) return;
+    const bool eight = nunits - u >= 2;
+    const int rr = srow + u * kUnit;
+    if ((lane & 1) == 0)
         tma_load_2d(st + rr * kCodeRowBytes, eight ? &sg.codes8 : &sg.codes4, chunk * (kCodeRowBytes / 8),
                     r0 + u * kUnit, bar);
+    else
         tma_load_2d(st + L.abs_off + rr * L.abs_row_bytes, eight ? &sg.abs8 : &sg.abs4, chunk * abs_elems,
                     r0 + u * kUnit, bar);
-        u += eight ? 2 : 1;
-    }
 }
 
 template <int GROUP>
 __global__ void __launch_bounds__(kThreads, 1) nf4_lut_kernel(const __grid_constant__ LutParams p, int stages) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
-    if (threadIdx.x == (kProducerWarp << 5)) {   // descriptors on their way before the first copies
-        for (int g = 0; g < p.nseg; ++g) {
-            prefetch_tensormap(&p.seg[g].codes8);
-            prefetch_tensormap(&p.seg[g].codes4);
-            prefetch_tensormap(&p.seg[g].abs8);
-            prefetch_tensormap(&p.seg[g].abs4);
-        }
-        prefetch_tensormap(&p.xmap);
-    }
+    // x's descriptor on its way (the weight boxes go out first thing below)
+    if (threadIdx.x == (kProducerWarp << 5)) prefetch_tensormap(&p.xmap);
     pdl_launch_dependents();
     const SlabGeom geo = slab_geom(p);
     const int K = p.K;
@@ -236,8 +233,9 @@ __global__ void __launch_bounds__(kThreads, 1) nf4_lut_kernel(const __grid_const
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int units = geo.total_rows / kUnit;
-    const int u_begin = static_cast<int>(static_cast<long long>(units) * blockIdx.x / gridDim.x);
-    const int u_end = static_cast<int>(static_cast<long long>(units) * (blockIdx.x + 1) / gridDim.x);
+    // units <= 2^15 (rows <= 131072), so 32-bit products suffice
+    const int u_begin = static_cast<int>(static_cast<unsigned int>(units) * blockIdx.x / gridDim.x);
+    const int u_end = static_cast<int>(static_cast<unsigned int>(units) * (blockIdx.x + 1) / gridDim.x);
 
     // The producer warp initialises the barriers and goes straight on to its
     // first copies; the other warps wait on named barrier 3 (all threads)
@@ -261,27 +259,40 @@ __global__ void __launch_bounds__(kThreads, 1) nf4_lut_kernel(const __grid_const
     }
 
     if (warp == kProducerWarp) {
-        if (lane == 0) {
-            SlabWalk walk{u_begin, u_end};
-            int seg, su, nunits, s = 0;
-            uint32_t ph = 0;
-            bool alive = true;
-            bool x_waited = false;
-            while (alive && walk.next(geo, seg, su, nunits)) {
-                const int rows = nunits * kUnit * (p.pair ? 2 : 1);
-                for (int c = 0; c < nchunks; ++c) {
-                    if (!mbar_wait(&empty[s], ph ^ 1u)) {
+        // The whole warp walks the slabs; lane 0 waits and arms, the box
+        // copies of a stage go out one per lane.  The first `stages` fills
+        // use fresh slots (no wait).
+        SlabWalk walk{u_begin, u_end};
+        int seg, su, nunits, s = 0, issued = 0;
+        uint32_t ph = 0;
+        bool alive = true;
+        bool x_waited = false;
+        while (alive && walk.next(geo, seg, su, nunits)) {
+            const int rows = nunits * kUnit * (p.pair ? 2 : 1);
+            for (int c = 0; c < nchunks; ++c) {
+                if (issued >= stages) {
+                    int ok = 1;
+                    if (lane == 0) ok = mbar_wait(&empty[s], ph ^ 1u) ? 1 : 0;
+                    if (!__shfl_sync(0xffffffffu, ok, 0)) {
                         alive = false;
                         break;
                     }
-                    const uint32_t st = stage_s + s * L.bytes;
+                }
+                const uint32_t st = stage_s + s * L.bytes;
+                if (lane == 0)
                     mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rows * (kCodeRowBytes + L.abs_row_bytes) + kXBytes));
-                    if (p.pair) {
-                        load_rows(p.seg[0], su * kUnit, nunits, 0, c, st, L, kAbsElems, &full[s]);
-                        load_rows(p.seg[1], su * kUnit, nunits, kSlabRows / 2, c, st, L, kAbsElems, &full[s]);
-                    } else {
-                        load_rows(p.seg[seg], su * kUnit - p.seg[seg].row0, nunits, 0, c, st, L, kAbsElems, &full[s]);
-                    }
+                __syncwarp();
+                if (p.pair) {
+                    if (lane < 8)
+                        load_rows_lane(lane, p.seg[0], su * kUnit, nunits, 0, c, st, L, kAbsElems, &full[s]);
+                    else if (lane < 16)
+                        load_rows_lane(lane - 8, p.seg[1], su * kUnit, nunits, kSlabRows / 2, c, st, L, kAbsElems,
+                                       &full[s]);
+                } else if (lane < 8) {
+                    load_rows_lane(lane, p.seg[seg], su * kUnit - p.seg[seg].row0, nunits, 0, c, st, L, kAbsElems,
+                                   &full[s]);
+                }
+                if (lane == 0) {
                     // x comes from the previous kernel: its first copy waits for it.
                     if (!x_waited) {
                         pdl_wait();
@@ -291,17 +302,18 @@ __global__ void __launch_bounds__(kThreads, 1) nf4_lut_kernel(const __grid_const
                                            static_cast<unsigned int>(*p.tpl.seq * p.tpl.wait_mul + p.tpl.wait_add));
                             fence_proxy_async_global();
                         }
-                        x_waited = true;
                     }
                     tma_load_2d(st + L.x_off, &p.xmap, 0, c * (kChunkElems / 32), &full[s]);
-                    if (++s == stages) {
-                        s = 0;
-                        ph ^= 1u;
-                    }
+                }
+                x_waited = true;
+                ++issued;
+                if (++s == stages) {
+                    s = 0;
+                    ph ^= 1u;
                 }
             }
-            if (alive && p.prefetch) prefetch_share(p.prefetch, p.prefetch_bytes);
         }
+        if (lane == 0 && alive && p.prefetch) prefetch_share(p.prefetch, p.prefetch_bytes);
         return;
     }
 
