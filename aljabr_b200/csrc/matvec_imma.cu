@@ -512,8 +512,9 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int units = p.total_rows / kUnit;
-    const int u_begin = static_cast<int>(static_cast<long long>(units) * blockIdx.x / gridDim.x);
-    const int u_end = static_cast<int>(static_cast<long long>(units) * (blockIdx.x + 1) / gridDim.x);
+    // units <= 2^15 (rows <= 131072), so 32-bit products suffice
+    const int u_begin = static_cast<int>(static_cast<unsigned int>(units) * blockIdx.x / gridDim.x);
+    const int u_end = static_cast<int>(static_cast<unsigned int>(units) * (blockIdx.x + 1) / gridDim.x);
 
     // The producer and epilogue warps initialise their own barriers and go
     // (bar.arrive); consumers wait for both (bar.sync) before touching them.
@@ -521,12 +522,11 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
     constexpr int kSetupBar = 1, kSetupThreads = kThreads;
     if (warp == kProducerWarp) {
         // Weights never depend on the previous kernel: copies start before
-        // griddepcontrol.wait.
+        // griddepcontrol.wait.  The whole warp walks the slabs; lane 0 waits
+        // and arms, and the boxes of a stage go out one per lane (lane j the
+        // rows 8j..8j+7, or a 4-row box for the last 4).  The first `stages`
+        // fills use fresh slots (no wait).
         if (lane == 0) {
-            for (int s = 0; s < p.nseg; ++s) {
-                prefetch_tensormap(&p.seg[s].map8);
-                prefetch_tensormap(&p.seg[s].map4);
-            }
             for (int s = 0; s < stages; ++s) {
                 mbar_init(&full[s], 1);
                 mbar_init(&empty[s], kCW);
@@ -535,36 +535,39 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
         }
         __syncwarp();
         named_bar_arrive(kSetupBar, kSetupThreads);
-        if (lane == 0) {
-            SlabWalk walk{u_begin, u_end};
-            int seg, su, nunits, s = 0, issued = 0;
-            uint32_t ph = 0;
-            bool alive = true;
-            while (alive && walk.next(p, seg, su, nunits)) {
-                const ImmaSegment& sg = p.seg[seg];
-                const int r0 = su * kUnit - sg.row0;
-                const int rows = nunits * kUnit;
-                for (int c = 0; c < nchunks; ++c) {
-                    if (!mbar_wait(&empty[s], ph ^ 1u)) {
+        SlabWalk walk{u_begin, u_end};
+        int seg, su, nunits, s = 0, issued = 0;
+        uint32_t ph = 0;
+        bool alive = true;
+        while (alive && walk.next(p, seg, su, nunits)) {
+            const ImmaSegment& sg = p.seg[seg];
+            const int r0 = su * kUnit - sg.row0;
+            const int rows = nunits * kUnit;
+            for (int c = 0; c < nchunks; ++c) {
+                if (issued >= stages) {
+                    int ok = 1;
+                    if (lane == 0) ok = mbar_wait(&empty[s], ph ^ 1u) ? 1 : 0;
+                    if (!__shfl_sync(0xffffffffu, ok, 0)) {
                         alive = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rows * kRS));
-                    const uint32_t st = smem_u32(stage0) + s * kStageBytes;
-                    const int cx = c * (G::kChunkBytes / 8);
-                    for (int r = 0; r < rows; r += 8)   // 8-row boxes, a 4-row box for the last 4
-                        tma_load_2d(st + r * kRS, rows - r >= 8 ? &sg.map8 : &sg.map4, cx, r0 + r, &full[s]);
-                    ++issued;
-                    if (++s == stages) {
-                        s = 0;
-                        ph ^= 1u;
-                    }
+                }
+                if (lane == 0) mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rows * kRS));
+                __syncwarp();
+                const int r = 8 * lane;
+                if (r < rows)
+                    tma_load_2d(smem_u32(stage0) + s * kStageBytes + r * kRS, rows - r >= 8 ? &sg.map8 : &sg.map4,
+                                c * (G::kChunkBytes / 8), r0 + r, &full[s]);
+                ++issued;
+                if (++s == stages) {
+                    s = 0;
+                    ph ^= 1u;
                 }
             }
-            // the next launch's share of weights into L2 (all of it: this
-            // keeps HBM busy across the launch boundary)
-            if (alive && p.prefetch) prefetch_share(p.prefetch, p.prefetch_bytes, p.prefetch_bytes);
         }
+        // the next launch's share of weights into L2 (all of it: this
+        // keeps HBM busy across the launch boundary)
+        if (lane == 0 && alive && p.prefetch) prefetch_share(p.prefetch, p.prefetch_bytes, p.prefetch_bytes);
         return;
     }
 
