@@ -718,7 +718,7 @@ bool matvec_tma_supported(int fmt, int K, int group) {
 
 cudaError_t launch_matvec(int fmt, const MatvecParams& p, cudaStream_t stream, bool pdl) {
     if (p.total_rows <= 0) return cudaSuccess;
-    if (fmt == FMT_Q4_K && matvec_imma_supported(fmt, p.K)) {   // K a multiple of 2048: integer tensor cores
+    if ((fmt == FMT_Q4_K || fmt == FMT_Q6_K) && matvec_imma_supported(fmt, p.K)) {   // K a multiple of 2048
         const cudaError_t e = launch_matvec_imma(fmt, p, stream, pdl);
         if (e != cudaErrorNotSupported) return e;
     }

@@ -1,4 +1,4 @@
-// Batch-1 GGUF Q4_0, Q8_0 and Q4_K dequantise-and-matvec (y = W x) on the integer
+// Batch-1 GGUF Q4_0, Q8_0, Q4_K and Q6_K dequantise-and-matvec (y = W x) on the integer
 // tensor-core path of B200 (sm_100a): mma.sync.m16n8k32 with s8 operands and
 // s32 accumulation, for K a multiple of 2048.
 //
@@ -107,6 +107,20 @@ struct IFmt<FMT_Q4_K> {
     static constexpr int kRowPad = 32;
     static constexpr int kWordsPerRow = 4;   // a lane takes one nibble of 16 code bytes per row and pair
 };
+// Q6_K: 210-byte super-blocks (ql[128] low nibbles, qh[64] two high bits,
+// int8 scales[16] per 16 values, fp16 d), 8 per 2048-column chunk (1680
+// bytes).  A "pair" is 64 values = blocks k0, k0 + 1 (k0 = 2 (j % 2)) of
+// half h = j / 2 of a super-block; a warp's two pairs (j = 2 (w % 2) and
+// + 1, super-block w / 2) read the same ql / qh bytes (other nibble, other
+// bit pair).  Super-blocks are only 2-byte aligned in shared memory.
+template <>
+struct IFmt<FMT_Q6_K> {
+    static constexpr int kPairBytes = 0;     // the warp's two pairs share their code bytes
+    static constexpr int kChunkPairs = 32;   // 2048 columns = 8 super-blocks
+    static constexpr int kChunkBytes = 1680;
+    static constexpr int kRowPad = 16;
+    static constexpr int kWordsPerRow = 0;
+};
 template <int FMT>
 struct IGeom {
     static constexpr int kChunkCols = IFmt<FMT>::kChunkPairs * 64;
@@ -144,8 +158,11 @@ __host__ __device__ constexpr int word_byte(int fmt, int t, int w, int q) {
 // high nibbles (sub-block 2j + 1) of the same 16 bytes per lane: byte
 // 16 (t % 2) + 4 w + q of the run holds element 16 (t % 2) + 4 w + q of
 // both, and code word w = 2 m + r feeds operand r of MMA m.
+// Q6_K (pair-relative): MMA m is block m of the pair, quad lanes 0-1 its
+// values 0..15, lanes 2-3 values 16..31, 8 per lane.
 __host__ __device__ constexpr int slot_elem(int fmt, int t, int m, int r, int q) {
-    return fmt == FMT_Q4_K ? 16 * (t & 1) + 4 * (2 * m + r) + q
+    return fmt == FMT_Q6_K   ? 32 * m + 16 * (t >> 1) + 8 * (t & 1) + 4 * r + q
+           : fmt == FMT_Q4_K ? 16 * (t & 1) + 4 * (2 * m + r) + q
            : fmt == FMT_Q4_0 ? (word_byte(fmt, t, r, q) - (t < 2 ? 2 : 20)) + 16 * m
                              : (word_byte(fmt, t, 2 * m + r, q) - (t < 2 ? 2 : 36));
 }
@@ -242,7 +259,14 @@ struct LaneCtx {
     uint32_t oddw;        // the warp's runs are sub-blocks 4..7 of their super-block
     uint32_t ksel[2];     // PRMT gathering the (scale, min) bytes of the lane's sub-block, run J
     uint32_t xsum_off;    // bytes from a block scale to the block's sum of x
-    float kmin;           // 1 on the quad lane that adds its sub-block's min term, else 0
+    float kmin;           // 1 on the quad lane that adds its sub-block's min term (Q6_K: offset term), else 0
+    // Q6_K only (oddw: the warp's super-block starts 2 bytes off a word)
+    uint32_t qoff[3];     // word-aligned offsets (row g, tile 0) of the lane's ql bytes (blocks 0, 1) and qh bytes
+    uint32_t soff;        // word-aligned offset of the word holding the lane's first scale byte
+    uint32_t ssel[4];     // sign-extending PRMT of scale e = 2 J + m out of words (0, 1), or (1, 2) if bit e of sw
+    uint32_t sw;
+    uint32_t doff, dsh;   // d's word-aligned offset and bit position (0 or 16)
+    uint32_t xs16l;       // smem address of this lane's half sums of x (its half of block 0), pair 0
 };
 
 __device__ __forceinline__ float f16_lo(uint32_t v) {
@@ -358,6 +382,97 @@ __device__ __forceinline__ void stage_pairs_k(const LaneCtx& L, uint32_t sc0, ui
     if constexpr (NRT >= 3) tile_k<2>(L, sc0, sh, B, xs2, xm2, y2);
 }
 
+// Q6_K: 8 bytes at row offset O + a (a word-aligned; `mis`: the field starts
+// 2 bytes past a), as two words.
+template <int O>
+__device__ __forceinline__ uint2 q6_field(uint32_t a, uint32_t mis) {
+    const uint32_t w0 = lds_at<O>(a), w1 = lds_at<O + 4>(a);
+    if (!mis) return make_uint2(w0, w1);
+    const uint32_t w2 = lds_at<O + 8>(a);
+    return make_uint2(__funnelshift_r(w0, w1, 16), __funnelshift_r(w1, w2, 16));
+}
+// Scale e = 2 J + m of the lane's half (int8, sign-extended by PRMT).
+__device__ __forceinline__ float q6_scale(const LaneCtx& L, int e, uint32_t s0, uint32_t s1, uint32_t s2) {
+    const bool hw = (L.sw >> e) & 1u;
+    return static_cast<float>(static_cast<int>(prmt(hw ? s1 : s0, hw ? s2 : s1, L.ssel[e])));
+}
+// 6-bit codes of 4 values: ql nibble J, qh bits 2k..2k+1 (k = 2 J + m) on top.
+template <int J, int M>
+__device__ __forceinline__ uint32_t q6_codes(uint32_t ql, uint32_t qh) {
+    constexpr int k = 2 * J + M;
+    const uint32_t lo = (J == 0 ? ql : ql >> 4) & 0x0F0F0F0Fu;
+    const uint32_t hi = (k == 0 ? qh << 4 : k == 1 ? qh << 2 : k == 2 ? qh : qh >> 2) & 0x30303030u;
+    return lo | hi;
+}
+// Q6_K, one 16-row tile RT: per row the lane's ql (blocks 0, 1) and qh bytes,
+// its four scales and d, shared by the warp's two pairs J; per (J, block m)
+// one u8 x s8 MMA on the codes q in 0..63, then per row
+// d * scale * (2^-F (digits) - 32 sum(x of the half)), the offset term once
+// per quad.
+template <int RT>
+__device__ __forceinline__ void tile_q6(const LaneCtx& L, uint32_t sb, const uint4 (&B)[2], const f2 (&xs2)[2][2],
+                                        const f2 (&xm2)[2][2], f2& y) {
+    constexpr int kRS = IGeom<FMT_Q6_K>::kRowStride;
+    constexpr int R0 = RT * 16 * kRS;
+    constexpr int R8 = RT < 2 ? R0 + 8 * kRS : R0;      // row g + 8 (tile 2: rows 32..35 only)
+    const uint2 ql0[2] = {q6_field<R0>(sb + L.qoff[0], L.oddw), q6_field<R8>(sb + L.qoff[0], L.oddw)};
+    const uint2 ql1[2] = {q6_field<R0>(sb + L.qoff[1], L.oddw), q6_field<R8>(sb + L.qoff[1], L.oddw)};
+    const uint2 qh[2] = {q6_field<R0>(sb + L.qoff[2], L.oddw), q6_field<R8>(sb + L.qoff[2], L.oddw)};
+    const uint32_t sa = sb + L.soff, da = sb + L.doff;
+    const uint32_t s00 = lds_at<R0>(sa), s01 = lds_at<R0 + 4>(sa), s02 = lds_at<R0 + 8>(sa);
+    const uint32_t s10 = lds_at<R8>(sa), s11 = lds_at<R8 + 4>(sa), s12 = lds_at<R8 + 8>(sa);
+    const float d0 = __half2float(__ushort_as_half(static_cast<unsigned short>((lds_at<R0>(da) >> L.dsh) & 0xFFFFu)));
+    const float d1 = __half2float(__ushort_as_half(static_cast<unsigned short>((lds_at<R8>(da) >> L.dsh) & 0xFFFFu)));
+#pragma unroll
+    for (int J = 0; J < 2; ++J)
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
+            const uint2 lo0 = m == 0 ? ql0[0] : ql1[0], lo1 = m == 0 ? ql0[1] : ql1[1];
+            uint32_t a0, a1, a2, a3;
+            if (J == 0 && m == 0) {
+                a0 = q6_codes<0, 0>(lo0.x, qh[0].x); a1 = q6_codes<0, 0>(lo1.x, qh[1].x);
+                a2 = q6_codes<0, 0>(lo0.y, qh[0].y); a3 = q6_codes<0, 0>(lo1.y, qh[1].y);
+            } else if (J == 0) {
+                a0 = q6_codes<0, 1>(lo0.x, qh[0].x); a1 = q6_codes<0, 1>(lo1.x, qh[1].x);
+                a2 = q6_codes<0, 1>(lo0.y, qh[0].y); a3 = q6_codes<0, 1>(lo1.y, qh[1].y);
+            } else if (m == 0) {
+                a0 = q6_codes<1, 0>(lo0.x, qh[0].x); a1 = q6_codes<1, 0>(lo1.x, qh[1].x);
+                a2 = q6_codes<1, 0>(lo0.y, qh[0].y); a3 = q6_codes<1, 0>(lo1.y, qh[1].y);
+            } else {
+                a0 = q6_codes<1, 1>(lo0.x, qh[0].x); a1 = q6_codes<1, 1>(lo1.x, qh[1].x);
+                a2 = q6_codes<1, 1>(lo0.y, qh[0].y); a3 = q6_codes<1, 1>(lo1.y, qh[1].y);
+            }
+            int acc[4] = {0, 0, 0, 0};
+            immau(acc, a0, a1, a2, a3, m == 0 ? B[J].x : B[J].z, m == 0 ? B[J].y : B[J].w);
+            const int e = 2 * J + m;
+            const f2 dd = mk2(d0 * q6_scale(L, e, s00, s01, s02), d1 * q6_scale(L, e, s10, s11, s12));
+            const f2 c0 = mk2(static_cast<float>(acc[0]), static_cast<float>(acc[2]));
+            const f2 c1 = mk2(static_cast<float>(acc[1]), static_cast<float>(acc[3]));
+            y = fma2(dd, fma2(xs2[J][m], fma2(c1, L.kd1, mul2(c0, L.kd0)), xm2[J][m]), y);
+        }
+}
+template <int NRT>
+__device__ __forceinline__ void stage_pairs_q6(const LaneCtx& L, uint32_t sb, uint32_t pb, uint32_t px, uint32_t px16,
+                                               f2& y0, f2& y1, f2& y2) {
+    const uint4 B[2] = {lds4_at<0>(pb), lds4_at<kRecBytes>(pb)};
+    f2 xs2[2][2], xm2[2][2];
+#pragma unroll
+    for (int J = 0; J < 2; ++J)
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
+            const float xs = __uint_as_float(J == 0 ? (m == 0 ? lds_at<0>(px) : lds_at<4>(px))
+                                                    : (m == 0 ? lds_at<8>(px) : lds_at<12>(px)));
+            const float hs = __uint_as_float(J == 0 ? (m == 0 ? lds_at<0>(px16) : lds_at<8>(px16))
+                                                    : (m == 0 ? lds_at<16>(px16) : lds_at<24>(px16)));
+            xs2[J][m] = mk2(xs, xs);
+            const float xm = -32.0f * L.kmin * hs;
+            xm2[J][m] = mk2(xm, xm);
+        }
+    tile_q6<0>(L, sb, B, xs2, xm2, y0);
+    if constexpr (NRT >= 2) tile_q6<1>(L, sb, B, xs2, xm2, y1);
+    if constexpr (NRT >= 3) tile_q6<2>(L, sb, B, xs2, xm2, y2);
+}
+
 // All of a stage's work for one warp: kPPW block pairs x NRT row tiles.
 template <int FMT, int NRT, int J = 0>
 __device__ __forceinline__ void stage_pairs(const LaneCtx& L, const uint32_t (&st)[4], uint32_t sv0, uint32_t svd,
@@ -413,6 +528,12 @@ __device__ __forceinline__ void stage_pass_a(const float4& v, int u, int warp, i
     const float inv = eb == 0xFFu ? __uint_as_float(0x7FC00000u)
                                   : __uint_as_float((ec - 21u - (FMT == FMT_Q4_0 ? 4u : 0u)) << 23);
     if ((lane & 7) == 0) xs[2 * unit_pair<FMT>(u, lane >> 4, warp) + ((lane >> 3) & 1)] = inv;
+    if constexpr (FMT == FMT_Q6_K) {   // each 16-value half's sum of x, for the -32 offset
+        float sm = (v.x + v.y) + (v.z + v.w);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+        if ((lane & 3) == 0) xsum[4 * unit_pair<FMT>(u, lane >> 4, warp) + ((lane >> 2) & 3)] = sm;
+    }
     if constexpr (FMT == FMT_Q4_K) {   // the block's sum of x, for the min term
         float sm = (v.x + v.y) + (v.z + v.w);
         sm += __shfl_xor_sync(0xffffffffu, sm, 1);
@@ -439,7 +560,7 @@ __device__ __forceinline__ void stage_x(const float* __restrict__ x, int nunits,
     const int jb = lane >> 4, gi = lane & 15;                  // pass B: (pair, t, m, r)
     const int t = gi >> 2, m = (gi >> 1) & 1, r = gi & 1;
     const int e0 = slot_elem(FMT, t, m, r, 0), e2 = slot_elem(FMT, t, m, r, 2);
-    const int bbase = jb * 64 + (t < 2 ? 0 : 32);
+    const int bbase = jb * 64 + (FMT != FMT_Q6_K && t >= 2 ? 32 : 0);   // Q6_K's slots are pair-relative
     const int wa = (bbase + e0) >> 2, wb = (bbase + e2) >> 2;  // scratch words holding bytes e0, e0+1 / e2, e2+1
     const uint32_t gsel = static_cast<uint32_t>((e0 & 3) | ((e0 & 3) + 1) << 4 | (4 + (e2 & 3)) << 8 |
                                                 (5 + (e2 & 3)) << 12);
@@ -499,8 +620,9 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
     sp += static_cast<size_t>(npairs) * kRecBytes;
     float* xs = reinterpret_cast<float*>(sp);             // [2 * npairs]
     sp += static_cast<size_t>(npairs) * 8;
-    float* xsum = reinterpret_cast<float*>(sp);           // Q4_K: [2 * npairs], each block's sum of x
+    float* xsum = reinterpret_cast<float*>(sp);           // Q4_K: [2 * npairs] block sums, Q6_K: [4 * npairs] half sums of x
     if (FMT == FMT_Q4_K) sp += static_cast<size_t>(npairs) * 8;
+    if (FMT == FMT_Q6_K) sp += static_cast<size_t>(npairs) * 16;
     float* red = reinterpret_cast<float*>(sp);            // [kRing][kCW][kRedRows]
     sp += kRing * kCW * kRedRows * 4;
     uint8_t* scratch = sp;                                // [kCW][kScratchBytes]: x staging
@@ -638,6 +760,33 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
         }
         L.xsum_off = static_cast<uint32_t>(npairs) * 8u;
         L.kmin = (t & 1) ? 0.0f : 1.0f;
+    } else if constexpr (FMT == FMT_Q6_K) {
+        // super-block w / 2 (byte B of the chunk row), half h = w % 2; lane
+        // values i0..i0+7 of each block (i0 = 16 (t / 2) + 8 (t % 2))
+        const int sbB = (warp >> 1) * 210, h = warp & 1, half = t >> 1;
+        const int i0 = 16 * half + 8 * (t & 1), off = sbB & 3;   // off: 0 or 2
+        const int rowg = g * kRS;
+        L.qoff[0] = static_cast<uint32_t>(rowg + sbB + 64 * h + i0 - off);
+        L.qoff[1] = static_cast<uint32_t>(rowg + sbB + 64 * h + 32 + i0 - off);
+        L.qoff[2] = static_cast<uint32_t>(rowg + sbB + 128 + 32 * h + i0 - off);
+        const int s0 = sbB + 192 + 8 * h + half, sa = s0 & ~3;   // scales[8h + 2k + half], k = 2J + m
+        L.soff = static_cast<uint32_t>(rowg + sa);
+        L.sw = 0u;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int pb = s0 - sa + 2 * e;
+            const uint32_t idx = static_cast<uint32_t>(pb < 8 ? pb : pb - 4);
+            if (pb >= 8) L.sw |= 1u << e;
+            L.ssel[e] = idx | (8u | idx) << 4 | (8u | idx) << 8 | (8u | idx) << 12;
+        }
+        const int dp = sbB + 208;
+        L.doff = static_cast<uint32_t>(rowg + (dp & ~3));
+        L.dsh = (dp & 3) ? 16u : 0u;
+        L.oddw = off != 0 ? 1u : 0u;
+        L.kmin = (t & 1) ? 0.0f : 1.0f;
+        L.nmask = 0u;
+        L.ksel[0] = L.ksel[1] = 0u;
+        L.xsum_off = 0u;
     } else {
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
@@ -658,7 +807,8 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
     const bool bact = t < 2 ? g < 3 : (g >= 4 && g < 7);
     const int slot = bact ? (t < 2 ? 2 * g + t : 6 + 2 * (g - 4) + (t - 2)) : kZeroSlot;
     L.brec = smem_u32(rec) + slot * 16;
-    L.xsl = smem_u32(xs) + 4u * (t >> 1);
+    L.xsl = smem_u32(xs) + (FMT == FMT_Q6_K ? 0u : 4u * (t >> 1));   // Q6_K: MMA m is block m for every lane
+    L.xs16l = smem_u32(xsum) + 4u * (t >> 1);
     L.kd0 = mk2((t & 1) ? 1.0f : 65536.0f, (t & 1) ? 1.0f : 65536.0f);
     L.kd1 = mk2((t & 1) ? 0.0f : 256.0f, (t & 1) ? 0.0f : 256.0f);
     if (FMT == FMT_Q4_K && t >= 2) {   // high nibbles enter as 16 c
@@ -687,6 +837,14 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
                         stage_pairs_k<1>(L, st[0], sb + L.v0, pb, px, y0, y1, y2);
                     else
                         stage_pairs_k<3>(L, st[0], sb + L.v0, pb, px, y0, y1, y2);
+                } else if constexpr (FMT == FMT_Q6_K) {
+                    const uint32_t px16 = L.xs16l + 16u * P0;
+                    if (ntiles == 2)
+                        stage_pairs_q6<2>(L, sb, pb, px, px16, y0, y1, y2);
+                    else if (ntiles == 1)
+                        stage_pairs_q6<1>(L, sb, pb, px, px16, y0, y1, y2);
+                    else
+                        stage_pairs_q6<3>(L, sb, pb, px, px16, y0, y1, y2);
                 } else {
                     if (ntiles == 2)
                         stage_pairs<FMT, 2>(L, st, sb + L.v0, sb + L.vd, pb, px, y0, y1, y2);
@@ -729,7 +887,8 @@ template <int FMT>
 bool encode_maps(ImmaSegment& ms, const void* w, int K, int rows) {
     auto fn = tensor_map_encoder();
     if (!fn) return false;
-    const size_t row_bytes = static_cast<size_t>(K) / 32 * (FMT == FMT_Q8_0 ? 34 : 18);   // Q4_K: K / 256 * 144
+    const size_t row_bytes = FMT == FMT_Q6_K ? static_cast<size_t>(K) / 256 * 210
+                                             : static_cast<size_t>(K) / 32 * (FMT == FMT_Q8_0 ? 34 : 18);   // Q4_K: K / 256 * 144
     const cuuint64_t dims[2] = {row_bytes / 8, static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {row_bytes};
     const cuuint32_t es[2] = {1, 1};
@@ -744,14 +903,16 @@ bool encode_maps(ImmaSegment& ms, const void* w, int K, int rows) {
 }
 
 int stage_bytes_of(int fmt) {
-    return fmt == FMT_Q4_0 ? IGeom<FMT_Q4_0>::kStageBytes
+    return fmt == FMT_Q4_0   ? IGeom<FMT_Q4_0>::kStageBytes
            : fmt == FMT_Q4_K ? IGeom<FMT_Q4_K>::kStageBytes
+           : fmt == FMT_Q6_K ? IGeom<FMT_Q6_K>::kStageBytes
                              : IGeom<FMT_Q8_0>::kStageBytes;
 }
 
 size_t fixed_smem(int fmt, int K) {
     const size_t npairs = static_cast<size_t>(K / 64);
-    return 1024 + npairs * (kRecBytes + (fmt == FMT_Q4_K ? 16 : 8)) + kRing * kCW * kRedRows * 4 + kCW * kScratchBytes +
+    return 1024 + npairs * (kRecBytes + (fmt == FMT_Q4_K ? 16 : fmt == FMT_Q6_K ? 24 : 8)) + kRing * kCW * kRedRows * 4 +
+           kCW * kScratchBytes +
            (2 * kMaxStages + 2 * kRing) * 8;
 }
 
@@ -766,7 +927,8 @@ void plan_smem(int fmt, int K, int* stages, size_t* smem) {
 }  // namespace
 
 bool matvec_imma_supported(int fmt, int K) {
-    if ((fmt != FMT_Q4_0 && fmt != FMT_Q8_0 && fmt != FMT_Q4_K) || K <= 0 || K % 2048 != 0) return false;
+    if ((fmt != FMT_Q4_0 && fmt != FMT_Q8_0 && fmt != FMT_Q4_K && fmt != FMT_Q6_K) || K <= 0 || K % 2048 != 0)
+        return false;
     int stages = 0;
     size_t smem = 0;
     plan_smem(fmt, K, &stages, &smem);
@@ -795,6 +957,7 @@ cudaError_t launch_matvec_imma(int fmt, const MatvecParams& mp, cudaStream_t str
         ImmaSegment& ms = p.seg[s];
         const bool ok = fmt == FMT_Q4_0   ? encode_maps<FMT_Q4_0>(ms, mp.seg[s].w, mp.K, mp.seg[s].rows)
                         : fmt == FMT_Q4_K ? encode_maps<FMT_Q4_K>(ms, mp.seg[s].w, mp.K, mp.seg[s].rows)
+                        : fmt == FMT_Q6_K ? encode_maps<FMT_Q6_K>(ms, mp.seg[s].w, mp.K, mp.seg[s].rows)
                                           : encode_maps<FMT_Q8_0>(ms, mp.seg[s].w, mp.K, mp.seg[s].rows);
         if (!ok) return cudaErrorInvalidValue;
         ms.bias = mp.seg[s].bias;
@@ -809,11 +972,12 @@ cudaError_t launch_matvec_imma(int fmt, const MatvecParams& mp, cudaStream_t str
     plan_smem(fmt, mp.K, &stages, &smem);
     auto kern = fmt == FMT_Q4_0   ? quant_imma_kernel<FMT_Q4_0>
                 : fmt == FMT_Q4_K ? quant_imma_kernel<FMT_Q4_K>
+                : fmt == FMT_Q6_K ? quant_imma_kernel<FMT_Q6_K>
                                   : quant_imma_kernel<FMT_Q8_0>;
-    static bool configured[3][64] = {};
+    static bool configured[4][64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    bool& done = configured[fmt == FMT_Q4_0 ? 0 : fmt == FMT_Q4_K ? 2 : 1][dev & 63];
+    bool& done = configured[fmt == FMT_Q4_0 ? 0 : fmt == FMT_Q4_K ? 2 : fmt == FMT_Q6_K ? 3 : 1][dev & 63];
     if (!done) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
         if (e != cudaSuccess) return e;

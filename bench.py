@@ -473,8 +473,7 @@ def run_extra(args, dev, stream, sh, l2, which=None, reps=200):
             alg = pair + sum(4 * (n + k) for n, k in shapes)
             out[f"{name}_llama_ffn"] = {"GB/s": round(alg / (ms * 1e-3) / 1e9, 1), "us_per_step": round(ms * 1e3, 3),
                                         "launches_per_step": 2, "algorithmic_bytes": alg,
-                                        "kernel": "quant_imma_kernel<Q4_K> (integer tensor cores)" if name == "q4_k"
-                                        else "q6k_matvec_kernel (4- or 8-row CTAs, 8 warps dealing block tasks)"}
+                                        "kernel": f"quant_imma_kernel<{name.upper()}> (integer tensor cores)"}
             del ws, xk, yk
 
     def c5_section():
