@@ -14,6 +14,9 @@
 //     sub-block 2j in its low and 2j + 1 in its high nibbles; quad lanes 0-1
 //     take the low, 2-3 the high nibbles of the same bytes, unsigned, and
 //     each row adds d scale 2^-F (digits) - dmin min sum(x) per sub-block.
+//     Q6_K (GgufQ6RawDot.dotRowQ6K): the 6-bit codes (ql nibble | qh bits)
+//     as u8 of one 32-value block per MMA, quad lanes 0-1 / 2-3 its two
+//     16-value scale groups; the -32 offset enters as -32 sum(x) per group.
 //   * B operand = x, split exactly into three balanced int8 digits per
 //     32-element block: X = rint(x 2^F) with F chosen from the block's max
 //     |x| so that |X| <= 2^22, X = h 2^16 + m 2^8 + l, l, m in [-128, 127],
