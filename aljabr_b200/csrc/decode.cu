@@ -12,8 +12,9 @@
 // RMSNorm scale is applied by the consumer) -> gate/up pair whose epilogue
 // applies SwiGLU -> down-proj whose epilogue does as the o-proj's for the
 // next layer.  Six launches per layer, chained with programmatic dependent
-// launch inside one CUDA graph.  GGUF-typed weights run the residual +
-// RMSNorm and SwiGLU as separate small launches instead.
+// launch inside one CUDA graph.  GGUF-typed weights run SwiGLU as a separate
+// small launch; their residual + RMSNorm is deferred the same way when every
+// matvec can carry it (typed_fusable), else it is a separate launch too.
 //
 // Tensor parallelism (2/4/8 GPUs, one process per GPU): every weight is
 // row-sharded (the caller passes each rank's contiguous row block) and
@@ -375,7 +376,7 @@ struct DecodeModel {
     float *x, *xn, *q, *k, *vv, *att_l, *att, *delta_l, *delta, *h_l, *hh, *logits_l, *logits, *scratch;
     float* norm_partials = nullptr;    // [matvec_max_ctas()] per-CTA sums of squares
     bool defer_norm = false;           // RMSNorm scale applied by the consuming matvec (one GPU)
-    bool typed = false;                // some tensor is not NF4: unfused residual / norm / SwiGLU launches
+    bool typed = false;                // some tensor is not NF4: SwiGLU (and maybe residual / norm) launched apart
     unsigned int* norm_counter = nullptr;
     float* act_base = nullptr;
     int* io = nullptr;                 // device {pos, token, argmax}
@@ -480,7 +481,29 @@ cudaError_t matvec(const DecodeModel& m, const Weight* ws, float* const* ys, con
     } while (0)
 
 // Enqueue one full decode step on m.stream (eagerly or under capture).
+// A GGUF-typed model defers its RMSNorms to the consuming launches (as the
+// NF4 step does) when every matvec of the step can: NF4 tensors on the
+// table kernel, the others on the integer tensor-core kernel (K a multiple
+// of 2048, rows in 4s, 16-byte aligned weights).
+bool typed_fusable(const DecodeModel& m) {
+    if (m.T != 1) return false;
+    auto ok = [&](const Weight& w, int K, int rows) {
+        if (w.fmt == FMT_NF4) return matvec_lut_supported(FMT_NF4, K, m.group) && rows % 4 == 0;
+        return matvec_imma_supported(w.fmt, K) && rows % 4 == 0 && (reinterpret_cast<uintptr_t>(w.codes) & 15) == 0;
+    };
+    const int D = m.D;
+    for (int l = 0; l < m.layers; ++l) {
+        const auto& w = m.w[l];
+        if (!ok(w[W_Q], m.H, m.hq * D) || !ok(w[W_K], m.H, m.hkv * D) || !ok(w[W_V], m.H, m.hkv * D) ||
+            !ok(w[W_O], m.Hq * D, m.h) || !ok(w[W_GATE], m.H, m.f) || !ok(w[W_UP], m.H, m.f) ||
+            !ok(w[W_DOWN], m.F, m.h))
+            return false;
+    }
+    return ok(m.head, m.H, m.v);
+}
+
 cudaError_t record_step(DecodeModel& m) {
+    if (m.typed) m.defer_norm = typed_fusable(m);
     const int D = m.D;
     const int sms = sm_count_for_current_device();
     const float* out_norm = m.norms + static_cast<size_t>(m.layers) * 2 * m.H;
@@ -537,7 +560,7 @@ cudaError_t record_step(DecodeModel& m) {
                 RECN(g_nccl.allGather(m.delta_l, m.delta, m.h, ncclFloat, m.comm, m.stream));
                 REC(launch_small(add_norm_kernel, 1, 1024, m.stream, m.x, static_cast<const float*>(m.delta), m.xn,
                                  ffn_norm, m.H, m.eps));
-            } else if (m.typed) {
+            } else if (m.typed && !m.defer_norm) {
                 float* ys[1] = {m.delta};
                 REC(matvec(m, ws, ys, rows, 1, m.att, m.Hq * D, EPI_STORE, nullptr, nullptr, nullptr));
                 REC(launch_small(add_norm_kernel, 1, 1024, m.stream, m.x, static_cast<const float*>(m.delta), m.xn,
@@ -552,7 +575,7 @@ cudaError_t record_step(DecodeModel& m) {
             const int rows[2] = {m.f, m.f};
             if (m.typed) {   // one GPU: gate -> h_l, up -> hh, then hh = SiLU(h_l) * hh
                 float* ys[2] = {m.h_l, m.hh};
-                REC(matvec(m, ws, ys, rows, 2, m.xn, m.H, EPI_STORE, nullptr, nullptr, nullptr));
+                REC(matvec(m, ws, ys, rows, 2, m.xn, m.H, EPI_STORE, nullptr, nullptr, nullptr, nullptr, true));
                 REC(launch_small(swiglu_kernel, std::max(1, std::min(sms, (m.F + 255) / 256)), 256, m.stream,
                                  static_cast<const float*>(m.h_l), m.hh, m.F));
             } else {
@@ -570,7 +593,7 @@ cudaError_t record_step(DecodeModel& m) {
                 RECN(g_nccl.allGather(m.delta_l, m.delta, m.h, ncclFloat, m.comm, m.stream));
                 REC(launch_small(add_norm_kernel, 1, 1024, m.stream, m.x, static_cast<const float*>(m.delta), m.xn,
                                  next_norm, m.H, m.eps));
-            } else if (m.typed) {
+            } else if (m.typed && !m.defer_norm) {
                 float* ys[1] = {m.delta};
                 REC(matvec(m, ws, ys, rows, 1, m.hh, m.F, EPI_STORE, nullptr, nullptr, nullptr));
                 REC(launch_small(add_norm_kernel, 1, 1024, m.stream, m.x, static_cast<const float*>(m.delta), m.xn,

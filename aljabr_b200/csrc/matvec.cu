@@ -723,9 +723,12 @@ cudaError_t launch_matvec(int fmt, const MatvecParams& p, cudaStream_t stream, b
         if (e != cudaErrorNotSupported) return e;
     }
     if (fmt == FMT_Q4_K || fmt == FMT_Q6_K) return launch_matvec_k(fmt, p, stream, pdl);
-    if (p.norm_defer || p.in_parts)   // only the NF4 table kernel splits the RMSNorm across launches
-        return fmt == FMT_NF4 && matvec_lut_supported(fmt, p.K, p.group) ? launch_matvec_lut(fmt, p, stream, pdl)
-                                                                         : cudaErrorNotSupported;
+    if (p.norm_defer || p.in_parts) {   // the NF4 table and integer tensor-core kernels split the RMSNorm
+        if (fmt == FMT_NF4)
+            return matvec_lut_supported(fmt, p.K, p.group) ? launch_matvec_lut(fmt, p, stream, pdl)
+                                                           : cudaErrorNotSupported;
+        return matvec_imma_supported(fmt, p.K) ? launch_matvec_imma(fmt, p, stream, pdl) : cudaErrorNotSupported;
+    }
     if (matvec_imma_supported(fmt, p.K)) {
         const cudaError_t e = launch_matvec_imma(fmt, p, stream, pdl);
         if (e != cudaErrorNotSupported) return e;

@@ -188,6 +188,17 @@ struct alignas(64) ImmaParams {
     const float* x;
     const uint8_t* prefetch;
     size_t prefetch_bytes;
+    // deferred RMSNorm (decode step, one segment): the epilogue also stores
+    // norm_out = y * norm_w and this CTA's sum of y^2 in norm_partials[cta];
+    // a launch with in_parts scales x by 1 / sqrt(sum(in_parts) / in_rows +
+    // in_eps) as it converts it
+    float* norm_out;
+    const float* norm_w;
+    float* norm_partials;
+    const float* in_parts;
+    int in_nparts;
+    int in_rows;
+    float in_eps;
 };
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
@@ -559,7 +570,7 @@ __device__ __forceinline__ void stage_pass_a(const float4& v, int u, int warp, i
 
 template <int FMT>
 __device__ __forceinline__ void stage_x(const float* __restrict__ x, int nunits, uint8_t* rec, float* xs,
-                                        uint8_t* scratch, int warp, int lane, float* xsum) {
+                                        uint8_t* scratch, int warp, int lane, float* xsum, float in_s) {
     const int jb = lane >> 4, gi = lane & 15;                  // pass B: (pair, t, m, r)
     const int t = gi >> 2, m = (gi >> 1) & 1, r = gi & 1;
     const int e0 = slot_elem(FMT, t, m, r, 0), e2 = slot_elem(FMT, t, m, r, 2);
@@ -585,6 +596,15 @@ __device__ __forceinline__ void stage_x(const float* __restrict__ x, int nunits,
             if (u0 + b < nunits)
                 v[b] = __ldg(reinterpret_cast<const float4*>(x + static_cast<size_t>(unit_pair<FMT>(u0 + b, lane >> 4, warp)) * 64) +
                              (lane & 15));
+        if (in_s != 1.0f) {
+#pragma unroll
+            for (int b = 0; b < kXBatch; ++b) {
+                v[b].x *= in_s;
+                v[b].y *= in_s;
+                v[b].z *= in_s;
+                v[b].w *= in_s;
+            }
+        }
         // two units per round: their shuffle / PRMT chains overlap
 #pragma unroll
         for (int b = 0; b < kXBatch; b += 2) {
@@ -711,6 +731,7 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
         pdl_wait();
         SlabWalk walk{u_begin, u_end};
         int seg, su, nunits, sl = 0;
+        float sq = 0.0f;   // deferred RMSNorm: this lane's sum of y^2
         while (walk.next(p, seg, su, nunits)) {
             const int b = sl % kRing;
             const bool ok = __all_sync(0xffffffffu, mbar_wait(&rfull[b], (sl / kRing) & 1));
@@ -724,10 +745,18 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
                 if (sg.bias) out += sg.bias[lrow];
                 if (sg.residual) out = sg.residual[lrow] + out;
                 sg.y[lrow] = out;
+                if (p.norm_out) {
+                    p.norm_out[lrow] = out * p.norm_w[lrow];
+                    sq = fmaf(out, out, sq);
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&rempty[b]);
             ++sl;
+        }
+        if (p.norm_out) {   // the consuming launch sums the partials (fixed order) and applies the scale
+            const float cta = warp_sum(sq);
+            if (lane == 0) p.norm_partials[blockIdx.x] = cta;
         }
         return;
     }
@@ -739,7 +768,14 @@ __global__ void __launch_bounds__(kThreads, 1) quant_imma_kernel(const __grid_co
     const int pair_first = warp * kPPW;                   // this warp's pairs in every chunk
     if (u_begin < u_end) {
         // digits of this warp's pairs for the whole launch (read by no other warp)
-        stage_x<FMT>(p.x, nchunks * kPPW / 2, rec, xs, scratch + warp * kScratchBytes, warp, lane, xsum);
+        // deferred RMSNorm of x: its scale from the producer's partials (fixed order)
+        float in_s = 1.0f;
+        if (p.in_parts) {
+            float part = 0.0f;
+            for (int b = lane; b < p.in_nparts; b += 32) part += __ldcg(p.in_parts + b);
+            in_s = 1.0f / sqrtf(warp_sum(part) / static_cast<float>(p.in_rows) + p.in_eps);
+        }
+        stage_x<FMT>(p.x, nchunks * kPPW / 2, rec, xs, scratch + warp * kScratchBytes, warp, lane, xsum, in_s);
         __syncwarp();
     }
     // Per-lane constants: offsets within a stage (row g of tile 0, pair 0 of
@@ -941,8 +977,12 @@ bool matvec_imma_supported(int fmt, int K) {
 
 cudaError_t launch_matvec_imma(int fmt, const MatvecParams& mp, cudaStream_t stream, bool pdl) {
     if (!matvec_imma_supported(fmt, mp.K)) return cudaErrorNotSupported;
-    if (mp.epilogue != EPI_STORE || mp.norm_out || mp.norm_defer || mp.in_parts || mp.tpl.tp > 1)
+    if (mp.epilogue != EPI_STORE || mp.tpl.tp > 1) return cudaErrorNotSupported;
+    // RMSNorm only deferred (no last-CTA pass), on a single segment
+    if (mp.norm_out && (!mp.norm_defer || mp.nseg != 1 || !mp.norm_w || !mp.norm_partials))
         return cudaErrorNotSupported;
+    if (mp.norm_defer && !mp.norm_out) return cudaErrorNotSupported;
+    if (mp.in_parts && (mp.in_nparts <= 0 || mp.in_rows <= 0)) return cudaErrorNotSupported;
     if ((reinterpret_cast<uintptr_t>(mp.x) & 15) != 0) return cudaErrorNotSupported;
     for (int s = 0; s < mp.nseg; ++s)
         if (mp.seg[s].rows % kUnit != 0 || (reinterpret_cast<uintptr_t>(mp.seg[s].w) & 15) != 0)
@@ -955,6 +995,13 @@ cudaError_t launch_matvec_imma(int fmt, const MatvecParams& mp, cudaStream_t str
     p.x = mp.x;
     p.prefetch = static_cast<const uint8_t*>(mp.prefetch);
     p.prefetch_bytes = mp.prefetch_bytes;
+    p.norm_out = mp.norm_out;
+    p.norm_w = mp.norm_w;
+    p.norm_partials = mp.norm_partials;
+    p.in_parts = mp.in_parts;
+    p.in_nparts = mp.in_nparts;
+    p.in_rows = mp.in_rows;
+    p.in_eps = mp.in_eps;
     int row0 = 0;
     for (int s = 0; s < mp.nseg; ++s) {
         ImmaSegment& ms = p.seg[s];
