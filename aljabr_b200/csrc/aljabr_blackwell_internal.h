@@ -68,12 +68,13 @@ struct MatvecParams {
     float norm_eps;
     float* norm_partials;
     unsigned int* norm_counter;
-    // Deferred RMSNorm (NF4 table kernel only).  norm_defer: instead of the
-    // last-CTA pass, write norm_out = y * norm_w (unscaled) and this CTA's sum
-    // of squares of y to norm_partials[CTA]; the consuming launch applies the
-    // scale.  in_parts (consuming side): x is such an unscaled vector whose
-    // producer left in_nparts partials; every output is multiplied by
-    // rsqrt(sum(partials) / in_rows + in_eps) before the epilogue.
+    // Deferred RMSNorm (NF4 table and integer tensor-core kernels).
+    // norm_defer: instead of the last-CTA pass, write norm_out = y * norm_w
+    // (unscaled) and this CTA's sum of squares of y to norm_partials[CTA]; the
+    // consuming launch applies the scale.  in_parts (consuming side): x is
+    // such an unscaled vector whose producer left in_nparts partials; the
+    // table kernel multiplies every output by rsqrt(sum(partials) / in_rows +
+    // in_eps), the integer kernel scales x by it while converting x.
     int norm_defer;
     const float* in_parts;
     int in_nparts;
@@ -92,8 +93,9 @@ int matvec_max_ctas();
 // programmatic dependent launch on the stream.
 cudaError_t launch_matvec(int fmt, const MatvecParams& p, cudaStream_t stream, bool pdl);
 bool matvec_tma_supported(int fmt, int K, int group);
-// Integer tensor-core path (Q4_0 / Q8_0, K a multiple of 2048, plain store
-// epilogue with bias / residual); launch_matvec picks it first.
+// Integer tensor-core path (Q4_0 / Q8_0 / Q4_K / Q6_K, K a multiple of 2048,
+// plain store epilogue with bias / residual and the deferred RMSNorm);
+// launch_matvec picks it first.
 bool matvec_imma_supported(int fmt, int K);
 cudaError_t launch_matvec_imma(int fmt, const MatvecParams& p, cudaStream_t stream, bool pdl);
 // fp16 tensor-core path (Q4_0 / Q8_0, K a multiple of 2048) with the fused
