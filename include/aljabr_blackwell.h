@@ -22,7 +22,11 @@
  *    The weight pointer B is a host address inside a buffer previously given
  *    to aljabr_blackwell_register_model_buffer (the mmap'd GGUF file), which
  *    the library copied to HBM once; a device pointer is accepted as well.
- *    They block until C is written.
+ *    They block until C is written.  A call whose matrices, sizes and
+ *    types were seen before is replayed as one cached CUDA graph (captured
+ *    on the second such call; at most 256 shapes per device, dropped when
+ *    their weights are unregistered); a call made while a prefetch hint is
+ *    pending runs its launches directly.
  *  - "_dev" entry points take device pointers for everything and are
  *    stream-ordered (stream = cudaStream_t, NULL = the library's stream for
  *    the current device); they do not synchronize.
