@@ -456,7 +456,9 @@ cudaError_t matvec(const DecodeModel& m, const Weight* ws, float* const* ys, con
     }
     if (scaled_x && m.defer_norm) {
         p.in_parts = m.norm_partials;
-        p.in_nparts = matvec_lut_grid(m.H);   // the producing o / down launch has H rows
+        // the producing o / down launch has H rows; the table and the integer
+        // tensor-core kernels both launch min(SMs, rows / 4) CTAs, one partial each
+        p.in_nparts = matvec_lut_grid(m.H);
         p.in_rows = m.H;
         p.in_eps = m.eps;
     }

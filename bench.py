@@ -441,7 +441,7 @@ def run_extra(args, dev, stream, sh, l2, which=None, reps=200):
                                                     "launches_per_call": 1}
 
     def kquant_section():
-        # GGUF Q4_K / Q6_K (SURVEY next row 1) at the Llama FFN shapes of the
+        # GGUF Q4_K / Q6_K (GgufQ4RawDot / GgufQ6RawDot) at the Llama FFN shapes of the
         # headline: up 14336x4096 + down 4096x14336 per step.  Synthetic
         # super-blocks: random code / scale bytes with fixed small fp16 super
         # scales (every byte pattern is a valid block).
